@@ -1,0 +1,143 @@
+/*
+ * spark_h3_b200.h -- C ABI of the B200 (sm_100a) Spark-H3 sparse-attention hot path.
+ *
+ * Every entry point takes plain device pointers, explicit sizes and a cudaStream_t
+ * passed as void*.  Nothing here allocates device memory: outputs and workspaces are
+ * owned by the caller.  No entry point synchronises the host with the device.
+ * Return value: 0 on success, a negative SB_ERR_* code on failure; sb_last_error()
+ * returns the message of the last failure on the calling host thread.
+ *
+ * Tensor layouts (row-major, innermost last):
+ *   Q, K, V, O        [B, T, H, D]        token-major "BTHD", as the reference's
+ *                                          spark_attention_bthd consumes them
+ *   query block means [B, NB, H, D] fp32  NB = ceil(T / block)
+ *   key block means   [B, NB, H, D] dtype
+ *   anchor            [B, H, D]     dtype (one global video anchor per head)
+ *   AK, AV            [B, H, NB, D] dtype (anchor-weighted key/value summaries)
+ *   LM                [B, H, NB]    fp32  (log-mass correction, natural log)
+ *   packed route      [B, QB, H, W] int32 W = ceil(NB / 32); bit (kb % 32) of word
+ *                                          (kb / 32) marks key block kb as exact
+ *   top-k indices     [B, QB, H, k] int32 ascending block indices
+ *   LSE               [B, T, H]     fp32  natural-log softmax normaliser
+ *
+ * dtype codes: SB_F32 (float32) or SB_BF16 (bfloat16).  The tensor-core attention
+ * path handles bf16 with D = 128; float32 inputs or D = 64 use the SIMT path of the
+ * same library (still on the GPU).  Block sizes 64 and 128 are supported.
+ */
+#ifndef SPARK_H3_B200_H
+#define SPARK_H3_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define SB_F32 0
+#define SB_BF16 1
+
+#define SB_OK 0
+#define SB_ERR_INVALID -1     /* bad argument: shape, dtype, alignment, null pointer */
+#define SB_ERR_CUDA -2        /* a CUDA runtime/driver call failed */
+#define SB_ERR_UNSUPPORTED -3 /* valid arguments this build does not implement */
+
+/* Library version (major * 10000 + minor * 100 + patch). */
+int sb_version(void);
+
+/* Message of the last failing call on this host thread ("" if none). */
+const char* sb_last_error(void);
+
+/* Device-side status word written by kernels whose waits are bounded.  Returns the
+ * value the last completed kernel left in it (0 = no timeout) and clears it.  This
+ * is the only entry point that synchronises the stream. */
+int sb_read_device_status(void* stream);
+
+/*
+ * Query block pooling.  Replaces the query-centroid half of
+ * h3_sparse_attention/spark_integration.py:111-127 (_sol_topk_policy_scores) and the
+ * per-64-row partial sums of sol_numerator_virtual_q.py:268-285 (_anchor_parts).
+ * qc[b, j, h, :] = (sum of the rows of block j, fp32, rows in order) / rows_in_block.
+ */
+int sb_pool_queries(const void* q, int dtype, int B, int T, int H, int D, int block,
+                    float* qc, void* stream);
+
+/*
+ * Global video anchor of each head, from the query block means.  Replaces
+ * sol_numerator_virtual_q.py:287-302 (_anchors_from_parts / build_virtual_anchors for
+ * the single global parent of landmark_virtual_q.py:54-65 with levels_up = 99).
+ * anchor[b, h, :] = (sum_j qc[b, j, h, :] * block) / (prefix_blocks * block), j in
+ * order, then rounded to anchor_dtype.
+ */
+int sb_query_anchor(const float* qc, int B, int NB, int H, int D, int block,
+                    int prefix_blocks, void* anchor, int anchor_dtype, void* stream);
+
+/*
+ * One pass over K and V: key block means (routing) and anchor-weighted summaries.
+ * Replaces sol_attn/preprocess.py:16-52 (_reduce_kc_kernel) and
+ * sol_numerator_virtual_q.py:93-135 (_summaries) for the global parent.
+ * weighted_kv != 0: AK/AV are softmax(anchor . k / sqrt(D))-weighted means, else plain
+ * means.  mass_bias != 0: LM = logsumexp(a.k/sqrt(D)) - a.AK_stored/sqrt(D), else
+ * LM = log(rows in block).  Any of kc / ak / av / lm may be NULL to skip that output
+ * (anchor may be NULL when ak, av and lm are all NULL).
+ */
+int sb_pool_keys_summaries(const void* k, const void* v, const void* anchor,
+                           int dtype, int anchor_dtype, int B, int T, int H, int D,
+                           int block, int weighted_kv, int mass_bias,
+                           void* kc, void* ak, void* av, float* lm, void* stream);
+
+/*
+ * Block scores and per-row Top-K.  Replaces spark_integration.py:94-175
+ * (_sol_topk_policy_scores + _sol_topk_route_from_scores) and
+ * sol_topk_cutoff.py:416-480 (gemm_topk_packed_route, including the packing kernel
+ * at :19-44).  score[b, i, h, j] = fp32(dot(qc[b,i,h,:], kc[b,j,h,:])) * scale_log2
+ * for j < candidates (dot = sequential fused multiply-add over d); each row keeps the
+ * topk largest scores, ties going to the lower block index.  packed_route must hold
+ * B*QB*H*ceil(NB/32) words; bits >= candidates are never set.
+ * workspace: at least sb_route_workspace_bytes(B, QB, H, candidates) bytes.
+ * indices may be NULL.
+ */
+int64_t sb_route_workspace_bytes(int B, int QB, int H, int candidates);
+int sb_route_topk(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
+                  int H, int D, int candidates, int topk, float scale_log2,
+                  void* workspace, int32_t* packed_route, int32_t* indices,
+                  void* stream);
+
+/*
+ * Sparse attention forward.  Replaces sol_numerator_virtual_q.py:717-977
+ * (_fused_virtual -> SparkReweightForwardSm*) with the semantics of the streamed
+ * oracle at sol_numerator_virtual_q.py:596-652 and
+ * tests/test_spark_installer.py:559-570:
+ *   for a query row in routed query block i (i < query_tokens / block):
+ *     exact key blocks E = route bits of (b, i, h)  U  [sink_first, sink_last)
+ *                          U  {|i - kb| <= local_radius}  (local_radius < 0: none)
+ *     logits = q.k / sqrt(D) over the tokens of E, and q.AK[kb] / sqrt(D) + LM[kb]
+ *     over every key block kb not in E; O = softmax(logits) @ [V ; AV].
+ *   rows >= query_tokens attend every key exactly (the dense suffix).
+ * packed_route: [B, QB, H, ceil(NB/32)] with QB >= query_tokens / block.
+ * ak/av/lm: summaries of the single global parent ([B, H, NB, D] / [B, H, NB]).
+ * lse may be NULL.
+ */
+int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype,
+                        int B, int T, int H, int D, int block,
+                        const int32_t* packed_route, int QB,
+                        const void* ak, const void* av, const float* lm,
+                        int query_tokens, int sink_first, int sink_last,
+                        int local_radius, void* out, float* lse, void* stream);
+
+/*
+ * Head-wise token permutation of the video prefix.  Replaces
+ * spark_integration.py:308-362 (_headwise_permute_video_tokens) and
+ * landmark_tree_v2_triton.py:19-90 (headwise_permute_bthd).
+ * dst[b, t, h, :] = src[b, perm[b, h, t], h, :] for t < video_tokens, and
+ * dst[b, t, h, :] = src[b, t, h, :] for t >= video_tokens.  perm is int32 or int64
+ * (index_bytes 4 or 8).  src and dst must not overlap.
+ */
+int sb_headwise_permute(const void* src, void* dst, const void* perm, int index_bytes,
+                        int B, int T, int H, int D, int elem_bytes, int video_tokens,
+                        void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* SPARK_H3_B200_H */

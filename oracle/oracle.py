@@ -1,0 +1,293 @@
+"""CPU oracle for the Spark-H3 hot path.
+
+TEST INFRASTRUCTURE ONLY.  Only ``tests/``, ``__graft_entry__.smoke()`` and the CPU-baseline
+leg of ``bench.py`` import this module, and only as the checker; the product path never
+calls it.
+
+Integer outputs (route indices, packed words) come from ``spark_oracle.c``, which fixes
+the arithmetic order shared with the CUDA kernels.  Floating-point outputs (anchor,
+summaries, attention) are restated here in numpy with float64 accumulation and the same
+storage roundings as the reference:
+
+* anchor        h3_sparse_attention/sol_numerator_virtual_q.py:268-302
+* summaries     h3_sparse_attention/sol_numerator_virtual_q.py:93-135 (_summaries)
+* attention     tests/test_spark_installer.py:559-570 (explicit exact/summary softmax) with
+                the exact-block rule of sol_attn/sm90/mainloop.py:590-667 and the dense
+                suffix of h3_sparse_attention/spark_integration.py:1251-1261
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+import os
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "_build" / "libsparkoracle.so"
+LOG2E = 1.4426950408889634
+LN2 = 0.6931471805599453
+
+
+def build() -> Path:
+    """Compile the C restatement (gcc, no contraction of multiply-adds)."""
+    LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
+    src = HERE / "spark_oracle.c"
+    if LIB_PATH.exists() and LIB_PATH.stat().st_mtime >= src.stat().st_mtime:
+        return LIB_PATH
+    tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
+    subprocess.check_call([
+        "gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", "-shared", "-fPIC",
+        "-o", str(tmp), str(src), "-lm",
+    ])
+    os.replace(tmp, LIB_PATH)
+    return LIB_PATH
+
+
+_LIB = None
+
+
+def _lib():
+    global _LIB
+    if _LIB is None:
+        lib = ctypes.CDLL(str(build()))
+        f32p = np.ctypeslib.ndpointer(np.float32, flags="C_CONTIGUOUS")
+        i32p = np.ctypeslib.ndpointer(np.int32, flags="C_CONTIGUOUS")
+        vp = ctypes.c_void_p
+        ci, cf, ci64 = ctypes.c_int, ctypes.c_float, ctypes.c_int64
+        lib.orc_block_means.argtypes = [vp, ci, ci, ci, ci, ci, ci, f32p]
+        lib.orc_round_bf16.argtypes = [f32p, ci64]
+        lib.orc_anchor.argtypes = [f32p, ci, ci, ci, ci, ci, ci, f32p]
+        lib.orc_scores.argtypes = [f32p, f32p, ci, ci, ci, ci, ci, ci, cf, f32p]
+        lib.orc_topk.argtypes = [f32p, ci64, ci, ci, ci, i32p, i32p]
+        for fn in (lib.orc_block_means, lib.orc_round_bf16, lib.orc_anchor, lib.orc_scores, lib.orc_topk):
+            fn.restype = None
+        _LIB = lib
+    return _LIB
+
+
+# ------------------------------------------------------------------ bf16 helpers
+def bf16_bits_to_f32(bits: np.ndarray) -> np.ndarray:
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bfloat16 bit patterns (NaN kept quiet)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    nan = (u & 0x7F800000) == 0x7F800000
+    nan &= (u & 0x007FFFFF) != 0
+    rounded = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16) & 0xFFFF
+    out = np.where(nan, ((u >> 16) | 0x40) & 0xFFFF, rounded)
+    return out.astype(np.uint16)
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(np.asarray(x, dtype=np.float32)))
+
+
+class Tensor:
+    """A host tensor in its storage dtype: float32 values or bfloat16 bit patterns."""
+
+    def __init__(self, data: np.ndarray, dtype: str):
+        if dtype not in ("float32", "bfloat16"):
+            raise ValueError("dtype must be float32 or bfloat16")
+        want = np.uint16 if dtype == "bfloat16" else np.float32
+        self.data = np.ascontiguousarray(data, dtype=want)
+        self.dtype = dtype
+
+    @property
+    def shape(self):
+        return self.data.shape
+
+    def float(self) -> np.ndarray:
+        return bf16_bits_to_f32(self.data) if self.dtype == "bfloat16" else self.data
+
+    @property
+    def code(self) -> int:
+        return 1 if self.dtype == "bfloat16" else 0
+
+
+def store(x: np.ndarray, dtype: str) -> np.ndarray:
+    """Round float values to a storage dtype and return them as float32."""
+    x = np.asarray(x, dtype=np.float32)
+    return round_bf16(x) if dtype == "bfloat16" else x
+
+
+# --------------------------------------------------------------- integer path
+def block_means(x: Tensor, block: int) -> np.ndarray:
+    B, T, H, D = x.shape
+    nb = -(-T // block)
+    out = np.empty((B, nb, H, D), dtype=np.float32)
+    _lib().orc_block_means(x.data.ctypes.data, x.code, B, T, H, D, block, out)
+    return out
+
+
+def key_means(k: Tensor, block: int) -> np.ndarray:
+    """Key block means stored at the key precision (returned as float32)."""
+    kc = block_means(k, block)
+    return store(kc, k.dtype)
+
+
+def anchor(qc: np.ndarray, block: int, prefix_blocks: int, dtype: str) -> np.ndarray:
+    B, NB, H, D = qc.shape
+    out = np.empty((B, H, D), dtype=np.float32)
+    _lib().orc_anchor(np.ascontiguousarray(qc), B, NB, H, D, block, prefix_blocks, out)
+    return store(out, dtype)
+
+
+def scale_log2(D: int) -> float:
+    return float(np.float32(D ** -0.5 * LOG2E))
+
+
+def scores(qc: np.ndarray, kc: np.ndarray, query_blocks: int, candidates: int) -> np.ndarray:
+    B, NB, H, D = qc.shape
+    out = np.empty((B, query_blocks, H, candidates), dtype=np.float32)
+    _lib().orc_scores(np.ascontiguousarray(qc), np.ascontiguousarray(kc, dtype=np.float32), B, query_blocks,
+                      NB, H, D, candidates, scale_log2(D), out)
+    return out
+
+
+def topk(score: np.ndarray, k: int, total_blocks: int) -> tuple[np.ndarray, np.ndarray]:
+    """Ascending top-k indices [B, QB, H, k] and packed words [B, QB, H, ceil(NB/32)]."""
+    B, QB, H, C = score.shape
+    words = -(-total_blocks // 32)
+    rows = B * QB * H
+    idx = np.empty((rows, k), dtype=np.int32)
+    packed = np.empty((rows, words), dtype=np.int32)
+    _lib().orc_topk(np.ascontiguousarray(score), rows, C, k, words, idx, packed)
+    return idx.reshape(B, QB, H, k), packed.reshape(B, QB, H, words)
+
+
+def target_topk(ratio: float, candidates: int) -> int:
+    """max(1, round(ratio * candidates)) capped at candidates (sol_topk_cutoff.py:342)."""
+    return min(max(1, round(ratio * candidates)), candidates)
+
+
+# ------------------------------------------------------------ float restatements
+def summaries(a: np.ndarray, k: Tensor, v: Tensor, block: int, *, weighted_kv: bool = True,
+              mass_bias: bool = True) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """AK, AV [B, H, NB, D] (stored precision) and LM [B, H, NB] for the global anchor."""
+    B, T, H, D = k.shape
+    nb = -(-T // block)
+    kf, vf = k.float().astype(np.float64), v.float().astype(np.float64)
+    scale = D ** -0.5
+    ak = np.empty((B, H, nb, D), dtype=np.float32)
+    av = np.empty_like(ak)
+    lm = np.empty((B, H, nb), dtype=np.float32)
+    for j in range(nb):
+        rows = slice(j * block, min(T, (j + 1) * block))
+        kk, vv = kf[:, rows], vf[:, rows]                    # [B, r, H, D]
+        count = kk.shape[1]
+        if weighted_kv or mass_bias:
+            logits = np.einsum("bhd,brhd->bhr", a.astype(np.float64), kk) * scale * LOG2E
+            mx = logits.max(-1, keepdims=True)
+            p = np.exp2(logits - mx)
+            den = p.sum(-1)
+        if weighted_kv:
+            w = store(p, k.dtype).astype(np.float64)
+            key = np.einsum("bhr,brhd->bhd", w, kk) / den[..., None]
+            val = np.einsum("bhr,brhd->bhd", w, vv) / den[..., None]
+        else:
+            key = kk.mean(1)
+            val = vv.mean(1)
+        ak[:, :, j] = store(key, k.dtype)
+        av[:, :, j] = store(val, v.dtype)
+        if mass_bias:
+            shift = np.einsum("bhd,bhd->bh", a.astype(np.float64), ak[:, :, j].astype(np.float64)) * scale
+            lm[:, :, j] = (mx[..., 0] + np.log2(den)) * LN2 - shift
+        else:
+            lm[:, :, j] = math.log(count)
+    return ak, av, lm
+
+
+def exact_blocks(packed_row: np.ndarray, qb: int, nb: int, sink_first: int, sink_last: int,
+                 local_radius: int) -> np.ndarray:
+    """Boolean [nb]: key blocks evaluated exactly for routed query block qb."""
+    kb = np.arange(nb)
+    bits = (packed_row[kb >> 5].astype(np.int64) >> (kb & 31)) & 1
+    exact = bits.astype(bool) | ((kb >= sink_first) & (kb < sink_last))
+    if local_radius >= 0:
+        exact |= np.abs(qb - kb) <= local_radius
+    return exact
+
+
+def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.ndarray, ak: np.ndarray,
+                     av: np.ndarray, lm: np.ndarray, query_tokens: int, sink_first: int, sink_last: int,
+                     local_radius: int = -1, rows: slice | None = None,
+                     heads: list[int] | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """Output [B, T, H, D] float32 (unrounded) and LSE [B, T, H] for the selected rows/heads.
+
+    Rows outside ``rows`` / heads outside ``heads`` are left as NaN.
+    """
+    B, T, H, D = q.shape
+    nb = -(-T // block)
+    qf, kf, vf = (x.float() for x in (q, k, v))
+    out = np.full((B, T, H, D), np.nan, dtype=np.float32)
+    lse = np.full((B, T, H), np.nan, dtype=np.float32)
+    rows = rows or slice(0, T)
+    r0, r1 = rows.start or 0, min(T, rows.stop if rows.stop is not None else T)
+    heads = list(range(H)) if heads is None else heads
+    scale = D ** -0.5
+    for b in range(B):
+        for h in heads:
+            kh = kf[b, :, h].astype(np.float64)
+            vh = vf[b, :, h].astype(np.float64)
+            akh = ak[b, h].astype(np.float64)
+            avh = av[b, h].astype(np.float64)
+            lmh = lm[b, h].astype(np.float64)
+            start = r0
+            while start < r1:
+                if start < query_tokens:
+                    qb = start // block
+                    stop = min(r1, (qb + 1) * block, query_tokens)
+                    exact = exact_blocks(packed[b, qb, h], qb, nb, sink_first, sink_last, local_radius)
+                else:
+                    qb = -1
+                    stop = r1
+                    exact = np.ones(nb, dtype=bool)
+                tok = np.repeat(exact, block)[:T]
+                keys = np.concatenate([kh[tok], akh[~exact]])
+                vals = np.concatenate([vh[tok], avh[~exact]])
+                qq = qf[b, start:stop, h].astype(np.float64)
+                logits = qq @ keys.T * scale
+                logits[:, int(tok.sum()):] += lmh[~exact]
+                mx = logits.max(-1, keepdims=True)
+                p = np.exp(logits - mx)
+                den = p.sum(-1, keepdims=True)
+                out[b, start:stop, h] = (p @ vals / den).astype(np.float32)
+                lse[b, start:stop, h] = (mx[:, 0] + np.log(den[:, 0])).astype(np.float32)
+                start = stop
+    return out, lse
+
+
+# ------------------------------------------------------------- full pipeline
+def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: float, video_tokens: int | None = None,
+                anchor_dtype: str | None = None, local_radius: int = -1, weighted_kv: bool = True,
+                mass_bias: bool = True, attention: bool = True, rows: slice | None = None,
+                heads: list[int] | None = None) -> dict:
+    """Route, summaries and (optionally) attention of one Spark layer, as the CUDA path does."""
+    B, T, H, D = q.shape
+    video = T if video_tokens is None else video_tokens
+    nb = -(-T // block)
+    query_tokens = (video // block) * block
+    query_blocks = query_tokens // block
+    candidates = video // block
+    sink_first = video // block
+    sink_last = -(-T // block) if T > video else sink_first
+    qc = block_means(q, block)
+    kc = key_means(k, block)
+    a = anchor(qc, block, query_blocks, anchor_dtype or q.dtype)
+    sc = scores(qc, kc, query_blocks, candidates)
+    kk = target_topk(topk_ratio, candidates)
+    idx, packed = topk(sc, kk, nb)
+    result = dict(qc=qc, kc=kc, anchor=a, scores=sc, indices=idx, packed=packed, topk=kk,
+                  query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last)
+    ak, av, lm = summaries(a, k, v, block, weighted_kv=weighted_kv, mass_bias=mass_bias)
+    result.update(ak=ak, av=av, lm=lm)
+    if attention:
+        out, lse = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens, sink_first, sink_last,
+                                    local_radius, rows=rows, heads=heads)
+        result.update(out=out, lse=lse)
+    return result

@@ -1,0 +1,103 @@
+// C-ABI plumbing: error reporting, the device status word, and the sparse attention
+// dispatcher (tensor-core kernel for bf16 / D = 128, SIMT kernel otherwise).
+#include <cstdarg>
+#include <cstdio>
+#include <mutex>
+
+#include "common.cuh"
+#include "attn_common.cuh"
+
+namespace sb {
+
+static thread_local char g_error[1024] = "";
+
+void set_error(const char* fmt, ...) {
+  va_list args;
+  va_start(args, fmt);
+  vsnprintf(g_error, sizeof(g_error), fmt, args);
+  va_end(args);
+}
+
+int cuda_error(cudaError_t err, const char* what) {
+  set_error("%s: %s (%s)", what, cudaGetErrorString(err), cudaGetErrorName(err));
+  return SB_ERR_CUDA;
+}
+
+// Written by kernels whose waits gave up (value = a site code), read by
+// sb_read_device_status.  One copy per device that loads the library.
+__device__ int g_device_status;
+
+int* device_status_ptr() {
+  static std::mutex mu;
+  static int* cached[64] = {nullptr};
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return nullptr;
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* ptr = nullptr;
+    if (cudaGetSymbolAddress(&ptr, g_device_status) != cudaSuccess) return nullptr;
+    cached[dev] = static_cast<int*>(ptr);
+  }
+  return cached[dev];
+}
+
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" int sb_version(void) { return 100; }
+
+extern "C" const char* sb_last_error(void) { return g_error; }
+
+extern "C" int sb_read_device_status(void* stream) {
+  int* ptr = device_status_ptr();
+  if (ptr == nullptr) return cuda_error(cudaGetLastError(), "sb_read_device_status: symbol address");
+  cudaStream_t s = (cudaStream_t)stream;
+  int value = 0;
+  cudaError_t err = cudaMemcpyAsync(&value, ptr, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err != cudaSuccess) return cuda_error(err, "sb_read_device_status: read");
+  const int zero = 0;
+  err = cudaMemcpyAsync(ptr, &zero, sizeof(int), cudaMemcpyHostToDevice, s);
+  if (err == cudaSuccess) err = cudaStreamSynchronize(s);
+  if (err != cudaSuccess) return cuda_error(err, "sb_read_device_status: clear");
+  return value;
+}
+
+extern "C" int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype, int B,
+                                   int T, int H, int D, int block, const int32_t* packed_route,
+                                   int QB, const void* ak, const void* av, const float* lm,
+                                   int query_tokens, int sink_first, int sink_last,
+                                   int local_radius, void* out, float* lse, void* stream) {
+  SB_CHECK_ARG(q && k && v && out, "sb_sparse_attention: null Q/K/V/out");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_sparse_attention: bad dtype");
+  SB_CHECK_ARG(B > 0 && T > 0 && H > 0, "sb_sparse_attention: B, T, H must be positive");
+  SB_CHECK_ARG(D == 64 || D == 128, "sb_sparse_attention: head dim must be 64 or 128, got %d", D);
+  SB_CHECK_ARG(block == 64 || block == 128, "sb_sparse_attention: block must be 64 or 128, got %d", block);
+  SB_CHECK_ARG(T <= (1 << 22), "sb_sparse_attention: at most 4194304 tokens are supported");
+  SB_CHECK_ARG(query_tokens >= 0 && query_tokens <= T && query_tokens % block == 0,
+               "sb_sparse_attention: query_tokens must be a block multiple in [0, T], got %d", query_tokens);
+  const int NB = ceil_div(T, block);
+  const int routed_blocks = query_tokens / block;
+  if (routed_blocks > 0) {
+    SB_CHECK_ARG(packed_route && ak && av && lm, "sb_sparse_attention: routed queries need the route and summaries");
+    SB_CHECK_ARG(QB >= routed_blocks && QB <= NB, "sb_sparse_attention: QB (%d) must lie in [%d, %d]", QB, routed_blocks, NB);
+  }
+  SB_CHECK_ARG(sink_first >= 0 && sink_first <= sink_last && sink_last <= NB,
+               "sb_sparse_attention: sink range [%d, %d) is outside [0, %d]", sink_first, sink_last, NB);
+  SB_CHECK_ARG(local_radius >= -1, "sb_sparse_attention: local_radius must be >= -1");
+  const uintptr_t mis = (uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out |
+                        (uintptr_t)ak | (uintptr_t)av;
+  SB_CHECK_ARG(mis % 16 == 0, "sb_sparse_attention: tensors must be 16-byte aligned");
+  AttnParams p{};
+  p.q = q; p.k = k; p.v = v; p.packed = packed_route; p.ak = ak; p.av = av; p.lm = lm;
+  p.out = out; p.lse = lse;
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return cuda_error(cudaGetLastError(), "sb_sparse_attention: status word");
+  p.B = B; p.T = T; p.H = H; p.block = block; p.NB = NB; p.QB = QB; p.words = ceil_div(NB, 32);
+  p.query_tokens = query_tokens; p.sink_first = sink_first; p.sink_last = sink_last;
+  p.local_radius = local_radius;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SB_BF16 && D == 128) return launch_sparse_attention_sm100(p, s);
+  return launch_sparse_attention_simt(p, dtype, D, s);
+}

@@ -1,0 +1,72 @@
+"""ctypes binding of the C ABI declared in include/spark_h3_b200.h.
+
+Loading fails loudly when the shared library is missing: there is no CPU or Python
+fallback for any entry point.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+
+from . import _build
+
+F32 = 0
+BF16 = 1
+
+_lock = threading.Lock()
+_lib = None
+
+_vp = ctypes.c_void_p
+_i = ctypes.c_int
+_f = ctypes.c_float
+_i64 = ctypes.c_int64
+
+# name -> (restype, argtypes); mirrors include/spark_h3_b200.h exactly.
+SIGNATURES = {
+    "sb_version": (_i, []),
+    "sb_last_error": (ctypes.c_char_p, []),
+    "sb_read_device_status": (_i, [_vp]),
+    "sb_pool_queries": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
+    "sb_query_anchor": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
+    "sb_pool_keys_summaries": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    "sb_route_workspace_bytes": (_i64, [_i, _i, _i, _i]),
+    "sb_route_topk": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
+    "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
+                                 _vp, _vp, _vp]),
+    "sb_headwise_permute": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+}
+
+
+class SparkKernelError(RuntimeError):
+    """A C-ABI call returned a negative status."""
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    global _lib
+    with _lock:
+        if _lib is not None:
+            return _lib
+        path = _build.LIB_PATH
+        if not path.exists():
+            if not build_if_missing:
+                raise RuntimeError(f"spark_h3_b200 native library is missing: {path}")
+            _build.build()
+        lib = ctypes.CDLL(str(path))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(lib, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = lib
+        return lib
+
+
+def check(status: int, what: str) -> None:
+    if status < 0:
+        message = load().sb_last_error().decode(errors="replace")
+        raise SparkKernelError(f"{what} failed ({status}): {message}")
+
+
+def call(name: str, *args) -> int:
+    status = getattr(load(), name)(*args)
+    check(status, name)
+    return status

@@ -1,0 +1,197 @@
+"""Tensor-level wrappers over the C ABI.  Every op runs on the GPU through
+libsparkh3b200.so; a non-CUDA tensor is an error, never a fallback."""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import _lib
+
+LOG2E = 1.4426950408889634
+
+
+def _dtype_code(t: torch.Tensor) -> int:
+    if t.dtype == torch.bfloat16:
+        return _lib.BF16
+    if t.dtype == torch.float32:
+        return _lib.F32
+    raise TypeError(f"spark_h3_b200 supports float32 and bfloat16 tensors, got {t.dtype}")
+
+
+def _require_cuda(*tensors: torch.Tensor) -> torch.device:
+    device = None
+    for t in tensors:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise RuntimeError("spark_h3_b200 kernels require CUDA tensors; there is no CPU path")
+        if not t.is_contiguous():
+            raise RuntimeError("spark_h3_b200 kernels require contiguous tensors")
+        if device is None:
+            device = t.device
+        elif t.device != device:
+            raise RuntimeError("all tensors must be on the same CUDA device")
+    return device
+
+
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def scale_log2(head_dim: int) -> float:
+    return float(torch.tensor(head_dim ** -0.5 * LOG2E, dtype=torch.float32))
+
+
+def target_topk(topk_ratio: float, candidates: int) -> int:
+    """max(1, round(ratio * candidates)), capped at the candidate count
+    (h3_sparse_attention/sol_topk_cutoff.py:342, spark_integration.py:132)."""
+    return min(max(1, round(topk_ratio * candidates)), candidates)
+
+
+def pool_queries(q: torch.Tensor, block: int) -> torch.Tensor:
+    device = _require_cuda(q)
+    B, T, H, D = q.shape
+    nb = math.ceil(T / block)
+    qc = torch.empty((B, nb, H, D), device=device, dtype=torch.float32)
+    with torch.cuda.device(device):
+        _lib.call("sb_pool_queries", q.data_ptr(), _dtype_code(q), B, T, H, D, block, qc.data_ptr(), _stream(device))
+    return qc
+
+
+def query_anchor(qc: torch.Tensor, block: int, prefix_blocks: int, dtype: torch.dtype) -> torch.Tensor:
+    device = _require_cuda(qc)
+    B, NB, H, D = qc.shape
+    anchor = torch.empty((B, H, D), device=device, dtype=dtype)
+    with torch.cuda.device(device):
+        _lib.call("sb_query_anchor", qc.data_ptr(), B, NB, H, D, block, prefix_blocks, anchor.data_ptr(),
+                  _dtype_code(anchor), _stream(device))
+    return anchor
+
+
+def pool_keys_summaries(k: torch.Tensor, v: torch.Tensor | None, anchor: torch.Tensor | None, block: int, *,
+                        weighted_kv: bool = True, mass_bias: bool = True, want_kc: bool = True,
+                        want_summaries: bool = True):
+    """Returns (kc, ak, av, lm); entries not requested are None."""
+    device = _require_cuda(k, v, anchor)
+    B, T, H, D = k.shape
+    nb = math.ceil(T / block)
+    kc = torch.empty((B, nb, H, D), device=device, dtype=k.dtype) if want_kc else None
+    ak = av = lm = None
+    if want_summaries:
+        if v is None or v.shape != k.shape or v.dtype != k.dtype:
+            raise ValueError("summaries need V with the shape and dtype of K")
+        ak = torch.empty((B, H, nb, D), device=device, dtype=k.dtype)
+        av = torch.empty_like(ak)
+        lm = torch.empty((B, H, nb), device=device, dtype=torch.float32)
+    anchor_code = _dtype_code(anchor) if anchor is not None else _dtype_code(k)
+    with torch.cuda.device(device):
+        _lib.call("sb_pool_keys_summaries", k.data_ptr(), _ptr(v), _ptr(anchor), _dtype_code(k), anchor_code,
+                  B, T, H, D, block, int(weighted_kv), int(mass_bias), _ptr(kc), _ptr(ak), _ptr(av), _ptr(lm),
+                  _stream(device))
+    return kc, ak, av, lm
+
+
+def route_workspace_bytes(B: int, query_blocks: int, H: int, candidates: int) -> int:
+    return int(_lib.load().sb_route_workspace_bytes(B, query_blocks, H, candidates))
+
+
+def route_topk(qc: torch.Tensor, kc: torch.Tensor, query_blocks: int, candidates: int, topk: int, *,
+               workspace: torch.Tensor | None = None, want_indices: bool = True):
+    """Packed route [B, QB, H, ceil(NB/32)] int32 and ascending indices [B, QB, H, topk]."""
+    device = _require_cuda(qc, kc, workspace)
+    B, NB, H, D = qc.shape
+    words = math.ceil(NB / 32)
+    need = route_workspace_bytes(B, query_blocks, H, candidates)
+    if workspace is None:
+        workspace = torch.empty(need, device=device, dtype=torch.uint8)
+    elif workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"route workspace holds {workspace.numel() * workspace.element_size()} bytes, needs {need}")
+    packed = torch.empty((B, query_blocks, H, words), device=device, dtype=torch.int32)
+    indices = torch.empty((B, query_blocks, H, topk), device=device, dtype=torch.int32) if want_indices else None
+    with torch.cuda.device(device):
+        _lib.call("sb_route_topk", qc.data_ptr(), kc.data_ptr(), _dtype_code(kc), B, query_blocks, NB, H, D,
+                  candidates, topk, scale_log2(D), workspace.data_ptr(), packed.data_ptr(), _ptr(indices),
+                  _stream(device))
+    return packed, indices
+
+
+def sparse_attention(q, k, v, block: int, packed: torch.Tensor | None, ak, av, lm, *, query_tokens: int,
+                     sink_first: int, sink_last: int, local_radius: int = -1, out: torch.Tensor | None = None,
+                     want_lse: bool = False):
+    device = _require_cuda(q, k, v, packed, ak, av, lm, out)
+    B, T, H, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape or k.dtype != q.dtype or v.dtype != q.dtype:
+        raise ValueError("Q, K and V must share shape and dtype")
+    if out is None:
+        out = torch.empty_like(q)
+    lse = torch.empty((B, T, H), device=device, dtype=torch.float32) if want_lse else None
+    QB = packed.shape[1] if packed is not None else 0
+    with torch.cuda.device(device):
+        _lib.call("sb_sparse_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, T, H, D,
+                  block, _ptr(packed), QB, _ptr(ak), _ptr(av), _ptr(lm), query_tokens, sink_first, sink_last,
+                  local_radius, out.data_ptr(), _ptr(lse), _stream(device))
+    return out, lse
+
+
+def headwise_permute(x: torch.Tensor, permutation: torch.Tensor, video_tokens: int,
+                     out: torch.Tensor | None = None) -> torch.Tensor:
+    """dst[b, t, h] = x[b, perm[b, h, t], h] for t < video_tokens; identity after."""
+    device = _require_cuda(x, permutation, out)
+    B, T, H, D = x.shape
+    if permutation.shape != (B, H, video_tokens):
+        raise ValueError(f"permutation must have shape {(B, H, video_tokens)}, got {tuple(permutation.shape)}")
+    if permutation.dtype not in (torch.int32, torch.int64):
+        raise TypeError("permutation must be int32 or int64")
+    if out is None:
+        out = torch.empty_like(x)
+    with torch.cuda.device(device):
+        _lib.call("sb_headwise_permute", x.data_ptr(), out.data_ptr(), permutation.data_ptr(),
+                  permutation.element_size(), B, T, H, D, x.element_size(), video_tokens, _stream(device))
+    return out
+
+
+def read_device_status(device: torch.device | None = None) -> int:
+    """Site code of the last bounded wait that gave up (0 = none); clears it.  Syncs."""
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    with torch.cuda.device(device):
+        status = _lib.load().sb_read_device_status(_stream(device))
+    _lib.check(min(status, 0), "sb_read_device_status")
+    return status
+
+
+def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int = 128, topk_ratio: float = 0.1,
+                video_tokens: int | None = None, anchor_dtype: torch.dtype | None = None, local_radius: int = -1,
+                weighted_kv: bool = True, mass_bias: bool = True, workspace: torch.Tensor | None = None,
+                out: torch.Tensor | None = None, return_route: bool = False):
+    """One Spark sparse attention layer on BTHD tensors whose video prefix comes first.
+
+    pool Q -> anchor -> pool K + summaries -> scores + Top-K -> sparse attention
+    (rows past the last complete video block are attended densely by the same kernel).
+    """
+    B, T, H, D = q.shape
+    video = T if video_tokens is None else int(video_tokens)
+    if not block <= video <= T:
+        raise ValueError(f"video_tokens must lie in [{block}, {T}]")
+    query_blocks = video // block
+    query_tokens = query_blocks * block
+    candidates = video // block
+    nb = math.ceil(T / block)
+    sink_first = video // block
+    sink_last = nb if T > video else sink_first
+    topk = target_topk(topk_ratio, candidates)
+    qc = pool_queries(q, block)
+    anchor = query_anchor(qc, block, query_blocks, anchor_dtype or q.dtype)
+    kc, ak, av, lm = pool_keys_summaries(k, v, anchor, block, weighted_kv=weighted_kv, mass_bias=mass_bias)
+    packed, indices = route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace,
+                                 want_indices=return_route)
+    o, _ = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens=query_tokens, sink_first=sink_first,
+                            sink_last=sink_last, local_radius=local_radius, out=out)
+    if return_route:
+        return o, dict(qc=qc, kc=kc, anchor=anchor, ak=ak, av=av, lm=lm, packed=packed, indices=indices,
+                       topk=topk, query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last)
+    return o

@@ -1,0 +1,166 @@
+"""GPU parity of every hot-path kernel against the CPU oracle (bit-exact for integer
+outputs and block means, within stated tolerances for floating-point outputs)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from spark_h3_b200 import ops
+from spark_h3_b200.synthetic import make_qkv
+
+pytestmark = pytest.mark.gpu
+
+# bf16 attention tolerance (north star): max-abs <= 2e-2 and cosine >= 0.9995.
+BF16_MAX_ABS = 2e-2
+BF16_MIN_COS = 0.9995
+F32_MAX_ABS = 1e-4
+
+
+def to_oracle(t: torch.Tensor) -> oracle.Tensor:
+    t = t.detach().cpu().contiguous()
+    if t.dtype == torch.bfloat16:
+        return oracle.Tensor(t.view(torch.int16).numpy().view(np.uint16), "bfloat16")
+    return oracle.Tensor(t.numpy(), "float32")
+
+
+def as_np(t: torch.Tensor) -> np.ndarray:
+    return t.detach().float().cpu().numpy()
+
+
+def cosine(a: np.ndarray, b: np.ndarray) -> float:
+    a = a.astype(np.float64).ravel()
+    b = b.astype(np.float64).ravel()
+    return float(a @ b / (np.linalg.norm(a) * np.linalg.norm(b)))
+
+
+CASES = [
+    # (grid, heads, head_dim, dtype, block, q_scale)
+    ((4, 32, 32), 4, 64, torch.float32, 64, 1.0),              # config 0 shape
+    ((4, 16, 33), 2, 128, torch.bfloat16, 128, 128 ** -0.5),   # partial 128-block tail
+    ((3, 16, 32), 2, 128, torch.bfloat16, 64, 128 ** -0.5),    # 64-token blocks on tensor cores
+]
+
+
+@pytest.mark.parametrize("grid,heads,head_dim,dtype,block,q_scale", CASES)
+def test_route_is_bit_exact(cuda_device, grid, heads, head_dim, dtype, block, q_scale):
+    q, k, v = make_qkv(grid, heads, head_dim, seed=3, dtype=dtype, q_scale=q_scale)
+    oq, ok_, ov = to_oracle(q), to_oracle(k), to_oracle(v)
+    ref = oracle.spark_layer(oq, ok_, ov, block=block, topk_ratio=0.1, attention=False)
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, return_route=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(as_np(route["qc"]), ref["qc"])
+    np.testing.assert_array_equal(as_np(route["kc"]), ref["kc"])
+    np.testing.assert_array_equal(as_np(route["anchor"]), ref["anchor"])
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    np.testing.assert_array_equal(route["packed"].cpu().numpy(), ref["packed"])
+    assert route["topk"] == ref["topk"]
+
+
+@pytest.mark.parametrize("grid,heads,head_dim,dtype,block,q_scale", CASES)
+def test_summaries_match_oracle(cuda_device, grid, heads, head_dim, dtype, block, q_scale):
+    q, k, v = make_qkv(grid, heads, head_dim, seed=5, dtype=dtype, q_scale=q_scale)
+    anchor = ops.query_anchor(ops.pool_queries(q.to(cuda_device), block), block,
+                              q.shape[1] // block, dtype)
+    _, ak, av, lm = ops.pool_keys_summaries(k.to(cuda_device), v.to(cuda_device), anchor, block)
+    ref_ak, ref_av, ref_lm = oracle.summaries(as_np(anchor), to_oracle(k), to_oracle(v), block)
+    tol = 1.6e-2 if dtype == torch.bfloat16 else 1e-5
+    np.testing.assert_allclose(as_np(ak), ref_ak, atol=tol, rtol=tol)
+    np.testing.assert_allclose(as_np(av), ref_av, atol=tol, rtol=tol)
+    np.testing.assert_allclose(as_np(lm), ref_lm, atol=2e-3 if dtype == torch.bfloat16 else 1e-5, rtol=1e-3)
+
+
+def _attention_case(cuda_device, grid, heads, head_dim, dtype, block, q_scale, *, video=None, local_radius=-1,
+                    seed=7):
+    q, k, v = make_qkv(grid, heads, head_dim, seed=seed, dtype=dtype, q_scale=q_scale)
+    T = q.shape[1]
+    video = T if video is None else video
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             video_tokens=video, local_radius=local_radius)
+    dev = cuda_device
+    packed = torch.from_numpy(ref["packed"]).to(dev)
+    cast = lambda a: torch.from_numpy(np.ascontiguousarray(a)).to(dev, dtype)
+    ak, av = cast(ref["ak"]), cast(ref["av"])
+    lm = torch.from_numpy(ref["lm"]).to(dev)
+    out, lse = ops.sparse_attention(q.to(dev), k.to(dev), v.to(dev), block, packed, ak, av, lm,
+                                    query_tokens=ref["query_tokens"], sink_first=ref["sink_first"],
+                                    sink_last=ref["sink_last"], local_radius=local_radius, want_lse=True)
+    torch.cuda.synchronize()
+    assert ops.read_device_status(dev) == 0
+    return as_np(out), as_np(lse), ref["out"], ref["lse"]
+
+
+def _check(out, ref, dtype):
+    assert np.isfinite(out).all()
+    err = np.abs(out - ref).max()
+    if dtype == torch.bfloat16:
+        assert err <= BF16_MAX_ABS, err
+        assert cosine(out, ref) >= BF16_MIN_COS
+    else:
+        assert err <= F32_MAX_ABS, err
+
+
+@pytest.mark.parametrize("grid,heads,head_dim,dtype,block,q_scale", CASES)
+def test_sparse_attention_matches_oracle(cuda_device, grid, heads, head_dim, dtype, block, q_scale):
+    out, lse, ref, ref_lse = _attention_case(cuda_device, grid, heads, head_dim, dtype, block, q_scale)
+    _check(out, ref, dtype)
+    np.testing.assert_allclose(lse, ref_lse, atol=2e-3 if dtype == torch.bfloat16 else 1e-5, rtol=1e-4)
+
+
+@pytest.mark.parametrize("block", [64, 128])
+def test_sparse_attention_context_sink_and_dense_suffix(cuda_device, block):
+    # 2112 video tokens followed by 150 context tokens: the context blocks are forced
+    # exact, and every row past the last complete video block is attended densely.
+    grid = (4, 16, 33)
+    q, k, v = make_qkv(grid, 2, 128, seed=11, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    extra = make_qkv((1, 10, 15), 2, 128, seed=12, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    q, k, v = (torch.cat((a, b), dim=1) for a, b in zip((q, k, v), extra))
+    T = q.shape[1]
+    video = 2112
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             video_tokens=video)
+    out = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block, topk_ratio=0.1,
+                          video_tokens=video)
+    torch.cuda.synchronize()
+    assert ref["sink_last"] > ref["sink_first"]
+    _check(as_np(out), ref["out"], torch.bfloat16)
+
+
+def test_sparse_attention_local_radius(cuda_device):
+    out, _, ref, _ = _attention_case(cuda_device, (3, 16, 32), 2, 128, torch.bfloat16, 64, 128 ** -0.5,
+                                     local_radius=1)
+    _check(out, ref, torch.bfloat16)
+
+
+def test_tensor_core_kernel_agrees_with_simt_kernel(cuda_device):
+    # The same bf16 problem through the sm100 kernel (D = 128) and through the SIMT kernel
+    # (fed float32 copies): both are GPU paths of the library and must agree.
+    q, k, v = make_qkv((2, 16, 40), 2, 128, seed=21, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    dev = cuda_device
+    out_tc, route = ops.spark_layer(q.to(dev), k.to(dev), v.to(dev), block=128, return_route=True)
+    f = lambda t: t.to(dev).float()
+    out_simt, _ = ops.sparse_attention(f(q), f(k), f(v), 128, route["packed"], route["ak"].float(),
+                                       route["av"].float(), route["lm"], query_tokens=route["query_tokens"],
+                                       sink_first=route["sink_first"], sink_last=route["sink_last"])
+    torch.cuda.synchronize()
+    _check(as_np(out_tc), as_np(out_simt), torch.bfloat16)
+
+
+def test_headwise_permute_roundtrip(cuda_device):
+    gen = torch.Generator().manual_seed(4)
+    B, T, H, D, video = 1, 1000, 3, 128, 900
+    x = torch.randn(B, T, H, D, generator=gen).to(torch.bfloat16)
+    perm = torch.stack([torch.randperm(video, generator=gen) for _ in range(H)])[None]
+    inv = torch.argsort(perm, dim=-1)
+    dev = cuda_device
+    y = ops.headwise_permute(x.to(dev), perm.to(dev), video)
+    z = ops.headwise_permute(y, inv.to(dev), video)
+    expected = x.clone()
+    for h in range(H):
+        expected[0, :video, h] = x[0, perm[0, h], h]
+    assert torch.equal(y.cpu(), expected)
+    assert torch.equal(z.cpu(), x)
+    y32 = ops.headwise_permute(x.to(dev), perm.to(dev).to(torch.int32), video)
+    assert torch.equal(y32.cpu(), expected)
