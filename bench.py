@@ -1,0 +1,379 @@
+"""Benchmark of one Spark-H3 sparse attention layer on B200.
+
+Workload: B=1, grid (31, 48, 84) -> N = 124,992 tokens, H = 32, D = 128, bf16, 128-token
+blocks, topk_ratio 0.1, anchor-weighted tail summaries with the log-mass correction, no
+reblock.  One step = pool Q -> anchor -> pool K + summaries -> block scores + Top-K ->
+sparse attention (the 64-row partial tail attends densely inside the same kernel).
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+With N > 1 (torchrun, one process per GPU) the 32 heads are split across ranks (strong
+scaling, no data-path collective); timing is the max over ranks.  `value` is the
+dense-equivalent throughput 4*N^2*H*D / time of the whole job.  `--impl reference` times
+the CPU restatement of the same layer (oracle/, the reference being a Python/Triton
+project that cannot run here) on a bounded sample and extrapolates to the full layer.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+for _p in (ROOT, ROOT / "spark-h3_b200"):
+    if str(_p) not in sys.path:
+        sys.path.insert(0, str(_p))
+
+METRIC = "sparse-attn ms/layer & eff. TFLOPS @N=125k,H=32,D=128,topk0.1; DiT step s/it"
+UNIT = "TFLOP/s (dense-equivalent 4*N^2*H*D per layer)"
+GRID = (31, 48, 84)
+HEADS = 32
+PROFILE_ONLY = False
+HEAD_DIM = 128
+BLOCK = 128
+TOPK_RATIO = 0.1
+
+
+def dense_flops(tokens: int, heads: int, dim: int) -> float:
+    return 4.0 * tokens * tokens * heads * dim
+
+
+def sparse_flops(tokens: int, heads: int, dim: int, block: int, topk: int) -> float:
+    """Algorithmic FLOPs of the sparse attention kernel: every routed query row sees topk
+    exact blocks plus one summary column per other key block; rows past the last complete
+    block attend every key."""
+    nb = math.ceil(tokens / block)
+    query_tokens = (tokens // block) * block
+    routed = 4.0 * query_tokens * heads * dim * (topk * block + (nb - topk))
+    dense = 4.0 * (tokens - query_tokens) * tokens * heads * dim
+    return routed + dense
+
+
+def load_peaks() -> dict:
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return dict(bf16=data.get("bf16_tflops_sustained") or data.get("bf16_tflops"), hbm=data.get("hbm_gbs"),
+                    source="MEASURED_PEAKS.json (bf16 sustained)")
+    return dict(bf16=1400.0, hbm=6650.0, source="fallback (1.4 PFLOP/s sustained, 6.65 TB/s)")
+
+
+class ClockSampler:
+    """nvidia-smi clock/throttle samples during the timed region."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+        return False
+
+    def summary(self) -> dict:
+        mhz, max_mhz, reasons = [], None, set()
+        names = ("hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap")
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                mhz.append(float(parts[1]))
+                max_mhz = float(parts[2])
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower().startswith("active"):
+                    reasons.add(name)
+        mhz.sort()
+        return dict(sm_mhz=mhz[len(mhz) // 2] if mhz else None, sm_max_mhz=max_mhz, reasons=sorted(reasons),
+                    samples=len(mhz))
+
+
+def cpu_baseline(sample_blocks: int = 96) -> dict:
+    """The CPU oracle on one head: full route + summaries, attention for `sample_blocks`
+    query blocks, extrapolated to all 977 blocks and 32 heads."""
+    import numpy as np
+    import torch
+
+    from oracle import oracle
+    from spark_h3_b200.synthetic import make_qkv
+
+    q, k, v = make_qkv(GRID, 1, HEAD_DIM, seed=0, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
+    host = lambda t: oracle.Tensor(t.contiguous().view(torch.int16).numpy().view(np.uint16), "bfloat16")
+    oq, ok_, ov = host(q), host(k), host(v)
+    T = q.shape[1]
+    nb = math.ceil(T / BLOCK)
+    qb = T // BLOCK
+    topk = oracle.target_topk(TOPK_RATIO, qb)
+    t0 = time.perf_counter()
+    qc = oracle.block_means(oq, BLOCK)
+    kc = oracle.key_means(ok_, BLOCK)
+    a = oracle.anchor(qc, BLOCK, qb, "bfloat16")
+    sc = oracle.scores(qc, kc, qb, qb)
+    _, packed = oracle.topk(sc, topk, nb)
+    ak, av, lm = oracle.summaries(a, ok_, ov, BLOCK)
+    t_route = time.perf_counter() - t0
+    t1 = time.perf_counter()
+    oracle.sparse_attention(oq, ok_, ov, BLOCK, packed, ak, av, lm, qb * BLOCK, qb, qb,
+                            rows=slice(0, sample_blocks * BLOCK))
+    t_attn = time.perf_counter() - t1
+    per_head = t_route + t_attn * nb / sample_blocks
+    layer_s = per_head * HEADS
+    return dict(value=dense_flops(T, HEADS, HEAD_DIM) / layer_s / 1e12, unit=UNIT, cores=os.cpu_count(),
+                kind="port", layer_seconds_extrapolated=layer_s,
+                sample=(f"1 of {HEADS} heads: full route+summaries ({t_route:.2f} s) and attention for "
+                        f"{sample_blocks} of {nb} query blocks ({t_attn:.2f} s); extrapolated x{nb}/{sample_blocks} "
+                        f"blocks and x{HEADS} heads; numpy/BLAS threads = all host cores"))
+
+
+def run_reference(args) -> None:
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    steps = []
+    base = None
+    for i in range(args.warmup + args.steps):
+        base = cpu_baseline(sample_blocks=args.reference_sample_blocks)
+        if i >= args.warmup:
+            steps.append(base["layer_seconds_extrapolated"])
+    layer_s = sorted(steps)[len(steps) // 2]
+    T = GRID[0] * GRID[1] * GRID[2]
+    value = dense_flops(T, HEADS, HEAD_DIM) / layer_s / 1e12
+    base["value"] = value
+    line = dict(metric=METRIC, value=value, unit=UNIT, impl="reference", n_gpus=args.gpus, steps=args.steps,
+                warmup=args.warmup, ms_per_step=layer_s * 1e3, higher_is_better=True, scaling="strong",
+                vs_baseline=None, dtype="bf16", data="synthetic",
+                config=dict(workload="config1: one sparse attention layer, N=124992 (31x48x84), H=32, D=128, "
+                                     "block 128, topk 0.1, reweight summaries", extrapolated=True),
+                cpu_baseline=base, e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
+    print(json.dumps(line), flush=True)
+
+
+def run_ours(args) -> None:
+    import torch
+    import torch.distributed as dist
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.synthetic import make_qkv
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+    if HEADS % world:
+        raise SystemExit("the head count must divide evenly across GPUs")
+    heads = HEADS // world
+    h0 = rank * heads
+
+    # Inputs: generated on the device (seeded), this rank's head shard made contiguous.
+    q, k, v = make_qkv(GRID, HEADS, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
+    q, k, v = (x[:, :, h0:h0 + heads].contiguous() for x in (q, k, v))
+    torch.cuda.synchronize()
+    T = q.shape[1]
+    nb = math.ceil(T / BLOCK)
+    qb = T // BLOCK
+    topk = ops.target_topk(TOPK_RATIO, qb)
+    workspace = torch.empty(ops.route_workspace_bytes(1, qb, heads, qb), device=dev, dtype=torch.uint8)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+
+    attn_events = []
+
+    def step(record: bool):
+        qc = ops.pool_queries(q, BLOCK)
+        anchor = ops.query_anchor(qc, BLOCK, qb, torch.bfloat16)
+        kc, ak, av, lm = ops.pool_keys_summaries(k, v, anchor, BLOCK)
+        packed, _ = ops.route_topk(qc, kc, qb, qb, topk, workspace=workspace, want_indices=False)
+        if record:
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+        ops.sparse_attention(q, k, v, BLOCK, packed, ak, av, lm, query_tokens=qb * BLOCK, sink_first=qb,
+                             sink_last=qb, out=out)
+        if record:
+            e1.record(stream)
+            attn_events.append((e0, e1))
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    for _ in range(args.warmup):
+        step(False)
+    barrier()
+    if ops.read_device_status(dev) != 0:
+        raise SystemExit("a kernel wait timed out during warm-up")
+
+    start, stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        start.record(stream)
+        for _ in range(args.steps):
+            step(True)
+        stop.record(stream)
+        barrier()
+    elapsed_ms = start.elapsed_time(stop)
+    attn_ms = sum(a.elapsed_time(b) for a, b in attn_events) / len(attn_events)
+    t = torch.tensor([elapsed_ms, attn_ms], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    elapsed_ms, attn_ms = float(t[0]), float(t[1])
+    ms_per_step = elapsed_ms / args.steps
+    total_dense = dense_flops(T, HEADS, HEAD_DIM)
+    value = total_dense / (ms_per_step * 1e-3) / 1e12
+    if PROFILE_ONLY:
+        if rank == 0:
+            print(json.dumps(dict(profile_case=True, grid=GRID, heads=HEADS, ms_per_step=ms_per_step,
+                                  attention_kernel_ms=attn_ms)), flush=True)
+        if world > 1:
+            dist.destroy_process_group()
+        return
+
+    # End to end through the public API with host buffers: H2D of Q/K/V from pinned memory,
+    # the layer, and D2H of the output, every step.
+    hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
+    hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
+
+    def e2e_step():
+        dq, dk, dv = (x.to(dev, non_blocking=True) for x in (hq, hk, hv))
+        o = ops.spark_layer(dq, dk, dv, block=BLOCK, topk_ratio=TOPK_RATIO, workspace=workspace)
+        hout.copy_(o, non_blocking=True)
+
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    barrier()
+    e_start, e_stop = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(1, min(args.steps, 5))
+    e_start.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e_stop.record(stream)
+    barrier()
+    t = torch.tensor([e_start.elapsed_time(e_stop) / e2e_steps], device=dev, dtype=torch.float64)
+    if world > 1:
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    e2e_ms = float(t[0])
+    h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv)) * world
+    d2h = hout.numel() * hout.element_size() * world
+
+    dense_sdpa_ms = None
+    if world == 1 and not args.no_dense:
+        from torch.nn.attention import SDPBackend, sdpa_kernel
+        qt, kt, vt = (x.transpose(1, 2) for x in (q, k, v))
+        try:
+            with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
+                torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
+                torch.cuda.synchronize()
+                d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                d0.record(stream)
+                for _ in range(2):
+                    torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
+                d1.record(stream)
+                torch.cuda.synchronize()
+                dense_sdpa_ms = d0.elapsed_time(d1) / 2
+        except RuntimeError as err:  # cuDNN backend unavailable
+            dense_sdpa_ms = f"unavailable: {err}".splitlines()[0][:200]
+
+    status = ops.read_device_status(dev)
+    if rank == 0:
+        peaks = load_peaks()
+        flops_launch = sparse_flops(T, heads, HEAD_DIM, BLOCK, topk)
+        achieved = flops_launch / (attn_ms * 1e-3) / 1e12
+        line = dict(
+            metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=ms_per_step, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
+            data="synthetic (seeded 8-sinusoid + 0.3 N(0,1) Q/K/V, Q scaled by 1/sqrt(D))",
+            config=dict(workload="config1: one sparse attention layer, N=124992 (31x48x84), H=32, D=128, block 128, "
+                                 "topk 0.1 (98 of 976 blocks), reweight summaries + LSE correction, no reblock",
+                        global_batch=1, seq_len=T, heads=HEADS, head_dim=HEAD_DIM, block=BLOCK, topk=topk,
+                        parallelism=f"heads/{world}" if world > 1 else "single GPU",
+                        l2="inputs (3 x 1.02 GB) exceed the 126 MB L2; no flush between steps"),
+            ms_per_layer=ms_per_step, attention_kernel_ms=attn_ms,
+            sparse_flops_per_layer=sparse_flops(T, HEADS, HEAD_DIM, BLOCK, topk),
+            dense_equivalent_flops_per_layer=total_dense,
+            dense_cudnn_sdpa_ms=dense_sdpa_ms,
+            speedup_vs_dense_sdpa=(dense_sdpa_ms / ms_per_step if isinstance(dense_sdpa_ms, float) else None),
+            roofline=dict(bound="tensor", kernel="sparse_attention_sm100_kernel", achieved=achieved,
+                          peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"], traffic=None,
+                          peak_source=peaks["source"],
+                          note="achieved = algorithmic sparse FLOPs per launch / mean CUDA-event launch time"),
+            e2e=dict(value=total_dense / (e2e_ms * 1e-3) / 1e12, unit=UNIT, ms_per_step=e2e_ms,
+                     h2d_bytes_per_step=h2d, d2h_bytes_per_step=d2h,
+                     path="spark_h3_b200.ops.spark_layer on pinned host Q/K/V, output copied back"),
+            gpu_launches=6 * args.steps,
+            clocks=clocks.summary(),
+            device_status=status,
+        )
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(sample_blocks=args.cpu_sample_blocks)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
+    ap.add_argument("--no-dense", action="store_true", help="skip the dense cuDNN SDPA comparison")
+    ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle baseline")
+    ap.add_argument("--cpu-sample-blocks", type=int, default=96,
+                    help="query blocks of the one-head CPU attention sample behind cpu_baseline")
+    ap.add_argument("--grid", type=str, default=None,
+                    help="T,H,W token grid for a smaller profiling case (default 31,48,84)")
+    ap.add_argument("--heads", type=int, default=None, help="head count for a smaller profiling case")
+    ap.add_argument("--profile-only", action="store_true",
+                    help="run only the device-resident steps (for ncu captures of a small case)")
+    ap.add_argument("--reference-sample-blocks", type=int, default=16,
+                    help="query blocks of the one-head CPU attention sample of each --impl reference step")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)  # at least three untimed warm-up steps
+    global GRID, HEADS, PROFILE_ONLY
+    if args.grid:
+        GRID = tuple(int(x) for x in args.grid.split(","))
+    if args.heads:
+        HEADS = args.heads
+    PROFILE_ONLY = args.profile_only
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

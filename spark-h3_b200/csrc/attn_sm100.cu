@@ -1,19 +1,24 @@
 // Sparse attention forward on the 5th-generation tensor cores (sm_100a), bf16, D = 128.
 //
-// One CTA per (128-row query tile, head, batch).  Roles:
-//   warps 0-3  softmax: thread r owns query row r of the tile (TMEM lane r)
-//   warp 4     TMA producer: Q once, then K/V tiles of the exact key blocks, then
+// One CTA per (128-row query tile, head, batch).  Roles (320 threads):
+//   warps 0-3  softmax group 0: row r = TMEM lane r, key columns 0-63 of every tile
+//   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
+//   warp 8     TMA producer: Q once, then K/V tiles of the exact key blocks, then the
 //              AK/AV summary tiles
-//   warp 5     tcgen05 issuer; also owns the TMEM allocation
-// TMEM (512 columns): S/P double buffer at columns [0,128) and [128,256), O at [256,384).
-// P overwrites the first 64 columns of its S buffer as packed bf16 pairs and feeds the
-// P.V product directly from TMEM.
+//   warp 9     tcgen05 issuer; owns the TMEM allocation
+// TMEM (512 columns): S double buffer at [0,128) and [128,256); O_A at [256,384) and
+// O_B at [384,512).  Each softmax group keeps its own running max, sum and output
+// accumulator (O_A += P_A V[0:64), O_B += P_B V[64:128)), so the groups never
+// synchronise inside the key loop; the epilogue merges the two partial softmaxes.
+// P is written back over the group's own S columns as packed bf16 pairs and feeds the
+// P.V product straight from TMEM.
 //
 // A query tile is two 64-row halves; each half has its own exact key-block set (with
 // 64-row blocks the halves are different query blocks).  Exact work is enumerated in
-// 64-key granules over the union of both halves' sets, two granules per 128-key tile,
-// with per-half visibility masks.  Summary tiles cover 128 summary entries (one per key
-// block) each; an entry is visible to a half when its block is not exact for that half.
+// 64-key granules over the union of both halves' sets, two granules per 128-key tile;
+// softmax group g handles granule slot g, so its visibility is one flag per row half.
+// Summary tiles cover 128 summary entries (one per key block); an entry is visible to
+// a half when its block is not exact for that half.
 #include "common.cuh"
 #include "attn_common.cuh"
 #include "sm100_ptx.cuh"
@@ -23,24 +28,31 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
+constexpr int kProducerWarp = 8;
+constexpr int kMmaWarp = 9;
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 bf16 operand tile
 constexpr int kHalfBytes = 128 * 64 * 2;   // one 64-column half of it
 constexpr int kBoxBytes = 64 * 64 * 2;     // one TMA box (64 columns x 64 rows)
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kColO = 256;
+constexpr uint32_t kColOA = 256;
+constexpr uint32_t kColOB = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: lazy O rescale
 
 struct __align__(8) Control {
   uint64_t bar_q_full;
   uint64_t bar_k_full[2], bar_k_empty[2];
   uint64_t bar_v_full[2], bar_v_empty[2];
-  uint64_t bar_s_full[2], bar_p_full[2];
-  uint64_t bar_o_done, bar_o_final;
+  uint64_t bar_s_full[2];
+  uint64_t bar_p_full[2][2];  // [group][stage]
+  uint64_t bar_o_done[2];     // [group]
+  uint64_t bar_o_final;
   uint32_t tmem_base;
   int abort_flag;
   int exact_granules;
   int has_summary;
+  float merge_m[2][128];
+  float merge_l[2][128];
 };
 
 // Walks the set bits of the granule bitset in ascending order.
@@ -85,6 +97,31 @@ __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran)
   return L;
 }
 
+// 2^x on the FMA/ALU pipes (offloads the MUFU unit): round-to-nearest range reduction
+// x = j + f with f in [-0.5, 0.5], a degree-3 polynomial for 2^f (least-squares fit on
+// Chebyshev nodes, max relative error 2.2e-4, below bf16 rounding), and j added to the
+// exponent field.  Inputs below -126 give a value below 2^-125 (effectively zero).
+__device__ __forceinline__ float exp2_poly(float x) {
+  x = fmaxf(x, -126.f);
+  const float shifter = 12582912.f;  // 1.5 * 2^23: rounds x to an integer in the mantissa
+  const float t = x + shifter;
+  const float j = t - shifter;
+  const float f = x - j;
+  float p = fmaf(0.05294328f, f, 0.24218228f);
+  p = fmaf(p, f, 0.6935803f);
+  p = fmaf(p, f, 0.99996096f);
+  return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
+  __nv_bfloat162 pair = __floats2bfloat162_rn(lo, hi);
+  return *reinterpret_cast<uint32_t*>(&pair);
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
 __global__ void __launch_bounds__(kThreads, 1)
 sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                               const __grid_constant__ CUtensorMap tm_k,
@@ -118,19 +155,20 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_init(smem_u32(&C.bar_v_full[s]), 1);
       mbar_init(smem_u32(&C.bar_v_empty[s]), 1);
       mbar_init(smem_u32(&C.bar_s_full[s]), 1);
-      mbar_init(smem_u32(&C.bar_p_full[s]), 128);
+      mbar_init(smem_u32(&C.bar_p_full[0][s]), 128);
+      mbar_init(smem_u32(&C.bar_p_full[1][s]), 128);
+      mbar_init(smem_u32(&C.bar_o_done[s]), 1);
     }
-    mbar_init(smem_u32(&C.bar_o_done), 1);
     mbar_init(smem_u32(&C.bar_o_final), 1);
     C.abort_flag = 0;
     C.exact_granules = 0;
     fence_barrier_init();
   }
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tmem_alloc(smem_u32(&C.tmem_base), kTmemCols);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) {
+  if (warp == kProducerWarp && lane == 0) {
     prefetch_tensormap(&tm_q);
     prefetch_tensormap(&tm_k);
     prefetch_tensormap(&tm_v);
@@ -201,7 +239,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   const uint32_t sK[2] = {base + L.k0, base + L.k1};
   const uint32_t sV[2] = {base + L.v0, base + L.v1};
 
-  if (warp == 4) {
+  if (warp == kProducerWarp) {
     // ------------------------------------------------------------ producer
     if (lane == 0) {
       const uint32_t bq = smem_u32(&C.bar_q_full);
@@ -257,7 +295,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       mbar_drain(bq, 0);
     }
-  } else if (warp == 5) {
+  } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 128, false);
@@ -266,15 +304,19 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       auto issue_pv = [&](int i) -> bool {
         const int s = i & 1;
         const uint32_t par = (i >> 1) & 1;
-        if (!mbar_wait(smem_u32(&C.bar_p_full[s]), par, abort_flag, p.status, 202)) return false;
         if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) return false;
-        tc_fence_after();
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t bdesc = smem_desc_sw128(sV[s] + kk * 2048, kHalfBytes, 1024);
-          mma_ts(tmem + kColO, tmem + s * 128 + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+        for (int g = 0; g < 2; ++g) {
+          if (!mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) return false;
+          tc_fence_after();
+          const uint32_t o_col = g ? kColOB : kColOA;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk) {
+            const uint64_t bdesc = smem_desc_sw128(sV[s] + (4 * g + kk) * 2048, kHalfBytes, 1024);
+            mma_ts(tmem + o_col, tmem + s * 128 + 64 * g + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&C.bar_o_done[g]));
         }
         tc_commit(smem_u32(&C.bar_v_empty[s]));
-        tc_commit(smem_u32(&C.bar_o_done));
         return true;
       };
       for (int j = 0; ok && j < total_tiles; ++j) {
@@ -285,6 +327,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           break;
         }
         tc_fence_after();
+#pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
           const uint64_t adesc = smem_desc_sw128(sQ + off, 16, 1024);
@@ -300,10 +343,13 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
   } else {
     // --------------------------------------------------------------- softmax
-    const int row = tid;  // 0..127, TMEM lane
+    const int grp = warp >> 2;        // 0: key columns 0-63, 1: key columns 64-127
+    const int row = tid & 127;        // TMEM lane = query row of the tile
     const int half = row >> 6;
     const int grow = row0 + row;
-    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
+    const uint32_t s_col = 64 * grp;  // this group's S / P columns inside a buffer
+    const uint32_t o_col = grp ? kColOB : kColOA;
     const uint32_t* ehalf = ebits + half * words_blk;
     const float scale_log2 = 0.08838834764831845f * kLog2e;
     const float* lm_row = p.lm ? p.lm + ((int64_t)b * p.H + h) * p.NB : nullptr;
@@ -315,10 +361,20 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       const int s = j & 1;
       const uint32_t par = (j >> 1) & 1;
       const bool exact = j < exact_tiles;
-      int g0 = 0, g1 = -1;
+      // Visibility of this group's 64 keys for this row half.
+      bool vis = true, masked = false;
+      int key0 = 0;
       if (exact) {
-        g0 = walk.next();
-        g1 = walk.next();
+        const int g0 = walk.next();
+        const int g1 = walk.next();
+        const int g = grp ? g1 : g0;
+        vis = g >= 0;
+        if (vis) {
+          const int kb = g * 64 / p.block;
+          vis = (ehalf[kb >> 5] >> (kb & 31)) & 1u;
+          key0 = g * 64;
+          masked = key0 + 64 > p.T;
+        }
       }
       const bool got_s = mbar_wait(smem_u32(&C.bar_s_full[s]), par, abort_flag, p.status, 301);
       if (!__all_sync(0xffffffffu, got_s)) {
@@ -326,58 +382,36 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         break;
       }
       tc_fence_after();
-      float x[128];
-      {
-        uint32_t r[128];
-#pragma unroll
-        for (int c = 0; c < 4; ++c) tmem_ld32(tmem + lane_base + s * 128 + 32 * c, r + 32 * c);
-        tmem_wait_ld();
-#pragma unroll
-        for (int i = 0; i < 128; ++i) x[i] = __uint_as_float(r[i]);
-      }
+      uint32_t r[64];
       float tile_max = -INFINITY;
-      if (exact) {
-        bool vis[2];
-        int key0[2];
-        const int gs[2] = {g0, g1};
-#pragma unroll
-        for (int slot = 0; slot < 2; ++slot) {
-          const int g = gs[slot];
-          bool v = g >= 0;
-          if (v) {
-            const int kb = g * 64 / p.block;
-            v = (ehalf[kb >> 5] >> (kb & 31)) & 1u;
-          }
-          vis[slot] = v;
-          key0[slot] = g * 64;
-        }
-#pragma unroll
-        for (int c = 0; c < 128; ++c) {
-          const int slot = c >> 6;
-          const bool visible = vis[slot] && (key0[slot] + (c & 63) < p.T);
-          const float val = visible ? x[c] * scale_log2 : -INFINITY;
-          x[c] = val;
-          tile_max = fmaxf(tile_max, val);
-        }
-      } else {
-        const int e0 = (j - exact_tiles) * 128;
-#pragma unroll
-        for (int wq = 0; wq < 4; ++wq) {
-          const int e_base = e0 + 32 * wq;
-          const uint32_t ex = e_base < p.NB ? ehalf[e_base >> 5] : 0xffffffffu;
-#pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int c = 32 * wq + i;
-            const int ee = e_base + i;
-            const bool visible = ee < p.NB && !((ex >> i) & 1u);
-            const float bias = visible ? __ldg(lm_row + ee) * kLog2e : 0.f;
-            const float val = visible ? fmaf(x[c], scale_log2, bias) : -INFINITY;
-            x[c] = val;
-            tile_max = fmaxf(tile_max, val);
-          }
-        }
+      const bool any_vis = __any_sync(0xffffffffu, vis || !exact);
+      if (any_vis) {
+        tmem_ld32(tmem + lane_base + s * 128 + s_col, r);
+        tmem_ld32(tmem + lane_base + s * 128 + s_col + 32, r + 32);
+        tmem_wait_ld();
       }
-      // Lazy rescale: only when the running max grows by more than the threshold.
+      // Masked logit of column i (summary tiles add LM * log2(e); invisible -> -inf).
+      const int e0 = (j - exact_tiles) * 128 + (int)s_col;
+      auto logit = [&](int i) -> float {
+        if (!exact) {
+          const int e = e0 + i;
+          const uint32_t ex = e < p.NB ? ehalf[e >> 5] : 0xffffffffu;
+          const bool visible = e < p.NB && !((ex >> (e & 31)) & 1u);
+          return visible ? fmaf(__uint_as_float(r[i]), scale_log2, __ldg(lm_row + e) * kLog2e) : -INFINITY;
+        }
+        return key0 + i < p.T ? __uint_as_float(r[i]) * scale_log2 : -INFINITY;
+      };
+      if (exact && vis && !masked) {
+        float raw = -INFINITY;
+#pragma unroll
+        for (int i = 0; i < 64; ++i) raw = fmaxf(raw, __uint_as_float(r[i]));
+        tile_max = raw * scale_log2;
+      } else if (!exact || vis) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) tile_max = fmaxf(tile_max, logit(i));
+      }
+      // Lazy rescale of this group's O: only when the running max grows by more than
+      // the threshold (or becomes finite for the first time).
       const float m_new = fmaxf(m_run, tile_max);
       const bool need = (m_new > m_run + kRescaleThreshold) || (m_run == -INFINITY && m_new != -INFINITY);
       float alpha = 1.f;
@@ -386,74 +420,107 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         m_run = m_new;
       }
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        const bool got_o = mbar_wait(smem_u32(&C.bar_o_done), (uint32_t)((j - 1) & 1), abort_flag, p.status, 302);
+        const bool got_o = mbar_wait(smem_u32(&C.bar_o_done[grp]), (uint32_t)((j - 1) & 1), abort_flag, p.status, 302);
         if (!__all_sync(0xffffffffu, got_o)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        uint32_t r[32];
+        uint32_t o[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint32_t ta = tmem + lane_base + kColO + 32 * c;
-          tmem_ld32(ta, r);
+          const uint32_t ta = tmem + lane_base + o_col + 32 * c;
+          tmem_ld32(ta, o);
           tmem_wait_ld();
 #pragma unroll
-          for (int i = 0; i < 32; ++i) r[i] = __float_as_uint(__uint_as_float(r[i]) * alpha);
-          tmem_st32(ta, r);
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(ta, o);
         }
         tmem_wait_st();
       }
       l_run *= alpha;
       const float base_m = m_run == -INFINITY ? 0.f : m_run;
+      uint32_t pk[32];
       float sum = 0.f;
-      uint32_t pk[64];
+      if (exact && vis && !masked) {
+        // Fast path: p = 2^(s * scale_log2 - m); every 4th pair uses the polynomial exp2.
+        const float nb_m = -base_m;
 #pragma unroll
-      for (int c = 0; c < 64; ++c) {
-        const float p0 = ex2_approx(x[2 * c] - base_m);
-        const float p1 = ex2_approx(x[2 * c + 1] - base_m);
-        sum += p0 + p1;
-        __nv_bfloat162 pair = __floats2bfloat162_rn(p0, p1);
-        pk[c] = *reinterpret_cast<uint32_t*>(&pair);
+        for (int c = 0; c < 32; ++c) {
+          const float a0 = fmaf(__uint_as_float(r[2 * c]), scale_log2, nb_m);
+          const float a1 = fmaf(__uint_as_float(r[2 * c + 1]), scale_log2, nb_m);
+          float p0, p1;
+          if ((c & 3) == 3) {
+            p0 = exp2_poly(a0);
+            p1 = exp2_poly(a1);
+          } else {
+            p0 = ex2_approx(a0);
+            p1 = ex2_approx(a1);
+          }
+          sum += p0 + p1;
+          pk[c] = pack_bf16(p0, p1);
+        }
+      } else if (!exact || vis) {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) {
+          const float p0 = ex2_approx(logit(2 * c) - base_m);
+          const float p1 = ex2_approx(logit(2 * c + 1) - base_m);
+          sum += p0 + p1;
+          pk[c] = pack_bf16(p0, p1);
+        }
+      } else {
+#pragma unroll
+        for (int c = 0; c < 32; ++c) pk[c] = 0u;
       }
       l_run += sum;
-      tmem_st32(tmem + lane_base + s * 128, pk);
-      tmem_st32(tmem + lane_base + s * 128 + 32, pk + 32);
+      tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(smem_u32(&C.bar_p_full[s]));
+      mbar_arrive(smem_u32(&C.bar_p_full[grp][s]));
     }
-    // Epilogue: O / l -> bf16, and the natural-log LSE.
+    // Epilogue: merge the two groups' partial softmaxes; group g writes head-dim columns
+    // 64g .. 64g+63 of the output row.
     const bool got_final = ok && mbar_wait(smem_u32(&C.bar_o_final), 0, abort_flag, p.status, 303);
+    C.merge_m[grp][row] = m_run;
+    C.merge_l[grp][row] = l_run;
+    named_barrier_sync(1, 256);
     if (__all_sync(0xffffffffu, got_final)) {
       tc_fence_after();
+      const float ma = C.merge_m[0][row], mb = C.merge_m[1][row];
+      const float la = C.merge_l[0][row], lb = C.merge_l[1][row];
+      const float m = fmaxf(ma, mb);
+      const float fa = ma == -INFINITY ? 0.f : ex2_approx(ma - m);
+      const float fb = mb == -INFINITY ? 0.f : ex2_approx(mb - m);
+      const float l = la * fa + lb * fb;
+      const float inv = l > 0.f ? 1.f / l : 0.f;
       const bool row_ok = grow < p.T;
-      const float inv = l_run > 0.f ? 1.f / l_run : 0.f;
-      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (((int64_t)b * p.T + grow) * p.H + h) * 128;
+      __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (((int64_t)b * p.T + grow) * p.H + h) * 128 + 64 * grp;
 #pragma unroll
-      for (int c = 0; c < 4; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tmem + lane_base + kColO + 32 * c, r);
+      for (int c = 0; c < 2; ++c) {
+        uint32_t oa[32], ob[32];
+        tmem_ld32(tmem + lane_base + kColOA + 64 * grp + 32 * c, oa);
+        tmem_ld32(tmem + lane_base + kColOB + 64 * grp + 32 * c, ob);
         tmem_wait_ld();
         if (row_ok) {
 #pragma unroll
           for (int v8 = 0; v8 < 4; ++v8) {
             float f[8];
 #pragma unroll
-            for (int i = 0; i < 8; ++i) f[i] = __uint_as_float(r[8 * v8 + i]) * inv;
+            for (int i = 0; i < 8; ++i)
+              f[i] = (__uint_as_float(oa[8 * v8 + i]) * fa + __uint_as_float(ob[8 * v8 + i]) * fb) * inv;
             store8(out + 32 * c + 8 * v8, f);
           }
         }
       }
-      if (row_ok && p.lse != nullptr)
-        p.lse[((int64_t)b * p.T + grow) * p.H + h] = l_run > 0.f ? (m_run + __log2f(l_run)) * kLn2 : -INFINITY;
+      if (grp == 0 && row_ok && p.lse != nullptr)
+        p.lse[((int64_t)b * p.T + grow) * p.H + h] = l > 0.f ? (m + __log2f(l)) * kLn2 : -INFINITY;
     }
   }
 
   // ---------------------------------------------------------------- teardown
   tc_fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == kMmaWarp) {
     tc_fence_after();
     // The final commit covers every MMA this CTA issued.
     mbar_drain(smem_u32(&C.bar_o_final), 0);

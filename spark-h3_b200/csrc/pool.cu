@@ -72,128 +72,193 @@ __global__ void query_anchor_kernel(const float* __restrict__ qc, int NB, int HD
   anchor[(int64_t)b * HD + col] = Elem<TA>::from_f(mean);
 }
 
-// One CTA per (key block, head, batch), 128 threads.  K and V rows of the block are
-// staged in shared memory as fp32 (block <= 128 rows, D <= 128).
+// One CTA per (key block, batch) covering every head: thread t owns 16 adjacent columns
+// of the H*D token row (D/16 threads per head), so each row is read with 32- or 64-byte
+// vector loads by the whole CTA.  Pass 1 streams K once: key block means (canonical
+// order) and the anchor logits.  Pass 2 re-reads K (an L2 hit) and streams V for the
+// weighted means; the weights are rounded to the K/V element type before the products,
+// as the tensor-core dot of the reference does.
+constexpr int kCPT = 16;  // columns per thread
+
+template <typename T> __device__ __forceinline__ void load16(const T* p, float* out);
+template <> __device__ __forceinline__ void load16<__nv_bfloat16>(const __nv_bfloat16* p, float* out) {
+  load8(p, out);
+  load8(p + 8, out + 8);
+}
+template <> __device__ __forceinline__ void load16<float>(const float* p, float* out) {
+  load8(p, out);
+  load8(p + 8, out + 8);
+}
+
+template <int GROUP>
+__device__ __forceinline__ float group_sum(float x) {
+#pragma unroll
+  for (int o = GROUP / 2; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
+  return x;
+}
+template <int GROUP>
+__device__ __forceinline__ float group_max(float x) {
+#pragma unroll
+  for (int o = GROUP / 2; o > 0; o >>= 1) x = fmaxf(x, __shfl_xor_sync(0xffffffffu, x, o));
+  return x;
+}
+
 template <typename T, typename TA, int D>
-__global__ void __launch_bounds__(128)
+__global__ void __launch_bounds__(256)
 pool_keys_summaries_kernel(const T* __restrict__ k, const T* __restrict__ v,
                            const TA* __restrict__ anchor, int T_, int H, int block,
                            int weighted_kv, int mass_bias, T* __restrict__ kc,
                            T* __restrict__ ak, T* __restrict__ av, float* __restrict__ lm) {
-  extern __shared__ float smem[];
-  const int kb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  constexpr int G = D / kCPT;  // threads per head
+  extern __shared__ float plog[];  // [H][block] logits, then probabilities
+  __shared__ float head_max[64], head_den[64];
+  const int kb = blockIdx.x, b = blockIdx.y;
   const int NB = gridDim.x;
   const int HD = H * D;
+  const int tid = threadIdx.x;
+  const int col = tid * kCPT;
+  const bool active = col < HD;
+  const int h = col / D, dcol = col % D;
+  const int glane = tid % G;
   const int row0 = kb * block;
   const int rows = min(block, T_ - row0);
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const bool want_sum = (ak != nullptr || av != nullptr || lm != nullptr);
-  float* sk = smem;                   // [block][D]
-  float* sv = sk + block * D;         // [block][D]
-  float* sa = sv + block * D;         // [D]
-  float* sp = sa + D;                 // [block] probabilities
-  float* red = sp + block;            // [8] reductions
+  const bool need_logits = want_sum && (weighted_kv || mass_bias);
+  const float scale = rsqrtf((float)D);
+  const float scale_log2 = scale * kLog2e;
 
-  // Stage K (and V, when summaries are wanted).  8 columns per thread-step.
-  constexpr int C8 = D / 8;
-  for (int idx = tid; idx < rows * C8; idx += blockDim.x) {
-    const int r = idx / C8, c = (idx % C8) * 8;
-    const int64_t g = ((int64_t)b * T_ + row0 + r) * HD + (int64_t)h * D + c;
-    load8(k + g, sk + r * D + c);
-    if (want_sum) load8(v + g, sv + r * D + c);
+  float a[kCPT];
+#pragma unroll
+  for (int i = 0; i < kCPT; ++i) a[i] = 0.f;
+  if (active && need_logits) {
+#pragma unroll
+    for (int i = 0; i < kCPT; ++i) a[i] = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + dcol + i]);
   }
-  if (want_sum && anchor != nullptr) {
-    for (int d = tid; d < D; d += blockDim.x) sa[d] = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + d]);
-  }
-  __syncthreads();
+  const T* kbase = k + ((int64_t)b * T_ + row0) * HD + col;
+  const T* vbase = v ? v + ((int64_t)b * T_ + row0) * HD + col : nullptr;
 
-  // Key block mean (routing centroid) in the canonical order.
-  if (kc != nullptr) {
-    for (int d = tid; d < D; d += blockDim.x) {
-      float total = 0.f;
-      for (int s = 0; s < rows; s += 64) {
-        const int sub = min(64, rows - s);
-        float acc = 0.f;
-        for (int r = 0; r < sub; ++r) acc = __fadd_rn(acc, sk[(s + r) * D + d]);
-        total = __fadd_rn(total, acc);
+  // Pass 1: K block means and anchor logits.
+  float total[kCPT];
+#pragma unroll
+  for (int i = 0; i < kCPT; ++i) total[i] = 0.f;
+  for (int s = 0; s < rows; s += 64) {
+    const int sub = min(64, rows - s);
+    float acc[kCPT];
+#pragma unroll
+    for (int i = 0; i < kCPT; ++i) acc[i] = 0.f;
+    int r = 0;
+    for (; r + 2 <= sub; r += 2) {
+      float x0[kCPT], x1[kCPT];
+      if (active) {
+        load16<T>(kbase + (int64_t)(s + r) * HD, x0);
+        load16<T>(kbase + (int64_t)(s + r + 1) * HD, x1);
       }
-      kc[(((int64_t)b * NB + kb) * H + h) * D + d] = Elem<T>::from_f(__fdiv_rn(total, (float)rows));
+      float d0 = 0.f, d1 = 0.f;
+#pragma unroll
+      for (int i = 0; i < kCPT; ++i) {
+        acc[i] = __fadd_rn(acc[i], x0[i]);
+        acc[i] = __fadd_rn(acc[i], x1[i]);
+        d0 = fmaf(a[i], x0[i], d0);
+        d1 = fmaf(a[i], x1[i], d1);
+      }
+      if (need_logits) {
+        d0 = group_sum<G>(d0);
+        d1 = group_sum<G>(d1);
+        if (active && glane == 0) {
+          plog[h * block + s + r] = d0 * scale_log2;
+          plog[h * block + s + r + 1] = d1 * scale_log2;
+        }
+      }
     }
+    for (; r < sub; ++r) {
+      float x0[kCPT];
+      if (active) load16<T>(kbase + (int64_t)(s + r) * HD, x0);
+      float d0 = 0.f;
+#pragma unroll
+      for (int i = 0; i < kCPT; ++i) {
+        acc[i] = __fadd_rn(acc[i], x0[i]);
+        d0 = fmaf(a[i], x0[i], d0);
+      }
+      if (need_logits) {
+        d0 = group_sum<G>(d0);
+        if (active && glane == 0) plog[h * block + s + r] = d0 * scale_log2;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < kCPT; ++i) total[i] = __fadd_rn(total[i], acc[i]);
+  }
+  if (kc != nullptr && active) {
+    float out[kCPT];
+#pragma unroll
+    for (int i = 0; i < kCPT; ++i) out[i] = __fdiv_rn(total[i], (float)rows);
+    T* dst = kc + (((int64_t)b * NB + kb) * H + h) * D + dcol;
+    store8(dst, out);
+    store8(dst + 8, out + 8);
   }
   if (!want_sum) return;
 
-  const float scale = rsqrtf((float)D);
-  const float scale_log2 = scale * kLog2e;
-  const float cnt = (float)rows;
-  float maximum = 0.f, den = 1.f;
-  if (weighted_kv || mass_bias) {
-    // logits[r] = (a . k_r) * scale * log2(e): warps split rows, lanes split d.
-    for (int r = warp; r < rows; r += 4) {
-      float part = 0.f;
-      for (int d = lane; d < D; d += 32) part = fmaf(sa[d], sk[r * D + d], part);
-      part = warp_sum(part);
-      if (lane == 0) sp[r] = part * scale_log2;
-    }
+  // Softmax over the block's rows, per head (the G threads of a head cooperate).
+  if (need_logits) {
     __syncthreads();
     float m = -INFINITY;
-    for (int r = tid; r < rows; r += blockDim.x) m = fmaxf(m, sp[r]);
-    m = warp_max(m);
-    if (lane == 0) red[warp] = m;
-    __syncthreads();
-    maximum = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-    __syncthreads();
-    float s = 0.f;
-    for (int r = tid; r < rows; r += blockDim.x) {
-      const float p = exp2f(sp[r] - maximum);
-      sp[r] = p;
-      s += p;
+    if (active)
+      for (int r = glane; r < rows; r += G) m = fmaxf(m, plog[h * block + r]);
+    m = group_max<G>(m);
+    float sum = 0.f;
+    if (active)
+      for (int r = glane; r < rows; r += G) {
+        const float p = exp2f(plog[h * block + r] - m);
+        plog[h * block + r] = p;
+        sum += p;
+      }
+    sum = group_sum<G>(sum);
+    if (active && glane == 0) {
+      head_max[h] = m;
+      head_den[h] = sum;
     }
-    s = warp_sum(s);
-    if (lane == 0) red[warp] = s;
-    __syncthreads();
-    den = (red[0] + red[1]) + (red[2] + red[3]);
     __syncthreads();
   }
+  // Inactive lanes (H*D not a multiple of 512) stay for the group shuffles below.
+  const float maximum = need_logits && active ? head_max[h] : 0.f;
+  const float den = need_logits && active ? head_den[h] : 1.f;
 
-  // Weighted (or plain) means.  The weights are rounded to the K/V element type
-  // before the products, as the tensor-core dot of the reference does.
-  T* ak_row = ak ? ak + (((int64_t)b * H + h) * NB + kb) * D : nullptr;
-  T* av_row = av ? av + (((int64_t)b * H + h) * NB + kb) * D : nullptr;
-  float shift_part = 0.f;
-  for (int d = tid; d < D; d += blockDim.x) {
-    float key_sum = 0.f, val_sum = 0.f;
-    if (weighted_kv) {
-      for (int r = 0; r < rows; ++r) {
-        const float w = Elem<T>::to_f(Elem<T>::from_f(sp[r]));
-        key_sum = fmaf(w, sk[r * D + d], key_sum);
-        val_sum = fmaf(w, sv[r * D + d], val_sum);
-      }
-      key_sum /= den;
-      val_sum /= den;
-    } else {
-      for (int r = 0; r < rows; ++r) {
-        key_sum += sk[r * D + d];
-        val_sum += sv[r * D + d];
-      }
-      key_sum /= cnt;
-      val_sum /= cnt;
+  // Pass 2: weighted (or plain) means of K and V.
+  float sk[kCPT], sv[kCPT];
+#pragma unroll
+  for (int i = 0; i < kCPT; ++i) sk[i] = sv[i] = 0.f;
+  for (int r = 0; active && r < rows; ++r) {
+    float x[kCPT], y[kCPT];
+    load16<T>(kbase + (int64_t)r * HD, x);
+    load16<T>(vbase + (int64_t)r * HD, y);
+    const float w = weighted_kv ? Elem<T>::to_f(Elem<T>::from_f(plog[h * block + r])) : 1.f;
+#pragma unroll
+    for (int i = 0; i < kCPT; ++i) {
+      sk[i] = fmaf(w, x[i], sk[i]);
+      sv[i] = fmaf(w, y[i], sv[i]);
     }
-    const T key_stored = Elem<T>::from_f(key_sum);
-    if (ak_row) ak_row[d] = key_stored;
-    if (av_row) av_row[d] = Elem<T>::from_f(val_sum);
-    if (mass_bias) shift_part = fmaf(sa[d], Elem<T>::to_f(key_stored), shift_part);
   }
-  if (lm == nullptr) return;
-  if (mass_bias) {
-    shift_part = warp_sum(shift_part);
-    if (lane == 0) red[4 + warp] = shift_part;
-    __syncthreads();
-    if (tid == 0) {
-      const float shift = ((red[4] + red[5]) + (red[6] + red[7])) * scale;
-      lm[((int64_t)b * H + h) * NB + kb] = (maximum + log2f(den)) * kLn2 - shift;
-    }
-  } else if (tid == 0) {
-    lm[((int64_t)b * H + h) * NB + kb] = logf(cnt);
+  const float norm = weighted_kv ? den : (float)rows;
+  float key_out[kCPT], val_out[kCPT];
+  float shift = 0.f;
+#pragma unroll
+  for (int i = 0; i < kCPT; ++i) {
+    key_out[i] = Elem<T>::to_f(Elem<T>::from_f(sk[i] / norm));
+    val_out[i] = sv[i] / norm;
+    shift = fmaf(a[i], key_out[i], shift);
+  }
+  const int64_t srow = (((int64_t)b * H + h) * NB + kb) * D + dcol;
+  if (ak && active) {
+    store8(ak + srow, key_out);
+    store8(ak + srow + 8, key_out + 8);
+  }
+  if (av && active) {
+    store8(av + srow, val_out);
+    store8(av + srow + 8, val_out + 8);
+  }
+  shift = group_sum<G>(shift);
+  if (lm != nullptr && active && glane == 0) {
+    const float value = mass_bias ? (maximum + log2f(den)) * kLn2 - shift * scale : logf((float)rows);
+    lm[((int64_t)b * H + h) * NB + kb] = value;
   }
 }
 
@@ -245,12 +310,17 @@ static int launch_pool_keys(const void* k, const void* v, const void* anchor, in
                             int block, int weighted_kv, int mass_bias, void* kc, void* ak, void* av,
                             float* lm, cudaStream_t s) {
   const int NB = ceil_div(tokens, block);
-  const size_t smem = (size_t)(2 * block * D + D + block + 8) * sizeof(float);
+  const int threads = ceil_div(H * D / kCPT, 32) * 32;
+  if (threads > 256 || H > 64) {
+    set_error("sb_pool_keys_summaries: H * D must be at most 4096 and H at most 64");
+    return SB_ERR_INVALID;
+  }
+  const size_t smem = (size_t)H * block * sizeof(float);
   auto kern = pool_keys_summaries_kernel<T, TA, D>;
   cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_pool_keys_summaries: set smem");
-  dim3 grid(NB, H, B);
-  kern<<<grid, 128, smem, s>>>((const T*)k, (const T*)v, (const TA*)anchor, tokens, H, block, weighted_kv,
+  dim3 grid(NB, B);
+  kern<<<grid, threads, smem, s>>>((const T*)k, (const T*)v, (const TA*)anchor, tokens, H, block, weighted_kv,
                               mass_bias, (T*)kc, (T*)ak, (T*)av, lm);
   SB_CHECK_LAUNCH("sb_pool_keys_summaries launch");
   return SB_OK;
