@@ -1,11 +1,11 @@
 // Sparse attention forward on the 5th-generation tensor cores (sm_100a), bf16, D = 128.
 //
-// One CTA per (128-row query tile, head, batch).  Roles (320 threads):
+// One CTA per (128-row query tile, head, batch).  Roles (352 threads):
 //   warps 0-3  softmax group 0: row r = TMEM lane r, key columns 0-63 of every tile
 //   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
-//   warp 8     TMA producer: Q once, then K/V tiles of the exact key blocks, then the
-//              AK/AV summary tiles
-//   warp 9     tcgen05 issuer; owns the TMEM allocation
+//   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages
+//   warp 9     TMA producer of the V (or AV summary) tiles, 2 stages
+//   warp 10    tcgen05 issuer; owns the TMEM allocation
 // TMEM (512 columns): S double buffer at [0,128) and [128,256); O_A at [256,384) and
 // O_B at [384,512).  Each softmax group keeps its own running max, sum and output
 // accumulator (O_A += P_A V[0:64), O_B += P_B V[64:128)), so the groups never
@@ -28,9 +28,12 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 320;
-constexpr int kProducerWarp = 8;
-constexpr int kMmaWarp = 9;
+constexpr int kThreads = 352;
+constexpr int kProducerWarp = 8;   // Q and K
+constexpr int kProducerVWarp = 9;  // V
+constexpr int kMmaWarp = 10;
+constexpr int kKStages = 3;
+constexpr int kVStages = 2;
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 bf16 operand tile
 constexpr int kHalfBytes = 128 * 64 * 2;   // one 64-column half of it
 constexpr int kBoxBytes = 64 * 64 * 2;     // one TMA box (64 columns x 64 rows)
@@ -41,8 +44,8 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: lazy O rescale
 
 struct __align__(8) Control {
   uint64_t bar_q_full;
-  uint64_t bar_k_full[2], bar_k_empty[2];
-  uint64_t bar_v_full[2], bar_v_empty[2];
+  uint64_t bar_k_full[kKStages], bar_k_empty[kKStages];
+  uint64_t bar_v_full[kVStages], bar_v_empty[kVStages];
   uint64_t bar_s_full[2];
   uint64_t bar_p_full[2][2];  // [group][stage]
   uint64_t bar_o_done[2];     // [group]
@@ -78,7 +81,7 @@ struct GranuleWalker {
 };
 
 struct SmemLayout {
-  uint32_t q, k0, k1, v0, v1;  // byte offsets from the 1024-aligned base
+  uint32_t q, k, v;  // byte offsets from the 1024-aligned base (stages are consecutive)
   uint32_t ctrl, ebits, ubits;
   uint32_t total;
 };
@@ -86,11 +89,9 @@ struct SmemLayout {
 __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran) {
   SmemLayout L;
   L.q = 0;
-  L.k0 = kTileBytes;
-  L.k1 = 2 * kTileBytes;
-  L.v0 = 3 * kTileBytes;
-  L.v1 = 4 * kTileBytes;
-  L.ctrl = 5 * kTileBytes;
+  L.k = kTileBytes;
+  L.v = L.k + kKStages * kTileBytes;
+  L.ctrl = L.v + kVStages * kTileBytes;
   L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);
   L.ubits = L.ebits + (uint32_t)(2 * words_blk * 4);
   L.total = L.ubits + (uint32_t)(words_gran * 4);
@@ -149,11 +150,15 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
     mbar_init(smem_u32(&C.bar_q_full), 1);
-    for (int s = 0; s < 2; ++s) {
+    for (int s = 0; s < kKStages; ++s) {
       mbar_init(smem_u32(&C.bar_k_full[s]), 1);
       mbar_init(smem_u32(&C.bar_k_empty[s]), 1);
+    }
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(smem_u32(&C.bar_v_full[s]), 1);
       mbar_init(smem_u32(&C.bar_v_empty[s]), 1);
+    }
+    for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&C.bar_s_full[s]), 1);
       mbar_init(smem_u32(&C.bar_p_full[0][s]), 128);
       mbar_init(smem_u32(&C.bar_p_full[1][s]), 128);
@@ -236,23 +241,33 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   volatile int* abort_flag = &C.abort_flag;
   const uint32_t base = smem_u32(smem);
   const uint32_t sQ = base + L.q;
-  const uint32_t sK[2] = {base + L.k0, base + L.k1};
-  const uint32_t sV[2] = {base + L.v0, base + L.v1};
+  const uint32_t sK0 = base + L.k;
+  const uint32_t sV0 = base + L.v;
 
-  if (warp == kProducerWarp) {
-    // ------------------------------------------------------------ producer
+  if (warp == kProducerWarp || warp == kProducerVWarp) {
+    // ----------------------------------------------------------- producers
+    // Warp 8 streams Q and the K side, warp 9 the V side; both walk the same tile list,
+    // so a slow P.V never delays the next K tile.
     if (lane == 0) {
+      const bool is_k = warp == kProducerWarp;
+      const int stages = is_k ? kKStages : kVStages;
+      const CUtensorMap* exact_map = is_k ? &tm_k : &tm_v;
+      const CUtensorMap* summ_map = is_k ? &tm_ak : &tm_av;
+      const uint32_t s_base = is_k ? sK0 : sV0;
+      uint64_t* full = is_k ? C.bar_k_full : C.bar_v_full;
+      uint64_t* empty = is_k ? C.bar_k_empty : C.bar_v_empty;
       const uint32_t bq = smem_u32(&C.bar_q_full);
-      mbar_arrive_expect_tx(bq, kTileBytes);
-      for (int dh = 0; dh < 2; ++dh)
-        for (int rh = 0; rh < 2; ++rh)
-          tma_load_3d(sQ + dh * kHalfBytes + rh * kBoxBytes, &tm_q, bq, h * 128 + 64 * dh, row0 + 64 * rh, b);
+      if (is_k) {
+        mbar_arrive_expect_tx(bq, kTileBytes);
+        for (int dh = 0; dh < 2; ++dh)
+          for (int rh = 0; rh < 2; ++rh)
+            tma_load_3d(sQ + dh * kHalfBytes + rh * kBoxBytes, &tm_q, bq, h * 128 + 64 * dh, row0 + 64 * rh, b);
+      }
       GranuleWalker walk;
       walk.init(ubits, words_gran);
-      int armed_k[2] = {0, 0}, armed_v[2] = {0, 0};
+      int armed[kKStages] = {0, 0, 0};
+      int s = 0, use = 0;  // stage and how many times it has been filled before
       for (int j = 0; j < total_tiles; ++j) {
-        const int s = j & 1;
-        const uint32_t par = ((j >> 1) & 1) ^ 1;
         int g0 = 0, g1 = 0;
         const bool exact = j < exact_tiles;
         if (exact) {
@@ -261,39 +276,29 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           if (g1 < 0) g1 = g0;
         }
         const int cc = j - exact_tiles;
-        const uint32_t bk = smem_u32(&C.bar_k_full[s]);
-        if (!mbar_wait(smem_u32(&C.bar_k_empty[s]), par, abort_flag, p.status, 101)) break;
-        mbar_arrive_expect_tx(bk, kTileBytes);
-        ++armed_k[s];
+        const uint32_t bar = smem_u32(&full[s]);
+        if (!mbar_wait(smem_u32(&empty[s]), (uint32_t)((use & 1) ^ 1), abort_flag, p.status, is_k ? 101 : 102)) break;
+        mbar_arrive_expect_tx(bar, kTileBytes);
+        ++armed[s];
+        const uint32_t st = s_base + s * kTileBytes;
         for (int slot = 0; slot < 2; ++slot) {
           for (int dh = 0; dh < 2; ++dh) {
-            const uint32_t dst = sK[s] + dh * kHalfBytes + slot * kBoxBytes;
+            const uint32_t dst = st + dh * kHalfBytes + slot * kBoxBytes;
             if (exact)
-              tma_load_3d(dst, &tm_k, bk, h * 128 + 64 * dh, (slot ? g1 : g0) * 64, b);
+              tma_load_3d(dst, exact_map, bar, h * 128 + 64 * dh, (slot ? g1 : g0) * 64, b);
             else
-              tma_load_3d(dst, &tm_ak, bk, 64 * dh, cc * 128 + 64 * slot, b * p.H + h);
+              tma_load_3d(dst, summ_map, bar, 64 * dh, cc * 128 + 64 * slot, b * p.H + h);
           }
         }
-        const uint32_t bv = smem_u32(&C.bar_v_full[s]);
-        if (!mbar_wait(smem_u32(&C.bar_v_empty[s]), par, abort_flag, p.status, 102)) break;
-        mbar_arrive_expect_tx(bv, kTileBytes);
-        ++armed_v[s];
-        for (int slot = 0; slot < 2; ++slot) {
-          for (int dh = 0; dh < 2; ++dh) {
-            const uint32_t dst = sV[s] + dh * kHalfBytes + slot * kBoxBytes;
-            if (exact)
-              tma_load_3d(dst, &tm_v, bv, h * 128 + 64 * dh, (slot ? g1 : g0) * 64, b);
-            else
-              tma_load_3d(dst, &tm_av, bv, 64 * dh, cc * 128 + 64 * slot, b * p.H + h);
-          }
+        if (++s == stages) {
+          s = 0;
+          ++use;
         }
       }
       // Every armed load must land before the CTA may exit.
-      for (int st = 0; st < 2; ++st) {
-        if (armed_k[st] > 0) mbar_drain(smem_u32(&C.bar_k_full[st]), (uint32_t)((armed_k[st] - 1) & 1));
-        if (armed_v[st] > 0) mbar_drain(smem_u32(&C.bar_v_full[st]), (uint32_t)((armed_v[st] - 1) & 1));
-      }
-      mbar_drain(bq, 0);
+      for (int st = 0; st < stages; ++st)
+        if (armed[st] > 0) mbar_drain(smem_u32(&full[st]), (uint32_t)((armed[st] - 1) & 1));
+      if (is_k) mbar_drain(bq, 0);
     }
   } else if (warp == kMmaWarp) {
     // ---------------------------------------------------------- MMA issuer
@@ -302,8 +307,9 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, true);
       bool ok = mbar_wait(smem_u32(&C.bar_q_full), 0, abort_flag, p.status, 201);
       auto issue_pv = [&](int i) -> bool {
-        const int s = i & 1;
+        const int s = i & 1;  // S/P buffer and V stage (kVStages == 2)
         const uint32_t par = (i >> 1) & 1;
+        const uint32_t sVs = sV0 + s * kTileBytes;
         if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) return false;
         for (int g = 0; g < 2; ++g) {
           if (!mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) return false;
@@ -311,7 +317,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           const uint32_t o_col = g ? kColOB : kColOA;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bdesc = smem_desc_sw128(sV[s] + (4 * g + kk) * 2048, kHalfBytes, 1024);
+            const uint64_t bdesc = smem_desc_sw128(sVs + (4 * g + kk) * 2048, kHalfBytes, 1024);
             mma_ts(tmem + o_col, tmem + s * 128 + 64 * g + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
           }
           tc_commit(smem_u32(&C.bar_o_done[g]));
@@ -319,23 +325,28 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         tc_commit(smem_u32(&C.bar_v_empty[s]));
         return true;
       };
+      int ks = 0, kuse = 0;
       for (int j = 0; ok && j < total_tiles; ++j) {
         const int s = j & 1;
-        const uint32_t par = (j >> 1) & 1;
-        if (!mbar_wait(smem_u32(&C.bar_k_full[s]), par, abort_flag, p.status, 204)) {
+        if (!mbar_wait(smem_u32(&C.bar_k_full[ks]), (uint32_t)(kuse & 1), abort_flag, p.status, 204)) {
           ok = false;
           break;
         }
         tc_fence_after();
+        const uint32_t sKs = sK0 + ks * kTileBytes;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
           const uint64_t adesc = smem_desc_sw128(sQ + off, 16, 1024);
-          const uint64_t bdesc = smem_desc_sw128(sK[s] + off, 16, 1024);
+          const uint64_t bdesc = smem_desc_sw128(sKs + off, 16, 1024);
           mma_ss(tmem + s * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(&C.bar_s_full[s]));
-        tc_commit(smem_u32(&C.bar_k_empty[s]));
+        tc_commit(smem_u32(&C.bar_k_empty[ks]));
+        if (++ks == kKStages) {
+          ks = 0;
+          ++kuse;
+        }
         if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
       if (ok && total_tiles > 0) issue_pv(total_tiles - 1);
@@ -383,33 +394,51 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       tc_fence_after();
       uint32_t r[64];
-      float tile_max = -INFINITY;
       const bool any_vis = __any_sync(0xffffffffu, vis || !exact);
       if (any_vis) {
         tmem_ld32(tmem + lane_base + s * 128 + s_col, r);
         tmem_ld32(tmem + lane_base + s * 128 + s_col + 32, r + 32);
         tmem_wait_ld();
       }
-      // Masked logit of column i (summary tiles add LM * log2(e); invisible -> -inf).
-      const int e0 = (j - exact_tiles) * 128 + (int)s_col;
-      auto logit = [&](int i) -> float {
-        if (!exact) {
-          const int e = e0 + i;
-          const uint32_t ex = e < p.NB ? ehalf[e >> 5] : 0xffffffffu;
-          const bool visible = e < p.NB && !((ex >> (e & 31)) & 1u);
-          return visible ? fmaf(__uint_as_float(r[i]), scale_log2, __ldg(lm_row + e) * kLog2e) : -INFINITY;
+      // fast: unmasked exact keys, r holds raw scores; otherwise r is rewritten in place
+      // with scaled (and, for summary tiles, LM-biased) logits, -inf where invisible.
+      const bool fast = exact && vis && !masked;
+      float mx[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      if (fast) {
+#pragma unroll
+        for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) mx[i] *= scale_log2;
+      } else if (!exact) {
+        // Summary entries e0 .. e0+63 of this group: logit + LM * log2(e), or -inf when the
+        // block is exact for this half (or past the last block).
+        const int e0 = (j - exact_tiles) * 128 + (int)s_col;
+#pragma unroll
+        for (int wq = 0; wq < 2; ++wq) {
+          const int eb = e0 + 32 * wq;
+          const uint32_t ex = eb < p.NB ? ehalf[eb >> 5] : 0xffffffffu;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int e = eb + i;
+            const bool visible = e < p.NB && !((ex >> i) & 1u);
+            const float v = visible ? fmaf(__uint_as_float(r[32 * wq + i]), scale_log2, __ldg(lm_row + e) * kLog2e)
+                                    : -INFINITY;
+            r[32 * wq + i] = __float_as_uint(v);
+            mx[i & 7] = fmaxf(mx[i & 7], v);
+          }
         }
-        return key0 + i < p.T ? __uint_as_float(r[i]) * scale_log2 : -INFINITY;
-      };
-      if (exact && vis && !masked) {
-        float raw = -INFINITY;
+      } else if (vis) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) raw = fmaxf(raw, __uint_as_float(r[i]));
-        tile_max = raw * scale_log2;
-      } else if (!exact || vis) {
-#pragma unroll
-        for (int i = 0; i < 64; ++i) tile_max = fmaxf(tile_max, logit(i));
+        for (int i = 0; i < 64; ++i) {
+          const float v = key0 + i < p.T ? __uint_as_float(r[i]) * scale_log2 : -INFINITY;
+          r[i] = __float_as_uint(v);
+          mx[i & 7] = fmaxf(mx[i & 7], v);
+        }
       }
+      const float tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
+                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
       // Lazy rescale of this group's O: only when the running max grows by more than
       // the threshold (or becomes finite for the first time).
       const float m_new = fmaxf(m_run, tile_max);
@@ -441,9 +470,9 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       l_run *= alpha;
       const float base_m = m_run == -INFINITY ? 0.f : m_run;
       uint32_t pk[32];
-      float sum = 0.f;
-      if (exact && vis && !masked) {
-        // Fast path: p = 2^(s * scale_log2 - m); every 4th pair uses the polynomial exp2.
+      float sums[4] = {0.f, 0.f, 0.f, 0.f};
+      if (fast) {
+        // p = 2^(s * scale_log2 - m); every 4th pair uses the polynomial exp2.
         const float nb_m = -base_m;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
@@ -457,21 +486,22 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
             p0 = ex2_approx(a0);
             p1 = ex2_approx(a1);
           }
-          sum += p0 + p1;
+          sums[c & 3] += p0 + p1;
           pk[c] = pack_bf16(p0, p1);
         }
       } else if (!exact || vis) {
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float p0 = ex2_approx(logit(2 * c) - base_m);
-          const float p1 = ex2_approx(logit(2 * c + 1) - base_m);
-          sum += p0 + p1;
+          const float p0 = ex2_approx(__uint_as_float(r[2 * c]) - base_m);
+          const float p1 = ex2_approx(__uint_as_float(r[2 * c + 1]) - base_m);
+          sums[c & 3] += p0 + p1;
           pk[c] = pack_bf16(p0, p1);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) pk[c] = 0u;
       }
+      const float sum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
       l_run += sum;
       tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
