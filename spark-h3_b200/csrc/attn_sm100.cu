@@ -1,11 +1,15 @@
 // Sparse attention forward on the 5th-generation tensor cores (sm_100a), bf16, D = 128.
 //
-// One CTA per (128-row query tile, head, batch).  Roles (352 threads):
+// One CTA per (128-row query tile, head, batch).  Roles (384 threads):
 //   warps 0-3  softmax group 0: row r = TMEM lane r, key columns 0-63 of every tile
 //   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
 //   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages
 //   warp 9     TMA producer of the V (or AV summary) tiles, 2 stages
-//   warp 10    tcgen05 issuer; owns the TMEM allocation
+//   warp 10    tcgen05 issuer of S = Q K^T; owns the TMEM allocation
+//   warp 11    tcgen05 issuer of O += P V
+// Issuing one tcgen05.mma occupies its thread for about as long as a third of the MMA's
+// execution, so two issuers keep the tensor pipe fed where one would stall it on every
+// wait and commit.
 // TMEM (512 columns): S double buffer at [0,128) and [128,256); O_A at [256,384) and
 // O_B at [384,512).  Each softmax group keeps its own running max, sum and output
 // accumulator (O_A += P_A V[0:64), O_B += P_B V[64:128)), so the groups never
@@ -23,17 +27,33 @@
 #include "attn_common.cuh"
 #include "sm100_ptx.cuh"
 
+// Optional per-event clock trace of one CTA (compile with -DSB_TRACE; off in the product).
+#ifdef SB_TRACE
+namespace sb {
+__device__ long long g_trace[16][4096];
+__device__ int g_trace_cta;
+}
+#define SB_TRACE_POINT(on, ev, j) \
+  do { if ((on) && (j) < 4096) ::sb::g_trace[ev][j] = clock64(); } while (0)
+#define SB_TRACE_CTA() ((int)blockIdx.x == ::sb::g_trace_cta && blockIdx.y == 0 && blockIdx.z == 0)
+#else
+#define SB_TRACE_POINT(on, ev, j) do { } while (0)
+#define SB_TRACE_CTA() false
+#endif
+
 namespace sb {
 namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 352;
+constexpr int kThreads = 384;
 constexpr int kProducerWarp = 8;   // Q and K
 constexpr int kProducerVWarp = 9;  // V
-constexpr int kMmaWarp = 10;
+constexpr int kMmaWarp = 10;       // S issuer
+constexpr int kPvWarp = 11;        // P.V issuer
 constexpr int kKStages = 3;
 constexpr int kVStages = 2;
+static_assert(kVStages == 2, "the P.V issue and the rescale wait index V stages by tile parity");
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 bf16 operand tile
 constexpr int kHalfBytes = 128 * 64 * 2;   // one 64-column half of it
 constexpr int kBoxBytes = 64 * 64 * 2;     // one TMA box (64 columns x 64 rows)
@@ -47,15 +67,16 @@ struct __align__(8) Control {
   uint64_t bar_k_full[kKStages], bar_k_empty[kKStages];
   uint64_t bar_v_full[kVStages], bar_v_empty[kVStages];
   uint64_t bar_s_full[2];
-  uint64_t bar_p_full[2][2];  // [group][stage]
-  uint64_t bar_o_done[2];     // [group]
-  uint64_t bar_o_final;
+  uint64_t bar_p_full[2];  // both softmax groups have written P into the S buffer (256)
+  uint64_t bar_xsum;       // both groups have published their final max and sum (256)
+  uint64_t bar_o_final;    // P.V issuer: every P.V (hence every S) has completed
+  uint64_t bar_s_final;    // S issuer: its last MMA has completed (drain before exit)
   uint32_t tmem_base;
   int abort_flag;
   int exact_granules;
   int has_summary;
-  float merge_m[2][128];
-  float merge_l[2][128];
+  float xmax[2][128];  // [group][row] final running max
+  float xsum[2][128];  // [group][row] final partial sums
 };
 
 // Walks the set bits of the granule bitset in ascending order.
@@ -82,19 +103,20 @@ struct GranuleWalker {
 
 struct SmemLayout {
   uint32_t q, k, v;  // byte offsets from the 1024-aligned base (stages are consecutive)
-  uint32_t ctrl, ebits, ubits;
+  uint32_t ctrl, ebits, ubits, lm;
   uint32_t total;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran) {
+__host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran, int nb_pad) {
   SmemLayout L;
   L.q = 0;
   L.k = kTileBytes;
   L.v = L.k + kKStages * kTileBytes;
   L.ctrl = L.v + kVStages * kTileBytes;
-  L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);
-  L.ubits = L.ebits + (uint32_t)(2 * words_blk * 4);
-  L.total = L.ubits + (uint32_t)(words_gran * 4);
+  L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);  // Control is small
+  L.ubits = L.ebits + (uint32_t)((2 * words_blk * 4 + 15) / 16 * 16);  // every region 16-byte aligned
+  L.lm = L.ubits + (uint32_t)((words_gran * 4 + 15) / 16 * 16);
+  L.total = L.lm + (uint32_t)(nb_pad * 4);  // LM * log2(e) of every key block
   return L;
 }
 
@@ -114,14 +136,26 @@ __device__ __forceinline__ float exp2_poly(float x) {
   return __int_as_float(__float_as_int(p) + (__float_as_int(t) << 23));
 }
 
-__device__ __forceinline__ uint32_t pack_bf16(float lo, float hi) {
-  __nv_bfloat162 pair = __floats2bfloat162_rn(lo, hi);
-  return *reinterpret_cast<uint32_t*>(&pair);
+// exp2_poly on a pair, with the float arithmetic in packed fp32x2 instructions.
+__device__ __forceinline__ void exp2_poly2(float x0, float x1, float& y0, float& y1) {
+  x0 = fmaxf(x0, -126.f);
+  x1 = fmaxf(x1, -126.f);
+  const uint64_t shifter = f2_pack(12582912.f, 12582912.f);
+  const uint64_t neg_shifter = f2_pack(-12582912.f, -12582912.f);
+  const uint64_t x = f2_pack(x0, x1);
+  const uint64_t t = f2_add(x, shifter);
+  const uint64_t j = f2_add(t, neg_shifter);
+  const uint64_t f = f2_fma(j, f2_pack(-1.f, -1.f), x);
+  uint64_t p = f2_fma(f2_pack(0.05294328f, 0.05294328f), f, f2_pack(0.24218228f, 0.24218228f));
+  p = f2_fma(p, f, f2_pack(0.6935803f, 0.6935803f));
+  p = f2_fma(p, f, f2_pack(0.99996096f, 0.99996096f));
+  float p0, p1, t0, t1;
+  f2_unpack(p, p0, p1);
+  f2_unpack(t, t0, t1);
+  y0 = __int_as_float(__float_as_int(p0) + (__float_as_int(t0) << 23));
+  y1 = __int_as_float(__float_as_int(p1) + (__float_as_int(t1) << 23));
 }
 
-__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
-}
 
 __global__ void __launch_bounds__(kThreads, 1)
 sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
@@ -129,14 +163,20 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                               const __grid_constant__ CUtensorMap tm_v,
                               const __grid_constant__ CUtensorMap tm_ak,
                               const __grid_constant__ CUtensorMap tm_av, AttnParams p) {
-  extern __shared__ __align__(1024) uint8_t smem_raw[];
-  // Align the operand region to 1024 bytes (128-byte swizzle atoms).
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  // The dynamic window starts 1024-byte aligned (the kernel has no static shared
+  // memory); the 128-byte swizzle atoms of the operand tiles rely on it.
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((sm100::smem_u32(smem) & 1023u) != 0u) {
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 900);
+    return;
+  }
   const int words_blk = p.words;
   const int n64 = ceil_div(p.T, 64);
   const int words_gran = ceil_div(n64, 32);
-  const SmemLayout L = smem_layout(words_blk, words_gran);
+  const int nb_pad = 128 * ceil_div(p.NB, 128);  // whole summary tiles
+  const SmemLayout L = smem_layout(words_blk, words_gran, nb_pad);
   Control& C = *reinterpret_cast<Control*>(smem + L.ctrl);
+  float* lm_s = reinterpret_cast<float*>(smem + L.lm);  // [nb_pad]
   uint32_t* ebits = reinterpret_cast<uint32_t*>(smem + L.ebits);  // [2][words_blk]
   uint32_t* ubits = reinterpret_cast<uint32_t*>(smem + L.ubits);  // [words_gran]
 
@@ -146,6 +186,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   const int tile = n_tiles - 1 - (int)blockIdx.x;  // the dense suffix tile launches first
   const int h = blockIdx.y, b = blockIdx.z;
   const int row0 = tile * 128;
+  const int gshift = p.block == 128 ? 1 : 0;
+  const bool trace = SB_TRACE_CTA();
 
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
@@ -160,11 +202,11 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
     for (int s = 0; s < 2; ++s) {
       mbar_init(smem_u32(&C.bar_s_full[s]), 1);
-      mbar_init(smem_u32(&C.bar_p_full[0][s]), 128);
-      mbar_init(smem_u32(&C.bar_p_full[1][s]), 128);
-      mbar_init(smem_u32(&C.bar_o_done[s]), 1);
+      mbar_init(smem_u32(&C.bar_p_full[s]), 256);
     }
     mbar_init(smem_u32(&C.bar_o_final), 1);
+    mbar_init(smem_u32(&C.bar_s_final), 1);
+    mbar_init(smem_u32(&C.bar_xsum), 256);
     C.abort_flag = 0;
     C.exact_granules = 0;
     fence_barrier_init();
@@ -212,12 +254,15 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     for (int i = 0; i < 32; ++i) {
       const int g = 32 * w + i;
       if (g >= n64) break;
-      const int kb = g * 64 / p.block;
+      const int kb = g >> gshift;  // granule -> key block (block is 64 or 128)
       const uint32_t either = ebits[kb >> 5] | ebits[words_blk + (kb >> 5)];
       if ((either >> (kb & 31)) & 1u) bits |= 1u << i;
     }
     ubits[w] = bits;
   }
+  const bool any_routed = row0 < p.query_tokens;
+  for (int e = tid; e < nb_pad; e += kThreads)
+    lm_s[e] = (any_routed && e < p.NB) ? __ldg(p.lm + ((int64_t)b * p.H + h) * p.NB + e) * kLog2e : 0.f;
   __syncthreads();
   if (warp == 0) {
     int cnt = 0;
@@ -265,7 +310,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       GranuleWalker walk;
       walk.init(ubits, words_gran);
-      int armed[kKStages] = {0, 0, 0};
+      int armed[kKStages > kVStages ? kKStages : kVStages] = {};
       int s = 0, use = 0;  // stage and how many times it has been filled before
       for (int j = 0; j < total_tiles; ++j) {
         int g0 = 0, g1 = 0;
@@ -279,6 +324,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         const uint32_t bar = smem_u32(&full[s]);
         if (!mbar_wait(smem_u32(&empty[s]), (uint32_t)((use & 1) ^ 1), abort_flag, p.status, is_k ? 101 : 102)) break;
         mbar_arrive_expect_tx(bar, kTileBytes);
+        SB_TRACE_POINT(trace, is_k ? 0 : 1, j);
         ++armed[s];
         const uint32_t st = s_base + s * kTileBytes;
         for (int slot = 0; slot < 2; ++slot) {
@@ -301,55 +347,66 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       if (is_k) mbar_drain(bq, 0);
     }
   } else if (warp == kMmaWarp) {
-    // ---------------------------------------------------------- MMA issuer
+    // ------------------------------------------------------------- S issuer
     if (lane == 0) {
       constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 128, false);
-      constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, true);
       bool ok = mbar_wait(smem_u32(&C.bar_q_full), 0, abort_flag, p.status, 201);
-      auto issue_pv = [&](int i) -> bool {
-        const int s = i & 1;  // S/P buffer and V stage (kVStages == 2)
-        const uint32_t par = (i >> 1) & 1;
-        const uint32_t sVs = sV0 + s * kTileBytes;
-        if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) return false;
-        for (int g = 0; g < 2; ++g) {
-          if (!mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) return false;
-          tc_fence_after();
-          const uint32_t o_col = g ? kColOB : kColOA;
-#pragma unroll
-          for (int kk = 0; kk < 4; ++kk) {
-            const uint64_t bdesc = smem_desc_sw128(sVs + (4 * g + kk) * 2048, kHalfBytes, 1024);
-            mma_ts(tmem + o_col, tmem + s * 128 + 64 * g + kk * 8, bdesc, idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
-          }
-          tc_commit(smem_u32(&C.bar_o_done[g]));
-        }
-        tc_commit(smem_u32(&C.bar_v_empty[s]));
-        return true;
-      };
+      // Descriptors differ only in the start-address field (bits 0-13, in 16-byte units).
+      const uint64_t qdesc0 = smem_desc_sw128(sQ, 16, 1024);
+      const uint64_t kdesc0 = smem_desc_sw128(sK0, 16, 1024);
       int ks = 0, kuse = 0;
       for (int j = 0; ok && j < total_tiles; ++j) {
         const int s = j & 1;
-        if (!mbar_wait(smem_u32(&C.bar_k_full[ks]), (uint32_t)(kuse & 1), abort_flag, p.status, 204)) {
-          ok = false;
+        if (!mbar_wait(smem_u32(&C.bar_k_full[ks]), (uint32_t)(kuse & 1), abort_flag, p.status, 204)) break;
+        SB_TRACE_POINT(trace, 2, j);
+        // S buffer s still holds P of tile j-2 until that P.V completes (it released its
+        // V stage).  That barrier cannot run two phases ahead: P.V of tile j needs S_j.
+        if (j >= 2 && !mbar_wait(smem_u32(&C.bar_v_empty[s]), (uint32_t)(((j - 2) >> 1) & 1), abort_flag, p.status,
+                                 205))
           break;
-        }
+        SB_TRACE_POINT(trace, 12, j);
         tc_fence_after();
-        const uint32_t sKs = sK0 + ks * kTileBytes;
+        const uint64_t kdesc = kdesc0 + (uint64_t)((ks * kTileBytes) >> 4);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
-          const uint32_t off = (kk >> 2) * kHalfBytes + (kk & 3) * 32;
-          const uint64_t adesc = smem_desc_sw128(sQ + off, 16, 1024);
-          const uint64_t bdesc = smem_desc_sw128(sKs + off, 16, 1024);
-          mma_ss(tmem + s * 128, adesc, bdesc, idesc_qk, kk > 0 ? 1u : 0u);
+          const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+          mma_ss(tmem + s * 128, qdesc0 + off, kdesc + off, idesc_qk, kk > 0 ? 1u : 0u);
         }
         tc_commit(smem_u32(&C.bar_s_full[s]));
+        SB_TRACE_POINT(trace, 3, j);
         tc_commit(smem_u32(&C.bar_k_empty[ks]));
         if (++ks == kKStages) {
           ks = 0;
           ++kuse;
         }
-        if (j >= 1 && !issue_pv(j - 1)) ok = false;
       }
-      if (ok && total_tiles > 0) issue_pv(total_tiles - 1);
+      tc_commit(smem_u32(&C.bar_s_final));
+    }
+  } else if (warp == kPvWarp) {
+    // ----------------------------------------------------------- P.V issuer
+    // O_A += P_A V[0:64), O_B += P_B V[64:128).  One wait on the shared P barrier (both
+    // groups) and one commit that releases the V stage; the softmax groups and the S
+    // issuer also use that commit to learn that this P.V has finished.
+    if (lane == 0) {
+      constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, true);
+      const uint64_t vdesc0 = smem_desc_sw128(sV0, kHalfBytes, 1024);
+      for (int i = 0; i < total_tiles; ++i) {
+        const int s = i & 1;  // S/P buffer (two in TMEM) and V stage (kVStages == 2)
+        const uint32_t par = (i >> 1) & 1;
+        const uint64_t vdesc = vdesc0 + (uint64_t)((s * kTileBytes) >> 4);
+        if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) break;
+        if (!mbar_wait(smem_u32(&C.bar_p_full[s]), par, abort_flag, p.status, 202)) break;
+        SB_TRACE_POINT(trace, 4, i);
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const int g = kk >> 2;
+          mma_ts(tmem + (g ? kColOB : kColOA), tmem + s * 128 + 64 * g + (kk & 3) * 8,
+                 vdesc + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || (kk & 3) > 0) ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&C.bar_v_empty[s]));
+        SB_TRACE_POINT(trace, 5, i);
+      }
       tc_commit(smem_u32(&C.bar_o_final));
     }
   } else {
@@ -359,11 +416,9 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int half = row >> 6;
     const int grow = row0 + row;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t s_col = 64 * grp;  // this group's S / P columns inside a buffer
-    const uint32_t o_col = grp ? kColOB : kColOA;
+    const uint32_t s_col = 64 * grp;  // this group's S columns inside a buffer
     const uint32_t* ehalf = ebits + half * words_blk;
     const float scale_log2 = 0.08838834764831845f * kLog2e;
-    const float* lm_row = p.lm ? p.lm + ((int64_t)b * p.H + h) * p.NB : nullptr;
     float m_run = -INFINITY, l_run = 0.f;
     GranuleWalker walk;
     walk.init(ubits, words_gran);
@@ -381,7 +436,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int g = grp ? g1 : g0;
         vis = g >= 0;
         if (vis) {
-          const int kb = g * 64 / p.block;
+          const int kb = g >> gshift;  // granule -> key block (block is 64 or 128)
           vis = (ehalf[kb >> 5] >> (kb & 31)) & 1u;
           key0 = g * 64;
           masked = key0 + 64 > p.T;
@@ -392,6 +447,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         ok = false;
         break;
       }
+      SB_TRACE_POINT(trace && row == 0, grp ? 10 : 7, j);
       tc_fence_after();
       uint32_t r[64];
       const bool any_vis = __any_sync(0xffffffffu, vis || !exact);
@@ -403,14 +459,13 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       // fast: unmasked exact keys, r holds raw scores; otherwise r is rewritten in place
       // with scaled (and, for summary tiles, LM-biased) logits, -inf where invisible.
       const bool fast = exact && vis && !masked;
-      float mx[8];
-#pragma unroll
-      for (int i = 0; i < 8; ++i) mx[i] = -INFINITY;
+      float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
       if (fast) {
 #pragma unroll
-        for (int i = 0; i < 64; ++i) mx[i & 7] = fmaxf(mx[i & 7], __uint_as_float(r[i]));
+        for (int i = 0; i < 64; i += 2)
+          mx[(i >> 1) & 3] = max3(mx[(i >> 1) & 3], __uint_as_float(r[i]), __uint_as_float(r[i + 1]));
 #pragma unroll
-        for (int i = 0; i < 8; ++i) mx[i] *= scale_log2;
+        for (int i = 0; i < 4; ++i) mx[i] *= scale_log2;
       } else if (!exact) {
         // Summary entries e0 .. e0+63 of this group: logit + LM * log2(e), or -inf when the
         // block is exact for this half (or past the last block).
@@ -419,14 +474,20 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int wq = 0; wq < 2; ++wq) {
           const int eb = e0 + 32 * wq;
           const uint32_t ex = eb < p.NB ? ehalf[eb >> 5] : 0xffffffffu;
+          const int valid = p.NB - eb;
+          const uint32_t live = valid >= 32 ? ~ex : (valid <= 0 ? 0u : (~ex & ((1u << valid) - 1u)));
+          const float4* lm4 = reinterpret_cast<const float4*>(lm_s + eb);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int e = eb + i;
-            const bool visible = e < p.NB && !((ex >> i) & 1u);
-            const float v = visible ? fmaf(__uint_as_float(r[32 * wq + i]), scale_log2, __ldg(lm_row + e) * kLog2e)
-                                    : -INFINITY;
-            r[32 * wq + i] = __float_as_uint(v);
-            mx[i & 7] = fmaxf(mx[i & 7], v);
+          for (int i4 = 0; i4 < 8; ++i4) {
+            const float4 l4 = lm4[i4];
+            const float lv[4] = {l4.x, l4.y, l4.z, l4.w};
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+              const int i = 4 * i4 + u;
+              const float v = ((live >> i) & 1u) ? fmaf(__uint_as_float(r[32 * wq + i]), scale_log2, lv[u]) : -INFINITY;
+              r[32 * wq + i] = __float_as_uint(v);
+              mx[i & 3] = fmaxf(mx[i & 3], v);
+            }
           }
         }
       } else if (vis) {
@@ -434,13 +495,13 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int i = 0; i < 64; ++i) {
           const float v = key0 + i < p.T ? __uint_as_float(r[i]) * scale_log2 : -INFINITY;
           r[i] = __float_as_uint(v);
-          mx[i & 7] = fmaxf(mx[i & 7], v);
+          mx[i & 3] = fmaxf(mx[i & 3], v);
         }
       }
-      const float tile_max = fmaxf(fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])),
-                                   fmaxf(fmaxf(mx[4], mx[5]), fmaxf(mx[6], mx[7])));
-      // Lazy rescale of this group's O: only when the running max grows by more than
-      // the threshold (or becomes finite for the first time).
+      const float tile_max = fmaxf(max3(mx[0], mx[1], mx[2]), mx[3]);
+      SB_TRACE_POINT(trace && row == 0 && grp == 0, 8, j);
+      // Lazy rescale of this group's O: only when the running max grows by more than the
+      // threshold (or becomes finite for the first time).
       const float m_new = fmaxf(m_run, tile_max);
       const bool need = (m_new > m_run + kRescaleThreshold) || (m_run == -INFINITY && m_new != -INFINITY);
       float alpha = 1.f;
@@ -448,8 +509,11 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_new);
         m_run = m_new;
       }
+      // P.V of tile j-1 has finished once its V stage was released; that barrier cannot
+      // be two phases ahead, since P.V of tile j+1 needs this group's P of tile j+1.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        const bool got_o = mbar_wait(smem_u32(&C.bar_o_done[grp]), (uint32_t)((j - 1) & 1), abort_flag, p.status, 302);
+        const bool got_o = mbar_wait(smem_u32(&C.bar_v_empty[(j - 1) & 1]), (uint32_t)(((j - 1) >> 1) & 1), abort_flag,
+                                     p.status, 302);
         if (!__all_sync(0xffffffffu, got_o)) {
           ok = false;
           break;
@@ -458,7 +522,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         uint32_t o[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const uint32_t ta = tmem + lane_base + o_col + 32 * c;
+          const uint32_t ta = tmem + lane_base + (grp ? kColOB : kColOA) + 32 * c;
           tmem_ld32(ta, o);
           tmem_wait_ld();
 #pragma unroll
@@ -470,54 +534,52 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       l_run *= alpha;
       const float base_m = m_run == -INFINITY ? 0.f : m_run;
       uint32_t pk[32];
-      float sums[4] = {0.f, 0.f, 0.f, 0.f};
-      if (fast) {
-        // p = 2^(s * scale_log2 - m); every 4th pair uses the polynomial exp2.
-        const float nb_m = -base_m;
+      uint64_t sums[2] = {0ull, 0ull};  // packed partial sums
+      if (!exact || vis) {
+        // p = 2^(s * scale - m) (fast path) or 2^(logit - m); pairs share one packed
+        // multiply-add.  On the fast path every 4th pair takes the polynomial exp2 on the
+        // FMA pipe, offloading the MUFU unit.
+        const uint64_t mul2 = fast ? f2_pack(scale_log2, scale_log2) : f2_pack(1.f, 1.f);
+        const uint64_t neg2 = f2_pack(-base_m, -base_m);
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const float a0 = fmaf(__uint_as_float(r[2 * c]), scale_log2, nb_m);
-          const float a1 = fmaf(__uint_as_float(r[2 * c + 1]), scale_log2, nb_m);
-          float p0, p1;
-          if ((c & 3) == 3) {
-            p0 = exp2_poly(a0);
-            p1 = exp2_poly(a1);
+          const uint64_t a2 = f2_fma(f2_pack(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])), mul2, neg2);
+          float a0, a1, p0, p1;
+          f2_unpack(a2, a0, a1);
+          if (fast && (c & 3) == 3) {
+            exp2_poly2(a0, a1, p0, p1);
           } else {
             p0 = ex2_approx(a0);
             p1 = ex2_approx(a1);
           }
-          sums[c & 3] += p0 + p1;
-          pk[c] = pack_bf16(p0, p1);
-        }
-      } else if (!exact || vis) {
-#pragma unroll
-        for (int c = 0; c < 32; ++c) {
-          const float p0 = ex2_approx(__uint_as_float(r[2 * c]) - base_m);
-          const float p1 = ex2_approx(__uint_as_float(r[2 * c + 1]) - base_m);
-          sums[c & 3] += p0 + p1;
-          pk[c] = pack_bf16(p0, p1);
+          sums[c & 1] = f2_add(sums[c & 1], f2_pack(p0, p1));
+          pk[c] = cvt_bf16x2(p0, p1);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) pk[c] = 0u;
       }
-      const float sum = (sums[0] + sums[1]) + (sums[2] + sums[3]);
-      l_run += sum;
+      float s0, s1, s2, s3;
+      f2_unpack(sums[0], s0, s1);
+      f2_unpack(sums[1], s2, s3);
+      l_run += (s0 + s1) + (s2 + s3);
       tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(smem_u32(&C.bar_p_full[grp][s]));
+      mbar_arrive(smem_u32(&C.bar_p_full[s]));
+      SB_TRACE_POINT(trace && row == 0, grp ? 11 : 9, j);
     }
-    // Epilogue: merge the two groups' partial softmaxes; group g writes head-dim columns
-    // 64g .. 64g+63 of the output row.
+    // Epilogue: merge the two groups' partial softmaxes (bounded mbarrier exchange);
+    // group g writes head-dim columns 64g .. 64g+63 of the output row.
     const bool got_final = ok && mbar_wait(smem_u32(&C.bar_o_final), 0, abort_flag, p.status, 303);
-    C.merge_m[grp][row] = m_run;
-    C.merge_l[grp][row] = l_run;
-    named_barrier_sync(1, 256);
-    if (__all_sync(0xffffffffu, got_final)) {
+    C.xmax[grp][row] = m_run;
+    C.xsum[grp][row] = l_run;
+    mbar_arrive(smem_u32(&C.bar_xsum));
+    const bool got_sum = got_final && mbar_wait(smem_u32(&C.bar_xsum), 0, abort_flag, p.status, 306);
+    if (__all_sync(0xffffffffu, got_sum)) {
       tc_fence_after();
-      const float ma = C.merge_m[0][row], mb = C.merge_m[1][row];
-      const float la = C.merge_l[0][row], lb = C.merge_l[1][row];
+      const float ma = C.xmax[0][row], mb = C.xmax[1][row];
+      const float la = C.xsum[0][row], lb = C.xsum[1][row];
       const float m = fmaxf(ma, mb);
       const float fa = ma == -INFINITY ? 0.f : ex2_approx(ma - m);
       const float fb = mb == -INFINITY ? 0.f : ex2_approx(mb - m);
@@ -552,8 +614,9 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   __syncthreads();
   if (warp == kMmaWarp) {
     tc_fence_after();
-    // The final commit covers every MMA this CTA issued.
+    // The two final commits cover every MMA this CTA issued.
     mbar_drain(smem_u32(&C.bar_o_final), 0);
+    mbar_drain(smem_u32(&C.bar_s_final), 0);
     tmem_dealloc(tmem, kTmemCols);
   }
 }
@@ -613,8 +676,8 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
     mav = mv;
   }
   const int n64 = ceil_div(p.T, 64);
-  const SmemLayout L = smem_layout(p.words, ceil_div(n64, 32));
-  const size_t smem = L.total + 1024;  // slack for the 1024-byte alignment of the base
+  const SmemLayout L = smem_layout(p.words, ceil_div(n64, 32), 128 * ceil_div(p.NB, 128));
+  const size_t smem = L.total;
   if (smem > 227 * 1024) {
     set_error("sb_sparse_attention: sequence too long for the tensor-core kernel (%zu bytes of shared memory)", smem);
     return SB_ERR_UNSUPPORTED;
@@ -629,3 +692,10 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
 }
 
 }  // namespace sb
+
+#ifdef SB_TRACE
+extern "C" int sb_trace_setup(int cta) { return (int)cudaMemcpyToSymbol(sb::g_trace_cta, &cta, sizeof(int)); }
+extern "C" int sb_trace_dump(long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, sb::g_trace, sizeof(long long) * 16 * 4096);
+}
+#endif
