@@ -103,6 +103,26 @@ int sb_route_topk(const float* qc, const void* kc, int kc_dtype, int B, int QB, 
                   void* stream);
 
 /*
+ * Allocation-free variant of sb_route_topk; no counterpart in the reference.
+ * For callers that cannot pass a device workspace, for instance a host that binds only this
+ * library through a thin FFI and owns no device allocator, or a serving loop that cannot
+ * accept the device synchronisation cudaMalloc implies.  The block scores live in a
+ * file-scope device array of SB_ROUTE_NOALLOC_SCRATCH_FLOATS floats (16 MiB), which every GPU
+ * that loads the library holds until the process exits.  Query blocks are processed in
+ * chunks that fit it, so the outputs equal sb_route_topk's; sizes with
+ * H * candidates > SB_ROUTE_NOALLOC_SCRATCH_FLOATS are rejected with SB_ERR_INVALID.
+ * No cudaMalloc, cudaFree or allocating library routine is called.  The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) and caches it; make
+ * that first call before any stream capture.  All calls share the one array: calls that
+ * overlap on the GPU (other streams, other host threads) race and must be serialised by
+ * the caller.  Every score a call reads was written earlier in the same call.
+ */
+#define SB_ROUTE_NOALLOC_SCRATCH_FLOATS (4 * 1024 * 1024)
+int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
+                          int H, int D, int candidates, int topk, float scale_log2,
+                          int32_t* packed_route, int32_t* indices, void* stream);
+
+/*
  * Sparse attention forward.  Replaces sol_numerator_virtual_q.py:717-977
  * (_fused_virtual -> SparkReweightForwardSm*) with the semantics of the streamed
  * oracle at sol_numerator_virtual_q.py:596-652 and

@@ -3,6 +3,9 @@
 //
 // score = fp32(sequential fused multiply-add over d of qc[d] * kc[d]) * scale_log2.
 // The CPU oracle computes the identical chain, so selections agree bit for bit.
+#include <algorithm>
+#include <mutex>
+
 #include "common.cuh"
 
 namespace sb {
@@ -211,5 +214,98 @@ extern "C" int sb_route_topk(const float* qc, const void* kc, int kc_dtype, int 
   SB_CHECK_ARG(rows < (1ll << 31), "sb_route_topk: too many rows");
   topk_rows_kernel<<<(unsigned)rows, kTopkThreads, key_smem, s>>>(scores, candidates, topk, words, packed_route, indices);
   SB_CHECK_LAUNCH("sb_route_topk: top-k launch");
+  return SB_OK;
+}
+
+// ------------------------------------------------------------------------------------------
+// Allocation-free variant of sb_route_topk.
+//
+// Some callers cannot hand this library a device workspace: a host that binds only this C ABI
+// through a thin FFI and owns no device allocator, or a serving loop that will not accept the
+// implicit device synchronisation cudaMalloc performs.  sb_route_topk_noalloc keeps the block
+// scores in the file-scope array below instead, and works through the query blocks in chunks
+// whose scores fit it, so any size whose per-query-block scores (H * candidates floats) fit
+// the array is accepted.
+constexpr int64_t kNoAllocScoreFloats = SB_ROUTE_NOALLOC_SCRATCH_FLOATS;
+static __device__ __align__(256) float g_route_noalloc_scratch[kNoAllocScoreFloats];
+
+// Device address of the scratch array on the current device, looked up once per device
+// (the symbol name is only a host-side stand-in; a kernel must be given this address).
+static float* route_noalloc_scratch(int* status) {
+  static std::mutex mu;
+  static float* cached[64] = {nullptr};
+  int dev = 0;
+  cudaError_t err = cudaGetDevice(&dev);
+  if (err != cudaSuccess) {
+    *status = cuda_error(err, "sb_route_topk_noalloc: cudaGetDevice");
+    return nullptr;
+  }
+  if (dev < 0 || dev >= 64) {
+    set_error("sb_route_topk_noalloc: device ordinal %d out of range", dev);
+    *status = SB_ERR_UNSUPPORTED;
+    return nullptr;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (cached[dev] == nullptr) {
+    void* ptr = nullptr;
+    err = cudaGetSymbolAddress(&ptr, g_route_noalloc_scratch);
+    if (err != cudaSuccess) {
+      *status = cuda_error(err, "sb_route_topk_noalloc: cudaGetSymbolAddress of the scratch array");
+      return nullptr;
+    }
+    cached[dev] = static_cast<float*>(ptr);
+  }
+  return cached[dev];
+}
+
+extern "C" int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB, int H,
+                                     int D, int candidates, int topk, float scale_log2, int32_t* packed_route,
+                                     int32_t* indices, void* stream) {
+  SB_CHECK_ARG(qc && kc && packed_route, "sb_route_topk_noalloc: null pointer");
+  SB_CHECK_ARG(kc_dtype == SB_F32 || kc_dtype == SB_BF16, "sb_route_topk_noalloc: bad key-centroid dtype");
+  SB_CHECK_ARG(B > 0 && QB > 0 && NB > 0 && H > 0, "sb_route_topk_noalloc: sizes must be positive");
+  SB_CHECK_ARG(QB <= NB, "sb_route_topk_noalloc: QB (%d) exceeds NB (%d)", QB, NB);
+  SB_CHECK_ARG(D == 64 || D == 128, "sb_route_topk_noalloc: head dim must be 64 or 128");
+  SB_CHECK_ARG(candidates >= 1 && candidates <= NB,
+               "sb_route_topk_noalloc: candidates must lie in [1, NB], got %d", candidates);
+  SB_CHECK_ARG(topk >= 1 && topk <= candidates,
+               "sb_route_topk_noalloc: topk must lie in [1, candidates], got %d", topk);
+  const int words = ceil_div(NB, 32);
+  SB_CHECK_ARG(words <= 256, "sb_route_topk_noalloc: at most 8192 key blocks are supported");
+  const size_t key_smem = (size_t)candidates * sizeof(uint32_t);
+  SB_CHECK_ARG(key_smem <= 200 * 1024, "sb_route_topk_noalloc: too many candidate blocks (%d)", candidates);
+  const int64_t per_block = (int64_t)H * candidates;
+  SB_CHECK_ARG(per_block <= kNoAllocScoreFloats,
+               "sb_route_topk_noalloc: H * candidates = %lld exceeds the %lld-float scratch array "
+               "(SB_ROUTE_NOALLOC_SCRATCH_FLOATS); use sb_route_topk with a caller workspace",
+               (long long)per_block, (long long)kNoAllocScoreFloats);
+  int status = SB_OK;
+  float* scratch = route_noalloc_scratch(&status);
+  if (scratch == nullptr) return status;
+  cudaStream_t s = (cudaStream_t)stream;
+  cudaError_t err = cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)key_smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_route_topk_noalloc: set smem");
+  const int chunk = (int)std::min<int64_t>(QB, kNoAllocScoreFloats / per_block);
+  const size_t kc_elem = kc_dtype == SB_BF16 ? 2 : 4;
+  for (int b = 0; b < B; ++b) {
+    const char* kc_b = static_cast<const char*>(kc) + (size_t)b * NB * H * D * kc_elem;
+    for (int q0 = 0; q0 < QB; q0 += chunk) {
+      const int n = std::min(chunk, QB - q0);
+      const float* qc_c = qc + ((int64_t)b * NB + q0) * H * D;
+      dim3 grid(ceil_div(candidates, kScoreTile), ceil_div(n, kScoreTile), H);
+      int rc;
+      if (kc_dtype == SB_BF16)
+        rc = D == 128 ? launch_scores<__nv_bfloat16, 128>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s)
+                      : launch_scores<__nv_bfloat16, 64>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
+      else
+        rc = D == 128 ? launch_scores<float, 128>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s)
+                      : launch_scores<float, 64>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
+      if (rc != SB_OK) return rc;
+      const int64_t row0 = ((int64_t)b * QB + q0) * H;
+      topk_rows_kernel<<<(unsigned)((int64_t)n * H), kTopkThreads, key_smem, s>>>(
+          scratch, candidates, topk, words, packed_route + row0 * words, indices ? indices + row0 * topk : nullptr);
+      SB_CHECK_LAUNCH("sb_route_topk_noalloc: top-k launch");
+    }
+  }
   return SB_OK;
 }

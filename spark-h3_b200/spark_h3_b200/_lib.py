@@ -31,6 +31,7 @@ SIGNATURES = {
     "sb_pool_keys_summaries": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
     "sb_route_workspace_bytes": (_i64, [_i, _i, _i, _i]),
     "sb_route_topk": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
+    "sb_route_topk_noalloc": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
     "sb_headwise_permute": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
