@@ -1,5 +1,18 @@
-"""B200-native (sm_100a) Spark-H3 adaptive block-sparse attention."""
-from . import ops
-from .ops import spark_layer
+"""B200-native (sm_100a) Spark-H3 adaptive block-sparse attention.
 
-__all__ = ["ops", "spark_layer"]
+Drop-in names of the reference package (`h3_sparse_attention`): the installers and config,
+the attention seam `spark_attention_bthd`, and the `spark_reweight` primitive.  Kernels live
+in libsparkh3b200.so (C ABI, include/spark_h3_b200.h) and always run on the GPU.
+"""
+from .attention import spark_attention_bthd, spark_reweight
+from .config import H3SparseAttentionConfig
+from .layout import PackedLayout, packed_layout
+from .processor import (H3SparseAttentionPlugin, install_h3_sol_attn, install_h3_spark_attn,
+                        install_h3_sparse_attention)
+from . import ops
+
+__all__ = [
+    "H3SparseAttentionConfig", "H3SparseAttentionPlugin", "PackedLayout", "install_h3_spark_attn",
+    "install_h3_sol_attn", "install_h3_sparse_attention", "ops", "packed_layout", "spark_attention_bthd",
+    "spark_reweight",
+]

@@ -1,0 +1,147 @@
+"""Spark sparse attention on packed BTHD tensors: the seam the C ABI replaces.
+
+`spark_attention_bthd` has the contract of
+h3_sparse_attention/spark_integration.py:883-1283 (video tokens first, context after; rows
+past the last complete video block attend densely; output in packed order) and runs the
+whole layer on the GPU through libsparkh3b200.so:
+    pool Q -> global anchor -> pool K + summaries -> scores + Top-K -> sparse attention.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from . import ops
+from .hierarchy import build_reblock_hierarchy, virtual_query_layout
+
+BACKEND_TENSOR = "b200_sm100_fused_virtual_query"
+BACKEND_SIMT = "b200_simt_virtual_query"
+
+
+def sparse_query_tokens(total_tokens: int, video_tokens: int, block: int, tail_mode: str = "dense") -> int:
+    """Query prefix evaluated sparsely (spark_integration.py:72-91): whole video blocks."""
+    if tail_mode == "dense":
+        return min(total_tokens, (video_tokens // block) * block)
+    if tail_mode != "pad":
+        raise ValueError("tail_mode must be 'dense' or 'pad'")
+    padded = math.ceil(video_tokens / block) * block
+    if padded > total_tokens:
+        raise ValueError("the packed suffix is too short to pad the final video query block")
+    return padded
+
+
+def reweight_flags(components: str) -> tuple[bool, bool]:
+    """(anchor-weighted K/V, log-mass bias) for sol_reweight_components
+    (sol_numerator_virtual_q.py:224-231)."""
+    return components in ("full", "weights_only"), components in ("full", "bias_only")
+
+
+def topk_density(stats: dict) -> dict:
+    """Analytic density of a fixed Top-K budget (spark_integration.py:228-242)."""
+    selected = min(stats["target_topk_blocks_per_query"], stats["candidate_video_blocks"])
+    return dict(additional_topk_density=selected / stats["candidate_video_blocks"],
+                effective_video_density=selected / stats["candidate_video_blocks"],
+                effective_packed_density=(selected + stats["sink_blocks"]) / stats["blocks"])
+
+
+def _check_inputs(q, k, v):
+    if q.shape != k.shape or q.shape != v.shape:
+        raise RuntimeError("Spark attention requires matching BTHD Q/K/V tensors")
+    if not (q.is_contiguous() and k.is_contiguous() and v.is_contiguous()):
+        raise RuntimeError("Spark attention requires contiguous BTHD Q/K/V tensors")
+    if q.device.type != "cuda":
+        raise RuntimeError("Spark-H3 requires CUDA tensors")
+    if q.dtype not in (torch.bfloat16, torch.float32) or q.shape[-1] not in (64, 128) or k.dtype != q.dtype:
+        raise RuntimeError("the B200 Spark kernels take BF16 or FP32 Q/K/V with head dimension 64 or 128; "
+                           f"got dtype={q.dtype}, head_dim={q.shape[-1]}")
+    capability = tuple(torch.cuda.get_device_capability(q.device))
+    if capability != (10, 0):
+        raise RuntimeError(f"the B200 Spark kernels are built for SM100 only; got SM{capability[0]}{capability[1]}")
+
+
+def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, return_bthd: bool = True,
+                         workspace: torch.Tensor | None = None):
+    cfg = controller.config
+    _check_inputs(q_bthd, k_bthd, v_bthd)
+    if cfg.sol_route_topk_ratio is None:
+        raise RuntimeError("the B200 path implements Top-K routed Spark attention; set sol_route_topk_ratio")
+    if cfg.sol_landmark_preprocess:
+        raise NotImplementedError("landmark-v2 reblocking (modes 'full' and 'reblock_only') is not available on the "
+                                  "B200 path yet; use mode='reweight_only' or 'topk_only'")
+    if cfg.sol_video_tail_mode != "dense" or cfg.sol_legacy_full_query:
+        raise NotImplementedError("the B200 path implements sol_video_tail_mode='dense' only")
+    if cfg.sol_tail_granularity != "query" or cfg.sol_reweight_summary_math != "tensorcore" \
+            or cfg.sol_reweight_logmass_key != "stored":
+        raise NotImplementedError("the B200 path implements the default reweight numerics "
+                                  "(tail granularity 'query', tensorcore summaries, stored log-mass key)")
+    if getattr(controller, "head_topk_budget", None) is not None:
+        raise NotImplementedError("per-head Top-K budgets are not available on the B200 path")
+    B, T, H, D = q_bthd.shape
+    block = cfg.sol_block_size
+    video = int(layout.video_tokens)
+    if video < block:
+        raise RuntimeError(f"Spark routing requires at least one complete {block}-token video block")
+    query_tokens = sparse_query_tokens(T, video, block, cfg.sol_video_tail_mode)
+    query_blocks = query_tokens // block
+    candidates = video // block
+    nb = math.ceil(T / block)
+    sink_tokens = layout.sequence_length - video
+    sink_first = video // block
+    sink_last = math.ceil((video + sink_tokens) / block) if sink_tokens else sink_first
+    topk = ops.target_topk(cfg.sol_route_topk_ratio, candidates)
+    weighted_kv, mass_bias = reweight_flags(cfg.sol_reweight_components)
+    anchor_dtype = torch.float32 if cfg.sol_global_anchor_dtype == "float32" or q_bthd.dtype == torch.float32 \
+        else q_bthd.dtype
+
+    qc = ops.pool_queries(q_bthd, block)
+    anchor = ops.query_anchor(qc, block, query_blocks, anchor_dtype)
+    kc, ak, av, lm = ops.pool_keys_summaries(k_bthd, v_bthd, anchor, block, weighted_kv=weighted_kv,
+                                             mass_bias=mass_bias)
+    packed, _ = ops.route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace, want_indices=False)
+    out, _ = ops.sparse_attention(q_bthd, k_bthd, v_bthd, block, packed, ak, av, lm, query_tokens=query_tokens,
+                                  sink_first=sink_first, sink_last=sink_last, local_radius=cfg.kernel_local_radius)
+
+    controller.sol_backend = BACKEND_TENSOR if (q_bthd.dtype == torch.bfloat16 and D == 128) else BACKEND_SIMT
+    controller.counts["sol_topk_packed_route_calls"] += 1
+    controller.counts["sol_virtual_query_calls"] += 1
+    controller.counts["sol_identity_virtual_query_calls"] += 1
+    if cfg.sol_spark_mode == "reweight_only":
+        controller.counts["sol_identity_reweight_calls"] += 1
+    controller.counts["sol_topk_calls"] += 1
+    if T > query_tokens:
+        controller.counts["sol_dense_context_queries"] += 1
+    key = ("identity_global_anchor", T, video, layout.grid)
+    topology = controller._virtual_query_layout_cache.get(key)
+    if topology is None and video >= 64:
+        hierarchy = build_reblock_hierarchy(video, cfg.landmark_tree_v2_children, grid_shape=tuple(layout.grid),
+                                            fanout_mode=cfg.landmark_tree_v2_fanout_mode)
+        topology = dict(virtual_query_layout(video, T, 99, hierarchy=hierarchy)["metadata"])
+        controller._virtual_query_layout_cache[key] = topology
+    if topology is not None:
+        controller.sol_virtual_query_layout = {**topology, "layout": "identity_physical_order",
+                                               "anchor_policy": "global"}
+    if cfg.sol_log_density and controller.sol_route_density is None:
+        stats = dict(block_size=block, blocks=nb, candidate_video_blocks=candidates, query_video_blocks=query_blocks,
+                     sink_blocks=max(0, nb - candidates), route_threshold_mode="gemm_exact_topk_packed_external",
+                     route_topk_ratio=cfg.sol_route_topk_ratio, target_topk_blocks_per_query=topk,
+                     packed_route_words=math.ceil(nb / 32))
+        stats.update(topk_density(stats))
+        controller.sol_route_density = stats
+    return out if return_bthd else out.permute(0, 2, 1, 3).contiguous()
+
+
+def spark_reweight(a: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int = 64,
+                   reweight_components: str = "full"):
+    """Anchor-conditioned summaries for query representatives a[B, P, H, D] and keys/values
+    k, v[B, T, H, D]: returns (AK, AV [B, P, H, NB, D], LM [B, P, H, NB]) like the reference's
+    spark_reweight = virtual_summaries (sol_numerator_virtual_q.py:334-353)."""
+    if a.ndim != 4 or k.ndim != 4 or v.shape != k.shape or a.shape[0] != k.shape[0] or a.shape[2:] != k.shape[2:]:
+        raise ValueError("requires nonempty A[BP H D] and matching K/V[BT H D]")
+    weighted_kv, mass_bias = reweight_flags(reweight_components)
+    parts = []
+    for p in range(a.shape[1]):
+        _, ak, av, lm = ops.pool_keys_summaries(k, v, a[:, p].contiguous(), block, weighted_kv=weighted_kv,
+                                                mass_bias=mass_bias, want_kc=False)
+        parts.append((ak, av, lm))
+    return tuple(torch.stack([part[i] for part in parts], dim=1) for i in range(3))

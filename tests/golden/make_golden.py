@@ -1,0 +1,184 @@
+"""Generate the golden fixtures in this directory from the reference's own code.
+
+Run in a container that has the read-only reference checkout (default /root/reference, or
+$SPARK_H3_REFERENCE); the tests only read the committed fixtures and never import the
+reference.  Inputs are regenerated deterministically by the tests from the recorded seeds
+(torch CPU generator) and checked against the recorded SHA-256 digests first.
+
+    python tests/golden/make_golden.py
+
+Fixtures:
+  hierarchy.json  build_reblock_hierarchy / virtual_query_layout (reblock_hierarchy.py,
+                  landmark_virtual_q.py) for a set of fanout schedules
+  layout.json     _packed_layout (processor.py:550-688) on tag/position patterns
+  route_*.npz     _sol_topk_policy_scores + _sol_topk_route_from_scores
+                  (spark_integration.py:94-175): the selected block sets per row, and the
+                  gap between the k-th and (k+1)-th score of every row
+  summaries.npz   the Triton _summaries kernel (sol_numerator_virtual_q.py:93-135) run under
+                  TRITON_INTERPRET=1 in fp32 at D=128
+  attention.npz   the explicit exact/summary softmax of tests/test_spark_installer.py:559-570
+                  applied to the reference's route and summaries (fp32)
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import math
+import os
+import sys
+from pathlib import Path
+
+os.environ.setdefault("TRITON_INTERPRET", "1")
+HERE = Path(__file__).resolve().parent
+ROOT = HERE.parents[1]
+REFERENCE = Path(os.environ.get("SPARK_H3_REFERENCE", "/root/reference"))
+sys.path[:0] = [str(REFERENCE), str(ROOT), str(ROOT / "spark-h3_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+
+def digest(t: torch.Tensor) -> str:
+    t = t.detach().cpu().contiguous()
+    raw = t.view(torch.int16).numpy() if t.dtype == torch.bfloat16 else t.numpy()
+    return hashlib.sha256(raw.tobytes()).hexdigest()
+
+
+def hierarchy_cases():
+    from h3_sparse_attention.landmark_virtual_q import virtual_query_layout
+    from h3_sparse_attention.reblock_hierarchy import build_reblock_hierarchy
+
+    cases = []
+    for video, children, mode, final in [
+        (72576, 16, "power_of_two_fanout", None), (4096, 16, "power_of_two_fanout", None),
+        (245952, 16, "power_of_two_fanout", None), (124992, 16, "power_of_two_fanout", None),
+        (124992, (8, 4), "power_of_two_fanout", None), (245952, 8, "arbitrary_fanout", None),
+        (245952, 16, "arbitrary_fanout", 12), (100000, 4, "power_of_two_arbitrary_final", 6),
+        (64 * 37, 2, "power_of_two_fanout", None), (64 * 1000, 32, "arbitrary_fanout", None),
+    ]:
+        h = build_reblock_hierarchy(video, children, fanout_mode=mode, final_fanout=final)
+        layout = virtual_query_layout(video, video + 999, 99, hierarchy=h)
+        levels = [list(map(list, level)) for level in h.levels]
+        cases.append(dict(video_tokens=video, children=children, fanout_mode=mode, final_fanout=final,
+                          levels=levels if video <= 8192 else None,
+                          levels_digest=hashlib.sha256(json.dumps(levels).encode()).hexdigest(),
+                          split_budgets=[[[size, list(b)] for size, b in rnd] for rnd in h.split_budgets],
+                          layout_ranges=[list(r) for r in layout["ranges"]],
+                          layout_metadata={k: layout["metadata"][k] for k in (
+                              "active_virtual_blocks", "total_virtual_blocks", "global_video_representative",
+                              "total_split_levels")}))
+    return cases
+
+
+def layout_cases():
+    from h3_sparse_attention.processor import _packed_layout
+
+    out = []
+    # video grid (3, 4, 5) shuffled, 7 text tokens interleaved
+    g = torch.Generator().manual_seed(5)
+    grid = torch.cartesian_prod(torch.arange(3), torch.arange(4), torch.arange(5))
+    order = torch.randperm(60, generator=g)
+    tags = torch.cat([torch.zeros(60, dtype=torch.long), torch.ones(7, dtype=torch.long)])
+    pos = torch.cat([grid[order], torch.zeros(7, 3, dtype=torch.long)])
+    mix = torch.randperm(67, generator=g)
+    tags, pos = tags[mix], pos[mix]
+    lay = _packed_layout(tags, pos)
+    out.append(dict(kind="tags_only", tags=tags.tolist(), positions=pos.tolist(),
+                    permutation=lay.permutation.tolist(), grid=list(lay.grid), video_tokens=lay.video_tokens))
+    # structural target suffix with conditioning video
+    tags = torch.tensor([0, 0, 1, 2, 0, 0, 0, 0])
+    pos = torch.tensor([[0, 0, 0], [0, 0, 1], [0, 0, 0], [0, 0, 0], [0, 1, 1], [0, 0, 0], [0, 1, 0], [0, 0, 1]])
+    for scope in ("target", "target_and_condition"):
+        ts = torch.tensor([1, 1, 0, 0, 0, 0, 0, 0]) if scope == "target_and_condition" else torch.zeros(8).long()
+        kwargs = dict(video_indices=torch.tensor([0, 1, 4, 5, 6, 7]), timestep_indices=ts,
+                      text_indices=torch.tensor([2]), sparse_video_scope=scope)
+        lay = _packed_layout(tags, pos, **kwargs)
+        out.append(dict(kind="indexed", scope=scope, tags=tags.tolist(), positions=pos.tolist(),
+                        video_indices=[0, 1, 4, 5, 6, 7], timestep_indices=ts.tolist(), text_indices=[2],
+                        permutation=lay.permutation.tolist(), grid=list(lay.grid), video_tokens=lay.video_tokens,
+                        target_video_tokens=lay.target_video_tokens,
+                        condition_video_tokens=lay.condition_video_tokens))
+    return out
+
+
+def block_mean(x: torch.Tensor, block: int) -> torch.Tensor:
+    """fp32 block mean (the reference's query centroid; for keys it is then rounded)."""
+    B, T, H, D = x.shape
+    nb = math.ceil(T / block)
+    pad = torch.nn.functional.pad(x.float(), (0, 0, 0, 0, 0, nb * block - T))
+    counts = torch.full((nb,), float(block))
+    counts[-1] = T - (nb - 1) * block
+    return pad.view(B, nb, block, H, D).sum(2) / counts.view(1, nb, 1, 1)
+
+
+def route_case(name, grid, heads, dim, dtype, q_scale, seed):
+    from h3_sparse_attention.spark_integration import _sol_topk_policy_scores, _sol_topk_route_from_scores
+    from spark_h3_b200.synthetic import make_qkv
+
+    q, k, v = make_qkv(grid, heads, dim, seed=seed, dtype=dtype, q_scale=q_scale)
+    T = q.shape[1]
+    kc = block_mean(k, 64).to(dtype)
+    scores, adjacent, cand, qblocks, target = _sol_topk_policy_scores(q, kc, video_tokens=T, topk_ratio=0.1)
+    route = _sol_topk_route_from_scores(scores, adjacent, candidate_blocks=cand, target_topk=target,
+                                        video_tokens=T, sink_tokens=0)
+    s = scores[..., :cand]
+    top = torch.sort(s, dim=-1, descending=True).values
+    gap = (top[..., target - 1] - top[..., target]).float() if target < cand else torch.full(top.shape[:-1], np.inf)
+    np.savez_compressed(HERE / f"route_{name}.npz", route=route[:, :qblocks, :, :cand].numpy().astype(np.uint8),
+                        gap=gap.numpy().astype(np.float32), kc_digest=np.array(digest(kc)),
+                        q_digest=np.array(digest(q)), k_digest=np.array(digest(k)), target=np.array(target),
+                        meta=np.array(json.dumps(dict(grid=grid, heads=heads, dim=dim, dtype=str(dtype),
+                                                      q_scale=q_scale, seed=seed))))
+
+
+def summaries_and_attention():
+    import triton
+    from h3_sparse_attention.sol_numerator_virtual_q import _summaries
+    from h3_sparse_attention.spark_integration import _sol_topk_policy_scores, _sol_topk_route_from_scores
+
+    gen = torch.Generator().manual_seed(17)
+    B, T, H, D = 1, 1000, 2, 128
+    q = torch.randn(B, T, H, D, generator=gen) * D ** -0.5
+    k = torch.randn(B, T, H, D, generator=gen)
+    v = torch.randn(B, T, H, D, generator=gen)
+    a = q[:, :960].mean(1, keepdim=True)  # anchor over the complete 64-token blocks
+    n = triton.cdiv(T, 64)
+    ak = torch.empty(B, 1, H, n, D)
+    av = torch.empty_like(ak)
+    lm = torch.empty(B, 1, H, n)
+    _summaries[(1, n, B * H)](a, k, v, ak, av, lm, T, H, n, 1, a.stride(0), a.stride(1), 0, 1, 16, H, 0, True, False,
+                              True, True, False, num_warps=4)
+    np.savez_compressed(HERE / "summaries.npz", a=a.numpy(), ak=ak.numpy(), av=av.numpy(), lm=lm.numpy(),
+                        q_digest=np.array(digest(q)), k_digest=np.array(digest(k)), v_digest=np.array(digest(v)))
+    kc = block_mean(k, 64)
+    scores, adjacent, cand, qblocks, target = _sol_topk_policy_scores(q, kc, video_tokens=960, topk_ratio=0.2)
+    route = _sol_topk_route_from_scores(scores, adjacent, candidate_blocks=cand, target_topk=target,
+                                        video_tokens=960, sink_tokens=40)
+    out = torch.empty_like(q)
+    for h in range(H):
+        for blk in range(960 // 64):
+            rows = slice(blk * 64, (blk + 1) * 64)
+            exact = route[0, blk, h].repeat_interleave(64)[:T]
+            approx = ~route[0, blk, h]
+            keys = torch.cat([k[0, exact, h], ak[0, 0, h, approx]])
+            vals = torch.cat([v[0, exact, h], av[0, 0, h, approx]])
+            logits = q[0, rows, h] @ keys.T / D ** 0.5
+            logits[:, int(exact.sum()):] += lm[0, 0, h, approx]
+            out[0, rows, h] = logits.softmax(-1) @ vals
+        out[0, 960:, h] = torch.softmax(q[0, 960:, h] @ k[0, :, h].T / D ** 0.5, -1) @ v[0, :, h]
+    rows = np.r_[0:128, 896:1000]  # two routed blocks, the last routed block and the dense tail
+    np.savez_compressed(HERE / "attention.npz", route=route[0].numpy().astype(np.uint8), rows=rows,
+                        out=out[0, rows].numpy(), target=np.array(target))
+
+
+def main():
+    (HERE / "hierarchy.json").write_text(json.dumps(hierarchy_cases()))
+    (HERE / "layout.json").write_text(json.dumps(layout_cases()))
+    route_case("config0", (4, 32, 32), 4, 64, torch.float32, 1.0, 0)
+    route_case("bf16_d128", (2, 32, 64), 2, 128, torch.bfloat16, 128 ** -0.5, 1)
+    summaries_and_attention()
+    print("golden fixtures written to", HERE)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,91 @@
+"""Processor gates and plugin installation on CPU (no kernel launches)."""
+import pytest
+import torch
+
+from spark_h3_b200 import H3SparseAttentionConfig, install_h3_spark_attn
+from spark_h3_b200.processor import _Controller, _H3SparseProcessor
+
+
+class FakeAttention(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.processor = "original-processor"
+
+    def get_processor(self):
+        return self.processor
+
+    def set_processor(self, processor):
+        self.processor = processor
+
+
+class FakeBlock(torch.nn.Module):
+    def __init__(self):
+        super().__init__()
+        self.attn = FakeAttention()
+
+
+class FakeTransformer(torch.nn.Module):
+    def __init__(self, layers=2):
+        super().__init__()
+        self.transformer_blocks = torch.nn.ModuleList([FakeBlock() for _ in range(layers)])
+
+    def forward(self, hidden_states, token_tags=None, position_ids=None):
+        return hidden_states
+
+
+def test_short_sequences_stay_dense_and_missing_layout_is_an_error():
+    cfg = H3SparseAttentionConfig.spark(num_denoise_steps=1, warmup_mode="warmup_steps", warmup_steps=0)
+    controller = _Controller(cfg)
+    controller.evaluation_index = 0
+    marker = object()
+    processor = _H3SparseProcessor(0, lambda attn, hs, rot, mask: marker, controller)
+    assert processor(None, torch.empty(1, 8191, 1)) is marker
+    assert controller.counts["dense:short_sequence"] == 1
+    with pytest.raises(RuntimeError, match="packed-layout metadata"):
+        processor(None, torch.empty(1, 8192, 1))
+
+
+def test_warmup_and_dense_layers_use_the_original_processor():
+    cfg = H3SparseAttentionConfig.spark(num_denoise_steps=3, warmup_mode="warmup_steps", warmup_steps=1,
+                                        sol_dense_layers=1, sol_min_tokens=0)
+    controller = _Controller(cfg)
+    calls = []
+    original = lambda attn, hs, rot, mask: calls.append(hs.shape) or "dense"
+    controller.evaluation_index = 0
+    assert _H3SparseProcessor(3, original, controller)(None, torch.empty(1, 4, 1)) == "dense"
+    assert controller.counts["dense:warmup"] == 1
+    controller.evaluation_index = 1
+    assert _H3SparseProcessor(0, original, controller)(None, torch.empty(1, 4, 1)) == "dense"
+    assert controller.counts["dense:dense_layer"] == 1
+
+
+def test_plugin_installs_hooks_and_restores_processors():
+    model = FakeTransformer()
+    plugin = install_h3_spark_attn(model, num_denoise_steps=2, mode="reweight_only")
+    with plugin:
+        assert all(isinstance(b.attn.processor, _H3SparseProcessor) for b in model.transformer_blocks)
+        tags = torch.zeros(8, dtype=torch.long)
+        pos = torch.cartesian_prod(torch.arange(2), torch.arange(2), torch.arange(2))
+        model(torch.zeros(1, 8, 4), token_tags=tags, position_ids=pos)
+        assert plugin.controller.layout.video_tokens == 8 and plugin.summary()["completed_evaluations"] == 1
+        model(torch.zeros(1, 8, 4), token_tags=tags, position_ids=pos)
+        with pytest.raises(RuntimeError, match="more transformer evaluations"):
+            model(torch.zeros(1, 8, 4), token_tags=tags, position_ids=pos)
+    assert all(b.attn.processor == "original-processor" for b in model.transformer_blocks)
+    assert not model._forward_pre_hooks
+
+
+def test_plugin_restores_processors_when_the_body_raises():
+    model = FakeTransformer()
+    with pytest.raises(ValueError, match="boom"):
+        with install_h3_spark_attn(model, num_denoise_steps=2):
+            raise ValueError("boom")
+    assert all(b.attn.processor == "original-processor" for b in model.transformer_blocks)
+    assert not model._forward_pre_hooks
+
+
+def test_forward_without_layout_metadata_is_rejected():
+    model = FakeTransformer()
+    with install_h3_spark_attn(model, num_denoise_steps=2):
+        with pytest.raises(RuntimeError, match="token_tags/position_ids"):
+            model(torch.zeros(1, 8, 4))
