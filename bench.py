@@ -37,6 +37,9 @@ PROFILE_ONLY = False
 HEAD_DIM = 128
 BLOCK = 128
 TOPK_RATIO = 0.1
+# DRAM bytes per launch of the attention kernel at this workload, from the one-pass ncu
+# capture summarised in profiles/config1_layer_launch_list.md (4.89 GB read + 1.05 GB write).
+ATTENTION_TRAFFIC_BYTES = 5.94e9
 
 
 def dense_flops(tokens: int, heads: int, dim: int) -> float:
@@ -326,7 +329,9 @@ def run_ours(args) -> None:
             dense_cudnn_sdpa_ms=dense_sdpa_ms,
             speedup_vs_dense_sdpa=(dense_sdpa_ms / ms_per_step if isinstance(dense_sdpa_ms, float) else None),
             roofline=dict(bound="tensor", kernel="sparse_attention_sm100_kernel", achieved=achieved,
-                          peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"], traffic=None,
+                          peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"],
+                          traffic=ATTENTION_TRAFFIC_BYTES if (GRID, world) == ((31, 48, 84), 1) else None,
+                          traffic_unit="bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                           peak_source=peaks["source"],
                           note="achieved = algorithmic sparse FLOPs per launch / mean CUDA-event launch time"),
             e2e=dict(value=total_dense / (e2e_ms * 1e-3) / 1e12, unit=UNIT, ms_per_step=e2e_ms,
