@@ -156,6 +156,53 @@ int sb_headwise_permute(const void* src, void* dst, const void* perm, int index_
                         int B, int T, int H, int D, int elem_bytes, int video_tokens,
                         void* stream);
 
+/*
+ * e4m3 row quantiser.  Replaces h3_sparse_attention/fp8_linear.py:75-145 (_quantize_rows_kernel
+ * / quantize_rows_reference): per row, scale = max(absmax * fp32(1/448), 1e-12) (fp32, as torch evaluates x / 448) and
+ * out = e4m3(clamp(x / scale, -448, 448)) with round-to-nearest-even.  Used for per-token
+ * activation scales and per-output-channel weight scales.  x: [M, K] (dtype), out: [M, K]
+ * bytes, scales: [M] fp32.  x must be 16-byte aligned (rows use 16-byte loads when K % 8 == 0).
+ */
+int sb_fp8_quantize_rows(const void* x, int dtype, int64_t M, int K, uint8_t* out,
+                         float* scales, void* stream);
+
+/*
+ * Fused SwiGLU + e4m3 row quantiser.  Replaces fp8_linear.py:92-108/128-138
+ * (_swiglu_quantize_kernel / swiglu_quantize): h is the [M, 2K] projection output (value
+ * half first, gate half second); the row quantiser above is applied to a * g * sigmoid(g)
+ * evaluated in fp32, without writing the activation.  out: [M, K] bytes, scales: [M] fp32.
+ */
+int sb_fp8_swiglu_quantize_rows(const void* h, int dtype, int64_t M, int K, uint8_t* out,
+                                float* scales, void* stream);
+
+/*
+ * Per-tensor e4m3 quantiser.  Replaces fp8_linear.py:160-180/201-214 (_absmax_kernel,
+ * _cast_scaled_kernel, quantize_tensor): one absmax over all n values, then
+ * scale = max(absmax * fp32(1/448), 1e-12) and out = e4m3(clamp(x / scale)).  scale: 1 fp32 (device),
+ * workspace: 1 fp32 of scratch (device).  Nothing is synchronised.
+ */
+int sb_fp8_quantize_tensor(const void* x, int dtype, int64_t n, uint8_t* out, float* scale,
+                           float* workspace, void* stream);
+
+/*
+ * act = bf16(a * g * sigmoid(g)) of a [M, 2K] projection output, the bf16 intermediate that
+ * the per-tensor SwiGLU path quantises (fp8_linear.py:182-198/223-239).  act: [M, K] bf16.
+ */
+int sb_fp8_swiglu(const void* h, int dtype, int64_t M, int K, void* act, void* stream);
+
+/*
+ * e4m3 GEMM with per-row scales on both operands, bf16 output.  Replaces the
+ * torch._scaled_mm call of fp8_linear.py:280-287 (Fp8Linear.forward_quantized):
+ *   out[m, n] = bf16(sum_k a[m, k] * b[n, k] * a_scale[m * sa] * b_scale[n * sb] + bias[n])
+ * with sa = a_scale_stride and sb = b_scale_stride, each 1 (per-token / per-output-channel
+ * scales) or 0 (one scale for the tensor).  a: [M, K] e4m3, b: [N, K] e4m3 (the weight,
+ * K-major), bias: [N] bf16 or NULL, out: [M, N] bf16.  K must be a multiple of 16.
+ * num_ctas <= 0 launches one persistent CTA per SM.
+ */
+int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
+                const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
+                void* out, int num_ctas, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

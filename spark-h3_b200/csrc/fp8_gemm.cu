@@ -1,0 +1,556 @@
+// e4m3 linears on sm_100a: a per-row quantiser and a persistent tcgen05 GEMM
+//   Y[m, n] = (sum_k A[m, k] * B[n, k]) * a_scale[m] * b_scale[n]  (+ bias[n]) -> bf16
+// with fp32 accumulation in TMEM (kind::f8f6f4, M = 128, N = 256, K = 32 per MMA).
+//
+// Roles (192 threads): warps 0-3 epilogue (thread r owns accumulator row r), warp 4 TMA
+// producer, warp 5 MMA issuer (owns the TMEM allocation).  Tiles are 128 x 256 outputs with
+// 128-byte K steps through a 4-stage ring (48 KB per stage); two TMEM accumulators let the
+// epilogue of one tile overlap the main loop of the next.  Tiles are visited n-fastest, so
+// the CTAs running at one time share the same A rows while B stays resident in L2.
+#include <algorithm>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace sb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kBM = 128, kBN = 256, kBK = 128;  // kBK in elements == bytes
+constexpr int kStages = 4;
+constexpr int kABytes = kBM * kBK;              // 16 KB
+constexpr int kBBytes = kBN * kBK;              // 32 KB
+constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
+constexpr int kGemmThreads = 192;
+constexpr uint32_t kAccCols = 256;
+
+struct __align__(8) GemmControl {
+  uint64_t full[kStages], empty[kStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;  // final commit of the MMA warp (drained before TMEM is freed)
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
+  return (1u << 4)                     // D format: f32
+         | (0u << 7) | (0u << 10)      // A, B format: e4m3
+         | ((uint32_t)(N >> 3) << 17)  // K-major A and B
+         | ((uint32_t)(M >> 4) << 24);
+}
+
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
+      : "memory");
+}
+
+struct GemmParams {
+  const float* a_scale;
+  const float* b_scale;
+  int a_scale_stride, b_scale_stride;  // 1: one scale per row / column, 0: one per tensor
+  const __nv_bfloat16* bias;
+  __nv_bfloat16* out;
+  int* status;
+  int64_t M;
+  int N, K;
+  int m_tiles, n_tiles, k_steps;
+};
+
+__global__ void __launch_bounds__(kGemmThreads, 1)
+fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0u) {
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 910);
+    return;
+  }
+  GemmControl& C = *reinterpret_cast<GemmControl*>(smem + kStages * kStageBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&C.full[s]), 1);
+      mbar_init(smem_u32(&C.empty[s]), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&C.acc_full[b]), 1);
+      mbar_init(smem_u32(&C.acc_empty[b]), 128);
+    }
+    mbar_init(smem_u32(&C.mma_done), 1);
+    C.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(&C.tmem_base), 2 * kAccCols);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(&tm_a);
+    prefetch_tensormap(&tm_b);
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = C.tmem_base;
+  volatile int* abort_flag = &C.abort_flag;
+  const uint32_t base = smem_u32(smem);
+  const int64_t total_tiles = (int64_t)p.m_tiles * p.n_tiles;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int s = 0, use = 0;
+      int armed[kStages] = {};
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
+        const int mt = (int)(t / p.n_tiles), nt = (int)(t % p.n_tiles);
+        for (int ks = 0; ks < p.k_steps; ++ks) {
+          if (!mbar_wait(smem_u32(&C.empty[s]), (uint32_t)((use & 1) ^ 1), abort_flag, p.status, 401)) {
+            ok = false;
+            break;
+          }
+          const uint32_t bar = smem_u32(&C.full[s]);
+          mbar_arrive_expect_tx(bar, kStageBytes);
+          ++armed[s];
+          const uint32_t st = base + s * kStageBytes;
+          tma_load_2d(st, &tm_a, bar, ks * kBK, mt * kBM);
+          tma_load_2d(st + kABytes, &tm_b, bar, ks * kBK, nt * kBN);
+          if (++s == kStages) {
+            s = 0;
+            ++use;
+          }
+        }
+      }
+      for (int st = 0; st < kStages; ++st)
+        if (armed[st] > 0) mbar_drain(smem_u32(&C.full[st]), (uint32_t)((armed[st] - 1) & 1));
+    }
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(kBM, kBN);
+      const uint64_t adesc0 = smem_desc_sw128(base, 16, 1024);
+      int s = 0, use = 0, local = 0;
+      bool ok = true;
+      for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++local) {
+        const int buf = local & 1;
+        // The epilogue must have drained this accumulator (two tiles ago).
+        if (local >= 2 && !mbar_wait(smem_u32(&C.acc_empty[buf]), (uint32_t)(((local - 2) >> 1) & 1), abort_flag,
+                                     p.status, 402)) {
+          ok = false;
+          break;
+        }
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * kAccCols;
+        for (int ks = 0; ks < p.k_steps; ++ks) {
+          if (!mbar_wait(smem_u32(&C.full[s]), (uint32_t)(use & 1), abort_flag, p.status, 403)) {
+            ok = false;
+            break;
+          }
+          const uint64_t sa = adesc0 + (uint64_t)((s * kStageBytes) >> 4);
+          const uint64_t sb = sa + (uint64_t)(kABytes >> 4);
+#pragma unroll
+          for (int kk = 0; kk < kBK / 32; ++kk)
+            mma_f8(acc, sa + (uint64_t)(kk * 2), sb + (uint64_t)(kk * 2), idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&C.empty[s]));
+          if (++s == kStages) {
+            s = 0;
+            ++use;
+          }
+        }
+        tc_commit(smem_u32(&C.acc_full[buf]));
+      }
+      tc_commit(smem_u32(&C.mma_done));  // covers every MMA this warp issued
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int row = threadIdx.x;  // 0..127 = TMEM lane
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    int local = 0;
+    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+      const int buf = local & 1;
+      const bool got = mbar_wait(smem_u32(&C.acc_full[buf]), (uint32_t)((local >> 1) & 1), abort_flag, p.status, 404);
+      if (!__all_sync(0xffffffffu, got)) break;
+      tc_fence_after();
+      const int mt = (int)(t / p.n_tiles), nt = (int)(t % p.n_tiles);
+      const int64_t m = (int64_t)mt * kBM + row;
+      const int n0 = nt * kBN;
+      const bool row_ok = m < p.M;
+      const float sa = row_ok ? __ldg(p.a_scale + m * p.a_scale_stride) : 0.f;
+      __nv_bfloat16* out_row = p.out + m * p.N;
+#pragma unroll 1
+      for (int c = 0; c < kBN / 32; ++c) {
+        uint32_t r[32];
+        tmem_ld32(tmem + lane_base + buf * kAccCols + 32 * c, r);
+        tmem_wait_ld();
+        const int nc = n0 + 32 * c;
+        if (row_ok && nc < p.N) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            const int n = nc + i;
+            const float sb = n < p.N ? __ldg(p.b_scale + (int64_t)n * p.b_scale_stride) : 0.f;
+            float y = __uint_as_float(r[i]) * sa * sb;
+            if (p.bias != nullptr && n < p.N) y += __bfloat162float(p.bias[n]);
+            f[i] = y;
+          }
+          if (nc + 32 <= p.N && (p.N % 8) == 0) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) store8(out_row + nc + 8 * v, f + 8 * v);
+          } else {
+            for (int i = 0; i < 32 && nc + i < p.N; ++i) out_row[nc + i] = __float2bfloat16_rn(f[i]);
+          }
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&C.acc_empty[buf]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    mbar_drain(smem_u32(&C.mma_done), 0);
+    tmem_dealloc(tmem, 2 * kAccCols);
+  }
+}
+
+// Row loaders for the quantisers: 8 consecutive fp32 values of row `row` from column c.
+template <typename T>
+struct PlainRows {
+  const T* x;
+  int K;
+  __device__ void load(int64_t row, int c, float* v) const {
+    const T* xr = x + row * K;
+    if (c + 8 <= K && (K % 8) == 0) {  // rows are 16-byte aligned only when K % 8 == 0
+      load8(xr + c, v);
+    } else {
+      for (int i = 0; i < 8; ++i) v[i] = c + i < K ? Elem<T>::to_f(xr[c + i]) : 0.f;
+    }
+  }
+};
+
+// a * silu(gate) of a [M, 2K] projection (value half first, gate half second), evaluated
+// in fp32 as a * g * sigmoid(g).
+template <typename T>
+struct SwigluRows {
+  const T* h;
+  int K;
+  __device__ void load(int64_t row, int c, float* v) const {
+    const T* hr = h + row * 2 * K;
+    float a[8], g[8];
+    if (c + 8 <= K && (K % 8) == 0) {
+      load8(hr + c, a);
+      load8(hr + K + c, g);
+    } else {
+      for (int i = 0; i < 8; ++i) {
+        a[i] = c + i < K ? Elem<T>::to_f(hr[c + i]) : 0.f;
+        g[i] = c + i < K ? Elem<T>::to_f(hr[K + c + i]) : 0.f;
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = a[i] * g[i] * (1.f / (1.f + __expf(-g[i])));
+  }
+};
+
+// The eager spelling divides a tensor by the Python scalar 448, which torch evaluates as a
+// multiplication by the fp32 reciprocal; the scale is taken the same way.
+constexpr float kInv448 = 1.0f / 448.0f;
+
+__device__ __forceinline__ void store_e4m3x8(uint8_t* yr, int c, int K, const float* v, float scale) {
+  uint16_t packed[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const float lo = fminf(fmaxf(__fdiv_rn(v[2 * i], scale), -448.f), 448.f);
+    const float hi = fminf(fmaxf(__fdiv_rn(v[2 * i + 1], scale), -448.f), 448.f);
+    uint16_t pr;
+    asm("cvt.rn.satfinite.e4m3x2.f32 %0, %1, %2;" : "=h"(pr) : "f"(hi), "f"(lo));
+    packed[i] = pr;
+  }
+  if (c + 8 <= K && (K % 8) == 0) {
+    *reinterpret_cast<uint2*>(yr + c) = *reinterpret_cast<uint2*>(packed);
+  } else {
+    const uint8_t* bytes = reinterpret_cast<const uint8_t*>(packed);
+    for (int i = 0; i < 8 && c + i < K; ++i) yr[c + i] = bytes[i];
+  }
+}
+
+// One warp per row: absmax, scale = max(absmax * fp32(1/448), 1e-12), y = sat_e4m3(x / scale).  The
+// second sweep over the row is served from L1/L2.
+template <typename Rows>
+__global__ void quantize_rows_kernel(Rows rows, int64_t M, int K, uint8_t* __restrict__ y,
+                                     float* __restrict__ scales) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  float amax = 0.f;
+  for (int c = lane * 8; c < K; c += 256) {
+    float v[8];
+    rows.load(row, c, v);
+#pragma unroll
+    for (int i = 0; i < 8; ++i) amax = fmaxf(amax, fabsf(v[i]));
+  }
+  amax = warp_max(amax);
+  const float scale = fmaxf(amax * kInv448, 1e-12f);
+  if (lane == 0) scales[row] = scale;
+  uint8_t* yr = y + row * K;
+  for (int c = lane * 8; c < K; c += 256) {
+    float v[8];
+    rows.load(row, c, v);
+    store_e4m3x8(yr, c, K, v, scale);
+  }
+}
+
+// Whole-tensor absmax in one read: per-CTA partial maximum, one atomic per CTA.  Absolute
+// values are non-negative, so their bit patterns order like unsigned integers.
+template <typename T>
+__global__ void absmax_kernel(const T* __restrict__ x, int64_t n, unsigned int* __restrict__ amax_bits) {
+  float m = 0.f;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    float v[8];
+    if (i + 8 <= n) {
+      load8(x + i, v);
+    } else {
+      for (int j = 0; j < 8; ++j) v[j] = i + j < n ? Elem<T>::to_f(x[i + j]) : 0.f;
+    }
+#pragma unroll
+    for (int j = 0; j < 8; ++j) m = fmaxf(m, fabsf(v[j]));
+  }
+  m = warp_max(m);
+  __shared__ float part[32];
+  if ((threadIdx.x & 31) == 0) part[threadIdx.x >> 5] = m;
+  __syncthreads();
+  if (threadIdx.x < 32) {
+    float w = threadIdx.x < blockDim.x / 32 ? part[threadIdx.x] : 0.f;
+    w = warp_max(w);
+    if (threadIdx.x == 0) atomicMax(amax_bits, __float_as_uint(w));
+  }
+}
+
+// y = sat_e4m3(x / scale) with scale = max(amax / 448, 1e-12) taken from the absmax pass.
+template <typename T>
+__global__ void cast_scaled_kernel(const T* __restrict__ x, int64_t n, const unsigned int* __restrict__ amax_bits,
+                                   uint8_t* __restrict__ y, float* __restrict__ scale_out) {
+  const float scale = fmaxf(__uint_as_float(*amax_bits) * kInv448, 1e-12f);
+  if (blockIdx.x == 0 && threadIdx.x == 0) *scale_out = scale;
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x * 8;
+  for (int64_t i = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) * 8; i < n; i += stride) {
+    float v[8];
+    if (i + 8 <= n) {
+      load8(x + i, v);
+    } else {
+      for (int j = 0; j < 8; ++j) v[j] = i + j < n ? Elem<T>::to_f(x[i + j]) : 0.f;
+    }
+    const int64_t rest = n - i;
+    store_e4m3x8(y + i, 0, rest < 8 ? (int)rest : 8, v, scale);
+  }
+}
+
+// a * silu(gate) rounded to bf16 (the per-tensor SwiGLU path quantises this tensor).
+template <typename T>
+__global__ void swiglu_kernel(const T* __restrict__ h, int64_t M, int K, __nv_bfloat16* __restrict__ act) {
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  SwigluRows<T> rows{h, K};
+  __nv_bfloat16* ar = act + row * K;
+  for (int c = lane * 8; c < K; c += 256) {
+    float v[8];
+    rows.load(row, c, v);
+    if (c + 8 <= K && (K % 8) == 0) {
+      store8(ar + c, v);
+    } else {
+      for (int i = 0; i < 8 && c + i < K; ++i) ar[c + i] = __float2bfloat16_rn(v[i]);
+    }
+  }
+}
+
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+int make_map_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr) {
+    set_error("sb_fp8_gemm: cuTensorMapEncodeTiled is unavailable");
+    return SB_ERR_CUDA;
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols};
+  const cuuint32_t box[2] = {(cuuint32_t)kBK, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("sb_fp8_gemm: cuTensorMapEncodeTiled failed (CUresult %d)", (int)r);
+    return SB_ERR_CUDA;
+  }
+  return SB_OK;
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+namespace {
+constexpr int kRowsPerCta = 8;
+
+template <typename Rows>
+int launch_rows(Rows rows, int64_t M, int K, uint8_t* out, float* scales, cudaStream_t s, const char* what) {
+  const int64_t grid = (M + kRowsPerCta - 1) / kRowsPerCta;
+  SB_CHECK_ARG(grid < (1ll << 31), "%s: too many rows", what);
+  quantize_rows_kernel<Rows><<<(unsigned)grid, 32 * kRowsPerCta, 0, s>>>(rows, M, K, out, scales);
+  SB_CHECK_LAUNCH(what);
+  return SB_OK;
+}
+
+int elementwise_grid(int64_t n) {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (n + 256 * 8 - 1) / (256 * 8);
+  return (int)std::max<int64_t>(1, std::min<int64_t>(want, (int64_t)sms * 8));
+}
+}  // namespace
+
+extern "C" int sb_fp8_quantize_rows(const void* x, int dtype, int64_t M, int K, uint8_t* out, float* scales,
+                                    void* stream) {
+  SB_CHECK_ARG(x && out && scales, "sb_fp8_quantize_rows: null pointer");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_fp8_quantize_rows: bad dtype");
+  SB_CHECK_ARG(M > 0 && K > 0, "sb_fp8_quantize_rows: M and K must be positive");
+  SB_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)out % 8) == 0,
+               "sb_fp8_quantize_rows: x must be 16-byte and out 8-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SB_BF16)
+    return launch_rows(PlainRows<__nv_bfloat16>{(const __nv_bfloat16*)x, K}, M, K, out, scales, s,
+                       "sb_fp8_quantize_rows launch");
+  return launch_rows(PlainRows<float>{(const float*)x, K}, M, K, out, scales, s, "sb_fp8_quantize_rows launch");
+}
+
+extern "C" int sb_fp8_swiglu_quantize_rows(const void* h, int dtype, int64_t M, int K, uint8_t* out, float* scales,
+                                           void* stream) {
+  SB_CHECK_ARG(h && out && scales, "sb_fp8_swiglu_quantize_rows: null pointer");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_fp8_swiglu_quantize_rows: bad dtype");
+  SB_CHECK_ARG(M > 0 && K > 0, "sb_fp8_swiglu_quantize_rows: M and K must be positive");
+  SB_CHECK_ARG(((uintptr_t)h % 16) == 0 && ((uintptr_t)out % 8) == 0,
+               "sb_fp8_swiglu_quantize_rows: h must be 16-byte and out 8-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SB_BF16)
+    return launch_rows(SwigluRows<__nv_bfloat16>{(const __nv_bfloat16*)h, K}, M, K, out, scales, s,
+                       "sb_fp8_swiglu_quantize_rows launch");
+  return launch_rows(SwigluRows<float>{(const float*)h, K}, M, K, out, scales, s,
+                     "sb_fp8_swiglu_quantize_rows launch");
+}
+
+extern "C" int sb_fp8_quantize_tensor(const void* x, int dtype, int64_t n, uint8_t* out, float* scale,
+                                      float* workspace, void* stream) {
+  SB_CHECK_ARG(x && out && scale && workspace, "sb_fp8_quantize_tensor: null pointer");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_fp8_quantize_tensor: bad dtype");
+  SB_CHECK_ARG(n > 0, "sb_fp8_quantize_tensor: n must be positive");
+  SB_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)out % 8) == 0,
+               "sb_fp8_quantize_tensor: x must be 16-byte and out 8-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  unsigned int* amax = reinterpret_cast<unsigned int*>(workspace);
+  cudaError_t err = cudaMemsetAsync(amax, 0, sizeof(unsigned int), s);
+  if (err != cudaSuccess) return cuda_error(err, "sb_fp8_quantize_tensor: clear absmax");
+  const int grid = elementwise_grid(n);
+  if (dtype == SB_BF16) {
+    absmax_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)x, n, amax);
+    cast_scaled_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)x, n, amax, out, scale);
+  } else {
+    absmax_kernel<float><<<grid, 256, 0, s>>>((const float*)x, n, amax);
+    cast_scaled_kernel<float><<<grid, 256, 0, s>>>((const float*)x, n, amax, out, scale);
+  }
+  SB_CHECK_LAUNCH("sb_fp8_quantize_tensor launch");
+  return SB_OK;
+}
+
+extern "C" int sb_fp8_swiglu(const void* h, int dtype, int64_t M, int K, void* act, void* stream) {
+  SB_CHECK_ARG(h && act, "sb_fp8_swiglu: null pointer");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_fp8_swiglu: bad dtype");
+  SB_CHECK_ARG(M > 0 && K > 0 && K % 8 == 0, "sb_fp8_swiglu: M > 0 and K a positive multiple of 8");
+  SB_CHECK_ARG(((uintptr_t)h % 16) == 0 && ((uintptr_t)act % 16) == 0, "sb_fp8_swiglu: 16-byte aligned rows");
+  const int64_t grid = (M + kRowsPerCta - 1) / kRowsPerCta;
+  SB_CHECK_ARG(grid < (1ll << 31), "sb_fp8_swiglu: too many rows");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SB_BF16)
+    swiglu_kernel<__nv_bfloat16><<<(unsigned)grid, 32 * kRowsPerCta, 0, s>>>((const __nv_bfloat16*)h, M, K,
+                                                                          (__nv_bfloat16*)act);
+  else
+    swiglu_kernel<float><<<(unsigned)grid, 32 * kRowsPerCta, 0, s>>>((const float*)h, M, K, (__nv_bfloat16*)act);
+  SB_CHECK_LAUNCH("sb_fp8_swiglu launch");
+  return SB_OK;
+}
+
+extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
+                           const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
+                           void* out, int num_ctas, void* stream) {
+  SB_CHECK_ARG(a && a_scale && b && b_scale && out, "sb_fp8_gemm: null pointer");
+  SB_CHECK_ARG(M > 0 && N > 0 && K > 0, "sb_fp8_gemm: M, N, K must be positive");
+  SB_CHECK_ARG(K % 16 == 0, "sb_fp8_gemm: K must be a multiple of 16 (TMA row pitch), got %d", K);
+  SB_CHECK_ARG(((uintptr_t)a % 16) == 0 && ((uintptr_t)b % 16) == 0 && ((uintptr_t)out % 16) == 0,
+               "sb_fp8_gemm: A, B and the output must be 16-byte aligned");
+  SB_CHECK_ARG(M < (1ll << 31), "sb_fp8_gemm: M must be below 2^31");
+  SB_CHECK_ARG((a_scale_stride == 0 || a_scale_stride == 1) && (b_scale_stride == 0 || b_scale_stride == 1),
+               "sb_fp8_gemm: scale strides must be 0 (per tensor) or 1 (per row / column)");
+  int* status = device_status_ptr();
+  if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_fp8_gemm: status word");
+  CUtensorMap ma, mb;
+  int rc;
+  if ((rc = make_map_u8(&ma, a, (uint64_t)K, (uint64_t)M, kBM)) != SB_OK) return rc;
+  if ((rc = make_map_u8(&mb, b, (uint64_t)K, (uint64_t)N, kBN)) != SB_OK) return rc;
+  GemmParams p{};
+  p.a_scale = a_scale;
+  p.b_scale = b_scale;
+  p.a_scale_stride = a_scale_stride;
+  p.b_scale_stride = b_scale_stride;
+  p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.out = static_cast<__nv_bfloat16*>(out);
+  p.status = status;
+  p.M = M;
+  p.N = N;
+  p.K = K;
+  p.m_tiles = (int)((M + kBM - 1) / kBM);
+  p.n_tiles = (N + kBN - 1) / kBN;
+  p.k_steps = (K + kBK - 1) / kBK;
+  const size_t smem = (size_t)kStages * kStageBytes + sizeof(GemmControl);
+  cudaError_t err = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: set smem");
+  int sms = num_ctas;
+  if (sms <= 0) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  }
+  const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
+  const int grid = (int)std::min<int64_t>(tiles, sms);
+  fp8_gemm_kernel<<<grid, kGemmThreads, smem, (cudaStream_t)stream>>>(ma, mb, p);
+  SB_CHECK_LAUNCH("sb_fp8_gemm launch");
+  return SB_OK;
+}

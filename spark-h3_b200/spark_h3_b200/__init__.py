@@ -5,6 +5,7 @@ the attention seam `spark_attention_bthd`, and the `spark_reweight` primitive.  
 in libsparkh3b200.so (C ABI, include/spark_h3_b200.h) and always run on the GPU.
 """
 from .attention import spark_attention_bthd, spark_reweight
+from .fp8_linear import Fp8Linear, convert_linear_to_fp8, install_fp8
 from .config import H3SparseAttentionConfig
 from .layout import PackedLayout, packed_layout
 from .processor import (H3SparseAttentionPlugin, install_h3_sol_attn, install_h3_spark_attn,
@@ -12,7 +13,7 @@ from .processor import (H3SparseAttentionPlugin, install_h3_sol_attn, install_h3
 from . import ops
 
 __all__ = [
-    "H3SparseAttentionConfig", "H3SparseAttentionPlugin", "PackedLayout", "install_h3_spark_attn",
+    "Fp8Linear", "H3SparseAttentionConfig", "H3SparseAttentionPlugin", "convert_linear_to_fp8", "install_fp8", "PackedLayout", "install_h3_spark_attn",
     "install_h3_sol_attn", "install_h3_sparse_attention", "ops", "packed_layout", "spark_attention_bthd",
     "spark_reweight",
 ]

@@ -35,6 +35,11 @@ SIGNATURES = {
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
     "sb_headwise_permute": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
+    "sb_fp8_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
+    "sb_fp8_swiglu_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
+    "sb_fp8_quantize_tensor": (_i, [_vp, _i, _i64, _vp, _vp, _vp, _vp]),
+    "sb_fp8_swiglu": (_i, [_vp, _i, _i64, _i, _vp, _vp]),
+    "sb_fp8_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _i, _vp]),
 }
 
 
