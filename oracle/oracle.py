@@ -34,13 +34,13 @@ LN2 = 0.6931471805599453
 def build() -> Path:
     """Compile the C restatement (gcc, no contraction of multiply-adds)."""
     LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
-    src = HERE / "spark_oracle.c"
-    if LIB_PATH.exists() and LIB_PATH.stat().st_mtime >= src.stat().st_mtime:
+    sources = [HERE / "spark_oracle.c", HERE / "reblock_oracle.c"]
+    if LIB_PATH.exists() and all(LIB_PATH.stat().st_mtime >= src.stat().st_mtime for src in sources):
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
     subprocess.check_call([
         "gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", "-shared", "-fPIC",
-        "-o", str(tmp), str(src), "-lm",
+        "-o", str(tmp), *map(str, sources), "-lm",
     ])
     os.replace(tmp, LIB_PATH)
     return LIB_PATH
@@ -64,6 +64,11 @@ def _lib():
         lib.orc_topk.argtypes = [f32p, ci64, ci, ci, ci, i32p, i32p]
         for fn in (lib.orc_block_means, lib.orc_round_bf16, lib.orc_anchor, lib.orc_scores, lib.orc_topk):
             fn.restype = None
+        u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
+        lib.orc_rb_norms.argtypes = [u16p, ci64, ci, f32p]
+        lib.orc_rb_norms.restype = None
+        lib.orc_rb_tree.argtypes = [u16p, ci, ci, ci, i32p, i32p, i32p]
+        lib.orc_rb_tree.restype = ci
         _LIB = lib
     return _LIB
 
@@ -291,3 +296,120 @@ def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: floa
                                     local_radius, rows=rows, heads=heads)
         result.update(out=out, lse=lse)
     return result
+
+
+# ------------------------------------------------------------- reblock (landmark tree v2)
+def hilbert_distances_3d(coords: np.ndarray, bits: int) -> np.ndarray:
+    """Skilling transpose -> Hilbert index of integer [N, 3] coordinates
+    (h3_sparse_attention/mahalanobis_kmeans.py:11-45)."""
+    x = coords.astype(np.int64).copy()
+    q = 1 << (bits - 1)
+    while q > 1:
+        mask = q - 1
+        for axis in range(3):
+            high = (x[:, axis] & q) != 0
+            x[high, 0] ^= mask
+            low = ~high
+            swap = (x[low, 0] ^ x[low, axis]) & mask
+            x[low, 0] ^= swap
+            x[low, axis] ^= swap
+        q >>= 1
+    x[:, 1] ^= x[:, 0]
+    x[:, 2] ^= x[:, 1]
+    t = np.zeros(len(x), dtype=np.int64)
+    q = 1 << (bits - 1)
+    while q > 1:
+        t[(x[:, 2] & q) != 0] ^= q - 1
+        q >>= 1
+    x ^= t[:, None]
+    out = np.zeros(len(x), dtype=np.int64)
+    for bit in range(bits - 1, -1, -1):
+        for axis in range(3):
+            out = (out << 1) | ((x[:, axis] >> bit) & 1)
+    return out
+
+
+def initial_order(grid, name: str = "flat") -> np.ndarray:
+    """Root token order (landmark_initial_order.py:44-62)."""
+    T_, H_, W_ = (int(g) for g in grid)
+    ids = np.arange(T_ * H_ * W_, dtype=np.int64)
+    if name == "flat":
+        return ids
+    t, h, w = ids // (H_ * W_), (ids // W_) % H_, ids % W_
+    if name == "tile_t4h4w4":
+        tile = ((t // 4) * ((H_ + 3) // 4) + h // 4) * ((W_ + 3) // 4) + w // 4
+        return np.argsort(tile * 64 + (t % 4) * 16 + (h % 4) * 4 + w % 4, kind="stable")
+    axes = dict(t=t, h=h, w=w)
+    coords = np.stack([axes[a] for a in name[8:]], axis=-1)
+    bits = max(1, (max(T_, H_, W_) - 1).bit_length())
+    return np.argsort(hilbert_distances_3d(coords, bits), kind="stable")
+
+
+def hilbert_midpoint_samples(grid, count: int) -> np.ndarray:
+    """count metric samples, uniformly spaced along the 3-D Hilbert order
+    (mahalanobis_kmeans.py:48-96)."""
+    order = initial_order(grid, "hilbert_thw")
+    n = len(order)
+    count = min(max(1, int(count)), n)
+    pos = np.floor((np.arange(count, dtype=np.float64) + 0.5) * n / count).astype(np.int64)
+    return order[np.minimum(pos, n - 1)]
+
+
+def metric_factors(q: Tensor, k: Tensor, samples: np.ndarray, video: int, ridge: float = 1e-3) -> np.ndarray:
+    """Ridged non-centred second moments of the sampled Q and K rows and their Cholesky
+    factors (mahalanobis_kmeans.py:309-388, landmark_direction.py:60-104), in float64:
+    returns L [2*B*H, D, D], rows [0, BH) = chol(M2(Q)) (applied to K) and
+    [BH, 2BH) = chol(M2(K)) (applied to Q)."""
+    B, T, H, D = q.shape
+    out = []
+    for src in (q, k):
+        x = src.float()[:, :video][:, samples].astype(np.float64)  # [B, S, H, D]
+        for b in range(B):
+            for h in range(H):
+                s = x[b, :, h]
+                m = s.T @ s / len(samples)
+                m = 0.5 * (m + m.T)
+                m[np.diag_indices(D)] += ridge * np.trace(m) / D
+                out.append(np.linalg.cholesky(m))
+    return np.stack(out)
+
+
+def reblock_features(q: Tensor, k: Tensor, factors: np.ndarray, video: int) -> np.ndarray:
+    """[K . Lq ; Q . Lk] of bf16 operands, accumulated exactly and stored bf16
+    (spark_integration.py:561-585): uint16 bf16 bits [2*B*H, video, D]."""
+    B, T, H, D = q.shape
+    rows = []
+    lf = round_bf16(np.asarray(factors, dtype=np.float32))
+    for side, src in enumerate((k, q)):
+        x = src.float()[:, :video]
+        for b in range(B):
+            for h in range(H):
+                r = side * B * H + b * H + h
+                prod = x[b, :, h].astype(np.float64) @ lf[r].astype(np.float64)
+                rows.append(f32_to_bf16_bits(prod.astype(np.float32)))
+    return np.stack(rows)
+
+
+def hierarchy_schedule(split_budgets) -> np.ndarray:
+    """Encode a hierarchy's per-round (leaves, child budgets) table for orc_rb_tree."""
+    words = [len(split_budgets)]
+    for level in split_budgets:
+        words.append(len(level))
+        for leaves, budgets in level:
+            words += [leaves, len(budgets), *budgets]
+    return np.asarray(words, dtype=np.int32)
+
+
+def reblock_tree(features_bits: np.ndarray, grid, split_budgets, order: str = "flat") -> tuple[np.ndarray, np.ndarray]:
+    """Landmark-tree-v2 permutation of bf16 features [rows, N, D] (reblock_oracle.c):
+    returns (permutation, inverse) int64 [rows, N]."""
+    x = np.ascontiguousarray(features_bits, dtype=np.uint16)
+    rows, n, d = x.shape
+    root = np.ascontiguousarray(initial_order(grid, order), dtype=np.int32)
+    perm = np.empty((rows, n), dtype=np.int32)
+    rc = _lib().orc_rb_tree(x, rows, n, d, root, hierarchy_schedule(split_budgets), perm)
+    if rc != 0:
+        raise RuntimeError(f"orc_rb_tree failed ({rc})")
+    inverse = np.empty_like(perm)
+    np.put_along_axis(inverse, perm, np.broadcast_to(np.arange(n, dtype=np.int32), perm.shape), axis=1)
+    return perm.astype(np.int64), inverse.astype(np.int64)

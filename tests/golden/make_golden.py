@@ -18,6 +18,12 @@ Fixtures:
                   TRITON_INTERPRET=1 in fp32 at D=128
   attention.npz   the explicit exact/summary softmax of tests/test_spark_installer.py:559-570
                   applied to the reference's route and summaries (fp32)
+  reblock_tree.npz  recursive_landmark_tree_v2_reference (landmark_tree_v2.py:790-832) on
+                  seeded bf16 features: the permutation per case
+  reblock_qk.npz  the full paired Q/K reblock (_landmark_tree_v2_qk_block_permutations,
+                  spark_integration.py:735-851, CPU controller, mode "full") on clustered
+                  synthetic Q/K: Hilbert metric samples, the Cholesky factors, the bf16
+                  features the tree consumed and the Q/K permutations
 """
 from __future__ import annotations
 
@@ -171,12 +177,70 @@ def summaries_and_attention():
                         out=out[0, rows].numpy(), target=np.array(target))
 
 
+REBLOCK_TREE_CASES = [
+    # (name, tokens, dim, children, grid, initial order, seed)
+    ("remainder", 4133, 128, 16, (1, 1, 4133), "flat", 0),
+    ("grid8k", 8192, 128, 16, (2, 64, 64), "flat", 1),
+    ("hilbert4", 3000, 64, 4, (3, 20, 50), "hilbert_thw", 2),
+    ("tiny", 130, 128, 16, (1, 2, 65), "flat", 3),
+    ("two_rounds", 20000, 128, 16, (5, 40, 100), "flat", 4),
+    ("fanout8", 6016, 128, 8, (4, 32, 47), "tile_t4h4w4", 5),
+]
+
+
+def reblock_tree_fixture():
+    from h3_sparse_attention.landmark_tree_v2 import recursive_landmark_tree_v2_reference
+
+    out = {}
+    for name, tokens, dim, children, grid, order, seed in REBLOCK_TREE_CASES:
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(2, tokens, dim, generator=g).to(torch.bfloat16)
+        ref = recursive_landmark_tree_v2_reference(x, grid_shape=grid, max_children=children, initial_order=order)
+        out[f"{name}_perm"] = ref.permutation.numpy().astype(np.int32)
+        out[f"{name}_digest"] = np.array(digest(x))
+    np.savez_compressed(HERE / "reblock_tree.npz", **out)
+
+
+def reblock_qk_fixture():
+    from types import SimpleNamespace
+
+    from h3_sparse_attention.landmark_direction import landmark_direction_factors
+    from h3_sparse_attention.mahalanobis_kmeans import hilbert_midpoint_sample_indices
+    from h3_sparse_attention.processor import H3SparseAttentionConfig, _Controller
+    from h3_sparse_attention.spark_integration import _landmark_tree_v2_qk_block_permutations
+    from spark_h3_b200.synthetic import make_qkv
+
+    grid, heads, dim = (2, 16, 40), 1, 128
+    q, k, _ = make_qkv(grid, heads, dim, seed=7, dtype=torch.bfloat16, clustered=True)
+    T = q.shape[1]
+    cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode="full", sol_route_topk_ratio=0.1)
+    controller = _Controller(cfg)
+    layout = SimpleNamespace(video_tokens=T, grid=grid, sequence_length=T)
+    qp, qi, kp, ki, _, _ = _landmark_tree_v2_qk_block_permutations(controller, q, k, layout)
+    samples = hilbert_midpoint_sample_indices(grid, T // 64, device="cpu")
+    flat_q = q.permute(0, 2, 1, 3).reshape(heads, T, dim)
+    flat_k = k.permute(0, 2, 1, 3).reshape(heads, T, dim)
+    lq, lk = landmark_direction_factors(flat_q, flat_k, samples, ridge=cfg.rope_sol_key_ridge_epsilon)
+    features = torch.cat([torch.bmm(flat_k, lq.to(torch.bfloat16)), torch.bmm(flat_q, lk.to(torch.bfloat16))])
+    np.savez_compressed(HERE / "reblock_qk.npz", grid=np.array(grid), heads=np.array(heads),
+                        q_digest=np.array(digest(q)), k_digest=np.array(digest(k)),
+                        samples=samples.numpy().astype(np.int32),
+                        samples_big=hilbert_midpoint_sample_indices((61, 48, 84), 245952 // 64,
+                                                                    device="cpu").numpy().astype(np.int32),
+                        factors=torch.cat([lq, lk]).numpy(),
+                        features=features.view(torch.int16).numpy().view(np.uint16),
+                        q_perm=qp.numpy().astype(np.int32), k_perm=kp.numpy().astype(np.int32),
+                        q_inv=qi.numpy().astype(np.int32), k_inv=ki.numpy().astype(np.int32))
+
+
 def main():
     (HERE / "hierarchy.json").write_text(json.dumps(hierarchy_cases()))
     (HERE / "layout.json").write_text(json.dumps(layout_cases()))
     route_case("config0", (4, 32, 32), 4, 64, torch.float32, 1.0, 0)
     route_case("bf16_d128", (2, 32, 64), 2, 128, torch.bfloat16, 128 ** -0.5, 1)
     summaries_and_attention()
+    reblock_tree_fixture()
+    reblock_qk_fixture()
     print("golden fixtures written to", HERE)
 
 

@@ -1,0 +1,77 @@
+"""The reblock oracle pinned to the reference: the landmark-tree-v2 permutations, the
+Hilbert metric samples and the metric factors of tests/golden/reblock_*.npz, which
+make_golden.py produced by running the reference's own CPU path."""
+from __future__ import annotations
+
+import hashlib
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from spark_h3_b200.hierarchy import build_reblock_hierarchy
+from spark_h3_b200.synthetic import make_qkv
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+TREE_CASES = [
+    ("remainder", 4133, 128, 16, (1, 1, 4133), "flat", 0),
+    ("grid8k", 8192, 128, 16, (2, 64, 64), "flat", 1),
+    ("hilbert4", 3000, 64, 4, (3, 20, 50), "hilbert_thw", 2),
+    ("tiny", 130, 128, 16, (1, 2, 65), "flat", 3),
+    ("two_rounds", 20000, 128, 16, (5, 40, 100), "flat", 4),
+    ("fanout8", 6016, 128, 8, (4, 32, 47), "tile_t4h4w4", 5),
+]
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def digest(t: torch.Tensor) -> str:
+    return hashlib.sha256(bits(t).tobytes()).hexdigest()
+
+
+@pytest.mark.parametrize("name,tokens,dim,children,grid,order,seed", TREE_CASES)
+def test_tree_matches_reference(name, tokens, dim, children, grid, order, seed):
+    z = np.load(GOLDEN / "reblock_tree.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, dim, generator=g).to(torch.bfloat16)
+    assert digest(x) == str(z[f"{name}_digest"]), "seeded features differ from the ones the fixture used"
+    hierarchy = build_reblock_hierarchy(tokens, children)
+    perm, inverse = oracle.reblock_tree(bits(x), grid, hierarchy.split_budgets, order)
+    assert np.array_equal(perm, z[f"{name}_perm"])
+    assert np.array_equal(np.take_along_axis(inverse, perm, 1), np.broadcast_to(np.arange(tokens), perm.shape))
+    rem = tokens % 64
+    if rem:  # the protected remainder sits at the tail in root order
+        tail = perm[:, tokens - rem:]
+        root = oracle.initial_order(grid, order)
+        rank = np.argsort(root)
+        assert (np.diff(rank[tail], axis=1) > 0).all()
+
+
+def test_qk_reblock_matches_reference():
+    z = np.load(GOLDEN / "reblock_qk.npz")
+    grid = tuple(int(g) for g in z["grid"])
+    heads = int(z["heads"])
+    T = int(np.prod(grid))
+    q, k, _ = make_qkv(grid, heads, 128, seed=7, dtype=torch.bfloat16, clustered=True)
+    assert digest(q) == str(z["q_digest"]) and digest(k) == str(z["k_digest"])
+    samples = oracle.hilbert_midpoint_samples(grid, T // 64)
+    assert np.array_equal(samples, z["samples"])
+    assert np.array_equal(oracle.hilbert_midpoint_samples((61, 48, 84), 245952 // 64), z["samples_big"])
+    # the tree on the reference's own features reproduces its permutations exactly
+    hierarchy = build_reblock_hierarchy(T, 16)
+    perm, inverse = oracle.reblock_tree(z["features"], grid, hierarchy.split_budgets)
+    ref = np.concatenate([z["k_perm"].reshape(heads, T), z["q_perm"].reshape(heads, T)])
+    ref_inv = np.concatenate([z["k_inv"].reshape(heads, T), z["q_inv"].reshape(heads, T)])
+    assert np.array_equal(perm, ref) and np.array_equal(inverse, ref_inv)
+    # metric factors (float64 here, fp32 Cholesky in the reference) and the bf16 features
+    tq = oracle.Tensor(bits(q), "bfloat16")
+    tk = oracle.Tensor(bits(k), "bfloat16")
+    factors = oracle.metric_factors(tq, tk, samples, T)
+    assert np.abs(factors - z["factors"]).max() <= 1e-4 * np.abs(z["factors"]).max()
+    features = oracle.bf16_bits_to_f32(oracle.reblock_features(tq, tk, factors, T))
+    ref_features = oracle.bf16_bits_to_f32(z["features"])
+    assert np.abs(features - ref_features).max() <= 2 ** -7 * np.abs(ref_features).max()
