@@ -203,6 +203,58 @@ int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, cons
                 const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
                 void* out, int num_ctas, void* stream);
 
+/*
+ * Reblock metric factors.  Replaces h3_sparse_attention/landmark_direction.py:60-104 with
+ * mahalanobis_kmeans.py:309-388 (landmark_direction_factors / batched_cross_metric_factors,
+ * raw moments, m2_side "both"): for every (batch, head) the non-centred second moment of the
+ * sampled Q rows and of the sampled K rows, M = X^T X / S, symmetrised, with
+ * ridge * trace(M) / D added to the diagonal, factored as L L^T (Cholesky, fp32).
+ * q, k: BTHD (dtype), D = 128.  samples: [S] token ids (device), the Hilbert-midpoint
+ * samples of mahalanobis_kmeans.py:87-96.  factors: [2*B*H, D, D] fp32 lower-triangular,
+ * rows [0, BH) = chol(M(Q)) (applied to K), rows [BH, 2BH) = chol(M(K)) (applied to Q).
+ */
+int sb_reblock_metric(const void* q, const void* k, int dtype, int B, int T, int H, int D,
+                      const int32_t* samples, int num_samples, float ridge, float* factors,
+                      void* stream);
+
+/*
+ * Reblock features.  Replaces the two bf16 bmm calls of spark_integration.py:561-585:
+ * features[r] = bf16(X_r . bf16(L_r)) over the first video_tokens tokens, X_r = K[b, :, h]
+ * for r = b*H + h < BH and Q[b, :, h] for r - BH.  q, k: BTHD bf16, D = 128;
+ * factors: as written by sb_reblock_metric; features: [2*B*H, video_tokens, D] bf16.
+ */
+int sb_reblock_transform(const void* q, const void* k, int B, int T, int H, int D,
+                         int video_tokens, const float* factors, void* features, void* stream);
+
+/*
+ * Reblock plan.  The splitting rounds of reblock_hierarchy.py:108-234
+ * (ReblockHierarchy.split_budgets) turned into per-round node tables for sb_reblock_tree.
+ * schedule: [rounds, then per round: entries, then per entry: leaves, children,
+ * budget_0 .. budget_{children-1}] (host).  plan: host buffer of `capacity` ints, or NULL
+ * to query the length.  Returns the plan length in ints, or a negative error.  The caller
+ * keeps the host plan and a device copy of the same ints.
+ */
+int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, int tokens, int32_t* plan,
+                        int64_t capacity);
+
+/* Scratch bytes sb_reblock_tree needs for `rows` feature rows under `plan` (host plan). */
+int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows);
+
+/*
+ * Landmark-tree-v2 permutation.  Replaces landmark_tree_v2.py:297-787
+ * (_recursive_landmark_tree_v2 with the defaults of PreparedLandmarkTreeV2Permutation:
+ * cosine distance, group size 1, 32 midpoint landmarks, linear aggregation, parent order,
+ * two mean-update proxy iterations from the farthest pair, power-of-two fanout) and
+ * landmark_tree_clustering.py:56-146, 290-565 (remainder, exact routing, stable partition).
+ * features: [rows, tokens, D] bf16, D = 128.  root_order: [tokens] device ids of the initial
+ * order, or NULL for the flat order.  perm / inverse: [rows, tokens] int32; perm holds the
+ * 64-token leaves in order, then the tokens mod 64 protected remainder tokens (largest
+ * squared feature norm, lower id first among equals) in root order.
+ */
+int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+                    const int32_t* plan_host, const int32_t* plan_device, void* workspace,
+                    int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,1096 @@
+// Landmark-tree-v2 reblocking on sm_100a: the per-(batch, head, side) token permutation
+// that groups similar tokens into 64-token blocks before Spark routing.
+//
+//   metric     ridged second moments of N/64 Hilbert-midpoint samples of Q and of K and their
+//              Cholesky factors (one CTA per matrix, factorisation in shared memory)
+//   transform  features = [K . L_Q ; Q . L_K] in bf16: a persistent tcgen05 GEMM (TMA tiles
+//              of 128 tokens x 128 dims, the factor resident in shared memory, two TMEM
+//              accumulators so the store of one tile overlaps the MMA of the next)
+//   tree       per splitting round: 32 midpoint landmarks and a binary proxy tree per node
+//              (one warp per node), cosine split scores per token (bandwidth-bound gather of
+//              the token's feature row), exact-capacity routing by (score, token id) with a
+//              radix select per internal proxy node, and a stable partition into the children
+//              (one CTA per node)
+//
+// The tree is bit-exact with the CPU restatement: every fp32 reduction follows one canonical
+// order.  A 128-vector lives on a warp with lane l holding elements 4l .. 4l+3; a dot product
+// is the lane's fma chain over its four elements followed by xor-butterfly sums over offsets
+// 16, 8, 4, 2, 1; unit(x) = x / max(sqrt(dot(x, x)), 1e-12) with IEEE division and square
+// root; weighted landmark means are fma chains over the 32 landmarks in index order.
+#include <algorithm>
+#include <vector>
+
+#include "common.cuh"
+#include "sm100_ptx.cuh"
+
+namespace sb {
+namespace {
+
+using namespace sm100;
+
+constexpr int kDim = 128;
+constexpr int kLandmarks = 32;
+constexpr int kMaxChildren = 64;
+constexpr int kNodeInts = 4 + kMaxChildren;  // start, tokens, children, unused, capacities
+constexpr int kPlanHeader = 8;
+constexpr int kLevelInts = 8;  // nodes, node table offset, tile table offset, P, score stride
+constexpr unsigned kFull = 0xffffffffu;
+
+// ------------------------------------------------------------ canonical arithmetic
+__device__ __forceinline__ float butterfly(float p) {
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) p = __fadd_rn(p, __shfl_xor_sync(kFull, p, o));
+  return p;
+}
+
+__device__ __forceinline__ float lane_dot4(const float* a, const float* b) {
+  float p = __fmul_rn(a[0], b[0]);
+  p = __fmaf_rn(a[1], b[1], p);
+  p = __fmaf_rn(a[2], b[2], p);
+  return __fmaf_rn(a[3], b[3], p);
+}
+
+__device__ __forceinline__ void unit4(const float* x, float* u) {
+  const float den = fmaxf(__fsqrt_rn(butterfly(lane_dot4(x, x))), 1e-12f);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) u[i] = __fdiv_rn(x[i], den);
+}
+
+__device__ __forceinline__ void load_row4(const __nv_bfloat16* row, int lane, float* x) {
+  const uint2 raw = __ldg(reinterpret_cast<const uint2*>(row + 4 * lane));
+  const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw);
+  const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+  x[0] = a.x, x[1] = a.y, x[2] = b.x, x[3] = b.y;
+}
+
+// Monotone unsigned key of an fp32 value; -0 and +0 map to the same key.
+__device__ __forceinline__ uint32_t order_key(float f) {
+  if (f == 0.0f) f = 0.0f;
+  const uint32_t u = __float_as_uint(f);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
+}
+
+// Reduce-scatter of P per-lane partials with the butterfly's summation tree: on return
+// lane l holds, in v[0 .. P/32) (or v[0] when P <= 32), the full sums of value indices
+//   P >= 32: (P/32) * l + i;   P < 32: l / (32 / P).
+template <int P>
+__device__ __forceinline__ void reduce_scatter(float (&v)[P], int lane) {
+  int m = P;
+#pragma unroll
+  for (int o = 16; o >= 1; o >>= 1) {
+    if (m > 1) {
+      const int half = m / 2;
+      const bool upper = (lane & o) != 0;
+#pragma unroll
+      for (int i = 0; i < P / 2; ++i) {
+        if (i < half) {
+          const float send = upper ? v[i] : v[half + i];
+          const float keep = upper ? v[half + i] : v[i];
+          v[i] = __fadd_rn(keep, __shfl_xor_sync(kFull, send, o));
+        }
+      }
+      m = half;
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(kFull, v[0], o));
+    }
+  }
+}
+
+// ===================================================================== metric
+// M[r] = X^T X / S over the S sampled tokens of one (side, batch, head); 16 rows per CTA.
+template <typename T>
+__global__ void __launch_bounds__(256) metric_moment_kernel(const T* __restrict__ q, const T* __restrict__ k, int T_,
+                                                            int H, int BH, const int32_t* __restrict__ samples, int S,
+                                                            float* __restrict__ moments) {
+  __shared__ float xs[32][kDim + 1];
+  const int r = blockIdx.y;
+  const int side = r / BH, bh = r % BH, b = bh / H, h = bh % H;
+  const T* src = side == 0 ? q : k;  // rows [0, BH): moments of Q; [BH, 2BH): moments of K
+  const int j = threadIdx.x & 127;
+  const int i0 = blockIdx.x * 16 + (threadIdx.x >> 7) * 8;
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  for (int s0 = 0; s0 < S; s0 += 32) {
+    __syncthreads();
+    for (int e = threadIdx.x; e < 32 * kDim; e += 256) {
+      const int s = s0 + e / kDim, d = e % kDim;
+      xs[e / kDim][d] = s < S ? Elem<T>::to_f(src[(((int64_t)b * T_ + samples[s]) * H + h) * kDim + d]) : 0.f;
+    }
+    __syncthreads();
+    const int count = min(32, S - s0);
+    for (int s = 0; s < count; ++s) {
+      const float xj = xs[s][j];
+#pragma unroll
+      for (int a = 0; a < 8; ++a) acc[a] = __fmaf_rn(xs[s][i0 + a], xj, acc[a]);
+    }
+  }
+  float* m = moments + (int64_t)r * kDim * kDim;
+#pragma unroll
+  for (int a = 0; a < 8; ++a) m[(i0 + a) * kDim + j] = __fdiv_rn(acc[a], (float)S);
+}
+
+// Symmetrise, add ridge * trace / D to the diagonal and factor L L^T in place (lower).
+__global__ void __launch_bounds__(256) cholesky_kernel(float* __restrict__ factors, float ridge) {
+  extern __shared__ float A[];  // [128][129]
+  constexpr int ld = kDim + 1;
+  float* m = factors + (int64_t)blockIdx.x * kDim * kDim;
+  for (int e = threadIdx.x; e < kDim * kDim; e += blockDim.x) A[(e / kDim) * ld + e % kDim] = m[e];
+  __syncthreads();
+  for (int e = threadIdx.x; e < kDim * kDim; e += blockDim.x) {
+    const int i = e / kDim, j = e % kDim;
+    if (i > j) {
+      const float s = __fmul_rn(0.5f, __fadd_rn(A[i * ld + j], A[j * ld + i]));
+      A[i * ld + j] = s;
+      A[j * ld + i] = s;
+    }
+  }
+  __syncthreads();
+  __shared__ float ridge_add;
+  if (threadIdx.x == 0) {
+    float tr = 0.f;
+    for (int i = 0; i < kDim; ++i) tr = __fadd_rn(tr, A[i * ld + i]);
+    ridge_add = __fmul_rn(ridge, __fdiv_rn(tr, (float)kDim));
+  }
+  __syncthreads();
+  if (threadIdx.x < kDim) A[threadIdx.x * ld + threadIdx.x] = __fadd_rn(A[threadIdx.x * ld + threadIdx.x], ridge_add);
+  __syncthreads();
+  __shared__ float pivot;
+  for (int c = 0; c < kDim; ++c) {
+    if (threadIdx.x == 0) {
+      pivot = __fsqrt_rn(A[c * ld + c]);
+      A[c * ld + c] = pivot;
+    }
+    __syncthreads();
+    for (int i = c + 1 + threadIdx.x; i < kDim; i += blockDim.x) A[i * ld + c] = __fdiv_rn(A[i * ld + c], pivot);
+    __syncthreads();
+    const int rest = kDim - c - 1;
+    for (int e = threadIdx.x; e < rest * rest; e += blockDim.x) {
+      const int i = c + 1 + e / rest, j = c + 1 + e % rest;
+      if (j <= i) A[i * ld + j] = __fsub_rn(A[i * ld + j], __fmul_rn(A[i * ld + c], A[j * ld + c]));
+    }
+    __syncthreads();
+  }
+  for (int e = threadIdx.x; e < kDim * kDim; e += blockDim.x) {
+    const int i = e / kDim, j = e % kDim;
+    m[e] = j <= i ? A[i * ld + j] : 0.f;
+  }
+}
+
+// ================================================================== transform
+constexpr int kTfThreads = 192;  // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer
+constexpr int kTfStages = 2;
+constexpr int kTfTileBytes = 128 * kDim * 2;  // 32 KB: two 64-column halves of 128 rows
+constexpr int kTfHalfBytes = kTfTileBytes / 2;
+
+struct __align__(8) TfControl {
+  uint64_t full[kTfStages], empty[kTfStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+struct TfParams {
+  const float* factors;
+  __nv_bfloat16* features;
+  int* status;
+  int T, H, BH, video, tiles, splits;
+};
+
+__global__ void __launch_bounds__(kTfThreads) reblock_transform_kernel(const __grid_constant__ CUtensorMap tm_k,
+                                                                       const __grid_constant__ CUtensorMap tm_q,
+                                                                       TfParams p) {
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0u) {
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 920);
+    return;
+  }
+  uint8_t* sB = smem;                                   // L^T, K-major, two 64-column halves
+  uint8_t* sA = smem + kTfTileBytes;                    // token tiles
+  TfControl& C = *reinterpret_cast<TfControl*>(smem + (1 + kTfStages) * kTfTileBytes);
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int r = blockIdx.y;
+  const int side = r / p.BH, bh = r % p.BH, b = bh / p.H, h = bh % p.H;
+  const CUtensorMap* map = side == 0 ? &tm_k : &tm_q;  // rows [0, BH): K . L_Q; [BH, 2BH): Q . L_K
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kTfStages; ++s) {
+      mbar_init(smem_u32(&C.full[s]), 1);
+      mbar_init(smem_u32(&C.empty[s]), 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(smem_u32(&C.acc_full[a]), 1);
+      mbar_init(smem_u32(&C.acc_empty[a]), 128);
+    }
+    mbar_init(smem_u32(&C.mma_done), 1);
+    C.abort_flag = 0;
+    fence_barrier_init();
+  }
+  if (warp < 4) {
+    // B[n][k] = bf16(L[k][n]) in the 128-byte-swizzled K-major layout.
+    const int n = threadIdx.x;
+    const float* L = p.factors + (int64_t)r * kDim * kDim;
+#pragma unroll 1
+    for (int kh = 0; kh < 2; ++kh)
+#pragma unroll 1
+      for (int c = 0; c < 8; ++c) {
+        uint32_t w[4];
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          const int k0 = kh * 64 + c * 8 + 2 * e;
+          w[e] = cvt_bf16x2(L[k0 * kDim + n], L[(k0 + 1) * kDim + n]);
+        }
+        *reinterpret_cast<uint4*>(sB + kh * kTfHalfBytes + n * 128 + ((c ^ (n & 7)) * 16)) =
+            make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+  }
+  if (warp == 5) {
+    tmem_alloc(smem_u32(&C.tmem_base), 256);
+    tmem_relinquish();
+  }
+  if (warp == 4 && lane == 0) prefetch_tensormap(map);
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = C.tmem_base;
+  volatile int* abort_flag = &C.abort_flag;
+  const uint32_t a_base = smem_u32(sA), b_base = smem_u32(sB);
+
+  if (warp == 4) {
+    if (lane == 0) {
+      int armed[kTfStages] = {};
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.tiles; tile += p.splits, ++local) {
+        const int s = local % kTfStages;
+        if (!mbar_wait(smem_u32(&C.empty[s]), (uint32_t)(((local / kTfStages) & 1) ^ 1), abort_flag, p.status, 501))
+          break;
+        const uint32_t bar = smem_u32(&C.full[s]);
+        mbar_arrive_expect_tx(bar, kTfTileBytes);
+        ++armed[s];
+        const uint32_t dst = a_base + s * kTfTileBytes;
+        for (int dh = 0; dh < 2; ++dh)
+          for (int rh = 0; rh < 2; ++rh)
+            tma_load_3d(dst + dh * kTfHalfBytes + rh * (kTfHalfBytes / 2), map, bar, h * kDim + 64 * dh,
+                        tile * 128 + 64 * rh, b);
+      }
+      for (int s = 0; s < kTfStages; ++s)
+        if (armed[s] > 0) mbar_drain(smem_u32(&C.full[s]), (uint32_t)((armed[s] - 1) & 1));
+    }
+  } else if (warp == 5) {
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(128, 128, false);
+      int local = 0;
+      for (int tile = blockIdx.x; tile < p.tiles; tile += p.splits, ++local) {
+        const int s = local % kTfStages, buf = local & 1;
+        if (local >= 2 && !mbar_wait(smem_u32(&C.acc_empty[buf]), (uint32_t)(((local - 2) >> 1) & 1), abort_flag,
+                                     p.status, 502))
+          break;
+        if (!mbar_wait(smem_u32(&C.full[s]), (uint32_t)((local / kTfStages) & 1), abort_flag, p.status, 503)) break;
+        tc_fence_after();
+        const uint32_t acc = tmem + buf * 128;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint64_t ad = smem_desc_sw128(a_base + s * kTfTileBytes + (kk >> 2) * kTfHalfBytes, 16, 1024) +
+                              (uint64_t)((kk & 3) * 2);
+          const uint64_t bd = smem_desc_sw128(b_base + (kk >> 2) * kTfHalfBytes, 16, 1024) + (uint64_t)((kk & 3) * 2);
+          mma_ss(acc, ad, bd, idesc, kk > 0 ? 1u : 0u);
+        }
+        tc_commit(smem_u32(&C.empty[s]));
+        tc_commit(smem_u32(&C.acc_full[buf]));
+      }
+      tc_commit(smem_u32(&C.mma_done));
+    }
+  } else {
+    const int row = threadIdx.x;
+    const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    int local = 0;
+    for (int tile = blockIdx.x; tile < p.tiles; tile += p.splits, ++local) {
+      const int buf = local & 1;
+      const bool got = mbar_wait(smem_u32(&C.acc_full[buf]), (uint32_t)((local >> 1) & 1), abort_flag, p.status, 504);
+      if (!__all_sync(kFull, got)) break;
+      tc_fence_after();
+      const int t = tile * 128 + row;
+      __nv_bfloat16* out = p.features + ((int64_t)r * p.video + t) * kDim;
+#pragma unroll 1
+      for (int c = 0; c < 4; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tmem + lane_base + buf * 128 + 32 * c, v);
+        tmem_wait_ld();
+        if (t < p.video) {
+          float f[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) store8(out + 32 * c + 8 * q, f + 8 * q);
+        }
+      }
+      tc_fence_before();
+      mbar_arrive(smem_u32(&C.acc_empty[buf]));
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) {
+    tc_fence_after();
+    mbar_drain(smem_u32(&C.mma_done), 0);
+    tmem_dealloc(tmem, 256);
+  }
+}
+
+// ======================================================================= tree
+// Root order without the protected remainder: the N mod 64 tokens of largest squared
+// feature norm (equal norms: lower id) go to the tail of the permutation in root order.
+__global__ void __launch_bounds__(1024) reblock_root_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
+                                                            const int32_t* __restrict__ root_order,
+                                                            float* __restrict__ norms, int32_t* __restrict__ idx0,
+                                                            int32_t* __restrict__ perm, int direct) {
+  const int r = blockIdx.x;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int rem = N - active;
+  float* nr = norms + (int64_t)r * N;
+  __shared__ float best_v[32];
+  __shared__ int best_i[32];
+  __shared__ int counts[32][2];
+  __shared__ int base[2];
+  if (rem > 0) {
+    for (int t = warp; t < N; t += 32) {
+      float x[4];
+      load_row4(F + ((int64_t)r * N + t) * kDim, lane, x);
+      const float n2 = butterfly(lane_dot4(x, x));
+      if (lane == 0) nr[t] = n2;
+    }
+    __syncthreads();
+    for (int k = 0; k < rem; ++k) {
+      float v = -2.f;
+      int vi = 0x7fffffff;
+      for (int t = threadIdx.x; t < N; t += 1024) {
+        const float x = nr[t];
+        if (x > v) v = x, vi = t;  // t increases: the first maximum stays
+      }
+#pragma unroll
+      for (int o = 16; o >= 1; o >>= 1) {
+        const float ov = __shfl_xor_sync(kFull, v, o);
+        const int oi = __shfl_xor_sync(kFull, vi, o);
+        if (ov > v || (ov == v && oi < vi)) v = ov, vi = oi;
+      }
+      if (lane == 0) best_v[warp] = v, best_i[warp] = vi;
+      __syncthreads();
+      if (warp == 0) {
+        v = best_v[lane];
+        vi = best_i[lane];
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          const float ov = __shfl_xor_sync(kFull, v, o);
+          const int oi = __shfl_xor_sync(kFull, vi, o);
+          if (ov > v || (ov == v && oi < vi)) v = ov, vi = oi;
+        }
+        if (lane == 0) nr[vi] = -1.0f;  // excluded (norms are never negative)
+      }
+      __syncthreads();
+    }
+  }
+  if (threadIdx.x == 0) base[0] = 0, base[1] = 0;
+  __syncthreads();
+  int32_t* act_out = direct ? perm + (int64_t)r * N : idx0 + (int64_t)r * N;
+  for (int c0 = 0; c0 < N; c0 += 1024) {
+    const int pos = c0 + threadIdx.x;
+    const bool valid = pos < N;
+    const int id = valid ? (root_order ? root_order[pos] : pos) : 0;
+    const bool ex = valid && rem > 0 && nr[id] == -1.0f;
+    const unsigned m_ex = __ballot_sync(kFull, valid && ex), m_in = __ballot_sync(kFull, valid && !ex);
+    if (lane == 0) counts[warp][0] = __popc(m_in), counts[warp][1] = __popc(m_ex);
+    __syncthreads();
+    int before_in = 0, before_ex = 0, tot_in = 0, tot_ex = 0;
+    for (int w = 0; w < 32; ++w) {
+      if (w < warp) before_in += counts[w][0], before_ex += counts[w][1];
+      tot_in += counts[w][0], tot_ex += counts[w][1];
+    }
+    const unsigned lt = (1u << lane) - 1u;
+    if (valid) {
+      if (ex)
+        perm[(int64_t)r * N + active + base[1] + before_ex + __popc(m_ex & lt)] = id;
+      else
+        act_out[base[0] + before_in + __popc(m_in & lt)] = id;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) base[0] += tot_in, base[1] += tot_ex;
+    __syncthreads();
+  }
+}
+
+struct TreeLevel {
+  const int32_t* nodes;  // [nodes][kNodeInts]
+  const int32_t* tiles;  // [active / 64] node of each 64-position tile, -1 when not split
+  int count, P, S;
+};
+
+// One warp per (node, row): midpoint landmarks, binary proxy tree, directions in heap order.
+struct ProxySmem {
+  __nv_bfloat16 x[kLandmarks][kDim];
+  float n[kLandmarks][kDim];
+  float dist[kLandmarks][kLandmarks + 1];
+  int act[2][kLandmarks][kLandmarks];
+};
+
+__global__ void __launch_bounds__(32) reblock_proxy_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
+                                                           TreeLevel lv, const int32_t* __restrict__ idx_in,
+                                                           float* __restrict__ dirs) {
+  extern __shared__ __align__(16) uint8_t smem_raw[];
+  ProxySmem& S = *reinterpret_cast<ProxySmem*>(smem_raw);
+  const int node = blockIdx.x, r = blockIdx.y, lane = threadIdx.x;
+  const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
+  const int start = tbl[0], n = tbl[1], C = tbl[2];
+  const int32_t* caps = tbl + 4;
+  const int32_t* ids = idx_in + (int64_t)r * N + start;
+  const __nv_bfloat16* Fr = F + (int64_t)r * N * kDim;
+  // midpoint landmarks and their interval weights
+  const int64_t lo = (int64_t)lane * n / kLandmarks, hi = (int64_t)(lane + 1) * n / kLandmarks;
+  const int my_id = ids[lo + (hi - lo) / 2];
+  const int my_w = (int)(hi - lo);
+  for (int i = 0; i < kLandmarks; ++i) {
+    const int id = __shfl_sync(kFull, my_id, i);
+    *reinterpret_cast<uint2*>(&S.x[i][4 * lane]) =
+        __ldg(reinterpret_cast<const uint2*>(Fr + (int64_t)id * kDim + 4 * lane));
+  }
+  __syncwarp();
+  for (int i = 0; i < kLandmarks; ++i) {
+    float x[4], u[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[e] = __bfloat162float(S.x[i][4 * lane + e]);
+    unit4(x, u);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) S.n[i][4 * lane + e] = u[e];
+  }
+  __syncwarp();
+  for (int i = 0; i < kLandmarks; ++i) {
+    float a[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[e] = S.n[i][4 * lane + e];
+    for (int k = i + 1; k < kLandmarks; ++k) {
+      float bb[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) bb[e] = S.n[k][4 * lane + e];
+      const float d = __fsub_rn(1.0f, butterfly(lane_dot4(a, bb)));
+      if (lane == 0) S.dist[i][k] = d;
+    }
+  }
+  S.act[0][0][lane] = my_w;
+  __syncwarp();
+  float* out = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
+  int cur = 0, depth_nodes = 1, first_heap = 0, span = C;
+  while (span > 1) {
+    for (int j = 0; j < depth_nodes; ++j) {
+      const int hnode = first_heap + j;
+      const int s0 = j * span, mid = s0 + span / 2, s1 = s0 + span;
+      int lc = 0, rc = 0;
+      for (int c = s0; c < mid; ++c) lc += caps[c];
+      for (int c = mid; c < s1; ++c) rc += caps[c];
+      const int a = S.act[cur][j][lane];
+      const unsigned vmask = __ballot_sync(kFull, a > 0);
+      int first = vmask ? __ffs(vmask) - 1 : 0, second = first;
+      if (__popc(vmask) >= 2) {
+        float bv = 0.f;
+        int bk = -1;
+        if (a > 0)
+          for (int k = lane + 1; k < kLandmarks; ++k)
+            if ((vmask >> k) & 1u) {
+              const float d = S.dist[lane][k];
+              if (bk < 0 || d > bv) bv = d, bk = k;
+            }
+        int bi = lane;
+#pragma unroll
+        for (int o = 16; o >= 1; o >>= 1) {
+          const float ov = __shfl_xor_sync(kFull, bv, o);
+          const int ok = __shfl_xor_sync(kFull, bk, o), oi = __shfl_xor_sync(kFull, bi, o);
+          const bool take = ok >= 0 && (bk < 0 || ov > bv || (ov == bv && oi < bi));
+          if (take) bv = ov, bk = ok, bi = oi;
+        }
+        first = bi;
+        second = bk;
+      }
+      float left[4], right[4];
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        left[e] = __bfloat162float(S.x[first][4 * lane + e]);
+        right[e] = __bfloat162float(S.x[second][4 * lane + e]);
+      }
+      int lw = 0, rw = 0;
+      for (int it = 0; it < 2; ++it) {
+        float ul[4], ur[4], dir[4];
+        unit4(left, ul);
+        unit4(right, ur);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) dir[e] = __fsub_rn(ur[e], ul[e]);
+        float v[32];
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+          float nn[4];
+#pragma unroll
+          for (int e = 0; e < 4; ++e) nn[e] = S.n[i][4 * lane + e];
+          v[i] = lane_dot4(nn, dir);
+        }
+        reduce_scatter<32>(v, lane);
+        const float my_s = v[0];  // score of landmark `lane`
+        int rank = 0;
+        for (int jj = 0; jj < 32; ++jj) {
+          const float sj = __shfl_sync(kFull, my_s, jj);
+          rank += (sj < my_s || (sj == my_s && jj < lane)) ? 1 : 0;
+        }
+        int before = 0;
+        for (int jj = 0; jj < 32; ++jj) {
+          const int rj = __shfl_sync(kFull, rank, jj), aj = __shfl_sync(kFull, a, jj);
+          if (rj < rank) before += aj;
+        }
+        lw = min(max(lc - before, 0), a);
+        rw = a - lw;
+        float accl[4] = {0.f, 0.f, 0.f, 0.f}, accr[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int jj = 0; jj < 32; ++jj) {
+          const float wl = (float)__shfl_sync(kFull, lw, jj), wr = (float)__shfl_sync(kFull, rw, jj);
+#pragma unroll
+          for (int e = 0; e < 4; ++e) {
+            const float xj = __bfloat162float(S.x[jj][4 * lane + e]);
+            accl[e] = __fmaf_rn(wl, xj, accl[e]);
+            accr[e] = __fmaf_rn(wr, xj, accr[e]);
+          }
+        }
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          left[e] = __fdiv_rn(accl[e], (float)lc);
+          right[e] = __fdiv_rn(accr[e], (float)rc);
+        }
+      }
+      float ul[4], ur[4], dir[4];
+      unit4(left, ul);
+      unit4(right, ur);
+#pragma unroll
+      for (int e = 0; e < 4; ++e) dir[e] = __fsub_rn(ur[e], ul[e]);
+      *reinterpret_cast<float4*>(out + (int64_t)hnode * kDim + 4 * lane) = make_float4(dir[0], dir[1], dir[2], dir[3]);
+      if (span > 2) {
+        S.act[cur ^ 1][2 * j][lane] = lw;
+        S.act[cur ^ 1][2 * j + 1][lane] = rw;
+      }
+    }
+    __syncwarp();
+    cur ^= 1;
+    first_heap += depth_nodes;
+    depth_nodes *= 2;
+    span /= 2;
+  }
+}
+
+// Split scores of every token of the splitting nodes: s[h] = dot(unit(x), dir_h).
+template <int P>
+__global__ void __launch_bounds__(256) reblock_score_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
+                                                            TreeLevel lv, const int32_t* __restrict__ idx_in,
+                                                            const float* __restrict__ dirs,
+                                                            float* __restrict__ scores) {
+  __shared__ __align__(16) float sd[P][kDim];
+  const int tile = blockIdx.x, r = blockIdx.y;
+  const int node = lv.tiles[tile];
+  if (node < 0) return;
+  const int C = lv.nodes[(int64_t)node * kNodeInts + 2];
+  const float* nd = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
+  for (int e = threadIdx.x; e < P * kDim; e += blockDim.x) sd[e / kDim][e % kDim] = e / kDim < C - 1 ? nd[e] : 0.f;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const __nv_bfloat16* Fr = F + (int64_t)r * N * kDim;
+  for (int i = 0; i < 8; ++i) {
+    const int pos = tile * 64 + warp * 8 + i;
+    const int id = idx_in[(int64_t)r * N + pos];
+    float x[4], u[4];
+    load_row4(Fr + (int64_t)id * kDim, lane, x);
+    unit4(x, u);
+    float v[P];
+#pragma unroll
+    for (int hh = 0; hh < P; ++hh) {
+      const float4 d4 = *reinterpret_cast<const float4*>(&sd[hh][4 * lane]);
+      const float d[4] = {d4.x, d4.y, d4.z, d4.w};
+      v[hh] = lane_dot4(u, d);
+    }
+    reduce_scatter<P>(v, lane);
+    float* out = scores + ((int64_t)r * active + pos) * lv.S;
+    if (P >= 32) {
+#pragma unroll
+      for (int q = 0; q < (P >= 32 ? P / 32 : 1); ++q) {
+        const int hh = (P / 32) * lane + q;
+        if (hh < C - 1) out[hh] = v[q];
+      }
+    } else {
+      constexpr int group = P < 32 ? 32 / P : 1;
+      const int hh = lane / group;
+      if (lane % group == 0 && hh < C - 1) out[hh] = v[0];
+    }
+  }
+}
+
+// Exact-capacity routing of one node (per internal proxy node: the left capacity goes to the
+// smallest (score, id) keys, found by radix select) and the stable partition into children.
+constexpr int kRouteThreads = 512;
+constexpr int kRouteWarps = kRouteThreads / 32;
+
+__global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int active, TreeLevel lv,
+                                                                      const int32_t* __restrict__ idx_in,
+                                                                      const float* __restrict__ scores,
+                                                                      uint32_t* __restrict__ keys,
+                                                                      uint8_t* __restrict__ state,
+                                                                      int32_t* __restrict__ idx_out,
+                                                                      int32_t* __restrict__ perm,
+                                                                      int* __restrict__ status) {
+  __shared__ int hist[32][256];
+  __shared__ int target[32], ties[32], need_ids[32];
+  __shared__ uint32_t prefix[32], id_prefix[32];
+  __shared__ int any_ids;
+  __shared__ int warp_cnt[kRouteWarps][kMaxChildren];
+  __shared__ int warp_off[kRouteWarps][kMaxChildren];
+  __shared__ int running[kMaxChildren], child_off[kMaxChildren];
+  const int node = blockIdx.x, r = blockIdx.y;
+  const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
+  const int start = tbl[0], n = tbl[1], C = tbl[2];
+  const int32_t* caps = tbl + 4;
+  const int32_t* ids = idx_in + (int64_t)r * N + start;
+  const float* sc = scores + ((int64_t)r * active + start) * lv.S;
+  uint32_t* key = keys + (int64_t)r * active + start;
+  uint8_t* st = state + (int64_t)r * active + start;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  for (int t = tid; t < n; t += kRouteThreads) st[t] = 0;
+  __syncthreads();
+  int depth_nodes = 1, first_heap = 0, span = C;
+  while (span > 1) {
+    const int nd = depth_nodes;
+    if (tid < nd) {
+      const int s0 = tid * span, mid = s0 + span / 2;
+      int lc = 0;
+      for (int c = s0; c < mid; ++c) lc += caps[c];
+      target[tid] = lc;
+      prefix[tid] = 0;
+      id_prefix[tid] = 0;
+    }
+    for (int t = tid; t < n; t += kRouteThreads) key[t] = order_key(sc[(int64_t)t * lv.S + st[t]]);
+    __syncthreads();
+    // radix select on the score key, most significant byte first
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+      __syncthreads();
+      for (int t = tid; t < n; t += kRouteThreads) {
+        const int j = st[t] - first_heap;
+        const uint32_t kk = key[t];
+        if (pass == 0 || (kk >> (shift + 8)) == (prefix[j] >> (shift + 8))) atomicAdd(&hist[j][(kk >> shift) & 255], 1);
+      }
+      __syncthreads();
+      if (tid < nd) {
+        int cum = 0, want = target[tid];
+        for (int bin = 0; bin < 256; ++bin) {
+          const int c = hist[tid][bin];
+          if (cum + c >= want) {
+            prefix[tid] |= (uint32_t)bin << shift;
+            target[tid] = want - cum;
+            ties[tid] = c;
+            break;
+          }
+          cum += c;
+        }
+      }
+      __syncthreads();
+    }
+    if (tid == 0) {
+      int any = 0;
+      for (int j = 0; j < nd; ++j) {
+        need_ids[j] = target[j] < ties[j] ? 1 : 0;
+        any |= need_ids[j];
+      }
+      any_ids = any;
+    }
+    __syncthreads();
+    if (any_ids) {
+      // equal scores at the cut: the lowest token ids among them go left
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+        __syncthreads();
+        for (int t = tid; t < n; t += kRouteThreads) {
+          const int j = st[t] - first_heap;
+          if (!need_ids[j] || key[t] != prefix[j]) continue;
+          const uint32_t id = (uint32_t)ids[t];
+          if (pass == 0 || (id >> (shift + 8)) == (id_prefix[j] >> (shift + 8))) atomicAdd(&hist[j][(id >> shift) & 255], 1);
+        }
+        __syncthreads();
+        if (tid < nd && need_ids[tid]) {
+          int cum = 0, want = target[tid];
+          for (int bin = 0; bin < 256; ++bin) {
+            const int c = hist[tid][bin];
+            if (cum + c >= want) {
+              id_prefix[tid] |= (uint32_t)bin << shift;
+              target[tid] = want - cum;
+              break;
+            }
+            cum += c;
+          }
+        }
+        __syncthreads();
+      }
+    }
+    for (int t = tid; t < n; t += kRouteThreads) {
+      const int hnode = st[t], j = hnode - first_heap;
+      const uint32_t kk = key[t];
+      const bool left = kk < prefix[j] || (kk == prefix[j] && (!need_ids[j] || (uint32_t)ids[t] <= id_prefix[j]));
+      st[t] = (uint8_t)(left ? 2 * hnode + 1 : 2 * hnode + 2);
+    }
+    __syncthreads();
+    first_heap += depth_nodes;
+    depth_nodes *= 2;
+    span /= 2;
+  }
+  // stable partition by child label
+  if (tid < C) {
+    int off = 0;
+    for (int c = 0; c < tid; ++c) off += caps[c];
+    child_off[tid] = off;
+    running[tid] = 0;
+  }
+  __syncthreads();
+  const int label_base = C - 1;
+  int32_t* out_next = idx_out + (int64_t)r * N + start;
+  int32_t* out_leaf = perm + (int64_t)r * N + start;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int c0 = 0; c0 < n; c0 += kRouteThreads) {
+    for (int c = lane; c < C; c += 32) warp_cnt[warp][c] = 0;
+    __syncwarp();
+    const int t = c0 + tid;
+    const bool valid = t < n;
+    const int label = valid ? st[t] - label_base : -1;
+    const unsigned peers = __match_any_sync(kFull, label);
+    const int rank = __popc(peers & lt);
+    if (valid && rank == 0) warp_cnt[warp][label] = __popc(peers);
+    __syncthreads();
+    if (tid < C) {
+      int base = running[tid];
+      for (int w = 0; w < kRouteWarps; ++w) {
+        warp_off[w][tid] = base;
+        base += warp_cnt[w][tid];
+      }
+      running[tid] = base;
+    }
+    __syncthreads();
+    if (valid) {
+      const int dst = child_off[label] + warp_off[warp][label] + rank;
+      (caps[label] == 64 ? out_leaf : out_next)[dst] = ids[t];
+    }
+  }
+  __syncthreads();
+  if (tid < C && running[tid] != caps[tid] && status) atomicExch(status, 610);
+}
+
+__global__ void reblock_inverse_kernel(const int32_t* __restrict__ perm, int N, int64_t total,
+                                       int32_t* __restrict__ inverse) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= total) return;
+  const int64_t r = i / N;
+  inverse[r * N + perm[i]] = (int32_t)(i - r * N);
+}
+
+// ----------------------------------------------------------------- host helpers
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (fn == nullptr) {
+    void* ptr = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(ptr);
+  }
+  return fn;
+}
+
+// {H*D, T, B} bf16 map, 64 x 64 box, 128-byte swizzle.
+int make_bthd_map(CUtensorMap* map, const void* base, int B, int T, int H) {
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr) {
+    set_error("sb_reblock_transform: cuTensorMapEncodeTiled is unavailable");
+    return SB_ERR_CUDA;
+  }
+  const uint64_t HD = (uint64_t)H * kDim;
+  const cuuint64_t dims[3] = {HD, (cuuint64_t)T, (cuuint64_t)B};
+  const cuuint64_t strides[2] = {HD * 2, HD * 2 * (uint64_t)T};
+  const cuuint32_t box[3] = {64, 64, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) {
+    set_error("sb_reblock_transform: cuTensorMapEncodeTiled failed (CUresult %d)", (int)res);
+    return SB_ERR_CUDA;
+  }
+  return SB_OK;
+}
+
+int sm_count() {
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+struct WorkspaceLayout {
+  size_t idx, scores, dirs, keys, state, total;
+};
+
+inline size_t align256(size_t x) { return (x + 255) & ~(size_t)255; }
+
+WorkspaceLayout workspace_layout(const int32_t* plan, int rows) {
+  const int64_t N = plan[1], A = plan[2], max_nodes = plan[3], max_s = std::max(1, plan[4] - 1);
+  WorkspaceLayout w{};
+  size_t off = 0;
+  w.idx = off;
+  off = align256(off + 2 * sizeof(int32_t) * (size_t)rows * N);
+  w.scores = off;
+  off = align256(off + sizeof(float) * (size_t)rows * A * max_s);
+  w.dirs = off;
+  off = align256(off + sizeof(float) * (size_t)rows * std::max<int64_t>(max_nodes, 1) * max_s * kDim);
+  w.keys = off;
+  off = align256(off + sizeof(uint32_t) * (size_t)rows * std::max(N, A));
+  w.state = off;
+  off = align256(off + (size_t)rows * A);
+  w.total = off;
+  return w;
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" int sb_reblock_metric(const void* q, const void* k, int dtype, int B, int T, int H, int D,
+                                 const int32_t* samples, int num_samples, float ridge, float* factors, void* stream) {
+  SB_CHECK_ARG(q && k && samples && factors, "sb_reblock_metric: null pointer");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_reblock_metric: bad dtype");
+  SB_CHECK_ARG(D == kDim, "sb_reblock_metric: head dimension must be 128, got %d", D);
+  SB_CHECK_ARG(B > 0 && T > 0 && H > 0 && num_samples > 0, "sb_reblock_metric: empty input");
+  SB_CHECK_ARG(ridge >= 0.f, "sb_reblock_metric: ridge must be non-negative");
+  cudaStream_t s = (cudaStream_t)stream;
+  const int BH = B * H;
+  dim3 grid(kDim / 16, 2 * BH);
+  if (dtype == SB_BF16)
+    metric_moment_kernel<__nv_bfloat16><<<grid, 256, 0, s>>>((const __nv_bfloat16*)q, (const __nv_bfloat16*)k, T, H,
+                                                             BH, samples, num_samples, factors);
+  else
+    metric_moment_kernel<float><<<grid, 256, 0, s>>>((const float*)q, (const float*)k, T, H, BH, samples, num_samples,
+                                                     factors);
+  SB_CHECK_LAUNCH("sb_reblock_metric: moments");
+  const int smem = kDim * (kDim + 1) * (int)sizeof(float);
+  cudaError_t err = cudaFuncSetAttribute(cholesky_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_reblock_metric: set smem");
+  cholesky_kernel<<<2 * BH, 256, smem, s>>>(factors, ridge);
+  SB_CHECK_LAUNCH("sb_reblock_metric: cholesky");
+  return SB_OK;
+}
+
+extern "C" int sb_reblock_transform(const void* q, const void* k, int B, int T, int H, int D, int video_tokens,
+                                    const float* factors, void* features, void* stream) {
+  SB_CHECK_ARG(q && k && factors && features, "sb_reblock_transform: null pointer");
+  SB_CHECK_ARG(D == kDim, "sb_reblock_transform: head dimension must be 128, got %d", D);
+  SB_CHECK_ARG(B > 0 && H > 0 && video_tokens > 0 && video_tokens <= T, "sb_reblock_transform: bad shape");
+  SB_CHECK_ARG(((uintptr_t)q % 16) == 0 && ((uintptr_t)k % 16) == 0 && ((uintptr_t)features % 16) == 0,
+               "sb_reblock_transform: tensors must be 16-byte aligned");
+  int* status = device_status_ptr();
+  if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_reblock_transform: status word");
+  CUtensorMap mk, mq;
+  int rc;
+  if ((rc = make_bthd_map(&mk, k, B, T, H)) != SB_OK) return rc;
+  if ((rc = make_bthd_map(&mq, q, B, T, H)) != SB_OK) return rc;
+  TfParams p{};
+  p.factors = factors;
+  p.features = static_cast<__nv_bfloat16*>(features);
+  p.status = status;
+  p.T = T;
+  p.H = H;
+  p.BH = B * H;
+  p.video = video_tokens;
+  p.tiles = ceil_div(video_tokens, 128);
+  const int rows = 2 * p.BH;
+  p.splits = std::max(1, std::min(p.tiles, ceil_div(2 * sm_count(), rows)));
+  const size_t smem = (size_t)(1 + kTfStages) * kTfTileBytes + sizeof(TfControl);
+  cudaError_t err = cudaFuncSetAttribute(reblock_transform_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_reblock_transform: set smem");
+  reblock_transform_kernel<<<dim3(p.splits, rows), kTfThreads, smem, (cudaStream_t)stream>>>(mk, mq, p);
+  SB_CHECK_LAUNCH("sb_reblock_transform launch");
+  return SB_OK;
+}
+
+extern "C" int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, int tokens, int32_t* plan,
+                                   int64_t capacity) {
+  SB_CHECK_ARG(schedule && schedule_len > 0, "sb_reblock_plan: empty schedule");
+  SB_CHECK_ARG(tokens >= 64, "sb_reblock_plan: at least 64 tokens are required, got %d", tokens);
+  const int active = tokens - tokens % 64;
+  const int tiles = active / 64;
+  struct Seg {
+    int start, leaves;
+  };
+  std::vector<Seg> segs{{0, tiles}};
+  std::vector<std::vector<int32_t>> level_nodes;
+  std::vector<int> level_P;
+  const int levels = schedule[0];
+  int pos = 1;
+  for (int level = 0; level < levels; ++level) {
+    SB_CHECK_ARG(pos < schedule_len, "sb_reblock_plan: schedule truncated");
+    const int entries = schedule[pos];
+    const int level_pos = pos + 1;
+    int p = level_pos;
+    for (int e = 0; e < entries; ++e) {
+      SB_CHECK_ARG(p + 1 < schedule_len, "sb_reblock_plan: schedule truncated");
+      p += 2 + schedule[p + 1];
+    }
+    SB_CHECK_ARG(p <= schedule_len, "sb_reblock_plan: schedule truncated");
+    pos = p;
+    std::vector<Seg> next;
+    std::vector<int32_t> nodes;
+    int maxC = 2;
+    for (const Seg& sg : segs) {
+      if (sg.leaves <= 1) continue;
+      int q = level_pos, found = -1;
+      for (int e = 0; e < entries; ++e) {
+        if (schedule[q] == sg.leaves) {
+          found = q;
+          break;
+        }
+        q += 2 + schedule[q + 1];
+      }
+      SB_CHECK_ARG(found >= 0, "sb_reblock_plan: no budget for a node of %d leaves at round %d", sg.leaves, level);
+      const int C = schedule[found + 1];
+      SB_CHECK_ARG(C >= 2 && C <= kMaxChildren && (C & (C - 1)) == 0,
+                   "sb_reblock_plan: the CUDA tree takes power-of-two fanouts up to 64, got %d children", C);
+      std::vector<int32_t> rec(kNodeInts, 0);
+      rec[0] = sg.start * 64;
+      rec[1] = sg.leaves * 64;
+      rec[2] = C;
+      int off = sg.start, sum = 0;
+      for (int c = 0; c < C; ++c) {
+        const int budget = schedule[found + 2 + c];
+        SB_CHECK_ARG(budget >= 1, "sb_reblock_plan: empty child");
+        rec[4 + c] = 64 * budget;
+        next.push_back({off, budget});
+        off += budget;
+        sum += budget;
+      }
+      SB_CHECK_ARG(sum == sg.leaves, "sb_reblock_plan: child budgets do not cover the node");
+      nodes.insert(nodes.end(), rec.begin(), rec.end());
+      maxC = std::max(maxC, C);
+    }
+    for (const Seg& sg : segs)
+      if (sg.leaves <= 1) next.push_back(sg);
+    std::sort(next.begin(), next.end(), [](const Seg& a, const Seg& b) { return a.start < b.start; });
+    segs.swap(next);
+    if (!nodes.empty()) {
+      level_nodes.push_back(std::move(nodes));
+      level_P.push_back(maxC);
+    }
+  }
+  for (const Seg& sg : segs)
+    SB_CHECK_ARG(sg.leaves == 1, "sb_reblock_plan: the schedule ends before every node is a leaf");
+  const int L = (int)level_nodes.size();
+  int64_t length = kPlanHeader + (int64_t)kLevelInts * L;
+  int max_nodes = 0, maxP = 2;
+  for (int l = 0; l < L; ++l) {
+    length += (int64_t)level_nodes[l].size() + tiles;
+    max_nodes = std::max(max_nodes, (int)(level_nodes[l].size() / kNodeInts));
+    maxP = std::max(maxP, level_P[l]);
+  }
+  if (plan == nullptr) return length;
+  SB_CHECK_ARG(capacity >= length, "sb_reblock_plan: plan buffer holds %lld ints, %lld needed", (long long)capacity,
+               (long long)length);
+  std::fill(plan, plan + length, 0);
+  plan[0] = L;
+  plan[1] = tokens;
+  plan[2] = active;
+  plan[3] = max_nodes;
+  plan[4] = maxP;
+  plan[5] = (int32_t)length;
+  int64_t off = kPlanHeader + (int64_t)kLevelInts * L;
+  for (int l = 0; l < L; ++l) {
+    int32_t* lv = plan + kPlanHeader + kLevelInts * l;
+    const int count = (int)(level_nodes[l].size() / kNodeInts);
+    lv[0] = count;
+    lv[1] = (int32_t)off;
+    std::copy(level_nodes[l].begin(), level_nodes[l].end(), plan + off);
+    off += (int64_t)level_nodes[l].size();
+    lv[2] = (int32_t)off;
+    int32_t* tile_tbl = plan + off;
+    std::fill(tile_tbl, tile_tbl + tiles, -1);
+    for (int j = 0; j < count; ++j) {
+      const int32_t* rec = plan + lv[1] + (int64_t)j * kNodeInts;
+      for (int t = rec[0] / 64; t < (rec[0] + rec[1]) / 64; ++t) tile_tbl[t] = j;
+    }
+    off += tiles;
+    lv[3] = level_P[l];
+    lv[4] = level_P[l] - 1;
+  }
+  return length;
+}
+
+extern "C" int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows) {
+  SB_CHECK_ARG(plan && rows > 0, "sb_reblock_workspace_bytes: bad arguments");
+  return (int64_t)workspace_layout(plan, rows).total;
+}
+
+extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+                               const int32_t* plan_host, const int32_t* plan_device, void* workspace,
+                               int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream) {
+  SB_CHECK_ARG(features && plan_host && plan_device && workspace && perm && inverse, "sb_reblock_tree: null pointer");
+  SB_CHECK_ARG(D == kDim, "sb_reblock_tree: feature dimension must be 128, got %d", D);
+  SB_CHECK_ARG(rows > 0 && rows < 65536, "sb_reblock_tree: rows must lie in [1, 65535]");
+  SB_CHECK_ARG(plan_host[1] == tokens, "sb_reblock_tree: the plan was built for %d tokens, not %d", plan_host[1],
+               tokens);
+  SB_CHECK_ARG(((uintptr_t)features % 16) == 0 && ((uintptr_t)workspace % 256) == 0,
+               "sb_reblock_tree: features must be 16-byte and the workspace 256-byte aligned");
+  const WorkspaceLayout W = workspace_layout(plan_host, rows);
+  SB_CHECK_ARG((size_t)workspace_bytes >= W.total, "sb_reblock_tree: workspace holds %lld bytes, %zu needed",
+               (long long)workspace_bytes, W.total);
+  int* status = device_status_ptr();
+  if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_reblock_tree: status word");
+  cudaStream_t s = (cudaStream_t)stream;
+  const __nv_bfloat16* F = static_cast<const __nv_bfloat16*>(features);
+  uint8_t* ws = static_cast<uint8_t*>(workspace);
+  int32_t* idx[2] = {reinterpret_cast<int32_t*>(ws + W.idx),
+                     reinterpret_cast<int32_t*>(ws + W.idx) + (size_t)rows * tokens};
+  float* scores = reinterpret_cast<float*>(ws + W.scores);
+  float* dirs = reinterpret_cast<float*>(ws + W.dirs);
+  uint32_t* keys = reinterpret_cast<uint32_t*>(ws + W.keys);
+  uint8_t* state = ws + W.state;
+  const int L = plan_host[0], active = plan_host[2];
+  reblock_root_kernel<<<rows, 1024, 0, s>>>(F, tokens, active, root_order, reinterpret_cast<float*>(keys), idx[0],
+                                            perm, L == 0 ? 1 : 0);
+  SB_CHECK_LAUNCH("sb_reblock_tree: root");
+  const int proxy_smem = (int)sizeof(ProxySmem);
+  cudaError_t err = cudaFuncSetAttribute(reblock_proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, proxy_smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
+  int cur = 0;
+  for (int l = 0; l < L; ++l) {
+    const int32_t* lh = plan_host + kPlanHeader + kLevelInts * l;
+    TreeLevel lv{plan_device + lh[1], plan_device + lh[2], lh[0], lh[3], lh[4]};
+    reblock_proxy_kernel<<<dim3(lv.count, rows), 32, proxy_smem, s>>>(F, tokens, active, lv, idx[cur], dirs);
+    SB_CHECK_LAUNCH("sb_reblock_tree: proxy");
+    const dim3 sgrid(active / 64, rows);
+    switch (lv.P) {
+      case 2: reblock_score_kernel<2><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 4: reblock_score_kernel<4><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 8: reblock_score_kernel<8><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 16: reblock_score_kernel<16><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 32: reblock_score_kernel<32><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 64: reblock_score_kernel<64><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      default: set_error("sb_reblock_tree: bad plan fanout %d", lv.P); return SB_ERR_INVALID;
+    }
+    SB_CHECK_LAUNCH("sb_reblock_tree: scores");
+    reblock_route_kernel<<<dim3(lv.count, rows), kRouteThreads, 0, s>>>(tokens, active, lv, idx[cur], scores, keys,
+                                                                         state, idx[cur ^ 1], perm, status);
+    SB_CHECK_LAUNCH("sb_reblock_tree: route");
+    cur ^= 1;
+  }
+  const int64_t total = (int64_t)rows * tokens;
+  reblock_inverse_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(perm, tokens, total, inverse);
+  SB_CHECK_LAUNCH("sb_reblock_tree: inverse");
+  return SB_OK;
+}

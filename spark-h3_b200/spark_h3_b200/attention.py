@@ -13,6 +13,7 @@ import math
 import torch
 
 from . import ops
+from . import reblock as _reblock
 from .hierarchy import build_reblock_hierarchy, virtual_query_layout
 
 BACKEND_TENSOR = "b200_sm100_fused_virtual_query"
@@ -66,9 +67,6 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     _check_inputs(q_bthd, k_bthd, v_bthd)
     if cfg.sol_route_topk_ratio is None:
         raise RuntimeError("the B200 path implements Top-K routed Spark attention; set sol_route_topk_ratio")
-    if cfg.sol_landmark_preprocess:
-        raise NotImplementedError("landmark-v2 reblocking (modes 'full' and 'reblock_only') is not available on the "
-                                  "B200 path yet; use mode='reweight_only' or 'topk_only'")
     if cfg.sol_video_tail_mode != "dense" or cfg.sol_legacy_full_query:
         raise NotImplementedError("the B200 path implements sol_video_tail_mode='dense' only")
     if cfg.sol_tail_granularity != "query" or cfg.sol_reweight_summary_math != "tensorcore" \
@@ -94,6 +92,22 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     anchor_dtype = torch.float32 if cfg.sol_global_anchor_dtype == "float32" or q_bthd.dtype == torch.float32 \
         else q_bthd.dtype
 
+    query_inverse = None
+    if cfg.sol_landmark_preprocess:
+        _check_reblock(cfg, q_bthd, block)
+        q_perm, query_inverse, k_perm, _, hierarchy = _reblock.qk_block_permutations(
+            q_bthd, k_bthd, video, layout.grid, children=cfg.landmark_tree_v2_children,
+            fanout_mode=cfg.landmark_tree_v2_fanout_mode, final_fanout=cfg.landmark_tree_v2_final_fanout,
+            root_fanout=cfg.landmark_tree_v2_root_fanout, ridge=cfg.rope_sol_key_ridge_epsilon,
+            initial_order=cfg.landmark_tree_v2_initial_order)
+        controller.landmark_reblock_hierarchy = hierarchy
+        q_bthd = ops.headwise_permute(q_bthd, q_perm, video)
+        k_bthd = ops.headwise_permute(k_bthd, k_perm, video)
+        v_bthd = ops.headwise_permute(v_bthd, k_perm, video)
+        controller.counts["rope_sol_landmark_tree_v2_key_assignments"] += 1
+        controller.counts["rope_sol_landmark_tree_v2_query_assignments"] += 1
+        controller.counts["sol_landmark_preprocess_calls"] += 1
+
     qc = ops.pool_queries(q_bthd, block)
     anchor = ops.query_anchor(qc, block, query_blocks, anchor_dtype)
     kc, ak, av, lm = ops.pool_keys_summaries(k_bthd, v_bthd, anchor, block, weighted_kv=weighted_kv,
@@ -105,20 +119,32 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     controller.sol_backend = BACKEND_TENSOR if (q_bthd.dtype == torch.bfloat16 and D == 128) else BACKEND_SIMT
     controller.counts["sol_topk_packed_route_calls"] += 1
     controller.counts["sol_virtual_query_calls"] += 1
-    controller.counts["sol_identity_virtual_query_calls"] += 1
-    if cfg.sol_spark_mode == "reweight_only":
-        controller.counts["sol_identity_reweight_calls"] += 1
+    if not cfg.sol_landmark_preprocess:
+        controller.counts["sol_identity_virtual_query_calls"] += 1
+        if cfg.sol_spark_mode == "reweight_only":
+            controller.counts["sol_identity_reweight_calls"] += 1
     controller.counts["sol_topk_calls"] += 1
     if T > query_tokens:
         controller.counts["sol_dense_context_queries"] += 1
-    key = ("identity_global_anchor", T, video, layout.grid)
-    topology = controller._virtual_query_layout_cache.get(key)
-    if topology is None and video >= 64:
+    if cfg.sol_landmark_preprocess:
+        key = ("reblock_global_anchor", T, video, controller.landmark_reblock_hierarchy)
+        topology = controller._virtual_query_layout_cache.get(key)
+        if topology is None:
+            topology = dict(virtual_query_layout(video, T, 99, hierarchy=controller.landmark_reblock_hierarchy)
+                            ["metadata"])
+            controller._virtual_query_layout_cache[key] = topology
+        controller.sol_virtual_query_layout = topology
+        controller.counts["sol_virtual_query_fused_permute_calls"] += 1
+        key = None
+    else:
+        key = ("identity_global_anchor", T, video, layout.grid)
+    topology = controller._virtual_query_layout_cache.get(key) if key is not None else None
+    if key is not None and topology is None and video >= 64:
         hierarchy = build_reblock_hierarchy(video, cfg.landmark_tree_v2_children, grid_shape=tuple(layout.grid),
                                             fanout_mode=cfg.landmark_tree_v2_fanout_mode)
         topology = dict(virtual_query_layout(video, T, 99, hierarchy=hierarchy)["metadata"])
         controller._virtual_query_layout_cache[key] = topology
-    if topology is not None:
+    if key is not None and topology is not None:
         controller.sol_virtual_query_layout = {**topology, "layout": "identity_physical_order",
                                                "anchor_policy": "global"}
     if cfg.sol_log_density and controller.sol_route_density is None:
@@ -128,7 +154,30 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
                      packed_route_words=math.ceil(nb / 32))
         stats.update(topk_density(stats))
         controller.sol_route_density = stats
+    if query_inverse is not None:
+        out = ops.headwise_permute(out, query_inverse, video)
     return out if return_bthd else out.permute(0, 2, 1, 3).contiguous()
+
+
+_REBLOCK_DEFAULTS = dict(
+    landmark_tree_v2_distance="cosine", landmark_tree_v2_order_mode="parent_order", landmark_tree_v2_mean_mode="raw",
+    landmark_tree_v2_moment_mode="raw", landmark_tree_v2_group_size=1, landmark_tree_v2_landmark_mode="midpoint",
+    landmark_tree_v2_landmark_count=32, landmark_tree_v2_aggregation="linear", landmark_tree_v2_m2_side="both",
+    landmark_tree_v2_m2_estimator="hilbert_midpoint", landmark_tree_v2_proxy_iterations=2,
+    landmark_tree_v2_proxy_seed_rule="farthest_pair", landmark_tree_v2_proxy_update_rule="mean",
+    landmark_tree_v2_layout_reuse="independent", landmark_tree_v2_fanout_mode="power_of_two_fanout")
+
+
+def _check_reblock(cfg, q, block: int) -> None:
+    """The B200 reblock implements the production landmark-tree-v2 configuration."""
+    if block != 64:
+        raise NotImplementedError("landmark reblocking builds 64-token blocks; use sol_block_size=64")
+    if q.dtype != torch.bfloat16 or q.shape[-1] != 128:
+        raise RuntimeError("the B200 reblock path takes bf16 Q/K/V with head dimension 128")
+    for name, default in _REBLOCK_DEFAULTS.items():
+        value = getattr(cfg, name)
+        if value != default:
+            raise NotImplementedError(f"the B200 reblock path implements {name}={default!r}; got {value!r}")
 
 
 def spark_reweight(a: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int = 64,

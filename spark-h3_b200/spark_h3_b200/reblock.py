@@ -1,0 +1,303 @@
+"""Landmark-tree-v2 reblocking on the B200: the per-(batch, head) token permutations that
+group similar queries and similar keys into 64-token blocks before Spark routing.
+
+Host side of the reference's reblock path:
+  * `hilbert_midpoint_sample_indices`  mahalanobis_kmeans.py:11-96 (Skilling 3-D Hilbert
+    order, N/64 uniformly spaced samples; integer host logic, cached per grid)
+  * `initial_token_indices`            landmark_initial_order.py:44-77 (root orders)
+  * `ReblockPlan`                      landmark_tree_v2.py:904-1172
+    (PreparedLandmarkTreeV2Permutation: the hierarchy's node tables and scratch, prepared
+    once per shape and reused)
+  * `spark_reblock`                    spark.py:32 / landmark_tree_v2.py:835-901
+    (recursive_landmark_tree_v2_blocks), default options only
+  * `qk_block_permutations`            spark_integration.py:394-851
+    (_landmark_tree_v2_qk_block_permutations: metric factors, [K.Lq ; Q.Lk] features, tree)
+All device work runs in libsparkh3b200.so (sb_reblock_metric / _transform / _tree).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+from functools import lru_cache
+
+import numpy as np
+import torch
+
+from . import _lib
+from .hierarchy import ReblockHierarchy, build_reblock_hierarchy
+from .ops import _dtype_code, _require_cuda, _stream
+
+INITIAL_ORDERS = ("flat", "tile_t4h4w4", "hilbert_thw", "hilbert_twh", "hilbert_htw", "hilbert_hwt", "hilbert_wth",
+                  "hilbert_wht")
+BLOCK = 64
+
+
+def _grid_tuple(grid_shape) -> tuple[int, int, int]:
+    if not isinstance(grid_shape, (tuple, list)) or len(grid_shape) != 3:
+        raise ValueError("grid_shape must contain three positive integers (T,H,W)")
+    grid = tuple(int(g) for g in grid_shape)
+    if any(g <= 0 for g in grid):
+        raise ValueError("grid_shape must contain three positive integers (T,H,W)")
+    return grid
+
+
+def _hilbert_index(coords: np.ndarray, bits: int) -> np.ndarray:
+    """Hilbert index of [N, 3] integer coordinates on a 2^bits cube (Skilling's transpose:
+    inverse-undo of the Gray-code excess, then bit interleaving, axis 0 most significant)."""
+    x = coords.astype(np.int64, copy=True)
+    top = 1 << (bits - 1)
+    q = top
+    while q > 1:
+        mask = q - 1
+        for axis in range(3):
+            hi = (x[:, axis] & q) != 0
+            x[hi, 0] ^= mask
+            lo = ~hi
+            t = (x[lo, 0] ^ x[lo, axis]) & mask
+            x[lo, 0] ^= t
+            x[lo, axis] ^= t
+        q >>= 1
+    x[:, 1] ^= x[:, 0]
+    x[:, 2] ^= x[:, 1]
+    gray = np.zeros(len(x), dtype=np.int64)
+    q = top
+    while q > 1:
+        gray[(x[:, 2] & q) != 0] ^= q - 1
+        q >>= 1
+    x ^= gray[:, None]
+    index = np.zeros(len(x), dtype=np.int64)
+    for bit in range(bits - 1, -1, -1):
+        for axis in range(3):
+            index = (index << 1) | ((x[:, axis] >> bit) & 1)
+    return index
+
+
+@lru_cache(maxsize=32)
+def _initial_order(grid: tuple[int, int, int], name: str) -> np.ndarray:
+    frames, height, width = grid
+    ids = np.arange(frames * height * width, dtype=np.int64)
+    if name == "flat":
+        return ids
+    t, h, w = ids // (height * width), (ids // width) % height, ids % width
+    if name == "tile_t4h4w4":
+        tile = ((t // 4) * ((height + 3) // 4) + h // 4) * ((width + 3) // 4) + w // 4
+        return np.argsort(tile * 64 + (t % 4) * 16 + (h % 4) * 4 + w % 4, kind="stable")
+    axes = {"t": t, "h": h, "w": w}
+    coords = np.stack([axes[a] for a in name[len("hilbert_"):]], axis=-1)
+    bits = max(1, (max(grid) - 1).bit_length())
+    return np.argsort(_hilbert_index(coords, bits), kind="stable")
+
+
+def initial_token_indices(grid_shape, initial_order: str = "flat") -> np.ndarray:
+    """Root order of the tree: raster ids in the named traversal (read-only, cached)."""
+    if initial_order not in INITIAL_ORDERS:
+        raise ValueError(f"initial_order must be one of {', '.join(INITIAL_ORDERS)}")
+    return _initial_order(_grid_tuple(grid_shape), initial_order)
+
+
+@lru_cache(maxsize=32)
+def _midpoints(grid: tuple[int, int, int], count: int) -> np.ndarray:
+    order = _initial_order(grid, "hilbert_thw")
+    n = len(order)
+    count = min(max(1, int(count)), n)
+    pos = np.floor((np.arange(count, dtype=np.float64) + 0.5) * n / count).astype(np.int64)
+    return order[np.minimum(pos, n - 1)]
+
+
+def hilbert_midpoint_sample_indices(grid_shape, count: int) -> np.ndarray:
+    """`count` token ids uniformly spaced along the 3-D Hilbert order of the grid; with
+    count = N // 64 the middle token of every Hilbert block of 64."""
+    return _midpoints(_grid_tuple(grid_shape), int(count))
+
+
+def _schedule(hierarchy: ReblockHierarchy) -> np.ndarray:
+    words = [len(hierarchy.split_budgets)]
+    for level in hierarchy.split_budgets:
+        words.append(len(level))
+        for leaves, budgets in level:
+            words += [int(leaves), len(budgets), *map(int, budgets)]
+    return np.asarray(words, dtype=np.int32)
+
+
+class ReblockPlan:
+    """Node tables of one (tokens, fanout schedule, grid, root order), prepared once and
+    reused for every call of that shape; scratch is kept per row count."""
+
+    def __init__(self, tokens: int, children=16, *, grid_shape=None, fanout_mode: str = "power_of_two_fanout",
+                 final_fanout=None, root_fanout=None, initial_order: str = "flat", device=None):
+        if tokens < BLOCK:
+            raise ValueError("landmark-tree-v2 requires at least 64 non-empty rows")
+        grid = _grid_tuple(grid_shape) if grid_shape is not None else (1, 1, tokens)
+        if math.prod(grid) != tokens:
+            raise ValueError("grid_shape product must equal the token count")
+        self.tokens = tokens
+        self.grid = grid
+        self.device = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+        self.hierarchy = build_reblock_hierarchy(tokens, children, grid_shape=grid, fanout_mode=fanout_mode,
+                                                 final_fanout=final_fanout, root_fanout=root_fanout)
+        schedule = _schedule(self.hierarchy)
+        length = _lib.load().sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens, None, 0)
+        _lib.check(int(length), "sb_reblock_plan")
+        self.plan_host = np.zeros(int(length), dtype=np.int32)
+        _lib.check(int(_lib.load().sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens,
+                                                   self.plan_host.ctypes.data, int(length))), "sb_reblock_plan")
+        self.plan_device = torch.from_numpy(self.plan_host).to(self.device)
+        order = initial_token_indices(grid, initial_order)
+        self.initial_order = initial_order
+        self.root = None if initial_order == "flat" else torch.from_numpy(order.astype(np.int32)).to(self.device)
+        self.num_excluded = tokens % BLOCK
+        self.active_tokens = tokens - self.num_excluded
+        self._workspace: dict[int, torch.Tensor] = {}
+
+    def workspace(self, rows: int) -> torch.Tensor:
+        ws = self._workspace.get(rows)
+        if ws is None:
+            nbytes = int(_lib.load().sb_reblock_workspace_bytes(self.plan_host.ctypes.data, rows))
+            _lib.check(nbytes, "sb_reblock_workspace_bytes")
+            ws = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+            self._workspace[rows] = ws
+        return ws
+
+    def run(self, features: torch.Tensor, perm: torch.Tensor | None = None, inverse: torch.Tensor | None = None):
+        """features [rows, tokens, 128] bf16 (CUDA) -> (permutation, inverse) int32 [rows, tokens]."""
+        if features.dim() != 3 or features.shape[1] != self.tokens:
+            raise ValueError(f"features must be [rows, {self.tokens}, D]")
+        if features.dtype != torch.bfloat16:
+            raise RuntimeError("the CUDA landmark tree takes bf16 features")
+        device = _require_cuda(features)
+        rows, tokens, dim = features.shape
+        if perm is None:
+            perm = torch.empty((rows, tokens), dtype=torch.int32, device=device)
+        if inverse is None:
+            inverse = torch.empty((rows, tokens), dtype=torch.int32, device=device)
+        ws = self.workspace(rows)
+        with torch.cuda.device(device):
+            _lib.call("sb_reblock_tree", features.data_ptr(), rows, tokens, dim,
+                      None if self.root is None else self.root.data_ptr(), self.plan_host.ctypes.data,
+                      self.plan_device.data_ptr(), ws.data_ptr(), ws.numel(), perm.data_ptr(), inverse.data_ptr(),
+                      _stream(device))
+        return perm, inverse
+
+
+@dataclass(frozen=True)
+class LandmarkTreeV2Result:
+    block_indices: torch.Tensor
+    excluded_indices: torch.Tensor
+    permutation: torch.Tensor
+    inverse_permutation: torch.Tensor
+    active_tokens: int
+    num_excluded: int
+    hierarchy: ReblockHierarchy
+
+
+_PLANS: dict[tuple, ReblockPlan] = {}
+
+
+def _plan(tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device) -> ReblockPlan:
+    key = (tokens, children if isinstance(children, int) else tuple(children), grid, fanout_mode, final_fanout,
+           root_fanout, initial_order, str(device))
+    plan = _PLANS.get(key)
+    if plan is None:
+        plan = ReblockPlan(tokens, children, grid_shape=grid, fanout_mode=fanout_mode, final_fanout=final_fanout,
+                           root_fanout=root_fanout, initial_order=initial_order, device=device)
+        _PLANS[key] = plan
+    return plan
+
+
+_DEFAULTS = dict(distance="cosine", order_mode="parent_order", group_size=1, fitting_samples=None,
+                 landmark_mode="midpoint", landmark_count=32, midpoint_direction_mode="legacy", aggregation="linear",
+                 proxy_iterations=2, seed_rule="farthest_pair", update_rule="mean", excluded_indices=None)
+
+
+def spark_reblock(samples: torch.Tensor, *, grid_shape, initial_order: str = "flat", validate: bool = True,
+                  max_children=16, fanout_mode: str = "power_of_two_fanout", fanout=None, final_fanout=None,
+                  root_fanout=None, **options) -> LandmarkTreeV2Result:
+    """Strict 64-token leaves of bf16 samples [..., N, 128] (landmark_tree_v2.py:835-901).
+
+    Implements the production defaults (cosine distance, single tokens, 32 midpoint
+    landmarks, linear aggregation, parent order, two mean-update proxy iterations from the
+    farthest pair, power-of-two fanout); other options raise NotImplementedError."""
+    for name, value in options.items():
+        if name not in _DEFAULTS:
+            raise TypeError(f"spark_reblock() got an unexpected keyword argument {name!r}")
+        default = _DEFAULTS[name]
+        if (value is not default) and value != default:
+            raise NotImplementedError(f"the B200 landmark tree implements {name}={default!r} only")
+    if fanout_mode != "power_of_two_fanout":
+        raise NotImplementedError("the B200 landmark tree implements fanout_mode='power_of_two_fanout' only")
+    if samples.ndim < 2 or not samples.is_floating_point():
+        raise ValueError("samples must be floating point with layout [...,N,D]")
+    leading = samples.shape[:-2]
+    tokens, dim = samples.shape[-2:]
+    if tokens < BLOCK or dim <= 0:
+        raise ValueError("landmark-tree-v2 requires at least 64 non-empty rows")
+    if samples.is_cuda and samples.dtype not in (torch.float16, torch.bfloat16):
+        raise ValueError("CUDA landmark-tree-v2 requires FP16 or BF16 input")
+    if dim != 128:
+        raise NotImplementedError("the B200 landmark tree takes 128-dimensional features")
+    children = fanout if fanout is not None else max_children
+    flat = samples.reshape(-1, tokens, dim).to(torch.bfloat16).contiguous()
+    plan = _plan(tokens, children, _grid_tuple(grid_shape), fanout_mode, final_fanout, root_fanout, initial_order,
+                 flat.device)
+    perm, inverse = plan.run(flat)
+    perm64, inv64 = perm.long(), inverse.long()
+    active = plan.active_tokens
+    return LandmarkTreeV2Result(
+        block_indices=perm64[:, :active].reshape(*leading, active // BLOCK, BLOCK),
+        excluded_indices=perm64[:, active:].reshape(*leading, plan.num_excluded),
+        permutation=perm64.reshape(*leading, tokens),
+        inverse_permutation=inv64.reshape(*leading, tokens),
+        active_tokens=active, num_excluded=plan.num_excluded, hierarchy=plan.hierarchy)
+
+
+def metric_factors(q: torch.Tensor, k: torch.Tensor, samples: torch.Tensor, ridge: float = 1e-3) -> torch.Tensor:
+    """Cholesky factors [2*B*H, 128, 128] fp32: rows [0, BH) from the sampled Q moments
+    (applied to K), rows [BH, 2BH) from the sampled K moments (applied to Q)."""
+    device = _require_cuda(q, k, samples)
+    B, T, H, D = q.shape
+    factors = torch.empty((2 * B * H, D, D), dtype=torch.float32, device=device)
+    with torch.cuda.device(device):
+        _lib.call("sb_reblock_metric", q.data_ptr(), k.data_ptr(), _dtype_code(q), B, T, H, D, samples.data_ptr(),
+                  samples.numel(), float(ridge), factors.data_ptr(), _stream(device))
+    return factors
+
+
+def transform(q: torch.Tensor, k: torch.Tensor, factors: torch.Tensor, video_tokens: int) -> torch.Tensor:
+    """Reblock features [2*B*H, video, 128] bf16 = [K . bf16(Lq) ; Q . bf16(Lk)]."""
+    device = _require_cuda(q, k, factors)
+    if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
+        raise RuntimeError("the reblock transform takes bf16 Q/K")
+    B, T, H, D = q.shape
+    features = torch.empty((2 * B * H, video_tokens, D), dtype=torch.bfloat16, device=device)
+    with torch.cuda.device(device):
+        _lib.call("sb_reblock_transform", q.data_ptr(), k.data_ptr(), B, T, H, D, video_tokens, factors.data_ptr(),
+                  features.data_ptr(), _stream(device))
+    return features
+
+
+_SAMPLES: dict[tuple, torch.Tensor] = {}
+
+
+def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, grid, *, children=16,
+                          fanout_mode: str = "power_of_two_fanout", final_fanout=None, root_fanout=None,
+                          ridge: float = 1e-3, initial_order: str = "flat"):
+    """Paired opposite-second-moment Q/K permutations (spark_integration.py:394-851 with
+    layout reuse "independent"): returns (q_perm, q_inv, k_perm, k_inv), int32 [B, H, video],
+    plus the reblock hierarchy."""
+    device = _require_cuda(q, k)
+    B, T, H, D = q.shape
+    grid = _grid_tuple(grid)
+    key = (grid, video_tokens // BLOCK, str(device))
+    samples = _SAMPLES.get(key)
+    if samples is None:
+        ids = hilbert_midpoint_sample_indices(grid, video_tokens // BLOCK)
+        samples = torch.from_numpy(ids.astype(np.int32)).to(device)
+        _SAMPLES[key] = samples
+    factors = metric_factors(q, k, samples, ridge)
+    features = transform(q, k, factors, video_tokens)
+    plan = _plan(video_tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device)
+    perm, inverse = plan.run(features)
+    BH = B * H
+    shape = (B, H, video_tokens)
+    return (perm[BH:].view(shape), inverse[BH:].view(shape), perm[:BH].view(shape), inverse[:BH].view(shape),
+            plan.hierarchy)

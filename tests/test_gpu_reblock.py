@@ -1,0 +1,146 @@
+"""Reblock on the B200 against the oracle: the landmark tree bit-exact on the same bf16
+features (and through the oracle, against the reference's own permutations), the metric
+factors and features within fp32 / bf16 rounding, and the full-mode Spark layer."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import oracle
+from spark_h3_b200 import ops, reblock
+from spark_h3_b200.hierarchy import build_reblock_hierarchy
+from spark_h3_b200.synthetic import make_qkv
+
+pytestmark = pytest.mark.gpu
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def bits(t: torch.Tensor) -> np.ndarray:
+    return t.detach().cpu().contiguous().view(torch.int16).numpy().view(np.uint16)
+
+
+def tree_on_gpu(x, grid, children=16, order="flat"):
+    result = reblock.spark_reblock(x, grid_shape=grid, max_children=children, initial_order=order)
+    return result.permutation.cpu().numpy().reshape(-1, x.shape[-2]), \
+        result.inverse_permutation.cpu().numpy().reshape(-1, x.shape[-2])
+
+
+@pytest.mark.parametrize("name,tokens,dim,children,grid,order,seed", [
+    ("remainder", 4133, 128, 16, (1, 1, 4133), "flat", 0),
+    ("grid8k", 8192, 128, 16, (2, 64, 64), "flat", 1),
+    ("tiny", 130, 128, 16, (1, 2, 65), "flat", 3),
+    ("two_rounds", 20000, 128, 16, (5, 40, 100), "flat", 4),
+    ("fanout8", 6016, 128, 8, (4, 32, 47), "tile_t4h4w4", 5),
+])
+def test_tree_matches_reference_fixtures(cuda_device, name, tokens, dim, children, grid, order, seed):
+    z = np.load(GOLDEN / "reblock_tree.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, dim, generator=g).to(torch.bfloat16)
+    perm, inverse = tree_on_gpu(x.to(cuda_device), grid, children, order)
+    assert np.array_equal(perm, z[f"{name}_perm"])
+    assert np.array_equal(np.take_along_axis(inverse, perm, 1), np.broadcast_to(np.arange(tokens), perm.shape))
+
+
+@pytest.mark.parametrize("grid,children,order,rows", [((1, 1, 64), 16, "flat", 1), ((1, 2, 64), 2, "flat", 3),
+                                                      ((3, 21, 65), 4, "hilbert_hwt", 2), ((1, 96, 128), 32, "flat", 2),
+                                                      ((2, 64, 64), 64, "flat", 1)])
+def test_tree_matches_oracle(cuda_device, grid, children, order, rows):
+    tokens = grid[0] * grid[1] * grid[2]
+    g = torch.Generator().manual_seed(tokens + children)
+    x = torch.randn(rows, tokens, 128, generator=g).to(torch.bfloat16)
+    perm, _ = tree_on_gpu(x.to(cuda_device), grid, children, order)
+    h = build_reblock_hierarchy(tokens, children)
+    ref, _ = oracle.reblock_tree(bits(x), grid, h.split_budgets, order)
+    assert np.array_equal(perm, ref)
+
+
+def test_tree_duplicate_features_tie_break(cuda_device):
+    """Repeated rows give exactly equal scores: ties resolve to the lower token id."""
+    g = torch.Generator().manual_seed(3)
+    base = torch.randn(1, 16, 128, generator=g)
+    x = base.repeat(1, 256, 1)[:, :4096].to(torch.bfloat16)
+    perm, _ = tree_on_gpu(x.to(cuda_device), (1, 1, 4096))
+    ref, _ = oracle.reblock_tree(bits(x), (1, 1, 4096), build_reblock_hierarchy(4096, 16).split_budgets)
+    assert np.array_equal(perm, ref)
+
+
+def test_tree_clustered_config2_rows(cuda_device):
+    """Config-2 sized rows (N = 245,952, clustered content): two feature rows, bit-exact."""
+    grid = (61, 48, 84)
+    q, k, _ = make_qkv(grid, 1, 128, seed=11, dtype=torch.bfloat16, clustered=True, device=cuda_device)
+    x = torch.cat([k[0].transpose(0, 1), q[0].transpose(0, 1)]).contiguous()
+    perm, _ = tree_on_gpu(x, grid)
+    ref, _ = oracle.reblock_tree(bits(x), grid, build_reblock_hierarchy(245952, 16).split_budgets)
+    assert np.array_equal(perm, ref)
+
+
+def test_metric_and_transform(cuda_device):
+    grid, H = (2, 16, 40), 2
+    q, k, _ = make_qkv(grid, H, 128, seed=7, dtype=torch.bfloat16, clustered=True, device=cuda_device)
+    T = q.shape[1]
+    samples_np = reblock.hilbert_midpoint_sample_indices(grid, T // 64)
+    samples = torch.from_numpy(samples_np.astype(np.int32)).to(cuda_device)
+    factors = reblock.metric_factors(q, k, samples)
+    tq, tk = oracle.Tensor(bits(q), "bfloat16"), oracle.Tensor(bits(k), "bfloat16")
+    ref = oracle.metric_factors(tq, tk, samples_np, T)
+    got = factors.cpu().numpy()
+    assert np.abs(got - ref).max() <= 1e-4 * np.abs(ref).max()
+    assert (np.triu(got[0], 1) == 0).all()
+    features = reblock.transform(q, k, factors, T)
+    ref_f = oracle.bf16_bits_to_f32(oracle.reblock_features(tq, tk, got.astype(np.float64), T))
+    got_f = oracle.bf16_bits_to_f32(bits(features))
+    assert np.abs(got_f - ref_f).max() <= 2 ** -7 * np.abs(ref_f).max()
+    assert (got_f == ref_f).mean() > 0.99
+
+
+def test_qk_permutations(cuda_device):
+    """GPU features -> GPU tree equals the oracle tree on those features, and agrees with the
+    reference's permutations of the same Q/K (whose features differ in last-bit roundings)."""
+    z = np.load(GOLDEN / "reblock_qk.npz")
+    grid = tuple(int(g) for g in z["grid"])
+    H = int(z["heads"])
+    q, k, _ = make_qkv(grid, H, 128, seed=7, dtype=torch.bfloat16, clustered=True)
+    q, k = q.to(cuda_device), k.to(cuda_device)
+    T = q.shape[1]
+    qp, qi, kp, ki, hierarchy = reblock.qk_block_permutations(q, k, T, grid)
+    samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype(np.int32)).to(cuda_device)
+    features = reblock.transform(q, k, reblock.metric_factors(q, k, samples), T)
+    ref, ref_inv = oracle.reblock_tree(bits(features), grid, hierarchy.split_budgets)
+    got = np.concatenate([kp.cpu().numpy().reshape(H, T), qp.cpu().numpy().reshape(H, T)])
+    got_inv = np.concatenate([ki.cpu().numpy().reshape(H, T), qi.cpu().numpy().reshape(H, T)])
+    assert np.array_equal(got, ref) and np.array_equal(got_inv, ref_inv)
+    reference = np.concatenate([z["k_perm"].reshape(H, T), z["q_perm"].reshape(H, T)])
+    assert (got == reference).mean() > 0.9
+
+
+def test_full_mode_layer(cuda_device):
+    """mode='full': the layer equals the oracle Spark layer evaluated on the permuted Q/K/V,
+    inverse-permuted, for the permutations the GPU chose (checked bit-exact above)."""
+    from spark_h3_b200.attention import spark_attention_bthd
+    from spark_h3_b200.config import H3SparseAttentionConfig
+    from spark_h3_b200.layout import PackedLayout
+    from spark_h3_b200.processor import _Controller
+
+    grid, H = (2, 16, 40), 2
+    q, k, v = make_qkv(grid, H, 128, seed=5, dtype=torch.bfloat16, q_scale=128 ** -0.5, clustered=True,
+                       device=cuda_device)
+    T = q.shape[1]
+    cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode="full", sol_route_topk_ratio=0.2)
+    controller = _Controller(cfg)
+    ids = torch.arange(T)
+    layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=grid, video_tokens=T, sequence_length=T,
+                          video_positions=torch.zeros(T, 3, dtype=torch.long))
+    out = spark_attention_bthd(controller, q, k, v, layout, 0)
+    qp, qi, kp, _, _ = reblock.qk_block_permutations(q, k, T, grid)
+    q2, k2, v2 = (ops.headwise_permute(t, p, T) for t, p in ((q, qp), (k, kp), (v, kp)))
+    res = oracle.spark_layer(*(oracle.Tensor(bits(t), "bfloat16") for t in (q2, k2, v2)), block=64,
+                             topk_ratio=0.2)
+    ref = torch.from_numpy(res["out"]).to(cuda_device)
+    expected = ops.headwise_permute(ref.to(torch.float32).contiguous(), qi, T)
+    diff = (out.float() - expected).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(out.float().flatten(), expected.flatten(), dim=0).item()
+    assert diff <= 2e-2 and cos >= 0.9995
+    assert controller.counts["sol_landmark_preprocess_calls"] == 1

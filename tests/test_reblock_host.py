@@ -1,0 +1,81 @@
+"""Host logic of the reblock path: root orders and Hilbert metric samples against the
+reference fixtures, and the node tables the C-ABI plan builder derives from the hierarchy
+(no GPU needed: sb_reblock_plan is host code)."""
+from __future__ import annotations
+
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+from oracle import oracle
+from spark_h3_b200 import reblock
+from spark_h3_b200.hierarchy import build_reblock_hierarchy
+
+GOLDEN = Path(__file__).resolve().parent / "golden"
+
+
+def test_hilbert_samples_match_reference():
+    z = np.load(GOLDEN / "reblock_qk.npz")
+    grid = tuple(int(g) for g in z["grid"])
+    assert np.array_equal(reblock.hilbert_midpoint_sample_indices(grid, int(np.prod(grid)) // 64), z["samples"])
+    assert np.array_equal(reblock.hilbert_midpoint_sample_indices((61, 48, 84), 245952 // 64), z["samples_big"])
+
+
+@pytest.mark.parametrize("order", reblock.INITIAL_ORDERS)
+def test_initial_orders(order):
+    grid = (3, 20, 50)
+    ids = reblock.initial_token_indices(grid, order)
+    assert np.array_equal(np.sort(ids), np.arange(3000))
+    assert np.array_equal(ids, oracle.initial_order(grid, order))
+
+
+def test_unknown_initial_order_rejected():
+    with pytest.raises(ValueError, match="initial_order"):
+        reblock.initial_token_indices((1, 1, 64), "spiral")
+
+
+@pytest.mark.parametrize("tokens,children", [(245952, 16), (4133, 16), (6016, 8), (3000, 4), (130, 16), (64, 16)])
+def test_plan_node_tables(tokens, children):
+    from spark_h3_b200 import _lib
+
+    h = build_reblock_hierarchy(tokens, children)
+    schedule = reblock._schedule(h)
+    lib = _lib.load()
+    n = lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens, None, 0)
+    assert n > 0
+    plan = np.zeros(n, dtype=np.int32)
+    assert lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens, plan.ctypes.data, n) == n
+    levels, N, active = plan[0], plan[1], plan[2]
+    assert N == tokens and active == tokens - tokens % 64
+    covered_leaves = 0
+    for l in range(levels):
+        count, node_off, tile_off, P, S = plan[8 + 8 * l: 8 + 8 * l + 5]
+        assert P >= 2 and (P & (P - 1)) == 0 and S == P - 1
+        tiles = plan[tile_off: tile_off + active // 64]
+        for j in range(count):
+            start, size, C = plan[node_off + 68 * j: node_off + 68 * j + 3]
+            caps = plan[node_off + 68 * j + 4: node_off + 68 * j + 4 + C]
+            assert size == caps.sum() and (caps % 64 == 0).all() and C <= P
+            assert (tiles[start // 64:(start + size) // 64] == j).all()
+            covered_leaves += int((caps == 64).sum())
+    assert covered_leaves == (active // 64 if active // 64 > 1 else 0)
+    assert lib.sb_reblock_workspace_bytes(plan.ctypes.data, 4) > 0
+
+
+def test_plan_rejects_short_schedule():
+    from spark_h3_b200 import _lib
+
+    h = build_reblock_hierarchy(4096, 16)
+    schedule = reblock._schedule(h)[:3]
+    assert _lib.load().sb_reblock_plan(schedule.ctypes.data, len(schedule), 4096, None, 0) < 0
+
+
+def test_spark_reblock_rejects_unimplemented_options():
+    import torch
+
+    x = torch.zeros(1, 128, 128, dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError, match="distance"):
+        reblock.spark_reblock(x, grid_shape=(1, 1, 128), distance="euclidean")
+    with pytest.raises(TypeError):
+        reblock.spark_reblock(x, grid_shape=(1, 1, 128), colour="blue")
