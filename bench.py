@@ -6,6 +6,14 @@ reblock.  One step = pool Q -> anchor -> pool K + summaries -> block scores + To
 sparse attention (the 64-row partial tail attends densely inside the same kernel).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                  [--workload config1|config2|fp8]
+
+`--workload config2` times the same layer in the reference's default "full" mode at the
+config-2 size (grid 61x48x84, N = 245,952, 64-token blocks, clustered content): reblock
+(metric factors, features, landmark tree, head-wise permutes) + the sparse layer + the
+inverse permute.  `--workload fp8` times the config-3 e4m3 linears (M = 124,992 tokens,
+K = 4096, N in {12288, 4096, 16384}).  Both print one JSON line each; the default run is
+config 1 only.
 
 With N > 1 (torchrun, one process per GPU) the 32 heads are split across ranks (strong
 scaling, no data-path collective); timing is the max over ranks.  `value` is the
@@ -349,6 +357,151 @@ def run_ours(args) -> None:
         dist.destroy_process_group()
 
 
+def _timed(fn, steps: int, warmup: int, stream) -> float:
+    """Mean CUDA-event milliseconds of fn() over `steps` calls after `warmup` calls."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(steps):
+        fn()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) / steps
+
+
+def run_config2(args) -> None:
+    """the full Spark mode (landmark-v2 reblock + Top-K + reweight) at
+    N = 245,952 on one GPU."""
+    import torch
+
+    from spark_h3_b200 import ops, reblock
+    from spark_h3_b200.attention import spark_attention_bthd
+    from spark_h3_b200.config import H3SparseAttentionConfig
+    from spark_h3_b200.layout import PackedLayout
+    from spark_h3_b200.processor import _Controller
+    from spark_h3_b200.synthetic import make_qkv
+
+    if args.gpus != 1:
+        raise SystemExit("--workload config2 runs on one GPU")
+    grid, heads, block = (61, 48, 84), 32, 64
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    q, k, v = make_qkv(grid, heads, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, clustered=True)
+    T = q.shape[1]
+    cfg = H3SparseAttentionConfig.spark(num_inference_steps=1000, mode="full", sol_route_topk_ratio=TOPK_RATIO)
+    controller = _Controller(cfg)
+    ids = torch.arange(T)
+    layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=grid, video_tokens=T, sequence_length=T,
+                          video_positions=torch.zeros(T, 3, dtype=torch.long))
+    stream = torch.cuda.current_stream(dev)
+    layer = lambda: spark_attention_bthd(controller, q, k, v, layout, 0)
+    with ClockSampler(0) as clocks:
+        ms = _timed(layer, args.steps, args.warmup, stream)
+    # stage breakdown (same inputs, same stream)
+    samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype("int32")).to(dev)
+    factors = reblock.metric_factors(q, k, samples)
+    features = reblock.transform(q, k, factors, T)
+    plan = reblock._plan(T, 16, grid, "power_of_two_fanout", None, None, "flat", dev)
+    metric_ms = _timed(lambda: reblock.metric_factors(q, k, samples), 3, 1, stream)
+    transform_ms = _timed(lambda: reblock.transform(q, k, factors, T), 3, 1, stream)
+    tree_ms = _timed(lambda: plan.run(features), 3, 1, stream)
+    qp, qi, kp, ki, _ = reblock.qk_block_permutations(q, k, T, grid)
+    permute_ms = _timed(lambda: [ops.headwise_permute(t, p, T) for t, p in ((q, qp), (k, kp), (v, kp))], 3, 1,
+                        stream)
+    status = ops.read_device_status(dev)
+    peaks = load_peaks()
+    rows = 2 * heads
+    transform_bytes = rows * T * HEAD_DIM * 2 * 2  # read Q or K rows, write the features
+    nb = T // block
+    topk = ops.target_topk(TOPK_RATIO, nb)
+    line = dict(
+        metric=METRIC + " [config 2: full mode with reblock]", value=dense_flops(T, heads, HEAD_DIM) / (ms * 1e-3) / 1e12,
+        unit=UNIT, n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True,
+        scaling="strong", vs_baseline=None, dtype="bf16",
+        data="synthetic (seeded 8-sinusoid + clustered content: 64 N(0,1) centroids on a 4x4x4 region partition, "
+             "0.25 N(0,1) noise)",
+        config=dict(workload="config2: mode full (landmark-v2 reblock, Top-K 0.1, reweight), N=245952 (61x48x84), "
+                             "H=32, D=128, block 64", seq_len=T, heads=heads, block=block, topk=topk,
+                    l2="inputs (3 x 2.0 GB) exceed the 126 MB L2; no flush between steps"),
+        ms_per_layer=ms,
+        stages_ms=dict(reblock_metric=metric_ms, reblock_transform=transform_ms, reblock_tree=tree_ms,
+                       qkv_permutes=permute_ms),
+        roofline=dict(bound="hbm", kernel="reblock_transform_kernel", achieved=transform_bytes / (transform_ms * 1e-3) / 1e9,
+                      peak=peaks["hbm"], unit="GB/s",
+                      frac=transform_bytes / (transform_ms * 1e-3) / 1e9 / peaks["hbm"], traffic=None,
+                      peak_source=peaks["source"].replace("bf16 sustained", "HBM copy"),
+                      note="algorithmic bytes: 64 rows x N x 128 x 2 B read + the same written"),
+        clocks=clocks.summary(), device_status=status)
+    print(json.dumps(line), flush=True)
+
+
+def run_fp8(args) -> None:
+    """e4m3 linears with per-token x per-output-channel scales."""
+    import torch
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.fp8_linear import fp8_gemm, quantize_rows, quantize_weight
+
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    M, K = 124992, 4096
+    g = torch.Generator(device=dev).manual_seed(0)
+    x = (torch.randn(M, K, device=dev, generator=g)
+         * torch.empty(M, 1, device=dev).log_normal_(0.0, 0.5, generator=g)).to(torch.bfloat16)
+    peaks = load_peaks()
+    fp8_peak = 2 * peaks["bf16"]
+    shapes = {}
+    with ClockSampler(0) as clocks:
+        quant_ms = _timed(lambda: quantize_rows(x), args.steps, args.warmup, stream)
+        xq, xs = quantize_rows(x)
+        for N in (12288, 4096, 16384):
+            w = (torch.randn(N, K, device=dev, generator=g) * 0.02).to(torch.bfloat16)
+            wq, ws = quantize_weight(w)
+            out = torch.empty(M, N, device=dev, dtype=torch.bfloat16)
+            gemm_ms = _timed(lambda: fp8_gemm(xq, xs, wq, ws, out=out), args.steps, args.warmup, stream)
+            flops = 2.0 * M * N * K
+            entry = dict(gemm_ms=gemm_ms, tflops=flops / (gemm_ms * 1e-3) / 1e12)
+            try:
+                one = torch.ones(1, 1, device=dev)
+                lib_ms = _timed(lambda: torch._scaled_mm(xq, wq.t(), scale_a=one, scale_b=one,
+                                                         out_dtype=torch.bfloat16, use_fast_accum=True),
+                                args.steps, args.warmup, stream)
+                entry["cublas_scaled_mm_per_tensor_ms"] = lib_ms
+                row_ms = _timed(lambda: torch._scaled_mm(xq, wq.t(), scale_a=xs, scale_b=ws.reshape(1, -1),
+                                                         out_dtype=torch.bfloat16, use_fast_accum=True),
+                                args.steps, args.warmup, stream)
+                entry["torch_scaled_mm_rowwise_ms"] = row_ms
+            except RuntimeError as err:
+                entry["library"] = f"unavailable: {err}".splitlines()[0][:160]
+            entry["bf16_matmul_ms"] = _timed(lambda: x @ w.t(), 2, 1, stream)
+            shapes[f"{K}->{N}"] = entry
+            del w, wq, out
+    total_flops = sum(2.0 * M * int(key.split("->")[1]) * K for key in shapes)
+    total_ms = sum(e["gemm_ms"] for e in shapes.values()) + 3 * quant_ms
+    best = max(shapes.values(), key=lambda e: e["tflops"])
+    status = ops.read_device_status(dev)
+    line = dict(
+        metric="fp8_linear e4m3 TFLOP/s (config 3: M=124992, K=4096, N in {12288, 4096, 16384})",
+        value=total_flops / (total_ms * 1e-3) / 1e12, unit="TFLOP/s (2*M*N*K, quantisation included)",
+        n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=total_ms, higher_is_better=True,
+        scaling="strong", vs_baseline=None, dtype="e4m3 inputs, fp32 accumulate, bf16 out",
+        data="synthetic: X ~ N(0,1) x LogNormal(0,0.5) per token, W ~ N(0,0.02)",
+        config=dict(workload="config3: three e4m3 linears per step with one per-token quantisation each", M=M, K=K),
+        quantize_rows_ms=quant_ms,
+        quantize_rows_gbs=(M * K * 3) / (quant_ms * 1e-3) / 1e9,
+        shapes=shapes,
+        roofline=dict(bound="tensor", kernel="fp8_gemm_kernel", achieved=best["tflops"], peak=fp8_peak,
+                      unit="TFLOP/s", frac=best["tflops"] / fp8_peak, traffic=None,
+                      peak_source="2 x " + peaks["source"] + " (e4m3 issues at twice the bf16 rate)"),
+        clocks=clocks.summary(), device_status=status)
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -364,6 +517,8 @@ def main():
     ap.add_argument("--heads", type=int, default=None, help="head count for a smaller profiling case")
     ap.add_argument("--profile-only", action="store_true",
                     help="run only the device-resident steps (for ncu captures of a small case)")
+    ap.add_argument("--workload", choices=("config1", "config2", "fp8"), default="config1",
+                    help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3)")
     ap.add_argument("--reference-sample-blocks", type=int, default=16,
                     help="query blocks of the one-head CPU attention sample of each --impl reference step")
     args = ap.parse_args()
@@ -376,6 +531,10 @@ def main():
     PROFILE_ONLY = args.profile_only
     if args.impl == "reference":
         run_reference(args)
+    elif args.workload == "config2":
+        run_config2(args)
+    elif args.workload == "fp8":
+        run_fp8(args)
     else:
         run_ours(args)
 
