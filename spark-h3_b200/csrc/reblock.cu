@@ -423,74 +423,134 @@ struct TreeLevel {
   int count, P, S;
 };
 
-// One warp per (node, row): midpoint landmarks, binary proxy tree, directions in heap order.
+// One CTA of four warps per (node, row): midpoint landmarks, their unit vectors and pairwise
+// cosine distances (four threads per vector), then the binary proxy tree with the internal
+// nodes of one depth spread over the warps; directions are written in heap order.
+constexpr int kProxyThreads = 128;
+
 struct ProxySmem {
   __nv_bfloat16 x[kLandmarks][kDim];
   float n[kLandmarks][kDim];
   float dist[kLandmarks][kLandmarks + 1];
   int act[2][kLandmarks][kLandmarks];
+  int id[kLandmarks], w[kLandmarks];
 };
 
-__global__ void __launch_bounds__(32) reblock_proxy_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
-                                                           TreeLevel lv, const int32_t* __restrict__ idx_in,
-                                                           float* __restrict__ dirs) {
+// Canonical dot products with four threads per 128-vector: thread t4 of the group holds the
+// lane groups l = t4 + 4j (j = 0..7), so the butterfly's offsets 16, 8 and 4 pair lane groups
+// inside the thread (j ^ 4, j ^ 2, j ^ 1) and only offsets 2 and 1 cross threads.  The
+// summation tree is the one of the 32-lane form, term for term.
+__device__ __forceinline__ float tree8(const float* p) {
+  float a[4], b[2];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) a[j] = __fadd_rn(p[j], p[j + 4]);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) b[j] = __fadd_rn(a[j], a[j + 2]);
+  return __fadd_rn(b[0], b[1]);
+}
+
+__device__ __forceinline__ uint64_t tree8x2(const uint64_t* p) {
+  uint64_t a[4], b[2];
+#pragma unroll
+  for (int j = 0; j < 4; ++j) a[j] = f2_add(p[j], p[j + 4]);
+#pragma unroll
+  for (int j = 0; j < 2; ++j) b[j] = f2_add(a[j], a[j + 2]);
+  return f2_add(b[0], b[1]);
+}
+
+// Full canonical dot of two quarter-held vectors (all four threads get the result).
+__device__ __forceinline__ float quad_dot(const float (&a)[8][4], const float (&b)[8][4]) {
+  float p[8];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) p[j] = lane_dot4(a[j], b[j]);
+  float v = tree8(p);
+  v = __fadd_rn(v, __shfl_xor_sync(kFull, v, 2));
+  return __fadd_rn(v, __shfl_xor_sync(kFull, v, 1));
+}
+
+// unit(x) of a quarter-held vector, in place.
+__device__ __forceinline__ void quad_unit(float (&x)[8][4]) {
+  const float den = fmaxf(__fsqrt_rn(quad_dot(x, x)), 1e-12f);
+#pragma unroll
+  for (int j = 0; j < 8; ++j)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) x[j][e] = __fdiv_rn(x[j][e], den);
+}
+
+__global__ void __launch_bounds__(kProxyThreads) reblock_proxy_kernel(const __nv_bfloat16* __restrict__ F, int N,
+                                                                       int active, TreeLevel lv,
+                                                                       const int32_t* __restrict__ idx_in,
+                                                                       float* __restrict__ dirs) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   ProxySmem& S = *reinterpret_cast<ProxySmem*>(smem_raw);
-  const int node = blockIdx.x, r = blockIdx.y, lane = threadIdx.x;
+  const int node = blockIdx.x, r = blockIdx.y;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
   const int start = tbl[0], n = tbl[1], C = tbl[2];
   const int32_t* caps = tbl + 4;
   const int32_t* ids = idx_in + (int64_t)r * N + start;
   const __nv_bfloat16* Fr = F + (int64_t)r * N * kDim;
-  // midpoint landmarks and their interval weights
-  const int64_t lo = (int64_t)lane * n / kLandmarks, hi = (int64_t)(lane + 1) * n / kLandmarks;
-  const int my_id = ids[lo + (hi - lo) / 2];
-  const int my_w = (int)(hi - lo);
-  for (int i = 0; i < kLandmarks; ++i) {
-    const int id = __shfl_sync(kFull, my_id, i);
+  if (tid < kLandmarks) {  // midpoint of each of 32 equal intervals, weighted by its length
+    const int64_t lo = (int64_t)tid * n / kLandmarks, hi = (int64_t)(tid + 1) * n / kLandmarks;
+    S.id[tid] = ids[lo + (hi - lo) / 2];
+    S.w[tid] = (int)(hi - lo);
+  }
+  __syncthreads();
+  for (int i = warp; i < kLandmarks; i += 4)
     *reinterpret_cast<uint2*>(&S.x[i][4 * lane]) =
-        __ldg(reinterpret_cast<const uint2*>(Fr + (int64_t)id * kDim + 4 * lane));
+        __ldg(reinterpret_cast<const uint2*>(Fr + (int64_t)S.id[i] * kDim + 4 * lane));
+  __syncthreads();
+  const int g = tid >> 2, t4 = tid & 3;  // four threads per landmark vector
+  {
+    float u[8][4];
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) u[j][e] = __bfloat162float(S.x[g][4 * (t4 + 4 * j) + e]);
+    quad_unit(u);
+#pragma unroll
+    for (int j = 0; j < 8; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) S.n[g][4 * (t4 + 4 * j) + e] = u[j][e];
   }
-  __syncwarp();
-  for (int i = 0; i < kLandmarks; ++i) {
-    float x[4], u[4];
+  __syncthreads();
+  {
+    // rows a and 31 - a (31 pairs together); the two halves of the groups take alternate pairs
+    const int a = g & 15, b = 31 - a, half = g >> 4;
+    for (int t = half; t < 31; t += 2) {
+      const int i = t < 31 - a ? a : b;
+      const int k = t < 31 - a ? a + 1 + t : b + 1 + (t - (31 - a));
+      float ni[8][4], nk[8][4];
 #pragma unroll
-    for (int e = 0; e < 4; ++e) x[e] = __bfloat162float(S.x[i][4 * lane + e]);
-    unit4(x, u);
+      for (int j = 0; j < 8; ++j)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) S.n[i][4 * lane + e] = u[e];
-  }
-  __syncwarp();
-  for (int i = 0; i < kLandmarks; ++i) {
-    float a[4];
-#pragma unroll
-    for (int e = 0; e < 4; ++e) a[e] = S.n[i][4 * lane + e];
-    for (int k = i + 1; k < kLandmarks; ++k) {
-      float bb[4];
-#pragma unroll
-      for (int e = 0; e < 4; ++e) bb[e] = S.n[k][4 * lane + e];
-      const float d = __fsub_rn(1.0f, butterfly(lane_dot4(a, bb)));
-      if (lane == 0) S.dist[i][k] = d;
+        for (int e = 0; e < 4; ++e) {
+          ni[j][e] = S.n[i][4 * (t4 + 4 * j) + e];
+          nk[j][e] = S.n[k][4 * (t4 + 4 * j) + e];
+        }
+      const float d = __fsub_rn(1.0f, quad_dot(ni, nk));
+      if (t4 == 0) S.dist[i][k] = d;
     }
   }
-  S.act[0][0][lane] = my_w;
-  __syncwarp();
+  if (tid < kLandmarks) S.act[0][0][tid] = S.w[tid];
+  __syncthreads();
   float* out = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
   int cur = 0, depth_nodes = 1, first_heap = 0, span = C;
   while (span > 1) {
-    for (int j = 0; j < depth_nodes; ++j) {
+    for (int j = warp; j < depth_nodes; j += 4) {
       const int hnode = first_heap + j;
       const int s0 = j * span, mid = s0 + span / 2, s1 = s0 + span;
       int lc = 0, rc = 0;
       for (int c = s0; c < mid; ++c) lc += caps[c];
       for (int c = mid; c < s1; ++c) rc += caps[c];
-      const int a = S.act[cur][j][lane];
-      const unsigned vmask = __ballot_sync(kFull, a > 0);
+      const int aw = S.act[cur][j][lane];
+      const unsigned vmask = __ballot_sync(kFull, aw > 0);
       int first = vmask ? __ffs(vmask) - 1 : 0, second = first;
       if (__popc(vmask) >= 2) {
+        // farthest valid pair, first in row-major (i, k) order
         float bv = 0.f;
         int bk = -1;
-        if (a > 0)
+        if (aw > 0)
           for (int k = lane + 1; k < kLandmarks; ++k)
             if ((vmask >> k) & 1u) {
               const float d = S.dist[lane][k];
@@ -537,11 +597,11 @@ __global__ void __launch_bounds__(32) reblock_proxy_kernel(const __nv_bfloat16* 
         }
         int before = 0;
         for (int jj = 0; jj < 32; ++jj) {
-          const int rj = __shfl_sync(kFull, rank, jj), aj = __shfl_sync(kFull, a, jj);
+          const int rj = __shfl_sync(kFull, rank, jj), aj = __shfl_sync(kFull, aw, jj);
           if (rj < rank) before += aj;
         }
-        lw = min(max(lc - before, 0), a);
-        rw = a - lw;
+        lw = min(max(lc - before, 0), aw);
+        rw = aw - lw;
         float accl[4] = {0.f, 0.f, 0.f, 0.f}, accr[4] = {0.f, 0.f, 0.f, 0.f};
         for (int jj = 0; jj < 32; ++jj) {
           const float wl = (float)__shfl_sync(kFull, lw, jj), wr = (float)__shfl_sync(kFull, rw, jj);
@@ -569,7 +629,7 @@ __global__ void __launch_bounds__(32) reblock_proxy_kernel(const __nv_bfloat16* 
         S.act[cur ^ 1][2 * j + 1][lane] = rw;
       }
     }
-    __syncwarp();
+    __syncthreads();
     cur ^= 1;
     first_heap += depth_nodes;
     depth_nodes *= 2;
@@ -577,55 +637,131 @@ __global__ void __launch_bounds__(32) reblock_proxy_kernel(const __nv_bfloat16* 
   }
 }
 
-// Split scores of every token of the splitting nodes: s[h] = dot(unit(x), dir_h).
+// Split scores of every token of the splitting nodes: s[h] = dot(unit(x), dir_h); four
+// threads per token, directions paired for packed f32x2 multiply-adds.  A CTA walks
+// kScoreTiles consecutive 64-token tiles (reloading the directions only when the node
+// changes) and fetches the next tile's feature rows while it scores the current one.
+constexpr int kScoreTiles = 8;
+
+template <int P>
+__device__ __forceinline__ void score_token(const uint2 (&raw)[8], const float2 (*sd)[kDim], int t4, int C,
+                                            float* out) {
+  float u[8][4];
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[j]);
+    const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+    u[j][0] = a.x, u[j][1] = a.y, u[j][2] = b.x, u[j][3] = b.y;
+  }
+  quad_unit(u);
+  float v[P];
+#pragma unroll
+  for (int q = 0; q < P / 2; ++q) {
+    uint64_t c[8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4* dp = reinterpret_cast<const float4*>(&sd[q][4 * (t4 + 4 * j)]);
+      const float4 d01 = dp[0], d23 = dp[1];  // (h0, h1) pairs of elements 0..3
+      uint64_t acc = f2_mul(f2_pack(u[j][0], u[j][0]), f2_pack(d01.x, d01.y));
+      acc = f2_fma(f2_pack(u[j][1], u[j][1]), f2_pack(d01.z, d01.w), acc);
+      acc = f2_fma(f2_pack(u[j][2], u[j][2]), f2_pack(d23.x, d23.y), acc);
+      c[j] = f2_fma(f2_pack(u[j][3], u[j][3]), f2_pack(d23.z, d23.w), acc);
+    }
+    f2_unpack(tree8x2(c), v[2 * q], v[2 * q + 1]);
+  }
+  // offsets 2 and 1: reduce-scatter of the P values over the four threads
+  int m = P;
+#pragma unroll
+  for (int o = 2; o >= 1; o >>= 1) {
+    if (m > 1) {
+      const int half = m / 2;
+      const bool upper = (t4 & o) != 0;
+#pragma unroll
+      for (int i = 0; i < P / 2; ++i) {
+        if (i < half) {
+          const float send = upper ? v[i] : v[half + i];
+          const float keep = upper ? v[half + i] : v[i];
+          v[i] = __fadd_rn(keep, __shfl_xor_sync(kFull, send, o));
+        }
+      }
+      m = half;
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(kFull, v[0], o));
+    }
+  }
+  if (P >= 4) {
+#pragma unroll
+    for (int i = 0; i < (P >= 4 ? P / 4 : 1); ++i) {
+      const int hh = t4 * (P / 4) + i;
+      if (hh < C - 1) out[hh] = v[i];
+    }
+  } else if ((t4 & 1) == 0 && (t4 >> 1) < C - 1) {
+    out[t4 >> 1] = v[0];
+  }
+}
+
 template <int P>
 __global__ void __launch_bounds__(256) reblock_score_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
                                                             TreeLevel lv, const int32_t* __restrict__ idx_in,
                                                             const float* __restrict__ dirs,
                                                             float* __restrict__ scores) {
-  __shared__ __align__(16) float sd[P][kDim];
-  const int tile = blockIdx.x, r = blockIdx.y;
-  const int node = lv.tiles[tile];
-  if (node < 0) return;
-  const int C = lv.nodes[(int64_t)node * kNodeInts + 2];
-  const float* nd = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
-  for (int e = threadIdx.x; e < P * kDim; e += blockDim.x) sd[e / kDim][e % kDim] = e / kDim < C - 1 ? nd[e] : 0.f;
+  static_assert(P >= 2 && (P & (P - 1)) == 0, "P is a power of two");
+  __shared__ __align__(16) float2 sd[P / 2][kDim];
+  __shared__ int s_node[kScoreTiles];
+  const int r = blockIdx.y;
+  const int tiles = active / 64;
+  const int tile0 = blockIdx.x * kScoreTiles;
+  const int ntiles = min(kScoreTiles, tiles - tile0);
+  if (threadIdx.x < kScoreTiles) s_node[threadIdx.x] = threadIdx.x < ntiles ? lv.tiles[tile0 + threadIdx.x] : -1;
   __syncthreads();
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int tk = threadIdx.x >> 2, t4 = threadIdx.x & 3;
   const __nv_bfloat16* Fr = F + (int64_t)r * N * kDim;
-  for (int i = 0; i < 8; ++i) {
-    const int pos = tile * 64 + warp * 8 + i;
-    const int id = idx_in[(int64_t)r * N + pos];
-    float x[4], u[4];
-    load_row4(Fr + (int64_t)id * kDim, lane, x);
-    unit4(x, u);
-    float v[P];
+  const int32_t* ir = idx_in + (int64_t)r * N;
+  auto fetch = [&](int tile, uint2 (&raw)[8]) {
+    const int id = ir[tile * 64 + tk];
+    const __nv_bfloat16* row = Fr + (int64_t)id * kDim;
 #pragma unroll
-    for (int hh = 0; hh < P; ++hh) {
-      const float4 d4 = *reinterpret_cast<const float4*>(&sd[hh][4 * lane]);
-      const float d[4] = {d4.x, d4.y, d4.z, d4.w};
-      v[hh] = lane_dot4(u, d);
-    }
-    reduce_scatter<P>(v, lane);
-    float* out = scores + ((int64_t)r * active + pos) * lv.S;
-    if (P >= 32) {
-#pragma unroll
-      for (int q = 0; q < (P >= 32 ? P / 32 : 1); ++q) {
-        const int hh = (P / 32) * lane + q;
-        if (hh < C - 1) out[hh] = v[q];
+    for (int j = 0; j < 8; ++j) raw[j] = __ldg(reinterpret_cast<const uint2*>(row + 4 * (t4 + 4 * j)));
+  };
+  int i = 0;
+  while (i < ntiles && s_node[i] < 0) ++i;
+  if (i == ntiles) return;
+  uint2 cur[8], nxt[8];
+  fetch(tile0 + i, cur);
+  int loaded = -1, C = 2;
+  while (i < ntiles) {
+    const int node = s_node[i];
+    int next = i + 1;
+    while (next < ntiles && s_node[next] < 0) ++next;
+    if (next < ntiles) fetch(tile0 + next, nxt);
+    if (node != loaded) {
+      __syncthreads();
+      C = lv.nodes[(int64_t)node * kNodeInts + 2];
+      const float* nd = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
+      for (int e = threadIdx.x; e < (P / 2) * kDim; e += blockDim.x) {
+        const int q = e / kDim, d = e % kDim;
+        sd[q][d] = make_float2(2 * q < C - 1 ? nd[(2 * q) * kDim + d] : 0.f,
+                               2 * q + 1 < C - 1 ? nd[(2 * q + 1) * kDim + d] : 0.f);
       }
-    } else {
-      constexpr int group = P < 32 ? 32 / P : 1;
-      const int hh = lane / group;
-      if (lane % group == 0 && hh < C - 1) out[hh] = v[0];
+      __syncthreads();
+      loaded = node;
     }
+    const int pos = (tile0 + i) * 64 + tk;
+    score_token<P>(cur, sd, t4, C, scores + ((int64_t)r * active + pos) * lv.S);
+#pragma unroll
+    for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+    i = next;
   }
 }
 
 // Exact-capacity routing of one node (per internal proxy node: the left capacity goes to the
-// smallest (score, id) keys, found by radix select) and the stable partition into children.
+// smallest (score, id) keys) and the stable partition into the children.  Nodes of up to
+// 1024 tokens sort (proxy node, score key, id) in shared memory each depth; larger nodes find
+// the cut with a radix select over the score key (ids break equal keys).
 constexpr int kRouteThreads = 512;
 constexpr int kRouteWarps = kRouteThreads / 32;
+constexpr int kSortMax = 1024;
+constexpr int kUnroll = 4;
 
 __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int active, TreeLevel lv,
                                                                       const int32_t* __restrict__ idx_in,
@@ -635,13 +771,16 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
                                                                       int32_t* __restrict__ idx_out,
                                                                       int32_t* __restrict__ perm,
                                                                       int* __restrict__ status) {
-  __shared__ int hist[32][256];
-  __shared__ int target[32], ties[32], need_ids[32];
+  __shared__ __align__(16) uint8_t scratch[32 * 256 * 4];  // histograms, or the sort arrays
+  __shared__ int target[32], ties[32], need_ids[32], seg[32];
   __shared__ uint32_t prefix[32], id_prefix[32];
   __shared__ int any_ids;
   __shared__ int warp_cnt[kRouteWarps][kMaxChildren];
   __shared__ int warp_off[kRouteWarps][kMaxChildren];
   __shared__ int running[kMaxChildren], child_off[kMaxChildren];
+  int(*hist)[256] = reinterpret_cast<int(*)[256]>(scratch);
+  unsigned long long* sk = reinterpret_cast<unsigned long long*>(scratch);
+  int* sp = reinterpret_cast<int*>(scratch + kSortMax * 8);
   const int node = blockIdx.x, r = blockIdx.y;
   const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
   const int start = tbl[0], n = tbl[1], C = tbl[2];
@@ -651,6 +790,9 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
   uint32_t* key = keys + (int64_t)r * active + start;
   uint8_t* st = state + (int64_t)r * active + start;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const bool small = n <= kSortMax;
+  int n2 = 1;
+  while (n2 < n) n2 <<= 1;
   for (int t = tid; t < n; t += kRouteThreads) st[t] = 0;
   __syncthreads();
   int depth_nodes = 1, first_heap = 0, span = C;
@@ -658,69 +800,101 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
     const int nd = depth_nodes;
     if (tid < nd) {
       const int s0 = tid * span, mid = s0 + span / 2;
-      int lc = 0;
+      int lc = 0, before = 0;
       for (int c = s0; c < mid; ++c) lc += caps[c];
+      for (int c = 0; c < s0; ++c) before += caps[c];
       target[tid] = lc;
+      seg[tid] = before;
       prefix[tid] = 0;
       id_prefix[tid] = 0;
     }
-    for (int t = tid; t < n; t += kRouteThreads) key[t] = order_key(sc[(int64_t)t * lv.S + st[t]]);
-    __syncthreads();
-    // radix select on the score key, most significant byte first
-    for (int pass = 0; pass < 4; ++pass) {
-      const int shift = 24 - 8 * pass;
-      for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
-      __syncthreads();
-      for (int t = tid; t < n; t += kRouteThreads) {
-        const int j = st[t] - first_heap;
-        const uint32_t kk = key[t];
-        if (pass == 0 || (kk >> (shift + 8)) == (prefix[j] >> (shift + 8))) atomicAdd(&hist[j][(kk >> shift) & 255], 1);
+    if (small) {
+      for (int e = tid; e < n2; e += kRouteThreads) {
+        unsigned long long k64 = ~0ull;
+        if (e < n) {
+          const int h = st[e];
+          const uint32_t kk = order_key(sc[(int64_t)e * lv.S + h]);
+          k64 = ((unsigned long long)(h - first_heap) << 57) | ((unsigned long long)kk << 25) |
+                (unsigned long long)(uint32_t)ids[e];
+        }
+        sk[e] = k64;
+        sp[e] = e;
       }
       __syncthreads();
-      if (tid < nd) {
-        int cum = 0, want = target[tid];
-        for (int bin = 0; bin < 256; ++bin) {
-          const int c = hist[tid][bin];
-          if (cum + c >= want) {
-            prefix[tid] |= (uint32_t)bin << shift;
-            target[tid] = want - cum;
-            ties[tid] = c;
-            break;
+      for (int k = 2; k <= n2; k <<= 1)
+        for (int j = k >> 1; j > 0; j >>= 1) {
+          for (int i = tid; i < n2; i += kRouteThreads) {
+            const int ixj = i ^ j;
+            if (ixj > i) {
+              const unsigned long long a = sk[i], b = sk[ixj];
+              if ((a > b) == ((i & k) == 0)) {
+                sk[i] = b;
+                sk[ixj] = a;
+                const int pa = sp[i];
+                sp[i] = sp[ixj];
+                sp[ixj] = pa;
+              }
+            }
           }
-          cum += c;
+          __syncthreads();
+        }
+      for (int e = tid; e < n; e += kRouteThreads) {
+        const int j = (int)(sk[e] >> 57);
+        const int hnode = first_heap + j;
+        st[sp[e]] = (uint8_t)(e - seg[j] < target[j] ? 2 * hnode + 1 : 2 * hnode + 2);
+      }
+      __syncthreads();
+    } else {
+      for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+        int hs[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = t0 + u * kRouteThreads;
+          hs[u] = t < n ? st[t] : 0;
+        }
+        float vs[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = t0 + u * kRouteThreads;
+          vs[u] = t < n ? sc[(int64_t)t * lv.S + hs[u]] : 0.f;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = t0 + u * kRouteThreads;
+          if (t < n) key[t] = order_key(vs[u]);
         }
       }
       __syncthreads();
-    }
-    if (tid == 0) {
-      int any = 0;
-      for (int j = 0; j < nd; ++j) {
-        need_ids[j] = target[j] < ties[j] ? 1 : 0;
-        any |= need_ids[j];
-      }
-      any_ids = any;
-    }
-    __syncthreads();
-    if (any_ids) {
-      // equal scores at the cut: the lowest token ids among them go left
+      // radix select on the score key, most significant byte first
       for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
         for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
         __syncthreads();
-        for (int t = tid; t < n; t += kRouteThreads) {
-          const int j = st[t] - first_heap;
-          if (!need_ids[j] || key[t] != prefix[j]) continue;
-          const uint32_t id = (uint32_t)ids[t];
-          if (pass == 0 || (id >> (shift + 8)) == (id_prefix[j] >> (shift + 8))) atomicAdd(&hist[j][(id >> shift) & 255], 1);
+        for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+          uint32_t ks[kUnroll];
+          int js[kUnroll];
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int t = t0 + u * kRouteThreads;
+            js[u] = t < n ? st[t] - first_heap : -1;
+            ks[u] = t < n ? key[t] : 0u;
+          }
+#pragma unroll
+          for (int u = 0; u < kUnroll; ++u) {
+            const int j = js[u];
+            if (j >= 0 && (pass == 0 || (ks[u] >> (shift + 8)) == (prefix[j] >> (shift + 8))))
+              atomicAdd(&hist[j][(ks[u] >> shift) & 255], 1);
+          }
         }
         __syncthreads();
-        if (tid < nd && need_ids[tid]) {
+        if (tid < nd) {
           int cum = 0, want = target[tid];
           for (int bin = 0; bin < 256; ++bin) {
             const int c = hist[tid][bin];
             if (cum + c >= want) {
-              id_prefix[tid] |= (uint32_t)bin << shift;
+              prefix[tid] |= (uint32_t)bin << shift;
               target[tid] = want - cum;
+              ties[tid] = c;
               break;
             }
             cum += c;
@@ -728,14 +902,65 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
         }
         __syncthreads();
       }
+      if (tid == 0) {
+        int any = 0;
+        for (int j = 0; j < nd; ++j) {
+          need_ids[j] = target[j] < ties[j] ? 1 : 0;
+          any |= need_ids[j];
+        }
+        any_ids = any;
+      }
+      __syncthreads();
+      if (any_ids) {
+        // equal scores at the cut: the lowest token ids among them go left
+        for (int pass = 0; pass < 4; ++pass) {
+          const int shift = 24 - 8 * pass;
+          for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+          __syncthreads();
+          for (int t = tid; t < n; t += kRouteThreads) {
+            const int j = st[t] - first_heap;
+            if (!need_ids[j] || key[t] != prefix[j]) continue;
+            const uint32_t id = (uint32_t)ids[t];
+            if (pass == 0 || (id >> (shift + 8)) == (id_prefix[j] >> (shift + 8)))
+              atomicAdd(&hist[j][(id >> shift) & 255], 1);
+          }
+          __syncthreads();
+          if (tid < nd && need_ids[tid]) {
+            int cum = 0, want = target[tid];
+            for (int bin = 0; bin < 256; ++bin) {
+              const int c = hist[tid][bin];
+              if (cum + c >= want) {
+                id_prefix[tid] |= (uint32_t)bin << shift;
+                target[tid] = want - cum;
+                break;
+              }
+              cum += c;
+            }
+          }
+          __syncthreads();
+        }
+      }
+      for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+        int hs[kUnroll];
+        uint32_t ks[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = t0 + u * kRouteThreads;
+          hs[u] = t < n ? st[t] : 0;
+          ks[u] = t < n ? key[t] : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = t0 + u * kRouteThreads;
+          if (t >= n) continue;
+          const int j = hs[u] - first_heap;
+          const bool left = ks[u] < prefix[j] ||
+                            (ks[u] == prefix[j] && (!need_ids[j] || (uint32_t)ids[t] <= id_prefix[j]));
+          st[t] = (uint8_t)(left ? 2 * hs[u] + 1 : 2 * hs[u] + 2);
+        }
+      }
+      __syncthreads();
     }
-    for (int t = tid; t < n; t += kRouteThreads) {
-      const int hnode = st[t], j = hnode - first_heap;
-      const uint32_t kk = key[t];
-      const bool left = kk < prefix[j] || (kk == prefix[j] && (!need_ids[j] || (uint32_t)ids[t] <= id_prefix[j]));
-      st[t] = (uint8_t)(left ? 2 * hnode + 1 : 2 * hnode + 2);
-    }
-    __syncthreads();
     first_heap += depth_nodes;
     depth_nodes *= 2;
     span /= 2;
@@ -758,6 +983,7 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
     const int t = c0 + tid;
     const bool valid = t < n;
     const int label = valid ? st[t] - label_base : -1;
+    const int id = valid ? ids[t] : 0;
     const unsigned peers = __match_any_sync(kFull, label);
     const int rank = __popc(peers & lt);
     if (valid && rank == 0) warp_cnt[warp][label] = __popc(peers);
@@ -773,7 +999,7 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
     __syncthreads();
     if (valid) {
       const int dst = child_off[label] + warp_off[warp][label] + rank;
-      (caps[label] == 64 ? out_leaf : out_next)[dst] = ids[t];
+      (caps[label] == 64 ? out_leaf : out_next)[dst] = id;
     }
   }
   __syncthreads();
@@ -1044,6 +1270,7 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   SB_CHECK_ARG(rows > 0 && rows < 65536, "sb_reblock_tree: rows must lie in [1, 65535]");
   SB_CHECK_ARG(plan_host[1] == tokens, "sb_reblock_tree: the plan was built for %d tokens, not %d", plan_host[1],
                tokens);
+  SB_CHECK_ARG(tokens < (1 << 25), "sb_reblock_tree: at most 2^25 - 1 tokens per row");
   SB_CHECK_ARG(((uintptr_t)features % 16) == 0 && ((uintptr_t)workspace % 256) == 0,
                "sb_reblock_tree: features must be 16-byte and the workspace 256-byte aligned");
   const WorkspaceLayout W = workspace_layout(plan_host, rows);
@@ -1071,9 +1298,9 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   for (int l = 0; l < L; ++l) {
     const int32_t* lh = plan_host + kPlanHeader + kLevelInts * l;
     TreeLevel lv{plan_device + lh[1], plan_device + lh[2], lh[0], lh[3], lh[4]};
-    reblock_proxy_kernel<<<dim3(lv.count, rows), 32, proxy_smem, s>>>(F, tokens, active, lv, idx[cur], dirs);
+    reblock_proxy_kernel<<<dim3(lv.count, rows), kProxyThreads, proxy_smem, s>>>(F, tokens, active, lv, idx[cur], dirs);
     SB_CHECK_LAUNCH("sb_reblock_tree: proxy");
-    const dim3 sgrid(active / 64, rows);
+    const dim3 sgrid(ceil_div(active / 64, kScoreTiles), rows);
     switch (lv.P) {
       case 2: reblock_score_kernel<2><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       case 4: reblock_score_kernel<4><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
