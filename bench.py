@@ -387,7 +387,8 @@ def run_config2(args) -> None:
 
     if args.gpus != 1:
         raise SystemExit("--workload config2 runs on one GPU")
-    grid, heads, block = (61, 48, 84), 32, 64
+    grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else (61, 48, 84)
+    heads, block = args.heads or 32, 64
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     q, k, v = make_qkv(grid, heads, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, clustered=True)
@@ -401,6 +402,10 @@ def run_config2(args) -> None:
     layer = lambda: spark_attention_bthd(controller, q, k, v, layout, 0)
     with ClockSampler(0) as clocks:
         ms = _timed(layer, args.steps, args.warmup, stream)
+    if args.profile_only:
+        print(json.dumps(dict(profile_case=True, workload="config2", grid=grid, heads=heads, ms_per_step=ms)),
+              flush=True)
+        return
     # stage breakdown (same inputs, same stream)
     samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype("int32")).to(dev)
     factors = reblock.metric_factors(q, k, samples)
@@ -449,7 +454,7 @@ def run_fp8(args) -> None:
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     stream = torch.cuda.current_stream(dev)
-    M, K = 124992, 4096
+    M, K = args.fp8_rows, 4096
     g = torch.Generator(device=dev).manual_seed(0)
     x = (torch.randn(M, K, device=dev, generator=g)
          * torch.empty(M, 1, device=dev).log_normal_(0.0, 0.5, generator=g)).to(torch.bfloat16)
@@ -519,6 +524,7 @@ def main():
                     help="run only the device-resident steps (for ncu captures of a small case)")
     ap.add_argument("--workload", choices=("config1", "config2", "fp8"), default="config1",
                     help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3)")
+    ap.add_argument("--fp8-rows", type=int, default=124992, help="token rows M of the fp8 workload")
     ap.add_argument("--reference-sample-blocks", type=int, default=16,
                     help="query blocks of the one-head CPU attention sample of each --impl reference step")
     args = ap.parse_args()
