@@ -191,6 +191,7 @@ def run_ours(args) -> None:
     import torch.distributed as dist
 
     from spark_h3_b200 import ops
+    from spark_h3_b200.sharding import max_over_ranks, shard_heads
     from spark_h3_b200.synthetic import make_qkv
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -206,11 +207,10 @@ def run_ours(args) -> None:
     if HEADS % world:
         raise SystemExit("the head count must divide evenly across GPUs")
     heads = HEADS // world
-    h0 = rank * heads
 
     # Inputs: generated on the device (seeded), this rank's head shard made contiguous.
     q, k, v = make_qkv(GRID, HEADS, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
-    q, k, v = (x[:, :, h0:h0 + heads].contiguous() for x in (q, k, v))
+    q, k, v = (shard_heads(x, world, rank) for x in (q, k, v))
     torch.cuda.synchronize()
     T = q.shape[1]
     nb = math.ceil(T / BLOCK)
@@ -257,10 +257,7 @@ def run_ours(args) -> None:
         barrier()
     elapsed_ms = start.elapsed_time(stop)
     attn_ms = sum(a.elapsed_time(b) for a, b in attn_events) / len(attn_events)
-    t = torch.tensor([elapsed_ms, attn_ms], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    elapsed_ms, attn_ms = float(t[0]), float(t[1])
+    elapsed_ms, attn_ms = max_over_ranks([elapsed_ms, attn_ms], device=dev)
     ms_per_step = elapsed_ms / args.steps
     total_dense = dense_flops(T, HEADS, HEAD_DIM)
     value = total_dense / (ms_per_step * 1e-3) / 1e12
@@ -292,10 +289,7 @@ def run_ours(args) -> None:
         e2e_step()
     e_stop.record(stream)
     barrier()
-    t = torch.tensor([e_start.elapsed_time(e_stop) / e2e_steps], device=dev, dtype=torch.float64)
-    if world > 1:
-        dist.all_reduce(t, op=dist.ReduceOp.MAX)
-    e2e_ms = float(t[0])
+    (e2e_ms,) = max_over_ranks([e_start.elapsed_time(e_stop) / e2e_steps], device=dev)
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv)) * world
     d2h = hout.numel() * hout.element_size() * world
 

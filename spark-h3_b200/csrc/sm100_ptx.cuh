@@ -1,5 +1,5 @@
 // Thin inline-PTX wrappers for the sm_100a features the kernels use: mbarriers, TMA tile
-// loads (no multicast), tcgen05 MMA / TMEM load-store / allocation, and descriptors.
+// loads (single-CTA destinations only), tcgen05 MMA / TMEM load-store / allocation, and descriptors.
 #pragma once
 
 #include <cuda.h>
