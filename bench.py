@@ -203,6 +203,7 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     if HEADS % world:
         raise SystemExit("the head count must divide evenly across GPUs")

@@ -61,6 +61,14 @@ constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColOA = 256;
 constexpr uint32_t kColOB = 384;
 constexpr float kRescaleThreshold = 8.0f;  // log2 units: lazy O rescale
+// Every kPolyEvery-th pair of exponentials on the fast path runs on the FMA pipe (0: none).
+// Measured at config 1 (attention kernel): 0 -- all on the MUFU unit -- 30.6-30.9 ms,
+// 1 in 16 31.0, 1 in 8 31.8, 1 in 4 33.9, 1 in 2 38.2 ms: the softmax is short of issue
+// slots, not of MUFU throughput.
+#ifndef SB_POLY_EVERY
+#define SB_POLY_EVERY 0
+#endif
+constexpr int kPolyEvery = SB_POLY_EVERY;
 
 struct __align__(8) Control {
   uint64_t bar_q_full;
@@ -124,7 +132,7 @@ __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran,
 // x = j + f with f in [-0.5, 0.5], a degree-3 polynomial for 2^f (least-squares fit on
 // Chebyshev nodes, max relative error 2.2e-4, below bf16 rounding), and j added to the
 // exponent field.  Inputs below -126 give a value below 2^-125 (effectively zero).
-__device__ __forceinline__ float exp2_poly(float x) {
+[[maybe_unused]] __device__ __forceinline__ float exp2_poly(float x) {
   x = fmaxf(x, -126.f);
   const float shifter = 12582912.f;  // 1.5 * 2^23: rounds x to an integer in the mantissa
   const float t = x + shifter;
@@ -537,8 +545,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       uint64_t sums[2] = {0ull, 0ull};  // packed partial sums
       if (!exact || vis) {
         // p = 2^(s * scale - m) (fast path) or 2^(logit - m); pairs share one packed
-        // multiply-add.  On the fast path every 4th pair takes the polynomial exp2 on the
-        // FMA pipe, offloading the MUFU unit.
+        // multiply-add.  kPolyEvery > 0 moves a share of the fast path's exponentials to
+        // the polynomial on the FMA pipe.
         const uint64_t mul2 = fast ? f2_pack(scale_log2, scale_log2) : f2_pack(1.f, 1.f);
         const uint64_t neg2 = f2_pack(-base_m, -base_m);
 #pragma unroll
@@ -546,7 +554,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           const uint64_t a2 = f2_fma(f2_pack(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])), mul2, neg2);
           float a0, a1, p0, p1;
           f2_unpack(a2, a0, a1);
-          if (fast && (c & 3) == 3) {
+          if (kPolyEvery > 0 && fast && (c % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
             exp2_poly2(a0, a1, p0, p1);
           } else {
             p0 = ex2_approx(a0);

@@ -6,7 +6,9 @@ fallback for any entry point.
 from __future__ import annotations
 
 import ctypes
+import os
 import threading
+from pathlib import Path
 
 from . import _build
 
@@ -57,7 +59,12 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        path = _build.LIB_PATH
+        # SPARK_H3_B200_LIB points at another build of the same library (e.g. one compiled
+        # with different flags); by default the in-tree build is used.
+        override = os.environ.get("SPARK_H3_B200_LIB")
+        path = Path(override) if override else _build.LIB_PATH
+        if override and not path.exists():
+            raise RuntimeError(f"SPARK_H3_B200_LIB={override} does not exist")
         if not path.exists():
             if not build_if_missing:
                 raise RuntimeError(f"spark_h3_b200 native library is missing: {path}")
