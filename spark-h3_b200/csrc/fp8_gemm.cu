@@ -1,12 +1,12 @@
-// e4m3 linears on sm_100a: a per-row quantiser and a persistent tcgen05 GEMM
+// e4m3 linears on sm_100a: row / tensor quantisers and a persistent tcgen05 GEMM
 //   Y[m, n] = (sum_k A[m, k] * B[n, k]) * a_scale[m] * b_scale[n]  (+ bias[n]) -> bf16
-// with fp32 accumulation in TMEM (kind::f8f6f4, M = 128, N = 256, K = 32 per MMA).
+// with fp32 accumulation in TMEM (kind::f8f6f4, K = 32 per MMA).
 //
-// Roles (192 threads): warps 0-3 epilogue (thread r owns accumulator row r), warp 4 TMA
-// producer, warp 5 MMA issuer (owns the TMEM allocation).  Tiles are 128 x 256 outputs with
-// 128-byte K steps through a 4-stage ring (48 KB per stage); two TMEM accumulators let the
-// epilogue of one tile overlap the main loop of the next.  Tiles are visited n-fastest, so
-// the CTAs running at one time share the same A rows while B stays resident in L2.
+// The GEMM runs on CTA pairs (clusters of two) with tcgen05.mma.cta_group::2: 256 x 256
+// output tiles, 256-byte K stages through a 3-stage ring (64 KB per CTA per stage), two
+// TMEM accumulators per CTA so the epilogue of one tile overlaps the main loop of the next.
+// Roles per CTA (192 threads): warps 0-3 epilogue (thread r owns accumulator row r), warp 4
+// TMA producer, warp 5 MMA issuer (rank 0 only) and TMEM owner.
 #include <algorithm>
 
 #include "common.cuh"
@@ -17,45 +17,16 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kBM = 128, kBN = 256, kBK = 128;  // kBK in elements == bytes
-constexpr int kStages = 4;
-constexpr int kABytes = kBM * kBK;              // 16 KB
-constexpr int kBBytes = kBN * kBK;              // 32 KB
-constexpr int kStageBytes = kABytes + kBBytes;  // 48 KB
-constexpr int kGemmThreads = 192;
-constexpr uint32_t kAccCols = 256;
+constexpr int kBK = 128;          // TMA box inner extent: one 128-byte swizzle span of K
+constexpr int kGemmThreads = 192;  // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer
+constexpr int kGroupM = 16;        // tiles are visited in groups of 16 row-tiles, rows fastest
 
-struct __align__(8) GemmControl {
-  uint64_t full[kStages], empty[kStages];
-  uint64_t acc_full[2], acc_empty[2];
-  uint64_t mma_done;  // final commit of the MMA warp (drained before TMEM is freed)
-  uint32_t tmem_base;
-  int abort_flag;
-};
-
+// Instruction descriptor for kind::f8f6f4 with e4m3 A and B, fp32 accumulation, K-major.
 __host__ __device__ constexpr uint32_t idesc_e4m3_f32(int M, int N) {
   return (1u << 4)                     // D format: f32
          | (0u << 7) | (0u << 10)      // A, B format: e4m3
          | ((uint32_t)(N >> 3) << 17)  // K-major A and B
          | ((uint32_t)(M >> 4) << 24);
-}
-
-__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
-                                       uint32_t accumulate) {
-  asm volatile(
-      "{\n\t.reg .pred p;\n\t"
-      "setp.ne.b32 p, %4, 0;\n\t"
-      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
-      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
-      : "memory");
-}
-
-__device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap* map, uint32_t bar, int x, int y) {
-  asm volatile(
-      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
-      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-      : "memory");
 }
 
 struct GemmParams {
@@ -70,31 +41,125 @@ struct GemmParams {
   int m_tiles, n_tiles, k_steps;
 };
 
+// ------------------------------------------------------------------ CTA-pair GEMM
+// A cluster of two CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2: CTA rank r
+// holds A rows [128r, 128r + 128) and B rows [128r, 128r + 128) of the tile in its own shared
+// memory, the pair's MMA (issued by rank 0) reads both halves, and each CTA's TMEM receives
+// its 128 rows x 256 columns of the accumulator.  Per SM this halves the operand bytes that
+// shared memory serves per MMA, which bounds the single-CTA 128 x 256 tile.
+//   full[s]      rank 0 only: armed by rank 0 for both CTAs' bytes; both CTAs' TMA loads
+//                complete on it (cta_group::2 loads with rank 0's barrier address)
+//   empty[s]     both CTAs: the MMA's commit to each CTA releases the stage
+//   acc_full[b]  both CTAs: the MMA's commit after the last K step of a tile
+//   acc_empty[b] rank 0 only: one arrival per epilogue warp of both CTAs (8)
+//   mma_done     both CTAs: final commit, waited before TMEM is freed
+constexpr int kPairStages = 3;
+constexpr int kPairBK = 256;                          // K bytes per stage: two 128-byte swizzle spans
+constexpr int kPairSpanBytes = 128 * 128;             // 16 KB: 128 rows x 128 K bytes
+constexpr int kPairOpBytes = 2 * kPairSpanBytes;      // one operand's rows of a stage (32 KB)
+constexpr int kPairStageBytes = 2 * kPairOpBytes;     // A half + B half per CTA (64 KB)
+constexpr uint32_t kPairAccCols = 256;
+
+struct __align__(8) PairControl {
+  uint64_t full[kPairStages], empty[kPairStages];
+  uint64_t acc_full[2], acc_empty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort_flag;
+};
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+// Address of the same shared-memory object in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa_shared(uint32_t addr, uint32_t rank) {
+  uint32_t d;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(d) : "r"(addr), "r"(rank));
+  return d;
+}
+// Every thread of both CTAs; releases this CTA's prior shared-memory writes to the peer.
+__device__ __forceinline__ void cluster_sync_all() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void mbar_arrive_cluster(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+__device__ __forceinline__ void tma_load_2d_pair(uint32_t dst, const CUtensorMap* map, uint32_t bar_cluster, int x,
+                                                 int y) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes"
+      " [%0], [%1, {%2, %3}], [%4];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar_cluster)
+      : "memory");
+}
+__device__ __forceinline__ void mma_f8_pair(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                            uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f8f6f4 [%0], %1, %2, %3, {%5, %5, %5, %5, %5, %5, %5, %5}, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(0u)
+      : "memory");
+}
+__device__ __forceinline__ void tc_commit_pair(uint32_t bar_cluster) {
+  asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(bar_cluster)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_alloc_pair(uint32_t holder_smem, uint32_t ncols) {
+  asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(holder_smem), "r"(ncols)
+               : "memory");
+}
+__device__ __forceinline__ void tmem_relinquish_pair() {
+  asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
+}
+__device__ __forceinline__ void tmem_dealloc_pair(uint32_t taddr, uint32_t ncols) {
+  asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(taddr), "r"(ncols) : "memory");
+}
+
+// Grouped raster: groups of kGroupM row-tiles; inside a group rows move fastest, so the
+// pairs running at one time share a few B panels and a few A panels (both stay in L2).
+__device__ __forceinline__ void tile_coords(int64_t t, int m_tiles, int n_tiles, int& mt, int& nt) {
+  const int64_t per_group = (int64_t)kGroupM * n_tiles;
+  const int group = (int)(t / per_group);
+  const int first_m = group * kGroupM;
+  const int gm = min(kGroupM, m_tiles - first_m);
+  const int within = (int)(t - (int64_t)group * per_group);
+  mt = first_m + within % gm;
+  nt = within / gm;
+}
+
 __global__ void __launch_bounds__(kGemmThreads, 1)
-fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
+fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
-  if ((smem_u32(smem) & 1023u) != 0u) {
-    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 910);
-    return;
-  }
-  GemmControl& C = *reinterpret_cast<GemmControl*>(smem + kStages * kStageBytes);
+  // Same layout in both CTAs, so both take the same branch here.
+  const bool aligned = (smem_u32(smem) & 1023u) == 0u;
+  PairControl& C = *reinterpret_cast<PairControl*>(smem + kPairStages * kPairStageBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  if (threadIdx.x == 0) {
-    for (int s = 0; s < kStages; ++s) {
+  const uint32_t rank = cluster_ctarank();
+  const bool leader = rank == 0;
+  if (aligned && threadIdx.x == 0) {
+    for (int s = 0; s < kPairStages; ++s) {
       mbar_init(smem_u32(&C.full[s]), 1);
       mbar_init(smem_u32(&C.empty[s]), 1);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&C.acc_full[b]), 1);
-      mbar_init(smem_u32(&C.acc_empty[b]), 128);
+      mbar_init(smem_u32(&C.acc_empty[b]), 8);
     }
     mbar_init(smem_u32(&C.mma_done), 1);
     C.abort_flag = 0;
     fence_barrier_init();
   }
+  cluster_sync_all();  // every barrier of the pair exists before either CTA signals one
+  if (!aligned) {
+    if (threadIdx.x == 0 && p.status) atomicExch(p.status, 911);
+    return;
+  }
   if (warp == 5) {
-    tmem_alloc(smem_u32(&C.tmem_base), 2 * kAccCols);
-    tmem_relinquish();
+    tmem_alloc_pair(smem_u32(&C.tmem_base), 2 * kPairAccCols);
+    tmem_relinquish_pair();
   }
   if (warp == 4 && lane == 0) {
     prefetch_tensormap(&tm_a);
@@ -106,123 +171,150 @@ fp8_gemm_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant_
   const uint32_t tmem = C.tmem_base;
   volatile int* abort_flag = &C.abort_flag;
   const uint32_t base = smem_u32(smem);
-  const int64_t total_tiles = (int64_t)p.m_tiles * p.n_tiles;
+  const int64_t pair = blockIdx.x >> 1, pairs = gridDim.x >> 1;
+  const int64_t total_tiles = (int64_t)p.m_tiles * p.n_tiles;  // 256 x 256 tiles
 
   if (warp == 4) {
-    // ------------------------------------------------------------ producer
+    // ------------------------------------------------------------ producer (both CTAs)
     if (lane == 0) {
       int s = 0, use = 0;
-      int armed[kStages] = {};
+      int armed[kPairStages] = {};
       bool ok = true;
-      for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x) {
-        const int mt = (int)(t / p.n_tiles), nt = (int)(t % p.n_tiles);
+      for (int64_t t = pair; ok && t < total_tiles; t += pairs) {
+        int mt, nt;
+        tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
         for (int ks = 0; ks < p.k_steps; ++ks) {
-          if (!mbar_wait(smem_u32(&C.empty[s]), (uint32_t)((use & 1) ^ 1), abort_flag, p.status, 401)) {
+          if (!mbar_wait(smem_u32(&C.empty[s]), (uint32_t)((use & 1) ^ 1), abort_flag, p.status, 421)) {
             ok = false;
             break;
           }
-          const uint32_t bar = smem_u32(&C.full[s]);
-          mbar_arrive_expect_tx(bar, kStageBytes);
+          const uint32_t full_leader = mapa_shared(smem_u32(&C.full[s]), 0);
+          if (leader) mbar_arrive_expect_tx(smem_u32(&C.full[s]), 2 * kPairStageBytes);
           ++armed[s];
-          const uint32_t st = base + s * kStageBytes;
-          tma_load_2d(st, &tm_a, bar, ks * kBK, mt * kBM);
-          tma_load_2d(st + kABytes, &tm_b, bar, ks * kBK, nt * kBN);
-          if (++s == kStages) {
+          const uint32_t st = base + s * kPairStageBytes;
+#pragma unroll
+          for (int kh = 0; kh < 2; ++kh) {
+            tma_load_2d_pair(st + kh * kPairSpanBytes, &tm_a, full_leader, ks * kPairBK + kh * 128,
+                             mt * 256 + (int)rank * 128);
+            tma_load_2d_pair(st + kPairOpBytes + kh * kPairSpanBytes, &tm_b, full_leader, ks * kPairBK + kh * 128,
+                             nt * 256 + (int)rank * 128);
+          }
+          if (++s == kPairStages) {
             s = 0;
             ++use;
           }
         }
       }
-      for (int st = 0; st < kStages; ++st)
-        if (armed[st] > 0) mbar_drain(smem_u32(&C.full[st]), (uint32_t)((armed[st] - 1) & 1));
+      // rank 0's full barriers complete only once both CTAs' bytes have landed
+      if (leader)
+        for (int st = 0; st < kPairStages; ++st)
+          if (armed[st] > 0) mbar_drain(smem_u32(&C.full[st]), (uint32_t)((armed[st] - 1) & 1));
     }
   } else if (warp == 5) {
-    // ------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      constexpr uint32_t idesc = idesc_e4m3_f32(kBM, kBN);
+    // ------------------------------------------------------------ MMA issuer (rank 0)
+    if (lane == 0 && leader) {
+      constexpr uint32_t idesc = idesc_e4m3_f32(256, 256);
       const uint64_t adesc0 = smem_desc_sw128(base, 16, 1024);
       int s = 0, use = 0, local = 0;
       bool ok = true;
-      for (int64_t t = blockIdx.x; ok && t < total_tiles; t += gridDim.x, ++local) {
+      for (int64_t t = pair; ok && t < total_tiles; t += pairs, ++local) {
         const int buf = local & 1;
-        // The epilogue must have drained this accumulator (two tiles ago).
         if (local >= 2 && !mbar_wait(smem_u32(&C.acc_empty[buf]), (uint32_t)(((local - 2) >> 1) & 1), abort_flag,
-                                     p.status, 402)) {
+                                     p.status, 422)) {
           ok = false;
           break;
         }
         tc_fence_after();
-        const uint32_t acc = tmem + buf * kAccCols;
+        const uint32_t acc = tmem + buf * kPairAccCols;
         for (int ks = 0; ks < p.k_steps; ++ks) {
-          if (!mbar_wait(smem_u32(&C.full[s]), (uint32_t)(use & 1), abort_flag, p.status, 403)) {
+          if (!mbar_wait(smem_u32(&C.full[s]), (uint32_t)(use & 1), abort_flag, p.status, 423)) {
             ok = false;
             break;
           }
-          const uint64_t sa = adesc0 + (uint64_t)((s * kStageBytes) >> 4);
-          const uint64_t sb = sa + (uint64_t)(kABytes >> 4);
+          tc_fence_after();
+          const uint64_t sa = adesc0 + (uint64_t)((s * kPairStageBytes) >> 4);
+          const uint64_t sb = sa + (uint64_t)(kPairOpBytes >> 4);
 #pragma unroll
-          for (int kk = 0; kk < kBK / 32; ++kk)
-            mma_f8(acc, sa + (uint64_t)(kk * 2), sb + (uint64_t)(kk * 2), idesc, (ks > 0 || kk > 0) ? 1u : 0u);
-          tc_commit(smem_u32(&C.empty[s]));
-          if (++s == kStages) {
+          for (int kk = 0; kk < kPairBK / 32; ++kk) {
+            const uint64_t off = (uint64_t)(((kk >> 2) * kPairSpanBytes + (kk & 3) * 32) >> 4);
+            mma_f8_pair(acc, sa + off, sb + off, idesc, (ks > 0 || kk > 0) ? 1u : 0u);
+          }
+          const uint32_t e = smem_u32(&C.empty[s]);
+          tc_commit_pair(mapa_shared(e, 0));
+          tc_commit_pair(mapa_shared(e, 1));
+          if (++s == kPairStages) {
             s = 0;
             ++use;
           }
         }
-        tc_commit(smem_u32(&C.acc_full[buf]));
+        if (!ok) break;
+        const uint32_t f = smem_u32(&C.acc_full[buf]);
+        tc_commit_pair(mapa_shared(f, 0));
+        tc_commit_pair(mapa_shared(f, 1));
       }
-      tc_commit(smem_u32(&C.mma_done));  // covers every MMA this warp issued
+      const uint32_t d = smem_u32(&C.mma_done);  // covers every MMA of the pair
+      tc_commit_pair(mapa_shared(d, 0));
+      tc_commit_pair(mapa_shared(d, 1));
     }
   } else {
-    // ------------------------------------------------------------ epilogue
-    const int row = threadIdx.x;  // 0..127 = TMEM lane
+    // ------------------------------------------------------------ epilogue (both CTAs)
+    const int row = threadIdx.x;  // TMEM lane of this CTA: tile row 128 * rank + row
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
     int local = 0;
-    for (int64_t t = blockIdx.x; t < total_tiles; t += gridDim.x, ++local) {
+    for (int64_t t = pair; t < total_tiles; t += pairs, ++local) {
       const int buf = local & 1;
-      const bool got = mbar_wait(smem_u32(&C.acc_full[buf]), (uint32_t)((local >> 1) & 1), abort_flag, p.status, 404);
+      const bool got = mbar_wait(smem_u32(&C.acc_full[buf]), (uint32_t)((local >> 1) & 1), abort_flag, p.status, 424);
       if (!__all_sync(0xffffffffu, got)) break;
       tc_fence_after();
-      const int mt = (int)(t / p.n_tiles), nt = (int)(t % p.n_tiles);
-      const int64_t m = (int64_t)mt * kBM + row;
-      const int n0 = nt * kBN;
+      int mt, nt;
+        tile_coords(t, p.m_tiles, p.n_tiles, mt, nt);
+      const int64_t m = (int64_t)mt * 256 + rank * 128 + row;
+      const int n0 = nt * 256;
       const bool row_ok = m < p.M;
       const float sa = row_ok ? __ldg(p.a_scale + m * p.a_scale_stride) : 0.f;
       __nv_bfloat16* out_row = p.out + m * p.N;
 #pragma unroll 1
-      for (int c = 0; c < kBN / 32; ++c) {
+      for (int c = 0; c < 256 / 32; ++c) {
         uint32_t r[32];
-        tmem_ld32(tmem + lane_base + buf * kAccCols + 32 * c, r);
-        tmem_wait_ld();
+        tmem_ld32(tmem + lane_base + buf * kPairAccCols + 32 * c, r);
+        // this chunk's 32 column scales and biases: one load per lane, broadcast by shuffle
         const int nc = n0 + 32 * c;
-        if (row_ok && nc < p.N) {
-          float f[32];
+        const int nl = nc + lane;
+        const float sb_l = nl < p.N ? __ldg(p.b_scale + (int64_t)nl * p.b_scale_stride) : 0.f;
+        const float bias_l = (p.bias != nullptr && nl < p.N) ? __bfloat162float(p.bias[nl]) : 0.f;
+        tmem_wait_ld();
+        float f[32];
 #pragma unroll
-          for (int i = 0; i < 32; ++i) {
-            const int n = nc + i;
-            const float sb = n < p.N ? __ldg(p.b_scale + (int64_t)n * p.b_scale_stride) : 0.f;
-            float y = __uint_as_float(r[i]) * sa * sb;
-            if (p.bias != nullptr && n < p.N) y += __bfloat162float(p.bias[n]);
-            f[i] = y;
-          }
+        for (int i = 0; i < 32; ++i) {
+          const float y = __uint_as_float(r[i]) * sa * __shfl_sync(0xffffffffu, sb_l, i);
+          f[i] = y + __shfl_sync(0xffffffffu, bias_l, i);
+        }
+        if (row_ok && nc < p.N) {
           if (nc + 32 <= p.N && (p.N % 8) == 0) {
 #pragma unroll
             for (int v = 0; v < 4; ++v) store8(out_row + nc + 8 * v, f + 8 * v);
           } else {
-            for (int i = 0; i < 32 && nc + i < p.N; ++i) out_row[nc + i] = __float2bfloat16_rn(f[i]);
+#pragma unroll
+            for (int i = 0; i < 32; ++i)
+              if (nc + i < p.N) out_row[nc + i] = __float2bfloat16_rn(f[i]);
           }
         }
       }
       tc_fence_before();
-      mbar_arrive(smem_u32(&C.acc_empty[buf]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&C.acc_empty[buf]), 0));
     }
   }
   tc_fence_before();
   __syncthreads();
   if (warp == 5) {
     tc_fence_after();
-    mbar_drain(smem_u32(&C.mma_done), 0);
-    tmem_dealloc(tmem, 2 * kAccCols);
+    mbar_drain(smem_u32(&C.mma_done), 0);  // rank 0's MMAs write both CTAs' TMEM
+  }
+  cluster_sync_all();  // no signal to the peer's shared memory is still in flight
+  if (warp == 5) {
+    tc_fence_after();
+    tmem_dealloc_pair(tmem, 2 * kPairAccCols);
   }
 }
 
@@ -523,8 +615,8 @@ extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_s
   if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_fp8_gemm: status word");
   CUtensorMap ma, mb;
   int rc;
-  if ((rc = make_map_u8(&ma, a, (uint64_t)K, (uint64_t)M, kBM)) != SB_OK) return rc;
-  if ((rc = make_map_u8(&mb, b, (uint64_t)K, (uint64_t)N, kBN)) != SB_OK) return rc;
+  if ((rc = make_map_u8(&ma, a, (uint64_t)K, (uint64_t)M, 128)) != SB_OK) return rc;
+  if ((rc = make_map_u8(&mb, b, (uint64_t)K, (uint64_t)N, 128)) != SB_OK) return rc;
   GemmParams p{};
   p.a_scale = a_scale;
   p.b_scale = b_scale;
@@ -536,21 +628,34 @@ extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_s
   p.M = M;
   p.N = N;
   p.K = K;
-  p.m_tiles = (int)((M + kBM - 1) / kBM);
-  p.n_tiles = (N + kBN - 1) / kBN;
-  p.k_steps = (K + kBK - 1) / kBK;
-  const size_t smem = (size_t)kStages * kStageBytes + sizeof(GemmControl);
-  cudaError_t err = cudaFuncSetAttribute(fp8_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  p.m_tiles = (int)((M + 255) / 256);
+  p.n_tiles = (N + 255) / 256;
+  p.k_steps = (K + kPairBK - 1) / kPairBK;
+  const size_t smem = (size_t)kPairStages * kPairStageBytes + sizeof(PairControl);
+  cudaError_t err = cudaFuncSetAttribute(fp8_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: set smem");
-  int sms = num_ctas;
-  if (sms <= 0) {
+  int ctas = num_ctas;
+  if (ctas <= 0) {
     int dev = 0;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&ctas, cudaDevAttrMultiProcessorCount, dev);
   }
   const int64_t tiles = (int64_t)p.m_tiles * p.n_tiles;
-  const int grid = (int)std::min<int64_t>(tiles, sms);
-  fp8_gemm_kernel<<<grid, kGemmThreads, smem, (cudaStream_t)stream>>>(ma, mb, p);
+  const int pairs = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, ctas / 2));
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3(2 * pairs, 1, 1);
+  cfg.blockDim = dim3(kGemmThreads, 1, 1);
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = (cudaStream_t)stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeClusterDimension;
+  attr[0].val.clusterDim.x = 2;
+  attr[0].val.clusterDim.y = 1;
+  attr[0].val.clusterDim.z = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  err = cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel, ma, mb, p);
+  if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: cluster launch");
   SB_CHECK_LAUNCH("sb_fp8_gemm launch");
   return SB_OK;
 }
