@@ -204,6 +204,16 @@ int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, cons
                 void* out, int num_ctas, void* stream);
 
 /*
+ * Strided copy (rows of `width` bytes, `height` rows) between host and device memory in either
+ * direction, asynchronous on `stream`: moves one head chunk of a BTHD tensor between a pinned
+ * host tensor and a contiguous device buffer.  No counterpart in the reference (its layer
+ * takes device tensors); the streamed layer of the Python API uses it to overlap transfers
+ * with compute.
+ */
+int sb_memcpy2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width,
+                int64_t height, void* stream);
+
+/*
  * Reblock metric factors.  Replaces h3_sparse_attention/landmark_direction.py:60-104 with
  * mahalanobis_kmeans.py:309-388 (landmark_direction_factors / batched_cross_metric_factors,
  * raw moments, m2_side "both"): for every (batch, head) the non-centred second moment of the

@@ -47,6 +47,17 @@ using namespace sb;
 
 extern "C" int sb_version(void) { return 100; }
 
+extern "C" int sb_memcpy2d(void* dst, int64_t dpitch, const void* src, int64_t spitch, int64_t width, int64_t height,
+                           void* stream) {
+  SB_CHECK_ARG(dst && src, "sb_memcpy2d: null pointer");
+  SB_CHECK_ARG(width >= 0 && height >= 0 && dpitch >= width && spitch >= width, "sb_memcpy2d: bad extents");
+  if (width == 0 || height == 0) return SB_OK;
+  cudaError_t err = cudaMemcpy2DAsync(dst, (size_t)dpitch, src, (size_t)spitch, (size_t)width, (size_t)height,
+                                      cudaMemcpyDefault, (cudaStream_t)stream);
+  if (err != cudaSuccess) return cuda_error(err, "sb_memcpy2d");
+  return SB_OK;
+}
+
 extern "C" const char* sb_last_error(void) { return g_error; }
 
 extern "C" int sb_read_device_status(void* stream) {

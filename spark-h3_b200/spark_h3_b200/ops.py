@@ -195,3 +195,69 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
         return o, dict(qc=qc, kc=kc, anchor=anchor, ak=ak, av=av, lm=lm, packed=packed, indices=indices,
                        topk=topk, query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last)
     return o
+
+
+def spark_layer_streamed(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, out: torch.Tensor, *, chunks: int = 4,
+                         device: torch.device | None = None, **layer_args) -> torch.Tensor:
+    """spark_layer on pinned host BTHD tensors, streamed by head chunks.
+
+    Every stage of the layer is independent per (batch, head), so the heads are split into
+    `chunks` groups: while group c runs on the GPU, group c+1 is uploaded and group c-1's
+    output is downloaded (strided host<->device copies on two copy streams, double-buffered
+    device memory).  `out` is the pinned host output.  Results are identical to spark_layer
+    on the whole tensors.  The call returns with the last download queued on the current
+    stream (synchronise it, or an event on it, before reading `out`)."""
+    for name, t in (("q", q), ("k", k), ("v", v), ("out", out)):
+        if t.is_cuda or not t.is_pinned() or not t.is_contiguous():
+            raise RuntimeError(f"spark_layer_streamed takes contiguous pinned host tensors; {name} is not")
+    if q.shape != k.shape or q.shape != v.shape or out.shape != q.shape or len({t.dtype for t in (q, k, v, out)}) != 1:
+        raise ValueError("q, k, v and out must share one BTHD shape and dtype")
+    B, T, H, D = q.shape
+    if chunks < 1 or H % chunks:
+        raise ValueError(f"{H} heads do not split into {chunks} equal chunks")
+    device = device or torch.device("cuda", torch.cuda.current_device())
+    hc = H // chunks
+    es = q.element_size()
+    row, chunk_row = H * D * es, hc * D * es
+    main = torch.cuda.current_stream(device)
+    up, down = torch.cuda.Stream(device), torch.cuda.Stream(device)
+    dev_in = [[torch.empty((B, T, hc, D), device=device, dtype=q.dtype) for _ in range(3)] for _ in range(2)]
+    dev_out = [torch.empty((B, T, hc, D), device=device, dtype=q.dtype) for _ in range(2)]
+    block = layer_args.get("block", 128)
+    video = layer_args.get("video_tokens") or T
+    ws = layer_args.pop("workspace", None)
+    if ws is None:
+        ws = torch.empty(route_workspace_bytes(B, video // block, hc, video // block), device=device, dtype=torch.uint8)
+    computed = [None, None]
+    downloaded = [None, None]
+    with torch.cuda.device(device):
+        start = torch.cuda.Event()
+        start.record(main)
+        for c in range(chunks):
+            slot = c & 1
+            up.wait_event(start)
+            if computed[slot] is not None:  # the slot's inputs were consumed by chunk c-2
+                up.wait_event(computed[slot])
+            for src, dst in zip((q, k, v), dev_in[slot]):
+                _lib.call("sb_memcpy2d", dst.data_ptr(), chunk_row, src.data_ptr() + c * chunk_row, row, chunk_row,
+                          B * T, up.cuda_stream)
+            uploaded = torch.cuda.Event()
+            uploaded.record(up)
+            main.wait_event(uploaded)
+            if downloaded[slot] is not None:  # the slot's output was read back for chunk c-2
+                main.wait_event(downloaded[slot])
+            spark_layer(*dev_in[slot], out=dev_out[slot], workspace=ws, **layer_args)
+            computed[slot] = torch.cuda.Event()
+            computed[slot].record(main)
+            down.wait_event(computed[slot])
+            _lib.call("sb_memcpy2d", out.data_ptr() + c * chunk_row, row, dev_out[slot].data_ptr(), chunk_row,
+                      chunk_row, B * T, down.cuda_stream)
+            downloaded[slot] = torch.cuda.Event()
+            downloaded[slot].record(down)
+        for ev in downloaded:
+            if ev is not None:
+                main.wait_event(ev)
+    for t in dev_in[0] + dev_in[1] + dev_out:
+        t.record_stream(up)
+        t.record_stream(down)
+    return out
