@@ -6,7 +6,7 @@ reblock.  One step = pool Q -> anchor -> pool K + summaries -> block scores + To
 sparse attention (the 64-row partial tail attends densely inside the same kernel).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload config1|config2|fp8]
+                  [--workload config1|config2|fp8|config4]
 
 `--workload config2` times the same layer in the reference's default "full" mode at the
 config-2 size (grid 61x48x84, N = 245,952, 64-token blocks, clustered content): reblock
@@ -503,6 +503,85 @@ def run_fp8(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_config4(args) -> None:
+    """the synthetic DiT block stack (8 blocks, hidden 4096, 32 x 128 heads,
+    GELU FFN 16384, e4m3 linears) at N = 245,952 tokens; 19 denoise steps = 4 dense warmup +
+    15 Spark steps.  Tokens are split across ranks for the pointwise work and the GEMMs, heads
+    for attention (NCCL all-to-all).  The timed dense and sparse steps give s/it of the schedule."""
+    import torch
+    import torch.distributed as dist
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.dit import DiTConfig, DiTStack
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local_rank)
+    dev = torch.device("cuda", local_rank)
+    if world > 1:
+        from datetime import timedelta
+        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
+    grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else (61, 48, 84)
+    heads = args.heads or 32
+    cfg = DiTConfig(hidden=heads * 128, heads=heads, ffn=4 * heads * 128)
+    stack = DiTStack(cfg, grid, device=dev, world=world, rank=rank, seed=0, spark_mode=args.spark_mode,
+                     topk_ratio=TOPK_RATIO)
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(stack.local, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    def timed(dense: bool, n: int) -> float:
+        barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for i in range(n):
+            stack.step(x, 900.0 - 50.0 * i, dense=dense)
+        e1.record(stream)
+        barrier()
+        return e0.elapsed_time(e1) / n
+
+    stack.step(x, 999.0, dense=True)  # warm-up: one dense and W - 1 sparse evaluations
+    for i in range(max(1, args.warmup - 1)):
+        stack.step(x, 950.0 - i, dense=False)
+    with ClockSampler(local_rank) as clocks:
+        sparse_ms = timed(False, args.steps)
+        dense_ms = timed(True, 1)
+    from spark_h3_b200.sharding import max_over_ranks
+    sparse_ms, dense_ms = max_over_ranks([sparse_ms, dense_ms], device=dev)
+    status = ops.read_device_status(dev)
+    schedule_s = (4 * dense_ms + 15 * sparse_ms) / 19 / 1e3
+    if rank == 0:
+        T = grid[0] * grid[1] * grid[2]
+        a2a = 4 * T * cfg.heads * cfg.head_dim * 2  # q, k, v out and o back, bytes per layer (whole job)
+        line = dict(
+            metric="DiT step s/it (config 4: 8-block synthetic DiT, 19 steps = 4 dense + 15 Spark)",
+            value=schedule_s, unit="s/it", n_gpus=world, steps=args.steps, warmup=args.warmup,
+            ms_per_step=schedule_s * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None,
+            dtype="e4m3 linears, bf16 activations and attention",
+            data="synthetic: latent tokens N(0,1), weights N(0,0.02), seeded",
+            config=dict(workload=f"config4: {cfg.blocks} blocks, hidden {cfg.hidden}, {heads} heads x 128, FFN "
+                                 f"{cfg.ffn} GELU, N={T} ({'x'.join(map(str, grid))}), Spark mode "
+                                 f"{args.spark_mode} topk {TOPK_RATIO}",
+                        parallelism=(f"tokens/{world} for pointwise + GEMMs, heads/{world} for attention, NCCL "
+                                     "all-to-all" if world > 1 else "single GPU")),
+            sparse_step_ms=sparse_ms, dense_step_ms=dense_ms,
+            all_to_all_bytes_per_layer=a2a if world > 1 else 0,
+            clocks=clocks.summary(), device_status=status)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier(device_ids=[local_rank])
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
@@ -518,8 +597,10 @@ def main():
     ap.add_argument("--heads", type=int, default=None, help="head count for a smaller profiling case")
     ap.add_argument("--profile-only", action="store_true",
                     help="run only the device-resident steps (for ncu captures of a small case)")
-    ap.add_argument("--workload", choices=("config1", "config2", "fp8"), default="config1",
-                    help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3)")
+    ap.add_argument("--workload", choices=("config1", "config2", "fp8", "config4"), default="config1",
+                    help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3), "
+                         "config4 (DiT block stack, multi-GPU with torchrun)")
+    ap.add_argument("--spark-mode", default="full", help="Spark mode of the config-4 sparse steps")
     ap.add_argument("--fp8-rows", type=int, default=124992, help="token rows M of the fp8 workload")
     ap.add_argument("--reference-sample-blocks", type=int, default=16,
                     help="query blocks of the one-head CPU attention sample of each --impl reference step")
@@ -537,6 +618,8 @@ def main():
         run_config2(args)
     elif args.workload == "fp8":
         run_fp8(args)
+    elif args.workload == "config4":
+        run_config4(args)
     else:
         run_ours(args)
 

@@ -204,6 +204,54 @@ int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, cons
                 void* out, int num_ctas, void* stream);
 
 /*
+ * fp8 GEMM with a gated residual epilogue for the DiT block stack (which
+ * the build writes itself; no counterpart in the reference's attention path):
+ *   out[m, n] = residual[m, n] + gate[n] * (sum_k a[m, k] b[n, k] a_scale[m] b_scale[n] + bias[n])
+ * residual / out: [M, N] bf16 (they may be the same buffer); gate: [N] fp32.  Otherwise as
+ * sb_fp8_gemm.
+ */
+int sb_fp8_gemm_residual(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
+                         const float* b_scale, int b_scale_stride, int64_t M, int N, int K,
+                         const void* bias, const void* residual, const float* gate, void* out,
+                         int num_ctas, void* stream);
+
+/*
+ * GELU (erf form) fused with the e4m3 row quantiser: quantize_rows(gelu(x)) of an FFN up
+ * projection without writing the activation (config 4; the reference's SwiGLU counterpart is
+ * fp8_linear.py:128-138).  x: [M, K] (dtype), out: [M, K] bytes, scales: [M] fp32.
+ */
+int sb_fp8_gelu_quantize_rows(const void* x, int dtype, int64_t M, int K, uint8_t* out,
+                              float* scales, void* stream);
+
+/*
+ * e4m3 row quantiser over a matrix stored as K / seg consecutive [M, seg] bf16 blocks,
+ * `seg_stride` elements apart: the attention output as the head-to-sequence all-to-all
+ * returns it (one block of heads per peer), quantised for the output projection without a
+ * reordering copy.  out: [M, K] bytes (row-major), scales: [M] fp32.
+ */
+int sb_fp8_quantize_segments(const void* x, int64_t M, int K, int seg, int64_t seg_stride,
+                             uint8_t* out, float* scales, void* stream);
+
+/*
+ * DiT block pointwise stage (config 4): per row, y = x / rms(x) * (1 + scale) + shift (RMSNorm
+ * with eps, adaLN modulation), quantised to e4m3 with one scale per row for the next GEMM.
+ * x: [M, C] bf16, shift / scale: [C] fp32, out: [M, C] bytes, scales: [M] fp32.
+ */
+int sb_dit_norm_modulate_quantize(const void* x, const float* shift, const float* scale, int64_t M,
+                                  int C, float eps, uint8_t* out, float* scales, void* stream);
+
+/*
+ * DiT attention input stage (config 4): from the fused projection qkv [M, 3, H, 128] bf16,
+ * per-head RMSNorm of q and k (weights wq, wk [128]) and the 3-D rotary embedding (pair j of
+ * the head dimension rotates by coords[m, axis[j]] * inv_freq[j]; coords [M, 3] int32 holds
+ * each token's (t, h, w)), written as q, k, v [shards][M][H / shards][128] bf16: the send
+ * layout of the sequence-to-head all-to-all.
+ */
+int sb_dit_qkv_norm_rope(const void* qkv, const float* wq, const float* wk, const int32_t* coords,
+                         const float* inv_freq, const int8_t* axis, int64_t M, int H, int D,
+                         int shards, float eps, void* q, void* k, void* v, void* stream);
+
+/*
  * Strided copy (rows of `width` bytes, `height` rows) between host and device memory in either
  * direction, asynchronous on `stream`: moves one head chunk of a BTHD tensor between a pinned
  * host tensor and a contiguous device buffer.  No counterpart in the reference (its layer

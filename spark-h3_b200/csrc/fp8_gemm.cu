@@ -34,6 +34,8 @@ struct GemmParams {
   const float* b_scale;
   int a_scale_stride, b_scale_stride;  // 1: one scale per row / column, 0: one per tensor
   const __nv_bfloat16* bias;
+  const __nv_bfloat16* residual;  // optional: out = residual + gate[n] * (scaled product + bias)
+  const float* gate;              // [N], required with residual
   __nv_bfloat16* out;
   int* status;
   int64_t M;
@@ -282,12 +284,26 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
         const int nl = nc + lane;
         const float sb_l = nl < p.N ? __ldg(p.b_scale + (int64_t)nl * p.b_scale_stride) : 0.f;
         const float bias_l = (p.bias != nullptr && nl < p.N) ? __bfloat162float(p.bias[nl]) : 0.f;
+        const float gate_l = (p.residual != nullptr && nl < p.N) ? __ldg(p.gate + nl) : 0.f;
         tmem_wait_ld();
         float f[32];
 #pragma unroll
         for (int i = 0; i < 32; ++i) {
           const float y = __uint_as_float(r[i]) * sa * __shfl_sync(0xffffffffu, sb_l, i);
           f[i] = y + __shfl_sync(0xffffffffu, bias_l, i);
+        }
+        if (p.residual != nullptr) {
+          float res[32];
+          const __nv_bfloat16* res_row = p.residual + m * p.N;
+          if (row_ok && nc + 32 <= p.N && (p.N % 8) == 0) {
+#pragma unroll
+            for (int v = 0; v < 4; ++v) load8(res_row + nc + 8 * v, res + 8 * v);
+          } else {
+#pragma unroll
+            for (int i = 0; i < 32; ++i) res[i] = (row_ok && nc + i < p.N) ? __bfloat162float(res_row[nc + i]) : 0.f;
+          }
+#pragma unroll
+          for (int i = 0; i < 32; ++i) f[i] = fmaf(__shfl_sync(0xffffffffu, gate_l, i), f[i], res[i]);
         }
         if (row_ok && nc < p.N) {
           if (nc + 32 <= p.N && (p.N % 8) == 0) {
@@ -359,6 +375,37 @@ struct SwigluRows {
 // The eager spelling divides a tensor by the Python scalar 448, which torch evaluates as a
 // multiplication by the fp32 reciprocal; the scale is taken the same way.
 constexpr float kInv448 = 1.0f / 448.0f;
+
+// GELU(x) = x * Phi(x) (erf form) of one [M, K] row.
+template <typename T>
+struct GeluRows {
+  const T* x;
+  int K;
+  __device__ void load(int64_t row, int c, float* v) const {
+    const T* xr = x + row * K;
+    if (c + 8 <= K && (K % 8) == 0) {
+      load8(xr + c, v);
+    } else {
+      for (int i = 0; i < 8; ++i) v[i] = c + i < K ? Elem<T>::to_f(xr[c + i]) : 0.f;
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.5f * v[i] * (1.f + erff(v[i] * 0.70710678118654752f));
+  }
+};
+
+// Row m of a matrix stored as `segments` consecutive [M, seg] blocks (seg columns each,
+// seg_stride elements apart): the layout an all-to-all returns when every peer sends one
+// column block of every row.
+template <typename T>
+struct SegmentRows {
+  const T* x;
+  int seg;
+  int64_t seg_stride;
+  __device__ void load(int64_t row, int c, float* v) const {
+    const int s = c / seg, off = c - s * seg;  // seg is a multiple of 8: one segment per vector
+    load8(x + s * seg_stride + row * seg + off, v);
+  }
+};
 
 __device__ __forceinline__ void store_e4m3x8(uint8_t* yr, int c, int K, const float* v, float scale) {
   uint16_t packed[4];
@@ -560,6 +607,32 @@ extern "C" int sb_fp8_swiglu_quantize_rows(const void* h, int dtype, int64_t M, 
                      "sb_fp8_swiglu_quantize_rows launch");
 }
 
+extern "C" int sb_fp8_gelu_quantize_rows(const void* x, int dtype, int64_t M, int K, uint8_t* out, float* scales,
+                                         void* stream) {
+  SB_CHECK_ARG(x && out && scales, "sb_fp8_gelu_quantize_rows: null pointer");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_fp8_gelu_quantize_rows: bad dtype");
+  SB_CHECK_ARG(M > 0 && K > 0, "sb_fp8_gelu_quantize_rows: M and K must be positive");
+  SB_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)out % 8) == 0,
+               "sb_fp8_gelu_quantize_rows: x must be 16-byte and out 8-byte aligned");
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SB_BF16)
+    return launch_rows(GeluRows<__nv_bfloat16>{(const __nv_bfloat16*)x, K}, M, K, out, scales, s,
+                       "sb_fp8_gelu_quantize_rows launch");
+  return launch_rows(GeluRows<float>{(const float*)x, K}, M, K, out, scales, s, "sb_fp8_gelu_quantize_rows launch");
+}
+
+extern "C" int sb_fp8_quantize_segments(const void* x, int64_t M, int K, int seg, int64_t seg_stride, uint8_t* out,
+                                        float* scales, void* stream) {
+  SB_CHECK_ARG(x && out && scales, "sb_fp8_quantize_segments: null pointer");
+  SB_CHECK_ARG(M > 0 && K > 0 && seg > 0 && seg % 8 == 0 && K % seg == 0,
+               "sb_fp8_quantize_segments: K must be a whole number of segments of a multiple of 8 columns");
+  SB_CHECK_ARG(seg_stride >= M * (int64_t)seg, "sb_fp8_quantize_segments: segments overlap");
+  SB_CHECK_ARG(((uintptr_t)x % 16) == 0 && ((uintptr_t)out % 8) == 0,
+               "sb_fp8_quantize_segments: x must be 16-byte and out 8-byte aligned");
+  return launch_rows(SegmentRows<__nv_bfloat16>{(const __nv_bfloat16*)x, seg, seg_stride}, M, K, out, scales,
+                     (cudaStream_t)stream, "sb_fp8_quantize_segments launch");
+}
+
 extern "C" int sb_fp8_quantize_tensor(const void* x, int dtype, int64_t n, uint8_t* out, float* scale,
                                       float* workspace, void* stream) {
   SB_CHECK_ARG(x && out && scale && workspace, "sb_fp8_quantize_tensor: null pointer");
@@ -600,10 +673,13 @@ extern "C" int sb_fp8_swiglu(const void* h, int dtype, int64_t M, int K, void* a
   return SB_OK;
 }
 
-extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
-                           const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
-                           void* out, int num_ctas, void* stream) {
+namespace {
+int launch_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
+                    const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
+                    const void* residual, const float* gate, void* out, int num_ctas, void* stream) {
   SB_CHECK_ARG(a && a_scale && b && b_scale && out, "sb_fp8_gemm: null pointer");
+  SB_CHECK_ARG(residual == nullptr || (gate != nullptr && ((uintptr_t)residual % 16) == 0),
+               "sb_fp8_gemm: a residual needs a gate vector and 16-byte alignment");
   SB_CHECK_ARG(M > 0 && N > 0 && K > 0, "sb_fp8_gemm: M, N, K must be positive");
   SB_CHECK_ARG(K % 16 == 0, "sb_fp8_gemm: K must be a multiple of 16 (TMA row pitch), got %d", K);
   SB_CHECK_ARG(((uintptr_t)a % 16) == 0 && ((uintptr_t)b % 16) == 0 && ((uintptr_t)out % 16) == 0,
@@ -623,6 +699,8 @@ extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_s
   p.a_scale_stride = a_scale_stride;
   p.b_scale_stride = b_scale_stride;
   p.bias = static_cast<const __nv_bfloat16*>(bias);
+  p.residual = static_cast<const __nv_bfloat16*>(residual);
+  p.gate = gate;
   p.out = static_cast<__nv_bfloat16*>(out);
   p.status = status;
   p.M = M;
@@ -658,4 +736,20 @@ extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_s
   if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: cluster launch");
   SB_CHECK_LAUNCH("sb_fp8_gemm launch");
   return SB_OK;
+}
+}  // namespace
+
+extern "C" int sb_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
+                           const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
+                           void* out, int num_ctas, void* stream) {
+  return launch_fp8_gemm(a, a_scale, a_scale_stride, b, b_scale, b_scale_stride, M, N, K, bias, nullptr, nullptr, out,
+                         num_ctas, stream);
+}
+
+extern "C" int sb_fp8_gemm_residual(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
+                                    const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
+                                    const void* residual, const float* gate, void* out, int num_ctas, void* stream) {
+  SB_CHECK_ARG(residual != nullptr, "sb_fp8_gemm_residual: null residual");
+  return launch_fp8_gemm(a, a_scale, a_scale_stride, b, b_scale, b_scale_stride, M, N, K, bias, residual, gate, out,
+                         num_ctas, stream);
 }
