@@ -203,7 +203,7 @@ def run_ours(args) -> None:
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep stdout to the one JSON line
+        quiet_nccl()
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
     if HEADS % world:
         raise SystemExit("the head count must divide evenly across GPUs")
@@ -503,6 +503,12 @@ def run_fp8(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def quiet_nccl() -> None:
+    """Keep stdout to the one JSON line: NCCL's version banner and warnings go to stderr."""
+    os.environ.setdefault("NCCL_DEBUG", "WARN")
+    os.environ.setdefault("NCCL_DEBUG_FILE", "/dev/stderr")
+
+
 def run_config4(args) -> None:
     """the synthetic DiT block stack (8 blocks, hidden 4096, 32 x 128 heads,
     GELU FFN 16384, e4m3 linears) at N = 245,952 tokens; 19 denoise steps = 4 dense warmup +
@@ -523,7 +529,7 @@ def run_config4(args) -> None:
     dev = torch.device("cuda", local_rank)
     if world > 1:
         from datetime import timedelta
-        os.environ.setdefault("NCCL_DEBUG", "WARN")
+        quiet_nccl()
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else (61, 48, 84)
     heads = args.heads or 32

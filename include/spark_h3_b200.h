@@ -145,6 +145,16 @@ int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype,
                         int local_radius, void* out, float* lse, void* stream);
 
 /*
+ * Dense attention of query rows [row_lo, row_hi) over all T keys (softmax scale D^-1/2); the
+ * other rows of out / lse are not written.  Replaces the dense-suffix SDPA overwrite of
+ * h3_sparse_attention/spark_integration.py:1238-1260 for the rows a padded sparse prefix
+ * covered (sol_video_tail_mode = "pad": the context rows that filled the final video query
+ * block, spark_integration.py:1173-1187).  Shapes, dtype and alignment as sb_sparse_attention.
+ */
+int sb_dense_rows_attention(const void* q, const void* k, const void* v, int dtype, int B, int T, int H, int D,
+                            int row_lo, int row_hi, void* out, float* lse, void* stream);
+
+/*
  * Head-wise token permutation of the video prefix.  Replaces
  * spark_integration.py:308-362 (_headwise_permute_video_tokens) and
  * landmark_tree_v2_triton.py:19-90 (headwise_permute_bthd).

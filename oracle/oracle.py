@@ -268,22 +268,48 @@ def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.nda
 
 
 # ------------------------------------------------------------- full pipeline
+def padded_tail(q: Tensor, video: int, query_tokens: int, block: int) -> Tensor:
+    """Q with rows [video, query_tokens) replaced by the mean of the final partial video
+    block's rows, fp32 mean rounded to Q's dtype (spark_integration.py:1173-1187)."""
+    if query_tokens <= video:
+        return q
+    tail_start = (video // block) * block
+    mean = q.float()[:, tail_start:video].astype(np.float64).mean(axis=1, keepdims=True).astype(np.float32)
+    data = q.data.copy()
+    if q.dtype == "bfloat16":
+        data[:, video:query_tokens] = f32_to_bf16_bits(mean)
+    else:
+        data[:, video:query_tokens] = mean
+    return Tensor(data, q.dtype)
+
+
 def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: float, video_tokens: int | None = None,
                 anchor_dtype: str | None = None, local_radius: int = -1, weighted_kv: bool = True,
                 mass_bias: bool = True, attention: bool = True, rows: slice | None = None,
-                heads: list[int] | None = None) -> dict:
-    """Route, summaries and (optionally) attention of one Spark layer, as the CUDA path does."""
+                heads: list[int] | None = None, tail_mode: str = "dense") -> dict:
+    """Route, summaries and (optionally) attention of one Spark layer, as the CUDA path does.
+
+    tail_mode "pad" (spark_integration.py:72-91, 935-938, 1173-1187, 1238-1260): the query
+    prefix extends over the partial final video block, whose missing rows are filled with
+    the mean of its video rows for the route; every row from the video end on is dense."""
     B, T, H, D = q.shape
     video = T if video_tokens is None else video_tokens
     nb = -(-T // block)
-    query_tokens = (video // block) * block
+    if tail_mode == "dense":
+        query_tokens = (video // block) * block
+    elif tail_mode == "pad":
+        query_tokens = -(-video // block) * block
+        if query_tokens > T:
+            raise ValueError("the packed suffix is too short to pad the final video query block")
+    else:
+        raise ValueError("tail_mode must be 'dense' or 'pad'")
     query_blocks = query_tokens // block
     candidates = video // block
     sink_first = video // block
     sink_last = -(-T // block) if T > video else sink_first
-    qc = block_means(q, block)
+    qc = block_means(padded_tail(q, video, query_tokens, block), block)
     kc = key_means(k, block)
-    a = anchor(qc, block, query_blocks, anchor_dtype or q.dtype)
+    a = anchor(qc, block, candidates, anchor_dtype or q.dtype)
     sc = scores(qc, kc, query_blocks, candidates)
     kk = target_topk(topk_ratio, candidates)
     idx, packed = topk(sc, kk, nb)
@@ -294,6 +320,13 @@ def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: floa
     if attention:
         out, lse = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens, sink_first, sink_last,
                                     local_radius, rows=rows, heads=heads)
+        if query_tokens > video:
+            r0 = max(video, (rows.start or 0) if rows else 0)
+            r1 = min(query_tokens, rows.stop if rows and rows.stop is not None else T)
+            if r0 < r1:
+                dense, dense_lse = sparse_attention(q, k, v, block, packed, ak, av, lm, 0, sink_first, sink_last,
+                                                    local_radius, rows=slice(r0, r1), heads=heads)
+                out[:, r0:r1], lse[:, r0:r1] = dense[:, r0:r1], dense_lse[:, r0:r1]
         result.update(out=out, lse=lse)
     return result
 

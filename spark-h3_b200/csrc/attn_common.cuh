@@ -18,6 +18,7 @@ struct AttnParams {
   int* status;            // device status word (bounded waits)
   int B, T, H, block, NB, QB, words;
   int query_tokens, sink_first, sink_last, local_radius;
+  int row_lo, row_hi;     // query rows computed and stored: [row_lo, row_hi)
 };
 
 // Key block kb is evaluated exactly for routed query block qb when the route marks it,

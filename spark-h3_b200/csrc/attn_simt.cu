@@ -11,9 +11,9 @@ __global__ void __launch_bounds__(128)
 sparse_attention_simt_kernel(AttnParams p) {
   constexpr int PER = D / 32;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int t = blockIdx.x * 4 + warp;
+  const int t = p.row_lo + blockIdx.x * 4 + warp;
   const int h = blockIdx.y, b = blockIdx.z;
-  if (t >= p.T) return;
+  if (t >= p.row_hi) return;
   const T* q = static_cast<const T*>(p.q);
   const T* k = static_cast<const T*>(p.k);
   const T* v = static_cast<const T*>(p.v);
@@ -75,7 +75,7 @@ sparse_attention_simt_kernel(AttnParams p) {
 }
 
 int launch_sparse_attention_simt(const AttnParams& p, int dtype, int D, cudaStream_t s) {
-  dim3 grid(ceil_div(p.T, 4), p.H, p.B);
+  dim3 grid(ceil_div(p.row_hi - p.row_lo, 4), p.H, p.B);
   if (dtype == SB_BF16) {
     if (D == 128) sparse_attention_simt_kernel<__nv_bfloat16, 128><<<grid, 128, 0, s>>>(p);
     else sparse_attention_simt_kernel<__nv_bfloat16, 64><<<grid, 128, 0, s>>>(p);

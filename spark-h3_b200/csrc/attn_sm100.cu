@@ -190,12 +190,11 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
-  const int n_tiles = ceil_div(p.T, 128);
-  const int tile = n_tiles - 1 - (int)blockIdx.x;  // the dense suffix tile launches first
+  const int tile = ceil_div(p.row_hi, 128) - 1 - (int)blockIdx.x;  // the dense suffix tile launches first
   const int h = blockIdx.y, b = blockIdx.z;
   const int row0 = tile * 128;
   const int gshift = p.block == 128 ? 1 : 0;
-  const bool trace = SB_TRACE_CTA();
+  [[maybe_unused]] const bool trace = SB_TRACE_CTA();
 
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
@@ -432,6 +431,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     walk.init(ubits, words_gran);
     bool ok = true;
     for (int j = 0; j < total_tiles; ++j) {
+      SB_TRACE_POINT(trace && row == 0, 13, j);
       const int s = j & 1;
       const uint32_t par = (j >> 1) & 1;
       const bool exact = j < exact_tiles;
@@ -450,6 +450,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           masked = key0 + 64 > p.T;
         }
       }
+      SB_TRACE_POINT(trace && row == 0, 14, j);
       const bool got_s = mbar_wait(smem_u32(&C.bar_s_full[s]), par, abort_flag, p.status, 301);
       if (!__all_sync(0xffffffffu, got_s)) {
         ok = false;
@@ -464,6 +465,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_ld32(tmem + lane_base + s * 128 + s_col + 32, r + 32);
         tmem_wait_ld();
       }
+      SB_TRACE_POINT(trace && row == 0, 6, j);
       // fast: unmasked exact keys, r holds raw scores; otherwise r is rewritten in place
       // with scaled (and, for summary tiles, LM-biased) logits, -inf where invisible.
       const bool fast = exact && vis && !masked;
@@ -571,6 +573,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       f2_unpack(sums[0], s0, s1);
       f2_unpack(sums[1], s2, s3);
       l_run += (s0 + s1) + (s2 + s3);
+      SB_TRACE_POINT(trace && row == 0, 15, j);
       tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
       tc_fence_before();
@@ -593,7 +596,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       const float fb = mb == -INFINITY ? 0.f : ex2_approx(mb - m);
       const float l = la * fa + lb * fb;
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const bool row_ok = grow < p.T;
+      const bool row_ok = grow >= p.row_lo && grow < p.row_hi;
       __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out) + (((int64_t)b * p.T + grow) * p.H + h) * 128 + 64 * grp;
 #pragma unroll
       for (int c = 0; c < 2; ++c) {
@@ -693,7 +696,7 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
   cudaError_t err = cudaFuncSetAttribute(sparse_attention_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_sparse_attention: set smem");
-  dim3 grid(ceil_div(p.T, 128), p.H, p.B);
+  dim3 grid(ceil_div(p.row_hi, 128) - p.row_lo / 128, p.H, p.B);
   sparse_attention_sm100_kernel<<<grid, kThreads, smem, s>>>(mq, mk, mv, mak, mav, p);
   SB_CHECK_LAUNCH("sb_sparse_attention: sm100 launch");
   return SB_OK;

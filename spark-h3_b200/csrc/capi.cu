@@ -108,6 +108,34 @@ extern "C" int sb_sparse_attention(const void* q, const void* k, const void* v, 
   p.B = B; p.T = T; p.H = H; p.block = block; p.NB = NB; p.QB = QB; p.words = ceil_div(NB, 32);
   p.query_tokens = query_tokens; p.sink_first = sink_first; p.sink_last = sink_last;
   p.local_radius = local_radius;
+  p.row_lo = 0;
+  p.row_hi = T;
+  cudaStream_t s = (cudaStream_t)stream;
+  if (dtype == SB_BF16 && D == 128) return launch_sparse_attention_sm100(p, s);
+  return launch_sparse_attention_simt(p, dtype, D, s);
+}
+
+extern "C" int sb_dense_rows_attention(const void* q, const void* k, const void* v, int dtype, int B, int T, int H,
+                                       int D, int row_lo, int row_hi, void* out, float* lse, void* stream) {
+  SB_CHECK_ARG(q && k && v && out, "sb_dense_rows_attention: null Q/K/V/out");
+  SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_dense_rows_attention: bad dtype");
+  SB_CHECK_ARG(B > 0 && T > 0 && H > 0, "sb_dense_rows_attention: B, T, H must be positive");
+  SB_CHECK_ARG(D == 64 || D == 128, "sb_dense_rows_attention: head dim must be 64 or 128, got %d", D);
+  SB_CHECK_ARG(T <= (1 << 22), "sb_dense_rows_attention: at most 4194304 tokens are supported");
+  SB_CHECK_ARG(row_lo >= 0 && row_lo <= row_hi && row_hi <= T,
+               "sb_dense_rows_attention: rows [%d, %d) are outside [0, %d]", row_lo, row_hi, T);
+  SB_CHECK_ARG((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v | (uintptr_t)out) % 16) == 0,
+               "sb_dense_rows_attention: tensors must be 16-byte aligned");
+  if (row_lo == row_hi) return SB_OK;
+  AttnParams p{};
+  p.q = q; p.k = k; p.v = v; p.out = out; p.lse = lse;
+  p.status = device_status_ptr();
+  if (p.status == nullptr) return cuda_error(cudaGetLastError(), "sb_dense_rows_attention: status word");
+  // Every row is a dense-suffix row: no route, no summaries, every key block exact.
+  p.B = B; p.T = T; p.H = H; p.block = 128; p.NB = ceil_div(T, 128); p.QB = 0; p.words = ceil_div(p.NB, 32);
+  p.query_tokens = 0; p.sink_first = 0; p.sink_last = 0; p.local_radius = -1;
+  p.row_lo = row_lo;
+  p.row_hi = row_hi;
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == SB_BF16 && D == 128) return launch_sparse_attention_sm100(p, s);
   return launch_sparse_attention_simt(p, dtype, D, s);

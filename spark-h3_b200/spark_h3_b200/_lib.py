@@ -36,6 +36,7 @@ SIGNATURES = {
     "sb_route_topk_noalloc": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
+    "sb_dense_rows_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "sb_headwise_permute": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "sb_fp8_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
     "sb_fp8_swiglu_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),

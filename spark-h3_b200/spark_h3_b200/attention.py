@@ -20,16 +20,7 @@ BACKEND_TENSOR = "b200_sm100_fused_virtual_query"
 BACKEND_SIMT = "b200_simt_virtual_query"
 
 
-def sparse_query_tokens(total_tokens: int, video_tokens: int, block: int, tail_mode: str = "dense") -> int:
-    """Query prefix evaluated sparsely (spark_integration.py:72-91): whole video blocks."""
-    if tail_mode == "dense":
-        return min(total_tokens, (video_tokens // block) * block)
-    if tail_mode != "pad":
-        raise ValueError("tail_mode must be 'dense' or 'pad'")
-    padded = math.ceil(video_tokens / block) * block
-    if padded > total_tokens:
-        raise ValueError("the packed suffix is too short to pad the final video query block")
-    return padded
+sparse_query_tokens = ops.sparse_query_tokens  # spark_integration.py:72-91
 
 
 def reweight_flags(components: str) -> tuple[bool, bool]:
@@ -67,8 +58,8 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     _check_inputs(q_bthd, k_bthd, v_bthd)
     if cfg.sol_route_topk_ratio is None:
         raise RuntimeError("the B200 path implements Top-K routed Spark attention; set sol_route_topk_ratio")
-    if cfg.sol_video_tail_mode != "dense" or cfg.sol_legacy_full_query:
-        raise NotImplementedError("the B200 path implements sol_video_tail_mode='dense' only")
+    if cfg.sol_legacy_full_query:
+        raise NotImplementedError("the B200 path does not implement sol_legacy_full_query")
     if cfg.sol_tail_granularity != "query" or cfg.sol_reweight_summary_math != "tensorcore" \
             or cfg.sol_reweight_logmass_key != "stored":
         raise NotImplementedError("the B200 path implements the default reweight numerics "
@@ -95,26 +86,28 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     query_inverse = None
     if cfg.sol_landmark_preprocess:
         _check_reblock(cfg, q_bthd, block)
-        q_perm, query_inverse, k_perm, _, hierarchy = _reblock.qk_block_permutations(
-            q_bthd, k_bthd, video, layout.grid, children=cfg.landmark_tree_v2_children,
-            fanout_mode=cfg.landmark_tree_v2_fanout_mode, final_fanout=cfg.landmark_tree_v2_final_fanout,
-            root_fanout=cfg.landmark_tree_v2_root_fanout, ridge=cfg.rope_sol_key_ridge_epsilon,
-            initial_order=cfg.landmark_tree_v2_initial_order)
+        q_perm, query_inverse, k_perm, hierarchy = _reblock_permutations(controller, q_bthd, k_bthd, layout,
+                                                                          layer, video)
         controller.landmark_reblock_hierarchy = hierarchy
         q_bthd = ops.headwise_permute(q_bthd, q_perm, video)
         k_bthd = ops.headwise_permute(k_bthd, k_perm, video)
         v_bthd = ops.headwise_permute(v_bthd, k_perm, video)
-        controller.counts["rope_sol_landmark_tree_v2_key_assignments"] += 1
-        controller.counts["rope_sol_landmark_tree_v2_query_assignments"] += 1
         controller.counts["sol_landmark_preprocess_calls"] += 1
 
-    qc = ops.pool_queries(q_bthd, block)
-    anchor = ops.query_anchor(qc, block, query_blocks, anchor_dtype)
+    # Padding fills after any reblock permutation (spark_integration.py:1173-1187); the anchor
+    # covers the complete video blocks only (landmark_virtual_q.py:30-41).
+    qc = ops.padded_query_means(q_bthd, ops.pool_queries(q_bthd, block), video, query_tokens, block)
+    anchor = ops.query_anchor(qc, block, candidates, anchor_dtype)
     kc, ak, av, lm = ops.pool_keys_summaries(k_bthd, v_bthd, anchor, block, weighted_kv=weighted_kv,
                                              mass_bias=mass_bias)
     packed, _ = ops.route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace, want_indices=False)
     out, _ = ops.sparse_attention(q_bthd, k_bthd, v_bthd, block, packed, ak, av, lm, query_tokens=query_tokens,
                                   sink_first=sink_first, sink_last=sink_last, local_radius=cfg.kernel_local_radius)
+    # Rows past dense_start attend densely (spark_integration.py:1238-1260): the kernel covers
+    # rows past the sparse prefix; the context rows that padded it are recomputed here.
+    dense_start = video if query_tokens > video else query_tokens
+    if query_tokens > video:
+        ops.dense_rows_attention(q_bthd, k_bthd, v_bthd, video, query_tokens, out)
 
     controller.sol_backend = BACKEND_TENSOR if (q_bthd.dtype == torch.bfloat16 and D == 128) else BACKEND_SIMT
     controller.counts["sol_topk_packed_route_calls"] += 1
@@ -124,7 +117,7 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
         if cfg.sol_spark_mode == "reweight_only":
             controller.counts["sol_identity_reweight_calls"] += 1
     controller.counts["sol_topk_calls"] += 1
-    if T > query_tokens:
+    if T > dense_start:
         controller.counts["sol_dense_context_queries"] += 1
     if cfg.sol_landmark_preprocess:
         key = ("reblock_global_anchor", T, video, controller.landmark_reblock_hierarchy)
@@ -166,6 +159,34 @@ _REBLOCK_DEFAULTS = dict(
     landmark_tree_v2_m2_estimator="hilbert_midpoint", landmark_tree_v2_proxy_iterations=2,
     landmark_tree_v2_proxy_seed_rule="farthest_pair", landmark_tree_v2_proxy_update_rule="mean",
     landmark_tree_v2_layout_reuse="independent", landmark_tree_v2_fanout_mode="power_of_two_fanout")
+
+
+def _reblock_permutations(controller, q_bthd, k_bthd, layout, layer: int, video: int):
+    """Query/key permutations of one layer, shared by groups of layers when the controller
+    asks for it (spark_integration.py:941-988): with `spark_reblock_reuse_layers` = R > 1,
+    layers from `spark_reblock_reuse_start_layer` on form groups of R, and every layer of a
+    group after its first reuses the first layer's permutations within the same evaluation."""
+    cfg = controller.config
+    reuse_layers = int(getattr(controller, "spark_reblock_reuse_layers", 1))
+    reuse_start = int(getattr(controller, "spark_reblock_reuse_start_layer", 0))
+    group = (layer - reuse_start) // reuse_layers if reuse_layers > 1 and layer >= reuse_start else None
+    key = (controller.evaluation_index, group)
+    cached = getattr(controller, "spark_last_reblock", None)
+    group_start = reuse_start + group * reuse_layers if group is not None else layer
+    if group is not None and layer != group_start and cached is not None and cached[0] == key:
+        controller.counts["sol_landmark_reuse_calls"] += 1
+        return cached[1]
+    q_perm, query_inverse, k_perm, _, hierarchy = _reblock.qk_block_permutations(
+        q_bthd, k_bthd, video, layout.grid, children=cfg.landmark_tree_v2_children,
+        fanout_mode=cfg.landmark_tree_v2_fanout_mode, final_fanout=cfg.landmark_tree_v2_final_fanout,
+        root_fanout=cfg.landmark_tree_v2_root_fanout, ridge=cfg.rope_sol_key_ridge_epsilon,
+        initial_order=cfg.landmark_tree_v2_initial_order)
+    controller.counts["rope_sol_landmark_tree_v2_key_assignments"] += 1
+    controller.counts["rope_sol_landmark_tree_v2_query_assignments"] += 1
+    result = (q_perm, query_inverse, k_perm, hierarchy)
+    if group is not None:
+        controller.spark_last_reblock = (key, result)
+    return result
 
 
 def _check_reblock(cfg, q, block: int) -> None:

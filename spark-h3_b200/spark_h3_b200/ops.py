@@ -138,6 +138,50 @@ def sparse_attention(q, k, v, block: int, packed: torch.Tensor | None, ak, av, l
     return out, lse
 
 
+def dense_rows_attention(q, k, v, row_lo: int, row_hi: int, out: torch.Tensor, *,
+                         lse: torch.Tensor | None = None) -> torch.Tensor:
+    """Dense attention of query rows [row_lo, row_hi) over every key, written into `out`
+    (and `lse`) in place; other rows are untouched (sb_dense_rows_attention)."""
+    device = _require_cuda(q, k, v, out, lse)
+    B, T, H, D = q.shape
+    if k.shape != q.shape or v.shape != q.shape or out.shape != q.shape or out.dtype != q.dtype:
+        raise ValueError("Q, K, V and out must share shape and dtype")
+    with torch.cuda.device(device):
+        _lib.call("sb_dense_rows_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, T, H, D,
+                  row_lo, row_hi, out.data_ptr(), _ptr(lse), _stream(device))
+    return out
+
+
+def padded_query_means(q: torch.Tensor, qc: torch.Tensor, video_tokens: int, query_tokens: int,
+                       block: int) -> torch.Tensor:
+    """sol_video_tail_mode = "pad" (spark_integration.py:1173-1187): the rows that fill the
+    final video query block take the mean of that block's video rows (fp32 mean, rounded to
+    Q's dtype), so its query mean is pooled over the padded block.  Only that block's mean
+    changes: it is pooled from a one-block copy and written into qc in place."""
+    tail_start = (video_tokens // block) * block
+    if query_tokens <= video_tokens:
+        return qc
+    tail = q[:, tail_start:query_tokens].clone()
+    tail[:, video_tokens - tail_start:] = q[:, tail_start:video_tokens].mean(dim=1, keepdim=True,
+                                                                             dtype=torch.float32).to(q.dtype)
+    qc[:, tail_start // block] = pool_queries(tail.contiguous(), block)[:, 0]
+    return qc
+
+
+def sparse_query_tokens(total_tokens: int, video_tokens: int, block: int, tail_mode: str = "dense") -> int:
+    """Query prefix evaluated sparsely (spark_integration.py:72-91): the complete video blocks
+    ("dense": the partial final block joins the dense suffix), or every video block with the
+    final one padded from the context that follows ("pad")."""
+    if tail_mode == "dense":
+        return min(total_tokens, (video_tokens // block) * block)
+    if tail_mode != "pad":
+        raise ValueError("tail_mode must be 'dense' or 'pad'")
+    padded = math.ceil(video_tokens / block) * block
+    if padded > total_tokens:
+        raise ValueError("the packed suffix is too short to pad the final video query block")
+    return padded
+
+
 def headwise_permute(x: torch.Tensor, permutation: torch.Tensor, video_tokens: int,
                      out: torch.Tensor | None = None) -> torch.Tensor:
     """dst[b, t, h] = x[b, perm[b, h, t], h] for t < video_tokens; identity after."""
@@ -167,30 +211,34 @@ def read_device_status(device: torch.device | None = None) -> int:
 def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int = 128, topk_ratio: float = 0.1,
                 video_tokens: int | None = None, anchor_dtype: torch.dtype | None = None, local_radius: int = -1,
                 weighted_kv: bool = True, mass_bias: bool = True, workspace: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, return_route: bool = False):
+                out: torch.Tensor | None = None, return_route: bool = False, tail_mode: str = "dense"):
     """One Spark sparse attention layer on BTHD tensors whose video prefix comes first.
 
     pool Q -> anchor -> pool K + summaries -> scores + Top-K -> sparse attention
-    (rows past the last complete video block are attended densely by the same kernel).
+    (rows past the sparse query prefix are attended densely by the same kernel).  With
+    tail_mode "pad" the partial final video block is routed as a padded block and the context
+    rows that padded it are then attended densely (sb_dense_rows_attention).
     """
     B, T, H, D = q.shape
     video = T if video_tokens is None else int(video_tokens)
     if not block <= video <= T:
         raise ValueError(f"video_tokens must lie in [{block}, {T}]")
-    query_blocks = video // block
-    query_tokens = query_blocks * block
+    query_tokens = sparse_query_tokens(T, video, block, tail_mode)
+    query_blocks = query_tokens // block
     candidates = video // block
     nb = math.ceil(T / block)
     sink_first = video // block
     sink_last = nb if T > video else sink_first
     topk = target_topk(topk_ratio, candidates)
-    qc = pool_queries(q, block)
-    anchor = query_anchor(qc, block, query_blocks, anchor_dtype or q.dtype)
+    qc = padded_query_means(q, pool_queries(q, block), video, query_tokens, block)
+    anchor = query_anchor(qc, block, candidates, anchor_dtype or q.dtype)
     kc, ak, av, lm = pool_keys_summaries(k, v, anchor, block, weighted_kv=weighted_kv, mass_bias=mass_bias)
     packed, indices = route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace,
                                  want_indices=return_route)
     o, _ = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens=query_tokens, sink_first=sink_first,
                             sink_last=sink_last, local_radius=local_radius, out=out)
+    if query_tokens > video:
+        dense_rows_attention(q, k, v, video, query_tokens, o)
     if return_route:
         return o, dict(qc=qc, kc=kc, anchor=anchor, ak=ak, av=av, lm=lm, packed=packed, indices=indices,
                        topk=topk, query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last)

@@ -19,6 +19,9 @@ from .layout import packed_layout
 class _Controller:
     def __init__(self, config: H3SparseAttentionConfig):
         self.config = config
+        # Reblock reuse across layers (spark_integration.py:944-945); kept over reset().
+        self.spark_reblock_reuse_layers = 1
+        self.spark_reblock_reuse_start_layer = 0
         self.reset()
 
     def reset(self):
@@ -34,6 +37,7 @@ class _Controller:
         self.exact_block_verbose_accumulator = None
         self.head_topk_budget = None
         self.spark_reblock_frozen_tail_indices = None
+        self.spark_last_reblock = None
 
     def begin_forward(self, _module, args, kwargs):
         """Forward pre-hook: count the evaluation and rebuild the packed layout."""

@@ -164,3 +164,48 @@ def test_headwise_permute_roundtrip(cuda_device):
     assert torch.equal(z.cpu(), x)
     y32 = ops.headwise_permute(x.to(dev), perm.to(dev).to(torch.int32), video)
     assert torch.equal(y32.cpu(), expected)
+
+
+@pytest.mark.parametrize("block", [64, 128])
+def test_pad_tail_mode_matches_oracle(cuda_device, block):
+    # 2100 video tokens (a partial final block) followed by 162 context tokens; tail mode
+    # "pad" routes the final video block padded with its own mean and attends the context
+    # rows that padded it densely.
+    q, k, v = make_qkv((4, 16, 33), 2, 128, seed=31, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    extra = make_qkv((1, 10, 15), 2, 128, seed=32, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    q, k, v = (torch.cat((a, b), dim=1) for a, b in zip((q, k, v), extra))
+    video = 2100
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             video_tokens=video, tail_mode="pad")
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, video_tokens=video, tail_mode="pad", return_route=True)
+    torch.cuda.synchronize()
+    assert route["query_tokens"] == ref["query_tokens"] == -(-video // block) * block
+    np.testing.assert_array_equal(as_np(route["qc"]), ref["qc"])
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    _check(as_np(out), ref["out"], torch.bfloat16)
+    # The dense rows differ from what the sparse prefix alone would give them.
+    dense = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                            topk_ratio=0.1, video_tokens=video)
+    torch.cuda.synchronize()
+    assert not torch.equal(dense[:, :video].cpu(), out[:, :video].cpu())
+    _check(as_np(out)[:, video:], as_np(dense)[:, video:], torch.bfloat16)
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
+def test_dense_rows_attention_window(cuda_device, dtype):
+    q, k, v = make_qkv((3, 16, 32), 2, 128, seed=41, dtype=dtype, q_scale=128 ** -0.5)
+    dev = cuda_device
+    T = q.shape[1]
+    out = torch.full_like(q, 7.0).to(dev)
+    lse = torch.full((1, T, 2), 7.0, device=dev)
+    ops.dense_rows_attention(q.to(dev), k.to(dev), v.to(dev), 70, 333, out, lse=lse)
+    torch.cuda.synchronize()
+    ref, ref_lse = oracle.sparse_attention(to_oracle(q), to_oracle(k), to_oracle(v), 64, np.zeros((1, 0, 2, 1)),
+                                           np.zeros((1, 2, 24, 128)), np.zeros((1, 2, 24, 128)),
+                                           np.zeros((1, 2, 24)), 0, 0, 0, rows=slice(70, 333))
+    o = as_np(out)
+    assert (o[:, :70] == 7.0).all() and (o[:, 333:] == 7.0).all()
+    _check(o[:, 70:333], ref[:, 70:333], dtype)
+    np.testing.assert_allclose(as_np(lse)[:, 70:333], ref_lse[:, 70:333], atol=2e-3, rtol=1e-4)
+    assert (as_np(lse)[:, :70] == 7.0).all() and (as_np(lse)[:, 333:] == 7.0).all()

@@ -50,24 +50,27 @@ def host(t):
     return oracle.Tensor(t.view(torch.int16).numpy().view(np.uint16), "bfloat16")
 
 
-@pytest.mark.parametrize("mode,block", [("reweight_only", 64), ("topk_only", 64), ("reweight_only", 128)])
-def test_plugin_matches_oracle(cuda_device, mode, block):
+@pytest.mark.parametrize("mode,block,tail_mode", [("reweight_only", 64, "dense"), ("topk_only", 64, "dense"),
+                                                  ("reweight_only", 128, "dense"), ("reweight_only", 64, "pad"),
+                                                  ("reweight_only", 128, "pad")])
+def test_plugin_matches_oracle(cuda_device, mode, block, tail_mode):
     torch.manual_seed(3)
     dev = cuda_device
     model = TinyTransformer().to(dev, torch.bfloat16)
     for lin in (model.transformer_blocks[0].attn.to_q, model.transformer_blocks[0].attn.to_k,
                 model.transformer_blocks[0].attn.to_v):
         torch.nn.init.normal_(lin.weight, std=0.06)
-    grid = (2, 16, 40)
+    grid = (2, 16, 40) if tail_mode == "dense" else (2, 16, 41)  # pad: a partial final video block
     video = grid[0] * grid[1] * grid[2]
-    text = 50
+    text = 50 if tail_mode == "dense" else 100
     tags = torch.cat([torch.ones(text), torch.zeros(video)]).long()     # text first in the raw order
     pos = torch.cat([torch.zeros(text, 3, dtype=torch.long),
                      torch.cartesian_prod(*(torch.arange(n) for n in grid))])
     x = torch.randn(1, video + text, 256, dtype=torch.bfloat16).to(dev)
     attn = model.transformer_blocks[0].attn
     with install_h3_spark_attn(model, num_denoise_steps=1, warmup_mode="warmup_steps", warmup_steps=0,
-                               min_tokens=0, mode=mode, sol_block_size=block) as plugin:
+                               min_tokens=0, mode=mode, sol_block_size=block,
+                               sol_video_tail_mode=tail_mode) as plugin:
         out = model(x, token_tags=tags.to(dev), position_ids=pos.to(dev))
         layout = plugin.controller.layout
         summary = plugin.summary()
@@ -81,7 +84,7 @@ def test_plugin_matches_oracle(cuda_device, mode, block):
         v = attn.to_v(x).unflatten(-1, (2, -1)).index_select(1, layout.permutation)
     weighted = mode != "topk_only"
     ref = oracle.spark_layer(host(q), host(k), host(v), block=block, topk_ratio=0.1, video_tokens=video,
-                             weighted_kv=weighted, mass_bias=weighted)
+                             weighted_kv=weighted, mass_bias=weighted, tail_mode=tail_mode)
     expected = torch.from_numpy(ref["out"]).to(dev)[:, layout.inverse_permutation].flatten(2, 3)
     err = (out.float() - expected).abs().max().item()
     cos = torch.nn.functional.cosine_similarity(out.float().flatten(), expected.flatten(), dim=0).item()

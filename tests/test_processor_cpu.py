@@ -89,3 +89,35 @@ def test_forward_without_layout_metadata_is_rejected():
     with install_h3_spark_attn(model, num_denoise_steps=2):
         with pytest.raises(RuntimeError, match="token_tags/position_ids"):
             model(torch.zeros(1, 8, 4))
+
+
+def test_sparse_query_prefix_by_tail_mode():
+    # spark_integration.py:72-91 and the reference's own expectations
+    # (tests/test_global_reweight_followup.py:14-16).
+    from spark_h3_b200.ops import sparse_query_tokens
+
+    assert sparse_query_tokens(8329, 8193, 64, "dense") == 8192
+    assert sparse_query_tokens(8329, 8193, 64, "pad") == 8256
+    assert sparse_query_tokens(8329, 8193, 128, "pad") == 8320
+    with pytest.raises(ValueError, match="too short to pad"):
+        sparse_query_tokens(8200, 8193, 64, "pad")
+    with pytest.raises(ValueError, match="tail_mode"):
+        sparse_query_tokens(8329, 8193, 64, "wrap")
+
+
+def test_oracle_pad_fill_is_the_tail_mean():
+    # The rows that pad the final video block hold the fp32 mean of its video rows rounded to
+    # bf16, as q[:, tail:video].mean(1, dtype=float32).to(bf16) (spark_integration.py:1180-1187).
+    import numpy as np
+
+    from oracle import oracle
+
+    torch.manual_seed(5)
+    q = torch.randn(1, 137, 2, 128).to(torch.bfloat16)
+    video, block = 97, 64
+    host = oracle.Tensor(q.view(torch.int16).numpy().view(np.uint16), "bfloat16")
+    padded = oracle.padded_tail(host, video, 128, block)
+    expected = q[:, 64:video].mean(1, keepdim=True, dtype=torch.float32).to(torch.bfloat16)
+    got = torch.from_numpy(padded.data.view(np.int16)).view(torch.bfloat16)
+    assert torch.equal(got[:, video:128], expected.expand(-1, 128 - video, -1, -1))
+    assert torch.equal(got[:, :video], q[:, :video]) and torch.equal(got[:, 128:], q[:, 128:])

@@ -79,3 +79,38 @@ def test_spark_reblock_rejects_unimplemented_options():
         reblock.spark_reblock(x, grid_shape=(1, 1, 128), distance="euclidean")
     with pytest.raises(TypeError):
         reblock.spark_reblock(x, grid_shape=(1, 1, 128), colour="blue")
+
+
+def test_reblock_reuse_across_layers(monkeypatch):
+    """Groups of `spark_reblock_reuse_layers` layers share the first layer's permutations
+    within one evaluation (spark_integration.py:941-988); a new evaluation rebuilds."""
+    from spark_h3_b200 import attention
+    from spark_h3_b200.config import H3SparseAttentionConfig
+    from spark_h3_b200.processor import _Controller
+
+    builds = []
+
+    def fake_builder(q, k, video, grid, **kwargs):
+        builds.append(q)
+        return (f"qp{len(builds)}", f"qi{len(builds)}", f"kp{len(builds)}", None, f"h{len(builds)}")
+
+    monkeypatch.setattr(attention._reblock, "qk_block_permutations", fake_builder)
+    controller = _Controller(H3SparseAttentionConfig.spark(num_inference_steps=4, mode="full",
+                                                           sol_route_topk_ratio=0.1))
+
+    class Layout:
+        grid = (1, 8, 8)
+
+    def run(layer):
+        return attention._reblock_permutations(controller, object(), object(), Layout, layer, 64)[0]
+
+    controller.evaluation_index = 0
+    assert [run(layer) for layer in range(4)] == ["qp1", "qp2", "qp3", "qp4"]  # default: no reuse
+    controller.spark_reblock_reuse_layers = 2
+    controller.spark_reblock_reuse_start_layer = 1
+    assert [run(layer) for layer in range(6)] == ["qp5", "qp6", "qp6", "qp7", "qp7", "qp8"]
+    assert controller.counts["sol_landmark_reuse_calls"] == 2
+    controller.evaluation_index = 1
+    assert run(1) == "qp9" and run(2) == "qp9"
+    controller.reset()
+    assert controller.spark_reblock_reuse_layers == 2  # settings survive reset, as in the reference
