@@ -5,15 +5,18 @@
 //   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
 //   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages
 //   warp 9     TMA producer of the V (or AV summary) tiles, 2 stages
-//   warp 10    tcgen05 issuer of S = Q K^T; owns the TMEM allocation
-//   warp 11    tcgen05 issuer of O += P V
+//   warp 10    tcgen05 issuer of S = Q K^T (one 128 x 64 product per group); owns TMEM
+//   warp 11    tcgen05 issuer of O += P V (one per group)
 // Issuing one tcgen05.mma occupies its thread for about as long as a third of the MMA's
 // execution, so two issuers keep the tensor pipe fed where one would stall it on every
 // wait and commit.
 // TMEM (512 columns): S double buffer at [0,128) and [128,256); O_A at [256,384) and
 // O_B at [384,512).  Each softmax group keeps its own running max, sum and output
-// accumulator (O_A += P_A V[0:64), O_B += P_B V[64:128)), so the groups never
-// synchronise inside the key loop; the epilogue merges the two partial softmaxes.
+// accumulator (O_A += P_A V[0:64), O_B += P_B V[64:128)) and has its own S product,
+// P.V product and barriers, so the groups never synchronise inside the key loop and
+// drift out of step: the two warps that share a scheduler (one per group) then take
+// turns on the exponential unit instead of contending for it.  The epilogue merges the
+// two partial softmaxes.
 // P is written back over the group's own S columns as packed bf16 pairs and feeds the
 // P.V product straight from TMEM.
 //
@@ -74,8 +77,9 @@ struct __align__(8) Control {
   uint64_t bar_q_full;
   uint64_t bar_k_full[kKStages], bar_k_empty[kKStages];
   uint64_t bar_v_full[kVStages], bar_v_empty[kVStages];
-  uint64_t bar_s_full[2];
-  uint64_t bar_p_full[2];  // both softmax groups have written P into the S buffer (256)
+  uint64_t bar_s_full[2][2];   // [group][buffer]: the group's S columns have landed
+  uint64_t bar_p_full[2][2];   // [group][buffer]: the group's P is in TMEM (one arrival per warp)
+  uint64_t bar_pv_done[2][2];  // [group][buffer]: the group's P.V has completed
   uint64_t bar_xsum;       // both groups have published their final max and sum (256)
   uint64_t bar_o_final;    // P.V issuer: every P.V (hence every S) has completed
   uint64_t bar_s_final;    // S issuer: its last MMA has completed (drain before exit)
@@ -87,31 +91,9 @@ struct __align__(8) Control {
   float xsum[2][128];  // [group][row] final partial sums
 };
 
-// Walks the set bits of the granule bitset in ascending order.
-struct GranuleWalker {
-  const uint32_t* words;
-  int nwords, w;
-  uint32_t bits;
-  __device__ void init(const uint32_t* u, int n) {
-    words = u;
-    nwords = n;
-    w = 0;
-    bits = n > 0 ? u[0] : 0u;
-  }
-  __device__ int next() {
-    while (bits == 0u) {
-      if (++w >= nwords) return -1;
-      bits = words[w];
-    }
-    const int g = 32 * w + __ffs(bits) - 1;
-    bits &= bits - 1u;
-    return g;
-  }
-};
-
 struct SmemLayout {
   uint32_t q, k, v;  // byte offsets from the 1024-aligned base (stages are consecutive)
-  uint32_t ctrl, ebits, ubits, lm;
+  uint32_t ctrl, ebits, ubits, lm, glist;
   uint32_t total;
 };
 
@@ -124,7 +106,8 @@ __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran,
   L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);  // Control is small
   L.ubits = L.ebits + (uint32_t)((2 * words_blk * 4 + 15) / 16 * 16);  // every region 16-byte aligned
   L.lm = L.ubits + (uint32_t)((words_gran * 4 + 15) / 16 * 16);
-  L.total = L.lm + (uint32_t)(nb_pad * 4);  // LM * log2(e) of every key block
+  L.glist = L.lm + (uint32_t)(nb_pad * 4);  // LM * log2(e) of every key block
+  L.total = L.glist + (uint32_t)((words_gran * 32 * 2 + 15) / 16 * 16);  // exact granules in order (uint16)
   return L;
 }
 
@@ -187,6 +170,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   float* lm_s = reinterpret_cast<float*>(smem + L.lm);  // [nb_pad]
   uint32_t* ebits = reinterpret_cast<uint32_t*>(smem + L.ebits);  // [2][words_blk]
   uint32_t* ubits = reinterpret_cast<uint32_t*>(smem + L.ubits);  // [words_gran]
+  uint16_t* glist = reinterpret_cast<uint16_t*>(smem + L.glist);  // [exact granules]
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
@@ -207,10 +191,12 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_init(smem_u32(&C.bar_v_full[s]), 1);
       mbar_init(smem_u32(&C.bar_v_empty[s]), 1);
     }
-    for (int s = 0; s < 2; ++s) {
-      mbar_init(smem_u32(&C.bar_s_full[s]), 1);
-      mbar_init(smem_u32(&C.bar_p_full[s]), 256);
-    }
+    for (int g = 0; g < 2; ++g)
+      for (int s = 0; s < 2; ++s) {
+        mbar_init(smem_u32(&C.bar_s_full[g][s]), 1);
+        mbar_init(smem_u32(&C.bar_p_full[g][s]), 4);
+        mbar_init(smem_u32(&C.bar_pv_done[g][s]), 1);
+      }
     mbar_init(smem_u32(&C.bar_o_final), 1);
     mbar_init(smem_u32(&C.bar_s_final), 1);
     mbar_init(smem_u32(&C.bar_xsum), 256);
@@ -272,9 +258,25 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     lm_s[e] = (any_routed && e < p.NB) ? __ldg(p.lm + ((int64_t)b * p.H + h) * p.NB + e) * kLog2e : 0.f;
   __syncthreads();
   if (warp == 0) {
+    // The exact granules in ascending order (granule ids are below 65536: T <= 2^22).
     int cnt = 0;
-    for (int w = lane; w < words_gran; w += 32) cnt += __popc(ubits[w]);
-    for (int o = 16; o > 0; o >>= 1) cnt += __shfl_xor_sync(0xffffffffu, cnt, o);
+    for (int w0 = 0; w0 < words_gran; w0 += 32) {
+      const int w = w0 + lane;
+      uint32_t bits = w < words_gran ? ubits[w] : 0u;
+      const int own = __popc(bits);
+      int incl = own;
+#pragma unroll
+      for (int o = 1; o < 32; o <<= 1) {
+        const int v = __shfl_up_sync(0xffffffffu, incl, o);
+        if (lane >= o) incl += v;
+      }
+      int pos = cnt + incl - own;
+      while (bits) {
+        glist[pos++] = (uint16_t)(32 * w + __ffs(bits) - 1);
+        bits &= bits - 1u;
+      }
+      cnt += __shfl_sync(0xffffffffu, incl, 31);
+    }
     if (lane == 0) {
       C.exact_granules = cnt;
       const bool routed0 = row0 < p.query_tokens && row0 < p.T;
@@ -315,17 +317,15 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           for (int rh = 0; rh < 2; ++rh)
             tma_load_3d(sQ + dh * kHalfBytes + rh * kBoxBytes, &tm_q, bq, h * 128 + 64 * dh, row0 + 64 * rh, b);
       }
-      GranuleWalker walk;
-      walk.init(ubits, words_gran);
+      const int n_gran = C.exact_granules;
       int armed[kKStages > kVStages ? kKStages : kVStages] = {};
       int s = 0, use = 0;  // stage and how many times it has been filled before
       for (int j = 0; j < total_tiles; ++j) {
         int g0 = 0, g1 = 0;
         const bool exact = j < exact_tiles;
         if (exact) {
-          g0 = walk.next();
-          g1 = walk.next();
-          if (g1 < 0) g1 = g0;
+          g0 = glist[2 * j];
+          g1 = 2 * j + 1 < n_gran ? (int)glist[2 * j + 1] : g0;  // an odd last granule fills both slots
         }
         const int cc = j - exact_tiles;
         const uint32_t bar = smem_u32(&full[s]);
@@ -355,8 +355,11 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
   } else if (warp == kMmaWarp) {
     // ------------------------------------------------------------- S issuer
+    // Two S products per tile, one per softmax group (N = 64: the group's granule slot),
+    // each with its own barriers, so the groups run out of step: while one group works
+    // through its exponentials the other can wait, load and reduce.
     if (lane == 0) {
-      constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 128, false);
+      constexpr uint32_t idesc_qk = idesc_bf16_f32(128, 64, false);
       bool ok = mbar_wait(smem_u32(&C.bar_q_full), 0, abort_flag, p.status, 201);
       // Descriptors differ only in the start-address field (bits 0-13, in 16-byte units).
       const uint64_t qdesc0 = smem_desc_sw128(sQ, 16, 1024);
@@ -366,20 +369,26 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         const int s = j & 1;
         if (!mbar_wait(smem_u32(&C.bar_k_full[ks]), (uint32_t)(kuse & 1), abort_flag, p.status, 204)) break;
         SB_TRACE_POINT(trace, 2, j);
-        // S buffer s still holds P of tile j-2 until that P.V completes (it released its
-        // V stage).  That barrier cannot run two phases ahead: P.V of tile j needs S_j.
-        if (j >= 2 && !mbar_wait(smem_u32(&C.bar_v_empty[s]), (uint32_t)(((j - 2) >> 1) & 1), abort_flag, p.status,
-                                 205))
-          break;
-        SB_TRACE_POINT(trace, 12, j);
-        tc_fence_after();
         const uint64_t kdesc = kdesc0 + (uint64_t)((ks * kTileBytes) >> 4);
+        for (int g = 0; ok && g < 2; ++g) {
+          // The group's S columns of buffer s still hold its P of tile j-2 until that P.V
+          // completes.  The barrier cannot run two phases ahead: P.V of tile j needs S_j.
+          if (j >= 2 && !mbar_wait(smem_u32(&C.bar_pv_done[g][s]), (uint32_t)(((j - 2) >> 1) & 1), abort_flag,
+                                   p.status, 205)) {
+            ok = false;
+            break;
+          }
+          if (g == 0) SB_TRACE_POINT(trace, 12, j);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
-          mma_ss(tmem + s * 128, qdesc0 + off, kdesc + off, idesc_qk, kk > 0 ? 1u : 0u);
+          for (int kk = 0; kk < 8; ++kk) {
+            const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+            mma_ss(tmem + s * 128 + 64 * g, qdesc0 + off, kdesc + off + (uint64_t)((g * kBoxBytes) >> 4), idesc_qk,
+                   kk > 0 ? 1u : 0u);
+          }
+          tc_commit(smem_u32(&C.bar_s_full[g][s]));
         }
-        tc_commit(smem_u32(&C.bar_s_full[s]));
+        if (!ok) break;
         SB_TRACE_POINT(trace, 3, j);
         tc_commit(smem_u32(&C.bar_k_empty[ks]));
         if (++ks == kKStages) {
@@ -391,26 +400,32 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
   } else if (warp == kPvWarp) {
     // ----------------------------------------------------------- P.V issuer
-    // O_A += P_A V[0:64), O_B += P_B V[64:128).  One wait on the shared P barrier (both
-    // groups) and one commit that releases the V stage; the softmax groups and the S
-    // issuer also use that commit to learn that this P.V has finished.
+    // O_A += P_A V[0:64), O_B += P_B V[64:128), each as soon as its group's P is in TMEM.
+    // Per group, a commit tells the S issuer and the group that the P.V has finished; one
+    // commit after both releases the V stage.
     if (lane == 0) {
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, true);
       const uint64_t vdesc0 = smem_desc_sw128(sV0, kHalfBytes, 1024);
-      for (int i = 0; i < total_tiles; ++i) {
+      bool ok = true;
+      for (int i = 0; ok && i < total_tiles; ++i) {
         const int s = i & 1;  // S/P buffer (two in TMEM) and V stage (kVStages == 2)
         const uint32_t par = (i >> 1) & 1;
         const uint64_t vdesc = vdesc0 + (uint64_t)((s * kTileBytes) >> 4);
         if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) break;
-        if (!mbar_wait(smem_u32(&C.bar_p_full[s]), par, abort_flag, p.status, 202)) break;
-        SB_TRACE_POINT(trace, 4, i);
-        tc_fence_after();
+        for (int g = 0; g < 2; ++g) {
+          if (!mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) {
+            ok = false;
+            break;
+          }
+          if (g == 0) SB_TRACE_POINT(trace, 4, i);
+          tc_fence_after();
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
-          const int g = kk >> 2;
-          mma_ts(tmem + (g ? kColOB : kColOA), tmem + s * 128 + 64 * g + (kk & 3) * 8,
-                 vdesc + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || (kk & 3) > 0) ? 1u : 0u);
+          for (int kk = 0; kk < 4; ++kk)
+            mma_ts(tmem + (g ? kColOB : kColOA), tmem + s * 128 + 64 * g + kk * 8,
+                   vdesc + (uint64_t)(((4 * g + kk) * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+          tc_commit(smem_u32(&C.bar_pv_done[g][s]));
         }
+        if (!ok) break;
         tc_commit(smem_u32(&C.bar_v_empty[s]));
         SB_TRACE_POINT(trace, 5, i);
       }
@@ -427,11 +442,20 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     const uint32_t* ehalf = ebits + half * words_blk;
     const float scale_log2 = 0.08838834764831845f * kLog2e;
     float m_run = -INFINITY, l_run = 0.f;
-    GranuleWalker walk;
-    walk.init(ubits, words_gran);
+    // Tile j's exact 64-key granule for this group is glist[2j + grp] (none past the end).
+    // Both shared-memory reads behind its visibility (the list entry and the exact-block
+    // word of the row half) are issued a tile ahead, so their latency -- long while the
+    // tensor pipe streams operands out of shared memory -- hides behind the exponentials.
+    const int n_gran = C.exact_granules;
+    auto granule = [&](int t) -> int {
+      const int i = 2 * t + grp;
+      return (t < exact_tiles && i < n_gran) ? (int)glist[i] : -1;
+    };
+    int g_cur = granule(0);
+    uint32_t w_cur = g_cur >= 0 ? ehalf[(g_cur >> gshift) >> 5] : 0u;
     bool ok = true;
     for (int j = 0; j < total_tiles; ++j) {
-      SB_TRACE_POINT(trace && row == 0, 13, j);
+      SB_TRACE_POINT(trace && tid == 0, 13, j);
       const int s = j & 1;
       const uint32_t par = (j >> 1) & 1;
       const bool exact = j < exact_tiles;
@@ -439,19 +463,13 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       bool vis = true, masked = false;
       int key0 = 0;
       if (exact) {
-        const int g0 = walk.next();
-        const int g1 = walk.next();
-        const int g = grp ? g1 : g0;
-        vis = g >= 0;
-        if (vis) {
-          const int kb = g >> gshift;  // granule -> key block (block is 64 or 128)
-          vis = (ehalf[kb >> 5] >> (kb & 31)) & 1u;
-          key0 = g * 64;
-          masked = key0 + 64 > p.T;
-        }
+        vis = g_cur >= 0 && ((w_cur >> ((g_cur >> gshift) & 31)) & 1u);
+        key0 = g_cur * 64;
+        masked = vis && key0 + 64 > p.T;
       }
-      SB_TRACE_POINT(trace && row == 0, 14, j);
-      const bool got_s = mbar_wait(smem_u32(&C.bar_s_full[s]), par, abort_flag, p.status, 301);
+      const int g_nxt = granule(j + 1);
+      SB_TRACE_POINT(trace && tid == 0, 14, j);
+      const bool got_s = mbar_wait(smem_u32(&C.bar_s_full[grp][s]), par, abort_flag, p.status, 301);
       if (!__all_sync(0xffffffffu, got_s)) {
         ok = false;
         break;
@@ -465,7 +483,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         tmem_ld32(tmem + lane_base + s * 128 + s_col + 32, r + 32);
         tmem_wait_ld();
       }
-      SB_TRACE_POINT(trace && row == 0, 6, j);
+      SB_TRACE_POINT(trace && tid == 0, 6, j);
       // fast: unmasked exact keys, r holds raw scores; otherwise r is rewritten in place
       // with scaled (and, for summary tiles, LM-biased) logits, -inf where invisible.
       const bool fast = exact && vis && !masked;
@@ -510,6 +528,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       }
       const float tile_max = fmaxf(max3(mx[0], mx[1], mx[2]), mx[3]);
       SB_TRACE_POINT(trace && row == 0 && grp == 0, 8, j);
+      const uint32_t w_nxt = g_nxt >= 0 ? ehalf[(g_nxt >> gshift) >> 5] : 0u;
       // Lazy rescale of this group's O: only when the running max grows by more than the
       // threshold (or becomes finite for the first time).
       const float m_new = fmaxf(m_run, tile_max);
@@ -519,11 +538,11 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         alpha = m_run == -INFINITY ? 0.f : ex2_approx(m_run - m_new);
         m_run = m_new;
       }
-      // P.V of tile j-1 has finished once its V stage was released; that barrier cannot
-      // be two phases ahead, since P.V of tile j+1 needs this group's P of tile j+1.
+      // The group's P.V of tile j-1 has finished; that barrier cannot be two phases
+      // ahead, since the group's P.V of tile j+1 needs its P of tile j+1.
       if (j > 0 && __any_sync(0xffffffffu, need)) {
-        const bool got_o = mbar_wait(smem_u32(&C.bar_v_empty[(j - 1) & 1]), (uint32_t)(((j - 1) >> 1) & 1), abort_flag,
-                                     p.status, 302);
+        const bool got_o = mbar_wait(smem_u32(&C.bar_pv_done[grp][(j - 1) & 1]), (uint32_t)(((j - 1) >> 1) & 1),
+                                     abort_flag, p.status, 302);
         if (!__all_sync(0xffffffffu, got_o)) {
           ok = false;
           break;
@@ -573,12 +592,15 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       f2_unpack(sums[0], s0, s1);
       f2_unpack(sums[1], s2, s3);
       l_run += (s0 + s1) + (s2 + s3);
-      SB_TRACE_POINT(trace && row == 0, 15, j);
+      SB_TRACE_POINT(trace && tid == 0, 15, j);
       tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(smem_u32(&C.bar_p_full[s]));
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&C.bar_p_full[grp][s]));
       SB_TRACE_POINT(trace && row == 0, grp ? 11 : 9, j);
+      g_cur = g_nxt;
+      w_cur = w_nxt;
     }
     // Epilogue: merge the two groups' partial softmaxes (bounded mbarrier exchange);
     // group g writes head-dim columns 64g .. 64g+63 of the output row.
