@@ -410,6 +410,8 @@ def run_config2(args) -> None:
     metric_ms = _timed(lambda: reblock.metric_factors(q, k, samples), 3, 1, stream)
     transform_ms = _timed(lambda: reblock.transform(q, k, factors, T), 3, 1, stream)
     tree_ms = _timed(lambda: plan.run(features), 3, 1, stream)
+    reblock.transform(q, k, factors, T, out=plan.features_buffer(2 * heads))
+    tree_graph_ms = _timed(lambda: plan.replay(2 * heads), 3, 1, stream)  # captured CUDA graph
     qp, qi, kp, ki, _ = reblock.qk_block_permutations(q, k, T, grid)
     permute_ms = _timed(lambda: [ops.headwise_permute(t, p, T) for t, p in ((q, qp), (k, kp), (v, kp))], 3, 1,
                         stream)
@@ -430,6 +432,7 @@ def run_config2(args) -> None:
                     l2="inputs (3 x 2.0 GB) exceed the 126 MB L2; no flush between steps"),
         ms_per_layer=ms,
         stages_ms=dict(reblock_metric=metric_ms, reblock_transform=transform_ms, reblock_tree=tree_ms,
+                       reblock_tree_graph=tree_graph_ms,
                        qkv_permutes=permute_ms),
         roofline=dict(bound="hbm", kernel="reblock_transform_kernel", achieved=transform_bytes / (transform_ms * 1e-3) / 1e9,
                       peak=peaks["hbm"], unit="GB/s",

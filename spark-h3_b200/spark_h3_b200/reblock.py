@@ -148,6 +148,9 @@ class ReblockPlan:
         self.num_excluded = tokens % BLOCK
         self.active_tokens = tokens - self.num_excluded
         self._workspace: dict[int, torch.Tensor] = {}
+        self._features: dict[int, torch.Tensor] = {}
+        self._graphs: dict[int, tuple] = {}  # rows -> (graph, features, perm, inverse)
+        self._eager_runs: dict[int, int] = {}
 
     def workspace(self, rows: int) -> torch.Tensor:
         ws = self._workspace.get(rows)
@@ -177,6 +180,41 @@ class ReblockPlan:
                       self.plan_device.data_ptr(), ws.data_ptr(), ws.numel(), perm.data_ptr(), inverse.data_ptr(),
                       _stream(device))
         return perm, inverse
+
+
+    def features_buffer(self, rows: int) -> torch.Tensor:
+        """The static features buffer [rows, tokens, 128] bf16 that replay() reads."""
+        buf = self._features.get(rows)
+        if buf is None:
+            buf = torch.empty((rows, self.tokens, 128), dtype=torch.bfloat16, device=self.device)
+            self._features[rows] = buf
+        return buf
+
+    def replay(self, rows: int) -> tuple[torch.Tensor, torch.Tensor]:
+        """The tree over features_buffer(rows) as one CUDA graph launch, like the reference's
+        prepared permutation (landmark_tree_v2.py:904-1172): the first call of a row count runs
+        eagerly (module loading, kernel attributes), the second captures the launch sequence,
+        later calls replay it.  Returns copies of (permutation, inverse) int32 [rows, tokens]."""
+        features = self.features_buffer(rows)
+        entry = self._graphs.get(rows)
+        if entry is None:
+            runs = self._eager_runs.get(rows, 0)
+            if runs == 0:
+                self._eager_runs[rows] = 1
+                perm, inverse = self.run(features)
+                return perm, inverse
+            perm = torch.empty((rows, self.tokens), dtype=torch.int32, device=self.device)
+            inverse = torch.empty_like(perm)
+            self.workspace(rows)
+            graph = torch.cuda.CUDAGraph()
+            torch.cuda.current_stream(self.device).synchronize()
+            with torch.cuda.device(self.device), torch.cuda.graph(graph):
+                self.run(features, perm, inverse)
+            entry = (graph, features, perm, inverse)
+            self._graphs[rows] = entry
+        graph, _, perm, inverse = entry
+        graph.replay()
+        return perm.clone(), inverse.clone()
 
 
 @dataclass(frozen=True)
@@ -262,13 +300,17 @@ def metric_factors(q: torch.Tensor, k: torch.Tensor, samples: torch.Tensor, ridg
     return factors
 
 
-def transform(q: torch.Tensor, k: torch.Tensor, factors: torch.Tensor, video_tokens: int) -> torch.Tensor:
+def transform(q: torch.Tensor, k: torch.Tensor, factors: torch.Tensor, video_tokens: int,
+              out: torch.Tensor | None = None) -> torch.Tensor:
     """Reblock features [2*B*H, video, 128] bf16 = [K . bf16(Lq) ; Q . bf16(Lk)]."""
-    device = _require_cuda(q, k, factors)
+    device = _require_cuda(q, k, factors, out)
     if q.dtype != torch.bfloat16 or k.dtype != torch.bfloat16:
         raise RuntimeError("the reblock transform takes bf16 Q/K")
     B, T, H, D = q.shape
-    features = torch.empty((2 * B * H, video_tokens, D), dtype=torch.bfloat16, device=device)
+    shape = (2 * B * H, video_tokens, D)
+    if out is not None and (tuple(out.shape) != shape or out.dtype != torch.bfloat16 or not out.is_contiguous()):
+        raise ValueError(f"out must be contiguous bf16 {shape}")
+    features = torch.empty(shape, dtype=torch.bfloat16, device=device) if out is None else out
     with torch.cuda.device(device):
         _lib.call("sb_reblock_transform", q.data_ptr(), k.data_ptr(), B, T, H, D, video_tokens, factors.data_ptr(),
                   features.data_ptr(), _stream(device))
@@ -280,10 +322,11 @@ _SAMPLES: dict[tuple, torch.Tensor] = {}
 
 def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, grid, *, children=16,
                           fanout_mode: str = "power_of_two_fanout", final_fanout=None, root_fanout=None,
-                          ridge: float = 1e-3, initial_order: str = "flat"):
+                          ridge: float = 1e-3, initial_order: str = "flat", use_graph: bool = True):
     """Paired opposite-second-moment Q/K permutations (spark_integration.py:394-851 with
     layout reuse "independent"): returns (q_perm, q_inv, k_perm, k_inv), int32 [B, H, video],
-    plus the reblock hierarchy."""
+    plus the reblock hierarchy.  With use_graph the tree replays a captured CUDA graph over
+    the plan's static features buffer (the transform writes into it)."""
     device = _require_cuda(q, k)
     B, T, H, D = q.shape
     grid = _grid_tuple(grid)
@@ -294,9 +337,12 @@ def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, g
         samples = torch.from_numpy(ids.astype(np.int32)).to(device)
         _SAMPLES[key] = samples
     factors = metric_factors(q, k, samples, ridge)
-    features = transform(q, k, factors, video_tokens)
     plan = _plan(video_tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device)
-    perm, inverse = plan.run(features)
+    if use_graph:
+        transform(q, k, factors, video_tokens, out=plan.features_buffer(2 * B * H))
+        perm, inverse = plan.replay(2 * B * H)
+    else:
+        perm, inverse = plan.run(transform(q, k, factors, video_tokens))
     BH = B * H
     shape = (B, H, video_tokens)
     return (perm[BH:].view(shape), inverse[BH:].view(shape), perm[:BH].view(shape), inverse[:BH].view(shape),

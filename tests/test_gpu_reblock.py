@@ -144,3 +144,20 @@ def test_full_mode_layer(cuda_device):
     cos = torch.nn.functional.cosine_similarity(out.float().flatten(), expected.flatten(), dim=0).item()
     assert diff <= 2e-2 and cos >= 0.9995
     assert controller.counts["sol_landmark_preprocess_calls"] == 1
+
+
+def test_graph_replay_matches_eager(cuda_device):
+    """qk_block_permutations through the captured CUDA graph (first call eager, second
+    captures, later calls replay) gives the eager pipeline's permutations, bit for bit, on
+    new Q/K every call."""
+    grid, H = (3, 16, 40), 2
+    T = grid[0] * grid[1] * grid[2]
+    for seed in (11, 12, 13, 14):
+        q, k, _ = make_qkv(grid, H, 128, seed=seed, dtype=torch.bfloat16, clustered=True, device=cuda_device)
+        graph = reblock.qk_block_permutations(q, k, T, grid, use_graph=True)
+        eager = reblock.qk_block_permutations(q, k, T, grid, use_graph=False)
+        torch.cuda.synchronize()
+        for a, b in zip(graph[:4], eager[:4]):
+            assert torch.equal(a, b)
+    plan = reblock._plan(T, 16, grid, "power_of_two_fanout", None, None, "flat", q.device)
+    assert 2 * H in plan._graphs  # the later calls replayed a captured graph
