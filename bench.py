@@ -443,6 +443,43 @@ def run_config2(args) -> None:
     print(json.dumps(line), flush=True)
 
 
+def run_tails(args) -> None:
+    """The Spark layer at config-1 size (N = 124,992, H = 32, D = 128, bf16) with the
+    reference's 64-token blocks, per tail granularity (query / block / block8x8) and summary
+    numerics: CUDA-event ms per layer, inputs resident in HBM."""
+    import torch
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.synthetic import make_qkv
+
+    if args.gpus != 1:
+        raise SystemExit("--workload tails runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else GRID
+    heads = args.heads or HEADS
+    q, k, v = make_qkv(grid, heads, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
+    out = torch.empty_like(q)
+    stream = torch.cuda.current_stream(dev)
+    cases = [("query", "tensorcore", "stored"), ("query", "comfy_fp32", "pre_round"), ("block", "tensorcore", "stored"),
+             ("block8x8", "tensorcore", "stored")]
+    ms = {}
+    with ClockSampler(0) as clocks:
+        for tail, math_, key in cases:
+            layer = lambda: ops.spark_layer(q, k, v, block=64, topk_ratio=TOPK_RATIO, out=out, tail_granularity=tail,
+                                            summary_math=math_, logmass_key=key)
+            ms[f"{tail}/{math_}/{key}"] = _timed(layer, args.steps, args.warmup, stream)
+    status = ops.read_device_status(dev)
+    T = q.shape[1]
+    print(json.dumps(dict(
+        metric="Spark layer ms per tail granularity and summary numerics (ablations)", value=ms["block/tensorcore/stored"],
+        unit="ms", n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms["block/tensorcore/stored"],
+        higher_is_better=False, scaling="strong", vs_baseline=None, dtype="bf16",
+        data="synthetic (seeded 8-sinusoid + 0.3 N(0,1) Q/K/V)",
+        config=dict(workload=f"tails: N={T} ({'x'.join(map(str, grid))}), H={heads}, D=128, block 64, topk {TOPK_RATIO}"),
+        ms_per_layer=ms, clocks=clocks.summary(), device_status=status)), flush=True)
+
+
 def run_fp8(args) -> None:
     """e4m3 linears with per-token x per-output-channel scales."""
     import torch
@@ -606,9 +643,9 @@ def main():
     ap.add_argument("--heads", type=int, default=None, help="head count for a smaller profiling case")
     ap.add_argument("--profile-only", action="store_true",
                     help="run only the device-resident steps (for ncu captures of a small case)")
-    ap.add_argument("--workload", choices=("config1", "config2", "fp8", "config4"), default="config1",
+    ap.add_argument("--workload", choices=("config1", "config2", "fp8", "config4", "tails"), default="config1",
                     help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3), "
-                         "config4 (DiT block stack, multi-GPU with torchrun)")
+                         "config4 (DiT block stack, multi-GPU with torchrun), tails (tail granularity ablations)")
     ap.add_argument("--spark-mode", default="full", help="Spark mode of the config-4 sparse steps")
     ap.add_argument("--fp8-rows", type=int, default=124992, help="token rows M of the fp8 workload")
     ap.add_argument("--reference-sample-blocks", type=int, default=16,
@@ -629,6 +666,8 @@ def main():
         run_fp8(args)
     elif args.workload == "config4":
         run_config4(args)
+    elif args.workload == "tails":
+        run_tails(args)
     else:
         run_ours(args)
 

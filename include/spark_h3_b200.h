@@ -78,11 +78,18 @@ int sb_query_anchor(const float* qc, int B, int NB, int H, int D, int block,
  * weighted_kv != 0: AK/AV are softmax(anchor . k / sqrt(D))-weighted means, else plain
  * means.  mass_bias != 0: LM = logsumexp(a.k/sqrt(D)) - a.AK_stored/sqrt(D), else
  * LM = log(rows in block).  Any of kc / ak / av / lm may be NULL to skip that output
- * (anchor may be NULL when ak, av and lm are all NULL).
+ * (anchor may be NULL when ak, av and lm are all NULL).  numerics selects the reference's
+ * summary ablations (sol_numerator_virtual_q.py:93-193, processor.py:61-68): 0 is its
+ * default (probabilities rounded to the K/V dtype in the weighted sums, LM shift from the
+ * stored key); SB_SUMMARY_PRE_ROUND_LOGMASS takes the shift from the fp32 key mean
+ * (sol_reweight_logmass_key = "pre_round"); SB_SUMMARY_FP32_WEIGHTS keeps the
+ * probabilities in fp32 (sol_reweight_summary_math = "comfy_fp32").
  */
+#define SB_SUMMARY_PRE_ROUND_LOGMASS 1
+#define SB_SUMMARY_FP32_WEIGHTS 2
 int sb_pool_keys_summaries(const void* k, const void* v, const void* anchor,
                            int dtype, int anchor_dtype, int B, int T, int H, int D,
-                           int block, int weighted_kv, int mass_bias,
+                           int block, int weighted_kv, int mass_bias, int numerics,
                            void* kc, void* ak, void* av, float* lm, void* stream);
 
 /*
@@ -134,7 +141,9 @@ int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dtype, int B, 
  *     over every key block kb not in E; O = softmax(logits) @ [V ; AV].
  *   rows >= query_tokens attend every key exactly (the dense suffix).
  * packed_route: [B, QB, H, ceil(NB/32)] with QB >= query_tokens / block.
- * ak/av/lm: summaries of the single global parent ([B, H, NB, D] / [B, H, NB]).
+ * ak/av/lm: summaries of the single global parent ([B, H, NB, D] / [B, H, NB]); all three
+ * NULL leaves the summary columns out, so routed rows attend their exact blocks only (the
+ * exact_attention stage of the reference's block tails, sol_numerator_virtual_q.py:655-660).
  * lse may be NULL.
  */
 int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype,
@@ -153,6 +162,36 @@ int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype,
  */
 int sb_dense_rows_attention(const void* q, const void* k, const void* v, int dtype, int B, int T, int H, int D,
                             int row_lo, int row_hi, void* out, float* lse, void* stream);
+
+/*
+ * Eight-key anchor summaries for the block8x8 tail.  Replaces sol_numerator_virtual_q.py:
+ * 193-242 (_summaries_block8) for the global parent: per group of 8 keys g (the last may be
+ * short), p = 2^(a.k / sqrt(D) log2 e - max) in fp32, AK8 = sum p k / sum p and AV8 likewise
+ * (plain means without weighted_kv), stored bf16; LM8 = (max + log2 sum p) ln 2 -
+ * a.AK8 / sqrt(D) with the stored key (SB_SUMMARY_PRE_ROUND_LOGMASS: the fp32 mean), or
+ * log(keys in the group) without mass_bias.  K, V [B, T, H, 128] bf16; anchor [B, H, 128]
+ * (anchor_dtype); ak8, av8 [B, H, ceil(T/8), 128] bf16; lm8 [B, H, ceil(T/8)] fp32.
+ */
+int sb_tail_summaries8(const void* k, const void* v, const void* anchor, int dtype, int anchor_dtype, int B, int T,
+                       int H, int D, int weighted_kv, int mass_bias, int numerics, void* ak8, void* av8, float* lm8,
+                       void* stream);
+
+/*
+ * Pooled tail merge for the tail granularities "block" (group_tokens = entry_tokens = block)
+ * and "block8x8" (8 and 8).  Replaces sol_numerator_virtual_q.py:415-499
+ * (_skip_merge_chunk_block, _skip_merge_chunk_block8) for the global parent.  out / lse hold
+ * the exact-keys-only output and its LSE (sb_sparse_attention without summaries) and are
+ * updated in place for the routed rows (< query_tokens): per query group of group_tokens
+ * rows, the mean query (fp32, rounded to bf16) takes an online softmax over the summary
+ * entries (ak, av [B, H, ceil(T / entry_tokens), 128] bf16, lm fp32) whose key block
+ * (entry * entry_tokens / block) is not exact for the group's query block, and each row
+ * becomes (we * out + wa * tail) / (we + wa), with we, wa = exp(lse_exact - m),
+ * exp(lse_tail - m), m their max; lse becomes m + log(we + wa).
+ */
+int sb_tail_merge(const void* q, const void* ak, const void* av, const float* lm, int dtype, int B, int T, int H,
+                  int D, int entry_tokens, int group_tokens, int block, const int32_t* packed_route, int QB,
+                  int query_tokens, int sink_first, int sink_last, int local_radius, void* out, float* lse,
+                  void* stream);
 
 /*
  * Head-wise token permutation of the video prefix.  Replaces

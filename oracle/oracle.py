@@ -172,8 +172,13 @@ def target_topk(ratio: float, candidates: int) -> int:
 
 # ------------------------------------------------------------ float restatements
 def summaries(a: np.ndarray, k: Tensor, v: Tensor, block: int, *, weighted_kv: bool = True,
-              mass_bias: bool = True) -> tuple[np.ndarray, np.ndarray, np.ndarray]:
-    """AK, AV [B, H, NB, D] (stored precision) and LM [B, H, NB] for the global anchor."""
+              mass_bias: bool = True, summary_math: str = "tensorcore",
+              logmass_key: str = "stored") -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """AK, AV [B, H, NB, D] (stored precision) and LM [B, H, NB] for the global anchor
+    (sol_numerator_virtual_q.py:93-193).  summary_math "tensorcore" rounds the
+    probabilities to the K/V dtype before the weighted sums, "comfy_fp32" keeps them in
+    fp32; logmass_key "stored" takes the LM shift from the stored key, "pre_round" from the
+    unrounded mean."""
     B, T, H, D = k.shape
     nb = -(-T // block)
     kf, vf = k.float().astype(np.float64), v.float().astype(np.float64)
@@ -191,7 +196,7 @@ def summaries(a: np.ndarray, k: Tensor, v: Tensor, block: int, *, weighted_kv: b
             p = np.exp2(logits - mx)
             den = p.sum(-1)
         if weighted_kv:
-            w = store(p, k.dtype).astype(np.float64)
+            w = (p if summary_math == "comfy_fp32" else store(p, k.dtype)).astype(np.float64)
             key = np.einsum("bhr,brhd->bhd", w, kk) / den[..., None]
             val = np.einsum("bhr,brhd->bhd", w, vv) / den[..., None]
         else:
@@ -200,11 +205,90 @@ def summaries(a: np.ndarray, k: Tensor, v: Tensor, block: int, *, weighted_kv: b
         ak[:, :, j] = store(key, k.dtype)
         av[:, :, j] = store(val, v.dtype)
         if mass_bias:
-            shift = np.einsum("bhd,bhd->bh", a.astype(np.float64), ak[:, :, j].astype(np.float64)) * scale
+            shift_key = key if logmass_key == "pre_round" else ak[:, :, j].astype(np.float64)
+            shift = np.einsum("bhd,bhd->bh", a.astype(np.float64), shift_key) * scale
             lm[:, :, j] = (mx[..., 0] + np.log2(den)) * LN2 - shift
         else:
             lm[:, :, j] = math.log(count)
     return ak, av, lm
+
+
+def summaries8(a: np.ndarray, k: Tensor, v: Tensor, *, weighted_kv: bool = True, mass_bias: bool = True,
+               logmass_key: str = "stored") -> tuple[np.ndarray, np.ndarray, np.ndarray]:
+    """Eight-key anchor summaries of the block8x8 tail (sol_numerator_virtual_q.py:193-242):
+    fp32 probabilities, keys and values stored at the K/V precision, LM from the stored key
+    (or the fp32 mean with logmass_key "pre_round")."""
+    B, T, H, D = k.shape
+    n8 = -(-T // 8)
+    kf, vf = k.float().astype(np.float64), v.float().astype(np.float64)
+    scale = D ** -0.5
+    ak = np.empty((B, H, n8, D), dtype=np.float32)
+    av = np.empty_like(ak)
+    lm = np.empty((B, H, n8), dtype=np.float32)
+    for g in range(n8):
+        kk, vv = kf[:, 8 * g:8 * g + 8], vf[:, 8 * g:8 * g + 8]
+        count = kk.shape[1]
+        logits = np.einsum("bhd,brhd->bhr", a.astype(np.float64), kk) * scale * LOG2E
+        mx = logits.max(-1)
+        p = np.exp2(logits - mx[..., None])
+        den = np.maximum(p.sum(-1), 1e-30)
+        if weighted_kv:
+            key = np.einsum("bhr,brhd->bhd", p, kk) / den[..., None]
+            val = np.einsum("bhr,brhd->bhd", p, vv) / den[..., None]
+        else:
+            key, val = kk.mean(1), vv.mean(1)
+        ak[:, :, g] = store(key, k.dtype)
+        av[:, :, g] = store(val, v.dtype)
+        if mass_bias:
+            shift_key = key if logmass_key == "pre_round" else ak[:, :, g].astype(np.float64)
+            lm[:, :, g] = (mx + np.log2(den)) * LN2 - np.einsum("bhd,bhd->bh", a.astype(np.float64), shift_key) * scale
+        else:
+            lm[:, :, g] = math.log(count)
+    return ak, av, lm
+
+
+def tail_merge(q: Tensor, exact_out: np.ndarray, exact_lse: np.ndarray, ak: np.ndarray, av: np.ndarray,
+               lm: np.ndarray, packed: np.ndarray, *, block: int, entry_tokens: int, group_tokens: int,
+               query_tokens: int, sink_first: int, sink_last: int, local_radius: int = -1,
+               heads: list[int] | None = None) -> tuple[np.ndarray, np.ndarray]:
+    """Pooled-tail merge (sol_numerator_virtual_q.py:415-499): per query group, the mean query
+    (fp32, stored at Q's precision) attends the summary entries whose key block is not exact;
+    rows blend that with their exact output by their LSE weights."""
+    B, T, H, D = q.shape
+    nb = -(-T // block)
+    out, lse = exact_out.copy(), exact_lse.copy()
+    qf = q.float()
+    scale = D ** -0.5
+    heads = list(range(H)) if heads is None else heads
+    n_entries = ak.shape[2]
+    entry_block = (np.arange(n_entries) * entry_tokens) // block
+    for b in range(B):
+        for h in heads:
+            for g0 in range(0, query_tokens, group_tokens):
+                rows = slice(g0, min(g0 + group_tokens, T))
+                qb = g0 // block
+                qmean = store(qf[b, rows, h].astype(np.float64).mean(0), q.dtype).astype(np.float64)
+                exact = exact_blocks(packed[b, qb, h], qb, nb, sink_first, sink_last, local_radius)
+                live = ~exact[entry_block]
+                if live.any():
+                    score = ak[b, h][live].astype(np.float64) @ qmean * scale + lm[b, h][live]
+                    m = score.max()
+                    p = np.exp(score - m)
+                    tail = p @ av[b, h][live].astype(np.float64) / p.sum()
+                    al = m + np.log(p.sum())
+                else:
+                    tail, al = np.zeros(D), -np.inf
+                el = exact_lse[b, rows, h].astype(np.float64)
+                mx = np.maximum(el, al)
+                with np.errstate(invalid="ignore"):
+                    we = np.where(np.isfinite(mx), np.exp(el - mx), 0.0)
+                    wa = np.where(np.isfinite(mx), np.exp(al - mx), 0.0)
+                tot = we + wa
+                blend = (we[:, None] * exact_out[b, rows, h] + wa[:, None] * tail[None, :]) / np.maximum(tot, 1e-30)[:, None]
+                out[b, rows, h] = blend.astype(np.float32)
+                with np.errstate(divide="ignore"):
+                    lse[b, rows, h] = np.where(tot > 0, mx + np.log(np.maximum(tot, 1e-300)), -np.inf).astype(np.float32)
+    return out, lse
 
 
 def exact_blocks(packed_row: np.ndarray, qb: int, nb: int, sink_first: int, sink_last: int,
@@ -239,9 +323,10 @@ def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.nda
         for h in heads:
             kh = kf[b, :, h].astype(np.float64)
             vh = vf[b, :, h].astype(np.float64)
-            akh = ak[b, h].astype(np.float64)
-            avh = av[b, h].astype(np.float64)
-            lmh = lm[b, h].astype(np.float64)
+            # ak/av/lm None: routed rows see their exact blocks only (no summary columns)
+            akh = ak[b, h].astype(np.float64) if ak is not None else np.zeros((nb, D))
+            avh = av[b, h].astype(np.float64) if av is not None else np.zeros((nb, D))
+            lmh = lm[b, h].astype(np.float64) if lm is not None else np.zeros(nb)
             start = r0
             while start < r1:
                 if start < query_tokens:
@@ -253,11 +338,17 @@ def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.nda
                     stop = r1
                     exact = np.ones(nb, dtype=bool)
                 tok = np.repeat(exact, block)[:T]
-                keys = np.concatenate([kh[tok], akh[~exact]])
-                vals = np.concatenate([vh[tok], avh[~exact]])
+                summ = ~exact if ak is not None else np.zeros(nb, dtype=bool)
+                keys = np.concatenate([kh[tok], akh[summ]])
+                vals = np.concatenate([vh[tok], avh[summ]])
                 qq = qf[b, start:stop, h].astype(np.float64)
                 logits = qq @ keys.T * scale
-                logits[:, int(tok.sum()):] += lmh[~exact]
+                logits[:, int(tok.sum()):] += lmh[summ]
+                if logits.shape[1] == 0:  # nothing visible
+                    out[b, start:stop, h] = 0.0
+                    lse[b, start:stop, h] = -np.inf
+                    start = stop
+                    continue
                 mx = logits.max(-1, keepdims=True)
                 p = np.exp(logits - mx)
                 den = p.sum(-1, keepdims=True)
@@ -286,7 +377,8 @@ def padded_tail(q: Tensor, video: int, query_tokens: int, block: int) -> Tensor:
 def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: float, video_tokens: int | None = None,
                 anchor_dtype: str | None = None, local_radius: int = -1, weighted_kv: bool = True,
                 mass_bias: bool = True, attention: bool = True, rows: slice | None = None,
-                heads: list[int] | None = None, tail_mode: str = "dense") -> dict:
+                heads: list[int] | None = None, tail_mode: str = "dense", tail_granularity: str = "query",
+                summary_math: str = "tensorcore", logmass_key: str = "stored") -> dict:
     """Route, summaries and (optionally) attention of one Spark layer, as the CUDA path does.
 
     tail_mode "pad" (spark_integration.py:72-91, 935-938, 1173-1187, 1238-1260): the query
@@ -315,9 +407,25 @@ def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: floa
     idx, packed = topk(sc, kk, nb)
     result = dict(qc=qc, kc=kc, anchor=a, scores=sc, indices=idx, packed=packed, topk=kk,
                   query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last)
-    ak, av, lm = summaries(a, k, v, block, weighted_kv=weighted_kv, mass_bias=mass_bias)
+    ak, av, lm = summaries(a, k, v, block, weighted_kv=weighted_kv, mass_bias=mass_bias,
+                           summary_math=summary_math, logmass_key=logmass_key)
     result.update(ak=ak, av=av, lm=lm)
-    if attention:
+    if attention and tail_granularity != "query":
+        # Exact keys only, then the pooled tail merged in (sol_numerator_virtual_q.py:655-660).
+        if tail_mode != "dense":
+            raise NotImplementedError("the oracle's pooled tails use tail_mode 'dense'")
+        eo, el = sparse_attention(q, k, v, block, packed, None, None, None, query_tokens, sink_first, sink_last,
+                                  local_radius, rows=rows, heads=heads)
+        if tail_granularity == "block":
+            tak, tav, tlm, entry, group = ak, av, lm, block, block
+        else:
+            tak, tav, tlm = summaries8(a, k, v, weighted_kv=weighted_kv, mass_bias=mass_bias, logmass_key=logmass_key)
+            entry, group = 8, 8
+        out, lse = tail_merge(q, np.nan_to_num(eo), el, tak, tav, tlm, packed, block=block, entry_tokens=entry,
+                              group_tokens=group, query_tokens=query_tokens, sink_first=sink_first,
+                              sink_last=sink_last, local_radius=local_radius, heads=heads)
+        result.update(out=out, lse=lse)
+    elif attention:
         out, lse = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens, sink_first, sink_last,
                                     local_radius, rows=rows, heads=heads)
         if query_tokens > video:

@@ -52,7 +52,7 @@ sparse_attention_simt_kernel(AttnParams p) {
         for (int i = 0; i < PER; ++i) acc[i] = acc[i] * alpha + pr * Elem<T>::to_f(v[koff + lane + 32 * i]);
         m = m_new;
       }
-    } else {
+    } else if (p.lm != nullptr) {  // without summaries, routed rows see their exact keys only
       const int64_t soff = (((int64_t)b * p.H + h) * p.NB + kb) * D;
       float part = 0.f;
 #pragma unroll

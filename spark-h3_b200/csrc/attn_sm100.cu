@@ -253,7 +253,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
     ubits[w] = bits;
   }
-  const bool any_routed = row0 < p.query_tokens;
+  const bool any_routed = row0 < p.query_tokens && p.lm != nullptr;  // summaries present
   for (int e = tid; e < nb_pad; e += kThreads)
     lm_s[e] = (any_routed && e < p.NB) ? __ldg(p.lm + ((int64_t)b * p.H + h) * p.NB + e) * kLog2e : 0.f;
   __syncthreads();
@@ -281,7 +281,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       C.exact_granules = cnt;
       const bool routed0 = row0 < p.query_tokens && row0 < p.T;
       const bool routed1 = row0 + 64 < p.query_tokens && row0 + 64 < p.T;
-      C.has_summary = (routed0 || routed1) ? 1 : 0;
+      C.has_summary = (routed0 || routed1) && p.lm != nullptr ? 1 : 0;  // no summaries: exact keys only
     }
   }
   tc_fence_before();

@@ -91,7 +91,9 @@ extern "C" int sb_sparse_attention(const void* q, const void* k, const void* v, 
   const int NB = ceil_div(T, block);
   const int routed_blocks = query_tokens / block;
   if (routed_blocks > 0) {
-    SB_CHECK_ARG(packed_route && ak && av && lm, "sb_sparse_attention: routed queries need the route and summaries");
+    SB_CHECK_ARG(packed_route, "sb_sparse_attention: routed queries need the route");
+    SB_CHECK_ARG((ak && av && lm) || (!ak && !av && !lm),
+                 "sb_sparse_attention: pass all of AK, AV and LM, or none (exact keys only)");
     SB_CHECK_ARG(QB >= routed_blocks && QB <= NB, "sb_sparse_attention: QB (%d) must lie in [%d, %d]", QB, routed_blocks, NB);
   }
   SB_CHECK_ARG(sink_first >= 0 && sink_first <= sink_last && sink_last <= NB,

@@ -107,7 +107,7 @@ template <typename T, typename TA, int D>
 __global__ void __launch_bounds__(256)
 pool_keys_summaries_kernel(const T* __restrict__ k, const T* __restrict__ v,
                            const TA* __restrict__ anchor, int T_, int H, int block,
-                           int weighted_kv, int mass_bias, T* __restrict__ kc,
+                           int weighted_kv, int mass_bias, int numerics, T* __restrict__ kc,
                            T* __restrict__ ak, T* __restrict__ av, float* __restrict__ lm) {
   constexpr int G = D / kCPT;  // threads per head
   extern __shared__ float plog[];  // [H][block] logits, then probabilities
@@ -230,7 +230,10 @@ pool_keys_summaries_kernel(const T* __restrict__ k, const T* __restrict__ v,
     float x[kCPT], y[kCPT];
     load16<T>(kbase + (int64_t)r * HD, x);
     load16<T>(vbase + (int64_t)r * HD, y);
-    const float w = weighted_kv ? Elem<T>::to_f(Elem<T>::from_f(plog[h * block + r])) : 1.f;
+    // The probability enters the weighted sums rounded to the K/V dtype (the reference's
+    // tensor-core summaries), or in fp32 with SB_SUMMARY_FP32_WEIGHTS (its comfy_fp32 mode).
+    const float pr = plog[h * block + r];
+    const float w = weighted_kv ? ((numerics & SB_SUMMARY_FP32_WEIGHTS) ? pr : Elem<T>::to_f(Elem<T>::from_f(pr))) : 1.f;
 #pragma unroll
     for (int i = 0; i < kCPT; ++i) {
       sk[i] = fmaf(w, x[i], sk[i]);
@@ -242,9 +245,12 @@ pool_keys_summaries_kernel(const T* __restrict__ k, const T* __restrict__ v,
   float shift = 0.f;
 #pragma unroll
   for (int i = 0; i < kCPT; ++i) {
-    key_out[i] = Elem<T>::to_f(Elem<T>::from_f(sk[i] / norm));
+    const float key = sk[i] / norm;
+    key_out[i] = Elem<T>::to_f(Elem<T>::from_f(key));
     val_out[i] = sv[i] / norm;
-    shift = fmaf(a[i], key_out[i], shift);
+    // The log-mass shift uses the stored (rounded) key, or the fp32 mean with
+    // SB_SUMMARY_PRE_ROUND_LOGMASS.
+    shift = fmaf(a[i], (numerics & SB_SUMMARY_PRE_ROUND_LOGMASS) ? key : key_out[i], shift);
   }
   const int64_t srow = (((int64_t)b * H + h) * NB + kb) * D + dcol;
   if (ak && active) {
@@ -307,8 +313,8 @@ extern "C" int sb_query_anchor(const float* qc, int B, int NB, int H, int D, int
 
 template <typename T, typename TA, int D>
 static int launch_pool_keys(const void* k, const void* v, const void* anchor, int B, int tokens, int H,
-                            int block, int weighted_kv, int mass_bias, void* kc, void* ak, void* av,
-                            float* lm, cudaStream_t s) {
+                            int block, int weighted_kv, int mass_bias, int numerics, void* kc, void* ak,
+                            void* av, float* lm, cudaStream_t s) {
   const int NB = ceil_div(tokens, block);
   const int threads = ceil_div(H * D / kCPT, 32) * 32;
   if (threads > 256 || H > 64) {
@@ -321,21 +327,23 @@ static int launch_pool_keys(const void* k, const void* v, const void* anchor, in
   if (err != cudaSuccess) return cuda_error(err, "sb_pool_keys_summaries: set smem");
   dim3 grid(NB, B);
   kern<<<grid, threads, smem, s>>>((const T*)k, (const T*)v, (const TA*)anchor, tokens, H, block, weighted_kv,
-                              mass_bias, (T*)kc, (T*)ak, (T*)av, lm);
+                              mass_bias, numerics, (T*)kc, (T*)ak, (T*)av, lm);
   SB_CHECK_LAUNCH("sb_pool_keys_summaries launch");
   return SB_OK;
 }
 
 extern "C" int sb_pool_keys_summaries(const void* k, const void* v, const void* anchor, int dtype,
                                       int anchor_dtype, int B, int T, int H, int D, int block,
-                                      int weighted_kv, int mass_bias, void* kc, void* ak, void* av,
-                                      float* lm, void* stream) {
+                                      int weighted_kv, int mass_bias, int numerics, void* kc, void* ak,
+                                      void* av, float* lm, void* stream) {
   const bool want_sum = ak || av || lm;
   SB_CHECK_ARG(k, "sb_pool_keys_summaries: null K");
   SB_CHECK_ARG(!want_sum || v, "sb_pool_keys_summaries: summaries need V");
   SB_CHECK_ARG(!want_sum || !(weighted_kv || mass_bias) || anchor,
                "sb_pool_keys_summaries: weighted summaries need the anchor");
   SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_pool_keys_summaries: bad dtype");
+  SB_CHECK_ARG((numerics & ~(SB_SUMMARY_PRE_ROUND_LOGMASS | SB_SUMMARY_FP32_WEIGHTS)) == 0,
+               "sb_pool_keys_summaries: unknown numerics flags %d", numerics);
   SB_CHECK_ARG(anchor_dtype == SB_F32 || anchor_dtype == SB_BF16, "sb_pool_keys_summaries: bad anchor dtype");
   SB_CHECK_ARG(B > 0 && T > 0 && H > 0, "sb_pool_keys_summaries: B, T, H must be positive");
   SB_CHECK_ARG(D == 64 || D == 128, "sb_pool_keys_summaries: head dim must be 64 or 128");
@@ -346,13 +354,13 @@ extern "C" int sb_pool_keys_summaries(const void* k, const void* v, const void* 
   const bool abf = anchor_dtype == SB_BF16;
   if (dtype == SB_BF16) {
     if (D == 128)
-      return abf ? launch_pool_keys<__nv_bfloat16, __nv_bfloat16, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, kc, ak, av, lm, s)
-                 : launch_pool_keys<__nv_bfloat16, float, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, kc, ak, av, lm, s);
-    return abf ? launch_pool_keys<__nv_bfloat16, __nv_bfloat16, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, kc, ak, av, lm, s)
-               : launch_pool_keys<__nv_bfloat16, float, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, kc, ak, av, lm, s);
+      return abf ? launch_pool_keys<__nv_bfloat16, __nv_bfloat16, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s)
+                 : launch_pool_keys<__nv_bfloat16, float, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
+    return abf ? launch_pool_keys<__nv_bfloat16, __nv_bfloat16, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s)
+               : launch_pool_keys<__nv_bfloat16, float, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
   }
   SB_CHECK_ARG(!abf, "sb_pool_keys_summaries: float32 K/V need a float32 anchor");
   if (D == 128)
-    return launch_pool_keys<float, float, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, kc, ak, av, lm, s);
-  return launch_pool_keys<float, float, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, kc, ak, av, lm, s);
+    return launch_pool_keys<float, float, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
+  return launch_pool_keys<float, float, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
 }

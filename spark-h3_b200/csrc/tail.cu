@@ -1,0 +1,240 @@
+// Pooled tails of the Spark layer: the reference's tail granularities "block" and "block8x8"
+// (sol_numerator_virtual_q.py:193-242, 415-499, 528-596).  The exact part comes from the
+// attention kernels run without summary columns (exact output and its LSE); here the
+// skipped key blocks are attended once per query group through the group's mean query, and
+// the two partial softmaxes are merged row by row:
+//   tail_summaries8_kernel  anchor-weighted summaries of every 8 keys (block8x8 only)
+//   tail_merge_kernel       per query group (64 or 8 rows): mean query rounded to the Q
+//                           dtype, online softmax over the summary entries whose key block is
+//                           not exact, then out = (we * exact + wa * tail) / (we + wa) with
+//                           we, wa the exponentials of the two LSEs relative to their max.
+#include "common.cuh"
+#include "attn_common.cuh"
+
+namespace sb {
+namespace {
+
+constexpr int kDim = 128;
+constexpr int kTailThreads = 128;  // 4 warps; a lane holds 4 of the 128 dimensions
+
+// One warp per 8-key group (sol_numerator_virtual_q.py:193-242): p = 2^(a.k/sqrt(D) log2 e
+// - max) in fp32, AK = sum p k / sum p, AV likewise (or plain means), stored in the K/V dtype;
+// LM = (max + log2 sum p) ln 2 - a.AK/sqrt(D) with the stored key (or the fp32 mean), or
+// log(keys in the group) without the mass bias.
+template <typename T, typename TA>
+__global__ void __launch_bounds__(kTailThreads) tail_summaries8_kernel(
+    const T* __restrict__ k, const T* __restrict__ v, const TA* __restrict__ anchor, int Tn, int H, int n8,
+    int weighted_kv, int mass_bias, int pre_round, T* __restrict__ ak8, T* __restrict__ av8, float* __restrict__ lm8) {
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int g = blockIdx.x * (kTailThreads / 32) + warp;
+  const int h = blockIdx.y, b = blockIdx.z;
+  if (g >= n8) return;
+  const int d0 = 4 * lane;
+  const int64_t HD = (int64_t)H * kDim;
+  float a[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) a[i] = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * kDim + d0 + i]);
+  const int row0 = 8 * g;
+  const int count = min(8, Tn - row0);
+  const float scale = rsqrtf((float)kDim);
+  float kr[8][4], vr[8][4], logit[8];
+  float mx = -INFINITY;
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) kr[r][i] = vr[r][i] = 0.f;
+    if (r < count) {
+      const int64_t off = ((int64_t)b * Tn + row0 + r) * HD + (int64_t)h * kDim + d0;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        kr[r][i] = Elem<T>::to_f(k[off + i]);
+        vr[r][i] = Elem<T>::to_f(v[off + i]);
+        part = fmaf(kr[r][i], a[i], part);
+      }
+    }
+    logit[r] = r < count ? warp_sum(part) * scale * kLog2e : -INFINITY;  // count is warp-uniform
+    mx = fmaxf(mx, logit[r]);
+  }
+  float den = 0.f, p[8];
+#pragma unroll
+  for (int r = 0; r < 8; ++r) {
+    p[r] = r < count ? exp2f(logit[r] - mx) : 0.f;
+    den += p[r];
+  }
+  den = fmaxf(den, 1e-30f);
+  float key[4], val[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    float sk = 0.f, sv = 0.f;
+#pragma unroll
+    for (int r = 0; r < 8; ++r) {
+      const float w = weighted_kv ? p[r] : (r < count ? 1.f : 0.f);
+      sk = fmaf(w, kr[r][i], sk);
+      sv = fmaf(w, vr[r][i], sv);
+    }
+    const float norm = weighted_kv ? den : (float)count;
+    key[i] = sk / norm;
+    val[i] = sv / norm;
+  }
+  const int64_t so = (((int64_t)b * H + h) * n8 + g) * kDim + d0;
+  float shift = 0.f;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const T ks = Elem<T>::from_f(key[i]);
+    ak8[so + i] = ks;
+    av8[so + i] = Elem<T>::from_f(val[i]);
+    shift = fmaf(a[i], pre_round ? key[i] : Elem<T>::to_f(ks), shift);
+  }
+  shift = warp_sum(shift) * scale;
+  if (lane == 0)
+    lm8[((int64_t)b * H + h) * n8 + g] = mass_bias ? (mx + log2f(den)) * kLn2 - shift : logf((float)count);
+}
+
+// One CTA per (query group, head, batch).  Summary entry e covers keys [e*E, e*E + E) of key
+// block (e*E) / block; an entry is skipped when that block is exact for the group's query
+// block (route bit, sink range or local radius).
+template <typename T>
+__global__ void __launch_bounds__(kTailThreads) tail_merge_kernel(
+    const T* __restrict__ q, const T* __restrict__ tk, const T* __restrict__ tv, const float* __restrict__ lmass,
+    const int32_t* __restrict__ packed, int QB, int words, int Tn, int H, int n_entries, int entry_tokens,
+    int group_tokens, int block, int sink_first, int sink_last, int local_radius, T* __restrict__ out,
+    float* __restrict__ lse) {
+  __shared__ float qmean[kDim];
+  __shared__ float wm[4], wden[4];
+  __shared__ float wacc[4][kDim];
+  __shared__ float row_w[2][kTailThreads];  // per row of the group (at most 128): exact and tail weights
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
+  const int grp = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int row0 = grp * group_tokens;
+  const int rows = min(group_tokens, Tn - row0);
+  const int qb = row0 / block;
+  const int64_t HD = (int64_t)H * kDim;
+  // Mean query of the group, in fp32 and rounded to the Q dtype (the reference's qmean).
+  {
+    float s = 0.f;
+    for (int r = 0; r < rows; ++r) s += Elem<T>::to_f(q[((int64_t)b * Tn + row0 + r) * HD + (int64_t)h * kDim + tid]);
+    qmean[tid] = Elem<T>::to_f(Elem<T>::from_f(s / (float)max(rows, 1)));
+  }
+  __syncthreads();
+  const int32_t* wrow = packed + (((int64_t)b * QB + qb) * H + h) * words;
+  const int d0 = 4 * lane;
+  float qm[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) qm[i] = qmean[d0 + i];
+  const float scale_log2 = rsqrtf((float)kDim) * kLog2e;
+  float m = -INFINITY, den = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  const int64_t ebase = ((int64_t)b * H + h) * n_entries;
+  for (int e = warp; e < n_entries; e += 4) {
+    const int kb = (e * entry_tokens) / block;
+    if (block_is_exact(wrow, kb, qb, sink_first, sink_last, local_radius)) continue;
+    const T* kp = tk + (ebase + e) * kDim + d0;
+    float part = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) part = fmaf(Elem<T>::to_f(kp[i]), qm[i], part);
+    const float score = warp_sum(part) * scale_log2 + lmass[ebase + e] * kLog2e;
+    const float m_new = fmaxf(m, score);
+    const float factor = m == -INFINITY ? 0.f : exp2f(m - m_new);
+    const float pr = exp2f(score - m_new);
+    const T* vp = tv + (ebase + e) * kDim + d0;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[i] = fmaf(acc[i], factor, pr * Elem<T>::to_f(vp[i]));
+    den = den * factor + pr;
+    m = m_new;
+  }
+  if (lane == 0) {
+    wm[warp] = m;
+    wden[warp] = den;
+  }
+#pragma unroll
+  for (int i = 0; i < 4; ++i) wacc[warp][d0 + i] = acc[i];
+  __syncthreads();
+  float M = -INFINITY;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w]);
+  float D = 0.f, A = 0.f;
+#pragma unroll
+  for (int w = 0; w < 4; ++w) {
+    const float f = wm[w] == -INFINITY ? 0.f : exp2f(wm[w] - M);
+    D = fmaf(wden[w], f, D);
+    A = fmaf(wacc[w][tid], f, A);
+  }
+  const bool has_tail = D > 0.f;
+  const float tail = has_tail ? A / D : 0.f;
+  const float al = has_tail ? (M + log2f(D)) * kLn2 : -INFINITY;
+  // Row weights of the merge (one thread per row), then every thread blends its dimension.
+  if (tid < rows) {
+    const int64_t rl = ((int64_t)b * Tn + row0 + tid) * H + h;
+    const float el = lse[rl];
+    const float mx = fmaxf(el, al);
+    const float we = mx == -INFINITY ? 0.f : expf(el - mx);
+    const float wa = mx == -INFINITY ? 0.f : expf(al - mx);
+    row_w[0][tid] = we;
+    row_w[1][tid] = wa;
+    lse[rl] = we + wa > 0.f ? mx + logf(we + wa) : -INFINITY;
+  }
+  __syncthreads();
+  for (int r = 0; r < rows; ++r) {
+    const float we = row_w[0][r], wa = row_w[1][r];
+    const int64_t o = ((int64_t)b * Tn + row0 + r) * HD + (int64_t)h * kDim + tid;
+    const float exact = Elem<T>::to_f(out[o]);
+    const float merged = ((we > 0.f ? we * exact : 0.f) + (wa > 0.f ? wa * tail : 0.f)) / fmaxf(we + wa, 1e-30f);
+    out[o] = Elem<T>::from_f(merged);
+  }
+}
+
+}  // namespace
+}  // namespace sb
+
+using namespace sb;
+
+extern "C" int sb_tail_summaries8(const void* k, const void* v, const void* anchor, int dtype, int anchor_dtype, int B,
+                                  int T, int H, int D, int weighted_kv, int mass_bias, int numerics, void* ak8,
+                                  void* av8, float* lm8, void* stream) {
+  SB_CHECK_ARG(k && v && anchor && ak8 && av8 && lm8, "sb_tail_summaries8: null pointer");
+  SB_CHECK_ARG(dtype == SB_BF16, "sb_tail_summaries8: K/V must be bf16");
+  SB_CHECK_ARG(anchor_dtype == SB_BF16 || anchor_dtype == SB_F32, "sb_tail_summaries8: bad anchor dtype");
+  SB_CHECK_ARG(B > 0 && T > 0 && H > 0 && D == kDim, "sb_tail_summaries8: needs B, T, H > 0 and D = 128");
+  SB_CHECK_ARG((numerics & ~SB_SUMMARY_PRE_ROUND_LOGMASS) == 0,
+               "sb_tail_summaries8: eight-key summaries take only SB_SUMMARY_PRE_ROUND_LOGMASS");
+  const int n8 = ceil_div(T, 8);
+  dim3 grid(ceil_div(n8, kTailThreads / 32), H, B);
+  cudaStream_t s = (cudaStream_t)stream;
+  const int pre = (numerics & SB_SUMMARY_PRE_ROUND_LOGMASS) ? 1 : 0;
+  if (anchor_dtype == SB_BF16)
+    tail_summaries8_kernel<__nv_bfloat16, __nv_bfloat16><<<grid, kTailThreads, 0, s>>>(
+        (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (const __nv_bfloat16*)anchor, T, H, n8, weighted_kv,
+        mass_bias, pre, (__nv_bfloat16*)ak8, (__nv_bfloat16*)av8, lm8);
+  else
+    tail_summaries8_kernel<__nv_bfloat16, float><<<grid, kTailThreads, 0, s>>>(
+        (const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (const float*)anchor, T, H, n8, weighted_kv, mass_bias,
+        pre, (__nv_bfloat16*)ak8, (__nv_bfloat16*)av8, lm8);
+  SB_CHECK_LAUNCH("sb_tail_summaries8 launch");
+  return SB_OK;
+}
+
+extern "C" int sb_tail_merge(const void* q, const void* ak, const void* av, const float* lm, int dtype, int B, int T,
+                             int H, int D, int entry_tokens, int group_tokens, int block,
+                             const int32_t* packed_route, int QB, int query_tokens, int sink_first, int sink_last,
+                             int local_radius, void* out, float* lse, void* stream) {
+  SB_CHECK_ARG(q && ak && av && lm && packed_route && out && lse, "sb_tail_merge: null pointer");
+  SB_CHECK_ARG(dtype == SB_BF16, "sb_tail_merge: Q and the output must be bf16");
+  SB_CHECK_ARG(B > 0 && T > 0 && H > 0 && D == kDim, "sb_tail_merge: needs B, T, H > 0 and D = 128");
+  SB_CHECK_ARG(block == 64 || block == 128, "sb_tail_merge: block must be 64 or 128");
+  SB_CHECK_ARG((entry_tokens == block || entry_tokens == 8) && (group_tokens == block || group_tokens == 8),
+               "sb_tail_merge: entries and query groups are whole blocks or 8 tokens");
+  SB_CHECK_ARG(query_tokens >= 0 && query_tokens <= T && query_tokens % block == 0,
+               "sb_tail_merge: query_tokens must be a block multiple in [0, T]");
+  const int NB = ceil_div(T, block);
+  SB_CHECK_ARG(QB >= query_tokens / block && QB <= NB, "sb_tail_merge: QB out of range");
+  SB_CHECK_ARG(sink_first >= 0 && sink_first <= sink_last && sink_last <= NB, "sb_tail_merge: bad sink range");
+  if (query_tokens == 0) return SB_OK;
+  const int n_entries = ceil_div(T, entry_tokens);
+  dim3 grid(query_tokens / group_tokens, H, B);
+  tail_merge_kernel<__nv_bfloat16><<<grid, kTailThreads, 0, (cudaStream_t)stream>>>(
+      (const __nv_bfloat16*)q, (const __nv_bfloat16*)ak, (const __nv_bfloat16*)av, lm, packed_route, QB,
+      ceil_div(NB, 32), T, H, n_entries, entry_tokens, group_tokens, block, sink_first, sink_last, local_radius,
+      (__nv_bfloat16*)out, lse);
+  SB_CHECK_LAUNCH("sb_tail_merge launch");
+  return SB_OK;
+}

@@ -23,6 +23,10 @@ _i = ctypes.c_int
 _f = ctypes.c_float
 _i64 = ctypes.c_int64
 
+# sb_pool_keys_summaries numerics flags (SB_SUMMARY_* in include/spark_h3_b200.h).
+SUMMARY_PRE_ROUND_LOGMASS = 1
+SUMMARY_FP32_WEIGHTS = 2
+
 # name -> (restype, argtypes); mirrors include/spark_h3_b200.h exactly.
 SIGNATURES = {
     "sb_version": (_i, []),
@@ -30,13 +34,17 @@ SIGNATURES = {
     "sb_read_device_status": (_i, [_vp]),
     "sb_pool_queries": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _vp]),
     "sb_query_anchor": (_i, [_vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp]),
-    "sb_pool_keys_summaries": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp, _vp]),
+    "sb_pool_keys_summaries": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp,
+                                    _vp]),
     "sb_route_workspace_bytes": (_i64, [_i, _i, _i, _i]),
     "sb_route_topk": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
     "sb_route_topk_noalloc": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
     "sb_dense_rows_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "sb_tail_summaries8": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
+    "sb_tail_merge": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp,
+                           _vp]),
     "sb_headwise_permute": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp]),
     "sb_fp8_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
     "sb_fp8_swiglu_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),

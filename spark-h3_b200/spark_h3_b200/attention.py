@@ -60,10 +60,8 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
         raise RuntimeError("the B200 path implements Top-K routed Spark attention; set sol_route_topk_ratio")
     if cfg.sol_legacy_full_query:
         raise NotImplementedError("the B200 path does not implement sol_legacy_full_query")
-    if cfg.sol_tail_granularity != "query" or cfg.sol_reweight_summary_math != "tensorcore" \
-            or cfg.sol_reweight_logmass_key != "stored":
-        raise NotImplementedError("the B200 path implements the default reweight numerics "
-                                  "(tail granularity 'query', tensorcore summaries, stored log-mass key)")
+    if cfg.sol_tail_granularity == "block8x8" and cfg.sol_reweight_summary_math != "tensorcore":
+        raise ValueError("block8x8 currently supports tensorcore numeric mode only")
     if getattr(controller, "head_topk_budget", None) is not None:
         raise NotImplementedError("per-head Top-K budgets are not available on the B200 path")
     B, T, H, D = q_bthd.shape
@@ -99,10 +97,14 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     qc = ops.padded_query_means(q_bthd, ops.pool_queries(q_bthd, block), video, query_tokens, block)
     anchor = ops.query_anchor(qc, block, candidates, anchor_dtype)
     kc, ak, av, lm = ops.pool_keys_summaries(k_bthd, v_bthd, anchor, block, weighted_kv=weighted_kv,
-                                             mass_bias=mass_bias)
+                                             mass_bias=mass_bias, summary_math=cfg.sol_reweight_summary_math,
+                                             logmass_key=cfg.sol_reweight_logmass_key)
     packed, _ = ops.route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace, want_indices=False)
-    out, _ = ops.sparse_attention(q_bthd, k_bthd, v_bthd, block, packed, ak, av, lm, query_tokens=query_tokens,
-                                  sink_first=sink_first, sink_last=sink_last, local_radius=cfg.kernel_local_radius)
+    out = ops.pooled_tail_attention(q_bthd, k_bthd, v_bthd, block, packed, ak, av, lm, anchor,
+                                    query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last,
+                                    local_radius=cfg.kernel_local_radius, tail_granularity=cfg.sol_tail_granularity,
+                                    weighted_kv=weighted_kv, mass_bias=mass_bias,
+                                    logmass_key=cfg.sol_reweight_logmass_key)
     # Rows past dense_start attend densely (spark_integration.py:1238-1260): the kernel covers
     # rows past the sparse prefix; the context rows that padded it are recomputed here.
     dense_start = video if query_tokens > video else query_tokens
@@ -202,6 +204,7 @@ def _check_reblock(cfg, q, block: int) -> None:
 
 
 def spark_reweight(a: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int = 64,
+                   summary_math: str = "tensorcore", logmass_key: str = "stored",
                    reweight_components: str = "full"):
     """Anchor-conditioned summaries for query representatives a[B, P, H, D] and keys/values
     k, v[B, T, H, D]: returns (AK, AV [B, P, H, NB, D], LM [B, P, H, NB]) like the reference's
@@ -212,6 +215,7 @@ def spark_reweight(a: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: 
     parts = []
     for p in range(a.shape[1]):
         _, ak, av, lm = ops.pool_keys_summaries(k, v, a[:, p].contiguous(), block, weighted_kv=weighted_kv,
-                                                mass_bias=mass_bias, want_kc=False)
+                                                mass_bias=mass_bias, want_kc=False, summary_math=summary_math,
+                                                logmass_key=logmass_key)
         parts.append((ak, av, lm))
     return tuple(torch.stack([part[i] for part in parts], dim=1) for i in range(3))

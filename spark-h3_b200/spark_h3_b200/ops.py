@@ -75,10 +75,18 @@ def query_anchor(qc: torch.Tensor, block: int, prefix_blocks: int, dtype: torch.
 
 def pool_keys_summaries(k: torch.Tensor, v: torch.Tensor | None, anchor: torch.Tensor | None, block: int, *,
                         weighted_kv: bool = True, mass_bias: bool = True, want_kc: bool = True,
-                        want_summaries: bool = True):
-    """Returns (kc, ak, av, lm); entries not requested are None."""
+                        want_summaries: bool = True, summary_math: str = "tensorcore",
+                        logmass_key: str = "stored"):
+    """Returns (kc, ak, av, lm); entries not requested are None.  summary_math and
+    logmass_key are the reference's summary ablations (processor.py:61-68)."""
     device = _require_cuda(k, v, anchor)
     B, T, H, D = k.shape
+    if summary_math not in ("tensorcore", "comfy_fp32") or logmass_key not in ("stored", "pre_round"):
+        raise ValueError("invalid reweight summary numeric mode")
+    if summary_math == "comfy_fp32" and k.dtype != torch.bfloat16:
+        raise ValueError("comfy_fp32 summaries require BF16 K/V")
+    numerics = (_lib.SUMMARY_FP32_WEIGHTS if summary_math == "comfy_fp32" else 0) | \
+        (_lib.SUMMARY_PRE_ROUND_LOGMASS if logmass_key == "pre_round" else 0)
     nb = math.ceil(T / block)
     kc = torch.empty((B, nb, H, D), device=device, dtype=k.dtype) if want_kc else None
     ak = av = lm = None
@@ -91,8 +99,8 @@ def pool_keys_summaries(k: torch.Tensor, v: torch.Tensor | None, anchor: torch.T
     anchor_code = _dtype_code(anchor) if anchor is not None else _dtype_code(k)
     with torch.cuda.device(device):
         _lib.call("sb_pool_keys_summaries", k.data_ptr(), _ptr(v), _ptr(anchor), _dtype_code(k), anchor_code,
-                  B, T, H, D, block, int(weighted_kv), int(mass_bias), _ptr(kc), _ptr(ak), _ptr(av), _ptr(lm),
-                  _stream(device))
+                  B, T, H, D, block, int(weighted_kv), int(mass_bias), numerics, _ptr(kc), _ptr(ak), _ptr(av),
+                  _ptr(lm), _stream(device))
     return kc, ak, av, lm
 
 
@@ -138,6 +146,33 @@ def sparse_attention(q, k, v, block: int, packed: torch.Tensor | None, ak, av, l
     return out, lse
 
 
+def pooled_tail_attention(q, k, v, block: int, packed, ak, av, lm, anchor, *, query_tokens: int, sink_first: int,
+                          sink_last: int, local_radius: int = -1, out: torch.Tensor | None = None,
+                          tail_granularity: str = "query", weighted_kv: bool = True, mass_bias: bool = True,
+                          logmass_key: str = "stored") -> torch.Tensor:
+    """The attention step of a Spark layer for each tail granularity
+    (sol_numerator_virtual_q.py:597-660): "query" attends the summaries row by row inside the
+    fused kernel; "block" and "block8x8" run the exact keys only and merge a pooled tail."""
+    if tail_granularity == "query":
+        o, _ = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens=query_tokens, sink_first=sink_first,
+                                sink_last=sink_last, local_radius=local_radius, out=out)
+        return o
+    if tail_granularity not in ("block", "block8x8"):
+        raise ValueError("tail_granularity must be 'query', 'block', or 'block8x8'")
+    o, lse = sparse_attention(q, k, v, block, packed, None, None, None, query_tokens=query_tokens,
+                              sink_first=sink_first, sink_last=sink_last, local_radius=local_radius, out=out,
+                              want_lse=True)
+    if tail_granularity == "block":
+        tak, tav, tlm, entry, group = ak, av, lm, block, block
+    else:
+        tak, tav, tlm = tail_summaries8(k, v, anchor, weighted_kv=weighted_kv, mass_bias=mass_bias,
+                                        logmass_key=logmass_key)
+        entry, group = 8, 8
+    return tail_merge(q, tak, tav, tlm, packed, o, lse, block=block, entry_tokens=entry, group_tokens=group,
+                      query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last,
+                      local_radius=local_radius)
+
+
 def dense_rows_attention(q, k, v, row_lo: int, row_hi: int, out: torch.Tensor, *,
                          lse: torch.Tensor | None = None) -> torch.Tensor:
     """Dense attention of query rows [row_lo, row_hi) over every key, written into `out`
@@ -149,6 +184,39 @@ def dense_rows_attention(q, k, v, row_lo: int, row_hi: int, out: torch.Tensor, *
     with torch.cuda.device(device):
         _lib.call("sb_dense_rows_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, T, H, D,
                   row_lo, row_hi, out.data_ptr(), _ptr(lse), _stream(device))
+    return out
+
+
+def tail_summaries8(k: torch.Tensor, v: torch.Tensor, anchor: torch.Tensor, *, weighted_kv: bool = True,
+                    mass_bias: bool = True, logmass_key: str = "stored"):
+    """Eight-key anchor summaries (AK8, AV8 [B, H, ceil(T/8), 128] bf16, LM8 fp32) of the
+    block8x8 tail (sb_tail_summaries8)."""
+    device = _require_cuda(k, v, anchor)
+    B, T, H, D = k.shape
+    if k.dtype != torch.bfloat16 or v.dtype != torch.bfloat16 or v.shape != k.shape or D != 128:
+        raise ValueError("eight-key summaries take bf16 K/V [B, T, H, 128]")
+    n8 = math.ceil(T / 8)
+    ak8 = torch.empty((B, H, n8, D), device=device, dtype=k.dtype)
+    av8 = torch.empty_like(ak8)
+    lm8 = torch.empty((B, H, n8), device=device, dtype=torch.float32)
+    numerics = _lib.SUMMARY_PRE_ROUND_LOGMASS if logmass_key == "pre_round" else 0
+    with torch.cuda.device(device):
+        _lib.call("sb_tail_summaries8", k.data_ptr(), v.data_ptr(), anchor.data_ptr(), _dtype_code(k),
+                  _dtype_code(anchor), B, T, H, D, int(weighted_kv), int(mass_bias), numerics, ak8.data_ptr(),
+                  av8.data_ptr(), lm8.data_ptr(), _stream(device))
+    return ak8, av8, lm8
+
+
+def tail_merge(q, ak, av, lm, packed: torch.Tensor, out: torch.Tensor, lse: torch.Tensor, *, block: int,
+               entry_tokens: int, group_tokens: int, query_tokens: int, sink_first: int, sink_last: int,
+               local_radius: int = -1) -> torch.Tensor:
+    """Merges the pooled tail into the exact-only output and LSE in place (sb_tail_merge)."""
+    device = _require_cuda(q, ak, av, lm, packed, out, lse)
+    B, T, H, D = q.shape
+    with torch.cuda.device(device):
+        _lib.call("sb_tail_merge", q.data_ptr(), ak.data_ptr(), av.data_ptr(), lm.data_ptr(), _dtype_code(q), B, T,
+                  H, D, entry_tokens, group_tokens, block, packed.data_ptr(), packed.shape[1], query_tokens,
+                  sink_first, sink_last, local_radius, out.data_ptr(), lse.data_ptr(), _stream(device))
     return out
 
 
@@ -211,13 +279,16 @@ def read_device_status(device: torch.device | None = None) -> int:
 def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int = 128, topk_ratio: float = 0.1,
                 video_tokens: int | None = None, anchor_dtype: torch.dtype | None = None, local_radius: int = -1,
                 weighted_kv: bool = True, mass_bias: bool = True, workspace: torch.Tensor | None = None,
-                out: torch.Tensor | None = None, return_route: bool = False, tail_mode: str = "dense"):
+                out: torch.Tensor | None = None, return_route: bool = False, tail_mode: str = "dense",
+                tail_granularity: str = "query", summary_math: str = "tensorcore", logmass_key: str = "stored"):
     """One Spark sparse attention layer on BTHD tensors whose video prefix comes first.
 
     pool Q -> anchor -> pool K + summaries -> scores + Top-K -> sparse attention
     (rows past the sparse query prefix are attended densely by the same kernel).  With
     tail_mode "pad" the partial final video block is routed as a padded block and the context
-    rows that padded it are then attended densely (sb_dense_rows_attention).
+    rows that padded it are then attended densely (sb_dense_rows_attention).  tail_granularity
+    "block" / "block8x8" replaces the per-row summary columns by a pooled tail per query block
+    / per 8 rows, merged into the exact-keys-only output (sb_tail_merge).
     """
     B, T, H, D = q.shape
     video = T if video_tokens is None else int(video_tokens)
@@ -232,11 +303,14 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
     topk = target_topk(topk_ratio, candidates)
     qc = padded_query_means(q, pool_queries(q, block), video, query_tokens, block)
     anchor = query_anchor(qc, block, candidates, anchor_dtype or q.dtype)
-    kc, ak, av, lm = pool_keys_summaries(k, v, anchor, block, weighted_kv=weighted_kv, mass_bias=mass_bias)
+    kc, ak, av, lm = pool_keys_summaries(k, v, anchor, block, weighted_kv=weighted_kv, mass_bias=mass_bias,
+                                         summary_math=summary_math, logmass_key=logmass_key)
     packed, indices = route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace,
                                  want_indices=return_route)
-    o, _ = sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens=query_tokens, sink_first=sink_first,
-                            sink_last=sink_last, local_radius=local_radius, out=out)
+    o = pooled_tail_attention(q, k, v, block, packed, ak, av, lm, anchor, query_tokens=query_tokens,
+                              sink_first=sink_first, sink_last=sink_last, local_radius=local_radius, out=out,
+                              tail_granularity=tail_granularity, weighted_kv=weighted_kv, mass_bias=mass_bias,
+                              logmass_key=logmass_key)
     if query_tokens > video:
         dense_rows_attention(q, k, v, video, query_tokens, o)
     if return_route:

@@ -209,3 +209,70 @@ def test_dense_rows_attention_window(cuda_device, dtype):
     _check(o[:, 70:333], ref[:, 70:333], dtype)
     np.testing.assert_allclose(as_np(lse)[:, 70:333], ref_lse[:, 70:333], atol=2e-3, rtol=1e-4)
     assert (as_np(lse)[:, :70] == 7.0).all() and (as_np(lse)[:, 333:] == 7.0).all()
+
+
+@pytest.mark.parametrize("summary_math,logmass_key", [("tensorcore", "pre_round"), ("comfy_fp32", "stored"),
+                                                      ("comfy_fp32", "pre_round")])
+def test_summary_ablations_match_oracle(cuda_device, summary_math, logmass_key):
+    """The reference's summary numerics ablations (processor.py:61-68): the oracle restated
+    with the same switch, and each switch changes what it should (bit-for-bit comparison
+    with the default summaries on the GPU)."""
+    grid, heads, block = (3, 16, 32), 2, 64
+    q, k, v = make_qkv(grid, heads, 128, seed=5, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    dev = cuda_device
+    anchor = ops.query_anchor(ops.pool_queries(q.to(dev), block), block, q.shape[1] // block, torch.float32)
+    _, ak, av, lm = ops.pool_keys_summaries(k.to(dev), v.to(dev), anchor, block, summary_math=summary_math,
+                                            logmass_key=logmass_key)
+    _, ak0, av0, lm0 = ops.pool_keys_summaries(k.to(dev), v.to(dev), anchor, block)
+    ref_ak, ref_av, ref_lm = oracle.summaries(as_np(anchor), to_oracle(k), to_oracle(v), block,
+                                              summary_math=summary_math, logmass_key=logmass_key)
+    np.testing.assert_allclose(as_np(ak), ref_ak, atol=1.6e-2, rtol=1.6e-2)
+    np.testing.assert_allclose(as_np(av), ref_av, atol=1.6e-2, rtol=1.6e-2)
+    np.testing.assert_allclose(as_np(lm), ref_lm, atol=2e-3, rtol=1e-3)
+    if summary_math == "comfy_fp32":
+        assert not torch.equal(ak, ak0) and not torch.equal(av, av0)
+    else:
+        assert torch.equal(ak, ak0) and torch.equal(av, av0)
+    assert not torch.equal(lm, lm0)
+
+
+def test_exact_only_attention_matches_oracle(cuda_device):
+    """Without summaries the kernel attends the exact blocks only (the first stage of the
+    block tails), for both the tensor-core and the SIMT kernel."""
+    q, k, v = make_qkv((3, 16, 32), 2, 128, seed=51, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=64, topk_ratio=0.1, attention=False)
+    dev = cuda_device
+    packed = torch.from_numpy(ref["packed"]).to(dev)
+    exp_out, exp_lse = oracle.sparse_attention(to_oracle(q), to_oracle(k), to_oracle(v), 64, ref["packed"], None,
+                                               None, None, ref["query_tokens"], ref["sink_first"], ref["sink_last"])
+    for cast in (lambda t: t.to(dev), lambda t: t.to(dev).float()):
+        out, lse = ops.sparse_attention(cast(q), cast(k), cast(v), 64, packed, None, None, None,
+                                        query_tokens=ref["query_tokens"], sink_first=ref["sink_first"],
+                                        sink_last=ref["sink_last"], want_lse=True)
+        torch.cuda.synchronize()
+        _check(as_np(out), exp_out, torch.bfloat16)
+        np.testing.assert_allclose(as_np(lse), exp_lse, atol=2e-3, rtol=1e-4)
+
+
+@pytest.mark.parametrize("granularity", ["block", "block8x8"])
+@pytest.mark.parametrize("block", [64, 128])
+def test_pooled_tails_match_oracle(cuda_device, granularity, block):
+    """Tail granularities "block" and "block8x8" (sol_numerator_virtual_q.py:415-499) with
+    context sinks and a dense suffix: route bit-exact, output within the bf16 tolerance."""
+    q, k, v = make_qkv((4, 16, 33), 2, 128, seed=61, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    extra = make_qkv((1, 10, 15), 2, 128, seed=62, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    q, k, v = (torch.cat((a, b), dim=1) for a, b in zip((q, k, v), extra))
+    video = 2112
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             video_tokens=video, tail_granularity=granularity)
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, video_tokens=video, tail_granularity=granularity, return_route=True)
+    torch.cuda.synchronize()
+    assert ops.read_device_status(cuda_device) == 0
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    _check(as_np(out), ref["out"], torch.bfloat16)
+    # The pooled tail differs from the per-row summaries of the default granularity.
+    per_row = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block, topk_ratio=0.1,
+                              video_tokens=video)
+    torch.cuda.synchronize()
+    assert not torch.equal(per_row.cpu(), out.cpu())

@@ -82,3 +82,21 @@ def test_oracle_attention_matches_reference_formula():
                                      s["lm"][:, 0], query_tokens=960, sink_first=15, sink_last=16)
     rows = g["rows"]
     np.testing.assert_allclose(out[0, rows], g["out"], atol=1e-5, rtol=1e-4)
+
+
+def test_pooled_tail_oracle_with_every_block_exact_is_dense_attention():
+    """With Top-K ratio 1 every block is exact, the pooled tails are empty and the layer is
+    plain softmax attention (the reference checks the same identity on the GPU,
+    tests/test_spark_installer.py:446-485)."""
+    import torch
+
+    from spark_h3_b200.synthetic import make_qkv
+
+    q, k, v = make_qkv((2, 8, 16), 1, 128, seed=3, dtype=torch.float32, q_scale=128 ** -0.5)
+    t = lambda x: oracle.Tensor(x.numpy(), "float32")
+    qf, kf, vf = (x[0, :, 0].double() for x in (q, k, v))
+    p = torch.softmax(qf @ kf.T * 128 ** -0.5, dim=-1)
+    dense = (p @ vf).numpy()
+    for granularity in ("block", "block8x8"):
+        ref = oracle.spark_layer(t(q), t(k), t(v), block=64, topk_ratio=1.0, tail_granularity=granularity)
+        np.testing.assert_allclose(ref["out"][0, :, 0], dense, atol=1e-5)
