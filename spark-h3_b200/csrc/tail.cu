@@ -4,10 +4,10 @@
 // skipped key blocks are attended once per query group through the group's mean query, and
 // the two partial softmaxes are merged row by row:
 //   tail_summaries8_kernel  anchor-weighted summaries of every 8 keys (block8x8 only)
-//   tail_merge_kernel       per query group (64 or 8 rows): mean query rounded to the Q
-//                           dtype, online softmax over the summary entries whose key block is
-//                           not exact, then out = (we * exact + wa * tail) / (we + wa) with
-//                           we, wa the exponentials of the two LSEs relative to their max.
+//   tail_merge_kernel       per query group (a whole block, or 8 rows): mean query rounded to
+//                           the Q dtype, online softmax over the summary entries whose key
+//                           block is not exact, then out = (we * exact + wa * tail) / (we + wa)
+//                           with we, wa the exponentials of the two LSEs relative to their max.
 #include "common.cuh"
 #include "attn_common.cuh"
 
@@ -91,95 +91,134 @@ __global__ void __launch_bounds__(kTailThreads) tail_summaries8_kernel(
     lm8[((int64_t)b * H + h) * n8 + g] = mass_bias ? (mx + log2f(den)) * kLn2 - shift : logf((float)count);
 }
 
-// One CTA per (query group, head, batch).  Summary entry e covers keys [e*E, e*E + E) of key
-// block (e*E) / block; an entry is skipped when that block is exact for the group's query
-// block (route bit, sink range or local radius).
-template <typename T>
+// One CTA per (query block, head, batch), serving the block's NG query groups of G rows
+// (NG = block / G: one group for "block", eight of 8 rows for "block8x8"), which share the
+// block's exact set.  Summary entry e covers keys [e*E, e*E + E) of key block (e*E) / block; it
+// is skipped when that block is exact for the query block (route bit, sink range or local
+// radius).  Each warp streams every fourth entry once and scores it against all NG group means.
+template <typename T, int NG>
 __global__ void __launch_bounds__(kTailThreads) tail_merge_kernel(
     const T* __restrict__ q, const T* __restrict__ tk, const T* __restrict__ tv, const float* __restrict__ lmass,
     const int32_t* __restrict__ packed, int QB, int words, int Tn, int H, int n_entries, int entry_tokens,
-    int group_tokens, int block, int sink_first, int sink_last, int local_radius, T* __restrict__ out,
-    float* __restrict__ lse) {
-  __shared__ float qmean[kDim];
-  __shared__ float wm[4], wden[4];
-  __shared__ float wacc[4][kDim];
-  __shared__ float row_w[2][kTailThreads];  // per row of the group (at most 128): exact and tail weights
+    int block, int sink_first, int sink_last, int local_radius, T* __restrict__ out, float* __restrict__ lse) {
+  constexpr int kWarps = kTailThreads / 32;
+  __shared__ float qmean[NG][kDim];
+  __shared__ float wm[kWarps][NG], wden[kWarps][NG];
+  __shared__ float wacc[kWarps][NG][kDim];
+  __shared__ float row_w[2][kTailThreads];  // per row of the block (at most 128): exact and tail weights
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, tid = threadIdx.x;
-  const int grp = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
-  const int row0 = grp * group_tokens;
-  const int rows = min(group_tokens, Tn - row0);
-  const int qb = row0 / block;
+  const int qb = blockIdx.x, h = blockIdx.y, b = blockIdx.z;
+  const int G = block / NG;  // rows per query group
+  const int row0 = qb * block;
   const int64_t HD = (int64_t)H * kDim;
-  // Mean query of the group, in fp32 and rounded to the Q dtype (the reference's qmean).
-  {
+  // Mean query of every group, in fp32 and rounded to the Q dtype (the reference's qmean).
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int r0 = row0 + g * G, rows = min(G, Tn - r0);
     float s = 0.f;
-    for (int r = 0; r < rows; ++r) s += Elem<T>::to_f(q[((int64_t)b * Tn + row0 + r) * HD + (int64_t)h * kDim + tid]);
-    qmean[tid] = Elem<T>::to_f(Elem<T>::from_f(s / (float)max(rows, 1)));
+    for (int r = 0; r < rows; ++r) s += Elem<T>::to_f(q[((int64_t)b * Tn + r0 + r) * HD + (int64_t)h * kDim + tid]);
+    qmean[g][tid] = Elem<T>::to_f(Elem<T>::from_f(s / (float)max(rows, 1)));
   }
   __syncthreads();
   const int32_t* wrow = packed + (((int64_t)b * QB + qb) * H + h) * words;
   const int d0 = 4 * lane;
-  float qm[4];
+  float qm[NG][4];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) qm[i] = qmean[d0 + i];
+  for (int g = 0; g < NG; ++g)
+#pragma unroll
+    for (int i = 0; i < 4; ++i) qm[g][i] = qmean[g][d0 + i];
   const float scale_log2 = rsqrtf((float)kDim) * kLog2e;
-  float m = -INFINITY, den = 0.f, acc[4] = {0.f, 0.f, 0.f, 0.f};
+  float m[NG], den[NG], acc[NG][4];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    m[g] = -INFINITY;
+    den[g] = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; ++i) acc[g][i] = 0.f;
+  }
   const int64_t ebase = ((int64_t)b * H + h) * n_entries;
-  for (int e = warp; e < n_entries; e += 4) {
+  for (int e = warp; e < n_entries; e += kWarps) {
     const int kb = (e * entry_tokens) / block;
     if (block_is_exact(wrow, kb, qb, sink_first, sink_last, local_radius)) continue;
+    float kv[4], vv[4];
     const T* kp = tk + (ebase + e) * kDim + d0;
-    float part = 0.f;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) part = fmaf(Elem<T>::to_f(kp[i]), qm[i], part);
-    const float score = warp_sum(part) * scale_log2 + lmass[ebase + e] * kLog2e;
-    const float m_new = fmaxf(m, score);
-    const float factor = m == -INFINITY ? 0.f : exp2f(m - m_new);
-    const float pr = exp2f(score - m_new);
     const T* vp = tv + (ebase + e) * kDim + d0;
 #pragma unroll
-    for (int i = 0; i < 4; ++i) acc[i] = fmaf(acc[i], factor, pr * Elem<T>::to_f(vp[i]));
-    den = den * factor + pr;
-    m = m_new;
-  }
-  if (lane == 0) {
-    wm[warp] = m;
-    wden[warp] = den;
+    for (int i = 0; i < 4; ++i) {
+      kv[i] = Elem<T>::to_f(kp[i]);
+      vv[i] = Elem<T>::to_f(vp[i]);
+    }
+    const float lm2 = lmass[ebase + e] * kLog2e;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      float part = 0.f;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) part = fmaf(kv[i], qm[g][i], part);
+      const float score = warp_sum(part) * scale_log2 + lm2;
+      const float m_new = fmaxf(m[g], score);
+      const float factor = m[g] == -INFINITY ? 0.f : exp2f(m[g] - m_new);
+      const float pr = exp2f(score - m_new);
+#pragma unroll
+      for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(acc[g][i], factor, pr * vv[i]);
+      den[g] = den[g] * factor + pr;
+      m[g] = m_new;
+    }
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) wacc[warp][d0 + i] = acc[i];
+  for (int g = 0; g < NG; ++g) {
+    if (lane == 0) {
+      wm[warp][g] = m[g];
+      wden[warp][g] = den[g];
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) wacc[warp][g][d0 + i] = acc[g][i];
+  }
   __syncthreads();
-  float M = -INFINITY;
+  // Per group: merge the warps' partial softmaxes into the pooled tail and its LSE; then one
+  // thread per row computes the blend weights, and every thread blends its dimension.
+  float tail[NG], al[NG];
 #pragma unroll
-  for (int w = 0; w < 4; ++w) M = fmaxf(M, wm[w]);
-  float D = 0.f, A = 0.f;
+  for (int g = 0; g < NG; ++g) {
+    float M = -INFINITY;
 #pragma unroll
-  for (int w = 0; w < 4; ++w) {
-    const float f = wm[w] == -INFINITY ? 0.f : exp2f(wm[w] - M);
-    D = fmaf(wden[w], f, D);
-    A = fmaf(wacc[w][tid], f, A);
+    for (int w = 0; w < kWarps; ++w) M = fmaxf(M, wm[w][g]);
+    float D = 0.f, A = 0.f;
+#pragma unroll
+    for (int w = 0; w < kWarps; ++w) {
+      const float f = wm[w][g] == -INFINITY ? 0.f : exp2f(wm[w][g] - M);
+      D = fmaf(wden[w][g], f, D);
+      A = fmaf(wacc[w][g][tid], f, A);
+    }
+    tail[g] = D > 0.f ? A / D : 0.f;
+    al[g] = D > 0.f ? (M + log2f(D)) * kLn2 : -INFINITY;
   }
-  const bool has_tail = D > 0.f;
-  const float tail = has_tail ? A / D : 0.f;
-  const float al = has_tail ? (M + log2f(D)) * kLn2 : -INFINITY;
-  // Row weights of the merge (one thread per row), then every thread blends its dimension.
+  const int rows = min(block, Tn - row0);
   if (tid < rows) {
+    float a_row = al[0];
+#pragma unroll
+    for (int g = 1; g < NG; ++g)
+      if (tid / G == g) a_row = al[g];
     const int64_t rl = ((int64_t)b * Tn + row0 + tid) * H + h;
     const float el = lse[rl];
-    const float mx = fmaxf(el, al);
+    const float mx = fmaxf(el, a_row);
     const float we = mx == -INFINITY ? 0.f : expf(el - mx);
-    const float wa = mx == -INFINITY ? 0.f : expf(al - mx);
+    const float wa = mx == -INFINITY ? 0.f : expf(a_row - mx);
     row_w[0][tid] = we;
     row_w[1][tid] = wa;
     lse[rl] = we + wa > 0.f ? mx + logf(we + wa) : -INFINITY;
   }
   __syncthreads();
-  for (int r = 0; r < rows; ++r) {
-    const float we = row_w[0][r], wa = row_w[1][r];
-    const int64_t o = ((int64_t)b * Tn + row0 + r) * HD + (int64_t)h * kDim + tid;
-    const float exact = Elem<T>::to_f(out[o]);
-    const float merged = ((we > 0.f ? we * exact : 0.f) + (wa > 0.f ? wa * tail : 0.f)) / fmaxf(we + wa, 1e-30f);
-    out[o] = Elem<T>::from_f(merged);
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    const int r0 = g * G, r1 = min(r0 + G, rows);
+    for (int r = r0; r < r1; ++r) {
+      const float we = row_w[0][r], wa = row_w[1][r];
+      const int64_t o = ((int64_t)b * Tn + row0 + r) * HD + (int64_t)h * kDim + tid;
+      const float exact = Elem<T>::to_f(out[o]);
+      const float merged =
+          ((we > 0.f ? we * exact : 0.f) + (wa > 0.f ? wa * tail[g] : 0.f)) / fmaxf(we + wa, 1e-30f);
+      out[o] = Elem<T>::from_f(merged);
+    }
   }
 }
 
@@ -221,8 +260,8 @@ extern "C" int sb_tail_merge(const void* q, const void* ak, const void* av, cons
   SB_CHECK_ARG(dtype == SB_BF16, "sb_tail_merge: Q and the output must be bf16");
   SB_CHECK_ARG(B > 0 && T > 0 && H > 0 && D == kDim, "sb_tail_merge: needs B, T, H > 0 and D = 128");
   SB_CHECK_ARG(block == 64 || block == 128, "sb_tail_merge: block must be 64 or 128");
-  SB_CHECK_ARG((entry_tokens == block || entry_tokens == 8) && (group_tokens == block || group_tokens == 8),
-               "sb_tail_merge: entries and query groups are whole blocks or 8 tokens");
+  SB_CHECK_ARG((entry_tokens == block && group_tokens == block) || (entry_tokens == 8 && group_tokens == 8),
+               "sb_tail_merge: entries and query groups are both whole blocks or both 8 tokens");
   SB_CHECK_ARG(query_tokens >= 0 && query_tokens <= T && query_tokens % block == 0,
                "sb_tail_merge: query_tokens must be a block multiple in [0, T]");
   const int NB = ceil_div(T, block);
@@ -230,11 +269,25 @@ extern "C" int sb_tail_merge(const void* q, const void* ak, const void* av, cons
   SB_CHECK_ARG(sink_first >= 0 && sink_first <= sink_last && sink_last <= NB, "sb_tail_merge: bad sink range");
   if (query_tokens == 0) return SB_OK;
   const int n_entries = ceil_div(T, entry_tokens);
-  dim3 grid(query_tokens / group_tokens, H, B);
-  tail_merge_kernel<__nv_bfloat16><<<grid, kTailThreads, 0, (cudaStream_t)stream>>>(
-      (const __nv_bfloat16*)q, (const __nv_bfloat16*)ak, (const __nv_bfloat16*)av, lm, packed_route, QB,
-      ceil_div(NB, 32), T, H, n_entries, entry_tokens, group_tokens, block, sink_first, sink_last, local_radius,
-      (__nv_bfloat16*)out, lse);
+  dim3 grid(query_tokens / block, H, B);
+  cudaStream_t s = (cudaStream_t)stream;
+  const auto* qq = (const __nv_bfloat16*)q;
+  const auto* kk = (const __nv_bfloat16*)ak;
+  const auto* vv = (const __nv_bfloat16*)av;
+  auto* oo = (__nv_bfloat16*)out;
+  const int words = ceil_div(NB, 32);
+  if (group_tokens == block)
+    tail_merge_kernel<__nv_bfloat16, 1><<<grid, kTailThreads, 0, s>>>(
+        qq, kk, vv, lm, packed_route, QB, words, T, H, n_entries, entry_tokens, block, sink_first, sink_last,
+        local_radius, oo, lse);
+  else if (block == 64)
+    tail_merge_kernel<__nv_bfloat16, 8><<<grid, kTailThreads, 0, s>>>(
+        qq, kk, vv, lm, packed_route, QB, words, T, H, n_entries, entry_tokens, block, sink_first, sink_last,
+        local_radius, oo, lse);
+  else
+    tail_merge_kernel<__nv_bfloat16, 16><<<grid, kTailThreads, 0, s>>>(
+        qq, kk, vv, lm, packed_route, QB, words, T, H, n_entries, entry_tokens, block, sink_first, sink_last,
+        local_radius, oo, lse);
   SB_CHECK_LAUNCH("sb_tail_merge launch");
   return SB_OK;
 }
