@@ -276,3 +276,20 @@ def test_pooled_tails_match_oracle(cuda_device, granularity, block):
                               video_tokens=video)
     torch.cuda.synchronize()
     assert not torch.equal(per_row.cpu(), out.cpu())
+
+
+@pytest.mark.parametrize("block,granularity", [(64, "query"), (128, "query"), (64, "block")])
+def test_batch_of_two_matches_oracle(cuda_device, block, granularity):
+    """Two batch entries with different content through one call: routes bit-exact and
+    outputs within tolerance per entry (every kernel indexes the batch explicitly)."""
+    parts = [make_qkv((3, 16, 33), 2, 128, seed=s, dtype=torch.bfloat16, q_scale=128 ** -0.5) for s in (71, 72)]
+    q, k, v = (torch.cat([p[i] for p in parts], dim=0) for i in range(3))
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             tail_granularity=granularity)
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, tail_granularity=granularity, return_route=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    assert not np.array_equal(ref["indices"][0], ref["indices"][1])
+    for b in range(2):
+        _check(as_np(out)[b], ref["out"][b], torch.bfloat16)

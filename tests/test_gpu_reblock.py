@@ -161,3 +161,20 @@ def test_graph_replay_matches_eager(cuda_device):
             assert torch.equal(a, b)
     plan = reblock._plan(T, 16, grid, "power_of_two_fanout", None, None, "flat", q.device)
     assert 2 * H in plan._graphs  # the later calls replayed a captured graph
+
+
+def test_qk_permutations_batch_of_two(cuda_device):
+    """Batch 2: rows b*H + h of the key side, then of the query side; each row's tree is the
+    oracle's on the GPU features, and the two entries differ."""
+    grid, H = (2, 16, 40), 2
+    T = grid[0] * grid[1] * grid[2]
+    parts = [make_qkv(grid, H, 128, seed=s, dtype=torch.bfloat16, clustered=True) for s in (81, 82)]
+    q, k = (torch.cat([p[i] for p in parts], dim=0).to(cuda_device) for i in range(2))
+    qp, qi, kp, ki, hierarchy = reblock.qk_block_permutations(q, k, T, grid, use_graph=False)
+    samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype(np.int32)).to(cuda_device)
+    features = reblock.transform(q, k, reblock.metric_factors(q, k, samples), T)
+    ref, ref_inv = oracle.reblock_tree(bits(features), grid, hierarchy.split_budgets)
+    got = np.concatenate([kp.cpu().numpy().reshape(2 * H, T), qp.cpu().numpy().reshape(2 * H, T)])
+    got_inv = np.concatenate([ki.cpu().numpy().reshape(2 * H, T), qi.cpu().numpy().reshape(2 * H, T)])
+    assert np.array_equal(got, ref) and np.array_equal(got_inv, ref_inv)
+    assert not np.array_equal(kp[0].cpu().numpy(), kp[1].cpu().numpy())
