@@ -643,6 +643,78 @@ __global__ void __launch_bounds__(kProxyThreads) reblock_proxy_kernel(const __nv
 // changes) and fetches the next tile's feature rows while it scores the current one.
 constexpr int kScoreTiles = 8;
 
+// Reduce-scatter of the P scores of one token over the four threads of its quad (offsets 2
+// and 1 of the butterfly), then the store of this thread's share.
+template <int P>
+__device__ __forceinline__ void score_reduce_store(float (&v)[P], int t4, int C, float* out) {
+  int m = P;
+#pragma unroll
+  for (int o = 2; o >= 1; o >>= 1) {
+    if (m > 1) {
+      const int half = m / 2;
+      const bool upper = (t4 & o) != 0;
+#pragma unroll
+      for (int i = 0; i < P / 2; ++i) {
+        if (i < half) {
+          const float send = upper ? v[i] : v[half + i];
+          const float keep = upper ? v[half + i] : v[i];
+          v[i] = __fadd_rn(keep, __shfl_xor_sync(kFull, send, o));
+        }
+      }
+      m = half;
+    } else {
+      v[0] = __fadd_rn(v[0], __shfl_xor_sync(kFull, v[0], o));
+    }
+  }
+  if (P >= 4) {
+#pragma unroll
+    for (int i = 0; i < (P >= 4 ? P / 4 : 1); ++i) {
+      const int hh = t4 * (P / 4) + i;
+      if (hh < C - 1) out[hh] = v[i];
+    }
+  } else if ((t4 & 1) == 0 && (t4 >> 1) < C - 1) {
+    out[t4 >> 1] = v[0];
+  }
+}
+
+// TT tokens per quad share every direction element read from shared memory.
+template <int P, int TT>
+__device__ __forceinline__ void score_tokens(const uint2 (&raw)[TT][8], const float2 (*sd)[kDim], int t4, int C,
+                                             float* const (&out)[TT]) {
+  float u[TT][8][4];
+#pragma unroll
+  for (int t = 0; t < TT; ++t) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&raw[t][j]);
+      const float2 a = __bfloat1622float2(h[0]), b = __bfloat1622float2(h[1]);
+      u[t][j][0] = a.x, u[t][j][1] = a.y, u[t][j][2] = b.x, u[t][j][3] = b.y;
+    }
+    quad_unit(u[t]);
+  }
+  float v[TT][P];
+#pragma unroll
+  for (int q = 0; q < P / 2; ++q) {
+    uint64_t c[TT][8];
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      const float4* dp = reinterpret_cast<const float4*>(&sd[q][4 * (t4 + 4 * j)]);
+      const float4 d01 = dp[0], d23 = dp[1];  // (h0, h1) pairs of elements 0..3
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        uint64_t acc = f2_mul(f2_pack(u[t][j][0], u[t][j][0]), f2_pack(d01.x, d01.y));
+        acc = f2_fma(f2_pack(u[t][j][1], u[t][j][1]), f2_pack(d01.z, d01.w), acc);
+        acc = f2_fma(f2_pack(u[t][j][2], u[t][j][2]), f2_pack(d23.x, d23.y), acc);
+        c[t][j] = f2_fma(f2_pack(u[t][j][3], u[t][j][3]), f2_pack(d23.z, d23.w), acc);
+      }
+    }
+#pragma unroll
+    for (int t = 0; t < TT; ++t) f2_unpack(tree8x2(c[t]), v[t][2 * q], v[t][2 * q + 1]);
+  }
+#pragma unroll
+  for (int t = 0; t < TT; ++t) score_reduce_store<P>(v[t], t4, C, out[t]);
+}
+
 template <int P>
 __device__ __forceinline__ void score_token(const uint2 (&raw)[8], const float2 (*sd)[kDim], int t4, int C,
                                             float* out) {
@@ -750,6 +822,70 @@ __global__ void __launch_bounds__(256) reblock_score_kernel(const __nv_bfloat16*
     score_token<P>(cur, sd, t4, C, scores + ((int64_t)r * active + pos) * lv.S);
 #pragma unroll
     for (int j = 0; j < 8; ++j) cur[j] = nxt[j];
+    i = next;
+  }
+}
+
+// The same scores with two tokens per quad (tokens tk and tk + 32 of a 64-token tile, 128
+// threads per CTA): each direction element read from shared memory serves both tokens,
+// halving the shared-memory traffic that bounds the one-token form.
+template <int P>
+__global__ void __launch_bounds__(128) reblock_score2_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
+                                                             TreeLevel lv, const int32_t* __restrict__ idx_in,
+                                                             const float* __restrict__ dirs,
+                                                             float* __restrict__ scores) {
+  static_assert(P >= 2 && (P & (P - 1)) == 0, "P is a power of two");
+  __shared__ __align__(16) float2 sd[P / 2][kDim];
+  __shared__ int s_node[kScoreTiles];
+  const int r = blockIdx.y;
+  const int tiles = active / 64;
+  const int tile0 = blockIdx.x * kScoreTiles;
+  const int ntiles = min(kScoreTiles, tiles - tile0);
+  if (threadIdx.x < kScoreTiles) s_node[threadIdx.x] = threadIdx.x < ntiles ? lv.tiles[tile0 + threadIdx.x] : -1;
+  __syncthreads();
+  const int tk = threadIdx.x >> 2, t4 = threadIdx.x & 3;  // tokens tk and tk + 32 of a tile
+  const __nv_bfloat16* Fr = F + (int64_t)r * N * kDim;
+  const int32_t* ir = idx_in + (int64_t)r * N;
+  auto fetch = [&](int tile, uint2 (&raw)[2][8]) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int id = ir[tile * 64 + tk + 32 * t];
+      const __nv_bfloat16* row = Fr + (int64_t)id * kDim;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) raw[t][j] = __ldg(reinterpret_cast<const uint2*>(row + 4 * (t4 + 4 * j)));
+    }
+  };
+  int i = 0;
+  while (i < ntiles && s_node[i] < 0) ++i;
+  if (i == ntiles) return;
+  uint2 cur[2][8], nxt[2][8];
+  fetch(tile0 + i, cur);
+  int loaded = -1, C = 2;
+  while (i < ntiles) {
+    const int node = s_node[i];
+    int next = i + 1;
+    while (next < ntiles && s_node[next] < 0) ++next;
+    if (next < ntiles) fetch(tile0 + next, nxt);
+    if (node != loaded) {
+      __syncthreads();
+      C = lv.nodes[(int64_t)node * kNodeInts + 2];
+      const float* nd = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
+      for (int e = threadIdx.x; e < (P / 2) * kDim; e += blockDim.x) {
+        const int q = e / kDim, d = e % kDim;
+        sd[q][d] = make_float2(2 * q < C - 1 ? nd[(2 * q) * kDim + d] : 0.f,
+                               2 * q + 1 < C - 1 ? nd[(2 * q + 1) * kDim + d] : 0.f);
+      }
+      __syncthreads();
+      loaded = node;
+    }
+    const int pos = (tile0 + i) * 64 + tk;
+    float* const outs[2] = {scores + ((int64_t)r * active + pos) * lv.S,
+                            scores + ((int64_t)r * active + pos + 32) * lv.S};
+    score_tokens<P, 2>(cur, sd, t4, C, outs);
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int j = 0; j < 8; ++j) cur[t][j] = nxt[t][j];
     i = next;
   }
 }
@@ -1304,8 +1440,8 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
     switch (lv.P) {
       case 2: reblock_score_kernel<2><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       case 4: reblock_score_kernel<4><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
-      case 8: reblock_score_kernel<8><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
-      case 16: reblock_score_kernel<16><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 8: reblock_score2_kernel<8><<<sgrid, 128, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 16: reblock_score2_kernel<16><<<sgrid, 128, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       case 32: reblock_score_kernel<32><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       case 64: reblock_score_kernel<64><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       default: set_error("sb_reblock_tree: bad plan fanout %d", lv.P); return SB_ERR_INVALID;
