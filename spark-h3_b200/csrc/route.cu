@@ -10,11 +10,12 @@
 
 namespace sb {
 
-constexpr int kScoreTile = 64;  // query blocks x key blocks per CTA
+constexpr int kScoreTile = 128;  // query blocks x key blocks per CTA
 constexpr int kScoreThreads = 256;
 
-// grid (ceil(C/64), ceil(QB/64), B*H).  Thread (ty, tx) computes 4x4 scores:
-// query rows ty + 16*i and key columns tx + 16*j.
+// grid (ceil(C/128), ceil(QB/128), B*H).  Thread (ty, tx) of a 16 x 16 grid computes 8 x 8
+// scores, query rows ty + 16*i and key columns tx + 16*j, each as one fma chain over d in
+// order: 64 multiply-adds per 16 shared-memory loads.
 template <typename TK, int D>
 __global__ void __launch_bounds__(kScoreThreads)
 block_scores_kernel(const float* __restrict__ qc, const TK* __restrict__ kc, int QB, int NB, int H,
@@ -33,30 +34,30 @@ block_scores_kernel(const float* __restrict__ qc, const TK* __restrict__ kc, int
   }
   __syncthreads();
   const int tx = tid % 16, ty = tid / 16;
-  float acc[4][4];
+  float acc[8][8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i)
+  for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0.f;
-#pragma unroll 4
+    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+#pragma unroll 2
   for (int d = 0; d < D; ++d) {
-    float a[4], w[4];
+    float a[8], w[8];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) a[i] = sq[ty + 16 * i][d];
+    for (int i = 0; i < 8; ++i) a[i] = sq[ty + 16 * i][d];
 #pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = sk[d][tx + 16 * j];
+    for (int j = 0; j < 8; ++j) w[j] = sk[d][tx + 16 * j];
 #pragma unroll
-    for (int i = 0; i < 4; ++i)
+    for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = __fmaf_rn(a[i], w[j], acc[i][j]);
+      for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(a[i], w[j], acc[i][j]);
   }
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
+  for (int i = 0; i < 8; ++i) {
     const int qi = q0 + ty + 16 * i;
     if (qi >= QB) continue;
     float* row = scores + (((int64_t)b * QB + qi) * H + h) * C;
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
+    for (int j = 0; j < 8; ++j) {
       const int ci = c0 + tx + 16 * j;
       if (ci < C) row[ci] = __fmul_rn(acc[i][j], scale_log2);
     }
@@ -69,95 +70,95 @@ __device__ __forceinline__ uint32_t float_key(float f) {
   return (u & 0x80000000u) ? ~u : (u | 0x80000000u);
 }
 
-constexpr int kTopkThreads = 256;
+// One warp per (b, query block, head) row, several rows per CTA, no CTA barriers: the row's
+// keys sit in the warp's slice of shared memory; a 4 x 8-bit radix select with a per-warp
+// histogram finds the key of the topk-th largest score; then 32 candidates at a time, the
+// keys above it and the lowest-index keys equal to it are taken (each ballot is one packed
+// route word).  Ties at the cut go to the lowest candidate index.
+constexpr int kTopkWarpMaxRows = 8;
 
-// One CTA per (b, query block, head) row.  Radix select (4 x 8 bits) finds the key of
-// the topk-th largest score; every score above it is kept, and of the scores equal to
-// it the lowest-index ones fill the remaining slots.
-__global__ void __launch_bounds__(kTopkThreads)
-topk_rows_kernel(const float* __restrict__ scores, int C, int topk, int words,
-                 int32_t* __restrict__ packed, int32_t* __restrict__ indices) {
-  extern __shared__ uint32_t keys[];  // [C]
-  __shared__ uint32_t hist[256];
-  __shared__ uint32_t sel_prefix, sel_need;
-  __shared__ uint32_t route_words[256];
-  __shared__ int warp_counts[kTopkThreads / 32];
-  __shared__ int eq_base;
-  const int64_t row = blockIdx.x;
-  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+__global__ void __launch_bounds__(32 * kTopkWarpMaxRows)
+topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int topk, int words,
+                      int32_t* __restrict__ packed, int32_t* __restrict__ indices) {
+  extern __shared__ uint32_t warp_smem[];  // per warp: hist[256] then keys[C]
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
+  if (row >= rows) return;
+  uint32_t* hist = warp_smem + (size_t)warp * (256 + C);
+  uint32_t* keys = hist + 256;
   const float* src = scores + row * C;
-  for (int i = tid; i < C; i += kTopkThreads) keys[i] = float_key(src[i]);
-  if (tid == 0) {
-    sel_prefix = 0;
-    sel_need = (uint32_t)topk;
-  }
-  __syncthreads();
-
-  // Radix select from the most significant byte.
+  for (int i = lane; i < C; i += 32) keys[i] = float_key(src[i]);
+  uint32_t prefix = 0, need = (uint32_t)topk;
+#pragma unroll 1
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
     const uint32_t mask_hi = pass == 0 ? 0u : (0xffffffffu << (32 - 8 * pass));
-    for (int i = tid; i < 256; i += kTopkThreads) hist[i] = 0;
-    __syncthreads();
-    const uint32_t prefix = sel_prefix;
-    for (int i = tid; i < C; i += kTopkThreads) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) hist[lane + 32 * i] = 0u;
+    __syncwarp();
+    for (int i = lane; i < C; i += 32) {
       const uint32_t kk = keys[i];
-      if ((kk & mask_hi) == prefix) atomicAdd(&hist[(kk >> shift) & 0xff], 1u);
+      if ((kk & mask_hi) == prefix) atomicAdd(&hist[(kk >> shift) & 0xffu], 1u);
     }
-    __syncthreads();
-    if (tid == 0) {
-      uint32_t need = sel_need, above = 0;
-      int digit = 255;
-      for (; digit > 0; --digit) {
-        if (above + hist[digit] >= need) break;
-        above += hist[digit];
+    __syncwarp();
+    // Lane l owns digits 255 - 8l .. 248 - 8l (descending); an exclusive prefix over lanes of
+    // the counts above gives each lane the number of keys in higher digits.
+    uint32_t c[8], own = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      c[i] = hist[255 - 8 * lane - i];
+      own += c[i];
+    }
+    uint32_t incl = own;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const uint32_t v = __shfl_up_sync(0xffffffffu, incl, o);
+      if (lane >= o) incl += v;
+    }
+    uint32_t above = incl - own;
+    int digit = -1;
+    uint32_t above_digit = 0;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      if (digit < 0 && above + c[i] >= need) {
+        digit = 255 - 8 * lane - i;
+        above_digit = above;
       }
-      sel_prefix = prefix | ((uint32_t)digit << shift);
-      sel_need = need - above;
+      above += c[i];
     }
-    __syncthreads();
+    // The selected digit is the first (highest) one where the running count reaches need;
+    // digit 0 takes whatever remains.
+    const unsigned has = __ballot_sync(0xffffffffu, digit >= 0);
+    const int src_lane = has ? __ffs(has) - 1 : 31;
+    int sel_digit = __shfl_sync(0xffffffffu, digit, src_lane);
+    uint32_t sel_above = __shfl_sync(0xffffffffu, above_digit, src_lane);
+    if (!has) {
+      sel_digit = 0;
+      sel_above = __shfl_sync(0xffffffffu, incl, 31) - __shfl_sync(0xffffffffu, c[7], 31);
+    }
+    prefix |= (uint32_t)sel_digit << shift;
+    need -= sel_above;
   }
-  const uint32_t thresh = sel_prefix;
-  const uint32_t take_equal = sel_need;  // how many entries equal to thresh to keep
-
-  // Exclusive scan of "equal to thresh" flags in index order gives the lowest-index rule;
-  // a second scan of the final selection writes ascending indices.
-  for (int i = tid; i < words; i += kTopkThreads) route_words[i] = 0;
-  if (tid == 0) eq_base = 0;
-  __syncthreads();
-  int out_base = 0;
-  for (int start = 0; start < C; start += kTopkThreads) {
-    const int i = start + tid;
+  const uint32_t thresh = prefix, take_equal = need;
+  uint32_t eq_seen = 0;
+  int out_pos = 0;
+  int32_t* prow = packed + row * words;
+  for (int w = 0; w < words; ++w) {
+    const int i = 32 * w + lane;
     const uint32_t kk = i < C ? keys[i] : 0u;
     const bool eq = i < C && kk == thresh;
     const unsigned eq_mask = __ballot_sync(0xffffffffu, eq);
-    if (lane == 0) warp_counts[warp] = __popc(eq_mask);
-    __syncthreads();
-    int eq_before = eq_base;
-    for (int w = 0; w < warp; ++w) eq_before += warp_counts[w];
-    eq_before += __popc(eq_mask & ((1u << lane) - 1u));
-    const bool sel = i < C && (kk > thresh || (eq && (uint32_t)eq_before < take_equal));
-    __syncthreads();
-    if (tid == 0) {
-      int tot = 0;
-      for (int w = 0; w < kTopkThreads / 32; ++w) tot += warp_counts[w];
-      eq_base += tot;
-    }
+    const uint32_t eq_before = eq_seen + __popc(eq_mask & ((1u << lane) - 1u));
+    const bool sel = i < C && (kk > thresh || (eq && eq_before < take_equal));
     const unsigned sel_mask = __ballot_sync(0xffffffffu, sel);
-    __syncthreads();
-    if (lane == 0) warp_counts[warp] = __popc(sel_mask);
-    __syncthreads();
-    int pos = out_base;
-    for (int w = 0; w < warp; ++w) pos += warp_counts[w];
-    pos += __popc(sel_mask & ((1u << lane) - 1u));
-    if (sel) {
-      atomicOr(&route_words[i >> 5], 1u << (i & 31));
-      if (indices != nullptr && pos < topk) indices[row * topk + pos] = i;
+    if (sel && indices != nullptr) {
+      const int pos = out_pos + __popc(sel_mask & ((1u << lane) - 1u));
+      if (pos < topk) indices[row * topk + pos] = i;
     }
-    for (int w = 0; w < kTopkThreads / 32; ++w) out_base += warp_counts[w];
-    __syncthreads();
+    if (lane == 0) prow[w] = (int32_t)sel_mask;
+    eq_seen += __popc(eq_mask);
+    out_pos += __popc(sel_mask);
   }
-  for (int i = tid; i < words; i += kTopkThreads) packed[row * words + i] = (int32_t)route_words[i];
 }
 
 }  // namespace sb
@@ -173,6 +174,25 @@ static int launch_scores(dim3 grid, const float* qc, const void* kc, int QB, int
   if (err != cudaSuccess) return cuda_error(err, "sb_route_topk: set score smem");
   kern<<<grid, kScoreThreads, smem, s>>>(qc, (const TK*)kc, QB, NB, H, C, scale_log2, scores);
   SB_CHECK_LAUNCH("sb_route_topk: score launch");
+  return SB_OK;
+}
+
+// Top-K of `rows` score rows of C candidates: warps of one row each, as many per CTA as their
+// keys (C x 4 B + a 1 KB histogram each) fit in 200 KB of shared memory.
+static int launch_topk(const float* scores, int64_t rows, int C, int topk, int words, int32_t* packed,
+                       int32_t* indices, cudaStream_t s) {
+  const size_t per_warp = (size_t)(256 + C) * sizeof(uint32_t);
+  const int warps = (int)std::min<size_t>(kTopkWarpMaxRows, std::max<size_t>(1, (200 * 1024) / per_warp));
+  const size_t smem = per_warp * warps;
+  if (smem > 200 * 1024) {
+    set_error("sb_route_topk: too many candidate blocks (%d)", C);
+    return SB_ERR_INVALID;
+  }
+  cudaError_t err = cudaFuncSetAttribute(topk_rows_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_route_topk: set smem");
+  topk_rows_warp_kernel<<<(unsigned)((rows + warps - 1) / warps), 32 * warps, smem, s>>>(scores, rows, C, topk, words, packed,
+                                                                                   indices);
+  SB_CHECK_LAUNCH("sb_route_topk: top-k launch");
   return SB_OK;
 }
 
@@ -208,13 +228,9 @@ extern "C" int sb_route_topk(const float* qc, const void* kc, int kc_dtype, int 
     rc = D == 128 ? launch_scores<float, 128>(grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s)
                   : launch_scores<float, 64>(grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s);
   if (rc != SB_OK) return rc;
-  cudaError_t err = cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)key_smem);
-  if (err != cudaSuccess) return cuda_error(err, "sb_route_topk: set smem");
   const int64_t rows = (int64_t)B * QB * H;
   SB_CHECK_ARG(rows < (1ll << 31), "sb_route_topk: too many rows");
-  topk_rows_kernel<<<(unsigned)rows, kTopkThreads, key_smem, s>>>(scores, candidates, topk, words, packed_route, indices);
-  SB_CHECK_LAUNCH("sb_route_topk: top-k launch");
-  return SB_OK;
+  return launch_topk(scores, rows, candidates, topk, words, packed_route, indices, s);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -283,8 +299,6 @@ extern "C" int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dty
   float* scratch = route_noalloc_scratch(&status);
   if (scratch == nullptr) return status;
   cudaStream_t s = (cudaStream_t)stream;
-  cudaError_t err = cudaFuncSetAttribute(topk_rows_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)key_smem);
-  if (err != cudaSuccess) return cuda_error(err, "sb_route_topk_noalloc: set smem");
   const int chunk = (int)std::min<int64_t>(QB, kNoAllocScoreFloats / per_block);
   const size_t kc_elem = kc_dtype == SB_BF16 ? 2 : 4;
   for (int b = 0; b < B; ++b) {
@@ -302,9 +316,9 @@ extern "C" int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dty
                       : launch_scores<float, 64>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
       if (rc != SB_OK) return rc;
       const int64_t row0 = ((int64_t)b * QB + q0) * H;
-      topk_rows_kernel<<<(unsigned)((int64_t)n * H), kTopkThreads, key_smem, s>>>(
-          scratch, candidates, topk, words, packed_route + row0 * words, indices ? indices + row0 * topk : nullptr);
-      SB_CHECK_LAUNCH("sb_route_topk_noalloc: top-k launch");
+      rc = launch_topk(scratch, (int64_t)n * H, candidates, topk, words, packed_route + row0 * words,
+                       indices ? indices + row0 * topk : nullptr, s);
+      if (rc != SB_OK) return rc;
     }
   }
   return SB_OK;
