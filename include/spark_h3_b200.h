@@ -53,6 +53,18 @@ const char* sb_last_error(void);
 int sb_read_device_status(void* stream);
 
 /*
+ * Self-check of the bounded waits every kernel uses (no counterpart in the reference): one
+ * CTA whose warp 0 waits on an mbarrier that nothing arrives on, for limit_cycles, then raises
+ * the CTA abort flag and records SB_SELFTEST_WAIT_SITE in the device status word; warp 1,
+ * waiting on another such barrier with the normal two-second limit, must leave when the flag
+ * rises.  result (device, 4 ints): per warp, whether its wait succeeded (expected 0) and
+ * whether it left within a bounded time (expected 1).  Nothing faults; the context stays
+ * usable.  limit_cycles in (0, 1e8].
+ */
+#define SB_SELFTEST_WAIT_SITE 990
+int sb_selftest_wait_timeout(long long limit_cycles, int* result, void* stream);
+
+/*
  * Query block pooling.  Replaces the query-centroid half of
  * h3_sparse_attention/spark_integration.py:111-127 (_sol_topk_policy_scores) and the
  * per-64-row partial sums of sol_numerator_virtual_q.py:268-285 (_anchor_parts).

@@ -6,6 +6,7 @@
 
 #include "common.cuh"
 #include "attn_common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace sb {
 
@@ -141,4 +142,50 @@ extern "C" int sb_dense_rows_attention(const void* q, const void* k, const void*
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == SB_BF16 && D == 128) return launch_sparse_attention_sm100(p, s);
   return launch_sparse_attention_simt(p, dtype, D, s);
+}
+
+// ------------------------------------------------------------------ bounded-wait self-check
+namespace sb {
+namespace {
+
+constexpr int kSelfTestSite = SB_SELFTEST_WAIT_SITE;
+
+// Warp 0 waits on an mbarrier that nothing arrives on, with a short limit: it gives up,
+// raises the CTA abort flag and records its site code.  Warp 1 waits on a second such
+// barrier with the kernels' normal two-second limit and must leave as soon as the flag is
+// up.  No fault, no unbounded wait: the kernel ends after about `limit` cycles.
+__global__ void wait_timeout_kernel(long long limit, int* status, int* result) {
+  __shared__ __align__(8) uint64_t bars[2];
+  __shared__ int abort_flag;
+  if (threadIdx.x == 0) {
+    sm100::mbar_init(sm100::smem_u32(&bars[0]), 1);
+    sm100::mbar_init(sm100::smem_u32(&bars[1]), 1);
+    sm100::fence_barrier_init();
+    abort_flag = 0;
+  }
+  __syncthreads();
+  const int warp = threadIdx.x >> 5;
+  const long long t0 = clock64();
+  const bool got = warp == 0 ? sm100::mbar_wait_limit(sm100::smem_u32(&bars[0]), 0, &abort_flag, status,
+                                                      kSelfTestSite, limit)
+                             : sm100::mbar_wait(sm100::smem_u32(&bars[1]), 0, &abort_flag, status, kSelfTestSite + 1);
+  const long long dt = clock64() - t0;
+  if ((threadIdx.x & 31) == 0) {
+    result[2 * warp] = got ? 1 : 0;
+    result[2 * warp + 1] = dt < 4 * limit + 1000000 ? 1 : 0;  // left within a bounded time
+  }
+}
+
+}  // namespace
+}  // namespace sb
+
+extern "C" int sb_selftest_wait_timeout(long long limit_cycles, int* result, void* stream) {
+  SB_CHECK_ARG(result, "sb_selftest_wait_timeout: null result");
+  SB_CHECK_ARG(limit_cycles > 0 && limit_cycles <= 100000000ll,
+               "sb_selftest_wait_timeout: limit must lie in (0, 1e8] cycles");
+  int* status = device_status_ptr();
+  if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_selftest_wait_timeout: status word");
+  wait_timeout_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(limit_cycles, status, result);
+  SB_CHECK_LAUNCH("sb_selftest_wait_timeout launch");
+  return SB_OK;
 }

@@ -37,22 +37,29 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after ~limit cycles, raising the CTA abort flag and recording
-// `site` in the device status word.  Returns false when the caller must stop.
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
-                                          int* status, int site) {
+// Bounded wait: gives up after `limit` cycles, raising the CTA abort flag and recording
+// `site` in the device status word, or as soon as another thread of the CTA has raised the
+// flag.  Returns false when the caller must stop.
+__device__ __forceinline__ bool mbar_wait_limit(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                                int* status, int site, long long limit) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long start = clock64();
-  constexpr long long kLimit = 4000000000ll;  // about two seconds at 1.9 GHz
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
-    if (clock64() - start > kLimit) {
+    if (clock64() - start > limit) {
       *abort_flag = 1;
       if (status) atomicExch(status, site);
       return false;
     }
   }
+}
+
+constexpr long long kWaitLimit = 4000000000ll;  // about two seconds at 1.9 GHz
+
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort_flag,
+                                          int* status, int site) {
+  return mbar_wait_limit(bar, parity, abort_flag, status, site, kWaitLimit);
 }
 
 // Bounded wait that ignores the abort flag: used to drain in-flight copies and MMAs

@@ -41,6 +41,7 @@ SIGNATURES = {
     "sb_route_topk_noalloc": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
+    "sb_selftest_wait_timeout": (_i, [ctypes.c_longlong, _vp, _vp]),
     "sb_dense_rows_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "sb_tail_summaries8": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),
     "sb_tail_merge": (_i, [_vp, _vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _i, _i, _i, _i, _vp, _vp,
