@@ -277,6 +277,23 @@ int sb_fp8_gemm_residual(const uint8_t* a, const float* a_scale, int a_scale_str
                          int num_ctas, void* stream);
 
 /*
+ * Attention-input producer for the DiT stack (config 4; the fused projection / RoPE producer
+ * the reference's ComfyUI path builds in native/spark_split/producer.cu): the fused QKV fp8
+ * GEMM (A [M, K] e4m3 with per-token scales, B [3 * heads * 128, K] e4m3 with per-channel
+ * scales, optional bf16 bias) whose epilogue, per head, rounds the projection to bf16, applies
+ * RMSNorm (q with norm_q, k with norm_k, both [128] fp32, eps) and the rotary embedding to q
+ * and k, and writes q, k and v head rows as [shards][M][heads / shards][128] bf16: the send
+ * layout of the sequence-to-head all-to-all.  Pair j of the head dimension rotates by
+ * rope[(j * rope_stride + coords[m, axis[j]]) * 2 + {0: cos, 1: sin}], coords [M, 3] int32,
+ * axis [64] int8.  heads must be even.  Replaces sb_fp8_gemm followed by sb_dit_qkv_norm_rope
+ * (no qkv intermediate).
+ */
+int sb_fp8_gemm_qkv_rope(const uint8_t* a, const float* a_scale, const uint8_t* b, const float* b_scale,
+                         int64_t M, int heads, int K, const void* bias, const float* norm_q, const float* norm_k,
+                         const float* rope, int rope_stride, const int32_t* coords, const int8_t* axis, int shards,
+                         float eps, void* q, void* k, void* v, int num_ctas, void* stream);
+
+/*
  * GELU (erf form) fused with the e4m3 row quantiser: quantize_rows(gelu(x)) of an FFN up
  * projection without writing the activation (config 4; the reference's SwiGLU counterpart is
  * fp8_linear.py:128-138).  x: [M, K] (dtype), out: [M, K] bytes, scales: [M] fp32.

@@ -41,7 +41,30 @@ struct GemmParams {
   int64_t M;
   int N, K;
   int m_tiles, n_tiles, k_steps;
+  // Attention-input producer (the fused QKV projection), active when qkv_out[0] is set:
+  // columns [0, H*128) are the q heads, then the k heads, then the v heads.  q and k get a
+  // per-head RMSNorm (weights norm_w[0] / norm_w[1], eps) of the bf16-rounded projection and
+  // the rotary embedding (pair j rotates by rope[j * rope_stride + coords[m, rope_axis[j]]],
+  // stored as (cos, sin)); v is stored as projected.  Head h of row m goes to
+  // qkv_out[section] + ((h / hp * M + m) * hp + h % hp) * 128, hp = heads / shards: the send
+  // layout of the sequence-to-head all-to-all.
+  __nv_bfloat16* qkv_out[3];
+  const float* norm_w[2];
+  const float2* rope;
+  const int32_t* coords;
+  const int8_t* rope_axis;
+  int rope_stride, heads, shards;
+  float eps;
 };
+
+// Projection of 32 accumulator columns to bf16-representable fp32 values (scales, bias).
+__device__ __forceinline__ void project_chunk(const uint32_t (&r)[32], float sa, float sb_l, float bias_l, float (&f)[32]) {
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    const float y = __uint_as_float(r[i]) * sa * __shfl_sync(0xffffffffu, sb_l, i);
+    f[i] = __bfloat162float(__float2bfloat16_rn(y + __shfl_sync(0xffffffffu, bias_l, i)));
+  }
+}
 
 // ------------------------------------------------------------------ CTA-pair GEMM
 // A cluster of two CTAs computes a 256 x 256 tile with tcgen05.mma.cta_group::2: CTA rank r
@@ -275,6 +298,70 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       const bool row_ok = m < p.M;
       const float sa = row_ok ? __ldg(p.a_scale + m * p.a_scale_stride) : 0.f;
       __nv_bfloat16* out_row = p.out + m * p.N;
+      if (p.qkv_out[0] != nullptr) {
+        // ------------------------------------------------ attention-input producer
+        const int HD = p.heads * 128;
+        const int section = n0 / HD;  // a 256-column tile never straddles q / k / v
+        const int hp = p.heads / p.shards;
+#pragma unroll 1
+        for (int hh = 0; hh < 2; ++hh) {
+          const int h = (n0 - section * HD) / 128 + hh;
+          __nv_bfloat16* dst = p.qkv_out[section] + (((int64_t)(h / hp) * p.M + m) * hp + h % hp) * 128;
+          const uint32_t col0 = buf * kPairAccCols + 128 * hh;
+          float rstd = 1.f;
+          if (section < 2) {
+            float ss = 0.f;
+#pragma unroll 1
+            for (int c = 0; c < 4; ++c) {
+              uint32_t r[32];
+              tmem_ld32(tmem + lane_base + col0 + 32 * c, r);
+              const int nl = n0 + 128 * hh + 32 * c + lane;
+              const float sb_l = __ldg(p.b_scale + (int64_t)nl * p.b_scale_stride);
+              const float bias_l = p.bias != nullptr ? __bfloat162float(p.bias[nl]) : 0.f;
+              tmem_wait_ld();
+              float f[32];
+              project_chunk(r, sa, sb_l, bias_l, f);
+#pragma unroll
+              for (int i = 0; i < 32; ++i) ss = fmaf(f[i], f[i], ss);
+            }
+            rstd = rsqrtf(ss / 128.f + p.eps);
+          }
+#pragma unroll 1
+          for (int c = 0; c < 4; ++c) {
+            uint32_t r[32];
+            tmem_ld32(tmem + lane_base + col0 + 32 * c, r);
+            const int nl = n0 + 128 * hh + 32 * c + lane;
+            const float sb_l = __ldg(p.b_scale + (int64_t)nl * p.b_scale_stride);
+            const float bias_l = p.bias != nullptr ? __bfloat162float(p.bias[nl]) : 0.f;
+            const float w_l = section < 2 ? __ldg(p.norm_w[section] + 32 * c + lane) : 1.f;
+            tmem_wait_ld();
+            float f[32];
+            project_chunk(r, sa, sb_l, bias_l, f);
+            if (section < 2) {
+#pragma unroll
+              for (int i = 0; i < 32; ++i) f[i] = f[i] * rstd * __shfl_sync(0xffffffffu, w_l, i);
+              if (row_ok) {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) {
+                  const int j = 16 * c + i;  // rotation pair (32c + 2i, 32c + 2i + 1)
+                  const float2 cs = __ldg(p.rope + (int64_t)j * p.rope_stride + p.coords[m * 3 + p.rope_axis[j]]);
+                  const float x0 = f[2 * i], x1 = f[2 * i + 1];
+                  f[2 * i] = x0 * cs.x - x1 * cs.y;
+                  f[2 * i + 1] = x0 * cs.y + x1 * cs.x;
+                }
+              }
+            }
+            if (row_ok) {
+#pragma unroll
+              for (int v = 0; v < 4; ++v) store8(dst + 32 * c + 8 * v, f + 8 * v);
+            }
+          }
+        }
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&C.acc_empty[buf]), 0));
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < 256 / 32; ++c) {
         uint32_t r[32];
@@ -674,9 +761,20 @@ extern "C" int sb_fp8_swiglu(const void* h, int dtype, int64_t M, int K, void* a
 }
 
 namespace {
+struct ProducerArgs {
+  void* qkv_out[3];
+  const float* norm_w[2];
+  const float* rope;
+  const int32_t* coords;
+  const int8_t* axis;
+  int rope_stride, heads, shards;
+  float eps;
+};
+
 int launch_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, const uint8_t* b,
                     const float* b_scale, int b_scale_stride, int64_t M, int N, int K, const void* bias,
-                    const void* residual, const float* gate, void* out, int num_ctas, void* stream) {
+                    const void* residual, const float* gate, void* out, int num_ctas, void* stream,
+                    const ProducerArgs* prod = nullptr) {
   SB_CHECK_ARG(a && a_scale && b && b_scale && out, "sb_fp8_gemm: null pointer");
   SB_CHECK_ARG(residual == nullptr || (gate != nullptr && ((uintptr_t)residual % 16) == 0),
                "sb_fp8_gemm: a residual needs a gate vector and 16-byte alignment");
@@ -709,6 +807,18 @@ int launch_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, 
   p.m_tiles = (int)((M + 255) / 256);
   p.n_tiles = (N + 255) / 256;
   p.k_steps = (K + kPairBK - 1) / kPairBK;
+  if (prod != nullptr) {
+    for (int i = 0; i < 3; ++i) p.qkv_out[i] = static_cast<__nv_bfloat16*>(prod->qkv_out[i]);
+    p.norm_w[0] = prod->norm_w[0];
+    p.norm_w[1] = prod->norm_w[1];
+    p.rope = reinterpret_cast<const float2*>(prod->rope);
+    p.coords = prod->coords;
+    p.rope_axis = prod->axis;
+    p.rope_stride = prod->rope_stride;
+    p.heads = prod->heads;
+    p.shards = prod->shards;
+    p.eps = prod->eps;
+  }
   const size_t smem = (size_t)kPairStages * kPairStageBytes + sizeof(PairControl);
   cudaError_t err = cudaFuncSetAttribute(fp8_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: set smem");
@@ -752,4 +862,32 @@ extern "C" int sb_fp8_gemm_residual(const uint8_t* a, const float* a_scale, int 
   SB_CHECK_ARG(residual != nullptr, "sb_fp8_gemm_residual: null residual");
   return launch_fp8_gemm(a, a_scale, a_scale_stride, b, b_scale, b_scale_stride, M, N, K, bias, residual, gate, out,
                          num_ctas, stream);
+}
+
+extern "C" int sb_fp8_gemm_qkv_rope(const uint8_t* a, const float* a_scale, const uint8_t* b, const float* b_scale,
+                                    int64_t M, int heads, int K, const void* bias, const float* norm_q,
+                                    const float* norm_k, const float* rope, int rope_stride, const int32_t* coords,
+                                    const int8_t* axis, int shards, float eps, void* q, void* k, void* v, int num_ctas,
+                                    void* stream) {
+  SB_CHECK_ARG(q && k && v && norm_q && norm_k && rope && coords && axis, "sb_fp8_gemm_qkv_rope: null pointer");
+  SB_CHECK_ARG(heads > 0 && heads % 2 == 0, "sb_fp8_gemm_qkv_rope: heads must be even (a tile holds two heads)");
+  SB_CHECK_ARG(shards > 0 && heads % shards == 0, "sb_fp8_gemm_qkv_rope: heads must split evenly across shards");
+  SB_CHECK_ARG(rope_stride > 0, "sb_fp8_gemm_qkv_rope: bad rope table stride");
+  SB_CHECK_ARG((((uintptr_t)q | (uintptr_t)k | (uintptr_t)v) % 16) == 0,
+               "sb_fp8_gemm_qkv_rope: q, k, v must be 16-byte aligned");
+  ProducerArgs prod{};
+  prod.qkv_out[0] = q;
+  prod.qkv_out[1] = k;
+  prod.qkv_out[2] = v;
+  prod.norm_w[0] = norm_q;
+  prod.norm_w[1] = norm_k;
+  prod.rope = rope;
+  prod.coords = coords;
+  prod.axis = axis;
+  prod.rope_stride = rope_stride;
+  prod.heads = heads;
+  prod.shards = shards;
+  prod.eps = eps;
+  return launch_fp8_gemm(a, a_scale, 1, b, b_scale, 1, M, 3 * heads * 128, K, bias, nullptr, nullptr, q, num_ctas,
+                         stream, &prod);
 }

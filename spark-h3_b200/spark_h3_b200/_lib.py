@@ -52,6 +52,8 @@ SIGNATURES = {
     "sb_fp8_quantize_tensor": (_i, [_vp, _i, _i64, _vp, _vp, _vp, _vp]),
     "sb_fp8_swiglu": (_i, [_vp, _i, _i64, _i, _vp, _vp]),
     "sb_fp8_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _i, _vp]),
+    "sb_fp8_gemm_qkv_rope": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, ctypes.c_float,
+                                  _vp, _vp, _vp, _i, _vp]),
     "sb_fp8_gemm_residual": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "sb_fp8_gelu_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
     "sb_fp8_quantize_segments": (_i, [_vp, _i64, _i, _i, _i64, _vp, _vp, _vp]),

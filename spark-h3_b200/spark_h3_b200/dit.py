@@ -100,7 +100,7 @@ class DiTStack:
     codes with per-channel scales."""
 
     def __init__(self, cfg: DiTConfig, grid, *, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
-                 spark_mode: str = "full", topk_ratio: float = 0.1, steps: int = 19):
+                 spark_mode: str = "full", topk_ratio: float = 0.1, steps: int = 19, fused_producer: bool = True):
         from .config import H3SparseAttentionConfig
         from .layout import PackedLayout
         from .processor import _Controller
@@ -128,6 +128,11 @@ class DiTStack:
                 ada=(torch.randn(6 * C, cfg.t_dim, device=self.device, generator=g) * 0.02).contiguous()))
         self.inv_freq, self.axis = rope_tables(cfg, self.device)
         self.coords = token_coords(self.grid, rank * self.local, self.local, self.device)
+        # (cos, sin) of every pair and coordinate value, for the GEMM-epilogue producer
+        self.fused_producer = fused_producer and cfg.heads % 2 == 0
+        self.rope_stride = max(self.grid)
+        ang = torch.arange(self.rope_stride, device=self.device, dtype=torch.float32)[None, :] * self.inv_freq[:, None]
+        self.rope = torch.stack((torch.cos(ang), torch.sin(ang)), dim=-1).contiguous()  # [D/2, stride, 2]
         sparse_cfg = H3SparseAttentionConfig.spark(num_inference_steps=steps, mode=spark_mode,
                                                    sol_route_topk_ratio=topk_ratio)
         self.controller = _Controller(sparse_cfg)
@@ -160,6 +165,19 @@ class DiTStack:
                   self.coords.data_ptr(), self.inv_freq.data_ptr(), self.axis.data_ptr(), self.local, cfg.heads,
                   cfg.head_dim, self.world, float(cfg.eps), q.data_ptr(), k.data_ptr(), v.data_ptr(),
                   _stream(self.device))
+        return q, k, v
+
+    def _qkv_producer(self, hq, hs, blk):
+        """The QKV projection with q/k RMSNorm and RoPE in its epilogue, written straight into
+        the all-to-all send layout (sb_fp8_gemm_qkv_rope)."""
+        cfg = self.cfg
+        codes, scale = blk["qkv"]
+        shape = (self.world, self.local, self.hp, cfg.head_dim)
+        q, k, v = (torch.empty(shape, device=self.device, dtype=torch.bfloat16) for _ in range(3))
+        _lib.call("sb_fp8_gemm_qkv_rope", hq.data_ptr(), hs.data_ptr(), codes.data_ptr(), scale.data_ptr(), self.local,
+                  cfg.heads, hq.shape[1], None, blk["norm_q"].data_ptr(), blk["norm_k"].data_ptr(), self.rope.data_ptr(),
+                  self.rope_stride, self.coords.data_ptr(), self.axis.data_ptr(), self.world, float(cfg.eps),
+                  q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, _stream(self.device))
         return q, k, v
 
     def _attention(self, q, k, v, layer: int, dense: bool):
@@ -199,9 +217,12 @@ class DiTStack:
         for layer, (blk, mod) in enumerate(zip(self.blocks, self.modulation(t))):
             shift1, scale1, gate1, shift2, scale2, gate2 = mod
             hq, hs = self._norm_quant(x, shift1, scale1)
-            qkv = fp8_gemm(hq, hs, *blk["qkv"])
-            q, k, v = self._qkv_rope(qkv, blk)
-            del qkv
+            if self.fused_producer:
+                q, k, v = self._qkv_producer(hq, hs, blk)
+            else:
+                qkv = fp8_gemm(hq, hs, *blk["qkv"])
+                q, k, v = self._qkv_rope(qkv, blk)
+                del qkv
             qh, kh, vh = (exchange_to_heads(t_, self.group).unsqueeze(0) for t_ in (q, k, v))
             o = self._attention(qh, kh, vh, layer, dense)
             del q, k, v, qh, kh, vh

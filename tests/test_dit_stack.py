@@ -100,3 +100,30 @@ def test_stack_step_matches_block_math(cuda_device, dense):
     cos = F.cosine_similarity(x.float().flatten(), ref.float().flatten(), dim=0).item()
     assert torch.isfinite(x).all()
     assert cos > 0.999 and diff <= 0.05 * ref.float().abs().max().item(), (cos, diff)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("world", [1, 2])
+def test_fused_producer_matches_separate_path(cuda_device, world):
+    """sb_fp8_gemm_qkv_rope (norm and RoPE in the GEMM epilogue) against sb_fp8_gemm +
+    sb_dit_qkv_norm_rope, in the send layout of `world` shards."""
+    from spark_h3_b200.dit import DiTConfig, DiTStack
+
+    cfg = DiTConfig(hidden=512, heads=4, ffn=1024, blocks=1)
+    grid = (2, 16, 24)
+    stack = DiTStack(cfg, grid, device=cuda_device, world=world, rank=0, seed=3)
+    g = torch.Generator(device=cuda_device).manual_seed(7)
+    x = torch.randn(stack.local, cfg.hidden, device=cuda_device, generator=g).to(torch.bfloat16)
+    blk = stack.blocks[0]
+    mod = stack.modulation(500.0)[0]
+    hq, hs = stack._norm_quant(x, mod[0], mod[1])
+    fused = stack._qkv_producer(hq, hs, blk)
+    from spark_h3_b200.fp8_linear import fp8_gemm
+
+    separate = stack._qkv_rope(fp8_gemm(hq, hs, *blk["qkv"]), blk)
+    torch.cuda.synchronize()
+    for a, b in zip(fused, separate):
+        assert a.shape == b.shape == (world, stack.local, cfg.heads // world, 128)
+        diff = (a.float() - b.float()).abs()
+        assert diff.max().item() <= 2e-2 * b.float().abs().max().item() + 1e-3
+        assert (a == b).float().mean().item() > 0.9  # same bf16 values but for sin/cos rounding
