@@ -183,7 +183,7 @@ def run_reference(args) -> None:
                 config=dict(workload="config1: one sparse attention layer, N=124992 (31x48x84), H=32, D=128, "
                                      "block 128, topk 0.1, reweight summaries", extrapolated=True),
                 cpu_baseline=base, e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
-    print(json.dumps(line), flush=True)
+    emit(json.dumps(line), flush=True)
 
 
 def run_ours(args) -> None:
@@ -264,7 +264,7 @@ def run_ours(args) -> None:
     value = total_dense / (ms_per_step * 1e-3) / 1e12
     if PROFILE_ONLY:
         if rank == 0:
-            print(json.dumps(dict(profile_case=True, grid=GRID, heads=HEADS, ms_per_step=ms_per_step,
+            emit(json.dumps(dict(profile_case=True, grid=GRID, heads=HEADS, ms_per_step=ms_per_step,
                                   attention_kernel_ms=attn_ms)), flush=True)
         if world > 1:
             dist.destroy_process_group()
@@ -347,7 +347,7 @@ def run_ours(args) -> None:
         )
         if world == 1 and not args.no_cpu_baseline:
             line["cpu_baseline"] = cpu_baseline(sample_blocks=args.cpu_sample_blocks)
-        print(json.dumps(line), flush=True)
+        emit(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -399,7 +399,7 @@ def run_config2(args) -> None:
     with ClockSampler(0) as clocks:
         ms = _timed(layer, args.steps, args.warmup, stream)
     if args.profile_only:
-        print(json.dumps(dict(profile_case=True, workload="config2", grid=grid, heads=heads, ms_per_step=ms)),
+        emit(json.dumps(dict(profile_case=True, workload="config2", grid=grid, heads=heads, ms_per_step=ms)),
               flush=True)
         return
     # stage breakdown (same inputs, same stream)
@@ -440,7 +440,7 @@ def run_config2(args) -> None:
                       peak_source=peaks["source"].replace("bf16 sustained", "HBM copy"),
                       note="algorithmic bytes: 64 rows x N x 128 x 2 B read + the same written"),
         clocks=clocks.summary(), device_status=status)
-    print(json.dumps(line), flush=True)
+    emit(json.dumps(line), flush=True)
 
 
 def run_tails(args) -> None:
@@ -471,7 +471,7 @@ def run_tails(args) -> None:
             ms[f"{tail}/{math_}/{key}"] = _timed(layer, args.steps, args.warmup, stream)
     status = ops.read_device_status(dev)
     T = q.shape[1]
-    print(json.dumps(dict(
+    emit(json.dumps(dict(
         metric="Spark layer ms per tail granularity and summary numerics (ablations)", value=ms["block/tensorcore/stored"],
         unit="ms", n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms["block/tensorcore/stored"],
         higher_is_better=False, scaling="strong", vs_baseline=None, dtype="bf16",
@@ -540,7 +540,28 @@ def run_fp8(args) -> None:
                       unit="TFLOP/s", frac=best["tflops"] / fp8_peak, traffic=None,
                       peak_source="2 x " + peaks["source"] + " (e4m3 issues at twice the bf16 rate)"),
         clocks=clocks.summary(), device_status=status)
-    print(json.dumps(line), flush=True)
+    emit(json.dumps(line), flush=True)
+
+
+_JSON_OUT = None
+
+
+def keep_stdout_for_json() -> None:
+    """The JSON line is the only thing this program writes to its stdout: the real stdout is
+    kept on a private descriptor and fd 1 is pointed at stderr, so banners that libraries
+    print to fd 1 (NCCL's version line among them) cannot mix into it."""
+    global _JSON_OUT
+    if _JSON_OUT is None:
+        sys.stdout.flush()
+        _JSON_OUT = os.fdopen(os.dup(1), "w", buffering=1)
+        os.dup2(2, 1)
+
+
+def emit(text: str, flush: bool = True) -> None:
+    out = _JSON_OUT if _JSON_OUT is not None else sys.stdout
+    out.write(text + "\n")
+    if flush:
+        out.flush()
 
 
 def quiet_nccl() -> None:
@@ -622,13 +643,14 @@ def run_config4(args) -> None:
             sparse_step_ms=sparse_ms, dense_step_ms=dense_ms,
             all_to_all_bytes_per_layer=a2a if world > 1 else 0,
             clocks=clocks.summary(), device_status=status)
-        print(json.dumps(line), flush=True)
+        emit(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
 
 
 def main():
+    keep_stdout_for_json()
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
