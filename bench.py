@@ -596,7 +596,7 @@ def run_config4(args) -> None:
     heads = args.heads or 32
     cfg = DiTConfig(hidden=heads * 128, heads=heads, ffn=4 * heads * 128)
     stack = DiTStack(cfg, grid, device=dev, world=world, rank=rank, seed=0, spark_mode=args.spark_mode,
-                     topk_ratio=TOPK_RATIO)
+                     topk_ratio=TOPK_RATIO, peer_exchange=not args.nccl_exchange)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn(stack.local, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
@@ -638,12 +638,15 @@ def run_config4(args) -> None:
             config=dict(workload=f"config4: {cfg.blocks} blocks, hidden {cfg.hidden}, {heads} heads x 128, FFN "
                                  f"{cfg.ffn} GELU, N={T} ({'x'.join(map(str, grid))}), Spark mode "
                                  f"{args.spark_mode} topk {TOPK_RATIO}",
-                        parallelism=(f"tokens/{world} for pointwise + GEMMs, heads/{world} for attention, NCCL "
-                                     "all-to-all" if world > 1 else "single GPU")),
+                        parallelism=(f"tokens/{world} for pointwise + GEMMs, heads/{world} for attention; "
+                                     + ("q/k/v all-to-all by the QKV GEMM epilogue's stores to peer buffers "
+                                        "(CUDA IPC over NVLink), output all-to-all by NCCL" if stack.peer is not None
+                                        else "NCCL all-to-all") if world > 1 else "single GPU")),
             sparse_step_ms=sparse_ms, dense_step_ms=dense_ms,
             all_to_all_bytes_per_layer=a2a if world > 1 else 0,
             clocks=clocks.summary(), device_status=status)
         emit(json.dumps(line), flush=True)
+    stack.close()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -669,6 +672,8 @@ def main():
                     help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3), "
                          "config4 (DiT block stack, multi-GPU with torchrun), tails (tail granularity ablations)")
     ap.add_argument("--spark-mode", default="full", help="Spark mode of the config-4 sparse steps")
+    ap.add_argument("--nccl-exchange", action="store_true",
+                    help="config 4: NCCL all-to-all for q/k/v instead of the producer's peer stores")
     ap.add_argument("--fp8-rows", type=int, default=124992, help="token rows M of the fp8 workload")
     ap.add_argument("--reference-sample-blocks", type=int, default=16,
                     help="query blocks of the one-head CPU attention sample of each --impl reference step")

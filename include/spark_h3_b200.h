@@ -65,6 +65,18 @@ int sb_read_device_status(void* stream);
 int sb_selftest_wait_timeout(long long limit_cycles, int* result, void* stream);
 
 /*
+ * Peer memory between the processes of one node (one per GPU; no counterpart in the
+ * reference): sb_ipc_alloc allocates a device buffer whose CUDA IPC handle (64 bytes,
+ * sb_ipc_handle) another process maps with sb_ipc_open (peer access enabled lazily) and
+ * unmaps with sb_ipc_close; sb_ipc_free releases the allocation.
+ */
+int sb_ipc_alloc(int64_t bytes, void** ptr);
+int sb_ipc_free(void* ptr);
+int sb_ipc_handle(const void* ptr, uint8_t* handle);
+int sb_ipc_open(const uint8_t* handle, void** ptr);
+int sb_ipc_close(void* ptr);
+
+/*
  * Query block pooling.  Replaces the query-centroid half of
  * h3_sparse_attention/spark_integration.py:111-127 (_sol_topk_policy_scores) and the
  * per-64-row partial sums of sol_numerator_virtual_q.py:268-285 (_anchor_parts).
@@ -292,6 +304,20 @@ int sb_fp8_gemm_qkv_rope(const uint8_t* a, const float* a_scale, const uint8_t* 
                          int64_t M, int heads, int K, const void* bias, const float* norm_q, const float* norm_k,
                          const float* rope, int rope_stride, const int32_t* coords, const int8_t* axis, int shards,
                          float eps, void* q, void* k, void* v, int num_ctas, void* stream);
+
+/*
+ * sb_fp8_gemm_qkv_rope whose epilogue performs the sequence-to-head all-to-all itself:
+ * peers is a device table [3][shards] of receive buffers (q, k, v; entry [s][r] is rank r's
+ * buffer, [shards][M][heads / shards][128] bf16 each, mapped into this process with
+ * sb_ipc_open), and head h of row m is stored over NVLink to
+ * peers[section][h / hp] + ((rank * M + m) * hp + h % hp) * 128.  The caller orders the
+ * ranks' kernels before any rank reads its buffers (a stream-ordered collective serves).
+ */
+int sb_fp8_gemm_qkv_rope_peers(const uint8_t* a, const float* a_scale, const uint8_t* b, const float* b_scale,
+                               int64_t M, int heads, int K, const void* bias, const float* norm_q,
+                               const float* norm_k, const float* rope, int rope_stride, const int32_t* coords,
+                               const int8_t* axis, int shards, int rank, float eps, void* const* peers, int num_ctas,
+                               void* stream);
 
 /*
  * GELU (erf form) fused with the e4m3 row quantiser: quantize_rows(gelu(x)) of an FFN up

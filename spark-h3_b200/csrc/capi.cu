@@ -2,6 +2,7 @@
 // dispatcher (tensor-core kernel for bf16 / D = 128, SIMT kernel otherwise).
 #include <cstdarg>
 #include <cstdio>
+#include <cstring>
 #include <mutex>
 
 #include "common.cuh"
@@ -187,5 +188,49 @@ extern "C" int sb_selftest_wait_timeout(long long limit_cycles, int* result, voi
   if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_selftest_wait_timeout: status word");
   wait_timeout_kernel<<<1, 64, 0, (cudaStream_t)stream>>>(limit_cycles, status, result);
   SB_CHECK_LAUNCH("sb_selftest_wait_timeout launch");
+  return SB_OK;
+}
+
+// ------------------------------------------------------------------ peer memory (CUDA IPC)
+// Receive buffers that other processes of the node write into directly (one process per
+// GPU): allocated here so that the IPC handle covers exactly the buffer.
+extern "C" int sb_ipc_alloc(int64_t bytes, void** ptr) {
+  SB_CHECK_ARG(ptr && bytes > 0, "sb_ipc_alloc: bad arguments");
+  *ptr = nullptr;
+  cudaError_t err = cudaMalloc(ptr, (size_t)bytes);
+  if (err != cudaSuccess) return cuda_error(err, "sb_ipc_alloc");
+  return SB_OK;
+}
+
+extern "C" int sb_ipc_free(void* ptr) {
+  if (ptr == nullptr) return SB_OK;
+  cudaError_t err = cudaFree(ptr);
+  if (err != cudaSuccess) return cuda_error(err, "sb_ipc_free");
+  return SB_OK;
+}
+
+extern "C" int sb_ipc_handle(const void* ptr, uint8_t* handle) {
+  SB_CHECK_ARG(ptr && handle, "sb_ipc_handle: null pointer");
+  cudaIpcMemHandle_t h;
+  cudaError_t err = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (err != cudaSuccess) return cuda_error(err, "sb_ipc_handle");
+  memcpy(handle, &h, sizeof(h));
+  return SB_OK;
+}
+
+extern "C" int sb_ipc_open(const uint8_t* handle, void** ptr) {
+  SB_CHECK_ARG(handle && ptr, "sb_ipc_open: null pointer");
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle, sizeof(h));
+  *ptr = nullptr;
+  cudaError_t err = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (err != cudaSuccess) return cuda_error(err, "sb_ipc_open");
+  return SB_OK;
+}
+
+extern "C" int sb_ipc_close(void* ptr) {
+  if (ptr == nullptr) return SB_OK;
+  cudaError_t err = cudaIpcCloseMemHandle(ptr);
+  if (err != cudaSuccess) return cuda_error(err, "sb_ipc_close");
   return SB_OK;
 }

@@ -49,6 +49,11 @@ struct GemmParams {
   // qkv_out[section] + ((h / hp * M + m) * hp + h % hp) * 128, hp = heads / shards: the send
   // layout of the sequence-to-head all-to-all.
   __nv_bfloat16* qkv_out[3];
+  // With qkv_peers ([3][shards] device pointers, one receive buffer per section and rank),
+  // head h of row m goes to qkv_peers[section][h / hp] + ((peer_rank * M + m) * hp + h % hp)
+  // * 128 instead: the all-to-all itself, done by the epilogue's stores over NVLink.
+  __nv_bfloat16* const* qkv_peers;
+  int peer_rank;
   const float* norm_w[2];
   const float2* rope;
   const int32_t* coords;
@@ -298,7 +303,7 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       const bool row_ok = m < p.M;
       const float sa = row_ok ? __ldg(p.a_scale + m * p.a_scale_stride) : 0.f;
       __nv_bfloat16* out_row = p.out + m * p.N;
-      if (p.qkv_out[0] != nullptr) {
+      if (p.heads > 0) {
         // ------------------------------------------------ attention-input producer
         const int HD = p.heads * 128;
         const int section = n0 / HD;  // a 256-column tile never straddles q / k / v
@@ -306,7 +311,10 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
 #pragma unroll 1
         for (int hh = 0; hh < 2; ++hh) {
           const int h = (n0 - section * HD) / 128 + hh;
-          __nv_bfloat16* dst = p.qkv_out[section] + (((int64_t)(h / hp) * p.M + m) * hp + h % hp) * 128;
+          __nv_bfloat16* dst =
+              p.qkv_peers != nullptr
+                  ? p.qkv_peers[section * p.shards + h / hp] + (((int64_t)p.peer_rank * p.M + m) * hp + h % hp) * 128
+                  : p.qkv_out[section] + (((int64_t)(h / hp) * p.M + m) * hp + h % hp) * 128;
           const uint32_t col0 = buf * kPairAccCols + 128 * hh;
           float rstd = 1.f;
           if (section < 2) {
@@ -407,6 +415,7 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       __syncwarp();
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&C.acc_empty[buf]), 0));
     }
+    if (p.qkv_peers != nullptr) __threadfence_system();  // the stores to peer buffers, before exit
   }
   tc_fence_before();
   __syncthreads();
@@ -763,6 +772,8 @@ extern "C" int sb_fp8_swiglu(const void* h, int dtype, int64_t M, int K, void* a
 namespace {
 struct ProducerArgs {
   void* qkv_out[3];
+  void* const* peers;  // optional [3][shards] device table of receive buffers
+  int rank;
   const float* norm_w[2];
   const float* rope;
   const int32_t* coords;
@@ -809,6 +820,8 @@ int launch_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, 
   p.k_steps = (K + kPairBK - 1) / kPairBK;
   if (prod != nullptr) {
     for (int i = 0; i < 3; ++i) p.qkv_out[i] = static_cast<__nv_bfloat16*>(prod->qkv_out[i]);
+    p.qkv_peers = reinterpret_cast<__nv_bfloat16* const*>(prod->peers);
+    p.peer_rank = prod->rank;
     p.norm_w[0] = prod->norm_w[0];
     p.norm_w[1] = prod->norm_w[1];
     p.rope = reinterpret_cast<const float2*>(prod->rope);
@@ -890,4 +903,31 @@ extern "C" int sb_fp8_gemm_qkv_rope(const uint8_t* a, const float* a_scale, cons
   prod.eps = eps;
   return launch_fp8_gemm(a, a_scale, 1, b, b_scale, 1, M, 3 * heads * 128, K, bias, nullptr, nullptr, q, num_ctas,
                          stream, &prod);
+}
+
+extern "C" int sb_fp8_gemm_qkv_rope_peers(const uint8_t* a, const float* a_scale, const uint8_t* b,
+                                          const float* b_scale, int64_t M, int heads, int K, const void* bias,
+                                          const float* norm_q, const float* norm_k, const float* rope,
+                                          int rope_stride, const int32_t* coords, const int8_t* axis, int shards,
+                                          int rank, float eps, void* const* peers, int num_ctas, void* stream) {
+  SB_CHECK_ARG(peers && norm_q && norm_k && rope && coords && axis, "sb_fp8_gemm_qkv_rope_peers: null pointer");
+  SB_CHECK_ARG(heads > 0 && heads % 2 == 0, "sb_fp8_gemm_qkv_rope_peers: heads must be even");
+  SB_CHECK_ARG(shards > 0 && heads % shards == 0 && rank >= 0 && rank < shards,
+               "sb_fp8_gemm_qkv_rope_peers: bad shard count or rank");
+  SB_CHECK_ARG(rope_stride > 0, "sb_fp8_gemm_qkv_rope_peers: bad rope table stride");
+  ProducerArgs prod{};
+  prod.peers = peers;
+  prod.rank = rank;
+  prod.norm_w[0] = norm_q;
+  prod.norm_w[1] = norm_k;
+  prod.rope = rope;
+  prod.coords = coords;
+  prod.axis = axis;
+  prod.rope_stride = rope_stride;
+  prod.heads = heads;
+  prod.shards = shards;
+  prod.eps = eps;
+  // `out` is not written in producer mode; any 16-byte-aligned pointer passes the checks.
+  return launch_fp8_gemm(a, a_scale, 1, b, b_scale, 1, M, 3 * heads * 128, K, bias, nullptr, nullptr,
+                         const_cast<uint8_t*>(a), num_ctas, stream, &prod);
 }

@@ -54,6 +54,13 @@ SIGNATURES = {
     "sb_fp8_gemm": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _i, _vp]),
     "sb_fp8_gemm_qkv_rope": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, ctypes.c_float,
                                   _vp, _vp, _vp, _i, _vp]),
+    "sb_fp8_gemm_qkv_rope_peers": (_i, [_vp, _vp, _vp, _vp, _i64, _i, _i, _vp, _vp, _vp, _vp, _i, _vp, _vp, _i, _i,
+                                        ctypes.c_float, _vp, _i, _vp]),
+    "sb_ipc_alloc": (_i, [_i64, _vp]),
+    "sb_ipc_free": (_i, [_vp]),
+    "sb_ipc_handle": (_i, [_vp, _vp]),
+    "sb_ipc_open": (_i, [_vp, _vp]),
+    "sb_ipc_close": (_i, [_vp]),
     "sb_fp8_gemm_residual": (_i, [_vp, _vp, _i, _vp, _vp, _i, _i64, _i, _i, _vp, _vp, _vp, _vp, _i, _vp]),
     "sb_fp8_gelu_quantize_rows": (_i, [_vp, _i, _i64, _i, _vp, _vp, _vp]),
     "sb_fp8_quantize_segments": (_i, [_vp, _i64, _i, _i, _i64, _vp, _vp, _vp]),

@@ -94,13 +94,82 @@ def exchange_to_tokens(out: torch.Tensor, world: int, group=None) -> torch.Tenso
     return recv
 
 
+class _DeviceBuffer:
+    """A torch view of a raw device allocation (bf16 as uint16 through the CUDA array
+    interface, then viewed back)."""
+
+    def __init__(self, ptr: int, shape, device):
+        self.__cuda_array_interface__ = dict(shape=tuple(shape), typestr="<u2", data=(ptr, False), version=3,
+                                             strides=None)
+        self.device = device
+
+    def tensor(self) -> torch.Tensor:
+        return torch.as_tensor(self, device=self.device).view(torch.bfloat16)
+
+
+class PeerExchange:
+    """Receive buffers for q, k and v [P, Nloc, Hp, D] that every rank's QKV producer writes
+    into directly over NVLink (the all-to-all done by the GEMM epilogue): allocated here,
+    mapped into the other processes of the node with CUDA IPC, and listed in a device table
+    [3][P] for the kernel."""
+
+    def __init__(self, shape, device, world: int, rank: int, group=None):
+        import ctypes
+
+        self.shape, self.device, self.world, self.rank = tuple(shape), torch.device(device), world, rank
+        nbytes = int(math.prod(self.shape)) * 2
+        self.local, self.opened = [], []
+        handles = []
+        for _ in range(3):
+            ptr = ctypes.c_void_p()
+            _lib.call("sb_ipc_alloc", nbytes, ctypes.byref(ptr))
+            self.local.append(ptr.value)
+            h = (ctypes.c_uint8 * 64)()
+            _lib.call("sb_ipc_handle", ptr.value, h)
+            handles.append(bytes(h))
+        gathered = [None] * world
+        dist.all_gather_object(gathered, handles, group=group)
+        table = []
+        for sec in range(3):
+            for r in range(world):
+                if r == rank:
+                    table.append(self.local[sec])
+                    continue
+                h = (ctypes.c_uint8 * 64).from_buffer_copy(gathered[r][sec])
+                ptr = ctypes.c_void_p()
+                _lib.call("sb_ipc_open", h, ctypes.byref(ptr))
+                table.append(ptr.value)
+                self.opened.append(ptr.value)
+        self.table = torch.tensor(table, dtype=torch.int64, device=self.device)
+        self.views = [_DeviceBuffer(ptr, self.shape, self.device).tensor() for ptr in self.local]
+        self.flag = torch.zeros(1, dtype=torch.float32, device=self.device)
+        self.group = group
+
+    def barrier(self):
+        """Stream-ordered: returns once every rank's producer kernel before it has completed."""
+        dist.all_reduce(self.flag, group=self.group)
+
+    def close(self):
+        """Unmap the peers' buffers, wait for every rank to do the same, free ours."""
+        torch.cuda.synchronize(self.device)
+        for ptr in self.opened:
+            _lib.call("sb_ipc_close", ptr)
+        self.opened = []
+        dist.barrier(group=self.group)
+        self.views = []
+        for ptr in self.local:
+            _lib.call("sb_ipc_free", ptr)
+        self.local = []
+
+
 class DiTStack:
     """The block stack on one rank.  Weights are generated from `seed` identically on every
     rank (so a P-rank run computes the same model as a 1-rank run) and kept only as e4m3
     codes with per-channel scales."""
 
     def __init__(self, cfg: DiTConfig, grid, *, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
-                 spark_mode: str = "full", topk_ratio: float = 0.1, steps: int = 19, fused_producer: bool = True):
+                 spark_mode: str = "full", topk_ratio: float = 0.1, steps: int = 19, fused_producer: bool = True,
+                 peer_exchange: bool = True):
         from .config import H3SparseAttentionConfig
         from .layout import PackedLayout
         from .processor import _Controller
@@ -136,6 +205,11 @@ class DiTStack:
         sparse_cfg = H3SparseAttentionConfig.spark(num_inference_steps=steps, mode=spark_mode,
                                                    sol_route_topk_ratio=topk_ratio)
         self.controller = _Controller(sparse_cfg)
+        # With several ranks, the producer's epilogue stores q, k, v into the owners' receive
+        # buffers itself (NCCL all-to-all otherwise).
+        self.peer = None
+        if world > 1 and peer_exchange and self.fused_producer:
+            self.peer = PeerExchange((world, self.local, self.hp, cfg.head_dim), self.device, world, rank, group)
         ids = torch.arange(self.tokens)
         self.layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=self.grid, video_tokens=self.tokens,
                                    sequence_length=self.tokens, video_positions=torch.zeros(self.tokens, 3,
@@ -180,6 +254,21 @@ class DiTStack:
                   q.data_ptr(), k.data_ptr(), v.data_ptr(), 0, _stream(self.device))
         return q, k, v
 
+    def _qkv_producer_peers(self, hq, hs, blk):
+        """The producer with the all-to-all in its epilogue: every head row goes straight to
+        its owner's receive buffer (sb_fp8_gemm_qkv_rope_peers)."""
+        cfg = self.cfg
+        codes, scale = blk["qkv"]
+        _lib.call("sb_fp8_gemm_qkv_rope_peers", hq.data_ptr(), hs.data_ptr(), codes.data_ptr(), scale.data_ptr(),
+                  self.local, cfg.heads, hq.shape[1], None, blk["norm_q"].data_ptr(), blk["norm_k"].data_ptr(),
+                  self.rope.data_ptr(), self.rope_stride, self.coords.data_ptr(), self.axis.data_ptr(), self.world,
+                  self.rank, float(cfg.eps), self.peer.table.data_ptr(), 0, _stream(self.device))
+
+    def close(self):
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
+
     def _attention(self, q, k, v, layer: int, dense: bool):
         if dense:
             o = F.scaled_dot_product_attention(q.transpose(1, 2), k.transpose(1, 2), v.transpose(1, 2))
@@ -217,15 +306,21 @@ class DiTStack:
         for layer, (blk, mod) in enumerate(zip(self.blocks, self.modulation(t))):
             shift1, scale1, gate1, shift2, scale2, gate2 = mod
             hq, hs = self._norm_quant(x, shift1, scale1)
-            if self.fused_producer:
-                q, k, v = self._qkv_producer(hq, hs, blk)
+            if self.peer is not None:
+                self._qkv_producer_peers(hq, hs, blk)
+                self.peer.barrier()
+                qh, kh, vh = (t_.reshape(-1, self.hp, self.cfg.head_dim).unsqueeze(0) for t_ in self.peer.views)
             else:
-                qkv = fp8_gemm(hq, hs, *blk["qkv"])
-                q, k, v = self._qkv_rope(qkv, blk)
-                del qkv
-            qh, kh, vh = (exchange_to_heads(t_, self.group).unsqueeze(0) for t_ in (q, k, v))
+                if self.fused_producer:
+                    q, k, v = self._qkv_producer(hq, hs, blk)
+                else:
+                    qkv = fp8_gemm(hq, hs, *blk["qkv"])
+                    q, k, v = self._qkv_rope(qkv, blk)
+                    del qkv
+                qh, kh, vh = (exchange_to_heads(t_, self.group).unsqueeze(0) for t_ in (q, k, v))
+                del q, k, v
             o = self._attention(qh, kh, vh, layer, dense)
-            del q, k, v, qh, kh, vh
+            del qh, kh, vh
             oq, os_ = self._out_quant(exchange_to_tokens(o[0], self.world, self.group))
             self._gemm_residual(oq, os_, blk["out"], x, gate1)
             hq, hs = self._norm_quant(x, shift2, scale2)

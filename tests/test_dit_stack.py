@@ -127,3 +127,56 @@ def test_fused_producer_matches_separate_path(cuda_device, world):
         diff = (a.float() - b.float()).abs()
         assert diff.max().item() <= 2e-2 * b.float().abs().max().item() + 1e-3
         assert (a == b).float().mean().item() > 0.9  # same bf16 values but for sin/cos rounding
+
+
+def _peer_worker(rank, world, port, results):
+    import os
+    from datetime import timedelta
+
+    from spark_h3_b200.dit import DiTConfig, DiTStack
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    os.environ["NCCL_NVLS_ENABLE"] = "0"
+    torch.cuda.set_device(rank)
+    dev = torch.device("cuda", rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60), device_id=dev)
+    try:
+        cfg = DiTConfig(hidden=256, heads=4, ffn=512, blocks=2)
+        outs = []
+        for peer in (True, False):
+            stack = DiTStack(cfg, (2, 16, 32), device=dev, world=world, rank=rank, seed=0,
+                             spark_mode="reweight_only", peer_exchange=peer)
+            assert (stack.peer is not None) == peer
+            g = torch.Generator(device=dev).manual_seed(100 + rank)
+            x = torch.randn(stack.local, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+            for dense in (True, False, False):
+                stack.step(x, 500.0, dense=dense)
+            torch.cuda.synchronize()
+            outs.append(x.clone())
+            stack.close()
+        results.put((rank, bool(torch.equal(outs[0], outs[1])), bool(torch.isfinite(outs[0]).all())))
+    except Exception as e:  # pragma: no cover - reported to the parent
+        results.put((rank, f"error: {e!r}", False))
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.gpu
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs two GPUs")
+def test_peer_exchange_matches_nccl_two_gpus():
+    """Two ranks, one per GPU: the stack with the all-to-all done by the producer's peer
+    stores equals the stack with the NCCL all-to-all, bit for bit, over dense and sparse
+    steps."""
+    import torch.multiprocessing as mp
+
+    ctx = mp.get_context("spawn")
+    results = ctx.Queue()
+    port = 29600 + (os.getpid() % 200)
+    procs = [ctx.Process(target=_peer_worker, args=(r, 2, port, results)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = [results.get(timeout=240) for _ in procs]
+    for p in procs:
+        p.join(timeout=60)
+    assert all(r[1] is True and r[2] for r in got), got
