@@ -111,7 +111,7 @@ def test_fused_producer_matches_separate_path(cuda_device, world):
 
     cfg = DiTConfig(hidden=512, heads=4, ffn=1024, blocks=1)
     grid = (2, 16, 24)
-    stack = DiTStack(cfg, grid, device=cuda_device, world=world, rank=0, seed=3)
+    stack = DiTStack(cfg, grid, device=cuda_device, world=world, rank=0, seed=3, peer_exchange=False)
     g = torch.Generator(device=cuda_device).manual_seed(7)
     x = torch.randn(stack.local, cfg.hidden, device=cuda_device, generator=g).to(torch.bfloat16)
     blk = stack.blocks[0]
