@@ -596,7 +596,7 @@ def run_config4(args) -> None:
     heads = args.heads or 32
     cfg = DiTConfig(hidden=heads * 128, heads=heads, ffn=4 * heads * 128)
     stack = DiTStack(cfg, grid, device=dev, world=world, rank=rank, seed=0, spark_mode=args.spark_mode,
-                     topk_ratio=TOPK_RATIO, peer_exchange=not args.nccl_exchange)
+                     topk_ratio=TOPK_RATIO, peer_exchange=args.peer_exchange)
     g = torch.Generator(device=dev).manual_seed(1000 + rank)
     x = torch.randn(stack.local, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
     stream = torch.cuda.current_stream(dev)
@@ -672,8 +672,9 @@ def main():
                     help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3), "
                          "config4 (DiT block stack, multi-GPU with torchrun), tails (tail granularity ablations)")
     ap.add_argument("--spark-mode", default="full", help="Spark mode of the config-4 sparse steps")
-    ap.add_argument("--nccl-exchange", action="store_true",
-                    help="config 4: NCCL all-to-all for q/k/v instead of the producer's peer stores")
+    ap.add_argument("--peer-exchange", action="store_true",
+                    help="config 4: the QKV producer's epilogue stores q/k/v to the owners' buffers over NVLink "
+                         "instead of the NCCL all-to-all")
     ap.add_argument("--fp8-rows", type=int, default=124992, help="token rows M of the fp8 workload")
     ap.add_argument("--reference-sample-blocks", type=int, default=16,
                     help="query blocks of the one-head CPU attention sample of each --impl reference step")

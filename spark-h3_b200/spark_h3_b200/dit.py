@@ -169,7 +169,7 @@ class DiTStack:
 
     def __init__(self, cfg: DiTConfig, grid, *, device, world: int = 1, rank: int = 0, group=None, seed: int = 0,
                  spark_mode: str = "full", topk_ratio: float = 0.1, steps: int = 19, fused_producer: bool = True,
-                 peer_exchange: bool = True):
+                 peer_exchange: bool = False):
         from .config import H3SparseAttentionConfig
         from .layout import PackedLayout
         from .processor import _Controller
@@ -205,8 +205,9 @@ class DiTStack:
         sparse_cfg = H3SparseAttentionConfig.spark(num_inference_steps=steps, mode=spark_mode,
                                                    sol_route_topk_ratio=topk_ratio)
         self.controller = _Controller(sparse_cfg)
-        # With several ranks, the producer's epilogue stores q, k, v into the owners' receive
-        # buffers itself (NCCL all-to-all otherwise).
+        # With several ranks and peer_exchange, the producer's epilogue stores q, k, v into the
+        # owners' receive buffers itself; by default NCCL's all-to-all moves them (measured
+        # slightly faster at 2 GPUs: its large transfers beat the epilogue's 16-byte row stores).
         self.peer = None
         if world > 1 and peer_exchange and self.fused_producer:
             self.peer = PeerExchange((world, self.local, self.hp, cfg.head_dim), self.device, world, rank, group)
