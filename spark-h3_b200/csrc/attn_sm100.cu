@@ -3,7 +3,7 @@
 // One CTA per (128-row query tile, head, batch).  Roles (384 threads):
 //   warps 0-3  softmax group 0: row r = TMEM lane r, key columns 0-63 of every tile
 //   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
-//   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages
+//   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages (2 on long sequences)
 //   warp 9     TMA producer of the V (or AV summary) tiles, 2 stages
 //   warp 10    tcgen05 issuer of S = Q K^T (one 128 x 64 product per group); owns TMEM
 //   warp 11    tcgen05 issuer of O += P V (one per group)
@@ -54,8 +54,9 @@ constexpr int kProducerWarp = 8;   // Q and K
 constexpr int kProducerVWarp = 9;  // V
 constexpr int kMmaWarp = 10;       // S issuer
 constexpr int kPvWarp = 11;        // P.V issuer
-constexpr int kKStages = 3;
+constexpr int kKStages = 3;  // K ring depth when it fits; 2 on long sequences (below)
 constexpr int kVStages = 2;
+constexpr uint32_t kSmemLimit = 227 * 1024;
 static_assert(kVStages == 2, "the P.V issue and the rescale wait index V stages by tile parity");
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 bf16 operand tile
 constexpr int kHalfBytes = 128 * 64 * 2;   // one 64-column half of it
@@ -95,13 +96,19 @@ struct SmemLayout {
   uint32_t q, k, v;  // byte offsets from the 1024-aligned base (stages are consecutive)
   uint32_t ctrl, ebits, ubits, lm, glist;
   uint32_t total;
+  int k_stages;
 };
 
-__host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran, int nb_pad) {
+// The per-sequence tables (route words, summary log-masses, granule list) grow with T; when
+// three K stages no longer fit beside them the ring drops to two.  With 64-key blocks that
+// moves the longest accepted sequence from about 330k to about 660k tokens (128-key blocks:
+// about 500k to 990k).
+__host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int words_gran, int nb_pad, int k_stages) {
   SmemLayout L;
+  L.k_stages = k_stages;
   L.q = 0;
   L.k = kTileBytes;
-  L.v = L.k + kKStages * kTileBytes;
+  L.v = L.k + k_stages * kTileBytes;
   L.ctrl = L.v + kVStages * kTileBytes;
   L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);  // Control is small
   L.ubits = L.ebits + (uint32_t)((2 * words_blk * 4 + 15) / 16 * 16);  // every region 16-byte aligned
@@ -109,6 +116,11 @@ __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran,
   L.glist = L.lm + (uint32_t)(nb_pad * 4);  // LM * log2(e) of every key block
   L.total = L.glist + (uint32_t)((words_gran * 32 * 2 + 15) / 16 * 16);  // exact granules in order (uint16)
   return L;
+}
+
+__host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran, int nb_pad) {
+  const SmemLayout L = smem_layout_stages(words_blk, words_gran, nb_pad, kKStages);
+  return L.total <= kSmemLimit ? L : smem_layout_stages(words_blk, words_gran, nb_pad, 2);
 }
 
 // 2^x on the FMA/ALU pipes (offloads the MUFU unit): round-to-nearest range reduction
@@ -183,7 +195,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
     mbar_init(smem_u32(&C.bar_q_full), 1);
-    for (int s = 0; s < kKStages; ++s) {
+    for (int s = 0; s < L.k_stages; ++s) {
       mbar_init(smem_u32(&C.bar_k_full[s]), 1);
       mbar_init(smem_u32(&C.bar_k_empty[s]), 1);
     }
@@ -304,7 +316,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     // so a slow P.V never delays the next K tile.
     if (lane == 0) {
       const bool is_k = warp == kProducerWarp;
-      const int stages = is_k ? kKStages : kVStages;
+      const int stages = is_k ? L.k_stages : kVStages;
       const CUtensorMap* exact_map = is_k ? &tm_k : &tm_v;
       const CUtensorMap* summ_map = is_k ? &tm_ak : &tm_av;
       const uint32_t s_base = is_k ? sK0 : sV0;
@@ -391,7 +403,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         if (!ok) break;
         SB_TRACE_POINT(trace, 3, j);
         tc_commit(smem_u32(&C.bar_k_empty[ks]));
-        if (++ks == kKStages) {
+        if (++ks == L.k_stages) {
           ks = 0;
           ++kuse;
         }
@@ -711,7 +723,7 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
   const int n64 = ceil_div(p.T, 64);
   const SmemLayout L = smem_layout(p.words, ceil_div(n64, 32), 128 * ceil_div(p.NB, 128));
   const size_t smem = L.total;
-  if (smem > 227 * 1024) {
+  if (smem > kSmemLimit) {
     set_error("sb_sparse_attention: sequence too long for the tensor-core kernel (%zu bytes of shared memory)", smem);
     return SB_ERR_UNSUPPORTED;
   }

@@ -293,3 +293,66 @@ def test_batch_of_two_matches_oracle(cuda_device, block, granularity):
     assert not np.array_equal(ref["indices"][0], ref["indices"][1])
     for b in range(2):
         _check(as_np(out)[b], ref["out"][b], torch.bfloat16)
+
+
+def _long_sequence_case(T: int, block: int, seed: int):
+    """Seeded bf16 Q/K/V for one head, a random route (eight routed key blocks per query
+    block), and random summaries: sized so that the route tables crowd the shared memory."""
+    g = torch.Generator().manual_seed(seed)
+    q, k, v = (torch.randn((1, T, 1, 128), generator=g).to(torch.bfloat16) for _ in range(3))
+    q = (q.float() * 128 ** -0.5).to(torch.bfloat16)
+    nb = -(-T // block)
+    words = -(-nb // 32)
+    rng = np.random.default_rng(seed)
+    bits = np.zeros((1, nb, 1, words * 32), dtype=np.uint8)
+    for qb in range(nb):
+        bits[0, qb, 0, rng.choice(nb, 8, replace=False)] = 1
+        bits[0, qb, 0, qb] = 1
+    packed = np.packbits(bits, axis=-1, bitorder="little").view(np.int32)
+    ak = (rng.standard_normal((1, 1, nb, 128)) * 0.5).astype(np.float32)
+    av = rng.standard_normal((1, 1, nb, 128)).astype(np.float32)
+    lm = rng.uniform(0.0, 4.0, (1, 1, nb)).astype(np.float32)
+    return q, k, v, packed, ak, av, lm
+
+
+def test_long_sequence_two_stage_key_ring(cuda_device):
+    # 400,037 tokens in 64-token blocks: the per-sequence tables leave room for two K stages
+    # only.  Rows of the first, a middle and the ragged last query tile are checked; the last
+    # tile holds routed rows and the 37 dense-suffix rows past the last whole block.
+    T, block = 400_037, 64
+    routed = T // block * block
+    q, k, v, packed, ak, av, lm = _long_sequence_case(T, block, seed=31)
+    dev = cuda_device
+    bf = lambda a: torch.from_numpy(a).to(dev, torch.bfloat16)
+    ak_d, av_d = bf(ak), bf(av)
+    out, lse = ops.sparse_attention(q.to(dev), k.to(dev), v.to(dev), block, torch.from_numpy(packed).to(dev),
+                                    ak_d, av_d, torch.from_numpy(lm).to(dev), query_tokens=routed,
+                                    sink_first=0, sink_last=0, want_lse=True)
+    torch.cuda.synchronize()
+    assert ops.read_device_status(dev) == 0
+    out, lse = as_np(out), as_np(lse)
+    ak_r, av_r = as_np(ak_d), as_np(av_d)  # the summaries as the kernel saw them (bf16)
+    last = (T - 1) // 128 * 128
+    oq, ok_, ov = to_oracle(q), to_oracle(k), to_oracle(v)
+    for r0, r1 in ((0, 128), (200_064, 200_192), (last, T)):
+        ref, ref_lse = oracle.sparse_attention(oq, ok_, ov, block, packed, ak_r, av_r, lm, routed, 0, 0,
+                                               rows=slice(r0, r1))
+        _check(out[:, r0:r1], ref[:, r0:r1], torch.bfloat16)
+        np.testing.assert_allclose(lse[:, r0:r1], ref_lse[:, r0:r1], atol=2e-3, rtol=1e-4)
+
+
+def test_sequence_past_shared_memory_limit_fails_loudly(cuda_device):
+    # 700,000 tokens in 64-token blocks: even two K stages no longer fit beside the tables;
+    # the launcher refuses before any launch and the context stays usable.
+    T, block = 700_000, 64
+    dev = cuda_device
+    nb = -(-T // block)
+    q = torch.zeros((1, T, 1, 128), device=dev, dtype=torch.bfloat16)
+    packed = torch.zeros((1, nb, 1, -(-nb // 32)), device=dev, dtype=torch.int32)
+    ak = torch.zeros((1, 1, nb, 128), device=dev, dtype=torch.bfloat16)
+    lm = torch.zeros((1, 1, nb), device=dev, dtype=torch.float32)
+    with pytest.raises(RuntimeError, match="too long for the tensor-core kernel"):
+        ops.sparse_attention(q, q, q, block, packed, ak, ak, lm, query_tokens=T // block * block, sink_first=0,
+                             sink_last=0)
+    torch.cuda.synchronize()
+    assert ops.read_device_status(dev) == 0
