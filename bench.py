@@ -46,8 +46,8 @@ HEAD_DIM = 128
 BLOCK = 128
 TOPK_RATIO = 0.1
 # DRAM bytes per launch of the attention kernel at this workload, from the one-pass ncu
-# capture summarised in profiles/config1_layer_launch_list.md (4.69 GB read + 1.03 GB write).
-ATTENTION_TRAFFIC_BYTES = 5.72e9
+# capture summarised in profiles/config1_layer_launch_list.md (4.74 GB read + 1.02 GB write).
+ATTENTION_TRAFFIC_BYTES = 5.76e9
 
 
 def dense_flops(tokens: int, heads: int, dim: int) -> float:
