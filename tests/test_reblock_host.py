@@ -114,3 +114,21 @@ def test_reblock_reuse_across_layers(monkeypatch):
     assert run(1) == "qp9" and run(2) == "qp9"
     controller.reset()
     assert controller.spark_reblock_reuse_layers == 2  # settings survive reset, as in the reference
+
+
+def test_public_spark_names_match_reference_exports():
+    """h3_sparse_attention/__init__.py:12-36 and spark.py:34-39: spark_reblock, spark_reweight
+    and spark_block (the initial public name of spark_reblock) from the package root and from
+    the spark module, as the same objects."""
+    import spark_h3_b200
+    from spark_h3_b200 import spark
+
+    assert spark_h3_b200.spark_block is spark_h3_b200.spark_reblock is reblock.spark_reblock
+    assert spark.spark_reblock is spark_h3_b200.spark_reblock
+    assert spark.spark_block is spark_h3_b200.spark_reblock
+    assert spark.spark_reweight is spark_h3_b200.spark_reweight
+    assert spark.install_h3_spark_attn is spark_h3_b200.install_h3_spark_attn
+    for name in ("spark_reblock", "spark_reweight", "spark_block", "install_fp8", "Fp8Linear",
+                 "convert_linear_to_fp8", "install_h3_spark_attn", "install_h3_sol_attn",
+                 "install_h3_sparse_attention", "H3SparseAttentionConfig", "H3SparseAttentionPlugin"):
+        assert name in spark_h3_b200.__all__, name
