@@ -128,9 +128,16 @@ def route_topk(qc: torch.Tensor, kc: torch.Tensor, query_blocks: int, candidates
     return packed, indices
 
 
+def _check_query_prefix(query_tokens: int, tokens: int, block: int) -> None:
+    """The sparse query prefix ends on a query block (sol_numerator_virtual_q.py:755-756)."""
+    if query_tokens % block or not 0 <= query_tokens <= tokens:
+        raise ValueError("query_tokens must end at a physical query-block boundary")
+
+
 def sparse_attention(q, k, v, block: int, packed: torch.Tensor | None, ak, av, lm, *, query_tokens: int,
                      sink_first: int, sink_last: int, local_radius: int = -1, out: torch.Tensor | None = None,
                      want_lse: bool = False):
+    _check_query_prefix(query_tokens, q.shape[1], block)
     device = _require_cuda(q, k, v, packed, ak, av, lm, out)
     B, T, H, D = q.shape
     if k.shape != q.shape or v.shape != q.shape or k.dtype != q.dtype or v.dtype != q.dtype:
@@ -211,6 +218,7 @@ def tail_merge(q, ak, av, lm, packed: torch.Tensor, out: torch.Tensor, lse: torc
                entry_tokens: int, group_tokens: int, query_tokens: int, sink_first: int, sink_last: int,
                local_radius: int = -1) -> torch.Tensor:
     """Merges the pooled tail into the exact-only output and LSE in place (sb_tail_merge)."""
+    _check_query_prefix(query_tokens, q.shape[1], block)
     device = _require_cuda(q, ak, av, lm, packed, out, lse)
     B, T, H, D = q.shape
     with torch.cuda.device(device):

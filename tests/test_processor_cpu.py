@@ -105,6 +105,21 @@ def test_sparse_query_prefix_by_tail_mode():
         sparse_query_tokens(8329, 8193, 64, "wrap")
 
 
+def test_query_prefix_off_a_block_boundary_is_rejected():
+    # tests/test_global_reweight_followup.py:66-67: a sparse query prefix that does not end
+    # on a query block is a ValueError, raised before any device work.
+    from spark_h3_b200 import ops
+
+    q = torch.zeros(1, 8329, 1, 128, dtype=torch.bfloat16)
+    for bad in (8191, 8193, -64, 8384):
+        with pytest.raises(ValueError, match="query-block boundary"):
+            ops.sparse_attention(q, q, q, 64, None, None, None, None, query_tokens=bad, sink_first=0,
+                                 sink_last=0)
+        with pytest.raises(ValueError, match="query-block boundary"):
+            ops.tail_merge(q, None, None, None, None, q, None, block=64, entry_tokens=64, group_tokens=64,
+                           query_tokens=bad, sink_first=0, sink_last=0)
+
+
 def test_oracle_pad_fill_is_the_tail_mean():
     # The rows that pad the final video block hold the fp32 mean of its video rows rounded to
     # bf16, as q[:, tail:video].mean(1, dtype=float32).to(bf16) (spark_integration.py:1180-1187).
