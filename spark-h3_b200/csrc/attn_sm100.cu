@@ -575,35 +575,34 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       l_run *= alpha;
       const float base_m = m_run == -INFINITY ? 0.f : m_run;
       uint32_t pk[32];
-      uint64_t sums[2] = {0ull, 0ull};  // packed partial sums
+      float ps[4] = {0.f, 0.f, 0.f, 0.f};  // partial sums: even pairs in 0-1, odd pairs in 2-3
       if (!exact || vis) {
-        // p = 2^(s * scale - m) (fast path) or 2^(logit - m); pairs share one packed
-        // multiply-add.  kPolyEvery > 0 moves a share of the fast path's exponentials to
-        // the polynomial on the FMA pipe.
-        const uint64_t mul2 = fast ? f2_pack(scale_log2, scale_log2) : f2_pack(1.f, 1.f);
-        const uint64_t neg2 = f2_pack(-base_m, -base_m);
+        // p = 2^(s * scale - m) (fast path) or 2^(logit - m).  Scalar FFMA and FADD, not the
+        // packed fp32x2 forms: measured at config 1, 27.6 ms against 28.0 ms with both
+        // packed and 29.3-29.9 ms with only one of them packed (same results bit for bit).
+        // kPolyEvery > 0 moves a share of the fast path's exponentials to the polynomial
+        // on the FMA pipe.
+        const float mul = fast ? scale_log2 : 1.f;
 #pragma unroll
         for (int c = 0; c < 32; ++c) {
-          const uint64_t a2 = f2_fma(f2_pack(__uint_as_float(r[2 * c]), __uint_as_float(r[2 * c + 1])), mul2, neg2);
-          float a0, a1, p0, p1;
-          f2_unpack(a2, a0, a1);
+          const float a0 = fmaf(__uint_as_float(r[2 * c]), mul, -base_m);
+          const float a1 = fmaf(__uint_as_float(r[2 * c + 1]), mul, -base_m);
+          float p0, p1;
           if (kPolyEvery > 0 && fast && (c % (kPolyEvery > 0 ? kPolyEvery : 1)) == kPolyEvery - 1) {
             exp2_poly2(a0, a1, p0, p1);
           } else {
             p0 = ex2_approx(a0);
             p1 = ex2_approx(a1);
           }
-          sums[c & 1] = f2_add(sums[c & 1], f2_pack(p0, p1));
+          ps[2 * (c & 1)] += p0;
+          ps[2 * (c & 1) + 1] += p1;
           pk[c] = cvt_bf16x2(p0, p1);
         }
       } else {
 #pragma unroll
         for (int c = 0; c < 32; ++c) pk[c] = 0u;
       }
-      float s0, s1, s2, s3;
-      f2_unpack(sums[0], s0, s1);
-      f2_unpack(sums[1], s2, s3);
-      l_run += (s0 + s1) + (s2 + s3);
+      l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
       SB_TRACE_POINT(trace && tid == 0, 15, j);
       tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
