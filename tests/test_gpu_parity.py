@@ -356,3 +356,51 @@ def test_sequence_past_shared_memory_limit_fails_loudly(cuda_device):
                              sink_last=0)
     torch.cuda.synchronize()
     assert ops.read_device_status(dev) == 0
+
+
+@pytest.mark.parametrize("block", [64, 128])
+def test_route_ties_take_the_lowest_block_ids(cuda_device, block):
+    # Key blocks repeat with period 4, so every query block sees each distinct score on
+    # 1/4 of the candidates: the Top-K cut falls inside a group of exactly equal scores and
+    # the lowest block ids of that group are taken (the oracle's stable descending order).
+    grid = (4, 16, 32)
+    q, k, v = make_qkv(grid, 2, 128, seed=51, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    T = q.shape[1]
+    nb = T // block
+    k = k.view(1, nb, block, 2, 128)[:, [b % 4 for b in range(nb)]].reshape(1, T, 2, 128).contiguous()
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1)
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, return_route=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    np.testing.assert_array_equal(route["packed"].cpu().numpy(), ref["packed"])
+    # The selection restated from the scores: every block above the k-th score, then the
+    # lowest ids among the blocks equal to it.
+    topk = ref["topk"]
+    sc = ref["scores"].reshape(-1, ref["scores"].shape[-1])
+    got = route["indices"].cpu().numpy().reshape(sc.shape[0], topk)
+    kth = -np.sort(-sc, axis=-1)[:, topk - 1]
+    cut_in_ties = 0
+    for row in range(sc.shape[0]):
+        above = np.flatnonzero(sc[row] > kth[row])
+        tied = np.flatnonzero(sc[row] == kth[row])
+        cut_in_ties += len(above) + len(tied) > topk
+        expected = np.concatenate([above, tied[:topk - len(above)]])
+        np.testing.assert_array_equal(np.sort(got[row]), np.sort(expected))
+    assert cut_in_ties == sc.shape[0]  # every row's cut falls inside a group of equal scores
+    _check(as_np(out), ref["out"], torch.bfloat16)
+
+
+def test_all_zero_inputs_match_oracle(cuda_device):
+    # Every score, summary logit and attention logit ties: uniform routing by block id,
+    # uniform summary weights, and a zero output.
+    q = torch.zeros((1, 2048, 2, 128), dtype=torch.bfloat16)
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(q), to_oracle(q), block=64, topk_ratio=0.1)
+    d = q.to(cuda_device)
+    out, route = ops.spark_layer(d, d, d, block=64, topk_ratio=0.1, return_route=True)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    np.testing.assert_array_equal(route["packed"].cpu().numpy(), ref["packed"])
+    assert np.all(as_np(out) == 0.0)
+    np.testing.assert_array_equal(ref["out"], 0.0)
+    assert ops.read_device_status(cuda_device) == 0
