@@ -1,11 +1,11 @@
 """Generate the golden fixtures in this directory from the reference's own code.
 
-Run in a container that has the read-only reference checkout (default /root/reference, or
-$SPARK_H3_REFERENCE); the tests only read the committed fixtures and never import the
+Run in a container that has a read-only checkout of the reference, with its path in
+$SPARK_H3_REFERENCE; the tests only read the committed fixtures and never import the
 reference.  Inputs are regenerated deterministically by the tests from the recorded seeds
 (torch CPU generator) and checked against the recorded SHA-256 digests first.
 
-    python tests/golden/make_golden.py
+    SPARK_H3_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Fixtures:
   hierarchy.json  build_reblock_hierarchy / virtual_query_layout (reblock_hierarchy.py,
@@ -37,7 +37,9 @@ from pathlib import Path
 os.environ.setdefault("TRITON_INTERPRET", "1")
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REFERENCE = Path(os.environ.get("SPARK_H3_REFERENCE", "/root/reference"))
+if not os.environ.get("SPARK_H3_REFERENCE"):
+    raise SystemExit("set SPARK_H3_REFERENCE to the reference checkout")
+REFERENCE = Path(os.environ["SPARK_H3_REFERENCE"])
 sys.path[:0] = [str(REFERENCE), str(ROOT), str(ROOT / "spark-h3_b200")]
 
 import numpy as np  # noqa: E402
