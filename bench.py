@@ -275,7 +275,9 @@ def run_ours(args) -> None:
     # copies overlap the compute (ops.spark_layer_streamed).
     hq, hk, hv = (x.cpu().pin_memory() for x in (q, k, v))
     hout = torch.empty(out.shape, dtype=out.dtype, pin_memory=True)
-    e2e_chunks = next(c for c in (8, 4, 2, 1) if heads % c == 0)
+    e2e_chunks = args.e2e_chunks or next(c for c in (16, 8, 4, 2, 1) if heads % c == 0)
+    if heads % e2e_chunks:
+        raise SystemExit(f"--e2e-chunks {e2e_chunks} does not divide the {heads} heads of a rank")
 
     def e2e_step():
         ops.spark_layer_streamed(hq, hk, hv, hout, chunks=e2e_chunks, device=dev, block=BLOCK, topk_ratio=TOPK_RATIO)
@@ -660,6 +662,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-dense", action="store_true", help="skip the dense cuDNN SDPA comparison")
+    ap.add_argument("--e2e-chunks", type=int, default=0,
+                    help="head chunks of the end-to-end streamed layer (0: 16 or the largest that divides)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle baseline")
     ap.add_argument("--cpu-sample-blocks", type=int, default=96,
                     help="query blocks of the one-head CPU attention sample behind cpu_baseline")
