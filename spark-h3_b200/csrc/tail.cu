@@ -95,12 +95,11 @@ __global__ void __launch_bounds__(kTailThreads) tail_summaries8_kernel(
 // (NG = block / G: one group for "block", eight or sixteen of 8 rows for "block8x8"), which
 // share the block's exact set.  Summary entry e covers keys [e*E, e*E + E) of key block
 // (e*E) / block; it is skipped when that block is exact for the query block (route bit, sink
-// range or local radius).  With one group, each warp streams every fourth entry and scores it
-// with a warp-wide dot product.  With 8 or 16 groups, a warp takes 32 entries at a time, one
-// per lane: the lane scores its entry against every group mean (full 128-term dot products,
-// the means read from shared memory as broadcasts), one warp max per group rescales the
-// chunk, and the probabilities reach the lanes that own the value dimensions by shuffles.
-// That is about 2.5 times fewer instructions per entry than a warp-wide dot per group.
+// range or local radius).  A warp takes 32 entries at a time, one per lane: the lane scores
+// its entry against every group mean (full 128-term dot products, the means read from shared
+// memory as broadcasts), one warp max per group rescales the chunk, and the probabilities
+// reach the lanes that own the value dimensions by shuffles.  That is about 2.5 times fewer
+// instructions per entry than a warp-wide dot product per group and entry.
 template <typename T, int NG>
 __global__ void __launch_bounds__(kTailThreads) tail_merge_kernel(
     const T* __restrict__ q, const T* __restrict__ tk, const T* __restrict__ tv, const float* __restrict__ lmass,
@@ -137,102 +136,67 @@ __global__ void __launch_bounds__(kTailThreads) tail_merge_kernel(
     for (int i = 0; i < 4; ++i) acc[g][i] = 0.f;
   }
   const int64_t ebase = ((int64_t)b * H + h) * n_entries;
-  if constexpr (NG > 1) {
-    float dl[NG];  // this lane's share of each group's denominator
+  float dl[NG];  // this lane's share of each group's denominator
 #pragma unroll
-    for (int g = 0; g < NG; ++g) dl[g] = 0.f;
-    for (int c0 = warp * 32; c0 < n_entries; c0 += kWarps * 32) {
-      const int e = c0 + lane;
-      bool live = e < n_entries;
-      if (live) live = !block_is_exact(wrow, (e * entry_tokens) / block, qb, sink_first, sink_last, local_radius);
-      float sc[NG];
+  for (int g = 0; g < NG; ++g) dl[g] = 0.f;
+  for (int c0 = warp * 32; c0 < n_entries; c0 += kWarps * 32) {
+    const int e = c0 + lane;
+    bool live = e < n_entries;
+    if (live) live = !block_is_exact(wrow, (e * entry_tokens) / block, qb, sink_first, sink_last, local_radius);
+    float sc[NG];
 #pragma unroll
-      for (int g = 0; g < NG; ++g) sc[g] = 0.f;
-      if (live) {
-        const T* kp = tk + (ebase + e) * kDim;
+    for (int g = 0; g < NG; ++g) sc[g] = 0.f;
+    if (live) {
+      const T* kp = tk + (ebase + e) * kDim;
 #pragma unroll 2
-        for (int d = 0; d < kDim; d += 8) {
-          float kf[8];
-          load8(kp + d, kf);
-#pragma unroll
-          for (int g = 0; g < NG; ++g) {
-            const float4 qa = *reinterpret_cast<const float4*>(&qmean[g][d]);
-            const float4 qc = *reinterpret_cast<const float4*>(&qmean[g][d + 4]);
-            float t = fmaf(kf[0], qa.x, sc[g]);
-            t = fmaf(kf[1], qa.y, t);
-            t = fmaf(kf[2], qa.z, t);
-            t = fmaf(kf[3], qa.w, t);
-            t = fmaf(kf[4], qc.x, t);
-            t = fmaf(kf[5], qc.y, t);
-            t = fmaf(kf[6], qc.z, t);
-            sc[g] = fmaf(kf[7], qc.w, t);
-          }
-        }
-      }
-      const float lm2 = live ? lmass[ebase + e] * kLog2e : 0.f;
-#pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const float score = live ? sc[g] * scale_log2 + lm2 : -INFINITY;
-        const float m_new = fmaxf(m[g], warp_max(score));
-        const float factor = m[g] == -INFINITY ? 0.f : exp2f(m[g] - m_new);
-        const float pr = live ? exp2f(score - m_new) : 0.f;
-        dl[g] = fmaf(dl[g], factor, pr);
-#pragma unroll
-        for (int i = 0; i < 4; ++i) acc[g][i] *= factor;
-        m[g] = m_new;
-        sc[g] = pr;
-      }
-      // P.V over the chunk's live entries: lane j's probabilities against entry j's values.
-      for (unsigned bits = __ballot_sync(0xffffffffu, live); bits; bits &= bits - 1u) {
-        const int j = __ffs(bits) - 1;
-        const T* vp = tv + (ebase + c0 + j) * kDim + d0;
-        float vv[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) vv[i] = Elem<T>::to_f(vp[i]);
+      for (int d = 0; d < kDim; d += 8) {
+        float kf[8];
+        load8(kp + d, kf);
 #pragma unroll
         for (int g = 0; g < NG; ++g) {
-          const float pj = __shfl_sync(0xffffffffu, sc[g], j);
-#pragma unroll
-          for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(pj, vv[i], acc[g][i]);
+          const float4 qa = *reinterpret_cast<const float4*>(&qmean[g][d]);
+          const float4 qc = *reinterpret_cast<const float4*>(&qmean[g][d + 4]);
+          float t = fmaf(kf[0], qa.x, sc[g]);
+          t = fmaf(kf[1], qa.y, t);
+          t = fmaf(kf[2], qa.z, t);
+          t = fmaf(kf[3], qa.w, t);
+          t = fmaf(kf[4], qc.x, t);
+          t = fmaf(kf[5], qc.y, t);
+          t = fmaf(kf[6], qc.z, t);
+          sc[g] = fmaf(kf[7], qc.w, t);
         }
       }
     }
-#pragma unroll
-    for (int g = 0; g < NG; ++g) den[g] = warp_sum(dl[g]);
-  } else {
-  float qm[NG][4];
-#pragma unroll
-  for (int g = 0; g < NG; ++g)
-#pragma unroll
-    for (int i = 0; i < 4; ++i) qm[g][i] = qmean[g][d0 + i];
-  for (int e = warp; e < n_entries; e += kWarps) {
-    const int kb = (e * entry_tokens) / block;
-    if (block_is_exact(wrow, kb, qb, sink_first, sink_last, local_radius)) continue;
-    float kv[4], vv[4];
-    const T* kp = tk + (ebase + e) * kDim + d0;
-    const T* vp = tv + (ebase + e) * kDim + d0;
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      kv[i] = Elem<T>::to_f(kp[i]);
-      vv[i] = Elem<T>::to_f(vp[i]);
-    }
-    const float lm2 = lmass[ebase + e] * kLog2e;
+    const float lm2 = live ? lmass[ebase + e] * kLog2e : 0.f;
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
-      float part = 0.f;
-#pragma unroll
-      for (int i = 0; i < 4; ++i) part = fmaf(kv[i], qm[g][i], part);
-      const float score = warp_sum(part) * scale_log2 + lm2;
-      const float m_new = fmaxf(m[g], score);
+      const float score = live ? sc[g] * scale_log2 + lm2 : -INFINITY;
+      const float m_new = fmaxf(m[g], warp_max(score));
       const float factor = m[g] == -INFINITY ? 0.f : exp2f(m[g] - m_new);
-      const float pr = exp2f(score - m_new);
+      const float pr = live ? exp2f(score - m_new) : 0.f;
+      dl[g] = fmaf(dl[g], factor, pr);
 #pragma unroll
-      for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(acc[g][i], factor, pr * vv[i]);
-      den[g] = den[g] * factor + pr;
+      for (int i = 0; i < 4; ++i) acc[g][i] *= factor;
       m[g] = m_new;
+      sc[g] = pr;
+    }
+    // P.V over the chunk's live entries: lane j's probabilities against entry j's values.
+    for (unsigned bits = __ballot_sync(0xffffffffu, live); bits; bits &= bits - 1u) {
+      const int j = __ffs(bits) - 1;
+      const T* vp = tv + (ebase + c0 + j) * kDim + d0;
+      float vv[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) vv[i] = Elem<T>::to_f(vp[i]);
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const float pj = __shfl_sync(0xffffffffu, sc[g], j);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(pj, vv[i], acc[g][i]);
+      }
     }
   }
-  }
+#pragma unroll
+  for (int g = 0; g < NG; ++g) den[g] = warp_sum(dl[g]);
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
     if (lane == 0) {
