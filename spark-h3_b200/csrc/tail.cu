@@ -139,59 +139,89 @@ __global__ void __launch_bounds__(kTailThreads) tail_merge_kernel(
   float dl[NG];  // this lane's share of each group's denominator
 #pragma unroll
   for (int g = 0; g < NG; ++g) dl[g] = 0.f;
-  for (int c0 = warp * 32; c0 < n_entries; c0 += kWarps * 32) {
-    const int e = c0 + lane;
-    bool live = e < n_entries;
-    if (live) live = !block_is_exact(wrow, (e * entry_tokens) / block, qb, sink_first, sink_last, local_radius);
-    float sc[NG];
+  // TT entries per lane: each group mean read from shared memory serves TT key rows.
+  constexpr int TT = NG >= 16 ? 1 : (NG >= 8 ? 2 : 4);
+  for (int c0 = warp * 32 * TT; c0 < n_entries; c0 += kWarps * 32 * TT) {
+    bool live[TT];
+    float sc[TT][NG];
 #pragma unroll
-    for (int g = 0; g < NG; ++g) sc[g] = 0.f;
-    if (live) {
-      const T* kp = tk + (ebase + e) * kDim;
+    for (int t = 0; t < TT; ++t) {
+      const int e = c0 + 32 * t + lane;
+      live[t] = e < n_entries;
+      if (live[t])
+        live[t] = !block_is_exact(wrow, (e * entry_tokens) / block, qb, sink_first, sink_last, local_radius);
+#pragma unroll
+      for (int g = 0; g < NG; ++g) sc[t][g] = 0.f;
+    }
 #pragma unroll 2
-      for (int d = 0; d < kDim; d += 8) {
-        float kf[8];
-        load8(kp + d, kf);
+    for (int d = 0; d < kDim; d += 8) {
+      float kf[TT][8];
 #pragma unroll
-        for (int g = 0; g < NG; ++g) {
-          const float4 qa = *reinterpret_cast<const float4*>(&qmean[g][d]);
-          const float4 qc = *reinterpret_cast<const float4*>(&qmean[g][d + 4]);
-          float t = fmaf(kf[0], qa.x, sc[g]);
-          t = fmaf(kf[1], qa.y, t);
-          t = fmaf(kf[2], qa.z, t);
-          t = fmaf(kf[3], qa.w, t);
-          t = fmaf(kf[4], qc.x, t);
-          t = fmaf(kf[5], qc.y, t);
-          t = fmaf(kf[6], qc.z, t);
-          sc[g] = fmaf(kf[7], qc.w, t);
+      for (int t = 0; t < TT; ++t) {
+        if (live[t]) {
+          load8(tk + (ebase + c0 + 32 * t + lane) * kDim + d, kf[t]);
+        } else {
+#pragma unroll
+          for (int i = 0; i < 8; ++i) kf[t][i] = 0.f;
+        }
+      }
+#pragma unroll
+      for (int g = 0; g < NG; ++g) {
+        const float4 qa = *reinterpret_cast<const float4*>(&qmean[g][d]);
+        const float4 qc = *reinterpret_cast<const float4*>(&qmean[g][d + 4]);
+#pragma unroll
+        for (int t = 0; t < TT; ++t) {
+          float x = fmaf(kf[t][0], qa.x, sc[t][g]);
+          x = fmaf(kf[t][1], qa.y, x);
+          x = fmaf(kf[t][2], qa.z, x);
+          x = fmaf(kf[t][3], qa.w, x);
+          x = fmaf(kf[t][4], qc.x, x);
+          x = fmaf(kf[t][5], qc.y, x);
+          x = fmaf(kf[t][6], qc.z, x);
+          sc[t][g] = fmaf(kf[t][7], qc.w, x);
         }
       }
     }
-    const float lm2 = live ? lmass[ebase + e] * kLog2e : 0.f;
+    float lm2[TT];
+#pragma unroll
+    for (int t = 0; t < TT; ++t) lm2[t] = live[t] ? lmass[ebase + c0 + 32 * t + lane] * kLog2e : 0.f;
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
-      const float score = live ? sc[g] * scale_log2 + lm2 : -INFINITY;
-      const float m_new = fmaxf(m[g], warp_max(score));
+      float score[TT], cm = -INFINITY;
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        score[t] = live[t] ? sc[t][g] * scale_log2 + lm2[t] : -INFINITY;
+        cm = fmaxf(cm, score[t]);
+      }
+      const float m_new = fmaxf(m[g], warp_max(cm));
       const float factor = m[g] == -INFINITY ? 0.f : exp2f(m[g] - m_new);
-      const float pr = live ? exp2f(score - m_new) : 0.f;
-      dl[g] = fmaf(dl[g], factor, pr);
+      float pr_sum = 0.f;
+#pragma unroll
+      for (int t = 0; t < TT; ++t) {
+        const float pr = live[t] ? exp2f(score[t] - m_new) : 0.f;
+        pr_sum += pr;
+        sc[t][g] = pr;
+      }
+      dl[g] = fmaf(dl[g], factor, pr_sum);
 #pragma unroll
       for (int i = 0; i < 4; ++i) acc[g][i] *= factor;
       m[g] = m_new;
-      sc[g] = pr;
     }
     // P.V over the chunk's live entries: lane j's probabilities against entry j's values.
-    for (unsigned bits = __ballot_sync(0xffffffffu, live); bits; bits &= bits - 1u) {
-      const int j = __ffs(bits) - 1;
-      const T* vp = tv + (ebase + c0 + j) * kDim + d0;
-      float vv[4];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) vv[i] = Elem<T>::to_f(vp[i]);
+    for (int t = 0; t < TT; ++t) {
+      for (unsigned bits = __ballot_sync(0xffffffffu, live[t]); bits; bits &= bits - 1u) {
+        const int j = __ffs(bits) - 1;
+        const T* vp = tv + (ebase + c0 + 32 * t + j) * kDim + d0;
+        float vv[4];
 #pragma unroll
-      for (int g = 0; g < NG; ++g) {
-        const float pj = __shfl_sync(0xffffffffu, sc[g], j);
+        for (int i = 0; i < 4; ++i) vv[i] = Elem<T>::to_f(vp[i]);
 #pragma unroll
-        for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(pj, vv[i], acc[g][i]);
+        for (int g = 0; g < NG; ++g) {
+          const float pj = __shfl_sync(0xffffffffu, sc[t][g], j);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) acc[g][i] = fmaf(pj, vv[i], acc[g][i]);
+        }
       }
     }
   }
