@@ -45,8 +45,8 @@ PROFILE_ONLY = False
 HEAD_DIM = 128
 BLOCK = 128
 TOPK_RATIO = 0.1
-# DRAM bytes per launch of the attention kernel at this workload, from the one-pass ncu
-# capture summarised in profiles/config1_layer_launch_list.md (4.74 GB read + 1.02 GB write).
+# DRAM bytes per launch of the attention kernel at this workload (dram__bytes_read.sum +
+# dram__bytes_write.sum of one ncu capture: 4.74 GB read + 1.02 GB write).
 ATTENTION_TRAFFIC_BYTES = 5.76e9
 
 

@@ -134,6 +134,23 @@ int sb_route_topk(const float* qc, const void* kc, int kc_dtype, int B, int QB, 
                   void* stream);
 
 /*
+ * Top-K with one budget per head.  Replaces head_budget.py:7-19 (route_with_head_budgets,
+ * reached from spark_integration.py:1344-1351 when the controller carries
+ * head_topk_budget): row (b, i, h) keeps the head_topk[h] largest of its candidate scores
+ * in stable descending order (ties to the lower block index), the budget clamped to
+ * [0, candidates].  head_topk: device int32 [H].  Scores, packed_route and the workspace are
+ * as for sb_route_topk.  indices (may be NULL) is [B, QB, H, index_width] with
+ * 1 <= index_width <= candidates: a row's ascending selections, -1 past its budget; a budget
+ * above index_width fills the row and the remaining selections appear only in packed_route.
+ * The caller makes the blocks past the candidates exact (the reference routes every block
+ * >= candidates when there are sink tokens or a partial video block).
+ */
+int sb_route_topk_head_budgets(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
+                               int H, int D, int candidates, const int32_t* head_topk,
+                               int index_width, float scale_log2, void* workspace,
+                               int32_t* packed_route, int32_t* indices, void* stream);
+
+/*
  * Allocation-free variant of sb_route_topk; no counterpart in the reference.
  * For callers that cannot pass a device workspace, for instance a host that binds only this
  * library through a thin FFI and owns no device allocator, or a serving loop that cannot

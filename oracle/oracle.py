@@ -18,6 +18,7 @@ storage roundings as the reference:
 from __future__ import annotations
 
 import ctypes
+import hashlib
 import math
 import os
 import subprocess
@@ -35,14 +36,15 @@ def build() -> Path:
     """Compile the C restatement (gcc, no contraction of multiply-adds)."""
     LIB_PATH.parent.mkdir(parents=True, exist_ok=True)
     sources = [HERE / "spark_oracle.c", HERE / "reblock_oracle.c"]
-    if LIB_PATH.exists() and all(LIB_PATH.stat().st_mtime >= src.stat().st_mtime for src in sources):
+    flags = ["-O2", "-ffp-contract=off", "-fno-fast-math", "-fopenmp", "-shared", "-fPIC"]
+    stamp = LIB_PATH.with_suffix(".stamp")
+    digest = hashlib.sha256(" ".join(flags).encode() + b"".join(src.read_bytes() for src in sources)).hexdigest()
+    if LIB_PATH.exists() and stamp.exists() and stamp.read_text() == digest:
         return LIB_PATH
     tmp = LIB_PATH.with_suffix(f".{os.getpid()}.tmp")
-    subprocess.check_call([
-        "gcc", "-O2", "-ffp-contract=off", "-fno-fast-math", "-shared", "-fPIC",
-        "-o", str(tmp), *map(str, sources), "-lm",
-    ])
+    subprocess.check_call(["gcc", *flags, "-o", str(tmp), *map(str, sources), "-lm"])
     os.replace(tmp, LIB_PATH)
+    stamp.write_text(digest)
     return LIB_PATH
 
 
@@ -62,7 +64,9 @@ def _lib():
         lib.orc_anchor.argtypes = [f32p, ci, ci, ci, ci, ci, ci, f32p]
         lib.orc_scores.argtypes = [f32p, f32p, ci, ci, ci, ci, ci, ci, cf, f32p]
         lib.orc_topk.argtypes = [f32p, ci64, ci, ci, ci, i32p, i32p]
-        for fn in (lib.orc_block_means, lib.orc_round_bf16, lib.orc_anchor, lib.orc_scores, lib.orc_topk):
+        lib.orc_topk_head_budgets.argtypes = [f32p, ci64, ci, ci, i32p, ci, ci, i32p, i32p]
+        for fn in (lib.orc_block_means, lib.orc_round_bf16, lib.orc_anchor, lib.orc_scores, lib.orc_topk,
+                   lib.orc_topk_head_budgets):
             fn.restype = None
         u16p = np.ctypeslib.ndpointer(np.uint16, flags="C_CONTIGUOUS")
         lib.orc_rb_norms.argtypes = [u16p, ci64, ci, f32p]
@@ -165,6 +169,22 @@ def topk(score: np.ndarray, k: int, total_blocks: int) -> tuple[np.ndarray, np.n
     return idx.reshape(B, QB, H, k), packed.reshape(B, QB, H, words)
 
 
+def topk_head_budgets(score: np.ndarray, budgets, total_blocks: int, width: int | None = None):
+    """Per-head budgets (head_budget.py:7-19): row (b, q, h) keeps the budgets[h] largest
+    scores, ties to the lower index.  Returns indices [B, QB, H, width] (ascending, -1 past
+    the row's budget; width defaults to the largest budget) and packed words."""
+    B, QB, H, C = score.shape
+    budgets = np.ascontiguousarray(np.asarray(budgets, dtype=np.int32).reshape(H))
+    if width is None:
+        width = max(1, int(np.clip(budgets, 0, C).max()))
+    words = -(-total_blocks // 32)
+    rows = B * QB * H
+    idx = np.empty((rows, width), dtype=np.int32)
+    packed = np.empty((rows, words), dtype=np.int32)
+    _lib().orc_topk_head_budgets(np.ascontiguousarray(score), rows, H, C, budgets, width, words, idx, packed)
+    return idx.reshape(B, QB, H, width), packed.reshape(B, QB, H, words)
+
+
 def target_topk(ratio: float, candidates: int) -> int:
     """max(1, round(ratio * candidates)) capped at candidates (sol_topk_cutoff.py:342)."""
     return min(max(1, round(ratio * candidates)), candidates)
@@ -181,35 +201,40 @@ def summaries(a: np.ndarray, k: Tensor, v: Tensor, block: int, *, weighted_kv: b
     unrounded mean."""
     B, T, H, D = k.shape
     nb = -(-T // block)
-    kf, vf = k.float().astype(np.float64), v.float().astype(np.float64)
+    kf, vf = k.float(), v.float()
+    a64 = a.astype(np.float64)
     scale = D ** -0.5
     ak = np.empty((B, H, nb, D), dtype=np.float32)
     av = np.empty_like(ak)
     lm = np.empty((B, H, nb), dtype=np.float32)
-    for j in range(nb):
-        rows = slice(j * block, min(T, (j + 1) * block))
-        kk, vv = kf[:, rows], vf[:, rows]                    # [B, r, H, D]
-        count = kk.shape[1]
+    full = T // block
+    # Runs of up to 64 whole blocks are evaluated together ([B, J, r, H, D] slabs); a partial
+    # final block is its own run.  Every block's arithmetic is the per-block formula.
+    runs = [(j, min(full, j + 64)) for j in range(0, full, 64)] + ([(full, nb)] if nb > full else [])
+    for j0, j1 in runs:
+        r = min(block, T - j0 * block)
+        kk = kf[:, j0 * block:min(T, j1 * block)].astype(np.float64).reshape(B, j1 - j0, r, H, D)
+        vv = vf[:, j0 * block:min(T, j1 * block)].astype(np.float64).reshape(B, j1 - j0, r, H, D)
         if weighted_kv or mass_bias:
-            logits = np.einsum("bhd,brhd->bhr", a.astype(np.float64), kk) * scale * LOG2E
+            logits = np.einsum("bhd,bjrhd->bhjr", a64, kk) * scale * LOG2E
             mx = logits.max(-1, keepdims=True)
             p = np.exp2(logits - mx)
-            den = p.sum(-1)
+            den = p.sum(-1)                                   # [B, H, J]
         if weighted_kv:
             w = (p if summary_math == "comfy_fp32" else store(p, k.dtype)).astype(np.float64)
-            key = np.einsum("bhr,brhd->bhd", w, kk) / den[..., None]
-            val = np.einsum("bhr,brhd->bhd", w, vv) / den[..., None]
+            key = np.einsum("bhjr,bjrhd->bhjd", w, kk) / den[..., None]
+            val = np.einsum("bhjr,bjrhd->bhjd", w, vv) / den[..., None]
         else:
-            key = kk.mean(1)
-            val = vv.mean(1)
-        ak[:, :, j] = store(key, k.dtype)
-        av[:, :, j] = store(val, v.dtype)
+            key = kk.mean(2).transpose(0, 2, 1, 3)
+            val = vv.mean(2).transpose(0, 2, 1, 3)
+        ak[:, :, j0:j1] = store(key, k.dtype)
+        av[:, :, j0:j1] = store(val, v.dtype)
         if mass_bias:
-            shift_key = key if logmass_key == "pre_round" else ak[:, :, j].astype(np.float64)
-            shift = np.einsum("bhd,bhd->bh", a.astype(np.float64), shift_key) * scale
-            lm[:, :, j] = (mx[..., 0] + np.log2(den)) * LN2 - shift
+            shift_key = key if logmass_key == "pre_round" else ak[:, :, j0:j1].astype(np.float64)
+            shift = np.einsum("bhd,bhjd->bhj", a64, shift_key) * scale
+            lm[:, :, j0:j1] = (mx[..., 0] + np.log2(den)) * LN2 - shift
         else:
-            lm[:, :, j] = math.log(count)
+            lm[:, :, j0:j1] = math.log(r)
     return ak, av, lm
 
 
@@ -304,19 +329,19 @@ def exact_blocks(packed_row: np.ndarray, qb: int, nb: int, sink_first: int, sink
 
 def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.ndarray, ak: np.ndarray,
                      av: np.ndarray, lm: np.ndarray, query_tokens: int, sink_first: int, sink_last: int,
-                     local_radius: int = -1, rows: slice | None = None,
+                     local_radius: int = -1, rows: slice | list[slice] | None = None,
                      heads: list[int] | None = None) -> tuple[np.ndarray, np.ndarray]:
     """Output [B, T, H, D] float32 (unrounded) and LSE [B, T, H] for the selected rows/heads.
 
-    Rows outside ``rows`` / heads outside ``heads`` are left as NaN.
+    ``rows`` is one slice or a list of slices.  Rows outside them / heads outside ``heads``
+    are left as NaN.
     """
     B, T, H, D = q.shape
     nb = -(-T // block)
     qf, kf, vf = (x.float() for x in (q, k, v))
     out = np.full((B, T, H, D), np.nan, dtype=np.float32)
     lse = np.full((B, T, H), np.nan, dtype=np.float32)
-    rows = rows or slice(0, T)
-    r0, r1 = rows.start or 0, min(T, rows.stop if rows.stop is not None else T)
+    spans = rows if isinstance(rows, list) else [rows or slice(0, T)]
     heads = list(range(H)) if heads is None else heads
     scale = D ** -0.5
     for b in range(B):
@@ -327,34 +352,36 @@ def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.nda
             akh = ak[b, h].astype(np.float64) if ak is not None else np.zeros((nb, D))
             avh = av[b, h].astype(np.float64) if av is not None else np.zeros((nb, D))
             lmh = lm[b, h].astype(np.float64) if lm is not None else np.zeros(nb)
-            start = r0
-            while start < r1:
-                if start < query_tokens:
-                    qb = start // block
-                    stop = min(r1, (qb + 1) * block, query_tokens)
-                    exact = exact_blocks(packed[b, qb, h], qb, nb, sink_first, sink_last, local_radius)
-                else:
-                    qb = -1
-                    stop = r1
-                    exact = np.ones(nb, dtype=bool)
-                tok = np.repeat(exact, block)[:T]
-                summ = ~exact if ak is not None else np.zeros(nb, dtype=bool)
-                keys = np.concatenate([kh[tok], akh[summ]])
-                vals = np.concatenate([vh[tok], avh[summ]])
-                qq = qf[b, start:stop, h].astype(np.float64)
-                logits = qq @ keys.T * scale
-                logits[:, int(tok.sum()):] += lmh[summ]
-                if logits.shape[1] == 0:  # nothing visible
-                    out[b, start:stop, h] = 0.0
-                    lse[b, start:stop, h] = -np.inf
+            for span in spans:
+                r0, r1 = span.start or 0, min(T, span.stop if span.stop is not None else T)
+                start = r0
+                while start < r1:
+                    if start < query_tokens:
+                        qb = start // block
+                        stop = min(r1, (qb + 1) * block, query_tokens)
+                        exact = exact_blocks(packed[b, qb, h], qb, nb, sink_first, sink_last, local_radius)
+                    else:
+                        qb = -1
+                        stop = r1
+                        exact = np.ones(nb, dtype=bool)
+                    tok = np.repeat(exact, block)[:T]
+                    summ = ~exact if ak is not None else np.zeros(nb, dtype=bool)
+                    keys = np.concatenate([kh[tok], akh[summ]])
+                    vals = np.concatenate([vh[tok], avh[summ]])
+                    qq = qf[b, start:stop, h].astype(np.float64)
+                    logits = qq @ keys.T * scale
+                    logits[:, int(tok.sum()):] += lmh[summ]
+                    if logits.shape[1] == 0:  # nothing visible
+                        out[b, start:stop, h] = 0.0
+                        lse[b, start:stop, h] = -np.inf
+                        start = stop
+                        continue
+                    mx = logits.max(-1, keepdims=True)
+                    p = np.exp(logits - mx)
+                    den = p.sum(-1, keepdims=True)
+                    out[b, start:stop, h] = (p @ vals / den).astype(np.float32)
+                    lse[b, start:stop, h] = (mx[:, 0] + np.log(den[:, 0])).astype(np.float32)
                     start = stop
-                    continue
-                mx = logits.max(-1, keepdims=True)
-                p = np.exp(logits - mx)
-                den = p.sum(-1, keepdims=True)
-                out[b, start:stop, h] = (p @ vals / den).astype(np.float32)
-                lse[b, start:stop, h] = (mx[:, 0] + np.log(den[:, 0])).astype(np.float32)
-                start = stop
     return out, lse
 
 
@@ -378,8 +405,12 @@ def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: floa
                 anchor_dtype: str | None = None, local_radius: int = -1, weighted_kv: bool = True,
                 mass_bias: bool = True, attention: bool = True, rows: slice | None = None,
                 heads: list[int] | None = None, tail_mode: str = "dense", tail_granularity: str = "query",
-                summary_math: str = "tensorcore", logmass_key: str = "stored") -> dict:
+                summary_math: str = "tensorcore", logmass_key: str = "stored", head_budgets=None) -> dict:
     """Route, summaries and (optionally) attention of one Spark layer, as the CUDA path does.
+
+    head_budgets (one int per head): the per-head Top-K of head_budget.py:7-19 replaces the
+    fixed budget, and every key block past the candidates is exact when there is a context
+    suffix or a partial video block (head_budget.py:16-18).
 
     tail_mode "pad" (spark_integration.py:72-91, 935-938, 1173-1187, 1238-1260): the query
     prefix extends over the partial final video block, whose missing rows are filled with
@@ -404,7 +435,12 @@ def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: floa
     a = anchor(qc, block, candidates, anchor_dtype or q.dtype)
     sc = scores(qc, kc, query_blocks, candidates)
     kk = target_topk(topk_ratio, candidates)
-    idx, packed = topk(sc, kk, nb)
+    if head_budgets is None:
+        idx, packed = topk(sc, kk, nb)
+    else:
+        idx, packed = topk_head_budgets(sc, head_budgets, nb, width=kk)
+        if T > video or video % block:
+            sink_first, sink_last = candidates, nb
     result = dict(qc=qc, kc=kc, anchor=a, scores=sc, indices=idx, packed=packed, topk=kk,
                   query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last)
     ak, av, lm = summaries(a, k, v, block, weighted_kv=weighted_kv, mass_bias=mass_bias,

@@ -43,24 +43,31 @@ static float load_elem(const void* x, int dtype, int64_t i) {
   return dtype == 1 ? bf16_to_f(((const uint16_t*)x)[i]) : ((const float*)x)[i];
 }
 
-/* Block means of x [B, T, H, D] -> out [B, NB, H, D] fp32. */
+/* Block means of x [B, T, H, D] -> out [B, NB, H, D] fp32.  Blocks are independent, so they
+ * are spread over OpenMP threads; each element's sum keeps the canonical order. */
 void orc_block_means(const void* x, int dtype, int B, int T, int H, int D, int block, float* out) {
   const int NB = (T + block - 1) / block;
   const int64_t HD = (int64_t)H * D;
+#pragma omp parallel for collapse(2) schedule(dynamic, 4)
   for (int b = 0; b < B; ++b)
     for (int j = 0; j < NB; ++j) {
       const int row0 = j * block;
       const int rows = T - row0 < block ? T - row0 : block;
-      for (int64_t c = 0; c < HD; ++c) {
-        float total = 0.f;
-        for (int s = 0; s < rows; s += 64) {
-          const int sub = rows - s < 64 ? rows - s : 64;
-          float acc = 0.f;
-          for (int r = 0; r < sub; ++r) acc = acc + load_elem(x, dtype, ((int64_t)b * T + row0 + s + r) * HD + c);
-          total = total + acc;
+      float* total = out + ((int64_t)b * NB + j) * HD;
+      float* acc = (float*)malloc(sizeof(float) * (size_t)HD);
+      for (int64_t c = 0; c < HD; ++c) total[c] = 0.f;
+      for (int s = 0; s < rows; s += 64) {
+        const int sub = rows - s < 64 ? rows - s : 64;
+        for (int64_t c = 0; c < HD; ++c) acc[c] = 0.f;
+        /* rows outer, columns inner: every column's chain still adds its rows in order */
+        for (int r = 0; r < sub; ++r) {
+          const int64_t base = ((int64_t)b * T + row0 + s + r) * HD;
+          for (int64_t c = 0; c < HD; ++c) acc[c] = acc[c] + load_elem(x, dtype, base + c);
         }
-        out[((int64_t)b * NB + j) * HD + c] = total / (float)rows;
+        for (int64_t c = 0; c < HD; ++c) total[c] = total[c] + acc[c];
       }
+      for (int64_t c = 0; c < HD; ++c) total[c] = total[c] / (float)rows;
+      free(acc);
     }
 }
 
@@ -80,19 +87,27 @@ void orc_anchor(const float* qc, int B, int NB, int H, int D, int block, int pre
     }
 }
 
-/* scores [B, QB, H, C] from qc [B, NB, H, D] and kc (already at key precision, fp32). */
+/* scores [B, QB, H, C] from qc [B, NB, H, D] and kc (already at key precision, fp32).
+ * Eight candidates at a time keep eight independent fma chains in flight; each chain is
+ * still the sequential one over d. */
 void orc_scores(const float* qc, const float* kc, int B, int QB, int NB, int H, int D, int C, float scale_log2,
                 float* scores) {
+#pragma omp parallel for collapse(3) schedule(static)
   for (int b = 0; b < B; ++b)
     for (int i = 0; i < QB; ++i)
       for (int h = 0; h < H; ++h) {
         const float* q = qc + (((int64_t)b * NB + i) * H + h) * D;
         float* row = scores + (((int64_t)b * QB + i) * H + h) * C;
-        for (int j = 0; j < C; ++j) {
-          const float* k = kc + (((int64_t)b * NB + j) * H + h) * D;
-          float s = 0.f;
-          for (int d = 0; d < D; ++d) s = fmaf(q[d], k[d], s);
-          row[j] = s * scale_log2;
+        for (int j0 = 0; j0 < C; j0 += 8) {
+          const int n = C - j0 < 8 ? C - j0 : 8;
+          const float* k[8];
+          float s[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+          for (int u = 0; u < 8; ++u) k[u] = kc + (((int64_t)b * NB + j0 + (u < n ? u : 0)) * H + h) * D;
+          for (int d = 0; d < D; ++d) {
+            const float qd = q[d];
+            for (int u = 0; u < 8; ++u) s[u] = fmaf(qd, k[u][d], s[u]);
+          }
+          for (int u = 0; u < n; ++u) row[j0 + u] = s[u] * scale_log2;
         }
       }
 }
@@ -115,26 +130,58 @@ static int int_cmp(const void* a, const void* b) {
   return x < y ? -1 : (x > y ? 1 : 0);
 }
 
+/* One row: keep the k largest of C scores (ties -> lower index), 0 <= k <= C.  Writes the k
+ * ascending indices into idx[0 .. k) and the packed words. */
+static void topk_row(const float* score, int C, int k, int words, Entry* e, int* sel, int32_t* idx, int32_t* w) {
+  for (int j = 0; j < C; ++j) {
+    e[j].v = score[j];
+    e[j].i = j;
+  }
+  qsort(e, (size_t)C, sizeof(Entry), entry_cmp);
+  for (int t = 0; t < k; ++t) sel[t] = e[t].i;
+  qsort(sel, (size_t)k, sizeof(int), int_cmp);
+  memset(w, 0, sizeof(int32_t) * (size_t)words);
+  for (int t = 0; t < k; ++t) {
+    idx[t] = sel[t];
+    w[sel[t] >> 5] = (int32_t)((uint32_t)w[sel[t] >> 5] | (1u << (sel[t] & 31)));
+  }
+}
+
 /* Per row: keep the topk largest scores (ties -> lower index).  Writes ascending indices
  * [rows, topk] and packed words [rows, words]. */
 void orc_topk(const float* scores, int64_t rows, int C, int topk, int words, int32_t* indices, int32_t* packed) {
-  Entry* e = (Entry*)malloc(sizeof(Entry) * (size_t)C);
-  int* sel = (int*)malloc(sizeof(int) * (size_t)topk);
-  for (int64_t r = 0; r < rows; ++r) {
-    for (int j = 0; j < C; ++j) {
-      e[j].v = scores[r * C + j];
-      e[j].i = j;
-    }
-    qsort(e, (size_t)C, sizeof(Entry), entry_cmp);
-    for (int t = 0; t < topk; ++t) sel[t] = e[t].i;
-    qsort(sel, (size_t)topk, sizeof(int), int_cmp);
-    int32_t* w = packed + r * words;
-    memset(w, 0, sizeof(int32_t) * (size_t)words);
-    for (int t = 0; t < topk; ++t) {
-      indices[r * topk + t] = sel[t];
-      w[sel[t] >> 5] = (int32_t)((uint32_t)w[sel[t] >> 5] | (1u << (sel[t] & 31)));
-    }
+#pragma omp parallel
+  {
+    Entry* e = (Entry*)malloc(sizeof(Entry) * (size_t)C);
+    int* sel = (int*)malloc(sizeof(int) * (size_t)C);
+#pragma omp for schedule(dynamic, 64)
+    for (int64_t r = 0; r < rows; ++r)
+      topk_row(scores + r * C, C, topk, words, e, sel, indices + r * topk, packed + r * words);
+    free(e);
+    free(sel);
   }
-  free(e);
-  free(sel);
+}
+
+/* Per-head budgets (head_budget.py:7-19, route_with_head_budgets): row r of the
+ * [B, QB, H] rows keeps the budget[r % H] largest scores in stable descending order, the
+ * budget clamped to [0, C].  indices rows are `width` wide; entries past a row's budget
+ * (or past width) are -1. */
+void orc_topk_head_budgets(const float* scores, int64_t rows, int H, int C, const int32_t* budget, int width,
+                           int words, int32_t* indices, int32_t* packed) {
+#pragma omp parallel
+  {
+    Entry* e = (Entry*)malloc(sizeof(Entry) * (size_t)C);
+    int* sel = (int*)malloc(sizeof(int) * (size_t)C);
+    int32_t* idx = (int32_t*)malloc(sizeof(int32_t) * (size_t)C);
+#pragma omp for schedule(dynamic, 64)
+    for (int64_t r = 0; r < rows; ++r) {
+      int k = budget[r % H];
+      k = k < 0 ? 0 : (k > C ? C : k);
+      topk_row(scores + r * C, C, k, words, e, sel, idx, packed + r * words);
+      for (int t = 0; t < width; ++t) indices[r * width + t] = t < k ? idx[t] : -1;
+    }
+    free(e);
+    free(sel);
+    free(idx);
+  }
 }

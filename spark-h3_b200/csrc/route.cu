@@ -4,6 +4,7 @@
 // score = fp32(sequential fused multiply-add over d of qc[d] * kc[d]) * scale_log2.
 // The CPU oracle computes the identical chain, so selections agree bit for bit.
 #include <algorithm>
+#include <cstdio>
 #include <mutex>
 
 #include "common.cuh"
@@ -72,23 +73,37 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 
 // One warp per (b, query block, head) row, several rows per CTA, no CTA barriers: the row's
 // keys sit in the warp's slice of shared memory; a 4 x 8-bit radix select with a per-warp
-// histogram finds the key of the topk-th largest score; then 32 candidates at a time, the
+// histogram finds the key of the k-th largest score; then 32 candidates at a time, the
 // keys above it and the lowest-index keys equal to it are taken (each ballot is one packed
 // route word).  Ties at the cut go to the lowest candidate index.
+//
+// k is `topk` for every row, or, with per-head budgets (head_budget.py:7-19), head_topk[h]
+// for the row's head h = row % H, clamped to [0, C].  Index rows are `index_width` wide;
+// positions past the row's k are written as -1.
 constexpr int kTopkWarpMaxRows = 8;
 
 __global__ void __launch_bounds__(32 * kTopkWarpMaxRows)
 topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int topk, int words,
+                      const int32_t* __restrict__ head_topk, int H, int index_width,
                       int32_t* __restrict__ packed, int32_t* __restrict__ indices) {
   extern __shared__ uint32_t warp_smem[];  // per warp: hist[256] then keys[C]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
+  int k = topk;
+  if (head_topk != nullptr) k = min(max(__ldg(head_topk + row % H), 0), C);
+  int32_t* prow = packed + row * words;
+  if (k == 0) {  // nothing routed: every candidate is summarised
+    for (int w = lane; w < words; w += 32) prow[w] = 0;
+    if (indices != nullptr)
+      for (int i = lane; i < index_width; i += 32) indices[row * index_width + i] = -1;
+    return;
+  }
   uint32_t* hist = warp_smem + (size_t)warp * (256 + C);
   uint32_t* keys = hist + 256;
   const float* src = scores + row * C;
   for (int i = lane; i < C; i += 32) keys[i] = float_key(src[i]);
-  uint32_t prefix = 0, need = (uint32_t)topk;
+  uint32_t prefix = 0, need = (uint32_t)k;
 #pragma unroll 1
   for (int pass = 0; pass < 4; ++pass) {
     const int shift = 24 - 8 * pass;
@@ -142,7 +157,6 @@ topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int
   const uint32_t thresh = prefix, take_equal = need;
   uint32_t eq_seen = 0;
   int out_pos = 0;
-  int32_t* prow = packed + row * words;
   for (int w = 0; w < words; ++w) {
     const int i = 32 * w + lane;
     const uint32_t kk = i < C ? keys[i] : 0u;
@@ -153,46 +167,100 @@ topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int
     const unsigned sel_mask = __ballot_sync(0xffffffffu, sel);
     if (sel && indices != nullptr) {
       const int pos = out_pos + __popc(sel_mask & ((1u << lane) - 1u));
-      if (pos < topk) indices[row * topk + pos] = i;
+      if (pos < index_width) indices[row * index_width + pos] = i;
     }
     if (lane == 0) prow[w] = (int32_t)sel_mask;
     eq_seen += __popc(eq_mask);
     out_pos += __popc(sel_mask);
   }
+  if (indices != nullptr)
+    for (int i = k + lane; i < index_width; i += 32) indices[row * index_width + i] = -1;
 }
 
 }  // namespace sb
 
 using namespace sb;
 
+// cuda_error with the failing entry point's name in front of the step.
+static int cuda_error_at(cudaError_t err, const char* who, const char* what) {
+  char buf[160];
+  snprintf(buf, sizeof(buf), "%s: %s", who, what);
+  return cuda_error(err, buf);
+}
+
 template <typename TK, int D>
-static int launch_scores(dim3 grid, const float* qc, const void* kc, int QB, int NB, int H, int C,
-                         float scale_log2, float* scores, cudaStream_t s) {
-  const size_t smem = (size_t)(kScoreTile * (D + 1) + D * (kScoreTile + 1)) * sizeof(float);
-  auto kern = block_scores_kernel<TK, D>;
-  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (err != cudaSuccess) return cuda_error(err, "sb_route_topk: set score smem");
-  kern<<<grid, kScoreThreads, smem, s>>>(qc, (const TK*)kc, QB, NB, H, C, scale_log2, scores);
-  SB_CHECK_LAUNCH("sb_route_topk: score launch");
+static size_t score_smem_bytes() {
+  return (size_t)(kScoreTile * (D + 1) + D * (kScoreTile + 1)) * sizeof(float);
+}
+
+// Raises the dynamic shared-memory limit of the score kernel for (TK, D); `who` names the
+// entry point in the error text.
+template <typename TK, int D>
+static int prepare_scores(const char* who) {
+  cudaError_t err = cudaFuncSetAttribute(block_scores_kernel<TK, D>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)score_smem_bytes<TK, D>());
+  if (err != cudaSuccess) return cuda_error_at(err, who, "set score smem");
   return SB_OK;
+}
+
+template <typename TK, int D>
+static int launch_scores(const char* who, dim3 grid, const float* qc, const void* kc, int QB, int NB, int H, int C,
+                         float scale_log2, float* scores, cudaStream_t s) {
+  block_scores_kernel<TK, D><<<grid, kScoreThreads, score_smem_bytes<TK, D>(), s>>>(qc, (const TK*)kc, QB, NB, H, C,
+                                                                                 scale_log2, scores);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_error_at(err, who, "score launch");
+  return SB_OK;
+}
+
+// Score-kernel dispatch on the key-centroid dtype and the head dim (prepare_scores first).
+static int scores_for(const char* who, int kc_dtype, int D, dim3 grid, const float* qc, const void* kc, int QB, int NB,
+                      int H, int C, float scale_log2, float* scores, cudaStream_t s) {
+  if (kc_dtype == SB_BF16)
+    return D == 128 ? launch_scores<__nv_bfloat16, 128>(who, grid, qc, kc, QB, NB, H, C, scale_log2, scores, s)
+                    : launch_scores<__nv_bfloat16, 64>(who, grid, qc, kc, QB, NB, H, C, scale_log2, scores, s);
+  return D == 128 ? launch_scores<float, 128>(who, grid, qc, kc, QB, NB, H, C, scale_log2, scores, s)
+                  : launch_scores<float, 64>(who, grid, qc, kc, QB, NB, H, C, scale_log2, scores, s);
+}
+
+static int prepare_scores_for(const char* who, int kc_dtype, int D) {
+  if (kc_dtype == SB_BF16) return D == 128 ? prepare_scores<__nv_bfloat16, 128>(who) : prepare_scores<__nv_bfloat16, 64>(who);
+  return D == 128 ? prepare_scores<float, 128>(who) : prepare_scores<float, 64>(who);
 }
 
 // Top-K of `rows` score rows of C candidates: warps of one row each, as many per CTA as their
 // keys (C x 4 B + a 1 KB histogram each) fit in 200 KB of shared memory.
-static int launch_topk(const float* scores, int64_t rows, int C, int topk, int words, int32_t* packed,
-                       int32_t* indices, cudaStream_t s) {
+struct TopkLaunch {
+  int warps;
+  size_t smem;
+};
+
+static TopkLaunch topk_shape(int C) {
   const size_t per_warp = (size_t)(256 + C) * sizeof(uint32_t);
   const int warps = (int)std::min<size_t>(kTopkWarpMaxRows, std::max<size_t>(1, (200 * 1024) / per_warp));
-  const size_t smem = per_warp * warps;
-  if (smem > 200 * 1024) {
-    set_error("sb_route_topk: too many candidate blocks (%d)", C);
+  return TopkLaunch{warps, per_warp * warps};
+}
+
+static int prepare_topk(const char* who, int C) {
+  const TopkLaunch t = topk_shape(C);
+  if (t.smem > 200 * 1024) {
+    set_error("%s: too many candidate blocks (%d)", who, C);
     return SB_ERR_INVALID;
   }
-  cudaError_t err = cudaFuncSetAttribute(topk_rows_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  if (err != cudaSuccess) return cuda_error(err, "sb_route_topk: set smem");
-  topk_rows_warp_kernel<<<(unsigned)((rows + warps - 1) / warps), 32 * warps, smem, s>>>(scores, rows, C, topk, words, packed,
-                                                                                   indices);
-  SB_CHECK_LAUNCH("sb_route_topk: top-k launch");
+  cudaError_t err = cudaFuncSetAttribute(topk_rows_warp_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)t.smem);
+  if (err != cudaSuccess) return cuda_error_at(err, who, "set top-k smem");
+  return SB_OK;
+}
+
+static int launch_topk(const char* who, const float* scores, int64_t rows, int C, int topk, int words,
+                       const int32_t* head_topk, int H, int index_width, int32_t* packed, int32_t* indices,
+                       cudaStream_t s) {
+  const TopkLaunch t = topk_shape(C);
+  topk_rows_warp_kernel<<<(unsigned)((rows + t.warps - 1) / t.warps), 32 * t.warps, t.smem, s>>>(
+      scores, rows, C, topk, words, head_topk, H, index_width, packed, indices);
+  cudaError_t err = cudaGetLastError();
+  if (err != cudaSuccess) return cuda_error_at(err, who, "top-k launch");
   return SB_OK;
 }
 
@@ -201,36 +269,64 @@ extern "C" int64_t sb_route_workspace_bytes(int B, int QB, int H, int candidates
   return (int64_t)B * QB * H * candidates * (int64_t)sizeof(float);
 }
 
+// Shared argument checks of the route entry points (`who` names the caller in the message).
+static int check_route_args(const char* who, const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
+                            int H, int D, int candidates) {
+  SB_CHECK_ARG(qc && kc, "%s: null pointer", who);
+  SB_CHECK_ARG(kc_dtype == SB_F32 || kc_dtype == SB_BF16, "%s: bad key-centroid dtype", who);
+  SB_CHECK_ARG(B > 0 && QB > 0 && NB > 0 && H > 0, "%s: sizes must be positive", who);
+  SB_CHECK_ARG(QB <= NB, "%s: QB (%d) exceeds NB (%d)", who, QB, NB);
+  SB_CHECK_ARG(D == 64 || D == 128, "%s: head dim must be 64 or 128", who);
+  SB_CHECK_ARG(candidates >= 1 && candidates <= NB, "%s: candidates must lie in [1, NB], got %d", who, candidates);
+  SB_CHECK_ARG(ceil_div(NB, 32) <= 256, "%s: at most 8192 key blocks are supported", who);
+  SB_CHECK_ARG((size_t)candidates * sizeof(uint32_t) <= 200 * 1024, "%s: too many candidate blocks (%d)", who,
+               candidates);
+  SB_CHECK_ARG((int64_t)B * QB * H < (1ll << 31), "%s: too many rows", who);
+  return SB_OK;
+}
+
+// Scores into `workspace`, then the Top-K of every row (a fixed k, or per-head budgets).
+static int route_with_workspace(const char* who, const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
+                                int H, int D, int candidates, int topk, const int32_t* head_topk, int index_width,
+                                float scale_log2, void* workspace, int32_t* packed_route, int32_t* indices,
+                                cudaStream_t s) {
+  int rc = prepare_scores_for(who, kc_dtype, D);
+  if (rc == SB_OK) rc = prepare_topk(who, candidates);
+  if (rc != SB_OK) return rc;
+  float* scores = (float*)workspace;
+  dim3 grid(ceil_div(candidates, kScoreTile), ceil_div(QB, kScoreTile), B * H);
+  rc = scores_for(who, kc_dtype, D, grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s);
+  if (rc != SB_OK) return rc;
+  return launch_topk(who, scores, (int64_t)B * QB * H, candidates, topk, ceil_div(NB, 32), head_topk, H, index_width,
+                     packed_route, indices, s);
+}
+
 extern "C" int sb_route_topk(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
                              int H, int D, int candidates, int topk, float scale_log2,
                              void* workspace, int32_t* packed_route, int32_t* indices,
                              void* stream) {
-  SB_CHECK_ARG(qc && kc && workspace && packed_route, "sb_route_topk: null pointer");
-  SB_CHECK_ARG(kc_dtype == SB_F32 || kc_dtype == SB_BF16, "sb_route_topk: bad key-centroid dtype");
-  SB_CHECK_ARG(B > 0 && QB > 0 && NB > 0 && H > 0, "sb_route_topk: sizes must be positive");
-  SB_CHECK_ARG(QB <= NB, "sb_route_topk: QB (%d) exceeds NB (%d)", QB, NB);
-  SB_CHECK_ARG(D == 64 || D == 128, "sb_route_topk: head dim must be 64 or 128");
-  SB_CHECK_ARG(candidates >= 1 && candidates <= NB,
-               "sb_route_topk: candidates must lie in [1, NB], got %d", candidates);
-  SB_CHECK_ARG(topk >= 1 && topk <= candidates, "sb_route_topk: topk must lie in [1, candidates], got %d", topk);
-  const int words = ceil_div(NB, 32);
-  SB_CHECK_ARG(words <= 256, "sb_route_topk: at most 8192 key blocks are supported");
-  const size_t key_smem = (size_t)candidates * sizeof(uint32_t);
-  SB_CHECK_ARG(key_smem <= 200 * 1024, "sb_route_topk: too many candidate blocks (%d)", candidates);
-  cudaStream_t s = (cudaStream_t)stream;
-  float* scores = (float*)workspace;
-  dim3 grid(ceil_div(candidates, kScoreTile), ceil_div(QB, kScoreTile), B * H);
-  int rc = SB_OK;
-  if (kc_dtype == SB_BF16)
-    rc = D == 128 ? launch_scores<__nv_bfloat16, 128>(grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s)
-                  : launch_scores<__nv_bfloat16, 64>(grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s);
-  else
-    rc = D == 128 ? launch_scores<float, 128>(grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s)
-                  : launch_scores<float, 64>(grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s);
+  const char* who = "sb_route_topk";
+  int rc = check_route_args(who, qc, kc, kc_dtype, B, QB, NB, H, D, candidates);
   if (rc != SB_OK) return rc;
-  const int64_t rows = (int64_t)B * QB * H;
-  SB_CHECK_ARG(rows < (1ll << 31), "sb_route_topk: too many rows");
-  return launch_topk(scores, rows, candidates, topk, words, packed_route, indices, s);
+  SB_CHECK_ARG(workspace && packed_route, "%s: null pointer", who);
+  SB_CHECK_ARG(topk >= 1 && topk <= candidates, "%s: topk must lie in [1, candidates], got %d", who, topk);
+  return route_with_workspace(who, qc, kc, kc_dtype, B, QB, NB, H, D, candidates, topk, nullptr, topk, scale_log2,
+                              workspace, packed_route, indices, (cudaStream_t)stream);
+}
+
+extern "C" int sb_route_topk_head_budgets(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB,
+                                          int H, int D, int candidates, const int32_t* head_topk, int index_width,
+                                          float scale_log2, void* workspace, int32_t* packed_route,
+                                          int32_t* indices, void* stream) {
+  const char* who = "sb_route_topk_head_budgets";
+  int rc = check_route_args(who, qc, kc, kc_dtype, B, QB, NB, H, D, candidates);
+  if (rc != SB_OK) return rc;
+  SB_CHECK_ARG(head_topk && workspace && packed_route, "%s: null pointer", who);
+  SB_CHECK_ARG(indices == nullptr || (index_width >= 1 && index_width <= candidates),
+               "%s: index_width must lie in [1, candidates], got %d", who, index_width);
+  return route_with_workspace(who, qc, kc, kc_dtype, B, QB, NB, H, D, candidates, 0, head_topk,
+                              indices ? index_width : 0, scale_log2, workspace, packed_route, indices,
+                              (cudaStream_t)stream);
 }
 
 // ------------------------------------------------------------------------------------------
@@ -277,29 +373,26 @@ static float* route_noalloc_scratch(int* status) {
 extern "C" int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dtype, int B, int QB, int NB, int H,
                                      int D, int candidates, int topk, float scale_log2, int32_t* packed_route,
                                      int32_t* indices, void* stream) {
-  SB_CHECK_ARG(qc && kc && packed_route, "sb_route_topk_noalloc: null pointer");
-  SB_CHECK_ARG(kc_dtype == SB_F32 || kc_dtype == SB_BF16, "sb_route_topk_noalloc: bad key-centroid dtype");
-  SB_CHECK_ARG(B > 0 && QB > 0 && NB > 0 && H > 0, "sb_route_topk_noalloc: sizes must be positive");
-  SB_CHECK_ARG(QB <= NB, "sb_route_topk_noalloc: QB (%d) exceeds NB (%d)", QB, NB);
-  SB_CHECK_ARG(D == 64 || D == 128, "sb_route_topk_noalloc: head dim must be 64 or 128");
-  SB_CHECK_ARG(candidates >= 1 && candidates <= NB,
-               "sb_route_topk_noalloc: candidates must lie in [1, NB], got %d", candidates);
-  SB_CHECK_ARG(topk >= 1 && topk <= candidates,
-               "sb_route_topk_noalloc: topk must lie in [1, candidates], got %d", topk);
-  const int words = ceil_div(NB, 32);
-  SB_CHECK_ARG(words <= 256, "sb_route_topk_noalloc: at most 8192 key blocks are supported");
-  const size_t key_smem = (size_t)candidates * sizeof(uint32_t);
-  SB_CHECK_ARG(key_smem <= 200 * 1024, "sb_route_topk_noalloc: too many candidate blocks (%d)", candidates);
+  const char* who = "sb_route_topk_noalloc";
+  int rc = check_route_args(who, qc, kc, kc_dtype, B, QB, NB, H, D, candidates);
+  if (rc != SB_OK) return rc;
+  SB_CHECK_ARG(packed_route, "%s: null pointer", who);
+  SB_CHECK_ARG(topk >= 1 && topk <= candidates, "%s: topk must lie in [1, candidates], got %d", who, topk);
   const int64_t per_block = (int64_t)H * candidates;
   SB_CHECK_ARG(per_block <= kNoAllocScoreFloats,
-               "sb_route_topk_noalloc: H * candidates = %lld exceeds the %lld-float scratch array "
+               "%s: H * candidates = %lld exceeds the %lld-float scratch array "
                "(SB_ROUTE_NOALLOC_SCRATCH_FLOATS); use sb_route_topk with a caller workspace",
-               (long long)per_block, (long long)kNoAllocScoreFloats);
+               who, (long long)per_block, (long long)kNoAllocScoreFloats);
   int status = SB_OK;
   float* scratch = route_noalloc_scratch(&status);
   if (scratch == nullptr) return status;
+  // Kernel attributes are set once, before the chunk loop.
+  rc = prepare_scores_for(who, kc_dtype, D);
+  if (rc == SB_OK) rc = prepare_topk(who, candidates);
+  if (rc != SB_OK) return rc;
   cudaStream_t s = (cudaStream_t)stream;
   const int chunk = (int)std::min<int64_t>(QB, kNoAllocScoreFloats / per_block);
+  const int words = ceil_div(NB, 32);
   const size_t kc_elem = kc_dtype == SB_BF16 ? 2 : 4;
   for (int b = 0; b < B; ++b) {
     const char* kc_b = static_cast<const char*>(kc) + (size_t)b * NB * H * D * kc_elem;
@@ -307,17 +400,11 @@ extern "C" int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dty
       const int n = std::min(chunk, QB - q0);
       const float* qc_c = qc + ((int64_t)b * NB + q0) * H * D;
       dim3 grid(ceil_div(candidates, kScoreTile), ceil_div(n, kScoreTile), H);
-      int rc;
-      if (kc_dtype == SB_BF16)
-        rc = D == 128 ? launch_scores<__nv_bfloat16, 128>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s)
-                      : launch_scores<__nv_bfloat16, 64>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
-      else
-        rc = D == 128 ? launch_scores<float, 128>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s)
-                      : launch_scores<float, 64>(grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
+      rc = scores_for(who, kc_dtype, D, grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
       if (rc != SB_OK) return rc;
       const int64_t row0 = ((int64_t)b * QB + q0) * H;
-      rc = launch_topk(scratch, (int64_t)n * H, candidates, topk, words, packed_route + row0 * words,
-                       indices ? indices + row0 * topk : nullptr, s);
+      rc = launch_topk(who, scratch, (int64_t)n * H, candidates, topk, words, nullptr, H, topk,
+                       packed_route + row0 * words, indices ? indices + row0 * topk : nullptr, s);
       if (rc != SB_OK) return rc;
     }
   }

@@ -1,6 +1,7 @@
 """Builds the sm_100a shared library in-tree with nvcc (no JIT cache, no torch extension)."""
 from __future__ import annotations
 
+import hashlib
 import os
 import shutil
 import subprocess
@@ -35,18 +36,31 @@ def sources() -> list[Path]:
     return sorted(CSRC_DIR.glob("*.cu"))
 
 
-def _stale() -> bool:
-    if not LIB_PATH.exists():
+STAMP_PATH = LIB_DIR / (LIB_NAME + ".sha256")
+
+
+def source_digest() -> str:
+    """SHA-256 over the compiler flags and every source and header the library is built from."""
+    h = hashlib.sha256(" ".join(NVCC_FLAGS).encode())
+    for path in sources() + sorted(CSRC_DIR.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h")):
+        h.update(path.name.encode())
+        h.update(path.read_bytes())
+    return h.hexdigest()
+
+
+def stale() -> bool:
+    """True when the library is missing or was built from other sources or flags (compared by
+    content, so copied trees with fresh modification times are judged correctly)."""
+    if not LIB_PATH.exists() or not STAMP_PATH.exists():
         return True
-    built = LIB_PATH.stat().st_mtime
-    deps = sources() + sorted(CSRC_DIR.glob("*.cuh")) + sorted(INCLUDE_DIR.glob("*.h"))
-    return any(p.stat().st_mtime > built for p in deps)
+    return STAMP_PATH.read_text().strip() != source_digest()
 
 
 def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> Path:
     """Compile every .cu under csrc/ for sm_100a and link libsparkh3b200.so."""
-    if not force and not _stale():
+    if not force and not stale():
         return LIB_PATH
+    digest = source_digest()
     nvcc = _nvcc()
     obj_dir = LIB_DIR / "_obj"
     obj_dir.mkdir(parents=True, exist_ok=True)
@@ -74,6 +88,7 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
     link = [nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-o", str(tmp), *map(str, objs)]
     subprocess.check_call(link)
     os.replace(tmp, LIB_PATH)
+    STAMP_PATH.write_text(digest + "\n")
     return LIB_PATH
 
 

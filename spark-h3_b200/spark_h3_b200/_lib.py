@@ -6,9 +6,7 @@ fallback for any entry point.
 from __future__ import annotations
 
 import ctypes
-import os
 import threading
-from pathlib import Path
 
 from . import _build
 
@@ -38,6 +36,7 @@ SIGNATURES = {
                                     _vp]),
     "sb_route_workspace_bytes": (_i64, [_i, _i, _i, _i]),
     "sb_route_topk": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp, _vp]),
+    "sb_route_topk_head_budgets": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _i, _f, _vp, _vp, _vp, _vp]),
     "sb_route_topk_noalloc": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
@@ -84,15 +83,10 @@ def load(build_if_missing: bool = True) -> ctypes.CDLL:
     with _lock:
         if _lib is not None:
             return _lib
-        # SPARK_H3_B200_LIB points at another build of the same library (e.g. one compiled
-        # with different flags); by default the in-tree build is used.
-        override = os.environ.get("SPARK_H3_B200_LIB")
-        path = Path(override) if override else _build.LIB_PATH
-        if override and not path.exists():
-            raise RuntimeError(f"SPARK_H3_B200_LIB={override} does not exist")
-        if not path.exists():
+        path = _build.LIB_PATH
+        if not path.exists() or _build.stale():
             if not build_if_missing:
-                raise RuntimeError(f"spark_h3_b200 native library is missing: {path}")
+                raise RuntimeError(f"spark_h3_b200 native library is missing or out of date: {path}")
             _build.build()
         lib = ctypes.CDLL(str(path))
         for name, (restype, argtypes) in SIGNATURES.items():

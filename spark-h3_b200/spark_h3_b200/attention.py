@@ -62,9 +62,8 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
         raise NotImplementedError("the B200 path does not implement sol_legacy_full_query")
     if cfg.sol_tail_granularity == "block8x8" and cfg.sol_reweight_summary_math != "tensorcore":
         raise ValueError("block8x8 currently supports tensorcore numeric mode only")
-    if getattr(controller, "head_topk_budget", None) is not None:
-        raise NotImplementedError("per-head Top-K budgets are not available on the B200 path")
     B, T, H, D = q_bthd.shape
+    head_budgets = _head_budgets(getattr(controller, "head_topk_budget", None), H, q_bthd.device)
     block = cfg.sol_block_size
     video = int(layout.video_tokens)
     if video < block:
@@ -77,6 +76,10 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     sink_first = video // block
     sink_last = math.ceil((video + sink_tokens) / block) if sink_tokens else sink_first
     topk = ops.target_topk(cfg.sol_route_topk_ratio, candidates)
+    if head_budgets is not None and (sink_tokens or video % block):
+        # head_budget.py:16-18: with per-head budgets the partial video block and all
+        # conditioning stay exact.
+        sink_first, sink_last = candidates, nb
     weighted_kv, mass_bias = reweight_flags(cfg.sol_reweight_components)
     anchor_dtype = torch.float32 if cfg.sol_global_anchor_dtype == "float32" or q_bthd.dtype == torch.float32 \
         else q_bthd.dtype
@@ -99,7 +102,8 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     kc, ak, av, lm = ops.pool_keys_summaries(k_bthd, v_bthd, anchor, block, weighted_kv=weighted_kv,
                                              mass_bias=mass_bias, summary_math=cfg.sol_reweight_summary_math,
                                              logmass_key=cfg.sol_reweight_logmass_key)
-    packed, _ = ops.route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace, want_indices=False)
+    packed, _ = ops.route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace, want_indices=False,
+                               head_budgets=head_budgets)
     out = ops.pooled_tail_attention(q_bthd, k_bthd, v_bthd, block, packed, ak, av, lm, anchor,
                                     query_tokens=query_tokens, sink_first=sink_first, sink_last=sink_last,
                                     local_radius=cfg.kernel_local_radius, tail_granularity=cfg.sol_tail_granularity,
@@ -143,8 +147,9 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
         controller.sol_virtual_query_layout = {**topology, "layout": "identity_physical_order",
                                                "anchor_policy": "global"}
     if cfg.sol_log_density and controller.sol_route_density is None:
+        mode = "per_head_exact_topk" if head_budgets is not None else "gemm_exact_topk_packed_external"
         stats = dict(block_size=block, blocks=nb, candidate_video_blocks=candidates, query_video_blocks=query_blocks,
-                     sink_blocks=max(0, nb - candidates), route_threshold_mode="gemm_exact_topk_packed_external",
+                     sink_blocks=max(0, nb - candidates), route_threshold_mode=mode,
                      route_topk_ratio=cfg.sol_route_topk_ratio, target_topk_blocks_per_query=topk,
                      packed_route_words=math.ceil(nb / 32))
         stats.update(topk_density(stats))
@@ -152,6 +157,18 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     if query_inverse is not None:
         out = ops.headwise_permute(out, query_inverse, video)
     return out if return_bthd else out.permute(0, 2, 1, 3).contiguous()
+
+
+def _head_budgets(budget, heads: int, device: torch.device) -> torch.Tensor | None:
+    """The controller's per-head Top-K budgets (processor.py:787-796 sets them from a
+    head_budget_allocator) as int32 [H] on the layer's device; one budget per head is
+    required, as in head_budget.py:9-10."""
+    if budget is None:
+        return None
+    budget = torch.as_tensor(budget)
+    if tuple(budget.shape) != (heads,):
+        raise ValueError("expected one budget per head")
+    return budget.to(device=device, dtype=torch.int32).contiguous()
 
 
 _REBLOCK_DEFAULTS = dict(

@@ -109,9 +109,14 @@ def route_workspace_bytes(B: int, query_blocks: int, H: int, candidates: int) ->
 
 
 def route_topk(qc: torch.Tensor, kc: torch.Tensor, query_blocks: int, candidates: int, topk: int, *,
-               workspace: torch.Tensor | None = None, want_indices: bool = True):
-    """Packed route [B, QB, H, ceil(NB/32)] int32 and ascending indices [B, QB, H, topk]."""
-    device = _require_cuda(qc, kc, workspace)
+               workspace: torch.Tensor | None = None, want_indices: bool = True,
+               head_budgets: torch.Tensor | None = None):
+    """Packed route [B, QB, H, ceil(NB/32)] int32 and ascending indices [B, QB, H, topk].
+
+    With head_budgets (int32 [H] on the device; head_budget.py:7-19) head h keeps its own
+    head_budgets[h] blocks, clamped to [0, candidates]; the index rows are then `topk` wide
+    and padded with -1 past each row's budget."""
+    device = _require_cuda(qc, kc, workspace, head_budgets)
     B, NB, H, D = qc.shape
     words = math.ceil(NB / 32)
     need = route_workspace_bytes(B, query_blocks, H, candidates)
@@ -122,9 +127,16 @@ def route_topk(qc: torch.Tensor, kc: torch.Tensor, query_blocks: int, candidates
     packed = torch.empty((B, query_blocks, H, words), device=device, dtype=torch.int32)
     indices = torch.empty((B, query_blocks, H, topk), device=device, dtype=torch.int32) if want_indices else None
     with torch.cuda.device(device):
-        _lib.call("sb_route_topk", qc.data_ptr(), kc.data_ptr(), _dtype_code(kc), B, query_blocks, NB, H, D,
-                  candidates, topk, scale_log2(D), workspace.data_ptr(), packed.data_ptr(), _ptr(indices),
-                  _stream(device))
+        if head_budgets is None:
+            _lib.call("sb_route_topk", qc.data_ptr(), kc.data_ptr(), _dtype_code(kc), B, query_blocks, NB, H, D,
+                      candidates, topk, scale_log2(D), workspace.data_ptr(), packed.data_ptr(), _ptr(indices),
+                      _stream(device))
+        else:
+            if head_budgets.dtype != torch.int32 or head_budgets.shape != (H,):
+                raise ValueError(f"head_budgets must be int32 [{H}], got {head_budgets.dtype} {tuple(head_budgets.shape)}")
+            _lib.call("sb_route_topk_head_budgets", qc.data_ptr(), kc.data_ptr(), _dtype_code(kc), B, query_blocks,
+                      NB, H, D, candidates, head_budgets.data_ptr(), topk, scale_log2(D), workspace.data_ptr(),
+                      packed.data_ptr(), _ptr(indices), _stream(device))
     return packed, indices
 
 
@@ -288,7 +300,8 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
                 video_tokens: int | None = None, anchor_dtype: torch.dtype | None = None, local_radius: int = -1,
                 weighted_kv: bool = True, mass_bias: bool = True, workspace: torch.Tensor | None = None,
                 out: torch.Tensor | None = None, return_route: bool = False, tail_mode: str = "dense",
-                tail_granularity: str = "query", summary_math: str = "tensorcore", logmass_key: str = "stored"):
+                tail_granularity: str = "query", summary_math: str = "tensorcore", logmass_key: str = "stored",
+                head_budgets: torch.Tensor | None = None):
     """One Spark sparse attention layer on BTHD tensors whose video prefix comes first.
 
     pool Q -> anchor -> pool K + summaries -> scores + Top-K -> sparse attention
@@ -296,7 +309,10 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
     tail_mode "pad" the partial final video block is routed as a padded block and the context
     rows that padded it are then attended densely (sb_dense_rows_attention).  tail_granularity
     "block" / "block8x8" replaces the per-row summary columns by a pooled tail per query block
-    / per 8 rows, merged into the exact-keys-only output (sb_tail_merge).
+    / per 8 rows, merged into the exact-keys-only output (sb_tail_merge).  head_budgets
+    (int32 [H] on the device) gives each head its own Top-K budget (head_budget.py:7-19); the
+    blocks past the candidates are then exact when there is a context suffix or a partial
+    video block.
     """
     B, T, H, D = q.shape
     video = T if video_tokens is None else int(video_tokens)
@@ -309,12 +325,14 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
     sink_first = video // block
     sink_last = nb if T > video else sink_first
     topk = target_topk(topk_ratio, candidates)
+    if head_budgets is not None and (T > video or video % block):
+        sink_first, sink_last = candidates, nb
     qc = padded_query_means(q, pool_queries(q, block), video, query_tokens, block)
     anchor = query_anchor(qc, block, candidates, anchor_dtype or q.dtype)
     kc, ak, av, lm = pool_keys_summaries(k, v, anchor, block, weighted_kv=weighted_kv, mass_bias=mass_bias,
                                          summary_math=summary_math, logmass_key=logmass_key)
     packed, indices = route_topk(qc, kc, query_blocks, candidates, topk, workspace=workspace,
-                                 want_indices=return_route)
+                                 want_indices=return_route, head_budgets=head_budgets)
     o = pooled_tail_attention(q, k, v, block, packed, ak, av, lm, anchor, query_tokens=query_tokens,
                               sink_first=sink_first, sink_last=sink_last, local_radius=local_radius, out=out,
                               tail_granularity=tail_granularity, weighted_kv=weighted_kv, mass_bias=mass_bias,

@@ -102,7 +102,20 @@ def apply_rotary_emb(hidden_states, rotary_emb):
 
 
 def _sol_attention(controller, q, k, v, layout, layer, *, return_bthd=False, inputs_bthd=False):
-    """q, k, v as BHTD (inputs_bthd=False) or BTHD; returns BTHD when return_bthd."""
+    """q, k, v as BHTD (inputs_bthd=False) or BTHD; returns BTHD when return_bthd.
+
+    A controller with a head_budget_allocator gets per-head Top-K budgets for this layer
+    from allocator(layer, evaluation_index, V as BHTD, video_tokens) (processor.py:782-796)."""
+    cfg = controller.config
+    allocator = getattr(controller, "head_budget_allocator", None)
+    if allocator is not None:
+        if cfg.sol_route_topk_ratio is None:
+            raise ValueError("head budget allocation requires a Top-K configuration")
+        budget_values = v.permute(0, 2, 1, 3) if inputs_bthd else v
+        controller.head_topk_budget = allocator(layer, controller.evaluation_index, budget_values,
+                                                layout.video_tokens)
+    else:
+        controller.head_topk_budget = None
     if not inputs_bthd:
         q, k, v = (x.permute(0, 2, 1, 3).contiguous() for x in (q, k, v))
     return spark_attention_bthd(controller, q, k, v, layout, layer, return_bthd=return_bthd)
@@ -151,7 +164,8 @@ class _H3SparseProcessor:
         del key
         packed_v = value.index_select(1, permutation).contiguous()
         del value
-        output = spark_attention_bthd(c, packed_q, packed_k, packed_v, layout, self.layer, return_bthd=True)
+        output = _sol_attention(c, packed_q, packed_k, packed_v, layout, self.layer, return_bthd=True,
+                                inputs_bthd=True)
         output = output.index_select(1, layout.inverse_permutation).flatten(2, 3).to(dtype)
         output = attn.to_out[0](output)
         output = attn.to_out[1](output)

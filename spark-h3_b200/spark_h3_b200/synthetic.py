@@ -53,14 +53,17 @@ def sinusoid_tensor(grid, heads: int, head_dim: int, *, generator: torch.Generat
 
 
 def make_qkv(grid, heads: int, head_dim: int, *, seed: int = 0, device=None, dtype=torch.bfloat16,
-             q_scale: float = 1.0, clustered: bool = False):
-    """Q, K, V [1, T, H, D]; Q is multiplied by q_scale (config 1 uses 1/sqrt(D))."""
+             q_scale: float = 1.0, clustered: bool = False, with_v: bool = True):
+    """Q, K, V [1, T, H, D]; Q is multiplied by q_scale (config 1 uses 1/sqrt(D)).  With
+    with_v=False only Q and K are drawn (V is drawn last, so Q and K are the same)."""
     gen = torch.Generator(device=device if device is not None else "cpu").manual_seed(seed)
     q = sinusoid_tensor(grid, heads, head_dim, generator=gen, device=device, clustered=clustered)
     if q_scale != 1.0:
         q.mul_(q_scale)
     q = q.to(dtype)
     k = sinusoid_tensor(grid, heads, head_dim, generator=gen, device=device, dtype=dtype, clustered=clustered)
+    if not with_v:
+        return q, k
     v = sinusoid_tensor(grid, heads, head_dim, generator=gen, device=device, dtype=dtype, clustered=clustered)
     return q, k, v
 

@@ -14,6 +14,15 @@ Fixtures:
   route_*.npz     _sol_topk_policy_scores + _sol_topk_route_from_scores
                   (spark_integration.py:94-175): the selected block sets per row, and the
                   gap between the k-th and (k+1)-th score of every row
+  route_config1_b64.npz  the same reference route at production size (
+                  grid (31, 48, 84), N = 124,992, H = 32, D = 128, bf16, 64-token blocks,
+                  k = 195 of 1953): per row a 64-bit digest (the first 8 bytes of the SHA-256
+                  of the ascending int32 block indices) and the k-th/(k+1)-th score gap, plus
+                  the full sets of 256 seeded sample rows
+  head_budget.npz route_with_head_budgets (head_budget.py:7-19): per-head budgets on seeded
+                  scores quantised to force ties at the cut ("ties"), and on the fp32
+                  scores of _sol_topk_policy_scores for synthetic Q/K with a context suffix
+                  ("pipeline"); the boolean routes over every key block
   summaries.npz   the Triton _summaries kernel (sol_numerator_virtual_q.py:93-135) run under
                   TRITON_INTERPRET=1 in fp32 at D=128
   attention.npz   the explicit exact/summary softmax of tests/test_spark_installer.py:559-570
@@ -139,6 +148,75 @@ def route_case(name, grid, heads, dim, dtype, q_scale, seed):
                                                       q_scale=q_scale, seed=seed))))
 
 
+def row_digests(indices: np.ndarray) -> np.ndarray:
+    """uint64 per row: the first 8 bytes (little endian) of the SHA-256 of the row's ascending
+    int32 indices."""
+    rows = np.ascontiguousarray(np.sort(indices.reshape(-1, indices.shape[-1]), axis=-1).astype("<i4"))
+    return np.array([int.from_bytes(hashlib.sha256(r.tobytes()).digest()[:8], "little") for r in rows],
+                    dtype=np.uint64)
+
+
+def route_config1_case():
+    """The reference's fp32 route at BASELINE config 1 with 64-token blocks (its only block
+    size): Q/K from the seeded generator the tests share, key centroids as the fp32 block mean
+    rounded to bf16 (the _reduce_kc_kernel rule, sol_attn/preprocess.py:16-52)."""
+    from h3_sparse_attention.spark_integration import _sol_topk_policy_scores, _sol_topk_route_from_scores
+    from spark_h3_b200.synthetic import make_qkv
+
+    grid, heads, dim, seed = (31, 48, 84), 32, 128, 0
+    q, k = make_qkv(grid, heads, dim, seed=seed, dtype=torch.bfloat16, q_scale=dim ** -0.5, with_v=False)
+    T = q.shape[1]
+    kc = block_mean(k, 64).to(torch.bfloat16)
+    scores, adjacent, cand, qblocks, target = _sol_topk_policy_scores(q, kc, video_tokens=T, topk_ratio=0.1)
+    route = _sol_topk_route_from_scores(scores, adjacent, candidate_blocks=cand, target_topk=target,
+                                        video_tokens=T, sink_tokens=0)
+    sel = route[0, :qblocks, :, :cand]                       # [QB, H, C]
+    assert int(sel.sum(-1).min()) == target and int(sel.sum(-1).max()) == target
+    idx = torch.nonzero(sel.reshape(-1, cand))[:, 1].reshape(-1, target).numpy()  # ascending per row
+    s = scores[0, :qblocks, :, :cand]
+    top = torch.topk(s, target + 1, dim=-1).values
+    gap = (top[..., target - 1] - top[..., target]).reshape(-1).numpy().astype(np.float32)
+    rng = np.random.default_rng(1)
+    sample = np.sort(rng.choice(idx.shape[0], 256, replace=False)).astype(np.int32)
+    np.savez_compressed(HERE / "route_config1_b64.npz", row_digest=row_digests(idx), gap=gap,
+                        sample_rows=sample, sample_sets=idx[sample].astype(np.int16),
+                        q_digest=np.array(digest(q)), k_digest=np.array(digest(k)), target=np.array(target),
+                        meta=np.array(json.dumps(dict(grid=grid, heads=heads, dim=dim, dtype="torch.bfloat16",
+                                                      q_scale=dim ** -0.5, seed=seed, block=64,
+                                                      topk_ratio=0.1))))
+
+
+def head_budget_fixture():
+    from h3_sparse_attention.head_budget import route_with_head_budgets
+    from h3_sparse_attention.spark_integration import _sol_topk_policy_scores
+    from spark_h3_b200.synthetic import make_qkv
+
+    out = {}
+    # ties: scores on a grid of 8 values, so every cut falls inside a group of equal scores;
+    # budgets include 0 and one above the candidate count.
+    gen = torch.Generator().manual_seed(23)
+    scores = torch.randint(0, 8, (1, 12, 5, 44), generator=gen).float() / 4.0
+    budgets = torch.tensor([0, 1, 7, 40, 50])
+    route = route_with_head_budgets(scores, budgets, 40, 40 * 64 + 17, 0)  # partial video block
+    out.update(ties_scores=scores.numpy(), ties_budgets=budgets.numpy().astype(np.int32),
+               ties_route=route.numpy().astype(np.uint8), ties_candidates=np.array(40),
+               ties_video=np.array(40 * 64 + 17))
+    # pipeline: fp32 policy scores of synthetic Q/K; 100 context tokens follow the video.
+    grid, heads, dim = (2, 16, 40), 4, 128
+    q, k, _ = make_qkv(grid, heads, dim, seed=29, dtype=torch.bfloat16, q_scale=dim ** -0.5)
+    T = q.shape[1]
+    video = T - 100
+    kc = block_mean(k, 64).to(torch.bfloat16)
+    scores, _, cand, qblocks, target = _sol_topk_policy_scores(q, kc, video_tokens=video, topk_ratio=0.1)
+    budgets = torch.tensor([3, 0, 12, 21])
+    route = route_with_head_budgets(scores, budgets, cand, video, T - video)
+    out.update(pipe_route=route[:, :qblocks].numpy().astype(np.uint8), pipe_budgets=budgets.numpy().astype(np.int32),
+               pipe_video=np.array(video), pipe_candidates=np.array(cand), pipe_q_digest=np.array(digest(q)),
+               pipe_k_digest=np.array(digest(k)),
+               pipe_meta=np.array(json.dumps(dict(grid=grid, heads=heads, dim=dim, seed=29, q_scale=dim ** -0.5))))
+    np.savez_compressed(HERE / "head_budget.npz", **out)
+
+
 def summaries_and_attention():
     import triton
     from h3_sparse_attention.sol_numerator_virtual_q import _summaries
@@ -240,6 +318,8 @@ def main():
     (HERE / "layout.json").write_text(json.dumps(layout_cases()))
     route_case("config0", (4, 32, 32), 4, 64, torch.float32, 1.0, 0)
     route_case("bf16_d128", (2, 32, 64), 2, 128, torch.bfloat16, 128 ** -0.5, 1)
+    route_config1_case()
+    head_budget_fixture()
     summaries_and_attention()
     reblock_tree_fixture()
     reblock_qk_fixture()
@@ -247,4 +327,8 @@ def main():
 
 
 if __name__ == "__main__":
-    main()
+    if len(sys.argv) > 1:
+        for name in sys.argv[1:]:  # a subset, e.g. route_config1_case
+            globals()[name]()
+    else:
+        main()

@@ -120,3 +120,23 @@ def test_tail_merge_and_summaries_reject_bad_arguments():
         args = {**summ, **change}
         assert lib.sb_pool_keys_summaries(*(args[n] for n in order)) == -1, change
         assert message in lib.sb_last_error(), (change, lib.sb_last_error())
+
+
+def test_route_entry_points_name_themselves_in_their_errors():
+    lib = _lib.load()
+    args = dict(qc=_P, kc=_P, dtype=1, B=1, QB=32, NB=32, H=2, D=128, candidates=32)
+    order = tuple(args)
+    base = [args[n] for n in order]
+    # sb_route_topk(..., topk, scale, workspace, packed, indices, stream)
+    assert lib.sb_route_topk(*base, 40, 1.0, _P, _P, None, None) == -1
+    assert lib.sb_last_error().startswith(b"sb_route_topk: topk must lie in [1, candidates], got 40")
+    assert lib.sb_route_topk_noalloc(*base, 0, 1.0, _P, None, None) == -1
+    assert lib.sb_last_error().startswith(b"sb_route_topk_noalloc: topk must lie in [1, candidates], got 0")
+    # sb_route_topk_head_budgets(..., head_topk, index_width, scale, workspace, packed, indices, stream)
+    assert lib.sb_route_topk_head_budgets(*base, None, 3, 1.0, _P, _P, None, None) == -1
+    assert lib.sb_last_error().startswith(b"sb_route_topk_head_budgets: null pointer")
+    assert lib.sb_route_topk_head_budgets(*base, _P, 33, 1.0, _P, _P, _P, None) == -1
+    assert lib.sb_last_error().startswith(b"sb_route_topk_head_budgets: index_width must lie in [1, candidates]")
+    bad = {**args, "D": 96}
+    assert lib.sb_route_topk_head_budgets(*(bad[n] for n in order), _P, 3, 1.0, _P, _P, None, None) == -1
+    assert lib.sb_last_error().startswith(b"sb_route_topk_head_budgets: head dim must be 64 or 128")

@@ -404,3 +404,34 @@ def test_all_zero_inputs_match_oracle(cuda_device):
     assert np.all(as_np(out) == 0.0)
     np.testing.assert_array_equal(ref["out"], 0.0)
     assert ops.read_device_status(cuda_device) == 0
+
+
+@pytest.mark.parametrize("block", [64, 128])
+@pytest.mark.parametrize("ties", [False, True])
+def test_head_budget_route_matches_oracle(cuda_device, block, ties):
+    """Per-head Top-K budgets (head_budget.py:7-19): budgets of 0, inside and above the
+    candidate count, a context suffix that keeps every block past the candidates exact, and
+    (ties=True) key blocks repeating with period 4 so every cut falls inside equal scores."""
+    grid = (2, 16, 40)
+    q, k, v = make_qkv(grid, 4, 128, seed=29, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    T = q.shape[1]
+    video = T - 100
+    if ties:
+        nb = T // block
+        k = k.view(1, nb, block, 4, 128)[:, [b % 4 for b in range(nb)]].reshape(1, T, 4, 128).contiguous()
+    candidates = video // block
+    budgets = np.array([3, 0, candidates - 1, candidates + 3], dtype=np.int32)
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             video_tokens=video, head_budgets=budgets)
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, video_tokens=video, return_route=True,
+                                 head_budgets=torch.from_numpy(budgets).to(cuda_device))
+    torch.cuda.synchronize()
+    assert (route["sink_first"], route["sink_last"]) == (ref["sink_first"], ref["sink_last"]) == \
+        (candidates, math.ceil(T / block))
+    np.testing.assert_array_equal(route["packed"].cpu().numpy(), ref["packed"])
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    counts = (route["indices"].cpu().numpy() >= 0).sum(-1)[0]
+    assert np.array_equal(counts, np.broadcast_to(np.minimum(np.clip(budgets, 0, candidates), ref["topk"]),
+                                                  counts.shape))
+    _check(as_np(out), ref["out"], torch.bfloat16)

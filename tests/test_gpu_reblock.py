@@ -112,8 +112,35 @@ def test_qk_permutations(cuda_device):
     got = np.concatenate([kp.cpu().numpy().reshape(H, T), qp.cpu().numpy().reshape(H, T)])
     got_inv = np.concatenate([ki.cpu().numpy().reshape(H, T), qi.cpu().numpy().reshape(H, T)])
     assert np.array_equal(got, ref) and np.array_equal(got_inv, ref_inv)
+    # Against the reference's permutations of the same Q/K: the metric factors differ (this
+    # build's fp32 moments and Cholesky against the reference's torch/LAPACK fp32 ones; their
+    # bf16 roundings differ in about 3 % of the factor elements), which moves about 4 % of the
+    # positions.  Given the reference's own factors the match is exact (next test).
     reference = np.concatenate([z["k_perm"].reshape(H, T), z["q_perm"].reshape(H, T)])
-    assert (got == reference).mean() > 0.9
+    assert (got == reference).mean() >= 0.95
+
+
+def test_transform_and_tree_reproduce_reference_permutations_given_its_factors(cuda_device):
+    """The reference's own Cholesky factors (tests/golden/reblock_qk.npz) through the GPU
+    feature transform and the GPU landmark tree give the reference's Q and K permutations and
+    inverses bit for bit: the tensor-core transform's last-bit roundings move no token here."""
+    z = np.load(GOLDEN / "reblock_qk.npz")
+    grid = tuple(int(g) for g in z["grid"])
+    H = int(z["heads"])
+    q, k, _ = make_qkv(grid, H, 128, seed=7, dtype=torch.bfloat16, clustered=True)
+    q, k = q.to(cuda_device), k.to(cuda_device)
+    T = q.shape[1]
+    factors = torch.from_numpy(np.ascontiguousarray(z["factors"], dtype=np.float32)).to(cuda_device)
+    features = reblock.transform(q, k, factors, T)
+    equal = (bits(features) == z["features"]).mean()
+    plan = reblock.ReblockPlan(T, 16, grid_shape=grid, device=cuda_device)
+    perm, inverse = plan.run(features)
+    torch.cuda.synchronize()
+    reference = np.concatenate([z["k_perm"].reshape(H, T), z["q_perm"].reshape(H, T)])
+    reference_inv = np.concatenate([z["k_inv"].reshape(H, T), z["q_inv"].reshape(H, T)])
+    print(f"features bit-equal to the reference's: {equal * 100:.4f} %")
+    assert np.array_equal(perm.cpu().numpy(), reference)
+    assert np.array_equal(inverse.cpu().numpy(), reference_inv)
 
 
 def test_full_mode_layer(cuda_device):

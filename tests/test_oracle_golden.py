@@ -100,3 +100,55 @@ def test_pooled_tail_oracle_with_every_block_exact_is_dense_attention():
     for granularity in ("block", "block8x8"):
         ref = oracle.spark_layer(t(q), t(k), t(v), block=64, topk_ratio=1.0, tail_granularity=granularity)
         np.testing.assert_allclose(ref["out"][0, :, 0], dense, atol=1e-5)
+
+
+def test_oracle_route_matches_reference_route_at_config1():
+    """Production size: every (query block, head) row of the oracle's route at BASELINE
+    config 1 with 64-token blocks (62,496 rows of 1953 candidates, k = 195) equals the
+    reference's own fp32 route, except rows where the reference's k-th and (k+1)-th scores
+    are exactly equal."""
+    import _config1
+
+    fx = _config1.fixture()
+    q, k = _config1.inputs(with_v=False)
+    T = q.shape[1]
+    candidates, nb = T // 64, -(-T // 64)
+    qc = oracle.block_means(_config1.host(q), 64)
+    kc = oracle.key_means(_config1.host(k), 64)
+    idx, _ = oracle.topk(oracle.scores(qc, kc, candidates, candidates), int(fx["target"]), nb)
+    differ = _config1.compare_with_reference(idx, fx)
+    assert differ.size == candidates * _config1.HEADS
+
+
+def test_oracle_head_budgets_match_reference():
+    """route_with_head_budgets (head_budget.py:7-19): per-head budgets, including 0 and one
+    above the candidate count, with every cut inside a group of equal scores, and on the fp32
+    policy scores of synthetic Q/K with a context suffix."""
+    g = np.load(GOLDEN / "head_budget.npz")
+    scores = g["ties_scores"]
+    cand = int(g["ties_candidates"])
+    nb = scores.shape[-1]
+    idx, packed = oracle.topk_head_budgets(np.ascontiguousarray(scores[..., :cand]), g["ties_budgets"], nb)
+    ref = g["ties_route"].astype(bool)
+    kb = np.arange(nb)
+    ours = ((packed[..., kb >> 5].astype(np.int64) >> (kb & 31)) & 1).astype(bool)
+    ours[..., cand:] = True  # the partial video block (video % 64 != 0) stays exact
+    np.testing.assert_array_equal(ours, ref)
+    budgets = np.clip(g["ties_budgets"], 0, cand)
+    assert np.array_equal((idx >= 0).sum(-1)[0, 0], budgets)
+
+    meta = json.loads(str(g["pipe_meta"]))
+    q, k, v = make_qkv(tuple(meta["grid"]), meta["heads"], meta["dim"], seed=meta["seed"], dtype=torch.bfloat16,
+                       q_scale=meta["q_scale"])
+    assert digest(q) == str(g["pipe_q_digest"]) and digest(k) == str(g["pipe_k_digest"])
+    video = int(g["pipe_video"])
+    res = oracle.spark_layer(host(q), host(k), host(v), block=64, topk_ratio=0.1, video_tokens=video,
+                             attention=False, head_budgets=g["pipe_budgets"])
+    nb = -(-q.shape[1] // 64)
+    kb = np.arange(nb)
+    ours = ((res["packed"][..., kb >> 5].astype(np.int64) >> (kb & 31)) & 1).astype(bool)
+    ours |= (kb >= res["sink_first"]) & (kb < res["sink_last"])
+    # The reference also routes the partial final video query block; with the dense tail its
+    # rows attend every key, so the routed query blocks are compared.
+    routed = res["packed"].shape[1]
+    np.testing.assert_array_equal(ours, g["pipe_route"][:, :routed].astype(bool))

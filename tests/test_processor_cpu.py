@@ -136,3 +136,45 @@ def test_oracle_pad_fill_is_the_tail_mean():
     got = torch.from_numpy(padded.data.view(np.int16)).view(torch.bfloat16)
     assert torch.equal(got[:, video:128], expected.expand(-1, 128 - video, -1, -1))
     assert torch.equal(got[:, :video], q[:, :video]) and torch.equal(got[:, 128:], q[:, 128:])
+
+
+def test_head_budget_allocator_sets_the_layer_budget(monkeypatch):
+    """processor.py:782-796: a controller's head_budget_allocator is called per sparse layer
+    with (layer, evaluation, V as BHTD, video tokens), and its result reaches the attention
+    seam as controller.head_topk_budget; without one the budget is cleared."""
+    from spark_h3_b200 import processor as proc
+
+    cfg = H3SparseAttentionConfig.spark(num_denoise_steps=1, warmup_mode="warmup_steps", warmup_steps=0)
+    controller = _Controller(cfg)
+    controller.evaluation_index = 0
+    seen = {}
+
+    def fake_seam(ctrl, q, k, v, layout, layer, return_bthd=True):
+        seen["budget"] = ctrl.head_topk_budget
+        return q
+
+    monkeypatch.setattr(proc, "spark_attention_bthd", fake_seam)
+    calls = []
+
+    def allocator(layer, evaluation, values, video_tokens):
+        calls.append((layer, evaluation, tuple(values.shape), video_tokens))
+        return torch.tensor([1, 2])
+
+    controller.head_budget_allocator = allocator
+    q = torch.zeros(1, 8, 2, 4)  # BTHD
+    layout = type("L", (), dict(video_tokens=6))()
+    proc._sol_attention(controller, q, q, q, layout, 3, return_bthd=True, inputs_bthd=True)
+    assert calls == [(3, 0, (1, 2, 8, 4), 6)]
+    assert seen["budget"].tolist() == [1, 2]
+    controller.head_budget_allocator = None
+    proc._sol_attention(controller, q, q, q, layout, 3, return_bthd=True, inputs_bthd=True)
+    assert seen["budget"] is None
+
+
+def test_head_budget_needs_one_budget_per_head():
+    from spark_h3_b200.attention import _head_budgets
+
+    assert _head_budgets(None, 4, torch.device("cpu")) is None
+    assert _head_budgets([1, 2, 3, 4], 4, torch.device("cpu")).dtype == torch.int32
+    with pytest.raises(ValueError, match="expected one budget per head"):
+        _head_budgets(torch.tensor([1, 2, 3]), 4, torch.device("cpu"))
