@@ -17,9 +17,15 @@ config 1 only.
 
 With N > 1 (torchrun, one process per GPU) the 32 heads are split across ranks (strong
 scaling, no data-path collective); timing is the max over ranks.  `value` is the
-dense-equivalent throughput 4*N^2*H*D / time of the whole job.  `--impl reference` times
-the CPU restatement of the same layer (oracle/, the reference being a Python/Triton
-project that cannot run here) on a bounded sample and extrapolates to the full layer.
+dense-equivalent throughput 4*N^2*H*D / time of the whole job.  Every `--gpus N` line also
+carries `dit_stack`: BASELINE config 4 (the 8-block synthetic DiT at N = 245,952) run as the
+19-step schedule (4 dense + 15 Spark evaluations) in one timed region, tokens split across
+the ranks and heads exchanged by NCCL all-to-all, with the exchange time per sparse step.
+
+`--impl reference` times the CPU restatement of the same layer (oracle/: the reference is
+a Python/Triton project whose kernels do not run on the host) on the host cores: the route
+and the summaries of all 32 heads in full, and the attention of a sample of query blocks of
+one head, extrapolated to the layer.  The repo arm's `cpu_baseline` is one such step.
 """
 from __future__ import annotations
 
@@ -66,12 +72,32 @@ def sparse_flops(tokens: int, heads: int, dim: int, block: int, topk: int) -> fl
 
 
 def load_peaks() -> dict:
+    """Roofline denominators.  The config-1 kernel is timed over well under a second, so
+    its peak is the burst bf16 figure; the sustained one (a seconds-long loop at the power
+    cap) is reported beside it."""
     path = ROOT / "MEASURED_PEAKS.json"
     if path.exists():
         data = json.loads(path.read_text())
-        return dict(bf16=data.get("bf16_tflops_sustained") or data.get("bf16_tflops"), hbm=data.get("hbm_gbs"),
-                    source="MEASURED_PEAKS.json (bf16 sustained)")
-    return dict(bf16=1400.0, hbm=6650.0, source="fallback (1.4 PFLOP/s sustained, 6.65 TB/s)")
+        burst = data.get("bf16_tflops") or data.get("bf16_tflops_sustained")
+        return dict(bf16=burst, bf16_sustained=data.get("bf16_tflops_sustained") or burst, hbm=data.get("hbm_gbs"),
+                    source="MEASURED_PEAKS.json bf16_tflops (burst; measured, not nominal)")
+    return dict(bf16=1590.0, bf16_sustained=1400.0, hbm=6650.0,
+                source="fallback (1.59 PFLOP/s burst, 1.4 sustained, 6.65 TB/s)")
+
+
+def config1_dict(world: int, topk: int, T: int) -> dict:
+    """The config entry shared by both arms of the config-1 line."""
+    nb = math.ceil(T / BLOCK)
+    name = "config1" if (GRID, HEADS) == ((31, 48, 84), 32) else "config1 shape, reduced"
+    return dict(workload=(f"{name}: one sparse attention layer, N={T} ({'x'.join(map(str, GRID))}), H={HEADS}, "
+                          f"D={HEAD_DIM}, block {BLOCK}, topk {TOPK_RATIO} ({topk} of {T // BLOCK} blocks; {nb} with "
+                          "the partial tail), reweight summaries + LSE correction, no reblock"),
+                global_batch=1, seq_len=T, heads=HEADS, head_dim=HEAD_DIM, block=BLOCK, topk=topk,
+                parallelism=f"heads/{world}" if world > 1 else "single GPU",
+                l2="inputs (3 x 1.02 GB) exceed the 126 MB L2; no flush between steps")
+
+
+DATA1 = "synthetic (seeded 8-sinusoid + 0.3 N(0,1) Q/K/V, Q scaled by 1/sqrt(D))"
 
 
 class ClockSampler:
@@ -126,19 +152,28 @@ class ClockSampler:
                     samples=len(mhz))
 
 
-def cpu_baseline(sample_blocks: int = 96) -> dict:
-    """The CPU oracle on one head: full route + summaries, attention for `sample_blocks`
-    query blocks, extrapolated to all 977 blocks and 32 heads."""
+def host_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except AttributeError:
+        return os.cpu_count() or 1
+
+
+def cpu_layer_sample(q, k, v, sample_blocks: int, summary_heads: int = 2) -> dict:
+    """One config-1 layer of the CPU restatement (oracle/) on bf16 CPU tensors [1, T, H, D]:
+    the route of every head in full (block means, fp32 scores, Top-K, in C with OpenMP
+    threads: the restatement of the reference's own CPU route); the anchor-weighted
+    summaries of `summary_heads` heads (numpy float64) and the attention of the first
+    `sample_blocks` query blocks of head 0 (numpy float64), whose times are extrapolated to
+    all heads and query blocks."""
     import numpy as np
     import torch
 
     from oracle import oracle
-    from spark_h3_b200.synthetic import make_qkv
 
-    q, k, v = make_qkv(GRID, 1, HEAD_DIM, seed=0, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
     host = lambda t: oracle.Tensor(t.contiguous().view(torch.int16).numpy().view(np.uint16), "bfloat16")
     oq, ok_, ov = host(q), host(k), host(v)
-    T = q.shape[1]
+    _, T, H, _ = q.shape
     nb = math.ceil(T / BLOCK)
     qb = T // BLOCK
     topk = oracle.target_topk(TOPK_RATIO, qb)
@@ -146,44 +181,64 @@ def cpu_baseline(sample_blocks: int = 96) -> dict:
     qc = oracle.block_means(oq, BLOCK)
     kc = oracle.key_means(ok_, BLOCK)
     a = oracle.anchor(qc, BLOCK, qb, "bfloat16")
-    sc = oracle.scores(qc, kc, qb, qb)
-    _, packed = oracle.topk(sc, topk, nb)
-    ak, av, lm = oracle.summaries(a, ok_, ov, BLOCK)
+    _, packed = oracle.topk(oracle.scores(qc, kc, qb, qb), topk, nb)
     t_route = time.perf_counter() - t0
-    t1 = time.perf_counter()
-    oracle.sparse_attention(oq, ok_, ov, BLOCK, packed, ak, av, lm, qb * BLOCK, qb, qb,
-                            rows=slice(0, sample_blocks * BLOCK))
-    t_attn = time.perf_counter() - t1
-    per_head = t_route + t_attn * nb / sample_blocks
-    layer_s = per_head * HEADS
-    return dict(value=dense_flops(T, HEADS, HEAD_DIM) / layer_s / 1e12, unit=UNIT, cores=os.cpu_count(),
-                kind="port", layer_seconds_extrapolated=layer_s,
-                sample=(f"1 of {HEADS} heads: full route+summaries ({t_route:.2f} s) and attention for "
-                        f"{sample_blocks} of {nb} query blocks ({t_attn:.2f} s); extrapolated x{nb}/{sample_blocks} "
-                        f"blocks and x{HEADS} heads; numpy/BLAS threads = all host cores"))
+    summary_heads = min(summary_heads, H)
+    ks, vs = (host(x[:, :, :summary_heads]) for x in (k, v))
+    t0 = time.perf_counter()
+    ak, av, lm = oracle.summaries(np.ascontiguousarray(a[:, :summary_heads]), ks, vs, BLOCK)
+    t_summ = time.perf_counter() - t0
+    q0, k0, v0 = (host(x[:, :, 0:1]) for x in (q, k, v))
+    t0 = time.perf_counter()
+    oracle.sparse_attention(q0, k0, v0, BLOCK, np.ascontiguousarray(packed[:, :, 0:1]), ak[:, 0:1], av[:, 0:1],
+                            lm[:, 0:1], qb * BLOCK, qb, qb, rows=slice(0, sample_blocks * BLOCK))
+    t_attn = time.perf_counter() - t0
+    factor = nb / sample_blocks * H
+    summ_factor = H / summary_heads
+    layer_s = t_route + t_summ * summ_factor + t_attn * factor
+    return dict(value=dense_flops(T, H, HEAD_DIM) / layer_s / 1e12, unit=UNIT, cores=host_cores(), kind="port",
+                layer_seconds_extrapolated=layer_s, sample_seconds=t_route + t_summ + t_attn,
+                attention_extrapolation_factor=factor, summary_extrapolation_factor=summ_factor,
+                sample=(f"route of all {H} heads in full ({t_route:.2f} s); summaries of {summary_heads} of {H} "
+                        f"heads ({t_summ:.2f} s) x {summ_factor:.0f}; attention of {sample_blocks} of {nb} query "
+                        f"blocks of one head ({t_attn:.2f} s) x {factor:.0f} ({nb}/{sample_blocks} blocks x {H} "
+                        f"heads); C oracle with OpenMP and numpy/BLAS on all {host_cores()} host threads"))
 
 
 def run_reference(args) -> None:
+    """The reference arm: the CPU restatement of the config-1 layer on this host's cores,
+    each step one cpu_layer_sample (rank 0 only; other ranks exit without work)."""
+    import torch
+
+    from spark_h3_b200.synthetic import make_qkv
+
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
         return
-    steps = []
-    base = None
+    q, k, v = make_qkv(GRID, HEADS, HEAD_DIM, seed=0, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
+    samples = []
     for i in range(args.warmup + args.steps):
-        base = cpu_baseline(sample_blocks=args.reference_sample_blocks)
+        base = cpu_layer_sample(q, k, v, args.cpu_sample_blocks)
         if i >= args.warmup:
-            steps.append(base["layer_seconds_extrapolated"])
-    layer_s = sorted(steps)[len(steps) // 2]
-    T = GRID[0] * GRID[1] * GRID[2]
+            samples.append(base)
+    samples.sort(key=lambda b: b["layer_seconds_extrapolated"])
+    base = samples[len(samples) // 2]
+    layer_s = base["layer_seconds_extrapolated"]
+    T = q.shape[1]
     value = dense_flops(T, HEADS, HEAD_DIM) / layer_s / 1e12
-    base["value"] = value
     line = dict(metric=METRIC, value=value, unit=UNIT, impl="reference", n_gpus=args.gpus, steps=args.steps,
                 warmup=args.warmup, ms_per_step=layer_s * 1e3, higher_is_better=True, scaling="strong",
-                vs_baseline=None, dtype="bf16", data="synthetic",
-                config=dict(workload="config1: one sparse attention layer, N=124992 (31x48x84), H=32, D=128, "
-                                     "block 128, topk 0.1, reweight summaries", extrapolated=True),
+                vs_baseline=None, dtype="bf16", data=DATA1,
+                config=config1_dict(1, ops_target_topk(T), T),
+                extrapolated=dict(layer_seconds=layer_s, sample_seconds_per_step=base["sample_seconds"],
+                                  attention_extrapolation_factor=base["attention_extrapolation_factor"]),
                 cpu_baseline=base, e2e=dict(value=value, unit=UNIT, h2d_bytes_per_step=0, d2h_bytes_per_step=0))
     emit(json.dumps(line), flush=True)
+
+
+def ops_target_topk(T: int) -> int:
+    qb = T // BLOCK
+    return min(max(1, round(TOPK_RATIO * qb)), qb)
 
 
 def run_ours(args) -> None:
@@ -296,25 +351,33 @@ def run_ours(args) -> None:
     h2d = sum(x.numel() * x.element_size() for x in (hq, hk, hv)) * world
     d2h = hout.numel() * hout.element_size() * world
 
-    dense_sdpa_ms = None
+    dense_sdpa_ms = dense_clocks = None
     if world == 1 and not args.no_dense:
         from torch.nn.attention import SDPBackend, sdpa_kernel
         qt, kt, vt = (x.transpose(1, 2) for x in (q, k, v))
         try:
             with sdpa_kernel(SDPBackend.CUDNN_ATTENTION):
-                torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
+                for _ in range(3):
+                    torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
                 torch.cuda.synchronize()
                 d0, d1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-                d0.record(stream)
-                for _ in range(2):
-                    torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
-                d1.record(stream)
-                torch.cuda.synchronize()
-                dense_sdpa_ms = d0.elapsed_time(d1) / 2
+                with ClockSampler(local_rank) as sdpa_clocks:
+                    d0.record(stream)
+                    for _ in range(args.dense_iters):
+                        torch.nn.functional.scaled_dot_product_attention(qt, kt, vt)
+                    d1.record(stream)
+                    torch.cuda.synchronize()
+                dense_sdpa_ms = d0.elapsed_time(d1) / args.dense_iters
+                dense_clocks = sdpa_clocks.summary()
         except RuntimeError as err:  # cuDNN backend unavailable
             dense_sdpa_ms = f"unavailable: {err}".splitlines()[0][:200]
+        del qt, kt, vt
 
     status = ops.read_device_status(dev)
+    cpu_inputs = None
+    if world == 1 and rank == 0 and not args.no_cpu_baseline:
+        cpu_inputs = tuple(x.cpu() for x in (q, k, v))
+    del hq, hk, hv, hout
     if rank == 0:
         peaks = load_peaks()
         flops_launch = sparse_flops(T, heads, HEAD_DIM, BLOCK, topk)
@@ -322,19 +385,16 @@ def run_ours(args) -> None:
         line = dict(
             metric=METRIC, value=value, unit=UNIT, n_gpus=world, steps=args.steps, warmup=args.warmup,
             ms_per_step=ms_per_step, higher_is_better=True, scaling="strong", vs_baseline=None, dtype="bf16",
-            data="synthetic (seeded 8-sinusoid + 0.3 N(0,1) Q/K/V, Q scaled by 1/sqrt(D))",
-            config=dict(workload="config1: one sparse attention layer, N=124992 (31x48x84), H=32, D=128, block 128, "
-                                 "topk 0.1 (98 of 976 blocks), reweight summaries + LSE correction, no reblock",
-                        global_batch=1, seq_len=T, heads=HEADS, head_dim=HEAD_DIM, block=BLOCK, topk=topk,
-                        parallelism=f"heads/{world}" if world > 1 else "single GPU",
-                        l2="inputs (3 x 1.02 GB) exceed the 126 MB L2; no flush between steps"),
+            data=DATA1, config=config1_dict(world, topk, T),
             ms_per_layer=ms_per_step, attention_kernel_ms=attn_ms,
             sparse_flops_per_layer=sparse_flops(T, HEADS, HEAD_DIM, BLOCK, topk),
             dense_equivalent_flops_per_layer=total_dense,
-            dense_cudnn_sdpa_ms=dense_sdpa_ms,
+            dense_cudnn_sdpa_ms=dense_sdpa_ms, dense_cudnn_sdpa_iters=args.dense_iters if dense_sdpa_ms else None,
+            dense_cudnn_sdpa_clocks=dense_clocks,
             speedup_vs_dense_sdpa=(dense_sdpa_ms / ms_per_step if isinstance(dense_sdpa_ms, float) else None),
             roofline=dict(bound="tensor", kernel="sparse_attention_sm100_kernel", achieved=achieved,
                           peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"],
+                          frac_of_sustained=achieved / peaks["bf16_sustained"],
                           traffic=ATTENTION_TRAFFIC_BYTES if (GRID, world) == ((31, 48, 84), 1) else None,
                           traffic_unit="bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
                           peak_source=peaks["source"],
@@ -347,12 +407,96 @@ def run_ours(args) -> None:
             clocks=clocks.summary(),
             device_status=status,
         )
-        if world == 1 and not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(sample_blocks=args.cpu_sample_blocks)
+    del q, k, v, out, workspace
+    torch.cuda.empty_cache()
+    dit = None if args.no_dit else dit_schedule(args, world, rank, local_rank, dev)
+    if rank == 0:
+        if dit is not None:
+            line["dit_stack"] = dit
+        if cpu_inputs is not None:
+            # one warm-up sample, then the median of three (host timings vary run to run)
+            runs = [cpu_layer_sample(*cpu_inputs, args.cpu_sample_blocks) for _ in range(4)][1:]
+            line["cpu_baseline"] = sorted(runs, key=lambda r: r["layer_seconds_extrapolated"])[1]
         emit(json.dumps(line), flush=True)
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
+
+
+def dit_schedule(args, world: int, rank: int, local_rank: int, dev, *, grid=None, heads: int = 32,
+                 spark_mode: str = "full", peer_exchange: bool = False) -> dict:
+    """BASELINE config 4 as the reference's sampling loop runs it: the 8-block synthetic DiT
+    at N = 245,952 for 19 evaluations (4 dense warm-up + 15 Spark, mode "full"), timed as one
+    region on every rank after one dense and two Spark warm-up evaluations; tokens are split
+    across the ranks for the pointwise stages and GEMMs and heads for attention (NCCL
+    all-to-all).  Returns s/it and the per-step and exchange times, each the max over ranks."""
+    import torch
+    import torch.distributed as dist
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.dit import DiTConfig, DiTStack
+    from spark_h3_b200.sharding import max_over_ranks
+
+    if grid is None:
+        grid = tuple(int(x) for x in args.dit_grid.split(",")) if args.dit_grid else (61, 48, 84)
+    cfg = DiTConfig(hidden=heads * 128, heads=heads, ffn=4 * heads * 128)
+    steps, dense_steps = 19, 4
+    stack = DiTStack(cfg, grid, device=dev, world=world, rank=rank, seed=0, spark_mode=spark_mode,
+                     topk_ratio=TOPK_RATIO, steps=steps, peer_exchange=peer_exchange)
+    exchange = ("q/k/v all-to-all by the QKV GEMM epilogue's stores to peer buffers (CUDA IPC over NVLink), output "
+                "all-to-all by NCCL" if stack.peer is not None else "NCCL all-to-all (q, k, v to heads; output back "
+                "to tokens)")
+    g = torch.Generator(device=dev).manual_seed(1000 + rank)
+    x = torch.randn(stack.local, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
+    stream = torch.cuda.current_stream(dev)
+
+    def barrier():
+        if world > 1:
+            dist.barrier(device_ids=[local_rank])
+        torch.cuda.synchronize()
+
+    stack.step(x, 999.0, dense=True)
+    stack.step(x, 990.0, dense=False)
+    stack.step(x, 980.0, dense=False)
+    barrier()
+    marks = [torch.cuda.Event(enable_timing=True) for _ in range(steps + 1)]
+    stack.exchange_events = [] if world > 1 else None
+    with ClockSampler(local_rank) as clocks:
+        barrier()
+        marks[0].record(stream)
+        for i in range(steps):
+            stack.step(x, 1000.0 * (1.0 - i / steps), dense=i < dense_steps)
+            marks[i + 1].record(stream)
+        barrier()
+    step_ms = [marks[i].elapsed_time(marks[i + 1]) for i in range(steps)]
+    total_ms = marks[0].elapsed_time(marks[steps])
+    per_step = 2 * cfg.blocks  # exchanges per evaluation: to heads, back to tokens, per block
+    events = stack.exchange_events or []
+    a2a_ms = sum(e0.elapsed_time(e1) for e0, e1 in events[dense_steps * per_step:]) / (steps - dense_steps)
+    dense_ms = sum(step_ms[:dense_steps]) / dense_steps
+    sparse_ms = sum(step_ms[dense_steps:]) / (steps - dense_steps)
+    total_ms, dense_ms, sparse_ms, a2a_ms = max_over_ranks([total_ms, dense_ms, sparse_ms, a2a_ms], device=dev)
+    status = ops.read_device_status(dev)
+    stack.close()
+    del stack, x
+    torch.cuda.empty_cache()
+    T = grid[0] * grid[1] * grid[2]
+    return dict(
+        metric="DiT step s/it (config 4: 8-block synthetic DiT, 19 steps = 4 dense + 15 Spark)",
+        value=total_ms / steps / 1e3, unit="s/it", higher_is_better=False, scaling="strong",
+        timed="one region of all 19 evaluations (CUDA events, barrier and synchronize on both sides, max over ranks)",
+        workload=(f"config4: {cfg.blocks} blocks, hidden {cfg.hidden}, {cfg.heads} heads x {cfg.head_dim}, FFN "
+                  f"{cfg.ffn} GELU, e4m3 linears, N={T} ({'x'.join(map(str, grid))}), Spark mode {spark_mode}, "
+                  f"topk {TOPK_RATIO}"),
+        parallelism=(f"tokens/{world} for the pointwise stages and GEMMs, heads/{world} for attention, {exchange}"
+                     if world > 1 else "single GPU"),
+        schedule_seconds=total_ms / 1e3, dense_step_ms=dense_ms, sparse_step_ms=sparse_ms,
+        all_to_all_ms_per_sparse_step=a2a_ms if world > 1 else 0.0,
+        all_to_all_share_of_sparse_step=(a2a_ms / sparse_ms) if world > 1 else 0.0,
+        all_to_all_bytes_per_layer=4 * T * cfg.heads * cfg.head_dim * 2 if world > 1 else 0,
+        note=("exchange time = CUDA events around the four all_to_all_single calls of each block, summed over "
+              "the 8 blocks; it includes waiting for the slowest rank"),
+        clocks=clocks.summary(), device_status=status)
 
 
 def _timed(fn, steps: int, warmup: int, stream) -> float:
@@ -373,7 +517,9 @@ def _timed(fn, steps: int, warmup: int, stream) -> float:
 
 def run_config2(args) -> None:
     """the full Spark mode (landmark-v2 reblock + Top-K + reweight) at
-    N = 245,952 on one GPU."""
+    N = 245,952 on one GPU, one JSON line per top-k ratio in {0.05, 0.1, 0.2} (BASELINE's
+    set; --topk-ratios to change it).  Each line carries the layer time, the attention
+    kernel alone on the reblocked Q/K/V with that ratio's route, and the reblock stages."""
     import torch
 
     from spark_h3_b200 import ops, reblock
@@ -387,24 +533,28 @@ def run_config2(args) -> None:
         raise SystemExit("--workload config2 runs on one GPU")
     grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else (61, 48, 84)
     heads, block = args.heads or 32, 64
+    ratios = [float(r) for r in args.topk_ratios.split(",")]
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     q, k, v = make_qkv(grid, heads, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, clustered=True)
     T = q.shape[1]
-    cfg = H3SparseAttentionConfig.spark(num_inference_steps=1000, mode="full", sol_route_topk_ratio=TOPK_RATIO)
-    controller = _Controller(cfg)
     ids = torch.arange(T)
     layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=grid, video_tokens=T, sequence_length=T,
                           video_positions=torch.zeros(T, 3, dtype=torch.long))
     stream = torch.cuda.current_stream(dev)
-    layer = lambda: spark_attention_bthd(controller, q, k, v, layout, 0)
+    layers = {}
     with ClockSampler(0) as clocks:
-        ms = _timed(layer, args.steps, args.warmup, stream)
+        for ratio in ratios:
+            cfg = H3SparseAttentionConfig.spark(num_inference_steps=1000, mode="full", sol_route_topk_ratio=ratio)
+            controller = _Controller(cfg)
+            layers[ratio] = _timed(lambda: spark_attention_bthd(controller, q, k, v, layout, 0), args.steps,
+                                   args.warmup, stream)
+    clock_summary = clocks.summary()
     if args.profile_only:
-        emit(json.dumps(dict(profile_case=True, workload="config2", grid=grid, heads=heads, ms_per_step=ms)),
-              flush=True)
+        emit(json.dumps(dict(profile_case=True, workload="config2", grid=grid, heads=heads, ms_per_step=layers)),
+             flush=True)
         return
-    # stage breakdown (same inputs, same stream)
+    # Stage breakdown (same inputs, same stream).
     samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype("int32")).to(dev)
     factors = reblock.metric_factors(q, k, samples)
     features = reblock.transform(q, k, factors, T)
@@ -414,35 +564,62 @@ def run_config2(args) -> None:
     tree_ms = _timed(lambda: plan.run(features), 3, 1, stream)
     reblock.transform(q, k, factors, T, out=plan.features_buffer(2 * heads))
     tree_graph_ms = _timed(lambda: plan.replay(2 * heads), 3, 1, stream)  # captured CUDA graph
+    del features
     qp, qi, kp, ki, _ = reblock.qk_block_permutations(q, k, T, grid)
     permute_ms = _timed(lambda: [ops.headwise_permute(t, p, T) for t, p in ((q, qp), (k, kp), (v, kp))], 3, 1,
                         stream)
-    status = ops.read_device_status(dev)
+    q2, k2, v2 = (ops.headwise_permute(t, p, T) for t, p in ((q, qp), (k, kp), (v, kp)))
+    del q, k, v
+    qc = ops.pool_queries(q2, block)
+    anchor = ops.query_anchor(qc, block, T // block, torch.bfloat16)
+    _, ak, av, lm = ops.pool_keys_summaries(k2, v2, anchor, block)
+    kc = ops.pool_keys_summaries(k2, None, None, block, want_summaries=False)[0]
+    out = torch.empty_like(q2)
     peaks = load_peaks()
     rows = 2 * heads
     transform_bytes = rows * T * HEAD_DIM * 2 * 2  # read Q or K rows, write the features
     nb = T // block
-    topk = ops.target_topk(TOPK_RATIO, nb)
-    line = dict(
-        metric=METRIC + " [config 2: full mode with reblock]", value=dense_flops(T, heads, HEAD_DIM) / (ms * 1e-3) / 1e12,
-        unit=UNIT, n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ms, higher_is_better=True,
-        scaling="strong", vs_baseline=None, dtype="bf16",
-        data="synthetic (seeded 8-sinusoid + clustered content: 64 N(0,1) centroids on a 4x4x4 region partition, "
-             "0.25 N(0,1) noise)",
-        config=dict(workload="config2: mode full (landmark-v2 reblock, Top-K 0.1, reweight), N=245952 (61x48x84), "
-                             "H=32, D=128, block 64", seq_len=T, heads=heads, block=block, topk=topk,
-                    l2="inputs (3 x 2.0 GB) exceed the 126 MB L2; no flush between steps"),
-        ms_per_layer=ms,
-        stages_ms=dict(reblock_metric=metric_ms, reblock_transform=transform_ms, reblock_tree=tree_ms,
-                       reblock_tree_graph=tree_graph_ms,
-                       qkv_permutes=permute_ms),
-        roofline=dict(bound="hbm", kernel="reblock_transform_kernel", achieved=transform_bytes / (transform_ms * 1e-3) / 1e9,
-                      peak=peaks["hbm"], unit="GB/s",
-                      frac=transform_bytes / (transform_ms * 1e-3) / 1e9 / peaks["hbm"], traffic=None,
-                      peak_source=peaks["source"].replace("bf16 sustained", "HBM copy"),
-                      note="algorithmic bytes: 64 rows x N x 128 x 2 B read + the same written"),
-        clocks=clocks.summary(), device_status=status)
-    emit(json.dumps(line), flush=True)
+    stages = dict(reblock_metric=metric_ms, reblock_transform=transform_ms, reblock_tree=tree_ms,
+                  reblock_tree_graph=tree_graph_ms, qkv_permutes=permute_ms)
+    transform_roofline = dict(
+        bound="hbm", kernel="reblock_transform_kernel", achieved=transform_bytes / (transform_ms * 1e-3) / 1e9,
+        peak=peaks["hbm"], unit="GB/s", frac=transform_bytes / (transform_ms * 1e-3) / 1e9 / peaks["hbm"],
+        traffic=None, peak_source="MEASURED_PEAKS.json hbm_gbs (copy bandwidth, measured)",
+        note="algorithmic bytes: 64 rows x N x 128 x 2 B read + the same written")
+    for ratio in ratios:
+        topk = ops.target_topk(ratio, nb)
+        packed, _ = ops.route_topk(qc, kc, nb, nb, topk, want_indices=False)
+        attn = lambda: ops.sparse_attention(q2, k2, v2, block, packed, ak, av, lm, query_tokens=nb * block,
+                                            sink_first=nb, sink_last=nb, out=out)
+        with ClockSampler(0) as attn_clocks:
+            attn_ms = _timed(attn, args.steps, args.warmup, stream)
+        flops = sparse_flops(T, heads, HEAD_DIM, block, topk)
+        achieved = flops / (attn_ms * 1e-3) / 1e12
+        ms = layers[ratio]
+        line = dict(
+            metric=METRIC + " [config 2: full mode with reblock]",
+            value=dense_flops(T, heads, HEAD_DIM) / (ms * 1e-3) / 1e12, unit=UNIT, n_gpus=1, steps=args.steps,
+            warmup=args.warmup, ms_per_step=ms, higher_is_better=True, scaling="strong", vs_baseline=None,
+            dtype="bf16",
+            data="synthetic (seeded 8-sinusoid + clustered content: 64 N(0,1) centroids on a 4x4x4 region "
+                 "partition, 0.25 N(0,1) noise)",
+            config=dict(workload=f"config2: mode full (landmark-v2 reblock, Top-K {ratio}, reweight), N={T} "
+                                 f"({'x'.join(map(str, grid))}), H={heads}, D=128, block 64",
+                        seq_len=T, heads=heads, block=block, topk_ratio=ratio, topk=topk,
+                        l2="inputs (3 x 2.0 GB) exceed the 126 MB L2; no flush between steps"),
+            ms_per_layer=ms, attention_kernel_ms=attn_ms, sparse_flops_per_layer=flops,
+            dense_equivalent_flops_per_layer=dense_flops(T, heads, HEAD_DIM),
+            stages_ms=stages,
+            roofline=dict(bound="tensor", kernel="sparse_attention_sm100_kernel", achieved=achieved,
+                          peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"],
+                          frac_of_sustained=achieved / peaks["bf16_sustained"], traffic=None,
+                          peak_source=peaks["source"],
+                          note="sparse FLOPs 4 D (k 64 + (n - k)) per routed query row; the kernel's 128-row tiles "
+                               "pair two 64-row query blocks and compute the union of their key sets"),
+            reblock_transform_roofline=transform_roofline,
+            clocks=clock_summary, attention_clocks=attn_clocks.summary(),
+            device_status=ops.read_device_status(dev))
+        emit(json.dumps(line), flush=True)
 
 
 def run_tails(args) -> None:
@@ -573,15 +750,10 @@ def quiet_nccl() -> None:
 
 
 def run_config4(args) -> None:
-    """the synthetic DiT block stack (8 blocks, hidden 4096, 32 x 128 heads,
-    GELU FFN 16384, e4m3 linears) at N = 245,952 tokens; 19 denoise steps = 4 dense warmup +
-    15 Spark steps.  Tokens are split across ranks for the pointwise work and the GEMMs, heads
-    for attention (NCCL all-to-all).  The timed dense and sparse steps give s/it of the schedule."""
+    """BASELINE config 4 on its own: the 19-step DiT schedule of dit_schedule, one JSON line
+    with s/it as the value (torchrun for N > 1)."""
     import torch
     import torch.distributed as dist
-
-    from spark_h3_b200 import ops
-    from spark_h3_b200.dit import DiTConfig, DiTStack
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
@@ -595,60 +767,16 @@ def run_config4(args) -> None:
         quiet_nccl()
         dist.init_process_group("nccl", timeout=timedelta(seconds=300), device_id=dev)
     grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else (61, 48, 84)
-    heads = args.heads or 32
-    cfg = DiTConfig(hidden=heads * 128, heads=heads, ffn=4 * heads * 128)
-    stack = DiTStack(cfg, grid, device=dev, world=world, rank=rank, seed=0, spark_mode=args.spark_mode,
-                     topk_ratio=TOPK_RATIO, peer_exchange=args.peer_exchange)
-    g = torch.Generator(device=dev).manual_seed(1000 + rank)
-    x = torch.randn(stack.local, cfg.hidden, device=dev, generator=g).to(torch.bfloat16)
-    stream = torch.cuda.current_stream(dev)
-
-    def barrier():
-        if world > 1:
-            dist.barrier(device_ids=[local_rank])
-        torch.cuda.synchronize()
-
-    def timed(dense: bool, n: int) -> float:
-        barrier()
-        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        e0.record(stream)
-        for i in range(n):
-            stack.step(x, 900.0 - 50.0 * i, dense=dense)
-        e1.record(stream)
-        barrier()
-        return e0.elapsed_time(e1) / n
-
-    stack.step(x, 999.0, dense=True)  # warm-up: one dense and W - 1 sparse evaluations
-    for i in range(max(1, args.warmup - 1)):
-        stack.step(x, 950.0 - i, dense=False)
-    with ClockSampler(local_rank) as clocks:
-        sparse_ms = timed(False, args.steps)
-        dense_ms = timed(True, 1)
-    from spark_h3_b200.sharding import max_over_ranks
-    sparse_ms, dense_ms = max_over_ranks([sparse_ms, dense_ms], device=dev)
-    status = ops.read_device_status(dev)
-    schedule_s = (4 * dense_ms + 15 * sparse_ms) / 19 / 1e3
+    dit = dit_schedule(args, world, rank, local_rank, dev, grid=grid, heads=args.heads or 32,
+                       spark_mode=args.spark_mode, peer_exchange=args.peer_exchange)
     if rank == 0:
-        T = grid[0] * grid[1] * grid[2]
-        a2a = 4 * T * cfg.heads * cfg.head_dim * 2  # q, k, v out and o back, bytes per layer (whole job)
-        line = dict(
-            metric="DiT step s/it (config 4: 8-block synthetic DiT, 19 steps = 4 dense + 15 Spark)",
-            value=schedule_s, unit="s/it", n_gpus=world, steps=args.steps, warmup=args.warmup,
-            ms_per_step=schedule_s * 1e3, higher_is_better=False, scaling="strong", vs_baseline=None,
-            dtype="e4m3 linears, bf16 activations and attention",
-            data="synthetic: latent tokens N(0,1), weights N(0,0.02), seeded",
-            config=dict(workload=f"config4: {cfg.blocks} blocks, hidden {cfg.hidden}, {heads} heads x 128, FFN "
-                                 f"{cfg.ffn} GELU, N={T} ({'x'.join(map(str, grid))}), Spark mode "
-                                 f"{args.spark_mode} topk {TOPK_RATIO}",
-                        parallelism=(f"tokens/{world} for pointwise + GEMMs, heads/{world} for attention; "
-                                     + ("q/k/v all-to-all by the QKV GEMM epilogue's stores to peer buffers "
-                                        "(CUDA IPC over NVLink), output all-to-all by NCCL" if stack.peer is not None
-                                        else "NCCL all-to-all") if world > 1 else "single GPU")),
-            sparse_step_ms=sparse_ms, dense_step_ms=dense_ms,
-            all_to_all_bytes_per_layer=a2a if world > 1 else 0,
-            clocks=clocks.summary(), device_status=status)
+        line = dict(metric=dit.pop("metric"), value=dit.pop("value"), unit=dit.pop("unit"), n_gpus=world,
+                    steps=19, warmup=3, ms_per_step=dit["schedule_seconds"] * 1e3 / 19,
+                    higher_is_better=dit.pop("higher_is_better"), scaling=dit.pop("scaling"), vs_baseline=None,
+                    dtype="e4m3 linears, bf16 activations and attention",
+                    data="synthetic: latent tokens N(0,1), weights N(0,0.02), seeded",
+                    config=dict(workload=dit.pop("workload"), parallelism=dit.pop("parallelism")), **dit)
         emit(json.dumps(line), flush=True)
-    stack.close()
     if world > 1:
         dist.barrier(device_ids=[local_rank])
         dist.destroy_process_group()
@@ -662,11 +790,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=("ours", "reference"), default="ours")
     ap.add_argument("--no-dense", action="store_true", help="skip the dense cuDNN SDPA comparison")
+    ap.add_argument("--dense-iters", type=int, default=10, help="timed iterations of the dense cuDNN SDPA")
+    ap.add_argument("--no-dit", action="store_true", help="skip the config-4 DiT schedule (dit_stack)")
+    ap.add_argument("--dit-grid", type=str, default=None,
+                    help="T,H,W token grid of the dit_stack schedule (default 61,48,84)")
     ap.add_argument("--e2e-chunks", type=int, default=0,
                     help="head chunks of the end-to-end streamed layer (0: 16 or the largest that divides)")
     ap.add_argument("--no-cpu-baseline", action="store_true", help="skip the CPU oracle baseline")
-    ap.add_argument("--cpu-sample-blocks", type=int, default=96,
-                    help="query blocks of the one-head CPU attention sample behind cpu_baseline")
+    ap.add_argument("--cpu-sample-blocks", type=int, default=16,
+                    help="query blocks of the one-head CPU attention sample (cpu_baseline and --impl reference)")
     ap.add_argument("--grid", type=str, default=None,
                     help="T,H,W token grid for a smaller profiling case (default 31,48,84)")
     ap.add_argument("--heads", type=int, default=None, help="head count for a smaller profiling case")
@@ -680,8 +812,8 @@ def main():
                     help="config 4: the QKV producer's epilogue stores q/k/v to the owners' buffers over NVLink "
                          "instead of the NCCL all-to-all")
     ap.add_argument("--fp8-rows", type=int, default=124992, help="token rows M of the fp8 workload")
-    ap.add_argument("--reference-sample-blocks", type=int, default=16,
-                    help="query blocks of the one-head CPU attention sample of each --impl reference step")
+    ap.add_argument("--topk-ratios", type=str, default="0.05,0.1,0.2",
+                    help="config 2: the top-k ratios, one JSON line each")
     args = ap.parse_args()
     args.warmup = max(args.warmup, 3)  # at least three untimed warm-up steps
     global GRID, HEADS, PROFILE_ONLY

@@ -420,17 +420,21 @@ def spark_layer(q: Tensor, k: Tensor, v: Tensor, *, block: int, topk_ratio: floa
     nb = -(-T // block)
     if tail_mode == "dense":
         query_tokens = (video // block) * block
+    elif tail_mode == "legacy_full":  # spark_integration.py:925-933, 1221-1262
+        query_tokens = -(-video // block) * block
+        if query_tokens > T:
+            raise NotImplementedError("the final query block must be filled by the sequence")
     elif tail_mode == "pad":
         query_tokens = -(-video // block) * block
         if query_tokens > T:
             raise ValueError("the packed suffix is too short to pad the final video query block")
     else:
-        raise ValueError("tail_mode must be 'dense' or 'pad'")
+        raise ValueError("tail_mode must be 'dense', 'pad' or 'legacy_full'")
     query_blocks = query_tokens // block
     candidates = video // block
     sink_first = video // block
     sink_last = -(-T // block) if T > video else sink_first
-    qc = block_means(padded_tail(q, video, query_tokens, block), block)
+    qc = block_means(padded_tail(q, video, query_tokens, block) if tail_mode == "pad" else q, block)
     kc = key_means(k, block)
     a = anchor(qc, block, candidates, anchor_dtype or q.dtype)
     sc = scores(qc, kc, query_blocks, candidates)

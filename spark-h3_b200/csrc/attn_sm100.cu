@@ -3,8 +3,8 @@
 // One CTA per (128-row query tile, head, batch).  Roles (384 threads):
 //   warps 0-3  softmax group 0: row r = TMEM lane r, key columns 0-63 of every tile
 //   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
-//   warp 8     TMA producer of Q and the K (or AK summary) granules
-//   warp 9     TMA producer of the V (or AV summary) granules
+//   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages (2 on long sequences)
+//   warp 9     TMA producer of the V (or AV summary) tiles, 2 stages
 //   warp 10    tcgen05 issuer of S = Q K^T (one 128 x 64 product per group); owns TMEM
 //   warp 11    tcgen05 issuer of O += P V (one per group)
 // Issuing one tcgen05.mma occupies its thread for about as long as a third of the MMA's
@@ -26,10 +26,6 @@
 // softmax group g handles granule slot g, so its visibility is one flag per row half.
 // Summary tiles cover 128 summary entries (one per key block); an entry is visible to
 // a half when its block is not exact for that half.
-// K and V are staged per granule (64 keys x 128 dims, 16 KB), in two rings of their own
-// depths: granule slot g of every tile is read by group g's products only, so each stage is
-// released as soon as that one product completes, and the V ring can run further ahead than
-// whole-tile stages would allow in the same shared memory.
 #include "common.cuh"
 #include "attn_common.cuh"
 #include "sm100_ptx.cuh"
@@ -58,25 +54,13 @@ constexpr int kProducerWarp = 8;   // Q and K
 constexpr int kProducerVWarp = 9;  // V
 constexpr int kMmaWarp = 10;       // S issuer
 constexpr int kPvWarp = 11;        // P.V issuer
-// Ring depths in 64-key granules.  Long sequences, whose per-sequence tables crowd shared
-// memory, fall back to 5 + 5 and then 4 + 4 granules (the footprint of the earlier whole-tile
-// rings, so the longest accepted sequence is unchanged).
-#ifndef SB_ATTN_K_GRANULES
-#define SB_ATTN_K_GRANULES 6
-#endif
-#ifndef SB_ATTN_V_GRANULES
-#define SB_ATTN_V_GRANULES 5
-#endif
-constexpr int kPrefKGran = SB_ATTN_K_GRANULES;
-constexpr int kPrefVGran = SB_ATTN_V_GRANULES;
-constexpr int kMaxGran = 8;  // barrier slots per ring
-static_assert(kPrefKGran >= 4 && kPrefKGran <= kMaxGran && kPrefVGran >= 4 && kPrefVGran <= kMaxGran,
-              "granule ring depths must lie in [4, 8]");
+constexpr int kKStages = 3;  // K ring depth when it fits; 2 on long sequences (below)
+constexpr int kVStages = 2;
 constexpr uint32_t kSmemLimit = 227 * 1024;
-constexpr int kTileBytes = 128 * 128 * 2;  // the Q tile: 128 rows x 128 dims, bf16
+static_assert(kVStages == 2, "the P.V issue and the rescale wait index V stages by tile parity");
+constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 bf16 operand tile
 constexpr int kHalfBytes = 128 * 64 * 2;   // one 64-column half of it
 constexpr int kBoxBytes = 64 * 64 * 2;     // one TMA box (64 columns x 64 rows)
-constexpr int kGranBytes = 2 * kBoxBytes;  // one K or V granule stage: 64 keys x 128 dims
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kColOA = 256;
 constexpr uint32_t kColOB = 384;
@@ -92,8 +76,8 @@ constexpr int kPolyEvery = SB_POLY_EVERY;
 
 struct __align__(8) Control {
   uint64_t bar_q_full;
-  uint64_t bar_k_full[kMaxGran], bar_k_empty[kMaxGran];
-  uint64_t bar_v_full[kMaxGran], bar_v_empty[kMaxGran];
+  uint64_t bar_k_full[kKStages], bar_k_empty[kKStages];
+  uint64_t bar_v_full[kVStages], bar_v_empty[kVStages];
   uint64_t bar_s_full[2][2];   // [group][buffer]: the group's S columns have landed
   uint64_t bar_p_full[2][2];   // [group][buffer]: the group's P is in TMEM (one arrival per warp)
   uint64_t bar_pv_done[2][2];  // [group][buffer]: the group's P.V has completed
@@ -112,22 +96,20 @@ struct SmemLayout {
   uint32_t q, k, v;  // byte offsets from the 1024-aligned base (stages are consecutive)
   uint32_t ctrl, ebits, ubits, lm, glist;
   uint32_t total;
-  int k_gran, v_gran;  // ring depths in granule stages
+  int k_stages;
 };
 
 // The per-sequence tables (route words, summary log-masses, granule list) grow with T; when
-// the preferred rings no longer fit beside them, shallower ones are used.  At the last
-// fallback (4 + 4 granules) the longest accepted sequence is about 660k tokens with 64-key
-// blocks and about 990k with 128-key blocks.
-__host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int words_gran, int nb_pad, int k_gran,
-                                                         int v_gran) {
+// three K stages no longer fit beside them the ring drops to two.  With 64-key blocks that
+// moves the longest accepted sequence from about 330k to about 660k tokens (128-key blocks:
+// about 500k to 990k).
+__host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int words_gran, int nb_pad, int k_stages) {
   SmemLayout L;
-  L.k_gran = k_gran;
-  L.v_gran = v_gran;
+  L.k_stages = k_stages;
   L.q = 0;
   L.k = kTileBytes;
-  L.v = L.k + k_gran * kGranBytes;
-  L.ctrl = L.v + v_gran * kGranBytes;
+  L.v = L.k + k_stages * kTileBytes;
+  L.ctrl = L.v + kVStages * kTileBytes;
   L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);  // Control is small
   L.ubits = L.ebits + (uint32_t)((2 * words_blk * 4 + 15) / 16 * 16);  // every region 16-byte aligned
   L.lm = L.ubits + (uint32_t)((words_gran * 4 + 15) / 16 * 16);
@@ -137,11 +119,8 @@ __host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int word
 }
 
 __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran, int nb_pad) {
-  SmemLayout L = smem_layout_stages(words_blk, words_gran, nb_pad, kPrefKGran, kPrefVGran);
-  if (L.total <= kSmemLimit) return L;
-  L = smem_layout_stages(words_blk, words_gran, nb_pad, 5, 5);
-  if (L.total <= kSmemLimit) return L;
-  return smem_layout_stages(words_blk, words_gran, nb_pad, 4, 4);
+  const SmemLayout L = smem_layout_stages(words_blk, words_gran, nb_pad, kKStages);
+  return L.total <= kSmemLimit ? L : smem_layout_stages(words_blk, words_gran, nb_pad, 2);
 }
 
 // 2^x on the FMA/ALU pipes (offloads the MUFU unit): round-to-nearest range reduction
@@ -216,11 +195,11 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
     mbar_init(smem_u32(&C.bar_q_full), 1);
-    for (int s = 0; s < L.k_gran; ++s) {
+    for (int s = 0; s < L.k_stages; ++s) {
       mbar_init(smem_u32(&C.bar_k_full[s]), 1);
       mbar_init(smem_u32(&C.bar_k_empty[s]), 1);
     }
-    for (int s = 0; s < L.v_gran; ++s) {
+    for (int s = 0; s < kVStages; ++s) {
       mbar_init(smem_u32(&C.bar_v_full[s]), 1);
       mbar_init(smem_u32(&C.bar_v_empty[s]), 1);
     }
@@ -333,13 +312,12 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
 
   if (warp == kProducerWarp || warp == kProducerVWarp) {
     // ----------------------------------------------------------- producers
-    // Warp 8 streams Q and the K side, warp 9 the V side; both walk the same granule list
-    // (unit u = 2 j + slot: slot `slot` of tile j), so a slow P.V never delays the next K.
-    // Q streams through L2 once (evict first); K, V and the summaries are read by every
-    // query tile of the head (evict last).
+    // Warp 8 streams Q and the K side, warp 9 the V side; both walk the same tile list,
+    // so a slow P.V never delays the next K tile.  Q streams through L2 once (evict first);
+    // K, V and the summaries are read again by every query tile of the head (evict last).
     if (lane == 0) {
       const bool is_k = warp == kProducerWarp;
-      const int stages = is_k ? L.k_gran : L.v_gran;
+      const int stages = is_k ? L.k_stages : kVStages;
       const CUtensorMap* exact_map = is_k ? &tm_k : &tm_v;
       const CUtensorMap* summ_map = is_k ? &tm_ak : &tm_av;
       const uint32_t s_base = is_k ? sK0 : sV0;
@@ -348,36 +326,38 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       const uint32_t bq = smem_u32(&C.bar_q_full);
       const uint64_t keep = l2_policy_evict_last();
       if (is_k) {
-        const uint64_t stream = l2_policy_evict_first();
+        const uint64_t once = l2_policy_evict_first();
         mbar_arrive_expect_tx(bq, kTileBytes);
         for (int dh = 0; dh < 2; ++dh)
           for (int rh = 0; rh < 2; ++rh)
             tma_load_3d_hint(sQ + dh * kHalfBytes + rh * kBoxBytes, &tm_q, bq, h * 128 + 64 * dh, row0 + 64 * rh, b,
-                             stream);
+                             once);
       }
       const int n_gran = C.exact_granules;
-      int armed[kMaxGran] = {};
+      int armed[kKStages > kVStages ? kKStages : kVStages] = {};
       int s = 0, use = 0;  // stage and how many times it has been filled before
-      for (int u = 0; u < 2 * total_tiles; ++u) {
-        const int j = u >> 1, slot = u & 1;
+      for (int j = 0; j < total_tiles; ++j) {
+        int g0 = 0, g1 = 0;
         const bool exact = j < exact_tiles;
-        int g = 0;
         if (exact) {
-          g = glist[2 * j];
-          if (slot && 2 * j + 1 < n_gran) g = glist[2 * j + 1];  // an odd last granule fills both slots
+          g0 = glist[2 * j];
+          g1 = 2 * j + 1 < n_gran ? (int)glist[2 * j + 1] : g0;  // an odd last granule fills both slots
         }
         const int cc = j - exact_tiles;
         const uint32_t bar = smem_u32(&full[s]);
         if (!mbar_wait(smem_u32(&empty[s]), (uint32_t)((use & 1) ^ 1), abort_flag, p.status, is_k ? 101 : 102)) break;
-        mbar_arrive_expect_tx(bar, kGranBytes);
-        SB_TRACE_POINT(trace && slot == 0, is_k ? 0 : 1, j);
+        mbar_arrive_expect_tx(bar, kTileBytes);
+        SB_TRACE_POINT(trace, is_k ? 0 : 1, j);
         ++armed[s];
-        const uint32_t st = s_base + s * kGranBytes;
-        for (int dh = 0; dh < 2; ++dh) {
-          if (exact)
-            tma_load_3d_hint(st + dh * kBoxBytes, exact_map, bar, h * 128 + 64 * dh, g * 64, b, keep);
-          else
-            tma_load_3d_hint(st + dh * kBoxBytes, summ_map, bar, 64 * dh, cc * 128 + 64 * slot, b * p.H + h, keep);
+        const uint32_t st = s_base + s * kTileBytes;
+        for (int slot = 0; slot < 2; ++slot) {
+          for (int dh = 0; dh < 2; ++dh) {
+            const uint32_t dst = st + dh * kHalfBytes + slot * kBoxBytes;
+            if (exact)
+              tma_load_3d_hint(dst, exact_map, bar, h * 128 + 64 * dh, (slot ? g1 : g0) * 64, b, keep);
+            else
+              tma_load_3d_hint(dst, summ_map, bar, 64 * dh, cc * 128 + 64 * slot, b * p.H + h, keep);
+          }
         }
         if (++s == stages) {
           s = 0;
@@ -403,13 +383,10 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       int ks = 0, kuse = 0;
       for (int j = 0; ok && j < total_tiles; ++j) {
         const int s = j & 1;
-        for (int g = 0; g < 2; ++g) {
-          // Group g's granule of tile j is K unit 2 j + g.
-          if (!mbar_wait(smem_u32(&C.bar_k_full[ks]), (uint32_t)(kuse & 1), abort_flag, p.status, 204)) {
-            ok = false;
-            break;
-          }
-          if (g == 0) SB_TRACE_POINT(trace, 2, j);
+        if (!mbar_wait(smem_u32(&C.bar_k_full[ks]), (uint32_t)(kuse & 1), abort_flag, p.status, 204)) break;
+        SB_TRACE_POINT(trace, 2, j);
+        const uint64_t kdesc = kdesc0 + (uint64_t)((ks * kTileBytes) >> 4);
+        for (int g = 0; ok && g < 2; ++g) {
           // The group's S columns of buffer s still hold its P of tile j-2 until that P.V
           // completes.  The barrier cannot run two phases ahead: P.V of tile j needs S_j.
           if (j >= 2 && !mbar_wait(smem_u32(&C.bar_pv_done[g][s]), (uint32_t)(((j - 2) >> 1) & 1), abort_flag,
@@ -419,22 +396,21 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           }
           if (g == 0) SB_TRACE_POINT(trace, 12, j);
           tc_fence_after();
-          const uint64_t kdesc = kdesc0 + (uint64_t)((ks * kGranBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
-            const uint64_t koff = (uint64_t)(((kk >> 2) * kBoxBytes + (kk & 3) * 32) >> 4);
-            const uint64_t qoff = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
-            mma_ss(tmem + s * 128 + 64 * g, qdesc0 + qoff, kdesc + koff, idesc_qk, kk > 0 ? 1u : 0u);
+            const uint64_t off = (uint64_t)(((kk >> 2) * kHalfBytes + (kk & 3) * 32) >> 4);
+            mma_ss(tmem + s * 128 + 64 * g, qdesc0 + off, kdesc + off + (uint64_t)((g * kBoxBytes) >> 4), idesc_qk,
+                   kk > 0 ? 1u : 0u);
           }
           tc_commit(smem_u32(&C.bar_s_full[g][s]));
-          tc_commit(smem_u32(&C.bar_k_empty[ks]));
-          if (++ks == L.k_gran) {
-            ks = 0;
-            ++kuse;
-          }
         }
         if (!ok) break;
         SB_TRACE_POINT(trace, 3, j);
+        tc_commit(smem_u32(&C.bar_k_empty[ks]));
+        if (++ks == L.k_stages) {
+          ks = 0;
+          ++kuse;
+        }
       }
       tc_commit(smem_u32(&C.bar_s_final));
     }
@@ -445,36 +421,28 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     // commit after both releases the V stage.
     if (lane == 0) {
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, true);
-      // V granule stages are MN-major B operands: 64 keys (K) x 128 dims (N) as two
-      // 64-column boxes kBoxBytes apart (the descriptor's leading byte offset).
-      const uint64_t vdesc0 = smem_desc_sw128(sV0, kBoxBytes, 1024);
+      const uint64_t vdesc0 = smem_desc_sw128(sV0, kHalfBytes, 1024);
       bool ok = true;
-      int vs = 0, vuse = 0;
       for (int i = 0; ok && i < total_tiles; ++i) {
-        const int s = i & 1;  // S/P buffer (two in TMEM)
+        const int s = i & 1;  // S/P buffer (two in TMEM) and V stage (kVStages == 2)
         const uint32_t par = (i >> 1) & 1;
+        const uint64_t vdesc = vdesc0 + (uint64_t)((s * kTileBytes) >> 4);
+        if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) break;
         for (int g = 0; g < 2; ++g) {
-          // Group g's granule of tile i is V unit 2 i + g.
-          if (!mbar_wait(smem_u32(&C.bar_v_full[vs]), (uint32_t)(vuse & 1), abort_flag, p.status, 203) ||
-              !mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) {
+          if (!mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) {
             ok = false;
             break;
           }
           if (g == 0) SB_TRACE_POINT(trace, 4, i);
           tc_fence_after();
-          const uint64_t vdesc = vdesc0 + (uint64_t)((vs * kGranBytes) >> 4);
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
             mma_ts(tmem + (g ? kColOB : kColOA), tmem + s * 128 + 64 * g + kk * 8,
-                   vdesc + (uint64_t)((kk * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
+                   vdesc + (uint64_t)(((4 * g + kk) * 2048) >> 4), idesc_pv, (i > 0 || kk > 0) ? 1u : 0u);
           tc_commit(smem_u32(&C.bar_pv_done[g][s]));
-          tc_commit(smem_u32(&C.bar_v_empty[vs]));
-          if (++vs == L.v_gran) {
-            vs = 0;
-            ++vuse;
-          }
         }
         if (!ok) break;
+        tc_commit(smem_u32(&C.bar_v_empty[s]));
         SB_TRACE_POINT(trace, 5, i);
       }
       tc_commit(smem_u32(&C.bar_o_final));

@@ -402,8 +402,10 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
         }
         if (row_ok && nc < p.N) {
           if (nc + 32 <= p.N && (p.N % 8) == 0) {
+            // The output is written once: evict-first keeps the A and B panels in L2.
+            const uint64_t once = l2_evict_first_policy();
 #pragma unroll
-            for (int v = 0; v < 4; ++v) store8(out_row + nc + 8 * v, f + 8 * v);
+            for (int v = 0; v < 4; ++v) store8_hint(out_row + nc + 8 * v, f + 8 * v, once);
           } else {
 #pragma unroll
             for (int i = 0; i < 32; ++i)

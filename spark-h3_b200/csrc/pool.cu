@@ -268,6 +268,203 @@ pool_keys_summaries_kernel(const T* __restrict__ k, const T* __restrict__ v,
   }
 }
 
+
+// bf16 K/V: one CTA per (key block, head, batch entry).  The block's K and V rows of the
+// head are staged in shared memory by 16-byte cp.async copies, so each is read from HBM
+// exactly once (the all-heads kernel above re-reads K for its weighted sums); the key
+// means (canonical order), the anchor logits, the block softmax and the weighted means
+// then run out of shared memory.  Three CTAs fit an SM, so one CTA's copies overlap
+// another's arithmetic.  Heads are the fastest grid index (x = key block * H + head), so
+// the CTAs in flight read whole token rows of consecutive blocks.
+constexpr int kHeadThreads = 256;
+
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
+               "l"(gmem)
+               : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
+
+template <int D, int BLOCK>
+struct HeadSmem {
+  static constexpr int kRowGroups = kHeadThreads / D;  // threads per column
+  static constexpr size_t kTile = (size_t)BLOCK * D * sizeof(__nv_bfloat16);
+  static constexpr size_t kBytes = 2 * kTile + BLOCK * sizeof(float) + 2 * kHeadThreads * sizeof(float) +
+                                   D * sizeof(float) + 64;
+};
+
+template <typename TA, int D, int BLOCK>
+__global__ void __launch_bounds__(kHeadThreads)
+kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat16* __restrict__ v,
+                         const TA* __restrict__ anchor, int T_, int H, int weighted_kv, int mass_bias, int numerics,
+                         __nv_bfloat16* __restrict__ kc, __nv_bfloat16* __restrict__ ak,
+                         __nv_bfloat16* __restrict__ av, float* __restrict__ lm) {
+  using S = HeadSmem<D, BLOCK>;
+  constexpr int CH = D * 2 / 16;  // 16-byte chunks per row
+  constexpr int RG = S::kRowGroups;
+  extern __shared__ __align__(16) uint8_t head_smem[];
+  __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(head_smem);
+  __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(head_smem + S::kTile);
+  float* plog = reinterpret_cast<float*>(head_smem + 2 * S::kTile);  // [BLOCK]
+  float* part_k = plog + BLOCK;                                     // [RG][D]
+  float* part_v = part_k + kHeadThreads;                            // [RG][D]
+  float* a_s = part_v + kHeadThreads;                               // [D] anchor
+  float* stat = a_s + D;                                            // max, den, 8 warp partials
+
+  const int kb = blockIdx.x / H, h = blockIdx.x % H, b = blockIdx.y;
+  const int NB = ceil_div(T_, BLOCK);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  const int row0 = kb * BLOCK;
+  const int rows = min(BLOCK, T_ - row0);
+  const bool want_sum = (ak != nullptr || av != nullptr || lm != nullptr);
+  const bool need_logits = want_sum && (weighted_kv || mass_bias);
+  const float scale = rsqrtf((float)D);
+  const float scale_log2 = scale * kLog2e;
+  const int64_t HD = (int64_t)H * D;
+  const __nv_bfloat16* kbase = k + ((int64_t)b * T_ + row0) * HD + (int64_t)h * D;
+
+  for (int i = tid; i < rows * CH; i += kHeadThreads) {
+    const int r = i / CH, c = i % CH;
+    cp_async16(ks + r * D + c * 8, kbase + r * HD + c * 8);
+  }
+  cp_async_commit();
+  if (want_sum) {
+    const __nv_bfloat16* vbase = v + ((int64_t)b * T_ + row0) * HD + (int64_t)h * D;
+    for (int i = tid; i < rows * CH; i += kHeadThreads) {
+      const int r = i / CH, c = i % CH;
+      cp_async16(vs + r * D + c * 8, vbase + r * HD + c * 8);
+    }
+  }
+  cp_async_commit();
+  cp_async_wait<1>();  // K has landed; V may still be in flight
+  __syncthreads();
+
+  const int col = tid % D, grp = tid / D;
+  // Key means: row group g sums 64-row sub-block g in token order; the sub-block sums are
+  // then added in order and divided by the rows present (the canonical order).
+  const int nsub = (rows + 63) / 64;
+  if (grp < nsub) {
+    float acc = 0.f;
+    const int r1 = min(rows, 64 * grp + 64);
+    for (int r = 64 * grp; r < r1; ++r) acc = __fadd_rn(acc, __bfloat162float(ks[r * D + col]));
+    part_k[grp * D + col] = acc;
+  }
+  // Anchor logits: PER = 256 / BLOCK threads per row, each a dot over D / PER columns in
+  // 16-byte chunks.  Chunk order is rotated by (thread & 7), so the eight threads of a
+  // shared-memory phase read eight different bank groups; the anchor sits in shared memory.
+  constexpr int PER = kHeadThreads / BLOCK;  // 2 (128-row blocks) or 4 (64-row blocks)
+  constexpr int CPT = D / 8 / PER;          // 16-byte chunks per thread
+  if (need_logits) {
+    if (tid < D) a_s[tid] = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + tid]);
+    __syncthreads();
+    const int r = tid / PER, part = tid % PER;
+    float d0 = 0.f, d1 = 0.f;
+    if (r < rows) {
+#pragma unroll
+      for (int j = 0; j < CPT; ++j) {
+        const int chunk = part * CPT + ((j + tid) & (CPT - 1));
+        const uint4 raw = *reinterpret_cast<const uint4*>(ks + r * D + chunk * 8);
+        const float4 a0 = *reinterpret_cast<const float4*>(a_s + chunk * 8);
+        const float4 a1 = *reinterpret_cast<const float4*>(a_s + chunk * 8 + 4);
+        const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&raw);
+        const float2 x0 = __bfloat1622float2(x[0]), x1 = __bfloat1622float2(x[1]);
+        const float2 x2 = __bfloat1622float2(x[2]), x3 = __bfloat1622float2(x[3]);
+        d0 = fmaf(a0.x, x0.x, d0);
+        d1 = fmaf(a0.y, x0.y, d1);
+        d0 = fmaf(a0.z, x1.x, d0);
+        d1 = fmaf(a0.w, x1.y, d1);
+        d0 = fmaf(a1.x, x2.x, d0);
+        d1 = fmaf(a1.y, x2.y, d1);
+        d0 = fmaf(a1.z, x3.x, d0);
+        d1 = fmaf(a1.w, x3.y, d1);
+      }
+    }
+    float d = d0 + d1;
+#pragma unroll
+    for (int o = PER / 2; o > 0; o >>= 1) d += __shfl_xor_sync(0xffffffffu, d, o);
+    if (r < rows && part == 0) plog[r] = d * scale_log2;
+  }
+  __syncthreads();
+  if (kc != nullptr && grp == 0) {
+    float total = 0.f;
+    for (int sb = 0; sb < nsub; ++sb) total = __fadd_rn(total, part_k[sb * D + col]);
+    kc[(((int64_t)b * NB + kb) * H + h) * D + col] = __float2bfloat16_rn(__fdiv_rn(total, (float)rows));
+  }
+  if (!want_sum) return;
+
+  // Softmax over the block's rows (warp 0).
+  if (need_logits && warp == 0) {
+    float m = -INFINITY;
+    for (int r = lane; r < rows; r += 32) m = fmaxf(m, plog[r]);
+    m = warp_max(m);
+    float sum = 0.f;
+    for (int r = lane; r < rows; r += 32) {
+      const float pr = exp2f(plog[r] - m);
+      plog[r] = pr;
+      sum += pr;
+    }
+    sum = warp_sum(sum);
+    if (lane == 0) {
+      stat[0] = m;
+      stat[1] = sum;
+    }
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  const float maximum = need_logits ? stat[0] : 0.f;
+  const float den = need_logits ? stat[1] : 1.f;
+
+  // Weighted (or plain) sums: row group g takes rows [g*span, (g+1)*span).  The probability
+  // enters rounded to bf16 (the reference's tensor-core summaries), or in fp32 with
+  // SB_SUMMARY_FP32_WEIGHTS (its comfy_fp32 mode).
+  const int span = (rows + RG - 1) / RG;
+  {
+    float sk = 0.f, sv = 0.f;
+    const int r1 = min(rows, (grp + 1) * span);
+    for (int r = grp * span; r < r1; ++r) {
+      const float pr = plog[r];
+      const float w = weighted_kv ? ((numerics & SB_SUMMARY_FP32_WEIGHTS) ? pr : __bfloat162float(__float2bfloat16_rn(pr)))
+                                  : 1.f;
+      sk = fmaf(w, __bfloat162float(ks[r * D + col]), sk);
+      sv = fmaf(w, __bfloat162float(vs[r * D + col]), sv);
+    }
+    part_k[grp * D + col] = sk;
+    part_v[grp * D + col] = sv;
+  }
+  __syncthreads();
+  if (grp == 0) {
+    float sk = 0.f, sv = 0.f;
+    for (int g = 0; g < RG; ++g) {
+      sk += part_k[g * D + col];
+      sv += part_v[g * D + col];
+    }
+    const float norm = weighted_kv ? den : (float)rows;
+    const float key = sk / norm;
+    const __nv_bfloat16 key_b = __float2bfloat16_rn(key);
+    const int64_t srow = (((int64_t)b * H + h) * NB + kb) * D + col;
+    if (ak) ak[srow] = key_b;
+    if (av) av[srow] = __float2bfloat16_rn(sv / norm);
+    // Log-mass shift: a . key over the head's columns, from the stored (rounded) key or, with
+    // SB_SUMMARY_PRE_ROUND_LOGMASS, the fp32 mean.
+    float shift = 0.f;
+    if (lm != nullptr && mass_bias) {
+      const float a_c = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + col]);
+      shift = a_c * ((numerics & SB_SUMMARY_PRE_ROUND_LOGMASS) ? key : __bfloat162float(key_b));
+    }
+    shift = warp_sum(shift);
+    if (lane == 0) stat[2 + warp] = shift;
+  }
+  __syncthreads();
+  if (tid == 0 && lm != nullptr) {
+    float shift = 0.f;
+    for (int w = 0; w < D / 32; ++w) shift += stat[2 + w];
+    lm[((int64_t)b * H + h) * NB + kb] =
+        mass_bias ? (maximum + log2f(den)) * kLn2 - shift * scale : logf((float)rows);
+  }
+}
+
 }  // namespace sb
 
 using namespace sb;
@@ -332,6 +529,37 @@ static int launch_pool_keys(const void* k, const void* v, const void* anchor, in
   return SB_OK;
 }
 
+template <typename TA, int D, int BLOCK>
+static int launch_kv_head(const void* k, const void* v, const void* anchor, int B, int tokens, int H,
+                          int weighted_kv, int mass_bias, int numerics, void* kc, void* ak, void* av, float* lm,
+                          cudaStream_t s) {
+  const size_t smem = HeadSmem<D, BLOCK>::kBytes;
+  auto kern = kv_summaries_head_kernel<TA, D, BLOCK>;
+  cudaError_t err = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (err != cudaSuccess) return cuda_error(err, "sb_pool_keys_summaries: set smem");
+  if ((int64_t)ceil_div(tokens, BLOCK) * H >= (1ll << 31) || B > 65535) {
+    set_error("sb_pool_keys_summaries: too many key blocks x heads");
+    return SB_ERR_INVALID;
+  }
+  dim3 grid(ceil_div(tokens, BLOCK) * H, B);
+  kern<<<grid, kHeadThreads, smem, s>>>((const __nv_bfloat16*)k, (const __nv_bfloat16*)v, (const TA*)anchor, tokens,
+                                        H, weighted_kv, mass_bias, numerics, (__nv_bfloat16*)kc,
+                                        (__nv_bfloat16*)ak, (__nv_bfloat16*)av, lm);
+  SB_CHECK_LAUNCH("sb_pool_keys_summaries launch");
+  return SB_OK;
+}
+
+template <typename TA>
+static int launch_kv_head_for(int D, int block, const void* k, const void* v, const void* anchor, int B, int tokens,
+                              int H, int weighted_kv, int mass_bias, int numerics, void* kc, void* ak, void* av,
+                              float* lm, cudaStream_t s) {
+  if (D == 128)
+    return block == 128 ? launch_kv_head<TA, 128, 128>(k, v, anchor, B, tokens, H, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s)
+                        : launch_kv_head<TA, 128, 64>(k, v, anchor, B, tokens, H, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
+  return block == 128 ? launch_kv_head<TA, 64, 128>(k, v, anchor, B, tokens, H, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s)
+                      : launch_kv_head<TA, 64, 64>(k, v, anchor, B, tokens, H, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
+}
+
 extern "C" int sb_pool_keys_summaries(const void* k, const void* v, const void* anchor, int dtype,
                                       int anchor_dtype, int B, int T, int H, int D, int block,
                                       int weighted_kv, int mass_bias, int numerics, void* kc, void* ak,
@@ -352,13 +580,11 @@ extern "C" int sb_pool_keys_summaries(const void* k, const void* v, const void* 
                "sb_pool_keys_summaries: K/V must be 16-byte aligned");
   cudaStream_t s = (cudaStream_t)stream;
   const bool abf = anchor_dtype == SB_BF16;
-  if (dtype == SB_BF16) {
-    if (D == 128)
-      return abf ? launch_pool_keys<__nv_bfloat16, __nv_bfloat16, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s)
-                 : launch_pool_keys<__nv_bfloat16, float, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
-    return abf ? launch_pool_keys<__nv_bfloat16, __nv_bfloat16, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s)
-               : launch_pool_keys<__nv_bfloat16, float, 64>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);
-  }
+  if (dtype == SB_BF16)  // one CTA per (key block, head): K and V read once
+    return abf ? launch_kv_head_for<__nv_bfloat16>(D, block, k, v, anchor, B, T, H, weighted_kv, mass_bias, numerics,
+                                                   kc, ak, av, lm, s)
+               : launch_kv_head_for<float>(D, block, k, v, anchor, B, T, H, weighted_kv, mass_bias, numerics, kc, ak,
+                                           av, lm, s);
   SB_CHECK_ARG(!abf, "sb_pool_keys_summaries: float32 K/V need a float32 anchor");
   if (D == 128)
     return launch_pool_keys<float, float, 128>(k, v, anchor, B, T, H, block, weighted_kv, mass_bias, numerics, kc, ak, av, lm, s);

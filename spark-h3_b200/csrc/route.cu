@@ -8,49 +8,55 @@
 #include <mutex>
 
 #include "common.cuh"
+#include "sm100_ptx.cuh"
 
 namespace sb {
 
 constexpr int kScoreTile = 128;  // query blocks x key blocks per CTA
 constexpr int kScoreThreads = 256;
+constexpr int kKeyStride = kScoreTile + 4;  // floats per d-row of the key tile (16-byte rows)
 
 // grid (ceil(C/128), ceil(QB/128), B*H).  Thread (ty, tx) of a 16 x 16 grid computes 8 x 8
-// scores, query rows ty + 16*i and key columns tx + 16*j, each as one fma chain over d in
-// order: 64 multiply-adds per 16 shared-memory loads.
+// scores: query rows ty + 16 i (i < 8) and key columns 2 tx + 32 p + {0, 1} (p < 4), each one
+// fma chain over d in order.  Two chains advance per instruction (fma.rn.f32x2 on a pair of
+// key columns: each lane is the same single-rounded fma as the scalar form, so the scores
+// are unchanged bit for bit); the query means sit in shared memory as (a, a) pairs so both
+// operands load as 64-bit words.
 template <typename TK, int D>
 __global__ void __launch_bounds__(kScoreThreads)
 block_scores_kernel(const float* __restrict__ qc, const TK* __restrict__ kc, int QB, int NB, int H,
                     int C, float scale_log2, float* __restrict__ scores) {
-  extern __shared__ float score_smem[];
-  float (*sq)[D + 1] = reinterpret_cast<float (*)[D + 1]>(score_smem);
-  float (*sk)[kScoreTile + 1] = reinterpret_cast<float (*)[kScoreTile + 1]>(score_smem + kScoreTile * (D + 1));
+  extern __shared__ __align__(16) float score_smem[];
+  float2* sq = reinterpret_cast<float2*>(score_smem);  // [128 rows][D] of (a, a)
+  float* sk = score_smem + 2 * kScoreTile * D;         // [D][kKeyStride]
   const int bh = blockIdx.z, b = bh / H, h = bh % H;
   const int q0 = blockIdx.y * kScoreTile, c0 = blockIdx.x * kScoreTile;
   const int tid = threadIdx.x;
   for (int idx = tid; idx < kScoreTile * D; idx += kScoreThreads) {
     const int r = idx / D, d = idx % D;
     const int qi = q0 + r, ci = c0 + r;
-    sq[r][d] = qi < QB ? qc[(((int64_t)b * NB + qi) * H + h) * D + d] : 0.f;
-    sk[d][r] = ci < C ? Elem<TK>::to_f(kc[(((int64_t)b * NB + ci) * H + h) * D + d]) : 0.f;
+    const float a = qi < QB ? qc[(((int64_t)b * NB + qi) * H + h) * D + d] : 0.f;
+    sq[r * D + d] = make_float2(a, a);
+    sk[d * kKeyStride + r] = ci < C ? Elem<TK>::to_f(kc[(((int64_t)b * NB + ci) * H + h) * D + d]) : 0.f;
   }
   __syncthreads();
   const int tx = tid % 16, ty = tid / 16;
-  float acc[8][8];
+  uint64_t acc[8][4];
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
-    for (int j = 0; j < 8; ++j) acc[i][j] = 0.f;
+    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
 #pragma unroll 2
   for (int d = 0; d < D; ++d) {
-    float a[8], w[8];
+    uint64_t a[8], w[4];
 #pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = sq[ty + 16 * i][d];
+    for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const uint64_t*>(sq + (ty + 16 * i) * D + d);
 #pragma unroll
-    for (int j = 0; j < 8; ++j) w[j] = sk[d][tx + 16 * j];
+    for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint64_t*>(sk + d * kKeyStride + 2 * tx + 32 * j);
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[i][j] = __fmaf_rn(a[i], w[j], acc[i][j]);
+      for (int j = 0; j < 4; ++j) acc[i][j] = sm100::f2_fma(a[i], w[j], acc[i][j]);
   }
 #pragma unroll
   for (int i = 0; i < 8; ++i) {
@@ -58,9 +64,12 @@ block_scores_kernel(const float* __restrict__ qc, const TK* __restrict__ kc, int
     if (qi >= QB) continue;
     float* row = scores + (((int64_t)b * QB + qi) * H + h) * C;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
-      const int ci = c0 + tx + 16 * j;
-      if (ci < C) row[ci] = __fmul_rn(acc[i][j], scale_log2);
+    for (int j = 0; j < 4; ++j) {
+      const int ci = c0 + 2 * tx + 32 * j;
+      float lo, hi;
+      sm100::f2_unpack(acc[i][j], lo, hi);
+      if (ci < C) row[ci] = __fmul_rn(lo, scale_log2);
+      if (ci + 1 < C) row[ci + 1] = __fmul_rn(hi, scale_log2);
     }
   }
 }
@@ -190,7 +199,7 @@ static int cuda_error_at(cudaError_t err, const char* who, const char* what) {
 
 template <typename TK, int D>
 static size_t score_smem_bytes() {
-  return (size_t)(kScoreTile * (D + 1) + D * (kScoreTile + 1)) * sizeof(float);
+  return (size_t)(2 * kScoreTile * D + D * kKeyStride) * sizeof(float);
 }
 
 // Raises the dynamic shared-memory limit of the score kernel for (TK, D); `who` names the

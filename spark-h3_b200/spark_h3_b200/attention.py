@@ -58,8 +58,6 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     _check_inputs(q_bthd, k_bthd, v_bthd)
     if cfg.sol_route_topk_ratio is None:
         raise RuntimeError("the B200 path implements Top-K routed Spark attention; set sol_route_topk_ratio")
-    if cfg.sol_legacy_full_query:
-        raise NotImplementedError("the B200 path does not implement sol_legacy_full_query")
     if cfg.sol_tail_granularity == "block8x8" and cfg.sol_reweight_summary_math != "tensorcore":
         raise ValueError("block8x8 currently supports tensorcore numeric mode only")
     B, T, H, D = q_bthd.shape
@@ -68,7 +66,8 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
     video = int(layout.video_tokens)
     if video < block:
         raise RuntimeError(f"Spark routing requires at least one complete {block}-token video block")
-    query_tokens = sparse_query_tokens(T, video, block, cfg.sol_video_tail_mode)
+    tail_mode = "legacy_full" if cfg.sol_legacy_full_query else cfg.sol_video_tail_mode
+    query_tokens = sparse_query_tokens(T, video, block, tail_mode)
     query_blocks = query_tokens // block
     candidates = video // block
     nb = math.ceil(T / block)
@@ -97,7 +96,11 @@ def spark_attention_bthd(controller, q_bthd, k_bthd, v_bthd, layout, layer, *, r
 
     # Padding fills after any reblock permutation (spark_integration.py:1173-1187); the anchor
     # covers the complete video blocks only (landmark_virtual_q.py:30-41).
-    qc = ops.padded_query_means(q_bthd, ops.pool_queries(q_bthd, block), video, query_tokens, block)
+    # With sol_legacy_full_query the partial final block keeps the mean of its real rows, video
+    # and context alike (spark_integration.py:925-933; _sol_topk_policy_scores pools every token).
+    qc = ops.pool_queries(q_bthd, block)
+    if tail_mode == "pad":
+        qc = ops.padded_query_means(q_bthd, qc, video, query_tokens, block)
     anchor = ops.query_anchor(qc, block, candidates, anchor_dtype)
     kc, ak, av, lm = ops.pool_keys_summaries(k_bthd, v_bthd, anchor, block, weighted_kv=weighted_kv,
                                              mass_bias=mass_bias, summary_math=cfg.sol_reweight_summary_math,

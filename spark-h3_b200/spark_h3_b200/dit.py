@@ -211,6 +211,8 @@ class DiTStack:
         self.peer = None
         if world > 1 and peer_exchange and self.fused_producer:
             self.peer = PeerExchange((world, self.local, self.hp, cfg.head_dim), self.device, world, rank, group)
+        # When a list, every sequence<->head exchange appends its (start, end) CUDA events.
+        self.exchange_events = None
         ids = torch.arange(self.tokens)
         self.layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=self.grid, video_tokens=self.tokens,
                                    sequence_length=self.tokens, video_positions=torch.zeros(self.tokens, 3,
@@ -295,6 +297,26 @@ class DiTStack:
                   _stream(self.device))
         return q, s
 
+    def _exchange(self):
+        """Brackets one exchange with CUDA events on the current stream when
+        exchange_events is a list (a no-op context otherwise)."""
+        import contextlib
+
+        if self.exchange_events is None or self.world == 1:
+            return contextlib.nullcontext()
+        events = self.exchange_events
+        stream = torch.cuda.current_stream(self.device)
+
+        @contextlib.contextmanager
+        def timed():
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            yield
+            e1.record(stream)
+            events.append((e0, e1))
+
+        return timed()
+
     def modulation(self, t: float):
         temb = F.silu(timestep_embedding(t, self.cfg.t_dim, self.device))
         return [(blk["ada"] @ temb).view(6, self.cfg.hidden).contiguous() for blk in self.blocks]
@@ -318,11 +340,15 @@ class DiTStack:
                     qkv = fp8_gemm(hq, hs, *blk["qkv"])
                     q, k, v = self._qkv_rope(qkv, blk)
                     del qkv
-                qh, kh, vh = (exchange_to_heads(t_, self.group).unsqueeze(0) for t_ in (q, k, v))
+                with self._exchange():
+                    qh, kh, vh = (exchange_to_heads(t_, self.group).unsqueeze(0) for t_ in (q, k, v))
                 del q, k, v
             o = self._attention(qh, kh, vh, layer, dense)
             del qh, kh, vh
-            oq, os_ = self._out_quant(exchange_to_tokens(o[0], self.world, self.group))
+            with self._exchange():
+                o_seg = exchange_to_tokens(o[0], self.world, self.group)
+            oq, os_ = self._out_quant(o_seg)
+            del o_seg
             self._gemm_residual(oq, os_, blk["out"], x, gate1)
             hq, hs = self._norm_quant(x, shift2, scale2)
             f = fp8_gemm(hq, hs, *blk["up"])

@@ -259,9 +259,17 @@ def padded_query_means(q: torch.Tensor, qc: torch.Tensor, video_tokens: int, que
 def sparse_query_tokens(total_tokens: int, video_tokens: int, block: int, tail_mode: str = "dense") -> int:
     """Query prefix evaluated sparsely (spark_integration.py:72-91): the complete video blocks
     ("dense": the partial final block joins the dense suffix), or every video block with the
-    final one padded from the context that follows ("pad")."""
+    final one padded from the context that follows ("pad"), or every video block with the
+    final one pooled over the real video and context rows it holds ("legacy_full", the
+    reference's sol_legacy_full_query, spark_integration.py:925-933)."""
     if tail_mode == "dense":
         return min(total_tokens, (video_tokens // block) * block)
+    if tail_mode == "legacy_full":
+        full = math.ceil(video_tokens / block) * block
+        if full > total_tokens:
+            raise NotImplementedError("sol_legacy_full_query with a final query block that the sequence does not "
+                                      "fill is not implemented on the B200 path")
+        return full
     if tail_mode != "pad":
         raise ValueError("tail_mode must be 'dense' or 'pad'")
     padded = math.ceil(video_tokens / block) * block
@@ -307,7 +315,9 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
     pool Q -> anchor -> pool K + summaries -> scores + Top-K -> sparse attention
     (rows past the sparse query prefix are attended densely by the same kernel).  With
     tail_mode "pad" the partial final video block is routed as a padded block and the context
-    rows that padded it are then attended densely (sb_dense_rows_attention).  tail_granularity
+    rows that padded it are then attended densely (sb_dense_rows_attention); "legacy_full"
+    routes it with the mean of all its rows, video and context, and attends its context rows
+    densely the same way.  tail_granularity
     "block" / "block8x8" replaces the per-row summary columns by a pooled tail per query block
     / per 8 rows, merged into the exact-keys-only output (sb_tail_merge).  head_budgets
     (int32 [H] on the device) gives each head its own Top-K budget (head_budget.py:7-19); the
@@ -327,7 +337,9 @@ def spark_layer(q: torch.Tensor, k: torch.Tensor, v: torch.Tensor, *, block: int
     topk = target_topk(topk_ratio, candidates)
     if head_budgets is not None and (T > video or video % block):
         sink_first, sink_last = candidates, nb
-    qc = padded_query_means(q, pool_queries(q, block), video, query_tokens, block)
+    qc = pool_queries(q, block)
+    if tail_mode == "pad":
+        qc = padded_query_means(q, qc, video, query_tokens, block)
     anchor = query_anchor(qc, block, candidates, anchor_dtype or q.dtype)
     kc, ak, av, lm = pool_keys_summaries(k, v, anchor, block, weighted_kv=weighted_kv, mass_bias=mass_bias,
                                          summary_math=summary_math, logmass_key=logmass_key)

@@ -1,5 +1,6 @@
 """The reference arm of bench.py (`--impl reference`): the CPU oracle port timed on the host
-cores, one JSON line on rank 0 with the contract's keys; other ranks print nothing."""
+cores, one JSON line on rank 0 with the contract's keys and the repo arm's config entry;
+other ranks print nothing.  A reduced grid keeps the CPU work to seconds."""
 import json
 import os
 import subprocess
@@ -8,7 +9,7 @@ from pathlib import Path
 
 ROOT = Path(__file__).resolve().parents[1]
 ARGS = [sys.executable, str(ROOT / "bench.py"), "--impl", "reference", "--steps", "1", "--warmup", "3",
-        "--reference-sample-blocks", "1"]
+        "--cpu-sample-blocks", "2", "--grid", "4,16,32", "--heads", "4"]
 
 
 def test_reference_arm_prints_one_contract_line():
@@ -28,6 +29,15 @@ def test_reference_arm_prints_one_contract_line():
     assert line["e2e"] == {"value": line["value"], "unit": line["unit"], "h2d_bytes_per_step": 0,
                            "d2h_bytes_per_step": 0}
     assert "workload" in line["config"]
+    sys.path.insert(0, str(ROOT))
+    import bench
+
+    bench.GRID, bench.HEADS = (4, 16, 32), 4
+    T = 4 * 16 * 32
+    assert line["config"] == json.loads(json.dumps(bench.config1_dict(1, bench.ops_target_topk(T), T)))
+    assert line["extrapolated"]["attention_extrapolation_factor"] == line["cpu_baseline"]["attention_extrapolation_factor"]
+    assert "route of all 4 heads in full" in line["cpu_baseline"]["sample"]
+    assert line["cpu_baseline"]["summary_extrapolation_factor"] == 2
 
 
 def test_reference_arm_other_ranks_stay_silent():

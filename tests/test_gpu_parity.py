@@ -192,6 +192,41 @@ def test_pad_tail_mode_matches_oracle(cuda_device, block):
     _check(as_np(out)[:, video:], as_np(dense)[:, video:], torch.bfloat16)
 
 
+@pytest.mark.parametrize("block", [64, 128])
+def test_legacy_full_query_matches_oracle(cuda_device, block):
+    # sol_legacy_full_query (spark_integration.py:925-933): the partial final video block is
+    # routed with the mean of all its rows (video and context), evaluated sparsely, and its
+    # context rows are then attended densely with every row after them.
+    q, k, v = make_qkv((4, 16, 33), 2, 128, seed=31, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    extra = make_qkv((1, 10, 15), 2, 128, seed=32, dtype=torch.bfloat16, q_scale=128 ** -0.5)
+    q, k, v = (torch.cat((a, b), dim=1) for a, b in zip((q, k, v), extra))
+    video = 2100
+    ref = oracle.spark_layer(to_oracle(q), to_oracle(k), to_oracle(v), block=block, topk_ratio=0.1,
+                             video_tokens=video, tail_mode="legacy_full")
+    out, route = ops.spark_layer(q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), block=block,
+                                 topk_ratio=0.1, video_tokens=video, tail_mode="legacy_full", return_route=True)
+    torch.cuda.synchronize()
+    assert route["query_tokens"] == ref["query_tokens"] == -(-video // block) * block
+    np.testing.assert_array_equal(as_np(route["qc"]), ref["qc"])
+    np.testing.assert_array_equal(route["indices"].cpu().numpy(), ref["indices"])
+    _check(as_np(out), ref["out"], torch.bfloat16)
+    # Through the attention seam with the reference's config flag.
+    from spark_h3_b200.attention import spark_attention_bthd
+    from spark_h3_b200.config import H3SparseAttentionConfig
+    from spark_h3_b200.layout import PackedLayout
+    from spark_h3_b200.processor import _Controller
+
+    T = q.shape[1]
+    cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode="reweight_only", sol_route_topk_ratio=0.1,
+                                        sol_legacy_full_query=True, sol_block_size=block)
+    ids = torch.arange(T)
+    layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=(1, 1, video), video_tokens=video,
+                          sequence_length=T, video_positions=torch.zeros(video, 3, dtype=torch.long))
+    seam = spark_attention_bthd(_Controller(cfg), q.to(cuda_device), k.to(cuda_device), v.to(cuda_device), layout, 0)
+    torch.cuda.synchronize()
+    assert torch.equal(seam.cpu(), out.cpu())
+
+
 @pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float32])
 def test_dense_rows_attention_window(cuda_device, dtype):
     q, k, v = make_qkv((3, 16, 32), 2, 128, seed=41, dtype=dtype, q_scale=128 ** -0.5)

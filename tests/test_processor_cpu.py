@@ -178,3 +178,15 @@ def test_head_budget_needs_one_budget_per_head():
     assert _head_budgets([1, 2, 3, 4], 4, torch.device("cpu")).dtype == torch.int32
     with pytest.raises(ValueError, match="expected one budget per head"):
         _head_budgets(torch.tensor([1, 2, 3]), 4, torch.device("cpu"))
+
+
+def test_legacy_full_query_prefix():
+    """sol_legacy_full_query (spark_integration.py:925-933): the sparse prefix covers every video
+    block, the partial final one included; a final block the sequence does not fill is refused."""
+    from spark_h3_b200.ops import sparse_query_tokens
+
+    assert sparse_query_tokens(2262, 2100, 64, "legacy_full") == 2112
+    assert sparse_query_tokens(2262, 2048, 64, "legacy_full") == 2048
+    assert sparse_query_tokens(2262, 2100, 128, "legacy_full") == 2176
+    with pytest.raises(NotImplementedError):
+        sparse_query_tokens(2105, 2100, 64, "legacy_full")
