@@ -16,61 +16,125 @@ constexpr int kScoreTile = 128;  // query blocks x key blocks per CTA
 constexpr int kScoreThreads = 256;
 constexpr int kKeyStride = kScoreTile + 4;  // floats per d-row of the key tile (16-byte rows)
 
-// grid (ceil(C/128), ceil(QB/128), B*H).  Thread (ty, tx) of a 16 x 16 grid computes 8 x 8
-// scores: query rows ty + 16 i (i < 8) and key columns 2 tx + 32 p + {0, 1} (p < 4), each one
-// fma chain over d in order.  Two chains advance per instruction (fma.rn.f32x2 on a pair of
-// key columns: each lane is the same single-rounded fma as the scalar form, so the scores
-// are unchanged bit for bit); the query means sit in shared memory as (a, a) pairs so both
-// operands load as 64-bit words.
+// grid (splits, ceil(QB/128), B*H).  A CTA keeps one 128-query-block tile's means in shared
+// memory and walks the candidate tiles blockIdx.x, blockIdx.x + splits, ...; the next
+// tile's key means are fetched into registers while the current tile is scored.  Thread
+// (ty, tx) of a 16 x 16 grid computes 8 x 8 scores: query rows ty + 16 i (i < 8) and key
+// columns 2 tx + 32 p + {0, 1} (p < 4), each one fma chain over d in order.  Two chains
+// advance per instruction (fma.rn.f32x2 on a pair of key columns: each lane is the same
+// single-rounded fma as the scalar form, so the scores are unchanged bit for bit); the query
+// means sit in shared memory as (a, a) pairs so both operands load as 64-bit words.
+template <typename TK> struct KeyChunk;  // 16 bytes of one key-mean row
+template <> struct KeyChunk<__nv_bfloat16> {
+  static constexpr int kElems = 8;
+  __device__ static void to_f(const uint4& raw, float* out) {
+    const __nv_bfloat162* x = reinterpret_cast<const __nv_bfloat162*>(&raw);
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float2 f = __bfloat1622float2(x[i]);
+      out[2 * i] = f.x;
+      out[2 * i + 1] = f.y;
+    }
+  }
+};
+template <> struct KeyChunk<float> {
+  static constexpr int kElems = 4;
+  __device__ static void to_f(const uint4& raw, float* out) {
+    out[0] = __uint_as_float(raw.x);
+    out[1] = __uint_as_float(raw.y);
+    out[2] = __uint_as_float(raw.z);
+    out[3] = __uint_as_float(raw.w);
+  }
+};
+
 template <typename TK, int D>
 __global__ void __launch_bounds__(kScoreThreads)
 block_scores_kernel(const float* __restrict__ qc, const TK* __restrict__ kc, int QB, int NB, int H,
                     int C, float scale_log2, float* __restrict__ scores) {
+  constexpr int EL = KeyChunk<TK>::kElems;
+  constexpr int CHUNKS = D / EL;                           // 16-byte chunks per key row
+  constexpr int PER = kScoreTile * CHUNKS / kScoreThreads;  // chunks a thread fetches per tile
   extern __shared__ __align__(16) float score_smem[];
   float2* sq = reinterpret_cast<float2*>(score_smem);  // [128 rows][D] of (a, a)
   float* sk = score_smem + 2 * kScoreTile * D;         // [D][kKeyStride]
   const int bh = blockIdx.z, b = bh / H, h = bh % H;
-  const int q0 = blockIdx.y * kScoreTile, c0 = blockIdx.x * kScoreTile;
+  const int q0 = blockIdx.y * kScoreTile;
   const int tid = threadIdx.x;
-  for (int idx = tid; idx < kScoreTile * D; idx += kScoreThreads) {
-    const int r = idx / D, d = idx % D;
-    const int qi = q0 + r, ci = c0 + r;
-    const float a = qi < QB ? qc[(((int64_t)b * NB + qi) * H + h) * D + d] : 0.f;
-    sq[r * D + d] = make_float2(a, a);
-    sk[d * kKeyStride + r] = ci < C ? Elem<TK>::to_f(kc[(((int64_t)b * NB + ci) * H + h) * D + d]) : 0.f;
+  for (int idx = tid; idx < kScoreTile * D / 4; idx += kScoreThreads) {
+    const int r = idx / (D / 4), d4 = idx % (D / 4);
+    const int qi = q0 + r;
+    float4 a = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (qi < QB) a = __ldg(reinterpret_cast<const float4*>(qc + (((int64_t)b * NB + qi) * H + h) * D) + d4);
+    float4* dst = reinterpret_cast<float4*>(sq + r * D + 4 * d4);
+    dst[0] = make_float4(a.x, a.x, a.y, a.y);
+    dst[1] = make_float4(a.z, a.z, a.w, a.w);
   }
-  __syncthreads();
+  // Key-mean tile c: thread t fetches chunks t, t + 256, ... with the row fastest
+  // (row = chunk % 128), so a warp's stores into the [d][row] tile hit 32 different banks.
+  uint4 next[PER];
+  auto fetch = [&](int c0) {
+#pragma unroll
+    for (int k = 0; k < PER; ++k) {
+      const int chunk = tid + kScoreThreads * k;
+      const int r = chunk % kScoreTile, part = chunk / kScoreTile;
+      const int ci = c0 + r;
+      next[k] = ci < C ? __ldg(reinterpret_cast<const uint4*>(kc + (((int64_t)b * NB + ci) * H + h) * D) + part)
+                       : make_uint4(0u, 0u, 0u, 0u);
+    }
+  };
+  const int tiles = ceil_div(C, kScoreTile);
   const int tx = tid % 16, ty = tid / 16;
-  uint64_t acc[8][4];
+  int ct = blockIdx.x;
+  if (ct < tiles) fetch(ct * kScoreTile);
+  for (; ct < tiles; ct += gridDim.x) {
+    const int c0 = ct * kScoreTile;
 #pragma unroll
-  for (int i = 0; i < 8; ++i)
+    for (int k = 0; k < PER; ++k) {
+      const int chunk = tid + kScoreThreads * k;
+      const int r = chunk % kScoreTile, part = chunk / kScoreTile;
+      float f[EL];
+      KeyChunk<TK>::to_f(next[k], f);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
-#pragma unroll 2
-  for (int d = 0; d < D; ++d) {
-    uint64_t a[8], w[4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const uint64_t*>(sq + (ty + 16 * i) * D + d);
-#pragma unroll
-    for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint64_t*>(sk + d * kKeyStride + 2 * tx + 32 * j);
+      for (int e = 0; e < EL; ++e) sk[(part * EL + e) * kKeyStride + r] = f[e];
+    }
+    __syncthreads();
+    if (ct + (int)gridDim.x < tiles) fetch((ct + gridDim.x) * kScoreTile);
+    uint64_t acc[8][4];
 #pragma unroll
     for (int i = 0; i < 8; ++i)
 #pragma unroll
-      for (int j = 0; j < 4; ++j) acc[i][j] = sm100::f2_fma(a[i], w[j], acc[i][j]);
-  }
+      for (int j = 0; j < 4; ++j) acc[i][j] = 0ull;
+#pragma unroll 2
+    for (int d = 0; d < D; ++d) {
+      uint64_t a[8], w[4];
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    const int qi = q0 + ty + 16 * i;
-    if (qi >= QB) continue;
-    float* row = scores + (((int64_t)b * QB + qi) * H + h) * C;
+      for (int i = 0; i < 8; ++i) a[i] = *reinterpret_cast<const uint64_t*>(sq + (ty + 16 * i) * D + d);
 #pragma unroll
-    for (int j = 0; j < 4; ++j) {
-      const int ci = c0 + 2 * tx + 32 * j;
-      float lo, hi;
-      sm100::f2_unpack(acc[i][j], lo, hi);
-      if (ci < C) row[ci] = __fmul_rn(lo, scale_log2);
-      if (ci + 1 < C) row[ci + 1] = __fmul_rn(hi, scale_log2);
+      for (int j = 0; j < 4; ++j) w[j] = *reinterpret_cast<const uint64_t*>(sk + d * kKeyStride + 2 * tx + 32 * j);
+#pragma unroll
+      for (int i = 0; i < 8; ++i)
+#pragma unroll
+        for (int j = 0; j < 4; ++j) acc[i][j] = sm100::f2_fma(a[i], w[j], acc[i][j]);
     }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const int qi = q0 + ty + 16 * i;
+      if (qi >= QB) continue;
+      float* row = scores + (((int64_t)b * QB + qi) * H + h) * C;
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        const int ci = c0 + 2 * tx + 32 * j;
+        float lo, hi;
+        sm100::f2_unpack(acc[i][j], lo, hi);
+        if (ci + 1 < C && (C & 1) == 0) {
+          *reinterpret_cast<float2*>(row + ci) = make_float2(__fmul_rn(lo, scale_log2), __fmul_rn(hi, scale_log2));
+        } else {
+          if (ci < C) row[ci] = __fmul_rn(lo, scale_log2);
+          if (ci + 1 < C) row[ci + 1] = __fmul_rn(hi, scale_log2);
+        }
+      }
+    }
+    __syncthreads();  // every thread is done with this key tile before the next overwrites it
   }
 }
 
@@ -81,21 +145,27 @@ __device__ __forceinline__ uint32_t float_key(float f) {
 }
 
 // One warp per (b, query block, head) row, several rows per CTA, no CTA barriers: the row's
-// keys sit in the warp's slice of shared memory; a 4 x 8-bit radix select with a per-warp
-// histogram finds the key of the k-th largest score; then 32 candidates at a time, the
+// keys sit in the warp's slice of shared memory; a radix select (8-bit digits) with per-warp
+// histograms finds the key of the k-th largest score; then 32 candidates at a time, the
 // keys above it and the lowest-index keys equal to it are taken (each ballot is one packed
 // route word).  Ties at the cut go to the lowest candidate index.
+// The row's scores reach shared memory by cp.async copies issued all at once (a row is read
+// with many loads in flight, not one dependent load per lane and step), and the key bits
+// that every candidate of the row shares (sign, exponent and leading mantissa bits of
+// clustered scores) are known without a pass, so the digits start below them.  Four warps
+// per CTA let several CTAs share an SM, so one row's copies overlap another's passes.
 //
 // k is `topk` for every row, or, with per-head budgets (head_budget.py:7-19), head_topk[h]
 // for the row's head h = row % H, clamped to [0, C].  Index rows are `index_width` wide;
 // positions past the row's k are written as -1.
-constexpr int kTopkWarpMaxRows = 8;
+constexpr int kTopkWarpMaxRows = 4;
+constexpr int kHistCopies = 1;
 
 __global__ void __launch_bounds__(32 * kTopkWarpMaxRows)
 topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int topk, int words,
                       const int32_t* __restrict__ head_topk, int H, int index_width,
                       int32_t* __restrict__ packed, int32_t* __restrict__ indices) {
-  extern __shared__ uint32_t warp_smem[];  // per warp: hist[256] then keys[C]
+  extern __shared__ uint32_t warp_smem[];  // per warp: hist[kHistCopies][256] then keys[C]
   const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
   const int64_t row = (int64_t)blockIdx.x * (blockDim.x >> 5) + warp;
   if (row >= rows) return;
@@ -108,21 +178,41 @@ topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int
       for (int i = lane; i < index_width; i += 32) indices[row * index_width + i] = -1;
     return;
   }
-  uint32_t* hist = warp_smem + (size_t)warp * (256 + C);
-  uint32_t* keys = hist + 256;
+  uint32_t* hist = warp_smem + (size_t)warp * (kHistCopies * 256 + C);
+  uint32_t* keys = hist + kHistCopies * 256;
+  uint32_t* my_hist = hist + 256 * (lane % kHistCopies);
   const float* src = scores + row * C;
-  for (int i = lane; i < C; i += 32) keys[i] = float_key(src[i]);
-  uint32_t prefix = 0, need = (uint32_t)k;
+  for (int i = lane; i < C; i += 32)
+    asm volatile("cp.async.ca.shared.global [%0], [%1], 4;" ::"r"((uint32_t)__cvta_generic_to_shared(keys + i)),
+                 "l"(src + i)
+                 : "memory");
+  asm volatile("cp.async.wait_all;" ::: "memory");
+  __syncwarp();
+  uint32_t all_and = 0xffffffffu, all_or = 0u;
+  for (int i = lane; i < C; i += 32) {
+    const uint32_t kk = float_key(__uint_as_float(keys[i]));
+    keys[i] = kk;
+    all_and &= kk;
+    all_or |= kk;
+  }
+  all_and = __reduce_and_sync(0xffffffffu, all_and);
+  all_or = __reduce_or_sync(0xffffffffu, all_or);
+  // Bits above `remaining` are common to every key: they are part of the threshold already.
+  int remaining = 32 - __clz(all_and ^ all_or);  // 0 when every key is equal
+  uint32_t prefix = remaining == 32 ? 0u : (all_and & (0xffffffffu << remaining));
+  uint32_t need = (uint32_t)k;
 #pragma unroll 1
-  for (int pass = 0; pass < 4; ++pass) {
-    const int shift = 24 - 8 * pass;
-    const uint32_t mask_hi = pass == 0 ? 0u : (0xffffffffu << (32 - 8 * pass));
+  while (remaining > 0) {
+    const int width = remaining < 8 ? remaining : 8;
+    const int shift = remaining - width;
+    const uint32_t mask_hi = remaining == 32 ? 0u : (0xffffffffu << remaining);
+    const uint32_t dmask = (1u << width) - 1u;
 #pragma unroll
-    for (int i = 0; i < 8; ++i) hist[lane + 32 * i] = 0u;
+    for (int i = 0; i < kHistCopies * 8; ++i) hist[lane + 32 * i] = 0u;
     __syncwarp();
     for (int i = lane; i < C; i += 32) {
       const uint32_t kk = keys[i];
-      if ((kk & mask_hi) == prefix) atomicAdd(&hist[(kk >> shift) & 0xffu], 1u);
+      if ((kk & mask_hi) == prefix) atomicAdd(&my_hist[(kk >> shift) & dmask], 1u);
     }
     __syncwarp();
     // Lane l owns digits 255 - 8l .. 248 - 8l (descending); an exclusive prefix over lanes of
@@ -130,7 +220,10 @@ topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int
     uint32_t c[8], own = 0;
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
-      c[i] = hist[255 - 8 * lane - i];
+      const int dg = 255 - 8 * lane - i;
+      c[i] = 0u;
+#pragma unroll
+      for (int cp = 0; cp < kHistCopies; ++cp) c[i] += hist[256 * cp + dg];
       own += c[i];
     }
     uint32_t incl = own;
@@ -162,6 +255,8 @@ topk_rows_warp_kernel(const float* __restrict__ scores, int64_t rows, int C, int
     }
     prefix |= (uint32_t)sel_digit << shift;
     need -= sel_above;
+    remaining = shift;
+    __syncwarp();
   }
   const uint32_t thresh = prefix, take_equal = need;
   uint32_t eq_seen = 0;
@@ -222,6 +317,21 @@ static int launch_scores(const char* who, dim3 grid, const float* qc, const void
   return SB_OK;
 }
 
+// Score grid: one CTA row per (query tile, head), and as many CTAs sharing its candidate
+// tiles as bring the launch to about two waves of the device's SMs (one CTA fits an SM).
+static dim3 score_grid(int candidates, int query_blocks, int heads) {
+  static int sms = 0;
+  if (sms == 0) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+      sms = 148;
+  }
+  const int q_tiles = ceil_div(query_blocks, kScoreTile), c_tiles = ceil_div(candidates, kScoreTile);
+  const int64_t rows = (int64_t)q_tiles * heads;
+  const int splits = (int)std::max<int64_t>(1, std::min<int64_t>(c_tiles, (2 * sms + rows - 1) / rows));
+  return dim3(splits, q_tiles, heads);
+}
+
 // Score-kernel dispatch on the key-centroid dtype and the head dim (prepare_scores first).
 static int scores_for(const char* who, int kc_dtype, int D, dim3 grid, const float* qc, const void* kc, int QB, int NB,
                       int H, int C, float scale_log2, float* scores, cudaStream_t s) {
@@ -245,7 +355,7 @@ struct TopkLaunch {
 };
 
 static TopkLaunch topk_shape(int C) {
-  const size_t per_warp = (size_t)(256 + C) * sizeof(uint32_t);
+  const size_t per_warp = (size_t)(kHistCopies * 256 + C) * sizeof(uint32_t);
   const int warps = (int)std::min<size_t>(kTopkWarpMaxRows, std::max<size_t>(1, (200 * 1024) / per_warp));
   return TopkLaunch{warps, per_warp * warps};
 }
@@ -303,7 +413,7 @@ static int route_with_workspace(const char* who, const float* qc, const void* kc
   if (rc == SB_OK) rc = prepare_topk(who, candidates);
   if (rc != SB_OK) return rc;
   float* scores = (float*)workspace;
-  dim3 grid(ceil_div(candidates, kScoreTile), ceil_div(QB, kScoreTile), B * H);
+  dim3 grid = score_grid(candidates, QB, B * H);
   rc = scores_for(who, kc_dtype, D, grid, qc, kc, QB, NB, H, candidates, scale_log2, scores, s);
   if (rc != SB_OK) return rc;
   return launch_topk(who, scores, (int64_t)B * QB * H, candidates, topk, ceil_div(NB, 32), head_topk, H, index_width,
@@ -408,7 +518,7 @@ extern "C" int sb_route_topk_noalloc(const float* qc, const void* kc, int kc_dty
     for (int q0 = 0; q0 < QB; q0 += chunk) {
       const int n = std::min(chunk, QB - q0);
       const float* qc_c = qc + ((int64_t)b * NB + q0) * H * D;
-      dim3 grid(ceil_div(candidates, kScoreTile), ceil_div(n, kScoreTile), H);
+      dim3 grid = score_grid(candidates, n, H);
       rc = scores_for(who, kc_dtype, D, grid, qc_c, kc_b, n, NB, H, candidates, scale_log2, scratch, s);
       if (rc != SB_OK) return rc;
       const int64_t row0 = ((int64_t)b * QB + q0) * H;
