@@ -51,9 +51,11 @@ PROFILE_ONLY = False
 HEAD_DIM = 128
 BLOCK = 128
 TOPK_RATIO = 0.1
-# DRAM bytes per launch of the attention kernel at this workload (dram__bytes_read.sum +
-# dram__bytes_write.sum of one ncu capture: 4.74 GB read + 1.02 GB write).
-ATTENTION_TRAFFIC_BYTES = 5.76e9
+# DRAM bytes per launch of the attention kernel at this workload: dram__bytes_read.sum +
+# dram__bytes_write.sum of one launch of the same layer with 4 of the 32 heads (0.648 GB read
+# + 0.119 GB written), scaled by 8.  Heads run one after another through the grid, so the
+# traffic grows with the head count.
+ATTENTION_TRAFFIC_BYTES = 8 * (647791616 + 118922240)
 
 
 def dense_flops(tokens: int, heads: int, dim: int) -> float:
@@ -396,7 +398,8 @@ def run_ours(args) -> None:
                           peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"],
                           frac_of_sustained=achieved / peaks["bf16_sustained"],
                           traffic=ATTENTION_TRAFFIC_BYTES if (GRID, world) == ((31, 48, 84), 1) else None,
-                          traffic_unit="bytes per launch (ncu dram__bytes_read.sum + dram__bytes_write.sum)",
+                          traffic_unit=("bytes per launch: ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                        "4-head layer, scaled x8 to 32 heads"),
                           peak_source=peaks["source"],
                           note="achieved = algorithmic sparse FLOPs per launch / mean CUDA-event launch time"),
             e2e=dict(value=total_dense / (e2e_ms * 1e-3) / 1e12, unit=UNIT, ms_per_step=e2e_ms,

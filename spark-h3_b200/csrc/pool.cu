@@ -289,10 +289,11 @@ __device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_gr
 
 template <int D, int BLOCK>
 struct HeadSmem {
-  static constexpr int kRowGroups = kHeadThreads / D;  // threads per column
   static constexpr size_t kTile = (size_t)BLOCK * D * sizeof(__nv_bfloat16);
-  static constexpr size_t kBytes = 2 * kTile + BLOCK * sizeof(float) + 2 * kHeadThreads * sizeof(float) +
-                                   D * sizeof(float) + 64;
+  // K tile, V tile, logits [BLOCK], mean partials [2][D], anchor [D], statistics
+  static constexpr size_t kBytes = 2 * kTile + BLOCK * sizeof(float) + 3 * D * sizeof(float) + 64;
+  // The weighted-sum partials ([kHeadThreads / (D / 8)][D] for K and for V) reuse the tiles.
+  static_assert(2 * (kHeadThreads / (D / 8)) * D * sizeof(float) <= 2 * kTile, "partials must fit the tiles");
 };
 
 template <typename TA, int D, int BLOCK>
@@ -303,14 +304,12 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
                          __nv_bfloat16* __restrict__ av, float* __restrict__ lm) {
   using S = HeadSmem<D, BLOCK>;
   constexpr int CH = D * 2 / 16;  // 16-byte chunks per row
-  constexpr int RG = S::kRowGroups;
   extern __shared__ __align__(16) uint8_t head_smem[];
   __nv_bfloat16* ks = reinterpret_cast<__nv_bfloat16*>(head_smem);
   __nv_bfloat16* vs = reinterpret_cast<__nv_bfloat16*>(head_smem + S::kTile);
   float* plog = reinterpret_cast<float*>(head_smem + 2 * S::kTile);  // [BLOCK]
-  float* part_k = plog + BLOCK;                                     // [RG][D]
-  float* part_v = part_k + kHeadThreads;                            // [RG][D]
-  float* a_s = part_v + kHeadThreads;                               // [D] anchor
+  float* part_k = plog + BLOCK;                                     // [2][D] key-mean partials
+  float* a_s = part_k + 2 * D;                                      // [D] anchor
   float* stat = a_s + D;                                            // max, den, 8 warp partials
 
   const int kb = blockIdx.x / H, h = blockIdx.x % H, b = blockIdx.y;
@@ -341,15 +340,27 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
   cp_async_wait<1>();  // K has landed; V may still be in flight
   __syncthreads();
 
-  const int col = tid % D, grp = tid / D;
-  // Key means: row group g sums 64-row sub-block g in token order; the sub-block sums are
-  // then added in order and divided by the rows present (the canonical order).
+  constexpr int OCT = D / 8;                  // 8-column octets of a row (one 16-byte chunk)
+  constexpr int GROUPS = kHeadThreads / OCT;  // row groups of the weighted sums
+  const int oct = tid % OCT, grp = tid / OCT;
+  // Key means: thread (column pair c, sub-block s) sums columns 2c, 2c + 1 over the rows of
+  // 64-row sub-block s in token order (two chains, one 32-bit read per row); the sub-block
+  // sums are then added in order and divided by the rows present (the canonical order).
   const int nsub = (rows + 63) / 64;
-  if (grp < nsub) {
-    float acc = 0.f;
-    const int r1 = min(rows, 64 * grp + 64);
-    for (int r = 64 * grp; r < r1; ++r) acc = __fadd_rn(acc, __bfloat162float(ks[r * D + col]));
-    part_k[grp * D + col] = acc;
+  {
+    const int pair = tid % (D / 2), sb = tid / (D / 2);
+    if (sb < nsub) {
+      float acc0 = 0.f, acc1 = 0.f;
+      const int r1 = min(rows, 64 * sb + 64);
+      const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(ks) + pair;
+      for (int r = 64 * sb; r < r1; ++r) {
+        const float2 f = __bfloat1622float2(src[r * (D / 2)]);
+        acc0 = __fadd_rn(acc0, f.x);
+        acc1 = __fadd_rn(acc1, f.y);
+      }
+      part_k[sb * D + 2 * pair] = acc0;
+      part_k[sb * D + 2 * pair + 1] = acc1;
+    }
   }
   // Anchor logits: PER = 256 / BLOCK threads per row, each a dot over D / PER columns in
   // 16-byte chunks.  Chunk order is rotated by (thread & 7), so the eight threads of a
@@ -387,10 +398,10 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
     if (r < rows && part == 0) plog[r] = d * scale_log2;
   }
   __syncthreads();
-  if (kc != nullptr && grp == 0) {
+  if (kc != nullptr && tid < D) {
     float total = 0.f;
-    for (int sb = 0; sb < nsub; ++sb) total = __fadd_rn(total, part_k[sb * D + col]);
-    kc[(((int64_t)b * NB + kb) * H + h) * D + col] = __float2bfloat16_rn(__fdiv_rn(total, (float)rows));
+    for (int sb = 0; sb < nsub; ++sb) total = __fadd_rn(total, part_k[sb * D + tid]);
+    kc[(((int64_t)b * NB + kb) * H + h) * D + tid] = __float2bfloat16_rn(__fdiv_rn(total, (float)rows));
   }
   if (!want_sum) return;
 
@@ -416,36 +427,53 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
   const float maximum = need_logits ? stat[0] : 0.f;
   const float den = need_logits ? stat[1] : 1.f;
 
-  // Weighted (or plain) sums: row group g takes rows [g*span, (g+1)*span).  The probability
-  // enters rounded to bf16 (the reference's tensor-core summaries), or in fp32 with
-  // SB_SUMMARY_FP32_WEIGHTS (its comfy_fp32 mode).
-  const int span = (rows + RG - 1) / RG;
-  {
-    float sk = 0.f, sv = 0.f;
-    const int r1 = min(rows, (grp + 1) * span);
-    for (int r = grp * span; r < r1; ++r) {
-      const float pr = plog[r];
-      const float w = weighted_kv ? ((numerics & SB_SUMMARY_FP32_WEIGHTS) ? pr : __bfloat162float(__float2bfloat16_rn(pr)))
-                                  : 1.f;
-      sk = fmaf(w, __bfloat162float(ks[r * D + col]), sk);
-      sv = fmaf(w, __bfloat162float(vs[r * D + col]), sv);
+  // Weighted (or plain) sums: thread (octet o, group g) accumulates the 8 columns of octet o
+  // over rows g, g + GROUPS, ... from 16-byte shared-memory reads.  The probability enters
+  // rounded to bf16 (the reference's tensor-core summaries), or in fp32 with
+  // SB_SUMMARY_FP32_WEIGHTS (its comfy_fp32 mode).  The group partials are then summed per
+  // column, in group order, through shared memory (the K tile's space, no longer read).
+  float sk[8], sv[8];
+#pragma unroll
+  for (int e = 0; e < 8; ++e) sk[e] = sv[e] = 0.f;
+  for (int r = grp; r < rows; r += GROUPS) {
+    const float pr = plog[r];
+    const float w = weighted_kv ? ((numerics & SB_SUMMARY_FP32_WEIGHTS) ? pr : __bfloat162float(__float2bfloat16_rn(pr)))
+                                : 1.f;
+    const uint4 kraw = *reinterpret_cast<const uint4*>(ks + r * D + oct * 8);
+    const uint4 vraw = *reinterpret_cast<const uint4*>(vs + r * D + oct * 8);
+    const __nv_bfloat162* kx = reinterpret_cast<const __nv_bfloat162*>(&kraw);
+    const __nv_bfloat162* vx = reinterpret_cast<const __nv_bfloat162*>(&vraw);
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 kf = __bfloat1622float2(kx[e]), vf = __bfloat1622float2(vx[e]);
+      sk[2 * e] = fmaf(w, kf.x, sk[2 * e]);
+      sk[2 * e + 1] = fmaf(w, kf.y, sk[2 * e + 1]);
+      sv[2 * e] = fmaf(w, vf.x, sv[2 * e]);
+      sv[2 * e + 1] = fmaf(w, vf.y, sv[2 * e + 1]);
     }
-    part_k[grp * D + col] = sk;
-    part_v[grp * D + col] = sv;
+  }
+  __syncthreads();  // every K and V read is done: the tiles' space takes the partials
+  float* red_k = reinterpret_cast<float*>(head_smem);  // [GROUPS][D]
+  float* red_v = red_k + GROUPS * D;
+#pragma unroll
+  for (int e = 0; e < 8; ++e) {
+    red_k[grp * D + oct * 8 + e] = sk[e];
+    red_v[grp * D + oct * 8 + e] = sv[e];
   }
   __syncthreads();
-  if (grp == 0) {
-    float sk = 0.f, sv = 0.f;
-    for (int g = 0; g < RG; ++g) {
-      sk += part_k[g * D + col];
-      sv += part_v[g * D + col];
+  if (tid < D) {
+    const int col = tid;
+    float sum_k = 0.f, sum_v = 0.f;
+    for (int g = 0; g < GROUPS; ++g) {
+      sum_k += red_k[g * D + col];
+      sum_v += red_v[g * D + col];
     }
     const float norm = weighted_kv ? den : (float)rows;
-    const float key = sk / norm;
+    const float key = sum_k / norm;
     const __nv_bfloat16 key_b = __float2bfloat16_rn(key);
     const int64_t srow = (((int64_t)b * H + h) * NB + kb) * D + col;
     if (ak) ak[srow] = key_b;
-    if (av) av[srow] = __float2bfloat16_rn(sv / norm);
+    if (av) av[srow] = __float2bfloat16_rn(sum_v / norm);
     // Log-mass shift: a . key over the head's columns, from the stored (rounded) key or, with
     // SB_SUMMARY_PRE_ROUND_LOGMASS, the fp32 mean.
     float shift = 0.f;

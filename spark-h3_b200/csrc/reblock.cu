@@ -177,9 +177,11 @@ __global__ void __launch_bounds__(256) cholesky_kernel(float* __restrict__ facto
 
 // ================================================================== transform
 constexpr int kTfThreads = 192;  // warps 0-3 epilogue, 4 TMA producer, 5 MMA issuer
-constexpr int kTfStages = 2;
+constexpr int kTfStages = 3;
 constexpr int kTfTileBytes = 128 * kDim * 2;  // 32 KB: two 64-column halves of 128 rows
 constexpr int kTfHalfBytes = kTfTileBytes / 2;
+constexpr int kTfWarpOutBytes = 32 * kDim * 2;  // one epilogue warp's 32 output rows (8 KB)
+constexpr int kTfOutBytes = 2 * 4 * kTfWarpOutBytes;  // double-buffered, four epilogue warps
 
 struct __align__(8) TfControl {
   uint64_t full[kTfStages], empty[kTfStages];
@@ -198,6 +200,7 @@ struct TfParams {
 
 __global__ void __launch_bounds__(kTfThreads) reblock_transform_kernel(const __grid_constant__ CUtensorMap tm_k,
                                                                        const __grid_constant__ CUtensorMap tm_q,
+                                                                       const __grid_constant__ CUtensorMap tm_out,
                                                                        TfParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_u32(smem) & 1023u) != 0u) {
@@ -206,7 +209,8 @@ __global__ void __launch_bounds__(kTfThreads) reblock_transform_kernel(const __g
   }
   uint8_t* sB = smem;                                   // L^T, K-major, two 64-column halves
   uint8_t* sA = smem + kTfTileBytes;                    // token tiles
-  TfControl& C = *reinterpret_cast<TfControl*>(smem + (1 + kTfStages) * kTfTileBytes);
+  uint8_t* sOut = smem + (1 + kTfStages) * kTfTileBytes;  // [2][4 warps][2 halves][32 rows][128 B]
+  TfControl& C = *reinterpret_cast<TfControl*>(sOut + kTfOutBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int r = blockIdx.y;
   const int side = r / p.BH, bh = r % p.BH, b = bh / p.H, h = bh % p.H;
@@ -247,7 +251,10 @@ __global__ void __launch_bounds__(kTfThreads) reblock_transform_kernel(const __g
     tmem_alloc(smem_u32(&C.tmem_base), 256);
     tmem_relinquish();
   }
-  if (warp == 4 && lane == 0) prefetch_tensormap(map);
+  if (warp == 4 && lane == 0) {
+    prefetch_tensormap(map);
+    prefetch_tensormap(&tm_out);
+  }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -300,32 +307,54 @@ __global__ void __launch_bounds__(kTfThreads) reblock_transform_kernel(const __g
       tc_commit(smem_u32(&C.mma_done));
     }
   } else {
+    // Epilogue: warp w owns rows 32w .. 32w + 31 of each tile.  It converts its rows to bf16
+    // into a 128-byte-swizzled staging buffer (16-byte chunk c of row r at c ^ (r & 7), the
+    // layout of a SWIZZLE_128B box) and writes them with two TMA stores (one per 64-column
+    // half); two buffers alternate, and a buffer is reused once its store has read it.
     const int row = threadIdx.x;
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    const uint32_t out_base = smem_u32(sOut) + (uint32_t)(warp * 2 * kTfWarpOutBytes);
     int local = 0;
     for (int tile = blockIdx.x; tile < p.tiles; tile += p.splits, ++local) {
       const int buf = local & 1;
       const bool got = mbar_wait(smem_u32(&C.acc_full[buf]), (uint32_t)((local >> 1) & 1), abort_flag, p.status, 504);
       if (!__all_sync(kFull, got)) break;
       tc_fence_after();
-      const int t = tile * 128 + row;
-      __nv_bfloat16* out = p.features + ((int64_t)r * p.video + t) * kDim;
+      if (lane == 0) bulk_wait_group_read<1>();  // the store that last read this buffer is done
+      __syncwarp();
+      const uint32_t stage = out_base + (uint32_t)(buf * kTfWarpOutBytes);
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t v[32];
         tmem_ld32(tmem + lane_base + buf * 128 + 32 * c, v);
         tmem_wait_ld();
-        if (t < p.video) {
-          float f[32];
+        const uint32_t half = stage + (uint32_t)((c >> 1) * (kTfWarpOutBytes / 2)) + (uint32_t)(lane * 128);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) f[i] = __uint_as_float(v[i]);
+        for (int q = 0; q < 4; ++q) {
+          const int chunk = (c & 1) * 4 + q;  // 16-byte chunk of the 128-byte half row
+          uint32_t w[4];
 #pragma unroll
-          for (int q = 0; q < 4; ++q) store8(out + 32 * c + 8 * q, f + 8 * q);
+          for (int e = 0; e < 4; ++e)
+            w[e] = cvt_bf16x2(__uint_as_float(v[8 * q + 2 * e]), __uint_as_float(v[8 * q + 2 * e + 1]));
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(half + (uint32_t)((chunk ^ (lane & 7)) * 16)),
+                       "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                       : "memory");
         }
       }
       tc_fence_before();
-      mbar_arrive(smem_u32(&C.acc_empty[buf]));
+      mbar_arrive(smem_u32(&C.acc_empty[buf]));  // TMEM columns are free once loaded
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        const int y = tile * 128 + warp * 32;  // rows past the video end are clipped by the store
+        tma_store_3d(&tm_out, stage, 0, y, r);
+        tma_store_3d(&tm_out, stage + kTfWarpOutBytes / 2, 64, y, r);
+        bulk_commit_group();
+      }
     }
+    if (lane == 0) bulk_wait_group<0>();  // every store has landed before the CTA exits
+    __syncwarp();
+    (void)row;
   }
   tc_fence_before();
   __syncthreads();
@@ -1189,6 +1218,28 @@ int make_bthd_map(CUtensorMap* map, const void* base, int B, int T, int H) {
   return SB_OK;
 }
 
+// Features [rows, video, 128] bf16 as a store target: boxes of 64 columns x 32 rows, 128-byte
+// swizzle (one epilogue warp's rows of one 64-column half).
+int make_features_map(CUtensorMap* map, void* base, int rows, int video) {
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr) {
+    set_error("sb_reblock_transform: cuTensorMapEncodeTiled is unavailable");
+    return SB_ERR_CUDA;
+  }
+  const cuuint64_t dims[3] = {(cuuint64_t)kDim, (cuuint64_t)video, (cuuint64_t)rows};
+  const cuuint64_t strides[2] = {(cuuint64_t)kDim * 2, (cuuint64_t)kDim * 2 * (uint64_t)video};
+  const cuuint32_t box[3] = {64, 32, 1};
+  const cuuint32_t estr[3] = {1, 1, 1};
+  CUresult res = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides, box, estr,
+                        CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                        CU_TENSOR_MAP_L2_PROMOTION_NONE, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (res != CUDA_SUCCESS) {
+    set_error("sb_reblock_transform: cuTensorMapEncodeTiled (features) failed (CUresult %d)", (int)res);
+    return SB_ERR_CUDA;
+  }
+  return SB_OK;
+}
+
 int sm_count() {
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
@@ -1250,6 +1301,28 @@ extern "C" int sb_reblock_metric(const void* q, const void* k, int dtype, int B,
   return SB_OK;
 }
 
+// Splits of each row's token tiles across CTAs, chosen so the rows x splits CTAs fill whole
+// waves of the resident slots (two CTAs per SM): with 64 rows on 296 slots, 5 splits (320
+// CTAs) leave 24 CTAs running alone in a second wave, while 37 splits make exactly 8 waves.
+// Among splits that give every CTA at least 8 tiles, the one with the least idle slot time
+// wins (ties: fewer splits).
+static int transform_splits(int tiles, int rows, int slots) {
+  int best = 1;
+  double best_eff = 0.0;
+  const int max_splits = std::max(1, tiles / 8);
+  for (int sp = 1; sp <= max_splits; ++sp) {
+    const int64_t ctas = (int64_t)rows * sp;
+    const int64_t waves = (ctas + slots - 1) / slots;
+    const double eff = (double)ctas / (double)(waves * slots);
+    if (eff > best_eff + 1e-9) {
+      best_eff = eff;
+      best = sp;
+    }
+    if (eff >= 0.999) break;
+  }
+  return best;
+}
+
 extern "C" int sb_reblock_transform(const void* q, const void* k, int B, int T, int H, int D, int video_tokens,
                                     const float* factors, void* features, void* stream) {
   SB_CHECK_ARG(q && k && factors && features, "sb_reblock_transform: null pointer");
@@ -1259,10 +1332,11 @@ extern "C" int sb_reblock_transform(const void* q, const void* k, int B, int T, 
                "sb_reblock_transform: tensors must be 16-byte aligned");
   int* status = device_status_ptr();
   if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_reblock_transform: status word");
-  CUtensorMap mk, mq;
+  CUtensorMap mk, mq, mo;
   int rc;
   if ((rc = make_bthd_map(&mk, k, B, T, H)) != SB_OK) return rc;
   if ((rc = make_bthd_map(&mq, q, B, T, H)) != SB_OK) return rc;
+  if ((rc = make_features_map(&mo, features, 2 * B * H, video_tokens)) != SB_OK) return rc;
   TfParams p{};
   p.factors = factors;
   p.features = static_cast<__nv_bfloat16*>(features);
@@ -1273,12 +1347,12 @@ extern "C" int sb_reblock_transform(const void* q, const void* k, int B, int T, 
   p.video = video_tokens;
   p.tiles = ceil_div(video_tokens, 128);
   const int rows = 2 * p.BH;
-  p.splits = std::max(1, std::min(p.tiles, ceil_div(2 * sm_count(), rows)));
-  const size_t smem = (size_t)(1 + kTfStages) * kTfTileBytes + sizeof(TfControl);
+  p.splits = transform_splits(p.tiles, rows, sm_count());  // one CTA per SM
+  const size_t smem = (size_t)(1 + kTfStages) * kTfTileBytes + kTfOutBytes + sizeof(TfControl);
   cudaError_t err = cudaFuncSetAttribute(reblock_transform_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_reblock_transform: set smem");
-  reblock_transform_kernel<<<dim3(p.splits, rows), kTfThreads, smem, (cudaStream_t)stream>>>(mk, mq, p);
+  reblock_transform_kernel<<<dim3(p.splits, rows), kTfThreads, smem, (cudaStream_t)stream>>>(mk, mq, mo, p);
   SB_CHECK_LAUNCH("sb_reblock_transform launch");
   return SB_OK;
 }
