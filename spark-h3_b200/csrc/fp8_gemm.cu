@@ -37,6 +37,7 @@ struct GemmParams {
   const __nv_bfloat16* residual;  // optional: out = residual + gate[n] * (scaled product + bias)
   const float* gate;              // [N], required with residual
   __nv_bfloat16* out;
+  int tma_out;  // 1: the plain / residual output is written by TMA stores (tm_out); 0: row stores
   int* status;
   int64_t M;
   int N, K;
@@ -89,6 +90,8 @@ constexpr int kPairSpanBytes = 128 * 128;             // 16 KB: 128 rows x 128 K
 constexpr int kPairOpBytes = 2 * kPairSpanBytes;      // one operand's rows of a stage (32 KB)
 constexpr int kPairStageBytes = 2 * kPairOpBytes;     // A half + B half per CTA (64 KB)
 constexpr uint32_t kPairAccCols = 256;
+constexpr int kPairOutBox = 32 * 64 * 2;         // one epilogue warp's 32 rows x 64 columns (4 KB)
+constexpr int kPairOutBytes = 4 * 2 * kPairOutBox;  // four epilogue warps, two staging buffers each
 
 struct __align__(8) PairControl {
   uint64_t full[kPairStages], empty[kPairStages];
@@ -161,11 +164,13 @@ __device__ __forceinline__ void tile_coords(int64_t t, int m_tiles, int n_tiles,
 }
 
 __global__ void __launch_bounds__(kGemmThreads, 1)
-fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b, GemmParams p) {
+fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_constant__ CUtensorMap tm_b,
+                     const __grid_constant__ CUtensorMap tm_out, GemmParams p) {
   extern __shared__ __align__(1024) uint8_t smem[];
   // Same layout in both CTAs, so both take the same branch here.
   const bool aligned = (smem_u32(smem) & 1023u) == 0u;
-  PairControl& C = *reinterpret_cast<PairControl*>(smem + kPairStages * kPairStageBytes);
+  uint8_t* sOut = smem + kPairStages * kPairStageBytes;  // output staging of the TMA-store epilogue
+  PairControl& C = *reinterpret_cast<PairControl*>(sOut + kPairOutBytes);
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const uint32_t rank = cluster_ctarank();
   const bool leader = rank == 0;
@@ -194,6 +199,7 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
   if (warp == 4 && lane == 0) {
     prefetch_tensormap(&tm_a);
     prefetch_tensormap(&tm_b);
+    if (p.tma_out) prefetch_tensormap(&tm_out);
   }
   tc_fence_before();
   __syncthreads();
@@ -290,6 +296,11 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
     // ------------------------------------------------------------ epilogue (both CTAs)
     const int row = threadIdx.x;  // TMEM lane of this CTA: tile row 128 * rank + row
     const uint32_t lane_base = (uint32_t)(warp * 32) << 16;
+    // TMA-store epilogue: warp w stages its 32 rows of each 64-column group in a 128-byte-
+    // swizzled box (16-byte chunk c of row r at c ^ (r & 7)) and stores it with one TMA store;
+    // two buffers alternate, a buffer being reused once its store has read it.
+    const uint32_t out_stage = smem_u32(sOut) + (uint32_t)(warp * 2 * kPairOutBox);
+    uint32_t groups_stored = 0;
     int local = 0;
     for (int64_t t = pair; t < total_tiles; t += pairs, ++local) {
       const int buf = local & 1;
@@ -400,6 +411,34 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
 #pragma unroll
           for (int i = 0; i < 32; ++i) f[i] = fmaf(__shfl_sync(0xffffffffu, gate_l, i), f[i], res[i]);
         }
+        if (p.tma_out) {
+          const uint32_t stage = out_stage + (groups_stored & 1u) * kPairOutBox;
+          if ((c & 1) == 0) {
+            if (lane == 0) bulk_wait_group_read<1>();  // the store that last read this buffer
+            __syncwarp();
+          }
+          const uint32_t rowp = stage + (uint32_t)(lane * 128);
+#pragma unroll
+          for (int q = 0; q < 4; ++q) {
+            const int chunk = (c & 1) * 4 + q;
+            uint32_t w[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e) w[e] = cvt_bf16x2(f[8 * q + 2 * e], f[8 * q + 2 * e + 1]);
+            asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rowp + (uint32_t)((chunk ^ (lane & 7)) * 16)),
+                         "r"(w[0]), "r"(w[1]), "r"(w[2]), "r"(w[3])
+                         : "memory");
+          }
+          if (c & 1) {
+            fence_proxy_async_smem();
+            __syncwarp();
+            if (lane == 0) {  // rows past M and columns past N are clipped by the store
+              tma_store_2d(&tm_out, stage, n0 + 64 * (c >> 1), (int)(mt * 256 + rank * 128 + warp * 32));
+              bulk_commit_group();
+            }
+            ++groups_stored;
+          }
+          continue;
+        }
         if (row_ok && nc < p.N) {
           if (nc + 32 <= p.N && (p.N % 8) == 0) {
             // The output is written once: evict-first keeps the A and B panels in L2.
@@ -418,6 +457,10 @@ fp8_gemm_pair_kernel(const __grid_constant__ CUtensorMap tm_a, const __grid_cons
       if (lane == 0) mbar_arrive_cluster(mapa_shared(smem_u32(&C.acc_empty[buf]), 0));
     }
     if (p.qkv_peers != nullptr) __threadfence_system();  // the stores to peer buffers, before exit
+    if (p.tma_out) {
+      if (lane == 0) bulk_wait_group<0>();  // every output store has landed before the CTA exits
+      __syncwarp();
+    }
   }
   tc_fence_before();
   __syncthreads();
@@ -630,6 +673,27 @@ EncodeTiledFn encode_fn() {
   return fn;
 }
 
+// bf16 output [rows, cols] as a store target: 64-column x 32-row boxes, 128-byte swizzle.
+int make_out_map(CUtensorMap* map, void* base, uint64_t cols, uint64_t rows) {
+  EncodeTiledFn encode = encode_fn();
+  if (encode == nullptr) {
+    set_error("sb_fp8_gemm: cuTensorMapEncodeTiled is unavailable");
+    return SB_ERR_CUDA;
+  }
+  const cuuint64_t dims[2] = {cols, rows};
+  const cuuint64_t strides[1] = {cols * 2};
+  const cuuint32_t box[2] = {64, 32};
+  const cuuint32_t estr[2] = {1, 1};
+  CUresult r = encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides, box, estr,
+                      CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                      CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  if (r != CUDA_SUCCESS) {
+    set_error("sb_fp8_gemm: cuTensorMapEncodeTiled (output) failed (CUresult %d)", (int)r);
+    return SB_ERR_CUDA;
+  }
+  return SB_OK;
+}
+
 int make_map_u8(CUtensorMap* map, const void* base, uint64_t cols, uint64_t rows, uint32_t box_rows) {
   EncodeTiledFn encode = encode_fn();
   if (encode == nullptr) {
@@ -834,7 +898,13 @@ int launch_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, 
     p.shards = prod->shards;
     p.eps = prod->eps;
   }
-  const size_t smem = (size_t)kPairStages * kPairStageBytes + sizeof(PairControl);
+  // Plain and residual outputs with 16-byte rows go out through TMA stores.
+  CUtensorMap mo = ma;
+  if (prod == nullptr && N % 8 == 0 && ((uintptr_t)out % 16) == 0) {
+    if ((rc = make_out_map(&mo, out, (uint64_t)N, (uint64_t)M)) != SB_OK) return rc;
+    p.tma_out = 1;
+  }
+  const size_t smem = (size_t)kPairStages * kPairStageBytes + kPairOutBytes + sizeof(PairControl);
   cudaError_t err = cudaFuncSetAttribute(fp8_gemm_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: set smem");
   int ctas = num_ctas;
@@ -857,7 +927,7 @@ int launch_fp8_gemm(const uint8_t* a, const float* a_scale, int a_scale_stride, 
   attr[0].val.clusterDim.z = 1;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  err = cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel, ma, mb, p);
+  err = cudaLaunchKernelEx(&cfg, fp8_gemm_pair_kernel, ma, mb, mo, p);
   if (err != cudaSuccess) return cuda_error(err, "sb_fp8_gemm: cluster launch");
   SB_CHECK_LAUNCH("sb_fp8_gemm launch");
   return SB_OK;
