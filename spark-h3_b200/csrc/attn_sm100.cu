@@ -3,8 +3,8 @@
 // One CTA per (128-row query tile, head, batch).  Roles (384 threads):
 //   warps 0-3  softmax group 0: row r = TMEM lane r, key columns 0-63 of every tile
 //   warps 4-7  softmax group 1: row r = TMEM lane r, key columns 64-127 of every tile
-//   warp 8     TMA producer of Q and the K (or AK summary) tiles, 3 stages (2 on long sequences)
-//   warp 9     TMA producer of the V (or AV summary) tiles, 2 stages
+//   warp 8     TMA producer of Q and the K (or AK summary) tiles, 2 stages
+//   warp 9     TMA producer of the V (or AV summary) tiles, 3 stages (2 on long sequences)
 //   warp 10    tcgen05 issuer of S = Q K^T (one 128 x 64 product per group); owns TMEM
 //   warp 11    tcgen05 issuer of O += P V (one per group)
 // Issuing one tcgen05.mma occupies its thread for about as long as a third of the MMA's
@@ -33,7 +33,7 @@
 // Optional per-event clock trace of one CTA (compile with -DSB_TRACE; off in the product).
 #ifdef SB_TRACE
 namespace sb {
-__device__ long long g_trace[16][4096];
+__device__ long long g_trace[24][4096];
 __device__ int g_trace_cta;
 }
 #define SB_TRACE_POINT(on, ev, j) \
@@ -54,10 +54,19 @@ constexpr int kProducerWarp = 8;   // Q and K
 constexpr int kProducerVWarp = 9;  // V
 constexpr int kMmaWarp = 10;       // S issuer
 constexpr int kPvWarp = 11;        // P.V issuer
-constexpr int kKStages = 3;  // K ring depth when it fits; 2 on long sequences (below)
-constexpr int kVStages = 2;
+// Ring depths when they fit; 2 + 2 on long sequences (below).  Measured at config 1 (A/B in
+// one session, attention kernel): K 2 + V 3 27.75-27.98 ms, K 3 + V 2 28.15-28.24 ms.
+#ifndef SB_K_STAGES
+#define SB_K_STAGES 2
+#endif
+#ifndef SB_V_STAGES
+#define SB_V_STAGES 3
+#endif
+constexpr int kKStages = SB_K_STAGES;
+constexpr int kVStages = SB_V_STAGES;
+constexpr int kMaxStages = kKStages > kVStages ? kKStages : kVStages;
 constexpr uint32_t kSmemLimit = 227 * 1024;
-static_assert(kVStages == 2, "the P.V issue and the rescale wait index V stages by tile parity");
+static_assert(kKStages >= 2 && kVStages >= 2, "both rings need two stages for the long-sequence layout");
 constexpr int kTileBytes = 128 * 128 * 2;  // one 128 x 128 bf16 operand tile
 constexpr int kHalfBytes = 128 * 64 * 2;   // one 64-column half of it
 constexpr int kBoxBytes = 64 * 64 * 2;     // one TMA box (64 columns x 64 rows)
@@ -96,20 +105,22 @@ struct SmemLayout {
   uint32_t q, k, v;  // byte offsets from the 1024-aligned base (stages are consecutive)
   uint32_t ctrl, ebits, ubits, lm, glist;
   uint32_t total;
-  int k_stages;
+  int k_stages, v_stages;
 };
 
 // The per-sequence tables (route words, summary log-masses, granule list) grow with T; when
-// three K stages no longer fit beside them the ring drops to two.  With 64-key blocks that
+// three V stages no longer fit beside them the ring drops to two.  With 64-key blocks that
 // moves the longest accepted sequence from about 330k to about 660k tokens (128-key blocks:
 // about 500k to 990k).
-__host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int words_gran, int nb_pad, int k_stages) {
+__host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int words_gran, int nb_pad, int k_stages,
+                                                         int v_stages) {
   SmemLayout L;
   L.k_stages = k_stages;
+  L.v_stages = v_stages;
   L.q = 0;
   L.k = kTileBytes;
   L.v = L.k + k_stages * kTileBytes;
-  L.ctrl = L.v + kVStages * kTileBytes;
+  L.ctrl = L.v + v_stages * kTileBytes;
   L.ebits = L.ctrl + (uint32_t)((sizeof(Control) + 15) / 16 * 16);  // Control is small
   L.ubits = L.ebits + (uint32_t)((2 * words_blk * 4 + 15) / 16 * 16);  // every region 16-byte aligned
   L.lm = L.ubits + (uint32_t)((words_gran * 4 + 15) / 16 * 16);
@@ -119,8 +130,8 @@ __host__ __device__ inline SmemLayout smem_layout_stages(int words_blk, int word
 }
 
 __host__ __device__ inline SmemLayout smem_layout(int words_blk, int words_gran, int nb_pad) {
-  const SmemLayout L = smem_layout_stages(words_blk, words_gran, nb_pad, kKStages);
-  return L.total <= kSmemLimit ? L : smem_layout_stages(words_blk, words_gran, nb_pad, 2);
+  const SmemLayout L = smem_layout_stages(words_blk, words_gran, nb_pad, kKStages, kVStages);
+  return L.total <= kSmemLimit ? L : smem_layout_stages(words_blk, words_gran, nb_pad, 2, 2);
 }
 
 // 2^x on the FMA/ALU pipes (offloads the MUFU unit): round-to-nearest range reduction
@@ -199,7 +210,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       mbar_init(smem_u32(&C.bar_k_full[s]), 1);
       mbar_init(smem_u32(&C.bar_k_empty[s]), 1);
     }
-    for (int s = 0; s < kVStages; ++s) {
+    for (int s = 0; s < L.v_stages; ++s) {
       mbar_init(smem_u32(&C.bar_v_full[s]), 1);
       mbar_init(smem_u32(&C.bar_v_empty[s]), 1);
     }
@@ -317,7 +328,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     // K, V and the summaries are read again by every query tile of the head (evict last).
     if (lane == 0) {
       const bool is_k = warp == kProducerWarp;
-      const int stages = is_k ? L.k_stages : kVStages;
+      const int stages = is_k ? L.k_stages : L.v_stages;
       const CUtensorMap* exact_map = is_k ? &tm_k : &tm_v;
       const CUtensorMap* summ_map = is_k ? &tm_ak : &tm_av;
       const uint32_t s_base = is_k ? sK0 : sV0;
@@ -334,7 +345,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
                              once);
       }
       const int n_gran = C.exact_granules;
-      int armed[kKStages > kVStages ? kKStages : kVStages] = {};
+      int armed[kMaxStages] = {};
       int s = 0, use = 0;  // stage and how many times it has been filled before
       for (int j = 0; j < total_tiles; ++j) {
         int g0 = 0, g1 = 0;
@@ -394,7 +405,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
             ok = false;
             break;
           }
-          if (g == 0) SB_TRACE_POINT(trace, 12, j);
+          SB_TRACE_POINT(trace, g ? 18 : 12, j);
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
@@ -423,17 +434,19 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       constexpr uint32_t idesc_pv = idesc_bf16_f32(128, 128, true);
       const uint64_t vdesc0 = smem_desc_sw128(sV0, kHalfBytes, 1024);
       bool ok = true;
+      int vs = 0, vuse = 0;  // V stage and how many times it has been filled before
       for (int i = 0; ok && i < total_tiles; ++i) {
-        const int s = i & 1;  // S/P buffer (two in TMEM) and V stage (kVStages == 2)
+        const int s = i & 1;  // S/P buffer (two in TMEM)
         const uint32_t par = (i >> 1) & 1;
-        const uint64_t vdesc = vdesc0 + (uint64_t)((s * kTileBytes) >> 4);
-        if (!mbar_wait(smem_u32(&C.bar_v_full[s]), par, abort_flag, p.status, 203)) break;
+        const uint64_t vdesc = vdesc0 + (uint64_t)((vs * kTileBytes) >> 4);
+        if (!mbar_wait(smem_u32(&C.bar_v_full[vs]), (uint32_t)(vuse & 1), abort_flag, p.status, 203)) break;
+        SB_TRACE_POINT(trace, 16, i);
         for (int g = 0; g < 2; ++g) {
           if (!mbar_wait(smem_u32(&C.bar_p_full[g][s]), par, abort_flag, p.status, 202)) {
             ok = false;
             break;
           }
-          if (g == 0) SB_TRACE_POINT(trace, 4, i);
+          SB_TRACE_POINT(trace, g ? 17 : 4, i);
           tc_fence_after();
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)
@@ -442,8 +455,12 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
           tc_commit(smem_u32(&C.bar_pv_done[g][s]));
         }
         if (!ok) break;
-        tc_commit(smem_u32(&C.bar_v_empty[s]));
+        tc_commit(smem_u32(&C.bar_v_empty[vs]));
         SB_TRACE_POINT(trace, 5, i);
+        if (++vs == L.v_stages) {
+          vs = 0;
+          ++vuse;
+        }
       }
       tc_commit(smem_u32(&C.bar_o_final));
     }
@@ -471,7 +488,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     uint32_t w_cur = g_cur >= 0 ? ehalf[(g_cur >> gshift) >> 5] : 0u;
     bool ok = true;
     for (int j = 0; j < total_tiles; ++j) {
-      SB_TRACE_POINT(trace && tid == 0, 13, j);
+      SB_TRACE_POINT(trace && row == 0, grp ? 19 : 13, j);
       const int s = j & 1;
       const uint32_t par = (j >> 1) & 1;
       const bool exact = j < exact_tiles;
@@ -607,7 +624,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         for (int c = 0; c < 32; ++c) pk[c] = 0u;
       }
       l_run += (ps[0] + ps[1]) + (ps[2] + ps[3]);
-      SB_TRACE_POINT(trace && tid == 0, 15, j);
+      SB_TRACE_POINT(trace && row == 0, grp ? 20 : 15, j);
       tmem_st32(tmem + lane_base + s * 128 + s_col, pk);
       tmem_wait_st();
       tc_fence_before();
@@ -744,6 +761,6 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
 #ifdef SB_TRACE
 extern "C" int sb_trace_setup(int cta) { return (int)cudaMemcpyToSymbol(sb::g_trace_cta, &cta, sizeof(int)); }
 extern "C" int sb_trace_dump(long long* host) {
-  return (int)cudaMemcpyFromSymbol(host, sb::g_trace, sizeof(long long) * 16 * 4096);
+  return (int)cudaMemcpyFromSymbol(host, sb::g_trace, sizeof(long long) * 24 * 4096);
 }
 #endif

@@ -350,8 +350,8 @@ def _long_sequence_case(T: int, block: int, seed: int):
     return q, k, v, packed, ak, av, lm
 
 
-def test_long_sequence_two_stage_key_ring(cuda_device):
-    # 400,037 tokens in 64-token blocks: the per-sequence tables leave room for two K stages
+def test_long_sequence_two_stage_value_ring(cuda_device):
+    # 400,037 tokens in 64-token blocks: the per-sequence tables leave room for two V stages
     # only.  Rows of the first, a middle and the ragged last query tile are checked; the last
     # tile holds routed rows and the 37 dense-suffix rows past the last whole block.
     T, block = 400_037, 64
