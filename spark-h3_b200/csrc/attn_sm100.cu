@@ -39,9 +39,32 @@ __device__ int g_trace_cta;
 #define SB_TRACE_POINT(on, ev, j) \
   do { if ((on) && (j) < 4096) ::sb::g_trace[ev][j] = clock64(); } while (0)
 #define SB_TRACE_CTA() ((int)blockIdx.x == ::sb::g_trace_cta && blockIdx.y == 0 && blockIdx.z == 0)
+// Start and end (%globaltimer, ns) and SM of every CTA of the first 64k.
+namespace sb {
+__device__ unsigned long long g_cta_time[65536][3];
+}
+__device__ __forceinline__ unsigned long long sb_globaltimer() {
+  unsigned long long t;
+  asm volatile("mov.u64 %0, %globaltimer;" : "=l"(t));
+  return t;
+}
+__device__ __forceinline__ unsigned sb_smid() {
+  unsigned r;
+  asm volatile("mov.u32 %0, %smid;" : "=r"(r));
+  return r;
+}
+#define SB_CTA_TIME(slot)                                                                          \
+  do {                                                                                             \
+    const unsigned cta_ = blockIdx.x + gridDim.x * (blockIdx.y + gridDim.y * blockIdx.z);          \
+    if (cta_ < 65536u) {                                                                           \
+      ::sb::g_cta_time[cta_][slot] = sb_globaltimer();                                             \
+      if ((slot) == 0) ::sb::g_cta_time[cta_][2] = sb_smid();                                      \
+    }                                                                                              \
+  } while (0)
 #else
 #define SB_TRACE_POINT(on, ev, j) do { } while (0)
 #define SB_TRACE_CTA() false
+#define SB_CTA_TIME(slot) do { } while (0)
 #endif
 
 namespace sb {
@@ -202,6 +225,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   const int row0 = tile * 128;
   const int gshift = p.block == 128 ? 1 : 0;
   [[maybe_unused]] const bool trace = SB_TRACE_CTA();
+  if (threadIdx.x == 0) SB_CTA_TIME(0);
 
   // ---------------------------------------------------------------- setup
   if (tid == 0) {
@@ -683,6 +707,7 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     mbar_drain(smem_u32(&C.bar_o_final), 0);
     mbar_drain(smem_u32(&C.bar_s_final), 0);
     tmem_dealloc(tmem, kTmemCols);
+    if (lane == 0) SB_CTA_TIME(1);
   }
 }
 
@@ -762,5 +787,8 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
 extern "C" int sb_trace_setup(int cta) { return (int)cudaMemcpyToSymbol(sb::g_trace_cta, &cta, sizeof(int)); }
 extern "C" int sb_trace_dump(long long* host) {
   return (int)cudaMemcpyFromSymbol(host, sb::g_trace, sizeof(long long) * 24 * 4096);
+}
+extern "C" int sb_cta_time_dump(unsigned long long* host) {
+  return (int)cudaMemcpyFromSymbol(host, sb::g_cta_time, sizeof(unsigned long long) * 65536 * 3);
 }
 #endif
