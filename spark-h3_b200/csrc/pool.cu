@@ -278,15 +278,6 @@ pool_keys_summaries_kernel(const T* __restrict__ k, const T* __restrict__ v,
 // the CTAs in flight read whole token rows of consecutive blocks.
 constexpr int kHeadThreads = 256;
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"((uint32_t)__cvta_generic_to_shared(smem)),
-               "l"(gmem)
-               : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() { asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory"); }
-
 template <int D, int BLOCK>
 struct HeadSmem {
   static constexpr size_t kTile = (size_t)BLOCK * D * sizeof(__nv_bfloat16);

@@ -855,51 +855,81 @@ __global__ void __launch_bounds__(256) reblock_score_kernel(const __nv_bfloat16*
   }
 }
 
-// The same scores with two tokens per quad (tokens tk and tk + 32 of a 64-token tile, 128
-// threads per CTA): each direction element read from shared memory serves both tokens,
-// halving the shared-memory traffic that bounds the one-token form.
+// The same scores with the gathered feature rows staged in shared memory.  A CTA first
+// copies the ids of its tiles, then streams the rows of up to two tiles ahead into a
+// three-stage ring with cp.async (16-byte chunks, XOR-swizzled by row so that the eight quads
+// of a warp read distinct banks) while it scores the current tile out of shared memory: the
+// loads in flight no longer cost registers.  Two tokens per quad (tokens tk and tk + 32 of a
+// 64-token tile) share each direction element read from shared memory; the arithmetic is
+// score_tokens<P, 2>.
+constexpr int kScoreStages = 3;
+constexpr int kScoreRowBytes = kDim * 2;  // one bf16 feature row
+constexpr int kScoreStageBytes = 64 * kScoreRowBytes;
+constexpr int kScoreRingBytes = kScoreStages * kScoreStageBytes;
+
 template <int P>
-__global__ void __launch_bounds__(128) reblock_score2_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
+__global__ void __launch_bounds__(128) reblock_score3_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
                                                              TreeLevel lv, const int32_t* __restrict__ idx_in,
                                                              const float* __restrict__ dirs,
                                                              float* __restrict__ scores) {
-  static_assert(P >= 2 && (P & (P - 1)) == 0, "P is a power of two");
+  static_assert(P >= 2 && (P & (P - 1)) == 0 && P <= 16, "P is a power of two up to 16");
+  extern __shared__ __align__(16) uint8_t ring[];  // [kScoreStages][64 rows][256 bytes]
   __shared__ __align__(16) float2 sd[P / 2][kDim];
-  __shared__ int s_node[kScoreTiles];
+  __shared__ int s_ids[kScoreTiles][64];
+  __shared__ int s_tile[kScoreTiles], s_node[kScoreTiles], s_count;
   const int r = blockIdx.y;
   const int tiles = active / 64;
   const int tile0 = blockIdx.x * kScoreTiles;
   const int ntiles = min(kScoreTiles, tiles - tile0);
-  if (threadIdx.x < kScoreTiles) s_node[threadIdx.x] = threadIdx.x < ntiles ? lv.tiles[tile0 + threadIdx.x] : -1;
-  __syncthreads();
-  const int tk = threadIdx.x >> 2, t4 = threadIdx.x & 3;  // tokens tk and tk + 32 of a tile
+  const int tid = threadIdx.x;
   const __nv_bfloat16* Fr = F + (int64_t)r * N * kDim;
-  const int32_t* ir = idx_in + (int64_t)r * N;
-  auto fetch = [&](int tile, uint2 (&raw)[2][8]) {
-#pragma unroll
-    for (int t = 0; t < 2; ++t) {
-      const int id = ir[tile * 64 + tk + 32 * t];
-      const __nv_bfloat16* row = Fr + (int64_t)id * kDim;
-#pragma unroll
-      for (int j = 0; j < 8; ++j) raw[t][j] = __ldg(reinterpret_cast<const uint2*>(row + 4 * (t4 + 4 * j)));
+  const int32_t* ir = idx_in + (int64_t)r * N + (int64_t)tile0 * 64;
+  for (int c = tid; c < ntiles * 64; c += blockDim.x) cp_async4(&s_ids[c >> 6][c & 63], ir + c);
+  cp_async_commit();
+  if (tid == 0) {
+    int m = 0;
+    for (int i = 0; i < ntiles; ++i) {
+      const int node = lv.tiles[tile0 + i];
+      if (node >= 0) {
+        s_tile[m] = i;
+        s_node[m] = node;
+        ++m;
+      }
     }
+    s_count = m;
+  }
+  cp_async_wait<0>();
+  __syncthreads();
+  const int M = s_count;
+  if (M == 0) return;
+  // Rows of the k-th listed tile into stage k mod kScoreStages: 16 threads per row, eight
+  // rows per thread.  One commit group per call (empty past the end), so that the group
+  // count is the same for every thread and every call.
+  auto issue = [&](int k) {
+    if (k < M) {
+      const int* ids = s_ids[s_tile[k]];
+      uint8_t* st = ring + (k % kScoreStages) * kScoreStageBytes;
+      const int chunk = tid & 15;
+#pragma unroll
+      for (int q = 0; q < 8; ++q) {
+        const int row = (tid >> 4) + 8 * q;
+        cp_async16(st + row * kScoreRowBytes + ((chunk ^ (row & 15)) << 4), Fr + (int64_t)ids[row] * kDim + chunk * 8);
+      }
+    }
+    cp_async_commit();
   };
-  int i = 0;
-  while (i < ntiles && s_node[i] < 0) ++i;
-  if (i == ntiles) return;
-  uint2 cur[2][8], nxt[2][8];
-  fetch(tile0 + i, cur);
+  issue(0);
+  issue(1);
+  const int tk = tid >> 2, t4 = tid & 3;  // tokens tk and tk + 32 of a tile
   int loaded = -1, C = 2;
-  while (i < ntiles) {
-    const int node = s_node[i];
-    int next = i + 1;
-    while (next < ntiles && s_node[next] < 0) ++next;
-    if (next < ntiles) fetch(tile0 + next, nxt);
+  for (int k = 0; k < M; ++k) {
+    cp_async_wait<1>();  // tile k's group has landed: only the newest group, tile k + 1's, may be in flight
+    __syncthreads();     // every thread's rows are visible, and stage (k + 2) mod 3 (tile k - 1) is free
+    const int node = s_node[k];
     if (node != loaded) {
-      __syncthreads();
       C = lv.nodes[(int64_t)node * kNodeInts + 2];
       const float* nd = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
-      for (int e = threadIdx.x; e < (P / 2) * kDim; e += blockDim.x) {
+      for (int e = tid; e < (P / 2) * kDim; e += blockDim.x) {
         const int q = e / kDim, d = e % kDim;
         sd[q][d] = make_float2(2 * q < C - 1 ? nd[(2 * q) * kDim + d] : 0.f,
                                2 * q + 1 < C - 1 ? nd[(2 * q + 1) * kDim + d] : 0.f);
@@ -907,15 +937,23 @@ __global__ void __launch_bounds__(128) reblock_score2_kernel(const __nv_bfloat16
       __syncthreads();
       loaded = node;
     }
-    const int pos = (tile0 + i) * 64 + tk;
+    issue(k + 2);
+    const uint8_t* st = ring + (k % kScoreStages) * kScoreStageBytes;
+    uint2 raw[2][8];
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const int row = tk + 32 * t;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const int byte = 8 * (t4 + 4 * j);  // elements 4 (t4 + 4 j) .. +3 of the row
+        raw[t][j] = *reinterpret_cast<const uint2*>(st + row * kScoreRowBytes + (((byte >> 4) ^ (row & 15)) << 4) +
+                                                    (byte & 15));
+      }
+    }
+    const int pos = (tile0 + s_tile[k]) * 64 + tk;
     float* const outs[2] = {scores + ((int64_t)r * active + pos) * lv.S,
                             scores + ((int64_t)r * active + pos + 32) * lv.S};
-    score_tokens<P, 2>(cur, sd, t4, C, outs);
-#pragma unroll
-    for (int t = 0; t < 2; ++t)
-#pragma unroll
-      for (int j = 0; j < 8; ++j) cur[t][j] = nxt[t][j];
-    i = next;
+    score_tokens<P, 2>(raw, sd, t4, C, outs);
   }
 }
 
@@ -926,7 +964,7 @@ __global__ void __launch_bounds__(128) reblock_score2_kernel(const __nv_bfloat16
 constexpr int kRouteThreads = 512;
 constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kSortMax = 1024;
-constexpr int kUnroll = 4;
+constexpr int kUnroll = 8;
 
 __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int active, TreeLevel lv,
                                                                       const int32_t* __restrict__ idx_in,
@@ -1169,6 +1207,235 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
   }
   __syncthreads();
   if (tid < C && running[tid] != caps[tid] && status) atomicExch(status, 610);
+}
+
+// The root round's one node per row spread over a cluster of kRootCluster CTAs (the one-CTA
+// kernel leaves most SMs idle there: one CTA per row).  Every CTA takes a contiguous slice of
+// the node's tokens; the per-pass histograms of the slices are summed through distributed
+// shared memory, and every CTA derives the same cut from the sum.  The stable partition
+// offsets each CTA by the child counts of the lower-ranked slices, so keys, cuts and output
+// order are those of reblock_route_kernel's radix path exactly.
+constexpr int kRootCluster = 8;
+constexpr int kClusterMaxNodes = 16;  // internal proxy nodes per depth: fanout up to 32
+
+__global__ void __cluster_dims__(kRootCluster, 1, 1) __launch_bounds__(kRouteThreads)
+    reblock_route_cluster_kernel(int N, int active, TreeLevel lv, const int32_t* __restrict__ idx_in,
+                                 const float* __restrict__ scores, uint32_t* __restrict__ keys,
+                                 uint8_t* __restrict__ state, int32_t* __restrict__ idx_out,
+                                 int32_t* __restrict__ perm, int* __restrict__ status) {
+  __shared__ __align__(16) int hist[kClusterMaxNodes][256];   // this CTA's slice
+  __shared__ __align__(16) int total[kClusterMaxNodes][256];  // summed over the cluster
+  __shared__ int target[kClusterMaxNodes], ties[kClusterMaxNodes], need_ids[kClusterMaxNodes];
+  __shared__ uint32_t prefix[kClusterMaxNodes], id_prefix[kClusterMaxNodes];
+  __shared__ int any_ids;
+  __shared__ int warp_cnt[kRouteWarps][kMaxChildren];
+  __shared__ int warp_off[kRouteWarps][kMaxChildren];
+  __shared__ int running[kMaxChildren], child_off[kMaxChildren], slice_cnt[kMaxChildren];
+  const uint32_t crank = cluster_ctarank();
+  const int node = blockIdx.x / kRootCluster, r = blockIdx.y;
+  const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
+  const int start = tbl[0], n_node = tbl[1], C = tbl[2];
+  const int32_t* caps = tbl + 4;
+  const int chunk = (n_node + kRootCluster - 1) / kRootCluster;
+  const int lo = min(n_node, (int)crank * chunk);
+  const int n = min(n_node, lo + chunk) - lo;  // this CTA's slice: tokens [lo, lo + n) of the node
+  const int32_t* ids = idx_in + (int64_t)r * N + start + lo;
+  const float* sc = scores + ((int64_t)r * active + start + lo) * lv.S;
+  uint32_t* key = keys + (int64_t)r * active + start + lo;
+  uint8_t* st = state + (int64_t)r * active + start + lo;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  // total = the sum of every slice's hist over the first `bins` bins.  The first barrier
+  // publishes the slices' counts; the second keeps any CTA from clearing its counts for the
+  // next pass while another still reads them.
+  auto cluster_sum = [&](int bins) {
+    cluster_sync_all();
+    for (int e = tid; e < bins; e += kRouteThreads) {
+      const uint32_t a = smem_u32(&hist[0][0] + e);
+      int sum = 0;
+#pragma unroll
+      for (int k = 0; k < kRootCluster; ++k) sum += (int)ld_shared_cluster_u32(mapa_shared(a, (uint32_t)k));
+      (&total[0][0])[e] = sum;
+    }
+    cluster_sync_all();
+  };
+  // The cut of every node of this depth from the summed histogram (one thread per node).
+  auto pick = [&](int nd, int shift, uint32_t* pre, bool key_pass) {
+    if (tid < nd && (key_pass || need_ids[tid])) {
+      int cum = 0;
+      const int want = target[tid];
+      for (int bin = 0; bin < 256; ++bin) {
+        const int c = total[tid][bin];
+        if (cum + c >= want) {
+          pre[tid] |= (uint32_t)bin << shift;
+          target[tid] = want - cum;
+          if (key_pass) ties[tid] = c;
+          break;
+        }
+        cum += c;
+      }
+    }
+    __syncthreads();
+  };
+  for (int t = tid; t < n; t += kRouteThreads) st[t] = 0;
+  __syncthreads();
+  int depth_nodes = 1, first_heap = 0, span = C;
+  while (span > 1) {
+    const int nd = depth_nodes;
+    if (tid < nd) {
+      const int s0 = tid * span, mid = s0 + span / 2;
+      int lc = 0;
+      for (int c = s0; c < mid; ++c) lc += caps[c];
+      target[tid] = lc;
+      prefix[tid] = 0;
+      id_prefix[tid] = 0;
+    }
+    for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+      int hs[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int t = t0 + u * kRouteThreads;
+        hs[u] = t < n ? st[t] : 0;
+      }
+      float vs[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int t = t0 + u * kRouteThreads;
+        vs[u] = t < n ? sc[(int64_t)t * lv.S + hs[u]] : 0.f;
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int t = t0 + u * kRouteThreads;
+        if (t < n) key[t] = order_key(vs[u]);
+      }
+    }
+    __syncthreads();
+    // radix select on the score key, most significant byte first
+    for (int pass = 0; pass < 4; ++pass) {
+      const int shift = 24 - 8 * pass;
+      for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+      __syncthreads();
+      for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+        uint32_t ks[kUnroll];
+        int js[kUnroll];
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int t = t0 + u * kRouteThreads;
+          js[u] = t < n ? st[t] - first_heap : -1;
+          ks[u] = t < n ? key[t] : 0u;
+        }
+#pragma unroll
+        for (int u = 0; u < kUnroll; ++u) {
+          const int j = js[u];
+          if (j >= 0 && (pass == 0 || (ks[u] >> (shift + 8)) == (prefix[j] >> (shift + 8))))
+            atomicAdd(&hist[j][(ks[u] >> shift) & 255], 1);
+        }
+      }
+      cluster_sum(nd * 256);
+      pick(nd, shift, prefix, true);
+    }
+    if (tid == 0) {
+      int any = 0;
+      for (int j = 0; j < nd; ++j) {
+        need_ids[j] = target[j] < ties[j] ? 1 : 0;
+        any |= need_ids[j];
+      }
+      any_ids = any;
+    }
+    __syncthreads();
+    if (any_ids) {  // the same in every CTA: it derives from the summed histograms
+      // equal scores at the cut: the lowest token ids among them go left
+      for (int pass = 0; pass < 4; ++pass) {
+        const int shift = 24 - 8 * pass;
+        for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+        __syncthreads();
+        for (int t = tid; t < n; t += kRouteThreads) {
+          const int j = st[t] - first_heap;
+          if (!need_ids[j] || key[t] != prefix[j]) continue;
+          const uint32_t id = (uint32_t)ids[t];
+          if (pass == 0 || (id >> (shift + 8)) == (id_prefix[j] >> (shift + 8)))
+            atomicAdd(&hist[j][(id >> shift) & 255], 1);
+        }
+        cluster_sum(nd * 256);
+        pick(nd, shift, id_prefix, false);
+      }
+    }
+    for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+      int hs[kUnroll];
+      uint32_t ks[kUnroll];
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int t = t0 + u * kRouteThreads;
+        hs[u] = t < n ? st[t] : 0;
+        ks[u] = t < n ? key[t] : 0u;
+      }
+#pragma unroll
+      for (int u = 0; u < kUnroll; ++u) {
+        const int t = t0 + u * kRouteThreads;
+        if (t >= n) continue;
+        const int j = hs[u] - first_heap;
+        const bool left = ks[u] < prefix[j] ||
+                          (ks[u] == prefix[j] && (!need_ids[j] || (uint32_t)ids[t] <= id_prefix[j]));
+        st[t] = (uint8_t)(left ? 2 * hs[u] + 1 : 2 * hs[u] + 2);
+      }
+    }
+    __syncthreads();
+    first_heap += depth_nodes;
+    depth_nodes *= 2;
+    span /= 2;
+  }
+  // stable partition by child label; this slice starts after the lower-ranked slices' tokens
+  // of each label
+  const int label_base = C - 1;
+  for (int c = tid; c < C; c += kRouteThreads) slice_cnt[c] = 0;
+  __syncthreads();
+  for (int w0 = tid - lane; w0 < n; w0 += kRouteThreads) {  // warp-uniform trip count
+    const int t = w0 + lane;
+    const int label = t < n ? st[t] - label_base : -1;
+    const unsigned peers = __match_any_sync(kFull, label);
+    if (label >= 0 && lane == __ffs(peers) - 1) atomicAdd(&slice_cnt[label], __popc(peers));
+  }
+  cluster_sync_all();
+  if (tid < C) {
+    int off = 0;
+    for (int c = 0; c < tid; ++c) off += caps[c];
+    child_off[tid] = off;
+    const uint32_t a = smem_u32(&slice_cnt[tid]);
+    int before = 0;
+    for (uint32_t k = 0; k < crank; ++k) before += (int)ld_shared_cluster_u32(mapa_shared(a, k));
+    running[tid] = before;
+  }
+  cluster_sync_all();  // no CTA reads slice_cnt any more; running and child_off are set
+  int32_t* out_next = idx_out + (int64_t)r * N + start;
+  int32_t* out_leaf = perm + (int64_t)r * N + start;
+  const unsigned lt = (1u << lane) - 1u;
+  for (int c0 = 0; c0 < n; c0 += kRouteThreads) {
+    for (int c = lane; c < C; c += 32) warp_cnt[warp][c] = 0;
+    __syncwarp();
+    const int t = c0 + tid;
+    const bool valid = t < n;
+    const int label = valid ? st[t] - label_base : -1;
+    const int id = valid ? ids[t] : 0;
+    const unsigned peers = __match_any_sync(kFull, label);
+    const int rnk = __popc(peers & lt);
+    if (valid && rnk == 0) warp_cnt[warp][label] = __popc(peers);
+    __syncthreads();
+    if (tid < C) {
+      int base = running[tid];
+      for (int w = 0; w < kRouteWarps; ++w) {
+        warp_off[w][tid] = base;
+        base += warp_cnt[w][tid];
+      }
+      running[tid] = base;
+    }
+    __syncthreads();
+    if (valid) {
+      const int dst = child_off[label] + warp_off[warp][label] + rnk;
+      (caps[label] == 64 ? out_leaf : out_next)[dst] = id;
+    }
+  }
+  __syncthreads();
+  // the last slice ends every child: its running counts are the whole node's
+  if (crank == kRootCluster - 1 && tid < C && running[tid] != caps[tid] && status) atomicExch(status, 610);
 }
 
 __global__ void reblock_inverse_kernel(const int32_t* __restrict__ perm, int N, int64_t total,
@@ -1504,6 +1771,11 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   const int proxy_smem = (int)sizeof(ProxySmem);
   cudaError_t err = cudaFuncSetAttribute(reblock_proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, proxy_smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
+  for (const void* fn : {(const void*)reblock_score3_kernel<2>, (const void*)reblock_score3_kernel<4>,
+                         (const void*)reblock_score3_kernel<8>, (const void*)reblock_score3_kernel<16>}) {
+    err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kScoreRingBytes);
+    if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
+  }
   int cur = 0;
   for (int l = 0; l < L; ++l) {
     const int32_t* lh = plan_host + kPlanHeader + kLevelInts * l;
@@ -1512,17 +1784,26 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
     SB_CHECK_LAUNCH("sb_reblock_tree: proxy");
     const dim3 sgrid(ceil_div(active / 64, kScoreTiles), rows);
     switch (lv.P) {
-      case 2: reblock_score_kernel<2><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
-      case 4: reblock_score_kernel<4><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
-      case 8: reblock_score2_kernel<8><<<sgrid, 128, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
-      case 16: reblock_score2_kernel<16><<<sgrid, 128, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
+      case 2: reblock_score3_kernel<2><<<sgrid, 128, kScoreRingBytes, s>>>(F, tokens, active, lv, idx[cur], dirs,
+                                                                            scores); break;
+      case 4: reblock_score3_kernel<4><<<sgrid, 128, kScoreRingBytes, s>>>(F, tokens, active, lv, idx[cur], dirs,
+                                                                            scores); break;
+      case 8: reblock_score3_kernel<8><<<sgrid, 128, kScoreRingBytes, s>>>(F, tokens, active, lv, idx[cur], dirs,
+                                                                            scores); break;
+      case 16: reblock_score3_kernel<16><<<sgrid, 128, kScoreRingBytes, s>>>(F, tokens, active, lv, idx[cur], dirs,
+                                                                              scores); break;
       case 32: reblock_score_kernel<32><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       case 64: reblock_score_kernel<64><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       default: set_error("sb_reblock_tree: bad plan fanout %d", lv.P); return SB_ERR_INVALID;
     }
     SB_CHECK_LAUNCH("sb_reblock_tree: scores");
-    reblock_route_kernel<<<dim3(lv.count, rows), kRouteThreads, 0, s>>>(tokens, active, lv, idx[cur], scores, keys,
-                                                                         state, idx[cur ^ 1], perm, status);
+    const int32_t* first = plan_host + lh[1];  // the level's first node record (start, tokens, children)
+    if (lv.count == 1 && first[1] > kSortMax && first[2] <= 2 * kClusterMaxNodes)
+      reblock_route_cluster_kernel<<<dim3(kRootCluster, rows), kRouteThreads, 0, s>>>(
+          tokens, active, lv, idx[cur], scores, keys, state, idx[cur ^ 1], perm, status);
+    else
+      reblock_route_kernel<<<dim3(lv.count, rows), kRouteThreads, 0, s>>>(tokens, active, lv, idx[cur], scores, keys,
+                                                                           state, idx[cur ^ 1], perm, status);
     SB_CHECK_LAUNCH("sb_reblock_tree: route");
     cur ^= 1;
   }
