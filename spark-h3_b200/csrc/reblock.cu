@@ -977,13 +977,13 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
   __shared__ __align__(16) uint8_t scratch[32 * 256 * 4];  // histograms, or the sort arrays
   __shared__ int target[32], ties[32], need_ids[32], seg[32];
   __shared__ uint32_t prefix[32], id_prefix[32];
+  __shared__ unsigned long long cut[32];  // small nodes: the key of the target-th smallest token
   __shared__ int any_ids;
   __shared__ int warp_cnt[kRouteWarps][kMaxChildren];
   __shared__ int warp_off[kRouteWarps][kMaxChildren];
   __shared__ int running[kMaxChildren], child_off[kMaxChildren];
   int(*hist)[256] = reinterpret_cast<int(*)[256]>(scratch);
   unsigned long long* sk = reinterpret_cast<unsigned long long*>(scratch);
-  int* sp = reinterpret_cast<int*>(scratch + kSortMax * 8);
   const int node = blockIdx.x, r = blockIdx.y;
   const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
   const int start = tbl[0], n = tbl[1], C = tbl[2];
@@ -1012,7 +1012,13 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
       id_prefix[tid] = 0;
     }
     if (small) {
-      for (int e = tid; e < n2; e += kRouteThreads) {
+      // (proxy node, score key, token id) as one unique 64-bit key per token; the sort only
+      // has to find, per proxy node, the key of its target-th smallest token (the cut), and
+      // every token then compares its own key with its node's cut.
+      unsigned long long mine[kSortMax / kRouteThreads];
+#pragma unroll
+      for (int q = 0; q < kSortMax / kRouteThreads; ++q) {
+        const int e = tid + q * kRouteThreads;
         unsigned long long k64 = ~0ull;
         if (e < n) {
           const int h = st[e];
@@ -1020,31 +1026,42 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
           k64 = ((unsigned long long)(h - first_heap) << 57) | ((unsigned long long)kk << 25) |
                 (unsigned long long)(uint32_t)ids[e];
         }
-        sk[e] = k64;
-        sp[e] = e;
+        mine[q] = k64;
+        if (e < n2) sk[e] = k64;
       }
       __syncthreads();
-      for (int k = 2; k <= n2; k <<= 1)
-        for (int j = k >> 1; j > 0; j >>= 1) {
-          for (int i = tid; i < n2; i += kRouteThreads) {
-            const int ixj = i ^ j;
-            if (ixj > i) {
-              const unsigned long long a = sk[i], b = sk[ixj];
+      // Bitonic sort, one compare-exchange per thread and step: only the first n2 / 2 threads
+      // (at least one warp) take part, synchronised by a named barrier of their own.
+      const int pairs = n2 >> 1;
+      const int sorters = pairs < 32 ? 32 : pairs;
+      if (tid < sorters) {
+        for (int k = 2; k <= n2; k <<= 1)
+          for (int j = k >> 1; j > 0; j >>= 1) {
+            if (tid < pairs) {
+              const int i = ((tid & ~(j - 1)) << 1) | (tid & (j - 1));  // bit j of i is clear
+              const unsigned long long a = sk[i], b = sk[i | j];
               if ((a > b) == ((i & k) == 0)) {
                 sk[i] = b;
-                sk[ixj] = a;
-                const int pa = sp[i];
-                sp[i] = sp[ixj];
-                sp[ixj] = pa;
+                sk[i | j] = a;
               }
             }
+            if (sorters == 32)
+              __syncwarp();
+            else
+              asm volatile("bar.sync 1, %0;" ::"r"(sorters) : "memory");
           }
-          __syncthreads();
+      }
+      __syncthreads();
+      if (tid < nd) cut[tid] = target[tid] > 0 ? sk[seg[tid] + target[tid] - 1] : 0ull;
+      __syncthreads();
+#pragma unroll
+      for (int q = 0; q < kSortMax / kRouteThreads; ++q) {
+        const int e = tid + q * kRouteThreads;
+        if (e < n) {
+          const int j = (int)(mine[q] >> 57);
+          const int hnode = first_heap + j;
+          st[e] = (uint8_t)(target[j] > 0 && mine[q] <= cut[j] ? 2 * hnode + 1 : 2 * hnode + 2);
         }
-      for (int e = tid; e < n; e += kRouteThreads) {
-        const int j = (int)(sk[e] >> 57);
-        const int hnode = first_heap + j;
-        st[sp[e]] = (uint8_t)(e - seg[j] < target[j] ? 2 * hnode + 1 : 2 * hnode + 2);
       }
       __syncthreads();
     } else {
