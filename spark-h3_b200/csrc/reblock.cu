@@ -966,7 +966,8 @@ constexpr int kRouteWarps = kRouteThreads / 32;
 constexpr int kSortMax = 1024;
 constexpr int kUnroll = 8;
 
-__global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int active, TreeLevel lv,
+template <int THREADS, bool RADIX>
+__global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int active, TreeLevel lv,
                                                                       const int32_t* __restrict__ idx_in,
                                                                       const float* __restrict__ scores,
                                                                       uint32_t* __restrict__ keys,
@@ -974,13 +975,14 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
                                                                       int32_t* __restrict__ idx_out,
                                                                       int32_t* __restrict__ perm,
                                                                       int* __restrict__ status) {
-  __shared__ __align__(16) uint8_t scratch[32 * 256 * 4];  // histograms, or the sort arrays
+  // radix histograms (32 nodes x 256 digits), or the sort keys
+  __shared__ __align__(16) uint8_t scratch[RADIX ? 32 * 256 * 4 : kSortMax * 8];
   __shared__ int target[32], ties[32], need_ids[32], seg[32];
   __shared__ uint32_t prefix[32], id_prefix[32];
   __shared__ unsigned long long cut[32];  // small nodes: the key of the target-th smallest token
   __shared__ int any_ids;
-  __shared__ int warp_cnt[kRouteWarps][kMaxChildren];
-  __shared__ int warp_off[kRouteWarps][kMaxChildren];
+  __shared__ int warp_cnt[(THREADS / 32)][kMaxChildren];
+  __shared__ int warp_off[(THREADS / 32)][kMaxChildren];
   __shared__ int running[kMaxChildren], child_off[kMaxChildren];
   int(*hist)[256] = reinterpret_cast<int(*)[256]>(scratch);
   unsigned long long* sk = reinterpret_cast<unsigned long long*>(scratch);
@@ -994,9 +996,13 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
   uint8_t* st = state + (int64_t)r * active + start;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const bool small = n <= kSortMax;
+  if (!RADIX && !small) {  // the launcher sends larger nodes to the radix form; refuse uniformly
+    if (threadIdx.x == 0 && status) atomicExch(status, 611);
+    return;
+  }
   int n2 = 1;
   while (n2 < n) n2 <<= 1;
-  for (int t = tid; t < n; t += kRouteThreads) st[t] = 0;
+  for (int t = tid; t < n; t += THREADS) st[t] = 0;
   __syncthreads();
   int depth_nodes = 1, first_heap = 0, span = C;
   while (span > 1) {
@@ -1015,10 +1021,10 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
       // (proxy node, score key, token id) as one unique 64-bit key per token; the sort only
       // has to find, per proxy node, the key of its target-th smallest token (the cut), and
       // every token then compares its own key with its node's cut.
-      unsigned long long mine[kSortMax / kRouteThreads];
+      unsigned long long mine[kSortMax / THREADS];
 #pragma unroll
-      for (int q = 0; q < kSortMax / kRouteThreads; ++q) {
-        const int e = tid + q * kRouteThreads;
+      for (int q = 0; q < kSortMax / THREADS; ++q) {
+        const int e = tid + q * THREADS;
         unsigned long long k64 = ~0ull;
         if (e < n) {
           const int h = st[e];
@@ -1033,12 +1039,12 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
       // Bitonic sort, one compare-exchange per thread and step: only the first n2 / 2 threads
       // (at least one warp) take part, synchronised by a named barrier of their own.
       const int pairs = n2 >> 1;
-      const int sorters = pairs < 32 ? 32 : pairs;
+      const int sorters = pairs < 32 ? 32 : (pairs < THREADS ? pairs : THREADS);
       if (tid < sorters) {
         for (int k = 2; k <= n2; k <<= 1)
           for (int j = k >> 1; j > 0; j >>= 1) {
-            if (tid < pairs) {
-              const int i = ((tid & ~(j - 1)) << 1) | (tid & (j - 1));  // bit j of i is clear
+            for (int p = tid; p < pairs; p += THREADS) {
+              const int i = ((p & ~(j - 1)) << 1) | (p & (j - 1));  // bit j of i is clear
               const unsigned long long a = sk[i], b = sk[i | j];
               if ((a > b) == ((i & k) == 0)) {
                 sk[i] = b;
@@ -1055,8 +1061,8 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
       if (tid < nd) cut[tid] = target[tid] > 0 ? sk[seg[tid] + target[tid] - 1] : 0ull;
       __syncthreads();
 #pragma unroll
-      for (int q = 0; q < kSortMax / kRouteThreads; ++q) {
-        const int e = tid + q * kRouteThreads;
+      for (int q = 0; q < kSortMax / THREADS; ++q) {
+        const int e = tid + q * THREADS;
         if (e < n) {
           const int j = (int)(mine[q] >> 57);
           const int hnode = first_heap + j;
@@ -1064,23 +1070,23 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
         }
       }
       __syncthreads();
-    } else {
-      for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+    } else if constexpr (RADIX) {
+      for (int t0 = tid; t0 < n; t0 += kUnroll * THREADS) {
         int hs[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const int t = t0 + u * kRouteThreads;
+          const int t = t0 + u * THREADS;
           hs[u] = t < n ? st[t] : 0;
         }
         float vs[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const int t = t0 + u * kRouteThreads;
+          const int t = t0 + u * THREADS;
           vs[u] = t < n ? sc[(int64_t)t * lv.S + hs[u]] : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const int t = t0 + u * kRouteThreads;
+          const int t = t0 + u * THREADS;
           if (t < n) key[t] = order_key(vs[u]);
         }
       }
@@ -1088,14 +1094,14 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
       // radix select on the score key, most significant byte first
       for (int pass = 0; pass < 4; ++pass) {
         const int shift = 24 - 8 * pass;
-        for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+        for (int e = tid; e < nd * 256; e += THREADS) hist[e >> 8][e & 255] = 0;
         __syncthreads();
-        for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+        for (int t0 = tid; t0 < n; t0 += kUnroll * THREADS) {
           uint32_t ks[kUnroll];
           int js[kUnroll];
 #pragma unroll
           for (int u = 0; u < kUnroll; ++u) {
-            const int t = t0 + u * kRouteThreads;
+            const int t = t0 + u * THREADS;
             js[u] = t < n ? st[t] - first_heap : -1;
             ks[u] = t < n ? key[t] : 0u;
           }
@@ -1135,9 +1141,9 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
         // equal scores at the cut: the lowest token ids among them go left
         for (int pass = 0; pass < 4; ++pass) {
           const int shift = 24 - 8 * pass;
-          for (int e = tid; e < nd * 256; e += kRouteThreads) hist[e >> 8][e & 255] = 0;
+          for (int e = tid; e < nd * 256; e += THREADS) hist[e >> 8][e & 255] = 0;
           __syncthreads();
-          for (int t = tid; t < n; t += kRouteThreads) {
+          for (int t = tid; t < n; t += THREADS) {
             const int j = st[t] - first_heap;
             if (!need_ids[j] || key[t] != prefix[j]) continue;
             const uint32_t id = (uint32_t)ids[t];
@@ -1160,18 +1166,18 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
           __syncthreads();
         }
       }
-      for (int t0 = tid; t0 < n; t0 += kUnroll * kRouteThreads) {
+      for (int t0 = tid; t0 < n; t0 += kUnroll * THREADS) {
         int hs[kUnroll];
         uint32_t ks[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const int t = t0 + u * kRouteThreads;
+          const int t = t0 + u * THREADS;
           hs[u] = t < n ? st[t] : 0;
           ks[u] = t < n ? key[t] : 0u;
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
-          const int t = t0 + u * kRouteThreads;
+          const int t = t0 + u * THREADS;
           if (t >= n) continue;
           const int j = hs[u] - first_heap;
           const bool left = ks[u] < prefix[j] ||
@@ -1197,7 +1203,7 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
   int32_t* out_next = idx_out + (int64_t)r * N + start;
   int32_t* out_leaf = perm + (int64_t)r * N + start;
   const unsigned lt = (1u << lane) - 1u;
-  for (int c0 = 0; c0 < n; c0 += kRouteThreads) {
+  for (int c0 = 0; c0 < n; c0 += THREADS) {
     for (int c = lane; c < C; c += 32) warp_cnt[warp][c] = 0;
     __syncwarp();
     const int t = c0 + tid;
@@ -1210,7 +1216,7 @@ __global__ void __launch_bounds__(kRouteThreads) reblock_route_kernel(int N, int
     __syncthreads();
     if (tid < C) {
       int base = running[tid];
-      for (int w = 0; w < kRouteWarps; ++w) {
+      for (int w = 0; w < (THREADS / 32); ++w) {
         warp_off[w][tid] = base;
         base += warp_cnt[w][tid];
       }
@@ -1751,6 +1757,13 @@ extern "C" int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, in
   return length;
 }
 
+// The largest node of a plan level (lh: the level's header in the plan).
+static int level_max_tokens(const int32_t* plan, const int32_t* lh) {
+  int most = 0;
+  for (int j = 0; j < lh[0]; ++j) most = std::max(most, plan[lh[1] + (int64_t)j * kNodeInts + 1]);
+  return most;
+}
+
 extern "C" int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows) {
   SB_CHECK_ARG(plan && rows > 0, "sb_reblock_workspace_bytes: bad arguments");
   return (int64_t)workspace_layout(plan, rows).total;
@@ -1818,9 +1831,12 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
     if (lv.count == 1 && first[1] > kSortMax && first[2] <= 2 * kClusterMaxNodes)
       reblock_route_cluster_kernel<<<dim3(kRootCluster, rows), kRouteThreads, 0, s>>>(
           tokens, active, lv, idx[cur], scores, keys, state, idx[cur ^ 1], perm, status);
+    else if (level_max_tokens(plan_host, lh) <= kSortMax)  // every node sorts: 128-thread CTAs
+      reblock_route_kernel<128, false><<<dim3(lv.count, rows), 128, 0, s>>>(tokens, active, lv, idx[cur], scores,
+                                                                            keys, state, idx[cur ^ 1], perm, status);
     else
-      reblock_route_kernel<<<dim3(lv.count, rows), kRouteThreads, 0, s>>>(tokens, active, lv, idx[cur], scores, keys,
-                                                                           state, idx[cur ^ 1], perm, status);
+      reblock_route_kernel<kRouteThreads, true><<<dim3(lv.count, rows), kRouteThreads, 0, s>>>(
+          tokens, active, lv, idx[cur], scores, keys, state, idx[cur ^ 1], perm, status);
     SB_CHECK_LAUNCH("sb_reblock_tree: route");
     cur ^= 1;
   }
