@@ -457,13 +457,21 @@ struct TreeLevel {
 // nodes of one depth spread over the warps; directions are written in heap order.
 constexpr int kProxyThreads = 128;
 
+// act (the landmark weights each internal node of a depth passes down, two depths) comes last
+// and is sized per level: [2][max(1, fanout / 2)][kLandmarks] ints.
 struct ProxySmem {
   __nv_bfloat16 x[kLandmarks][kDim];
   float n[kLandmarks][kDim];
   float dist[kLandmarks][kLandmarks + 1];
-  int act[2][kLandmarks][kLandmarks];
   int id[kLandmarks], w[kLandmarks];
+  int act[1];
 };
+
+__host__ __device__ constexpr int proxy_act_rows(int fanout) { return fanout / 2 > 1 ? fanout / 2 : 1; }
+
+inline size_t proxy_smem_bytes(int fanout) {
+  return offsetof(ProxySmem, act) + sizeof(int) * 2 * proxy_act_rows(fanout) * kLandmarks;
+}
 
 // Canonical dot products with four threads per 128-vector: thread t4 of the group holds the
 // lane groups l = t4 + 4j (j = 0..7), so the butterfly's offsets 16, 8 and 4 pair lane groups
@@ -506,12 +514,14 @@ __device__ __forceinline__ void quad_unit(float (&x)[8][4]) {
     for (int e = 0; e < 4; ++e) x[j][e] = __fdiv_rn(x[j][e], den);
 }
 
-__global__ void __launch_bounds__(kProxyThreads) reblock_proxy_kernel(const __nv_bfloat16* __restrict__ F, int N,
+__global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const __nv_bfloat16* __restrict__ F, int N,
                                                                        int active, TreeLevel lv,
                                                                        const int32_t* __restrict__ idx_in,
                                                                        float* __restrict__ dirs) {
   extern __shared__ __align__(16) uint8_t smem_raw[];
   ProxySmem& S = *reinterpret_cast<ProxySmem*>(smem_raw);
+  const int act_rows = proxy_act_rows(lv.P);
+  auto act = [&](int buf, int j) -> int* { return S.act + (buf * act_rows + j) * kLandmarks; };
   const int node = blockIdx.x, r = blockIdx.y;
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int32_t* tbl = lv.nodes + (int64_t)node * kNodeInts;
@@ -561,7 +571,7 @@ __global__ void __launch_bounds__(kProxyThreads) reblock_proxy_kernel(const __nv
       if (t4 == 0) S.dist[i][k] = d;
     }
   }
-  if (tid < kLandmarks) S.act[0][0][tid] = S.w[tid];
+  if (tid < kLandmarks) act(0, 0)[tid] = S.w[tid];
   __syncthreads();
   float* out = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
   int cur = 0, depth_nodes = 1, first_heap = 0, span = C;
@@ -572,7 +582,7 @@ __global__ void __launch_bounds__(kProxyThreads) reblock_proxy_kernel(const __nv
       int lc = 0, rc = 0;
       for (int c = s0; c < mid; ++c) lc += caps[c];
       for (int c = mid; c < s1; ++c) rc += caps[c];
-      const int aw = S.act[cur][j][lane];
+      const int aw = act(cur, j)[lane];
       const unsigned vmask = __ballot_sync(kFull, aw > 0);
       int first = vmask ? __ffs(vmask) - 1 : 0, second = first;
       if (__popc(vmask) >= 2) {
@@ -654,8 +664,8 @@ __global__ void __launch_bounds__(kProxyThreads) reblock_proxy_kernel(const __nv
       for (int e = 0; e < 4; ++e) dir[e] = __fsub_rn(ur[e], ul[e]);
       *reinterpret_cast<float4*>(out + (int64_t)hnode * kDim + 4 * lane) = make_float4(dir[0], dir[1], dir[2], dir[3]);
       if (span > 2) {
-        S.act[cur ^ 1][2 * j][lane] = lw;
-        S.act[cur ^ 1][2 * j + 1][lane] = rw;
+        act(cur ^ 1, 2 * j)[lane] = lw;
+        act(cur ^ 1, 2 * j + 1)[lane] = rw;
       }
     }
     __syncthreads();
@@ -1798,8 +1808,8 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   reblock_root_kernel<<<rows, 1024, 0, s>>>(F, tokens, active, root_order, reinterpret_cast<float*>(keys), idx[0],
                                             perm, L == 0 ? 1 : 0);
   SB_CHECK_LAUNCH("sb_reblock_tree: root");
-  const int proxy_smem = (int)sizeof(ProxySmem);
-  cudaError_t err = cudaFuncSetAttribute(reblock_proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, proxy_smem);
+  cudaError_t err = cudaFuncSetAttribute(reblock_proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                         (int)proxy_smem_bytes(kMaxChildren));
   if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
   for (const void* fn : {(const void*)reblock_score3_kernel<2>, (const void*)reblock_score3_kernel<4>,
                          (const void*)reblock_score3_kernel<8>, (const void*)reblock_score3_kernel<16>}) {
@@ -1810,7 +1820,8 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   for (int l = 0; l < L; ++l) {
     const int32_t* lh = plan_host + kPlanHeader + kLevelInts * l;
     TreeLevel lv{plan_device + lh[1], plan_device + lh[2], lh[0], lh[3], lh[4]};
-    reblock_proxy_kernel<<<dim3(lv.count, rows), kProxyThreads, proxy_smem, s>>>(F, tokens, active, lv, idx[cur], dirs);
+    reblock_proxy_kernel<<<dim3(lv.count, rows), kProxyThreads, proxy_smem_bytes(lv.P), s>>>(F, tokens, active, lv,
+                                                                                              idx[cur], dirs);
     SB_CHECK_LAUNCH("sb_reblock_tree: proxy");
     const dim3 sgrid(ceil_div(active / 64, kScoreTiles), rows);
     switch (lv.P) {
