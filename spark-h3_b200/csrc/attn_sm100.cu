@@ -106,6 +106,15 @@ constexpr float kRescaleThreshold = 8.0f;  // log2 units: lazy O rescale
 #endif
 constexpr int kPolyEvery = SB_POLY_EVERY;
 
+// Bits [a, b) of a 32-bit word, clamped to [0, 32).
+__device__ __forceinline__ uint32_t range_bits(int a, int b) {
+  a = max(a, 0);
+  b = min(b, 32);
+  if (a >= b) return 0u;
+  const uint32_t upto_b = b == 32 ? 0xffffffffu : ((1u << b) - 1u);
+  return upto_b & ~((1u << a) - 1u);
+}
+
 struct __align__(8) Control {
   uint64_t bar_q_full;
   uint64_t bar_k_full[kKStages], bar_k_empty[kKStages];
@@ -262,7 +271,21 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     prefetch_tensormap(&tm_ak);
     prefetch_tensormap(&tm_av);
   }
-  // Exact block sets of the two 64-row halves (block units).
+  // LM * log2(e) of every key block: the copies are issued first, so their latency overlaps
+  // the route words below.
+  {
+    const bool any_routed = row0 < p.query_tokens && p.lm != nullptr;  // summaries present
+    const int lm_end = any_routed ? p.NB : 0;
+    for (int e = tid; e < nb_pad; e += kThreads) {
+      if (e < lm_end)
+        cp_async4(lm_s + e, p.lm + ((int64_t)b * p.H + h) * p.NB + e);
+      else
+        lm_s[e] = 0.f;
+    }
+    cp_async_commit();
+  }
+  // Exact block sets of the two 64-row halves (block units): the route word, the sink range
+  // and the local band as whole-word masks.
   for (int idx = tid; idx < 2 * words_blk; idx += kThreads) {
     const int half = idx / words_blk, w = idx % words_blk;
     const int hrow = row0 + 64 * half;
@@ -272,23 +295,19 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
       if (hrow < p.query_tokens) {
         const int qb = hrow / p.block;
         bits = (uint32_t)p.packed[(((int64_t)b * p.QB + qb) * p.H + h) * p.words + w];
-        for (int i = 0; i < 32; ++i) {
-          const int kb = lo + i;
-          if (kb >= p.NB) break;
-          const bool sink = kb >= p.sink_first && kb < p.sink_last;
-          const int dist = qb > kb ? qb - kb : kb - qb;
-          const bool local = p.local_radius >= 0 && dist <= p.local_radius;
-          if (sink || local) bits |= 1u << i;
-        }
+        bits |= range_bits(p.sink_first - lo, p.sink_last - lo);
+        if (p.local_radius >= 0) bits |= range_bits(qb - p.local_radius - lo, qb + p.local_radius + 1 - lo);
       } else {
         bits = 0xffffffffu;  // dense suffix rows: every key block exact
       }
-      const int valid = p.NB - lo;
-      if (valid < 32) bits &= valid <= 0 ? 0u : ((1u << valid) - 1u);
+      bits &= range_bits(0, p.NB - lo);
     }
     ebits[idx] = bits;
   }
   __syncthreads();
+  // Exact 64-key granules of either half.  (A whole-word form of this loop, with 128-key
+  // blocks spreading each block bit over two granule bits, costs the softmax loop registers:
+  // the kernel sits at its 168-register cap.)
   for (int w = tid; w < words_gran; w += kThreads) {
     uint32_t bits = 0u;
     for (int i = 0; i < 32; ++i) {
@@ -300,9 +319,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
     ubits[w] = bits;
   }
-  const bool any_routed = row0 < p.query_tokens && p.lm != nullptr;  // summaries present
-  for (int e = tid; e < nb_pad; e += kThreads)
-    lm_s[e] = (any_routed && e < p.NB) ? __ldg(p.lm + ((int64_t)b * p.H + h) * p.NB + e) * kLog2e : 0.f;
+  cp_async_wait<0>();
+  for (int e = tid; e < nb_pad; e += kThreads) lm_s[e] *= kLog2e;  // this thread's own copies
   __syncthreads();
   if (warp == 0) {
     // The exact granules in ascending order (granule ids are below 65536: T <= 2^22).
