@@ -592,8 +592,9 @@ def run_config2(args) -> None:
     for ratio in ratios:
         topk = ops.target_topk(ratio, nb)
         packed, _ = ops.route_topk(qc, kc, nb, nb, topk, want_indices=False)
+        pairs = ops.route_pairs(packed, nb)  # the layer pairs the query blocks; the kernel alone is timed below
         attn = lambda: ops.sparse_attention(q2, k2, v2, block, packed, ak, av, lm, query_tokens=nb * block,
-                                            sink_first=nb, sink_last=nb, out=out)
+                                            sink_first=nb, sink_last=nb, out=out, pairs=pairs)
         with ClockSampler(0) as attn_clocks:
             attn_ms = _timed(attn, args.steps, args.warmup, stream)
         flops = sparse_flops(T, heads, HEAD_DIM, block, topk)

@@ -195,6 +195,37 @@ int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype,
                         int local_radius, void* out, float* lse, void* stream);
 
 /*
+ * Pairing of 64-token query blocks for the tensor-core kernel (no reference counterpart: a
+ * scheduling choice of this library; the reference runs one 64-row block per tile,
+ * spark_reweight_sm100.py:1495-1700).  Its 128-row tiles hold two query blocks and do the
+ * exact key work of the union of their route sets; this pairs, per (b, h) and in block
+ * order, each unpaired block among the first `blocks` of packed_route with the unpaired block
+ * of the largest route overlap among the next 64 (ties: the nearer), then the blocks left
+ * without a partner with each other in order.
+ * packed_route: [B, QB, H, words] (words <= 256); pairs: [B, H, ceil(blocks/2), 2] int32,
+ * -1 for the empty half of an odd count.  workspace: sb_route_pair_workspace_bytes(B, H,
+ * blocks) bytes of device memory.
+ */
+int64_t sb_route_pair_workspace_bytes(int B, int H, int blocks);
+int sb_route_pair_blocks(const int32_t* packed_route, int B, int QB, int H, int words, int blocks,
+                         void* workspace, int32_t* pairs, void* stream);
+
+/*
+ * sb_sparse_attention with the routed query blocks tiled by block_pairs (as produced by
+ * sb_route_pair_blocks over the query_tokens / 64 routed blocks; block must be 64); the rows
+ * from query_tokens on form tiles of 128 in order.  Every row's result is sb_sparse_attention's
+ * up to the order of its online-softmax accumulation.  block_pairs NULL: sb_sparse_attention.
+ * The fp32 / D = 64 kernel works row by row and ignores the pairs.
+ */
+int sb_sparse_attention_pairs(const void* q, const void* k, const void* v, int dtype,
+                              int B, int T, int H, int D, int block,
+                              const int32_t* packed_route, int QB,
+                              const void* ak, const void* av, const float* lm,
+                              int query_tokens, int sink_first, int sink_last,
+                              int local_radius, const int32_t* block_pairs, void* out, float* lse,
+                              void* stream);
+
+/*
  * Dense attention of query rows [row_lo, row_hi) over all T keys (softmax scale D^-1/2); the
  * other rows of out / lse are not written.  Replaces the dense-suffix SDPA overwrite of
  * h3_sparse_attention/spark_integration.py:1238-1260 for the rows a padded sparse prefix

@@ -386,6 +386,43 @@ def sparse_attention(q: Tensor, k: Tensor, v: Tensor, block: int, packed: np.nda
 
 
 # ------------------------------------------------------------- full pipeline
+def block_pairs(packed: np.ndarray, blocks: int, window: int = 64) -> np.ndarray:
+    """Query-block pairs of sb_route_pair_blocks, restated for its test (a tile scheduling
+    choice of this build with no reference counterpart).  Per (b, h), in block order, every
+    unpaired block among the first `blocks` takes the unpaired block of the largest route
+    overlap among the next `window` (ties: the nearer); blocks left without a partner are
+    then paired with each other in order.  Returns [B, H, ceil(blocks / 2), 2] int32, -1 for
+    the empty half of an odd count."""
+    B, QB, H, words = packed.shape
+    bits = np.unpackbits(np.ascontiguousarray(packed).view(np.uint8), axis=-1, bitorder="little").astype(bool)
+    out = np.full((B, H, -(-blocks // 2), 2), -1, np.int32)
+    for b in range(B):
+        for h in range(H):
+            rows = bits[b, :blocks, h]
+            taken = np.zeros(blocks, bool)
+            pairs, singles = [], []
+            for a in range(blocks):
+                if taken[a]:
+                    continue
+                taken[a] = True
+                best, best_ov = -1, -1
+                for c in range(a + 1, min(blocks, a + 1 + window)):
+                    if taken[c]:
+                        continue
+                    ov = int(np.count_nonzero(rows[a] & rows[c]))
+                    if ov > best_ov:
+                        best, best_ov = c, ov
+                if best < 0:
+                    singles.append(a)
+                else:
+                    taken[best] = True
+                    pairs.append((a, best))
+            for i in range(0, len(singles), 2):
+                pairs.append((singles[i], singles[i + 1] if i + 1 < len(singles) else -1))
+            out[b, h] = np.asarray(pairs, np.int32)
+    return out
+
+
 def padded_tail(q: Tensor, video: int, query_tokens: int, block: int) -> Tensor:
     """Q with rows [video, query_tokens) replaced by the mean of the final partial video
     block's rows, fp32 mean rounded to Q's dtype (spark_integration.py:1173-1187)."""

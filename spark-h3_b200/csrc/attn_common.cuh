@@ -19,6 +19,11 @@ struct AttnParams {
   int B, T, H, block, NB, QB, words;
   int query_tokens, sink_first, sink_last, local_radius;
   int row_lo, row_hi;     // query rows computed and stored: [row_lo, row_hi)
+  // Optional query-block pairs (64-token blocks, sm100 kernel): tile t of (b, h) holds blocks
+  // pairs[((b * H + h) * pair_tiles + t) * 2 + {0, 1}] (-1: no block); rows past the routed
+  // prefix form 128-row tiles from query_tokens on.  Null: tile t holds rows 128 t .. 128 t + 127.
+  const int32_t* pairs;
+  int pair_tiles;
 };
 
 // Key block kb is evaluated exactly for routed query block qb when the route marks it,

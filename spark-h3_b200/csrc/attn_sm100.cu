@@ -229,9 +229,25 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int tid = threadIdx.x;
-  const int tile = ceil_div(p.row_hi, 128) - 1 - (int)blockIdx.x;  // the dense suffix tile launches first
+  // First rows of the tile's two 64-row halves (-1: an empty half).  The dense suffix tiles
+  // launch first.
+  int hb[2];
+  if (p.pairs != nullptr) {
+    const int suffix_tiles = ceil_div(p.row_hi - p.query_tokens, 128);
+    if ((int)blockIdx.x < suffix_tiles) {
+      hb[0] = p.query_tokens + 128 * (suffix_tiles - 1 - (int)blockIdx.x);
+      hb[1] = hb[0] + 64;
+    } else {
+      const int32_t* pr = p.pairs + (((int64_t)blockIdx.z * p.H + blockIdx.y) * p.pair_tiles +
+                                     ((int)blockIdx.x - suffix_tiles)) * 2;
+      hb[0] = pr[0] >= 0 ? pr[0] * p.block : -1;
+      hb[1] = pr[1] >= 0 ? pr[1] * p.block : -1;
+    }
+  } else {
+    hb[0] = 128 * (ceil_div(p.row_hi, 128) - 1 - (int)blockIdx.x);
+    hb[1] = hb[0] + 64;
+  }
   const int h = blockIdx.y, b = blockIdx.z;
-  const int row0 = tile * 128;
   const int gshift = p.block == 128 ? 1 : 0;
   [[maybe_unused]] const bool trace = SB_TRACE_CTA();
   if (threadIdx.x == 0) SB_CTA_TIME(0);
@@ -274,7 +290,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   // LM * log2(e) of every key block: the copies are issued first, so their latency overlaps
   // the route words below.
   {
-    const bool any_routed = row0 < p.query_tokens && p.lm != nullptr;  // summaries present
+    const bool any_routed = ((hb[0] >= 0 && hb[0] < p.query_tokens) || (hb[1] >= 0 && hb[1] < p.query_tokens)) &&
+                            p.lm != nullptr;  // summaries present
     const int lm_end = any_routed ? p.NB : 0;
     for (int e = tid; e < nb_pad; e += kThreads) {
       if (e < lm_end)
@@ -288,9 +305,9 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
   // and the local band as whole-word masks.
   for (int idx = tid; idx < 2 * words_blk; idx += kThreads) {
     const int half = idx / words_blk, w = idx % words_blk;
-    const int hrow = row0 + 64 * half;
+    const int hrow = hb[half];
     uint32_t bits = 0u;
-    if (hrow < p.T) {
+    if (hrow >= 0 && hrow < p.T) {
       const int lo = 32 * w;
       if (hrow < p.query_tokens) {
         const int qb = hrow / p.block;
@@ -344,8 +361,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     }
     if (lane == 0) {
       C.exact_granules = cnt;
-      const bool routed0 = row0 < p.query_tokens && row0 < p.T;
-      const bool routed1 = row0 + 64 < p.query_tokens && row0 + 64 < p.T;
+      const bool routed0 = hb[0] >= 0 && hb[0] < p.query_tokens && hb[0] < p.T;
+      const bool routed1 = hb[1] >= 0 && hb[1] < p.query_tokens && hb[1] < p.T;
       C.has_summary = (routed0 || routed1) && p.lm != nullptr ? 1 : 0;  // no summaries: exact keys only
     }
   }
@@ -383,7 +400,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
         mbar_arrive_expect_tx(bq, kTileBytes);
         for (int dh = 0; dh < 2; ++dh)
           for (int rh = 0; rh < 2; ++rh)
-            tma_load_3d_hint(sQ + dh * kHalfBytes + rh * kBoxBytes, &tm_q, bq, h * 128 + 64 * dh, row0 + 64 * rh, b,
+            tma_load_3d_hint(sQ + dh * kHalfBytes + rh * kBoxBytes, &tm_q, bq, h * 128 + 64 * dh,
+                             hb[rh] >= 0 ? hb[rh] : p.T, b,
                              once);
       }
       const int n_gran = C.exact_granules;
@@ -511,7 +529,8 @@ sparse_attention_sm100_kernel(const __grid_constant__ CUtensorMap tm_q,
     const int grp = warp >> 2;        // 0: key columns 0-63, 1: key columns 64-127
     const int row = tid & 127;        // TMEM lane = query row of the tile
     const int half = row >> 6;
-    const int grow = row0 + row;
+    const int half_row0 = hb[half];  // -1: this half holds no rows
+    const int grow = half_row0 >= 0 ? half_row0 + (row & 63) : -1;
     const uint32_t lane_base = (uint32_t)((warp & 3) * 32) << 16;
     const uint32_t s_col = 64 * grp;  // this group's S columns inside a buffer
     const uint32_t* ehalf = ebits + half * words_blk;
@@ -793,7 +812,9 @@ int launch_sparse_attention_sm100(const AttnParams& p, cudaStream_t s) {
   cudaError_t err = cudaFuncSetAttribute(sparse_attention_sm100_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)smem);
   if (err != cudaSuccess) return cuda_error(err, "sb_sparse_attention: set smem");
-  dim3 grid(ceil_div(p.row_hi, 128) - p.row_lo / 128, p.H, p.B);
+  const int tiles = p.pairs != nullptr ? p.pair_tiles + ceil_div(p.row_hi - p.query_tokens, 128)
+                                       : ceil_div(p.row_hi, 128) - p.row_lo / 128;
+  dim3 grid(tiles, p.H, p.B);
   sparse_attention_sm100_kernel<<<grid, kThreads, smem, s>>>(mq, mk, mv, mak, mav, p);
   SB_CHECK_LAUNCH("sb_sparse_attention: sm100 launch");
   return SB_OK;

@@ -77,11 +77,12 @@ extern "C" int sb_read_device_status(void* stream) {
   return value;
 }
 
-extern "C" int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype, int B,
-                                   int T, int H, int D, int block, const int32_t* packed_route,
-                                   int QB, const void* ak, const void* av, const float* lm,
-                                   int query_tokens, int sink_first, int sink_last,
-                                   int local_radius, void* out, float* lse, void* stream) {
+extern "C" int sb_sparse_attention_pairs(const void* q, const void* k, const void* v, int dtype, int B,
+                                         int T, int H, int D, int block, const int32_t* packed_route,
+                                         int QB, const void* ak, const void* av, const float* lm,
+                                         int query_tokens, int sink_first, int sink_last,
+                                         int local_radius, const int32_t* block_pairs, void* out, float* lse,
+                                         void* stream) {
   SB_CHECK_ARG(q && k && v && out, "sb_sparse_attention: null Q/K/V/out");
   SB_CHECK_ARG(dtype == SB_F32 || dtype == SB_BF16, "sb_sparse_attention: bad dtype");
   SB_CHECK_ARG(B > 0 && T > 0 && H > 0, "sb_sparse_attention: B, T, H must be positive");
@@ -114,9 +115,24 @@ extern "C" int sb_sparse_attention(const void* q, const void* k, const void* v, 
   p.local_radius = local_radius;
   p.row_lo = 0;
   p.row_hi = T;
+  if (block_pairs != nullptr) {
+    SB_CHECK_ARG(block == 64, "sb_sparse_attention_pairs: query-block pairs need 64-token blocks");
+    SB_CHECK_ARG(routed_blocks >= 1, "sb_sparse_attention_pairs: pairs need routed query blocks");
+    p.pairs = block_pairs;
+    p.pair_tiles = ceil_div(routed_blocks, 2);
+  }
   cudaStream_t s = (cudaStream_t)stream;
   if (dtype == SB_BF16 && D == 128) return launch_sparse_attention_sm100(p, s);
-  return launch_sparse_attention_simt(p, dtype, D, s);
+  return launch_sparse_attention_simt(p, dtype, D, s);  // row by row: pairs do not apply
+}
+
+extern "C" int sb_sparse_attention(const void* q, const void* k, const void* v, int dtype, int B,
+                                   int T, int H, int D, int block, const int32_t* packed_route,
+                                   int QB, const void* ak, const void* av, const float* lm,
+                                   int query_tokens, int sink_first, int sink_last,
+                                   int local_radius, void* out, float* lse, void* stream) {
+  return sb_sparse_attention_pairs(q, k, v, dtype, B, T, H, D, block, packed_route, QB, ak, av, lm, query_tokens,
+                                   sink_first, sink_last, local_radius, nullptr, out, lse, stream);
 }
 
 extern "C" int sb_dense_rows_attention(const void* q, const void* k, const void* v, int dtype, int B, int T, int H,

@@ -40,6 +40,10 @@ SIGNATURES = {
     "sb_route_topk_noalloc": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _f, _vp, _vp, _vp]),
     "sb_sparse_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i, _i,
                                  _vp, _vp, _vp]),
+    "sb_route_pair_workspace_bytes": (_i64, [_i, _i, _i]),
+    "sb_route_pair_blocks": (_i, [_vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
+    "sb_sparse_attention_pairs": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _vp, _i, _vp, _vp, _vp, _i, _i, _i,
+                                       _i, _vp, _vp, _vp, _vp]),
     "sb_selftest_wait_timeout": (_i, [ctypes.c_longlong, _vp, _vp]),
     "sb_dense_rows_attention": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "sb_tail_summaries8": (_i, [_vp, _vp, _vp, _i, _i, _i, _i, _i, _i, _i, _i, _i, _vp, _vp, _vp, _vp]),

@@ -146,9 +146,30 @@ def _check_query_prefix(query_tokens: int, tokens: int, block: int) -> None:
         raise ValueError("query_tokens must end at a physical query-block boundary")
 
 
+PAIR_MAX_WORDS = 256  # sb_route_pair_blocks handles routes of up to 256 words (8192 candidate blocks)
+
+
+def route_pairs(packed: torch.Tensor, blocks: int) -> torch.Tensor:
+    """Query-block pairs [B, H, ceil(blocks/2), 2] int32 for the attention kernel's 128-row
+    tiles (sb_route_pair_blocks): each of the first `blocks` routed blocks with the unpaired
+    block of the largest route overlap among the next 64."""
+    device = _require_cuda(packed)
+    B, QB, H, words = packed.shape
+    pairs = torch.empty((B, H, -(-blocks // 2), 2), device=device, dtype=torch.int32)
+    with torch.cuda.device(device):
+        lib = _lib.load()
+        ws = torch.empty(int(lib.sb_route_pair_workspace_bytes(B, H, blocks)), device=device, dtype=torch.uint8)
+        _lib.call("sb_route_pair_blocks", packed.data_ptr(), B, QB, H, words, blocks, ws.data_ptr(),
+                  pairs.data_ptr(), _stream(device))
+    return pairs
+
+
 def sparse_attention(q, k, v, block: int, packed: torch.Tensor | None, ak, av, lm, *, query_tokens: int,
                      sink_first: int, sink_last: int, local_radius: int = -1, out: torch.Tensor | None = None,
-                     want_lse: bool = False):
+                     want_lse: bool = False, pair_blocks: bool = True, pairs: torch.Tensor | None = None):
+    """The fused sparse attention (sb_sparse_attention).  With 64-token blocks on the
+    tensor-core kernel the routed query blocks are paired by route overlap first
+    (route_pairs), unless pair_blocks is False; `pairs` passes precomputed pairs."""
     _check_query_prefix(query_tokens, q.shape[1], block)
     device = _require_cuda(q, k, v, packed, ak, av, lm, out)
     B, T, H, D = q.shape
@@ -158,10 +179,14 @@ def sparse_attention(q, k, v, block: int, packed: torch.Tensor | None, ak, av, l
         out = torch.empty_like(q)
     lse = torch.empty((B, T, H), device=device, dtype=torch.float32) if want_lse else None
     QB = packed.shape[1] if packed is not None else 0
+    routed = query_tokens // block
+    if (pairs is None and pair_blocks and block == 64 and routed >= 2 and q.dtype == torch.bfloat16 and D == 128
+            and packed.shape[-1] <= PAIR_MAX_WORDS):
+        pairs = route_pairs(packed, routed)
     with torch.cuda.device(device):
-        _lib.call("sb_sparse_attention", q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, T, H, D,
-                  block, _ptr(packed), QB, _ptr(ak), _ptr(av), _ptr(lm), query_tokens, sink_first, sink_last,
-                  local_radius, out.data_ptr(), _ptr(lse), _stream(device))
+        _lib.call("sb_sparse_attention_pairs", q.data_ptr(), k.data_ptr(), v.data_ptr(), _dtype_code(q), B, T, H,
+                  D, block, _ptr(packed), QB, _ptr(ak), _ptr(av), _ptr(lm), query_tokens, sink_first, sink_last,
+                  local_radius, _ptr(pairs), out.data_ptr(), _ptr(lse), _stream(device))
     return out, lse
 
 
