@@ -6,14 +6,16 @@ reblock.  One step = pool Q -> anchor -> pool K + summaries -> block scores + To
 sparse attention (the 64-row partial tail attends densely inside the same kernel).
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
-                  [--workload config1|config2|fp8|config4]
+                  [--workload config1|config2|fp8|config4|tails|sm100_reference|summaries]
 
 `--workload config2` times the same layer in the reference's default "full" mode at the
 config-2 size (grid 61x48x84, N = 245,952, 64-token blocks, clustered content): reblock
 (metric factors, features, landmark tree, head-wise permutes) + the sparse layer + the
 inverse permute.  `--workload fp8` times the config-3 e4m3 linears (M = 124,992 tokens,
 K = 4096, N in {12288, 4096, 16384}).  Both print one JSON line each; the default run is
-config 1 only.
+config 1 only.  `--workload sm100_reference` times our attention kernel beside the
+reference's own tcgen05 kernel (SparkReweightForwardSm100, installed under baseline/_ref) at
+config 1 with 64-token blocks, same inputs and route, and prints both with their ratio.
 
 With N > 1 (torchrun, one process per GPU) the 32 heads are split across ranks (strong
 scaling, no data-path collective); timing is the max over ranks.  `value` is the
@@ -729,6 +731,179 @@ def run_fp8(args) -> None:
 _JSON_OUT = None
 
 
+def run_summaries(args) -> None:
+    """The bf16 key/value summaries kernel alone (key means, anchor logits, AK / AV / LM),
+    CUDA-event ms per call and HBM GB/s for K and V read once, at config 1 (128- and 64-token
+    blocks) and config 2 (64-token blocks); a SHA-256 prefix of the outputs for bit-for-bit
+    comparisons between builds."""
+    import hashlib
+
+    import torch
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.synthetic import make_qkv
+
+    if args.gpus != 1:
+        raise SystemExit("--workload summaries runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    stream = torch.cuda.current_stream(dev)
+    peak = load_peaks()["hbm"]
+    cases = {}
+    for name, block, grid in (("config1_block128", 128, (31, 48, 84)), ("config1_block64", 64, (31, 48, 84)),
+                              ("config2_block64", 64, (61, 48, 84))):
+        q, k, v = make_qkv(grid, HEADS, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
+        n = q.shape[1] // block
+        anchor = ops.query_anchor(ops.pool_queries(q, block), block, n, q.dtype)
+        del q
+        call = lambda: ops.pool_keys_summaries(k, v, anchor, block)
+        digest = hashlib.sha256()
+        for t in call():
+            digest.update(t.contiguous().view(torch.uint8).cpu().numpy().tobytes())
+        ms = _timed(call, args.steps, args.warmup, stream)
+        gbs = 2 * k.numel() * k.element_size() / ms / 1e6
+        cases[name] = dict(ms=ms, gbs=gbs, frac_of_measured_copy=gbs / peak, sha256_16=digest.hexdigest()[:16])
+        del k, v, anchor
+    emit(json.dumps(dict(
+        metric="kv summaries kernel ms per call (K and V read once)", value=cases["config1_block128"]["ms"], unit="ms",
+        n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=cases["config1_block128"]["ms"],
+        higher_is_better=False, scaling="strong", vs_baseline=None, dtype="bf16", data=DATA1,
+        config=dict(workload="kv summaries: H=32, D=128; config 1 (N=124992) and config 2 (N=245952)",
+                    l2="K and V (2.05 / 4.03 GB) exceed the 126 MB L2; no flush between calls"),
+        cases=cases, device_status=ops.read_device_status(dev))), flush=True)
+
+
+def _import_reference_sm100():
+    """The reference's fused SM100 attention (`SparkReweightForwardSm100`, reached through
+    `h3_sparse_attention/sol_numerator_virtual_q.py::virtual_q_attention` with
+    H3_SPARK_REWEIGHT_FUSED=1) from the installed copy under baseline/_ref.  The reference's
+    code is not changed.  One adapter sits in front of it: the CuTe DSL in this image returns
+    a compiled callable whose parameters are positional only, while the reference passes
+    `stream=` by keyword, so the adapter hands the stream over positionally."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    if not (ref_dir / "h3_sparse_attention").is_dir():
+        raise SystemExit("--workload sm100_reference needs the reference installed under baseline/_ref")
+    if str(ref_dir) not in sys.path:
+        sys.path.insert(0, str(ref_dir))
+    os.environ["H3_SPARK_REWEIGHT_FUSED"] = "1"
+    import cutlass.cute as cute
+
+    compile_ = cute.compile
+
+    class _StreamPositional:
+        def __init__(self, fn):
+            self.fn = fn
+
+        def __call__(self, *a, stream=None):
+            return self.fn(*a) if stream is None else self.fn(*a, stream)
+
+    cute.compile = lambda *a, **kw: _StreamPositional(compile_(*a, **kw))
+    import h3_sparse_attention.sol_numerator_virtual_q as rw
+    from sol_attn.preprocess import _reduce_kv
+
+    return rw, _reduce_kv
+
+
+def run_sm100_reference(args) -> None:
+    """Config 1 at the reference's 64-token blocks: our attention kernel beside the
+    reference's own tcgen05/TMEM kernel, on the same Q/K/V and the same route, on one GPU.
+
+    One parent range covers the sequence; our route (pool, anchor, summaries, Top-K) is
+    unpacked into the reference's dense uint8 route, and the reference receives its own
+    anchors and summaries (`build_virtual_anchors`, `virtual_summaries`) precomputed, so both
+    timed calls are the attention kernel alone.  The reference is also timed with its
+    summaries inside the call.  Outputs are compared (max abs, cosine) before timing.  Each
+    launch is timed alone with CUDA events after a device sleep, median of `--steps`."""
+    import torch
+
+    from spark_h3_b200 import ops
+    from spark_h3_b200.synthetic import make_qkv
+
+    if args.gpus != 1:
+        raise SystemExit("--workload sm100_reference runs on one GPU")
+    dev = torch.device("cuda", 0)
+    torch.cuda.set_device(dev)
+    rw, reduce_kv = _import_reference_sm100()
+    grid = tuple(int(x) for x in args.grid.split(",")) if args.grid else GRID
+    heads = args.heads or HEADS
+    block = 64
+    q, k, v = make_qkv(grid, heads, HEAD_DIM, seed=0, device=dev, dtype=torch.bfloat16, q_scale=HEAD_DIM ** -0.5)
+    B, T, H, D = q.shape
+    n = T // block
+    qc = ops.pool_queries(q, block)
+    anchor = ops.query_anchor(qc, block, n, q.dtype)
+    kc, ak, av, lm = ops.pool_keys_summaries(k, v, anchor, block)
+    topk = ops.target_topk(TOPK_RATIO, n)
+    packed, _ = ops.route_topk(qc, kc, n, n, topk)
+    pairs = ops.route_pairs(packed, n)
+    out = torch.empty_like(q)
+
+    def ours():
+        return ops.sparse_attention(q, k, v, block, packed, ak, av, lm, query_tokens=T, sink_first=n, sink_last=n,
+                                    out=out, pairs=pairs)[0]
+
+    ranges = torch.tensor([[0, T]], device=dev, dtype=torch.int64)
+    mapping = torch.zeros(n, device=dev, dtype=torch.int64)
+    dense_route = rw.unpack_packed_route(packed, n)
+    kc_ref, _ = reduce_kv(k, v)
+    anchors_ref = rw.build_virtual_anchors(q, ranges)
+    summaries_ref = rw.virtual_summaries(anchors_ref, k, v)
+
+    def ref(precomputed: bool):
+        kw = dict(virtual_anchors=anchors_ref, precomputed_summaries=summaries_ref) if precomputed else {}
+        return rw.virtual_q_attention(q, k, v, virtual_ranges=ranges, leaf_to_virtual=mapping, key_centroids=kc_ref,
+                                      route=dense_route, sink_tokens=0, force_local_blocks=False, **kw)
+
+    t0 = time.time()
+    o_ref = ref(True)
+    torch.cuda.synchronize()
+    compile_s = time.time() - t0
+    o_ours = ours()
+    torch.cuda.synchronize()
+    diff = (o_ours.float() - o_ref.float()).abs()
+    a, b = o_ours.float().flatten(), o_ref.float().flatten()
+    cosine = float((a @ b) / (a.norm() * b.norm() + 1e-30))
+    max_abs, mean_abs = float(diff.max()), float(diff.mean())
+    del diff, a, b
+
+    def each(fn, iters):
+        for _ in range(args.warmup):
+            fn()
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ts = []
+        for _ in range(iters):
+            torch.cuda._sleep(2_000_000)  # the host's enqueue stays outside the timed interval
+            e0.record()
+            fn()
+            e1.record()
+            e1.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return sorted(ts)[len(ts) // 2], ts
+
+    with ClockSampler(0) as clocks:
+        ours_ms, ours_raw = each(ours, args.steps)
+        ref_ms, ref_raw = each(lambda: ref(True), args.steps)
+        ref_full_ms, _ = each(lambda: ref(False), max(3, args.steps // 2))
+    status = ops.read_device_status(dev)
+    flops = sparse_flops(T, H, D, block, topk)
+    emit(json.dumps(dict(
+        metric="attention kernel ms at config 1 with 64-token blocks: ours beside the reference's SM100 kernel",
+        value=ours_ms, unit="ms", n_gpus=1, steps=args.steps, warmup=args.warmup, ms_per_step=ours_ms,
+        higher_is_better=False, scaling="strong", vs_baseline=None, dtype="bf16",
+        data="synthetic (seeded 8-sinusoid + 0.3 N(0,1) Q/K/V, Q scaled by 1/sqrt(D))",
+        config=dict(workload=f"config1 at block 64: N={T} ({'x'.join(map(str, grid))}), H={H}, D={D}, topk {topk} "
+                             f"of {n} blocks, one parent range, no sinks", block=block, topk=topk,
+                    l2="inputs (3 x 1.02 GB at full size) exceed the 126 MB L2; no flush between launches"),
+        reference=dict(kernel="SparkReweightForwardSm100 via virtual_q_attention (H3_SPARK_REWEIGHT_FUSED=1)",
+                       attention_ms=ref_ms, with_summaries_ms=ref_full_ms, first_call_s=round(compile_s, 1)),
+        ref_ms_over_ours_ms=ref_ms / ours_ms,
+        tflops=dict(ours=flops / ours_ms * 1e-9, reference=flops / ref_ms * 1e-9,
+                    note="algorithmic sparse FLOPs of our exact-block + summary work at this route"),
+        parity=dict(max_abs=max_abs, mean_abs=mean_abs, cosine=cosine),
+        raw_ms=dict(ours=ours_raw, reference=ref_raw), clocks=clocks.summary(), device_status=status)), flush=True)
+
+
 def keep_stdout_for_json() -> None:
     """The JSON line is the only thing this program writes to its stdout: the real stdout is
     kept on a private descriptor and fd 1 is pointed at stderr, so banners that libraries
@@ -808,9 +983,13 @@ def main():
     ap.add_argument("--heads", type=int, default=None, help="head count for a smaller profiling case")
     ap.add_argument("--profile-only", action="store_true",
                     help="run only the device-resident steps (for ncu captures of a small case)")
-    ap.add_argument("--workload", choices=("config1", "config2", "fp8", "config4", "tails"), default="config1",
+    ap.add_argument("--workload", choices=("config1", "config2", "fp8", "config4", "tails", "sm100_reference",
+                                           "summaries"),
+                    default="config1",
                     help="config1 (default, the headline layer), config2 (full mode with reblock), fp8 (config 3), "
-                         "config4 (DiT block stack, multi-GPU with torchrun), tails (tail granularity ablations)")
+                         "config4 (DiT block stack, multi-GPU with torchrun), tails (tail granularity ablations), "
+                         "sm100_reference (our attention beside the reference's SM100 kernel, block 64), "
+                         "summaries (the K/V summaries kernel alone)")
     ap.add_argument("--spark-mode", default="full", help="Spark mode of the config-4 sparse steps")
     ap.add_argument("--peer-exchange", action="store_true",
                     help="config 4: the QKV producer's epilogue stores q/k/v to the owners' buffers over NVLink "
@@ -836,6 +1015,10 @@ def main():
         run_config4(args)
     elif args.workload == "tails":
         run_tails(args)
+    elif args.workload == "sm100_reference":
+        run_sm100_reference(args)
+    elif args.workload == "summaries":
+        run_summaries(args)
     else:
         run_ours(args)
 

@@ -315,6 +315,10 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
   const int64_t HD = (int64_t)H * D;
   const __nv_bfloat16* kbase = k + ((int64_t)b * T_ + row0) * HD + (int64_t)h * D;
 
+  // The anchor row is fetched into a register before the tiles are waited on, so its L2
+  // latency overlaps the K and V copies instead of following the key means.
+  float anchor_col = 0.f;
+  if (need_logits && tid < D) anchor_col = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + tid]);
   for (int i = tid; i < rows * CH; i += kHeadThreads) {
     const int r = i / CH, c = i % CH;
     cp_async16(ks + r * D + c * 8, kbase + r * HD + c * 8);
@@ -328,6 +332,7 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
     }
   }
   cp_async_commit();
+  if (need_logits && tid < D) a_s[tid] = anchor_col;
   cp_async_wait<1>();  // K has landed; V may still be in flight
   __syncthreads();
 
@@ -344,10 +349,20 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
       float acc0 = 0.f, acc1 = 0.f;
       const int r1 = min(rows, 64 * sb + 64);
       const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(ks) + pair;
-      for (int r = 64 * sb; r < r1; ++r) {
-        const float2 f = __bfloat1622float2(src[r * (D / 2)]);
-        acc0 = __fadd_rn(acc0, f.x);
-        acc1 = __fadd_rn(acc1, f.y);
+      if (r1 - 64 * sb == 64) {
+        // A full sub-block: 16 rows' reads are issued ahead of their (in-order) adds.
+#pragma unroll 16
+        for (int r = 64 * sb; r < 64 * sb + 64; ++r) {
+          const float2 f = __bfloat1622float2(src[r * (D / 2)]);
+          acc0 = __fadd_rn(acc0, f.x);
+          acc1 = __fadd_rn(acc1, f.y);
+        }
+      } else {
+        for (int r = 64 * sb; r < r1; ++r) {
+          const float2 f = __bfloat1622float2(src[r * (D / 2)]);
+          acc0 = __fadd_rn(acc0, f.x);
+          acc1 = __fadd_rn(acc1, f.y);
+        }
       }
       part_k[sb * D + 2 * pair] = acc0;
       part_k[sb * D + 2 * pair + 1] = acc1;
@@ -359,8 +374,6 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
   constexpr int PER = kHeadThreads / BLOCK;  // 2 (128-row blocks) or 4 (64-row blocks)
   constexpr int CPT = D / 8 / PER;          // 16-byte chunks per thread
   if (need_logits) {
-    if (tid < D) a_s[tid] = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + tid]);
-    __syncthreads();
     const int r = tid / PER, part = tid % PER;
     float d0 = 0.f, d1 = 0.f;
     if (r < rows) {
@@ -469,7 +482,7 @@ kv_summaries_head_kernel(const __nv_bfloat16* __restrict__ k, const __nv_bfloat1
     // SB_SUMMARY_PRE_ROUND_LOGMASS, the fp32 mean.
     float shift = 0.f;
     if (lm != nullptr && mass_bias) {
-      const float a_c = Elem<TA>::to_f(anchor[((int64_t)b * H + h) * D + col]);
+      const float a_c = a_s[col];  // written at the start: mass_bias implies need_logits
       shift = a_c * ((numerics & SB_SUMMARY_PRE_ROUND_LOGMASS) ? key : __bfloat162float(key_b));
     }
     shift = warp_sum(shift);

@@ -213,6 +213,43 @@ def test_fp8_gemm_matches_dequantised_reference(cuda_device, M, N, K, bias):
 
 
 @pytest.mark.gpu
+@pytest.mark.parametrize("M,N,K,bias", [(512, 768, 1024, False), (4000, 2048, 4096, False), (1024, 1536, 4096, True)])
+def test_fp8_gemm_matches_the_references_scaled_mm(cuda_device, M, N, K, bias):
+    """The reference's own GEMM call on a B200 (fp8_linear.py:150-156, 280-287): per-tensor
+    scales on both operands, `torch._scaled_mm(x, w.t(), scale_a, scale_b, out_dtype=bf16,
+    use_fast_accum=True)`, then `out + bias` in bf16.  Both GEMMs sum exact e4m3 products in
+    fp32 and round once to bf16, so they differ only where the summation order moves the fp32
+    sum across a bf16 rounding boundary: at most one bf16 ulp, on a small share of the
+    elements.  With a bias the reference rounds twice (the product, then the sum with the
+    bias) where this GEMM rounds once, so each may be off by half an ulp of the product and
+    of the sum; where the bias cancels the product, that bound is set by the product's
+    magnitude, not the result's."""
+    torch.manual_seed(M + 3 * N + K)
+    x = (torch.randn(M, K, device=cuda_device) * torch.empty(M, 1, device=cuda_device).log_normal_(0.0, 0.5)
+         ).to(torch.bfloat16)
+    w = (torch.randn(N, K, device=cuda_device) * 0.02).to(torch.bfloat16)
+    b = torch.randn(N, device=cuda_device, dtype=torch.bfloat16) if bias else None
+    x_fp8, x_scale = quantize_tensor(x)
+    w_fp8, w_scale = quantize_tensor(w)
+    ref = torch._scaled_mm(x_fp8, w_fp8.t(), scale_a=x_scale.reshape(()), scale_b=w_scale.reshape(()),
+                           out_dtype=torch.bfloat16, use_fast_accum=True)
+    if b is not None:
+        ref = ref + b
+    out = fp8_gemm(x_fp8, x_scale, w_fp8, w_scale, b)
+    assert out.dtype == torch.bfloat16 and out.shape == ref.shape
+    diff = (out.float() - ref.float()).abs()
+    if b is None:
+        assert bool((diff <= 2.0 ** -7 * ref.float().abs() + 1e-30).all()), float(diff.max())
+        assert float((diff == 0).float().mean()) >= 0.98
+        assert rel_frobenius(out, ref) <= 1e-3
+    else:
+        product = (ref.float() - b.float()).abs()
+        bound = 2.0 ** -7 * (product + ref.float().abs()) + 1e-30
+        assert bool((diff <= bound).all()), float((diff / bound).max())
+        assert rel_frobenius(out, ref) <= 4e-3
+
+
+@pytest.mark.gpu
 def test_fp8_gemm_per_tensor_scales_and_persistent_grid(cuda_device):
     """Per-tensor scales on either side, and a grid smaller than the tile count (each CTA
     walks several tiles through both accumulators)."""
