@@ -454,7 +454,8 @@ int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows);
  * Landmark-tree-v2 permutation.  Replaces landmark_tree_v2.py:297-787
  * (_recursive_landmark_tree_v2 with the defaults of PreparedLandmarkTreeV2Permutation:
  * cosine distance, group size 1, 32 midpoint landmarks, linear aggregation, parent order,
- * two mean-update proxy iterations from the farthest pair, power-of-two fanout) and
+ * two mean-update proxy iterations from the farthest pair; any fanout mode, i.e. nodes of 2
+ * to 64 children over the split topology of landmark_v2_terminal.py:11-33) and
  * landmark_tree_clustering.py:56-146, 290-565 (remainder, exact routing, stable partition).
  * features: [rows, tokens, D] bf16, D = 128.  root_order: [tokens] device ids of the initial
  * order, or NULL for the flat order.  perm / inverse: [rows, tokens] int32; perm holds the

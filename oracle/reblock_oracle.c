@@ -1,8 +1,9 @@
 /*
  * CPU restatement of the landmark-tree-v2 reblock permutation (the default "full" Spark
  * mode: cosine distance, one token per group, 32 midpoint landmarks, linear aggregation,
- * parent order, two mean-update proxy iterations from the farthest pair, power-of-two
- * fanout).  TEST INFRASTRUCTURE ONLY: the tests and the smoke check compare the CUDA
+ * parent order, two mean-update proxy iterations from the farthest pair; any child count from
+ * 2 to 64, so the power-of-two, arbitrary and power-of-two-arbitrary-final fanout modes all
+ * run through it).  TEST INFRASTRUCTURE ONLY: the tests and the smoke check compare the CUDA
  * reblock against it; the product never links or calls it.
  *
  * Follows h3_sparse_attention:
@@ -13,7 +14,11 @@
  *                  per node child capacities 64 x budget, children laid out in order)
  *   - landmarks:   landmark_tree_v2.py:175-228 (_torch_interval_landmarks, midpoint mode) with
  *                  landmark_tree_clustering.py:49-53 (_midpoint_positions)
- *   - proxy tree:  landmark_v2_cosine.py:40-84 (cosine_proxy_scores_reference)
+ *   - proxy tree:  landmark_v2_cosine.py:40-84 (cosine_proxy_scores_reference) and, for any
+ *                  child count, landmark_v2_terminal.py:62-148 (node_split_reference) over the
+ *                  split topology of landmark_v2_terminal.py:11-33 (split_topology: a node of
+ *                  children [s0, s1) splits at s0 + (s1 - s0 + 1) / 2, internal nodes numbered
+ *                  breadth first, a child's landmark weights kept in slot 2 * node + 1 or + 2)
  *   - routing:     landmark_tree_clustering.py:290-515 (_exact_tree_route, CPU arm: per
  *                  internal node the left capacity goes to the smallest (score, index))
  *   - partition:   landmark_tree_clustering.py:516-565 (_stable_counting_partition)
@@ -90,27 +95,63 @@ static int rb_key_cmp(const void* a, const void* b) {
   return (x->id > y->id) - (x->id < y->id);
 }
 
-/* Proxy tree over 32 landmark centers: directions [children-1][d] in heap order. */
+/* One internal node of the split topology: children [s0, s1) split at mid; tags >= 0 name the
+ * internal child node, tags < 0 a finished child (-1 - child); slot indexes the landmark
+ * weights the node receives from its parent. */
+typedef struct {
+  int s0, s1, mid, slot, ltag, rtag;
+} RbTopo;
+
+/* Breadth-first split topology of `children` children: returns the node count, children - 1.
+ * For a power-of-two count the numbering is the heap's (node h has children 2h+1, 2h+2). */
+static int rb_topology(int children, RbTopo* rec) {
+  if (children < 2) return 0;
+  int count = 1;
+  rec[0].s0 = 0;
+  rec[0].s1 = children;
+  rec[0].slot = 0;
+  for (int k = 0; k < count; ++k) {
+    RbTopo* r = &rec[k];
+    r->mid = r->s0 + (r->s1 - r->s0 + 1) / 2;
+    const int a[2] = {r->s0, r->mid}, b[2] = {r->mid, r->s1};
+    int tag[2];
+    for (int side = 0; side < 2; ++side) {
+      if (b[side] - a[side] == 1) {
+        tag[side] = -1 - a[side];
+      } else {
+        rec[count].s0 = a[side];
+        rec[count].s1 = b[side];
+        rec[count].slot = 2 * k + 1 + side;
+        tag[side] = count++;
+      }
+    }
+    r->ltag = tag[0];
+    r->rtag = tag[1];
+  }
+  return count;
+}
+
+/* Proxy tree over 32 landmark centers: directions [children-1][d] by topology node. */
 static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t* caps, int children, int d,
                           float* dirs) {
   static float n[RB_LANDMARKS][RB_MAX_D];
   static float dist[RB_LANDMARKS][RB_LANDMARKS];
   static int64_t act[2 * RB_MAX_CHILDREN][RB_LANDMARKS];
+  RbTopo topo[RB_MAX_CHILDREN];
+  const int nodes = rb_topology(children, topo);
   for (int i = 0; i < RB_LANDMARKS; ++i) rb_unit(x + (int64_t)i * d, n[i], d);
   for (int i = 0; i < RB_LANDMARKS; ++i)
     for (int k = i + 1; k < RB_LANDMARKS; ++k) dist[i][k] = 1.0f - rb_dot(n[i], n[k], d);
   for (int i = 0; i < RB_LANDMARKS; ++i) act[0][i] = weights[i];
-  int depth_nodes = 1, first_node = 0, span = children;
-  while (span > 1) {
-    for (int j = 0; j < depth_nodes; ++j) {
-      const int h = first_node + j;
-      const int start = j * span, mid = start + span / 2, end = start + span;
+  for (int h = 0; h < nodes; ++h) {
+    const int slot = topo[h].slot, start = topo[h].s0, mid = topo[h].mid, end = topo[h].s1;
+    {
       int64_t lc = 0, rc = 0;
       for (int c = start; c < mid; ++c) lc += caps[c];
       for (int c = mid; c < end; ++c) rc += caps[c];
       int nvalid = 0, only = -1;
       for (int i = 0; i < RB_LANDMARKS; ++i)
-        if (act[h][i] > 0) {
+        if (act[slot][i] > 0) {
           ++nvalid;
           if (only < 0) only = i;
         }
@@ -121,9 +162,9 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
         float best = -INFINITY;
         int found = 0;
         for (int i = 0; i < RB_LANDMARKS; ++i) {
-          if (act[h][i] <= 0) continue;
+          if (act[slot][i] <= 0) continue;
           for (int k = i + 1; k < RB_LANDMARKS; ++k) {
-            if (act[h][k] <= 0) continue;
+            if (act[slot][k] <= 0) continue;
             if (!found || dist[i][k] > best) {
               best = dist[i][k];
               first = i;
@@ -153,10 +194,10 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
           const int i = key[r].id;
           int64_t take = lc - before;
           if (take < 0) take = 0;
-          if (take > act[h][i]) take = act[h][i];
+          if (take > act[slot][i]) take = act[slot][i];
           lw[i] = take;
-          rw[i] = act[h][i] - take;
-          before += act[h][i];
+          rw[i] = act[slot][i] - take;
+          before += act[slot][i];
         }
         for (int e = 0; e < d; ++e) {
           float a = 0.f, b = 0.f;
@@ -176,9 +217,6 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
         act[2 * h + 2][i] = rw[i];
       }
     }
-    first_node += depth_nodes;
-    depth_nodes *= 2;
-    span /= 2;
   }
 }
 
@@ -196,7 +234,7 @@ static int rb_split_node(const uint16_t* x, int d, const int32_t* ids, int64_t n
   }
   float* dirs = (float*)malloc(sizeof(float) * (size_t)(children - 1) * d);
   float* scores = (float*)malloc(sizeof(float) * (size_t)n * (children - 1));
-  uint8_t* node = (uint8_t*)calloc((size_t)n, 1);
+  int16_t* node = (int16_t*)calloc((size_t)n, sizeof(int16_t)); /* topology node, or -1 - child */
   RbKey* keys = (RbKey*)malloc(sizeof(RbKey) * (size_t)n);
   if (!dirs || !scores || !node || !keys) {
     free(dirs), free(scores), free(node), free(keys);
@@ -210,33 +248,27 @@ static int rb_split_node(const uint16_t* x, int d, const int32_t* ids, int64_t n
     rb_unit(v, u, d);
     for (int h = 0; h < children - 1; ++h) scores[t * (children - 1) + h] = rb_dot(u, dirs + (int64_t)h * d, d);
   }
-  /* exact capacity routing, heap node by heap node */
-  int depth_nodes = 1, first_node = 0, span = children;
-  while (span > 1) {
-    for (int j = 0; j < depth_nodes; ++j) {
-      const int h = first_node + j;
-      const int start = j * span, mid = start + span / 2;
-      int64_t lc = 0;
-      for (int c = start; c < mid; ++c) lc += caps[c];
-      int64_t m = 0;
-      for (int64_t t = 0; t < n; ++t)
-        if (node[t] == h) {
-          keys[m].score = scores[t * (children - 1) + h];
-          keys[m].id = ids[t];
-          keys[m].pos = (int32_t)t;
-          ++m;
-        }
-      qsort(keys, (size_t)m, sizeof(RbKey), rb_key_cmp);
-      for (int64_t r = 0; r < m; ++r) node[keys[r].pos] = (uint8_t)(r < lc ? 2 * h + 1 : 2 * h + 2);
-    }
-    first_node += depth_nodes;
-    depth_nodes *= 2;
-    span /= 2;
+  /* exact capacity routing, topology node by topology node (breadth first) */
+  RbTopo topo[RB_MAX_CHILDREN];
+  const int nodes = rb_topology(children, topo);
+  for (int h = 0; h < nodes; ++h) {
+    int64_t lc = 0;
+    for (int c = topo[h].s0; c < topo[h].mid; ++c) lc += caps[c];
+    int64_t m = 0;
+    for (int64_t t = 0; t < n; ++t)
+      if (node[t] == h) {
+        keys[m].score = scores[t * (children - 1) + h];
+        keys[m].id = ids[t];
+        keys[m].pos = (int32_t)t;
+        ++m;
+      }
+    qsort(keys, (size_t)m, sizeof(RbKey), rb_key_cmp);
+    for (int64_t r = 0; r < m; ++r) node[keys[r].pos] = (int16_t)(r < lc ? topo[h].ltag : topo[h].rtag);
   }
   /* stable partition by label */
   int64_t offset = 0;
   for (int c = 0; c < children; ++c) {
-    const int label = c + children - 1;
+    const int label = -1 - c;
     int64_t w = offset;
     for (int64_t t = 0; t < n; ++t)
       if (node[t] == label) out[w++] = ids[t];
@@ -328,7 +360,7 @@ int orc_rb_tree(const uint16_t* x, int rows, int tokens, int d, const int32_t* r
           break;
         }
         const int children = schedule[found + 1];
-        if (children < 2 || children > RB_MAX_CHILDREN || (children & (children - 1))) {
+        if (children < 2 || children > RB_MAX_CHILDREN) {
           rc = -13;
           break;
         }

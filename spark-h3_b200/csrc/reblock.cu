@@ -452,18 +452,74 @@ struct TreeLevel {
   int count, P, S;
 };
 
+// The binary proxy tree over a node's C children (h3_sparse_attention
+// landmark_v2_terminal.py:11-33, split_topology): the internal node of children [s0, s1)
+// splits them at mid = s0 + (s1 - s0 + 1) / 2, internal nodes are numbered breadth first,
+// and a child range of one child is finished.  Tags below kFinished name an internal node;
+// kFinished + c names finished child c.  For a power-of-two C this is the heap: node h has
+// children 2h + 1 and 2h + 2 and every child finishes at the last depth.
+constexpr int kFinished = 64;
+constexpr int kMaxDepths = 7;  // ceil(log2 64) depths of internal nodes, plus one
+
+struct Topology {
+  int lc[kMaxChildren], rc[kMaxChildren];  // token capacities of the left and right children
+  uint8_t s0[kMaxChildren], mid[kMaxChildren], s1[kMaxChildren];
+  uint8_t ltag[kMaxChildren], rtag[kMaxChildren];
+  uint8_t first[kMaxDepths + 1];  // first internal node of each depth; first[depths] = C - 1
+  int depths;
+};
+
+// Breadth-first construction by one thread (C <= 64: at most 63 internal nodes); caps holds
+// the C child capacities in tokens.
+__device__ void build_topology(int C, const int32_t* caps, Topology& t) {
+  int count = 1, depth = 0;
+  t.s0[0] = 0;
+  t.s1[0] = (uint8_t)C;
+  t.first[0] = 0;
+  int depth_end = 1;  // one past the last node of the current depth
+  for (int k = 0; k < count; ++k) {
+    if (k == depth_end) {
+      t.first[++depth] = (uint8_t)k;
+      depth_end = count;
+    }
+    const int a = t.s0[k], b = t.s1[k], m = a + (b - a + 1) / 2;
+    t.mid[k] = (uint8_t)m;
+    if (m - a == 1) {
+      t.ltag[k] = (uint8_t)(kFinished + a);
+    } else {
+      t.s0[count] = (uint8_t)a, t.s1[count] = (uint8_t)m, t.ltag[k] = (uint8_t)count++;
+    }
+    if (b - m == 1) {
+      t.rtag[k] = (uint8_t)(kFinished + m);
+    } else {
+      t.s0[count] = (uint8_t)m, t.s1[count] = (uint8_t)b, t.rtag[k] = (uint8_t)count++;
+    }
+  }
+  t.depths = depth + 1;
+  t.first[t.depths] = (uint8_t)count;
+  for (int k = 0; k < count; ++k) {
+    int l = 0, r = 0;
+    for (int c = t.s0[k]; c < t.mid[k]; ++c) l += caps[c];
+    for (int c = t.mid[k]; c < t.s1[k]; ++c) r += caps[c];
+    t.lc[k] = l;
+    t.rc[k] = r;
+  }
+}
+
 // One CTA of four warps per (node, row): midpoint landmarks, their unit vectors and pairwise
 // cosine distances (four threads per vector), then the binary proxy tree with the internal
-// nodes of one depth spread over the warps; directions are written in heap order.
+// nodes of one depth spread over the warps; directions are written by topology node.
 constexpr int kProxyThreads = 128;
 
 // act (the landmark weights each internal node of a depth passes down, two depths) comes last
-// and is sized per level: [2][max(1, fanout / 2)][kLandmarks] ints.
+// and is sized per level: [2][max(1, fanout / 2)][kLandmarks] ints (a depth of a C-child tree
+// holds at most C / 2 internal nodes).
 struct ProxySmem {
   __nv_bfloat16 x[kLandmarks][kDim];
   float n[kLandmarks][kDim];
   float dist[kLandmarks][kLandmarks + 1];
   int id[kLandmarks], w[kLandmarks];
+  Topology topo;
   int act[1];
 };
 
@@ -534,6 +590,7 @@ __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const _
     S.id[tid] = ids[lo + (hi - lo) / 2];
     S.w[tid] = (int)(hi - lo);
   }
+  if (tid == kLandmarks) build_topology(C, caps, S.topo);
   __syncthreads();
   for (int i = warp; i < kLandmarks; i += 4)
     *reinterpret_cast<uint2*>(&S.x[i][4 * lane]) =
@@ -574,14 +631,13 @@ __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const _
   if (tid < kLandmarks) act(0, 0)[tid] = S.w[tid];
   __syncthreads();
   float* out = dirs + ((int64_t)r * lv.count + node) * lv.S * kDim;
-  int cur = 0, depth_nodes = 1, first_heap = 0, span = C;
-  while (span > 1) {
-    for (int j = warp; j < depth_nodes; j += 4) {
-      const int hnode = first_heap + j;
-      const int s0 = j * span, mid = s0 + span / 2, s1 = s0 + span;
-      int lc = 0, rc = 0;
-      for (int c = s0; c < mid; ++c) lc += caps[c];
-      for (int c = mid; c < s1; ++c) rc += caps[c];
+  const Topology& topo = S.topo;
+  int cur = 0;
+  for (int depth = 0; depth < topo.depths; ++depth) {
+    const int k0 = topo.first[depth], next0 = topo.first[depth + 1];
+    for (int j = warp; j < next0 - k0; j += 4) {
+      const int hnode = k0 + j;
+      const int lc = topo.lc[hnode], rc = topo.rc[hnode];
       const int aw = act(cur, j)[lane];
       const unsigned vmask = __ballot_sync(kFull, aw > 0);
       int first = vmask ? __ffs(vmask) - 1 : 0, second = first;
@@ -663,16 +719,12 @@ __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const _
 #pragma unroll
       for (int e = 0; e < 4; ++e) dir[e] = __fsub_rn(ur[e], ul[e]);
       *reinterpret_cast<float4*>(out + (int64_t)hnode * kDim + 4 * lane) = make_float4(dir[0], dir[1], dir[2], dir[3]);
-      if (span > 2) {
-        act(cur ^ 1, 2 * j)[lane] = lw;
-        act(cur ^ 1, 2 * j + 1)[lane] = rw;
-      }
+      // internal children take their weights at their place in the next depth
+      if (topo.ltag[hnode] < kFinished) act(cur ^ 1, topo.ltag[hnode] - next0)[lane] = lw;
+      if (topo.rtag[hnode] < kFinished) act(cur ^ 1, topo.rtag[hnode] - next0)[lane] = rw;
     }
     __syncthreads();
     cur ^= 1;
-    first_heap += depth_nodes;
-    depth_nodes *= 2;
-    span /= 2;
   }
 }
 
@@ -994,6 +1046,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
   __shared__ int warp_cnt[(THREADS / 32)][kMaxChildren];
   __shared__ int warp_off[(THREADS / 32)][kMaxChildren];
   __shared__ int running[kMaxChildren], child_off[kMaxChildren];
+  __shared__ Topology topo;
   int(*hist)[256] = reinterpret_cast<int(*)[256]>(scratch);
   unsigned long long* sk = reinterpret_cast<unsigned long long*>(scratch);
   const int node = blockIdx.x, r = blockIdx.y;
@@ -1013,16 +1066,19 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
   int n2 = 1;
   while (n2 < n) n2 <<= 1;
   for (int t = tid; t < n; t += THREADS) st[t] = 0;
+  if (tid == 0) build_topology(C, caps, topo);
   __syncthreads();
-  int depth_nodes = 1, first_heap = 0, span = C;
-  while (span > 1) {
-    const int nd = depth_nodes;
+  // st[t]: the token's internal proxy node, or kFinished + child once its child is decided
+  for (int depth = 0; depth < topo.depths; ++depth) {
+    const int first_heap = topo.first[depth];
+    const int nd = topo.first[depth + 1] - first_heap;
     if (tid < nd) {
-      const int s0 = tid * span, mid = s0 + span / 2;
-      int lc = 0, before = 0;
-      for (int c = s0; c < mid; ++c) lc += caps[c];
-      for (int c = 0; c < s0; ++c) before += caps[c];
-      target[tid] = lc;
+      // the node's left capacity; the tokens of the depth's earlier nodes (their whole
+      // capacities) come before its own in the sorted keys
+      const int k = first_heap + tid;
+      int before = 0;
+      for (int jn = first_heap; jn < k; ++jn) before += topo.lc[jn] + topo.rc[jn];
+      target[tid] = topo.lc[k];
       seg[tid] = before;
       prefix[tid] = 0;
       id_prefix[tid] = 0;
@@ -1035,8 +1091,8 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
 #pragma unroll
       for (int q = 0; q < kSortMax / THREADS; ++q) {
         const int e = tid + q * THREADS;
-        unsigned long long k64 = ~0ull;
-        if (e < n) {
+        unsigned long long k64 = ~0ull;  // padding and finished tokens sort last
+        if (e < n && st[e] < kFinished) {
           const int h = st[e];
           const uint32_t kk = order_key(sc[(int64_t)e * lv.S + h]);
           k64 = ((unsigned long long)(h - first_heap) << 57) | ((unsigned long long)kk << 25) |
@@ -1073,10 +1129,10 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
 #pragma unroll
       for (int q = 0; q < kSortMax / THREADS; ++q) {
         const int e = tid + q * THREADS;
-        if (e < n) {
+        if (e < n && mine[q] != ~0ull) {
           const int j = (int)(mine[q] >> 57);
           const int hnode = first_heap + j;
-          st[e] = (uint8_t)(target[j] > 0 && mine[q] <= cut[j] ? 2 * hnode + 1 : 2 * hnode + 2);
+          st[e] = target[j] > 0 && mine[q] <= cut[j] ? topo.ltag[hnode] : topo.rtag[hnode];
         }
       }
       __syncthreads();
@@ -1086,18 +1142,18 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int t = t0 + u * THREADS;
-          hs[u] = t < n ? st[t] : 0;
+          hs[u] = t < n ? st[t] : kFinished;
         }
         float vs[kUnroll];
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int t = t0 + u * THREADS;
-          vs[u] = t < n ? sc[(int64_t)t * lv.S + hs[u]] : 0.f;
+          vs[u] = hs[u] < kFinished ? sc[(int64_t)t * lv.S + hs[u]] : 0.f;
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int t = t0 + u * THREADS;
-          if (t < n) key[t] = order_key(vs[u]);
+          if (hs[u] < kFinished) key[t] = order_key(vs[u]);
         }
       }
       __syncthreads();
@@ -1112,8 +1168,9 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
 #pragma unroll
           for (int u = 0; u < kUnroll; ++u) {
             const int t = t0 + u * THREADS;
-            js[u] = t < n ? st[t] - first_heap : -1;
-            ks[u] = t < n ? key[t] : 0u;
+            const int h = t < n ? st[t] : kFinished;
+            js[u] = h < kFinished ? h - first_heap : -1;
+            ks[u] = h < kFinished ? key[t] : 0u;
           }
 #pragma unroll
           for (int u = 0; u < kUnroll; ++u) {
@@ -1154,7 +1211,9 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
           for (int e = tid; e < nd * 256; e += THREADS) hist[e >> 8][e & 255] = 0;
           __syncthreads();
           for (int t = tid; t < n; t += THREADS) {
-            const int j = st[t] - first_heap;
+            const int h = st[t];
+            if (h >= kFinished) continue;
+            const int j = h - first_heap;
             if (!need_ids[j] || key[t] != prefix[j]) continue;
             const uint32_t id = (uint32_t)ids[t];
             if (pass == 0 || (id >> (shift + 8)) == (id_prefix[j] >> (shift + 8)))
@@ -1182,24 +1241,21 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int t = t0 + u * THREADS;
-          hs[u] = t < n ? st[t] : 0;
-          ks[u] = t < n ? key[t] : 0u;
+          hs[u] = t < n ? st[t] : kFinished;
+          ks[u] = hs[u] < kFinished ? key[t] : 0u;
         }
 #pragma unroll
         for (int u = 0; u < kUnroll; ++u) {
           const int t = t0 + u * THREADS;
-          if (t >= n) continue;
+          if (hs[u] >= kFinished) continue;
           const int j = hs[u] - first_heap;
           const bool left = ks[u] < prefix[j] ||
                             (ks[u] == prefix[j] && (!need_ids[j] || (uint32_t)ids[t] <= id_prefix[j]));
-          st[t] = (uint8_t)(left ? 2 * hs[u] + 1 : 2 * hs[u] + 2);
+          st[t] = left ? topo.ltag[hs[u]] : topo.rtag[hs[u]];
         }
       }
       __syncthreads();
     }
-    first_heap += depth_nodes;
-    depth_nodes *= 2;
-    span /= 2;
   }
   // stable partition by child label
   if (tid < C) {
@@ -1209,7 +1265,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
     running[tid] = 0;
   }
   __syncthreads();
-  const int label_base = C - 1;
+  const int label_base = kFinished;
   int32_t* out_next = idx_out + (int64_t)r * N + start;
   int32_t* out_leaf = perm + (int64_t)r * N + start;
   const unsigned lt = (1u << lane) - 1u;
@@ -1697,8 +1753,7 @@ extern "C" int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, in
       }
       SB_CHECK_ARG(found >= 0, "sb_reblock_plan: no budget for a node of %d leaves at round %d", sg.leaves, level);
       const int C = schedule[found + 1];
-      SB_CHECK_ARG(C >= 2 && C <= kMaxChildren && (C & (C - 1)) == 0,
-                   "sb_reblock_plan: the CUDA tree takes power-of-two fanouts up to 64, got %d children", C);
+      SB_CHECK_ARG(C >= 2 && C <= kMaxChildren, "sb_reblock_plan: the CUDA tree takes 2 to 64 children, got %d", C);
       std::vector<int32_t> rec(kNodeInts, 0);
       rec[0] = sg.start * 64;
       rec[1] = sg.leaves * 64;
@@ -1721,8 +1776,12 @@ extern "C" int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, in
     std::sort(next.begin(), next.end(), [](const Seg& a, const Seg& b) { return a.start < b.start; });
     segs.swap(next);
     if (!nodes.empty()) {
+      // kernels are instantiated per power-of-two fanout; a level runs with the smallest one
+      // that holds its largest node (the score kernels store only a node's C - 1 scores)
+      int P = 2;
+      while (P < maxC) P *= 2;
       level_nodes.push_back(std::move(nodes));
-      level_P.push_back(maxC);
+      level_P.push_back(P);
     }
   }
   for (const Seg& sg : segs)
@@ -1839,7 +1898,8 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
     }
     SB_CHECK_LAUNCH("sb_reblock_tree: scores");
     const int32_t* first = plan_host + lh[1];  // the level's first node record (start, tokens, children)
-    if (lv.count == 1 && first[1] > kSortMax && first[2] <= 2 * kClusterMaxNodes)
+    // the cluster form walks the heap of a power-of-two fanout; other roots take the radix form
+    if (lv.count == 1 && first[1] > kSortMax && first[2] <= 2 * kClusterMaxNodes && (first[2] & (first[2] - 1)) == 0)
       reblock_route_cluster_kernel<<<dim3(kRootCluster, rows), kRouteThreads, 0, s>>>(
           tokens, active, lv, idx[cur], scores, keys, state, idx[cur ^ 1], perm, status);
     else if (level_max_tokens(plan_host, lh) <= kSortMax)  // every node sorts: 128-thread CTAs

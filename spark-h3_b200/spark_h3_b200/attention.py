@@ -180,7 +180,7 @@ _REBLOCK_DEFAULTS = dict(
     landmark_tree_v2_landmark_count=32, landmark_tree_v2_aggregation="linear", landmark_tree_v2_m2_side="both",
     landmark_tree_v2_m2_estimator="hilbert_midpoint", landmark_tree_v2_proxy_iterations=2,
     landmark_tree_v2_proxy_seed_rule="farthest_pair", landmark_tree_v2_proxy_update_rule="mean",
-    landmark_tree_v2_layout_reuse="independent", landmark_tree_v2_fanout_mode="power_of_two_fanout")
+    landmark_tree_v2_layout_reuse="independent")
 
 
 def _reblock_permutations(controller, q_bthd, k_bthd, layout, layer: int, video: int):

@@ -254,15 +254,16 @@ def spark_reblock(samples: torch.Tensor, *, grid_shape, initial_order: str = "fl
 
     Implements the production defaults (cosine distance, single tokens, 32 midpoint
     landmarks, linear aggregation, parent order, two mean-update proxy iterations from the
-    farthest pair, power-of-two fanout); other options raise NotImplementedError."""
+    farthest pair) with every fanout mode of reblock_hierarchy.py (power_of_two_fanout,
+    arbitrary_fanout, power_of_two_arbitrary_final: nodes of 2 to 64 children, split over
+    landmark_v2_terminal.py's breadth-first topology); other options raise
+    NotImplementedError."""
     for name, value in options.items():
         if name not in _DEFAULTS:
             raise TypeError(f"spark_reblock() got an unexpected keyword argument {name!r}")
         default = _DEFAULTS[name]
         if (value is not default) and value != default:
             raise NotImplementedError(f"the B200 landmark tree implements {name}={default!r} only")
-    if fanout_mode != "power_of_two_fanout":
-        raise NotImplementedError("the B200 landmark tree implements fanout_mode='power_of_two_fanout' only")
     if samples.ndim < 2 or not samples.is_floating_point():
         raise ValueError("samples must be floating point with layout [...,N,D]")
     leading = samples.shape[:-2]

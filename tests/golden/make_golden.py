@@ -29,6 +29,10 @@ Fixtures:
                   applied to the reference's route and summaries (fp32)
   reblock_tree.npz  recursive_landmark_tree_v2_reference (landmark_tree_v2.py:790-832) on
                   seeded bf16 features: the permutation per case
+  reblock_tree_modes.npz  the same on the other two fanout modes, arbitrary_fanout and
+                  power_of_two_arbitrary_final (reblock_hierarchy.py:124-160), whose nodes
+                  split into non-power-of-two child counts over landmark_v2_terminal.py's
+                  split topology; the permutation and the hierarchy's split budgets per case
   reblock_qk.npz  the full paired Q/K reblock (_landmark_tree_v2_qk_block_permutations,
                   spark_integration.py:735-851, CPU controller, mode "full") on clustered
                   synthetic Q/K: Hilbert metric samples, the Cholesky factors, the bf16
@@ -281,6 +285,33 @@ def reblock_tree_fixture():
     np.savez_compressed(HERE / "reblock_tree.npz", **out)
 
 
+REBLOCK_TREE_MODE_CASES = [
+    # (name, tokens, children, final fanout, fanout mode, grid, initial order, seed)
+    ("arb_two_rounds", 20000, 16, None, "arbitrary_fanout", (5, 40, 100), "flat", 21),
+    ("arb_fanout8", 6016, 8, None, "arbitrary_fanout", (4, 32, 47), "tile_t4h4w4", 22),
+    ("p2final_8_16", 6016, 8, 16, "power_of_two_arbitrary_final", (4, 32, 47), "flat", 23),
+    ("arb_final12", 13000, 16, 12, "arbitrary_fanout", (1, 1, 13000), "flat", 24),
+    ("arb_root3", 12352, 4, 3, "arbitrary_fanout", (2, 32, 193), "hilbert_thw", 25),
+]
+
+
+def reblock_tree_modes_fixture():
+    from h3_sparse_attention.landmark_tree_v2 import recursive_landmark_tree_v2_reference
+
+    out = {}
+    for name, tokens, children, final_fanout, mode, grid, order, seed in REBLOCK_TREE_MODE_CASES:
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+        ref = recursive_landmark_tree_v2_reference(x, grid_shape=grid, max_children=children,
+                                                   final_fanout=final_fanout, fanout_mode=mode,
+                                                   initial_order=order)
+        out[f"{name}_perm"] = ref.permutation.numpy().astype(np.int32)
+        out[f"{name}_digest"] = np.array(digest(x))
+        out[f"{name}_budgets"] = np.array(json.dumps([[list(map(int, b)) for _, b in rnd]
+                                                      for rnd in ref.hierarchy.split_budgets]))
+    np.savez_compressed(HERE / "reblock_tree_modes.npz", **out)
+
+
 def reblock_qk_fixture():
     from types import SimpleNamespace
 
@@ -322,6 +353,7 @@ def main():
     head_budget_fixture()
     summaries_and_attention()
     reblock_tree_fixture()
+    reblock_tree_modes_fixture()
     reblock_qk_fixture()
     print("golden fixtures written to", HERE)
 

@@ -57,6 +57,52 @@ def test_tree_matches_oracle(cuda_device, grid, children, order, rows):
     assert np.array_equal(perm, ref)
 
 
+TREE_MODE_CASES = [
+    # (name, tokens, children, final fanout, fanout mode, grid, initial order, seed)
+    ("arb_two_rounds", 20000, 16, None, "arbitrary_fanout", (5, 40, 100), "flat", 21),
+    ("arb_fanout8", 6016, 8, None, "arbitrary_fanout", (4, 32, 47), "tile_t4h4w4", 22),
+    ("p2final_8_16", 6016, 8, 16, "power_of_two_arbitrary_final", (4, 32, 47), "flat", 23),
+    ("arb_final12", 13000, 16, 12, "arbitrary_fanout", (1, 1, 13000), "flat", 24),
+    ("arb_root3", 12352, 4, 3, "arbitrary_fanout", (2, 32, 193), "hilbert_thw", 25),
+]
+
+
+@pytest.mark.parametrize("name,tokens,children,final_fanout,mode,grid,order,seed", TREE_MODE_CASES)
+def test_tree_fanout_modes_match_reference_fixtures(cuda_device, name, tokens, children, final_fanout, mode, grid,
+                                                    order, seed):
+    """Nodes of 3, 6, 7, 9, 10, 11, 12 and 15 children: the GPU tree reproduces the reference's
+    own CPU tree (recursive_landmark_tree_v2_reference) in the arbitrary and
+    power-of-two-arbitrary-final fanout modes."""
+    z = np.load(GOLDEN / "reblock_tree_modes.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    result = reblock.spark_reblock(x.to(cuda_device), grid_shape=grid, max_children=children,
+                                   final_fanout=final_fanout, fanout_mode=mode, initial_order=order)
+    perm = result.permutation.cpu().numpy().reshape(-1, tokens)
+    inverse = result.inverse_permutation.cpu().numpy().reshape(-1, tokens)
+    assert np.array_equal(perm, z[f"{name}_perm"])
+    assert np.array_equal(np.take_along_axis(inverse, perm, 1), np.broadcast_to(np.arange(tokens), perm.shape))
+
+
+@pytest.mark.parametrize("tokens,children,final_fanout,mode,rows", [
+    # a 3-child root of 3,072 tokens: the one-CTA radix route, not the cluster form
+    (3072, 4, 4, "arbitrary_fanout", 2),
+    # 50-child nodes of 3,200 tokens: 64-wide score kernel, radix route with 25 nodes a depth
+    (12800, 64, None, "arbitrary_fanout", 1),
+    # power-of-two rounds of 32 children, then finals of 9 and 10 children that sort
+    (20000, 32, 24, "power_of_two_arbitrary_final", 2),
+])
+def test_tree_fanout_modes_match_oracle(cuda_device, tokens, children, final_fanout, mode, rows):
+    g = torch.Generator().manual_seed(tokens + children)
+    x = torch.randn(rows, tokens, 128, generator=g).to(torch.bfloat16)
+    grid = (1, 1, tokens)
+    result = reblock.spark_reblock(x.to(cuda_device), grid_shape=grid, max_children=children,
+                                   final_fanout=final_fanout, fanout_mode=mode)
+    h = build_reblock_hierarchy(tokens, children, final_fanout=final_fanout, fanout_mode=mode)
+    ref, _ = oracle.reblock_tree(bits(x), grid, h.split_budgets)
+    assert np.array_equal(result.permutation.cpu().numpy().reshape(-1, tokens), ref)
+
+
 def test_tree_duplicate_features_tie_break(cuda_device):
     """Repeated rows give exactly equal scores: ties resolve to the lower token id."""
     g = torch.Generator().manual_seed(3)

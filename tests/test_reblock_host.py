@@ -35,11 +35,19 @@ def test_unknown_initial_order_rejected():
         reblock.initial_token_indices((1, 1, 64), "spiral")
 
 
-@pytest.mark.parametrize("tokens,children", [(245952, 16), (4133, 16), (6016, 8), (3000, 4), (130, 16), (64, 16)])
-def test_plan_node_tables(tokens, children):
+@pytest.mark.parametrize("tokens,children,final_fanout,mode", [
+    (245952, 16, None, "power_of_two_fanout"), (4133, 16, None, "power_of_two_fanout"),
+    (6016, 8, None, "power_of_two_fanout"), (3000, 4, None, "power_of_two_fanout"),
+    (130, 16, None, "power_of_two_fanout"), (64, 16, None, "power_of_two_fanout"),
+    (20000, 16, None, "arbitrary_fanout"), (13000, 16, 12, "arbitrary_fanout"),
+    (6016, 8, 16, "power_of_two_arbitrary_final"), (12352, 4, 3, "arbitrary_fanout"),
+    (245952, 64, None, "arbitrary_fanout")])
+def test_plan_node_tables(tokens, children, final_fanout, mode):
+    """Node tables of every fanout mode; a level runs with the smallest power-of-two fanout
+    that holds its largest node, whatever the node's own child count."""
     from spark_h3_b200 import _lib
 
-    h = build_reblock_hierarchy(tokens, children)
+    h = build_reblock_hierarchy(tokens, children, final_fanout=final_fanout, fanout_mode=mode)
     schedule = reblock._schedule(h)
     lib = _lib.load()
     n = lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens, None, 0)
@@ -53,6 +61,8 @@ def test_plan_node_tables(tokens, children):
         count, node_off, tile_off, P, S = plan[8 + 8 * l: 8 + 8 * l + 5]
         assert P >= 2 and (P & (P - 1)) == 0 and S == P - 1
         tiles = plan[tile_off: tile_off + active // 64]
+        largest = max(int(plan[node_off + 68 * j + 2]) for j in range(count))
+        assert P // 2 < largest <= P
         for j in range(count):
             start, size, C = plan[node_off + 68 * j: node_off + 68 * j + 3]
             caps = plan[node_off + 68 * j + 4: node_off + 68 * j + 4 + C]
@@ -69,6 +79,14 @@ def test_plan_rejects_short_schedule():
     h = build_reblock_hierarchy(4096, 16)
     schedule = reblock._schedule(h)[:3]
     assert _lib.load().sb_reblock_plan(schedule.ctypes.data, len(schedule), 4096, None, 0) < 0
+
+
+def test_plan_rejects_more_than_64_children():
+    from spark_h3_b200 import _lib
+
+    schedule = np.array([1, 1, 65, 65, *([1] * 65)], dtype=np.int32)
+    assert _lib.load().sb_reblock_plan(schedule.ctypes.data, len(schedule), 65 * 64, None, 0) < 0
+    assert "2 to 64 children" in _lib.load().sb_last_error().decode()
 
 
 def test_spark_reblock_rejects_unimplemented_options():

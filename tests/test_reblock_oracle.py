@@ -51,6 +51,34 @@ def test_tree_matches_reference(name, tokens, dim, children, grid, order, seed):
         assert (np.diff(rank[tail], axis=1) > 0).all()
 
 
+TREE_MODE_CASES = [
+    # (name, tokens, children, final fanout, fanout mode, grid, initial order, seed)
+    ("arb_two_rounds", 20000, 16, None, "arbitrary_fanout", (5, 40, 100), "flat", 21),
+    ("arb_fanout8", 6016, 8, None, "arbitrary_fanout", (4, 32, 47), "tile_t4h4w4", 22),
+    ("p2final_8_16", 6016, 8, 16, "power_of_two_arbitrary_final", (4, 32, 47), "flat", 23),
+    ("arb_final12", 13000, 16, 12, "arbitrary_fanout", (1, 1, 13000), "flat", 24),
+    ("arb_root3", 12352, 4, 3, "arbitrary_fanout", (2, 32, 193), "hilbert_thw", 25),
+]
+
+
+@pytest.mark.parametrize("name,tokens,children,final_fanout,mode,grid,order,seed", TREE_MODE_CASES)
+def test_tree_fanout_modes_match_reference(name, tokens, children, final_fanout, mode, grid, order, seed):
+    """The arbitrary and power-of-two-arbitrary-final fanout modes: nodes split into 3, 6, 7,
+    9, 10, 11, 12 or 15 children over the breadth-first split topology; the reference's own
+    CPU tree (recursive_landmark_tree_v2_reference) gave the permutations."""
+    import json
+
+    z = np.load(GOLDEN / "reblock_tree_modes.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    assert digest(x) == str(z[f"{name}_digest"]), "seeded features differ from the ones the fixture used"
+    hierarchy = build_reblock_hierarchy(tokens, children, final_fanout=final_fanout, fanout_mode=mode)
+    assert [[list(b) for _, b in rnd] for rnd in hierarchy.split_budgets] == json.loads(str(z[f"{name}_budgets"]))
+    perm, inverse = oracle.reblock_tree(bits(x), grid, hierarchy.split_budgets, order)
+    assert np.array_equal(perm, z[f"{name}_perm"])
+    assert np.array_equal(np.take_along_axis(inverse, perm, 1), np.broadcast_to(np.arange(tokens), perm.shape))
+
+
 def test_qk_reblock_matches_reference():
     z = np.load(GOLDEN / "reblock_qk.npz")
     grid = tuple(int(g) for g in z["grid"])
