@@ -447,6 +447,18 @@ int sb_reblock_transform(const void* q, const void* k, int B, int T, int H, int 
 int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, int tokens, int32_t* plan,
                         int64_t capacity);
 
+/*
+ * Proxy controls of a plan (host), before its device copy is made.  Replaces the
+ * proxy_iterations / seed_rule arguments of landmark_tree_v2.py:790-832 and
+ * landmark_v2_terminal.py:43-50 (_normalize_proxy_controls): proxy_iterations mean-update
+ * passes of every proxy node, 0, 1, 2 or 4 (with 0, one assignment pass hands the children
+ * their landmark weights and the seed pair gives the split direction); endpoint_seeds 0 seeds
+ * each proxy node with its farthest valid landmark pair (seed_rule "farthest_pair"), 1 with
+ * its lowest and highest valid landmark ("endpoint_order").  sb_reblock_plan sets the
+ * production controls, 2 and 0.  Returns 0, or SB_ERR_INVALID for other values.
+ */
+int sb_reblock_plan_proxy(int32_t* plan, int proxy_iterations, int endpoint_seeds);
+
 /* Scratch bytes sb_reblock_tree needs for `rows` feature rows under `plan` (host plan). */
 int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows);
 
@@ -465,6 +477,20 @@ int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows);
 int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
                     const int32_t* plan_host, const int32_t* plan_device, void* workspace,
                     int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream);
+
+/*
+ * sb_reblock_tree with the protected remainder chosen by the caller: the excluded_indices
+ * argument of landmark_tree_v2.py:790-832 and landmark_tree_clustering.py:85-119
+ * (_initial_hilbert_partition's frozen tail).  excluded: [rows, tokens mod 64] device int32
+ * token ids, unique and in [0, tokens) per row (NULL allowed when tokens is a multiple of 64);
+ * those tokens form the tail of each permutation in root order, whatever their norms.  The
+ * caller validates the ids: an out-of-range id is skipped and a tail of the wrong size sets
+ * device status 612 (sb_read_device_status), with every write still inside the row.
+ */
+int sb_reblock_tree_frozen(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+                           const int32_t* excluded, const int32_t* plan_host, const int32_t* plan_device,
+                           void* workspace, int64_t workspace_bytes, int32_t* perm, int32_t* inverse,
+                           void* stream);
 
 #ifdef __cplusplus
 }

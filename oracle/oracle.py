@@ -73,6 +73,8 @@ def _lib():
         lib.orc_rb_norms.restype = None
         lib.orc_rb_tree.argtypes = [u16p, ci, ci, ci, i32p, i32p, i32p]
         lib.orc_rb_tree.restype = ci
+        lib.orc_rb_tree_proxy.argtypes = [u16p, ci, ci, ci, i32p, i32p, ci, ci, ctypes.c_void_p, i32p]
+        lib.orc_rb_tree_proxy.restype = ci
         _LIB = lib
     return _LIB
 
@@ -618,14 +620,24 @@ def hierarchy_schedule(split_budgets) -> np.ndarray:
     return np.asarray(words, dtype=np.int32)
 
 
-def reblock_tree(features_bits: np.ndarray, grid, split_budgets, order: str = "flat") -> tuple[np.ndarray, np.ndarray]:
-    """Landmark-tree-v2 permutation of bf16 features [rows, N, D] (reblock_oracle.c):
-    returns (permutation, inverse) int64 [rows, N]."""
+def reblock_tree(features_bits: np.ndarray, grid, split_budgets, order: str = "flat", *, proxy_iterations: int = 2,
+                 seed_rule: str = "farthest_pair", excluded=None) -> tuple[np.ndarray, np.ndarray]:
+    """Landmark-tree-v2 permutation of bf16 features [rows, N, D] (reblock_oracle.c), with the
+    proxy controls of landmark_v2_terminal.py:43-50 (mean updates) and optionally the caller's
+    protected remainder `excluded` [rows, N mod 64]: returns (permutation, inverse) int64
+    [rows, N]."""
+    if seed_rule not in ("farthest_pair", "endpoint_order"):
+        raise ValueError("seed_rule must be farthest_pair or endpoint_order")
     x = np.ascontiguousarray(features_bits, dtype=np.uint16)
     rows, n, d = x.shape
     root = np.ascontiguousarray(initial_order(grid, order), dtype=np.int32)
     perm = np.empty((rows, n), dtype=np.int32)
-    rc = _lib().orc_rb_tree(x, rows, n, d, root, hierarchy_schedule(split_budgets), perm)
+    frozen = None if excluded is None else np.ascontiguousarray(excluded, dtype=np.int32)
+    if frozen is not None and frozen.shape != (rows, n % 64):
+        raise ValueError(f"excluded must have shape {(rows, n % 64)}")
+    rc = _lib().orc_rb_tree_proxy(x, rows, n, d, root, hierarchy_schedule(split_budgets), proxy_iterations,
+                                  int(seed_rule == "endpoint_order"),
+                                  None if frozen is None else frozen.ctypes.data, perm)
     if rc != 0:
         raise RuntimeError(f"orc_rb_tree failed ({rc})")
     inverse = np.empty_like(perm)

@@ -131,9 +131,19 @@ static int rb_topology(int children, RbTopo* rec) {
   return count;
 }
 
+/* Proxy controls (landmark_v2_terminal.py:43-50, 62-148): mean-update passes (0, 1, 2 or 4;
+ * with 0 one assignment pass still hands the children their landmark weights and the seeds
+ * give the direction) and the seed rule (farthest valid pair, or the lowest and highest
+ * valid landmark).  Updates are the capacity-weighted means. */
+typedef struct {
+  int iterations, endpoint_seeds;
+} RbProxy;
+
+static const RbProxy rb_default_proxy = {2, 0};
+
 /* Proxy tree over 32 landmark centers: directions [children-1][d] by topology node. */
 static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t* caps, int children, int d,
-                          float* dirs) {
+                          const RbProxy* proxy, float* dirs) {
   static float n[RB_LANDMARKS][RB_MAX_D];
   static float dist[RB_LANDMARKS][RB_LANDMARKS];
   static int64_t act[2 * RB_MAX_CHILDREN][RB_LANDMARKS];
@@ -157,7 +167,13 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
         }
       if (only < 0) only = 0;
       int first = only, second = only;
-      if (nvalid >= 2) {
+      if (nvalid >= 2 && proxy->endpoint_seeds) {
+        for (int i = RB_LANDMARKS - 1; i >= 0; --i)
+          if (act[slot][i] > 0) {
+            second = i;
+            break;
+          }
+      } else if (nvalid >= 2) {
         /* first maximum in row-major (i, k) order over valid pairs i < k */
         float best = -INFINITY;
         int found = 0;
@@ -178,7 +194,8 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
       memcpy(left, x + (int64_t)first * d, sizeof(float) * d);
       memcpy(right, x + (int64_t)second * d, sizeof(float) * d);
       int64_t lw[RB_LANDMARKS], rw[RB_LANDMARKS];
-      for (int it = 0; it < 2; ++it) {
+      const int rounds = proxy->iterations > 0 ? proxy->iterations : 1;
+      for (int it = 0; it < rounds; ++it) {
         rb_unit(left, ul, d);
         rb_unit(right, ur, d);
         for (int i = 0; i < d; ++i) dir[i] = ur[i] - ul[i];
@@ -199,6 +216,7 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
           rw[i] = act[slot][i] - take;
           before += act[slot][i];
         }
+        if (it >= proxy->iterations) break; /* zero updates: one assignment, seeds kept */
         for (int e = 0; e < d; ++e) {
           float a = 0.f, b = 0.f;
           for (int i = 0; i < RB_LANDMARKS; ++i) {
@@ -222,7 +240,7 @@ static void rb_proxy_tree(const float* x, const int32_t* weights, const int64_t*
 
 /* Split one node: ids[n] (node order) -> out[n] grouped by child, stable. */
 static int rb_split_node(const uint16_t* x, int d, const int32_t* ids, int64_t n, const int64_t* caps, int children,
-                         int32_t* out) {
+                         const RbProxy* proxy, int32_t* out) {
   float centers[RB_LANDMARKS * RB_MAX_D];
   int32_t weights[RB_LANDMARKS];
   for (int i = 0; i < RB_LANDMARKS; ++i) {
@@ -240,7 +258,7 @@ static int rb_split_node(const uint16_t* x, int d, const int32_t* ids, int64_t n
     free(dirs), free(scores), free(node), free(keys);
     return -1;
   }
-  rb_proxy_tree(centers, weights, caps, children, d, dirs);
+  rb_proxy_tree(centers, weights, caps, children, d, proxy, dirs);
   float v[RB_MAX_D], u[RB_MAX_D];
   for (int64_t t = 0; t < n; ++t) {
     const uint16_t* row = x + (int64_t)ids[t] * d;
@@ -289,9 +307,13 @@ static int rb_split_node(const uint16_t* x, int d, const int32_t* ids, int64_t n
  * budget_0 .. budget_{children-1}].  perm [rows, tokens] int32: leaves in order, then the
  * N mod 64 protected remainder tokens in root order.  Returns 0, or a negative error.
  */
-int orc_rb_tree(const uint16_t* x, int rows, int tokens, int d, const int32_t* root_order, const int32_t* schedule,
-                int32_t* perm) {
+int orc_rb_tree_proxy(const uint16_t* x, int rows, int tokens, int d, const int32_t* root_order,
+                      const int32_t* schedule, int iterations, int endpoint_seeds, const int32_t* frozen,
+                      int32_t* perm) {
   if (d % RB_LANES != 0 || d > RB_MAX_D || tokens < 64) return -10;
+  if (iterations != 0 && iterations != 1 && iterations != 2 && iterations != 4) return -15;
+  const RbProxy proxy_controls = {iterations, endpoint_seeds != 0};
+  const RbProxy* proxy = &proxy_controls;
   const int rem = tokens % 64;
   const int64_t active = tokens - rem;
   int32_t* cur = (int32_t*)malloc(sizeof(int32_t) * (size_t)tokens);
@@ -311,7 +333,17 @@ int orc_rb_tree(const uint16_t* x, int rows, int tokens, int d, const int32_t* r
     const uint16_t* xr = x + (int64_t)r * tokens * d;
     int32_t* pr = perm + (int64_t)r * tokens;
     memset(excluded, 0, (size_t)tokens);
-    if (rem) {
+    if (rem && frozen) { /* the caller's protected remainder (landmark_tree_clustering.py:103-119) */
+      for (int k = 0; k < rem; ++k) {
+        const int32_t id = frozen[(int64_t)r * rem + k];
+        if (id < 0 || id >= tokens || excluded[id]) {
+          rc = -16;
+          break;
+        }
+        excluded[id] = 1;
+      }
+      if (rc) break;
+    } else if (rem) {
       orc_rb_norms(xr, tokens, d, norms);
       for (int k = 0; k < rem; ++k) {
         int best = -1;
@@ -372,7 +404,7 @@ int orc_rb_tree(const uint16_t* x, int rows, int tokens, int d, const int32_t* r
           nseg_leaves[nn++] = schedule[found + 2 + c];
           off += caps[c];
         }
-        rc = rb_split_node(xr, d, cur + seg_start[s], 64 * seg_leaves[s], caps, children, nxt + seg_start[s]);
+        rc = rb_split_node(xr, d, cur + seg_start[s], 64 * seg_leaves[s], caps, children, proxy, nxt + seg_start[s]);
       }
       int32_t* t = cur;
       cur = nxt;
@@ -389,4 +421,11 @@ done:
   free(cur), free(nxt), free(norms), free(excluded);
   free(seg_start), free(seg_leaves), free(nseg_start), free(nseg_leaves);
   return rc;
+}
+
+/* The production proxy controls: two mean updates from the farthest pair. */
+int orc_rb_tree(const uint16_t* x, int rows, int tokens, int d, const int32_t* root_order, const int32_t* schedule,
+                int32_t* perm) {
+  return orc_rb_tree_proxy(x, rows, tokens, d, root_order, schedule, rb_default_proxy.iterations,
+                           rb_default_proxy.endpoint_seeds, NULL, perm);
 }

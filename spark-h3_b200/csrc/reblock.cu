@@ -368,10 +368,15 @@ __global__ void __launch_bounds__(kTfThreads) reblock_transform_kernel(const __g
 // ======================================================================= tree
 // Root order without the protected remainder: the N mod 64 tokens of largest squared
 // feature norm (equal norms: lower id) go to the tail of the permutation in root order.
+// With `frozen` ([rows][N mod 64] token ids, the caller's excluded_indices) those tokens form
+// the tail instead; an id out of range is skipped, and a tail of the wrong size (out-of-range
+// or repeated ids) sets status 612.  Every write stays inside the row either way.
 __global__ void __launch_bounds__(1024) reblock_root_kernel(const __nv_bfloat16* __restrict__ F, int N, int active,
                                                             const int32_t* __restrict__ root_order,
+                                                            const int32_t* __restrict__ frozen,
                                                             float* __restrict__ norms, int32_t* __restrict__ idx0,
-                                                            int32_t* __restrict__ perm, int direct) {
+                                                            int32_t* __restrict__ perm, int direct,
+                                                            int* __restrict__ status) {
   const int r = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int rem = N - active;
@@ -380,7 +385,15 @@ __global__ void __launch_bounds__(1024) reblock_root_kernel(const __nv_bfloat16*
   __shared__ int best_i[32];
   __shared__ int counts[32][2];
   __shared__ int base[2];
-  if (rem > 0) {
+  if (rem > 0 && frozen != nullptr) {
+    for (int t = threadIdx.x; t < N; t += 1024) nr[t] = 0.f;
+    __syncthreads();
+    if (threadIdx.x < rem) {
+      const int id = frozen[(int64_t)r * rem + threadIdx.x];
+      if (id >= 0 && id < N) nr[id] = -1.0f;
+    }
+    __syncthreads();
+  } else if (rem > 0) {
     for (int t = warp; t < N; t += 32) {
       float x[4];
       load_row4(F + ((int64_t)r * N + t) * kDim, lane, x);
@@ -444,6 +457,7 @@ __global__ void __launch_bounds__(1024) reblock_root_kernel(const __nv_bfloat16*
     if (threadIdx.x == 0) base[0] += tot_in, base[1] += tot_ex;
     __syncthreads();
   }
+  if (threadIdx.x == 0 && base[1] != rem && status) atomicExch(status, 612);
 }
 
 struct TreeLevel {
@@ -570,6 +584,9 @@ __device__ __forceinline__ void quad_unit(float (&x)[8][4]) {
     for (int e = 0; e < 4; ++e) x[j][e] = __fdiv_rn(x[j][e], den);
 }
 
+// kIters: mean-update passes of the proxy tree, 0, 1, 2 (production) or 4; kEndpoint: seeds are
+// the lowest and highest valid landmark instead of the farthest pair (landmark_v2_terminal.py:43-50).
+template <int kIters, bool kEndpoint>
 __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const __nv_bfloat16* __restrict__ F, int N,
                                                                        int active, TreeLevel lv,
                                                                        const int32_t* __restrict__ idx_in,
@@ -641,7 +658,9 @@ __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const _
       const int aw = act(cur, j)[lane];
       const unsigned vmask = __ballot_sync(kFull, aw > 0);
       int first = vmask ? __ffs(vmask) - 1 : 0, second = first;
-      if (__popc(vmask) >= 2) {
+      if (kEndpoint && __popc(vmask) >= 2) {
+        second = 31 - __clz(vmask);  // the lowest and the highest valid landmark
+      } else if (__popc(vmask) >= 2) {
         // farthest valid pair, first in row-major (i, k) order
         float bv = 0.f;
         int bk = -1;
@@ -669,7 +688,9 @@ __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const _
         right[e] = __bfloat162float(S.x[second][4 * lane + e]);
       }
       int lw = 0, rw = 0;
-      for (int it = 0; it < 2; ++it) {
+      // max(1, passes) assignments; with zero updates the one assignment only hands the
+      // children their landmark weights, and the seeds give the direction
+      for (int it = 0; it < (kIters > 0 ? kIters : 1); ++it) {
         float ul[4], ur[4], dir[4];
         unit4(left, ul);
         unit4(right, ur);
@@ -697,6 +718,7 @@ __global__ void __launch_bounds__(kProxyThreads, 7) reblock_proxy_kernel(const _
         }
         lw = min(max(lc - before, 0), aw);
         rw = aw - lw;
+        if (it >= kIters) break;
         float accl[4] = {0.f, 0.f, 0.f, 0.f}, accr[4] = {0.f, 0.f, 0.f, 0.f};
         for (int jj = 0; jj < 32; ++jj) {
           const float wl = (float)__shfl_sync(kFull, lw, jj), wr = (float)__shfl_sync(kFull, rw, jj);
@@ -1532,7 +1554,9 @@ __global__ void reblock_inverse_kernel(const int32_t* __restrict__ perm, int N, 
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= total) return;
   const int64_t r = i / N;
-  inverse[r * N + perm[i]] = (int32_t)(i - r * N);
+  const int32_t p = perm[i];
+  // a malformed caller tail (status 612) can leave positions of perm unwritten
+  if (p >= 0 && p < N) inverse[r * N + p] = (int32_t)(i - r * N);
 }
 
 // ----------------------------------------------------------------- host helpers
@@ -1804,6 +1828,8 @@ extern "C" int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, in
   plan[3] = max_nodes;
   plan[4] = maxP;
   plan[5] = (int32_t)length;
+  plan[6] = 2;  // proxy controls (sb_reblock_plan_proxy): two mean updates from the farthest pair
+  plan[7] = 0;
   int64_t off = kPlanHeader + (int64_t)kLevelInts * L;
   for (int l = 0; l < L; ++l) {
     int32_t* lv = plan + kPlanHeader + kLevelInts * l;
@@ -1826,6 +1852,33 @@ extern "C" int64_t sb_reblock_plan(const int32_t* schedule, int schedule_len, in
   return length;
 }
 
+extern "C" int sb_reblock_plan_proxy(int32_t* plan, int proxy_iterations, int endpoint_seeds) {
+  SB_CHECK_ARG(plan != nullptr, "sb_reblock_plan_proxy: null plan");
+  SB_CHECK_ARG(proxy_iterations == 0 || proxy_iterations == 1 || proxy_iterations == 2 || proxy_iterations == 4,
+               "sb_reblock_plan_proxy: proxy_iterations must be 0, 1, 2, or 4, got %d", proxy_iterations);
+  SB_CHECK_ARG(endpoint_seeds == 0 || endpoint_seeds == 1,
+               "sb_reblock_plan_proxy: endpoint_seeds must be 0 (farthest_pair) or 1 (endpoint_order)");
+  plan[6] = proxy_iterations;
+  plan[7] = endpoint_seeds;
+  return SB_OK;
+}
+
+using ProxyKernel = void (*)(const __nv_bfloat16*, int, int, TreeLevel, const int32_t*, float*);
+
+// The proxy kernel for the plan's controls (validated by the caller).
+static ProxyKernel proxy_kernel_for(int iterations, int endpoint_seeds) {
+  switch (iterations * 2 + endpoint_seeds) {
+    case 0: return reblock_proxy_kernel<0, false>;
+    case 1: return reblock_proxy_kernel<0, true>;
+    case 2: return reblock_proxy_kernel<1, false>;
+    case 3: return reblock_proxy_kernel<1, true>;
+    case 5: return reblock_proxy_kernel<2, true>;
+    case 8: return reblock_proxy_kernel<4, false>;
+    case 9: return reblock_proxy_kernel<4, true>;
+    default: return reblock_proxy_kernel<2, false>;
+  }
+}
+
 // The largest node of a plan level (lh: the level's header in the plan).
 static int level_max_tokens(const int32_t* plan, const int32_t* lh) {
   int most = 0;
@@ -1838,9 +1891,9 @@ extern "C" int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows) {
   return (int64_t)workspace_layout(plan, rows).total;
 }
 
-extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
-                               const int32_t* plan_host, const int32_t* plan_device, void* workspace,
-                               int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream) {
+static int reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+                        const int32_t* frozen, const int32_t* plan_host, const int32_t* plan_device, void* workspace,
+                        int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream) {
   SB_CHECK_ARG(features && plan_host && plan_device && workspace && perm && inverse, "sb_reblock_tree: null pointer");
   SB_CHECK_ARG(D == kDim, "sb_reblock_tree: feature dimension must be 128, got %d", D);
   SB_CHECK_ARG(rows > 0 && rows < 65536, "sb_reblock_tree: rows must lie in [1, 65535]");
@@ -1849,6 +1902,9 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   SB_CHECK_ARG(tokens < (1 << 25), "sb_reblock_tree: at most 2^25 - 1 tokens per row");
   SB_CHECK_ARG(((uintptr_t)features % 16) == 0 && ((uintptr_t)workspace % 256) == 0,
                "sb_reblock_tree: features must be 16-byte and the workspace 256-byte aligned");
+  SB_CHECK_ARG((plan_host[6] == 0 || plan_host[6] == 1 || plan_host[6] == 2 || plan_host[6] == 4) &&
+                   (plan_host[7] == 0 || plan_host[7] == 1),
+               "sb_reblock_tree: the plan's proxy controls are invalid");
   const WorkspaceLayout W = workspace_layout(plan_host, rows);
   SB_CHECK_ARG((size_t)workspace_bytes >= W.total, "sb_reblock_tree: workspace holds %lld bytes, %zu needed",
                (long long)workspace_bytes, W.total);
@@ -1864,10 +1920,11 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   uint32_t* keys = reinterpret_cast<uint32_t*>(ws + W.keys);
   uint8_t* state = ws + W.state;
   const int L = plan_host[0], active = plan_host[2];
-  reblock_root_kernel<<<rows, 1024, 0, s>>>(F, tokens, active, root_order, reinterpret_cast<float*>(keys), idx[0],
-                                            perm, L == 0 ? 1 : 0);
+  reblock_root_kernel<<<rows, 1024, 0, s>>>(F, tokens, active, root_order, frozen, reinterpret_cast<float*>(keys),
+                                            idx[0], perm, L == 0 ? 1 : 0, status);
   SB_CHECK_LAUNCH("sb_reblock_tree: root");
-  cudaError_t err = cudaFuncSetAttribute(reblock_proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  const ProxyKernel proxy_kernel = proxy_kernel_for(plan_host[6], plan_host[7]);
+  cudaError_t err = cudaFuncSetAttribute(proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)proxy_smem_bytes(kMaxChildren));
   if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
   for (const void* fn : {(const void*)reblock_score3_kernel<2>, (const void*)reblock_score3_kernel<4>,
@@ -1879,8 +1936,8 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   for (int l = 0; l < L; ++l) {
     const int32_t* lh = plan_host + kPlanHeader + kLevelInts * l;
     TreeLevel lv{plan_device + lh[1], plan_device + lh[2], lh[0], lh[3], lh[4]};
-    reblock_proxy_kernel<<<dim3(lv.count, rows), kProxyThreads, proxy_smem_bytes(lv.P), s>>>(F, tokens, active, lv,
-                                                                                              idx[cur], dirs);
+    proxy_kernel<<<dim3(lv.count, rows), kProxyThreads, proxy_smem_bytes(lv.P), s>>>(F, tokens, active, lv, idx[cur],
+                                                                                      dirs);
     SB_CHECK_LAUNCH("sb_reblock_tree: proxy");
     const dim3 sgrid(ceil_div(active / 64, kScoreTiles), rows);
     switch (lv.P) {
@@ -1915,4 +1972,21 @@ extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D
   reblock_inverse_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(perm, tokens, total, inverse);
   SB_CHECK_LAUNCH("sb_reblock_tree: inverse");
   return SB_OK;
+}
+
+extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+                               const int32_t* plan_host, const int32_t* plan_device, void* workspace,
+                               int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream) {
+  return reblock_tree(features, rows, tokens, D, root_order, nullptr, plan_host, plan_device, workspace,
+                      workspace_bytes, perm, inverse, stream);
+}
+
+extern "C" int sb_reblock_tree_frozen(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+                                      const int32_t* excluded, const int32_t* plan_host, const int32_t* plan_device,
+                                      void* workspace, int64_t workspace_bytes, int32_t* perm, int32_t* inverse,
+                                      void* stream) {
+  SB_CHECK_ARG(excluded != nullptr || tokens % 64 == 0,
+               "sb_reblock_tree_frozen: excluded ids are required for the %d remainder tokens", tokens % 64);
+  return reblock_tree(features, rows, tokens, D, root_order, excluded, plan_host, plan_device, workspace,
+                      workspace_bytes, perm, inverse, stream);
 }

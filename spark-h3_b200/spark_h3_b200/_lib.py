@@ -73,8 +73,10 @@ SIGNATURES = {
     "sb_reblock_metric": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _vp, _i, ctypes.c_float, _vp, _vp]),
     "sb_reblock_transform": (_i, [_vp, _vp, _i, _i, _i, _i, _i, _vp, _vp, _vp]),
     "sb_reblock_plan": (_i64, [_vp, _i, _i, _vp, _i64]),
+    "sb_reblock_plan_proxy": (_i, [_vp, _i, _i]),
     "sb_reblock_workspace_bytes": (_i64, [_vp, _i]),
     "sb_reblock_tree": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "sb_reblock_tree_frozen": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
 }
 
 

@@ -124,7 +124,9 @@ class ReblockPlan:
     reused for every call of that shape; scratch is kept per row count."""
 
     def __init__(self, tokens: int, children=16, *, grid_shape=None, fanout_mode: str = "power_of_two_fanout",
-                 final_fanout=None, root_fanout=None, initial_order: str = "flat", device=None):
+                 final_fanout=None, root_fanout=None, initial_order: str = "flat", proxy_iterations: int = 2,
+                 seed_rule: str = "farthest_pair", device=None):
+        proxy_iterations, seed_rule = normalize_proxy_controls(proxy_iterations, seed_rule)
         if tokens < BLOCK:
             raise ValueError("landmark-tree-v2 requires at least 64 non-empty rows")
         grid = _grid_tuple(grid_shape) if grid_shape is not None else (1, 1, tokens)
@@ -141,6 +143,9 @@ class ReblockPlan:
         self.plan_host = np.zeros(int(length), dtype=np.int32)
         _lib.check(int(_lib.load().sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens,
                                                    self.plan_host.ctypes.data, int(length))), "sb_reblock_plan")
+        _lib.check(int(_lib.load().sb_reblock_plan_proxy(self.plan_host.ctypes.data, proxy_iterations,
+                                                         int(seed_rule == "endpoint_order"))), "sb_reblock_plan_proxy")
+        self.proxy_iterations, self.seed_rule = proxy_iterations, seed_rule
         self.plan_device = torch.from_numpy(self.plan_host).to(self.device)
         order = initial_token_indices(grid, initial_order)
         self.initial_order = initial_order
@@ -161,24 +166,33 @@ class ReblockPlan:
             self._workspace[rows] = ws
         return ws
 
-    def run(self, features: torch.Tensor, perm: torch.Tensor | None = None, inverse: torch.Tensor | None = None):
-        """features [rows, tokens, 128] bf16 (CUDA) -> (permutation, inverse) int32 [rows, tokens]."""
+    def run(self, features: torch.Tensor, perm: torch.Tensor | None = None, inverse: torch.Tensor | None = None,
+            excluded_indices: torch.Tensor | None = None):
+        """features [rows, tokens, 128] bf16 (CUDA) -> (permutation, inverse) int32 [rows, tokens].
+        excluded_indices [rows, tokens mod 64]: the protected remainder chosen by the caller
+        instead of the largest-norm tokens (landmark_tree_clustering.py:99-119, same checks)."""
         if features.dim() != 3 or features.shape[1] != self.tokens:
             raise ValueError(f"features must be [rows, {self.tokens}, D]")
         if features.dtype != torch.bfloat16:
             raise RuntimeError("the CUDA landmark tree takes bf16 features")
         device = _require_cuda(features)
         rows, tokens, dim = features.shape
+        frozen = None if excluded_indices is None else validate_excluded(excluded_indices, rows, tokens, device)
         if perm is None:
             perm = torch.empty((rows, tokens), dtype=torch.int32, device=device)
         if inverse is None:
             inverse = torch.empty((rows, tokens), dtype=torch.int32, device=device)
         ws = self.workspace(rows)
+        root = None if self.root is None else self.root.data_ptr()
         with torch.cuda.device(device):
-            _lib.call("sb_reblock_tree", features.data_ptr(), rows, tokens, dim,
-                      None if self.root is None else self.root.data_ptr(), self.plan_host.ctypes.data,
-                      self.plan_device.data_ptr(), ws.data_ptr(), ws.numel(), perm.data_ptr(), inverse.data_ptr(),
-                      _stream(device))
+            if frozen is None:
+                _lib.call("sb_reblock_tree", features.data_ptr(), rows, tokens, dim, root, self.plan_host.ctypes.data,
+                          self.plan_device.data_ptr(), ws.data_ptr(), ws.numel(), perm.data_ptr(), inverse.data_ptr(),
+                          _stream(device))
+            else:
+                _lib.call("sb_reblock_tree_frozen", features.data_ptr(), rows, tokens, dim, root, frozen.data_ptr(),
+                          self.plan_host.ctypes.data, self.plan_device.data_ptr(), ws.data_ptr(), ws.numel(),
+                          perm.data_ptr(), inverse.data_ptr(), _stream(device))
         return perm, inverse
 
 
@@ -231,13 +245,49 @@ class LandmarkTreeV2Result:
 _PLANS: dict[tuple, ReblockPlan] = {}
 
 
-def _plan(tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device) -> ReblockPlan:
+def validate_excluded(excluded_indices, rows: int, tokens: int, device) -> torch.Tensor:
+    """The caller's protected remainder, checked as landmark_tree_clustering.py:104-114 checks
+    it (same messages): shape (rows, tokens mod 64), ids in range, unique per row.  Returns
+    int32 ids on the device."""
+    remainder = tokens % BLOCK
+    excluded = torch.as_tensor(excluded_indices).to(device=device, dtype=torch.long)
+    if tuple(excluded.shape) != (rows, remainder):
+        raise ValueError(f"excluded_indices must have shape {(rows, remainder)}")
+    if remainder:
+        if bool(((excluded < 0) | (excluded >= tokens)).any()):
+            raise ValueError("excluded_indices must lie in the original token range")
+        ordered = excluded.sort(1).values
+        if bool((ordered[:, 1:] == ordered[:, :-1]).any()):
+            raise ValueError("excluded_indices must be unique per batch row")
+    return excluded.to(torch.int32).contiguous()
+
+
+def normalize_proxy_controls(proxy_iterations, seed_rule, update_rule="mean"):
+    """The proxy controls of landmark_v2_terminal.py:43-50 (_normalize_proxy_controls), same
+    messages.  The medoid update is refused: its choice between the two landmarks of a
+    two-landmark side is an exact tie in real arithmetic, and the reference settles it by the
+    rounding of its BLAS distance products, which no other arithmetic reproduces (on the
+    reference's own fixtures, 31-39 % of permutation positions agreed)."""
+    if type(proxy_iterations) is not int or proxy_iterations not in (0, 1, 2, 4):
+        raise ValueError("proxy_iterations must be 0, 1, 2, or 4")
+    if seed_rule not in ("farthest_pair", "endpoint_order"):
+        raise ValueError("seed_rule must be farthest_pair or endpoint_order")
+    if update_rule not in ("mean", "medoid"):
+        raise ValueError("update_rule must be mean or medoid")
+    if update_rule != "mean":
+        raise NotImplementedError("the B200 landmark tree implements update_rule='mean' only")
+    return proxy_iterations, seed_rule
+
+
+def _plan(tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device,
+          proxy_iterations: int = 2, seed_rule: str = "farthest_pair") -> ReblockPlan:
     key = (tokens, children if isinstance(children, int) else tuple(children), grid, fanout_mode, final_fanout,
-           root_fanout, initial_order, str(device))
+           root_fanout, initial_order, proxy_iterations, seed_rule, str(device))
     plan = _PLANS.get(key)
     if plan is None:
         plan = ReblockPlan(tokens, children, grid_shape=grid, fanout_mode=fanout_mode, final_fanout=final_fanout,
-                           root_fanout=root_fanout, initial_order=initial_order, device=device)
+                           root_fanout=root_fanout, initial_order=initial_order, proxy_iterations=proxy_iterations,
+                           seed_rule=seed_rule, device=device)
         _PLANS[key] = plan
     return plan
 
@@ -253,14 +303,20 @@ def spark_reblock(samples: torch.Tensor, *, grid_shape, initial_order: str = "fl
     """Strict 64-token leaves of bf16 samples [..., N, 128] (landmark_tree_v2.py:835-901).
 
     Implements the production defaults (cosine distance, single tokens, 32 midpoint
-    landmarks, linear aggregation, parent order, two mean-update proxy iterations from the
-    farthest pair) with every fanout mode of reblock_hierarchy.py (power_of_two_fanout,
-    arbitrary_fanout, power_of_two_arbitrary_final: nodes of 2 to 64 children, split over
-    landmark_v2_terminal.py's breadth-first topology); other options raise
-    NotImplementedError."""
-    for name, value in options.items():
+    landmarks, linear aggregation, parent order) with every fanout mode of
+    reblock_hierarchy.py (power_of_two_fanout, arbitrary_fanout, power_of_two_arbitrary_final:
+    nodes of 2 to 64 children, split over landmark_v2_terminal.py's breadth-first topology),
+    the proxy controls proxy_iterations (0, 1, 2, 4) and seed_rule (farthest_pair,
+    endpoint_order) with mean updates, and a caller-chosen protected remainder
+    (excluded_indices [rows, N mod 64]); other options raise NotImplementedError."""
+    for name in options:
         if name not in _DEFAULTS:
             raise TypeError(f"spark_reblock() got an unexpected keyword argument {name!r}")
+    proxy_iterations, seed_rule = normalize_proxy_controls(
+        options.pop("proxy_iterations", 2), options.pop("seed_rule", "farthest_pair"),
+        options.pop("update_rule", "mean"))
+    excluded_indices = options.pop("excluded_indices", None)
+    for name, value in options.items():
         default = _DEFAULTS[name]
         if (value is not default) and value != default:
             raise NotImplementedError(f"the B200 landmark tree implements {name}={default!r} only")
@@ -277,8 +333,8 @@ def spark_reblock(samples: torch.Tensor, *, grid_shape, initial_order: str = "fl
     children = fanout if fanout is not None else max_children
     flat = samples.reshape(-1, tokens, dim).to(torch.bfloat16).contiguous()
     plan = _plan(tokens, children, _grid_tuple(grid_shape), fanout_mode, final_fanout, root_fanout, initial_order,
-                 flat.device)
-    perm, inverse = plan.run(flat)
+                 flat.device, proxy_iterations, seed_rule)
+    perm, inverse = plan.run(flat, excluded_indices=excluded_indices)
     perm64, inv64 = perm.long(), inverse.long()
     active = plan.active_tokens
     return LandmarkTreeV2Result(
@@ -323,7 +379,8 @@ _SAMPLES: dict[tuple, torch.Tensor] = {}
 
 def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, grid, *, children=16,
                           fanout_mode: str = "power_of_two_fanout", final_fanout=None, root_fanout=None,
-                          ridge: float = 1e-3, initial_order: str = "flat", use_graph: bool = True):
+                          ridge: float = 1e-3, initial_order: str = "flat", use_graph: bool = True,
+                          proxy_iterations: int = 2, seed_rule: str = "farthest_pair"):
     """Paired opposite-second-moment Q/K permutations (spark_integration.py:394-851 with
     layout reuse "independent"): returns (q_perm, q_inv, k_perm, k_inv), int32 [B, H, video],
     plus the reblock hierarchy.  With use_graph the tree replays a captured CUDA graph over
@@ -338,7 +395,8 @@ def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, g
         samples = torch.from_numpy(ids.astype(np.int32)).to(device)
         _SAMPLES[key] = samples
     factors = metric_factors(q, k, samples, ridge)
-    plan = _plan(video_tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device)
+    plan = _plan(video_tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device,
+                 proxy_iterations, seed_rule)
     if use_graph:
         transform(q, k, factors, video_tokens, out=plan.features_buffer(2 * B * H))
         perm, inverse = plan.replay(2 * B * H)

@@ -33,6 +33,11 @@ Fixtures:
                   power_of_two_arbitrary_final (reblock_hierarchy.py:124-160), whose nodes
                   split into non-power-of-two child counts over landmark_v2_terminal.py's
                   split topology; the permutation and the hierarchy's split budgets per case
+  reblock_tree_proxy.npz  the same with the proxy controls of landmark_v2_terminal.py:43-50
+                  (proxy_iterations 0 / 1 / 4, seed_rule endpoint_order), which the reference
+                  always runs through node_split_reference
+  reblock_tree_frozen.npz  the same with a caller-chosen protected remainder (excluded_indices,
+                  landmark_tree_clustering.py:99-119): the seeded ids and the permutation
   reblock_qk.npz  the full paired Q/K reblock (_landmark_tree_v2_qk_block_permutations,
                   spark_integration.py:735-851, CPU controller, mode "full") on clustered
                   synthetic Q/K: Hilbert metric samples, the Cholesky factors, the bf16
@@ -312,6 +317,55 @@ def reblock_tree_modes_fixture():
     np.savez_compressed(HERE / "reblock_tree_modes.npz", **out)
 
 
+REBLOCK_TREE_PROXY_CASES = [
+    # (name, tokens, children, fanout mode, grid, proxy_iterations, seed_rule, seed)
+    ("iter0_endpoint", 4096, 4, "power_of_two_fanout", (1, 64, 64), 0, "endpoint_order", 31),
+    ("iter1_farthest", 8192, 16, "power_of_two_fanout", (2, 64, 64), 1, "farthest_pair", 32),
+    ("iter4_farthest", 6016, 8, "power_of_two_fanout", (4, 32, 47), 4, "farthest_pair", 33),
+    ("iter1_endpoint", 4133, 16, "power_of_two_fanout", (1, 1, 4133), 1, "endpoint_order", 34),
+    ("iter0_arbitrary", 6016, 8, "arbitrary_fanout", (4, 32, 47), 0, "farthest_pair", 35),
+    ("iter4_endpoint_arbitrary", 20000, 16, "arbitrary_fanout", (5, 40, 100), 4, "endpoint_order", 36),
+]
+
+
+def reblock_tree_proxy_fixture():
+    from h3_sparse_attention.landmark_tree_v2 import recursive_landmark_tree_v2_reference
+
+    out = {}
+    for name, tokens, children, mode, grid, iterations, seed_rule, seed in REBLOCK_TREE_PROXY_CASES:
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+        ref = recursive_landmark_tree_v2_reference(x, grid_shape=grid, max_children=children, fanout_mode=mode,
+                                                   proxy_iterations=iterations, seed_rule=seed_rule)
+        out[f"{name}_perm"] = ref.permutation.numpy().astype(np.int32)
+        out[f"{name}_digest"] = np.array(digest(x))
+    np.savez_compressed(HERE / "reblock_tree_proxy.npz", **out)
+
+
+REBLOCK_TREE_FROZEN_CASES = [
+    # (name, tokens, children, grid, initial order, seed)
+    ("frozen_remainder", 4133, 16, (1, 1, 4133), "flat", 41),
+    ("frozen_two", 130, 16, (1, 2, 65), "flat", 42),
+    ("frozen_hilbert", 20000, 16, (5, 40, 100), "hilbert_thw", 43),
+]
+
+
+def reblock_tree_frozen_fixture():
+    from h3_sparse_attention.landmark_tree_v2 import recursive_landmark_tree_v2_reference
+
+    out = {}
+    for name, tokens, children, grid, order, seed in REBLOCK_TREE_FROZEN_CASES:
+        g = torch.Generator().manual_seed(seed)
+        x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+        excluded = torch.stack([torch.randperm(tokens, generator=g)[:tokens % 64] for _ in range(2)])
+        ref = recursive_landmark_tree_v2_reference(x, grid_shape=grid, max_children=children, initial_order=order,
+                                                   excluded_indices=excluded)
+        out[f"{name}_perm"] = ref.permutation.numpy().astype(np.int32)
+        out[f"{name}_excluded"] = excluded.numpy().astype(np.int32)
+        out[f"{name}_digest"] = np.array(digest(x))
+    np.savez_compressed(HERE / "reblock_tree_frozen.npz", **out)
+
+
 def reblock_qk_fixture():
     from types import SimpleNamespace
 
@@ -354,6 +408,8 @@ def main():
     summaries_and_attention()
     reblock_tree_fixture()
     reblock_tree_modes_fixture()
+    reblock_tree_proxy_fixture()
+    reblock_tree_frozen_fixture()
     reblock_qk_fixture()
     print("golden fixtures written to", HERE)
 

@@ -103,6 +103,87 @@ def test_tree_fanout_modes_match_oracle(cuda_device, tokens, children, final_fan
     assert np.array_equal(result.permutation.cpu().numpy().reshape(-1, tokens), ref)
 
 
+TREE_PROXY_CASES = [
+    # (name, tokens, children, fanout mode, grid, proxy_iterations, seed_rule, seed)
+    ("iter0_endpoint", 4096, 4, "power_of_two_fanout", (1, 64, 64), 0, "endpoint_order", 31),
+    ("iter1_farthest", 8192, 16, "power_of_two_fanout", (2, 64, 64), 1, "farthest_pair", 32),
+    ("iter4_farthest", 6016, 8, "power_of_two_fanout", (4, 32, 47), 4, "farthest_pair", 33),
+    ("iter1_endpoint", 4133, 16, "power_of_two_fanout", (1, 1, 4133), 1, "endpoint_order", 34),
+    ("iter0_arbitrary", 6016, 8, "arbitrary_fanout", (4, 32, 47), 0, "farthest_pair", 35),
+    ("iter4_endpoint_arbitrary", 20000, 16, "arbitrary_fanout", (5, 40, 100), 4, "endpoint_order", 36),
+]
+
+
+@pytest.mark.parametrize("name,tokens,children,mode,grid,iterations,seed_rule,seed", TREE_PROXY_CASES)
+def test_tree_proxy_controls_match_reference_fixtures(cuda_device, name, tokens, children, mode, grid, iterations,
+                                                      seed_rule, seed):
+    """Proxy controls (0, 1 or 4 mean updates; endpoint-order seeds): the GPU tree reproduces
+    the reference's own CPU tree, which runs them through node_split_reference."""
+    z = np.load(GOLDEN / "reblock_tree_proxy.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    result = reblock.spark_reblock(x.to(cuda_device), grid_shape=grid, max_children=children, fanout_mode=mode,
+                                   proxy_iterations=iterations, seed_rule=seed_rule)
+    assert np.array_equal(result.permutation.cpu().numpy().reshape(-1, tokens), z[f"{name}_perm"])
+
+
+@pytest.mark.parametrize("iterations,seed_rule", [(0, "farthest_pair"), (1, "endpoint_order"), (4, "farthest_pair"),
+                                                  (2, "endpoint_order")])
+def test_tree_proxy_controls_match_oracle(cuda_device, iterations, seed_rule):
+    tokens, grid = 24576, (3, 64, 128)
+    g = torch.Generator().manual_seed(iterations * 7 + len(seed_rule))
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    result = reblock.spark_reblock(x.to(cuda_device), grid_shape=grid, proxy_iterations=iterations,
+                                   seed_rule=seed_rule)
+    ref, _ = oracle.reblock_tree(bits(x), grid, build_reblock_hierarchy(tokens, 16).split_budgets,
+                                 proxy_iterations=iterations, seed_rule=seed_rule)
+    assert np.array_equal(result.permutation.cpu().numpy().reshape(-1, tokens), ref)
+
+
+TREE_FROZEN_CASES = [
+    # (name, tokens, children, grid, initial order, seed)
+    ("frozen_remainder", 4133, 16, (1, 1, 4133), "flat", 41),
+    ("frozen_two", 130, 16, (1, 2, 65), "flat", 42),
+    ("frozen_hilbert", 20000, 16, (5, 40, 100), "hilbert_thw", 43),
+]
+
+
+@pytest.mark.parametrize("name,tokens,children,grid,order,seed", TREE_FROZEN_CASES)
+def test_tree_frozen_remainder_matches_reference_fixtures(cuda_device, name, tokens, children, grid, order, seed):
+    """excluded_indices: the caller's ids form the tail in root order, and the GPU tree
+    reproduces the reference's own permutation around them."""
+    z = np.load(GOLDEN / "reblock_tree_frozen.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    excluded = torch.from_numpy(z[f"{name}_excluded"]).to(cuda_device)
+    result = reblock.spark_reblock(x.to(cuda_device), grid_shape=grid, max_children=children, initial_order=order,
+                                   excluded_indices=excluded)
+    assert np.array_equal(result.permutation.cpu().numpy().reshape(-1, tokens), z[f"{name}_perm"])
+    assert ops.read_device_status(cuda_device) == 0
+
+
+def test_tree_frozen_tail_of_the_wrong_size_sets_status(cuda_device):
+    """A repeated id (which the Python layer refuses) reaching the C ABI: every write stays
+    in the row, and the kernel reports status 612."""
+    from spark_h3_b200 import _lib
+
+    tokens = 130
+    ops.read_device_status(cuda_device)  # start from a clear status word
+    plan = reblock._plan(tokens, 16, (1, 2, 65), "power_of_two_fanout", None, None, "flat", cuda_device)
+    x = torch.randn(1, tokens, 128, device=cuda_device).to(torch.bfloat16)
+    frozen = torch.tensor([[5, 5]], device=cuda_device, dtype=torch.int32)
+    perm = torch.full((1, tokens), -1, device=cuda_device, dtype=torch.int32)
+    inverse = torch.empty_like(perm)
+    ws = plan.workspace(1)
+    lib = _lib.load()
+    rc = lib.sb_reblock_tree_frozen(x.data_ptr(), 1, tokens, 128, None, frozen.data_ptr(), plan.plan_host.ctypes.data,
+                                    plan.plan_device.data_ptr(), ws.data_ptr(), ws.numel(), perm.data_ptr(),
+                                    inverse.data_ptr(), torch.cuda.current_stream(cuda_device).cuda_stream)
+    assert rc == 0
+    assert ops.read_device_status(cuda_device) == 612
+    assert int(perm.min()) >= -1 and int(perm.max()) < tokens
+
+
 def test_tree_duplicate_features_tie_break(cuda_device):
     """Repeated rows give exactly equal scores: ties resolve to the lower token id."""
     g = torch.Generator().manual_seed(3)

@@ -95,8 +95,52 @@ def test_spark_reblock_rejects_unimplemented_options():
     x = torch.zeros(1, 128, 128, dtype=torch.bfloat16)
     with pytest.raises(NotImplementedError, match="distance"):
         reblock.spark_reblock(x, grid_shape=(1, 1, 128), distance="euclidean")
+    with pytest.raises(NotImplementedError, match="update_rule"):
+        reblock.spark_reblock(x, grid_shape=(1, 1, 128), update_rule="medoid")
     with pytest.raises(TypeError):
         reblock.spark_reblock(x, grid_shape=(1, 1, 128), colour="blue")
+
+
+@pytest.mark.parametrize("kwargs,match", [({"proxy_iterations": 3}, "proxy_iterations"),
+                                          ({"seed_rule": "random"}, "seed_rule"),
+                                          ({"update_rule": "median"}, "update_rule")])
+def test_proxy_controls_reject_undefined_semantics(kwargs, match):
+    """The reference's own cases (tests/test_reblock_proxy_controls.py:113-126), same messages."""
+    import torch
+
+    with pytest.raises(ValueError, match=match):
+        reblock.spark_reblock(torch.zeros(1, 128, 128, dtype=torch.bfloat16), grid_shape=(1, 2, 64), **kwargs)
+
+
+@pytest.mark.parametrize("excluded,match", [([[1]], "shape"), ([[1, 1]], "unique"), ([[1, 130]], "range")])
+def test_frozen_excluded_indices_are_strictly_validated(excluded, match):
+    """The reference's own cases (tests/test_reblock_proxy_controls.py:159-173), same messages."""
+    import torch
+
+    with pytest.raises(ValueError, match=match):
+        reblock.validate_excluded(torch.tensor(excluded), 1, 130, torch.device("cpu"))
+    ids = reblock.validate_excluded(torch.tensor([[77, 3]]), 1, 130, torch.device("cpu"))
+    assert ids.dtype == torch.int32 and ids.tolist() == [[77, 3]]
+
+
+def test_plan_proxy_controls():
+    from spark_h3_b200 import _lib
+
+    lib = _lib.load()
+    h = build_reblock_hierarchy(4096, 16)
+    schedule = reblock._schedule(h)
+    n = lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), 4096, None, 0)
+    plan = np.zeros(n, dtype=np.int32)
+    assert lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), 4096, plan.ctypes.data, n) == n
+    assert list(plan[6:8]) == [2, 0]  # the production controls
+    for iterations, endpoint in ((0, 1), (1, 0), (4, 1), (2, 0)):
+        assert lib.sb_reblock_plan_proxy(plan.ctypes.data, iterations, endpoint) == 0
+        assert list(plan[6:8]) == [iterations, endpoint]
+    for iterations, endpoint in ((3, 0), (-1, 0), (8, 0), (2, 2)):
+        assert lib.sb_reblock_plan_proxy(plan.ctypes.data, iterations, endpoint) < 0
+        assert list(plan[6:8]) == [2, 0]
+    assert lib.sb_reblock_plan_proxy(plan.ctypes.data, 3, 0) < 0
+    assert "proxy_iterations must be 0, 1, 2, or 4" in lib.sb_last_error().decode()
 
 
 def test_reblock_reuse_across_layers(monkeypatch):

@@ -79,6 +79,55 @@ def test_tree_fanout_modes_match_reference(name, tokens, children, final_fanout,
     assert np.array_equal(np.take_along_axis(inverse, perm, 1), np.broadcast_to(np.arange(tokens), perm.shape))
 
 
+TREE_PROXY_CASES = [
+    # (name, tokens, children, fanout mode, grid, proxy_iterations, seed_rule, seed)
+    ("iter0_endpoint", 4096, 4, "power_of_two_fanout", (1, 64, 64), 0, "endpoint_order", 31),
+    ("iter1_farthest", 8192, 16, "power_of_two_fanout", (2, 64, 64), 1, "farthest_pair", 32),
+    ("iter4_farthest", 6016, 8, "power_of_two_fanout", (4, 32, 47), 4, "farthest_pair", 33),
+    ("iter1_endpoint", 4133, 16, "power_of_two_fanout", (1, 1, 4133), 1, "endpoint_order", 34),
+    ("iter0_arbitrary", 6016, 8, "arbitrary_fanout", (4, 32, 47), 0, "farthest_pair", 35),
+    ("iter4_endpoint_arbitrary", 20000, 16, "arbitrary_fanout", (5, 40, 100), 4, "endpoint_order", 36),
+]
+
+
+@pytest.mark.parametrize("name,tokens,children,mode,grid,iterations,seed_rule,seed", TREE_PROXY_CASES)
+def test_tree_proxy_controls_match_reference(name, tokens, children, mode, grid, iterations, seed_rule, seed):
+    """Proxy controls (landmark_v2_terminal.py:43-148): 0, 1 or 4 mean updates and
+    endpoint-order seeds; the reference's own CPU tree gave the permutations."""
+    z = np.load(GOLDEN / "reblock_tree_proxy.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    assert digest(x) == str(z[f"{name}_digest"]), "seeded features differ from the ones the fixture used"
+    hierarchy = build_reblock_hierarchy(tokens, children, fanout_mode=mode)
+    perm, _ = oracle.reblock_tree(bits(x), grid, hierarchy.split_budgets, proxy_iterations=iterations,
+                                  seed_rule=seed_rule)
+    assert np.array_equal(perm, z[f"{name}_perm"])
+
+
+TREE_FROZEN_CASES = [
+    # (name, tokens, children, grid, initial order, seed)
+    ("frozen_remainder", 4133, 16, (1, 1, 4133), "flat", 41),
+    ("frozen_two", 130, 16, (1, 2, 65), "flat", 42),
+    ("frozen_hilbert", 20000, 16, (5, 40, 100), "hilbert_thw", 43),
+]
+
+
+@pytest.mark.parametrize("name,tokens,children,grid,order,seed", TREE_FROZEN_CASES)
+def test_tree_frozen_remainder_matches_reference(name, tokens, children, grid, order, seed):
+    """A caller-chosen protected remainder (excluded_indices): the ids form the tail in root
+    order, whatever their norms, and the tree splits the rest as the reference does."""
+    z = np.load(GOLDEN / "reblock_tree_frozen.npz")
+    g = torch.Generator().manual_seed(seed)
+    x = torch.randn(2, tokens, 128, generator=g).to(torch.bfloat16)
+    assert digest(x) == str(z[f"{name}_digest"]), "seeded features differ from the ones the fixture used"
+    excluded = z[f"{name}_excluded"]
+    perm, _ = oracle.reblock_tree(bits(x), grid, build_reblock_hierarchy(tokens, children).split_budgets, order,
+                                  excluded=excluded)
+    assert np.array_equal(perm, z[f"{name}_perm"])
+    tail = perm[:, tokens - tokens % 64:]
+    assert (np.sort(tail, 1) == np.sort(excluded, 1)).all()
+
+
 def test_qk_reblock_matches_reference():
     z = np.load(GOLDEN / "reblock_qk.npz")
     grid = tuple(int(g) for g in z["grid"])
