@@ -380,11 +380,18 @@ _SAMPLES: dict[tuple, torch.Tensor] = {}
 def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, grid, *, children=16,
                           fanout_mode: str = "power_of_two_fanout", final_fanout=None, root_fanout=None,
                           ridge: float = 1e-3, initial_order: str = "flat", use_graph: bool = True,
-                          proxy_iterations: int = 2, seed_rule: str = "farthest_pair"):
-    """Paired opposite-second-moment Q/K permutations (spark_integration.py:394-851 with
-    layout reuse "independent"): returns (q_perm, q_inv, k_perm, k_inv), int32 [B, H, video],
-    plus the reblock hierarchy.  With use_graph the tree replays a captured CUDA graph over
-    the plan's static features buffer (the transform writes into it)."""
+                          proxy_iterations: int = 2, seed_rule: str = "farthest_pair",
+                          layout_reuse: str = "independent"):
+    """Paired opposite-second-moment Q/K permutations (spark_integration.py:394-851):
+    returns (q_perm, q_inv, k_perm, k_inv), int32 [B, H, video], plus the reblock hierarchy.
+
+    layout_reuse (spark_integration.py:365-380, 562-585, 725-729): "independent" builds a tree
+    for K (features K . Lq) and one for Q (features Q . Lk); "q_from_k" builds only K's and Q
+    takes the same permutation; "k_from_q" builds only Q's and K takes it.  With use_graph the
+    independent trees replay a captured CUDA graph over the plan's static features buffer
+    (the transform writes into it); a shared layout runs its one tree eagerly."""
+    if layout_reuse not in ("independent", "q_from_k", "k_from_q"):
+        raise ValueError(f"unknown layout reuse mode: {layout_reuse}")
     device = _require_cuda(q, k)
     B, T, H, D = q.shape
     grid = _grid_tuple(grid)
@@ -397,12 +404,19 @@ def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, g
     factors = metric_factors(q, k, samples, ridge)
     plan = _plan(video_tokens, children, grid, fanout_mode, final_fanout, root_fanout, initial_order, device,
                  proxy_iterations, seed_rule)
+    BH = B * H
+    shape = (B, H, video_tokens)
+    if layout_reuse != "independent":
+        # rows [0, BH) of the features are K . Lq, rows [BH, 2BH) Q . Lk
+        features = transform(q, k, factors, video_tokens)
+        source = features[:BH] if layout_reuse == "q_from_k" else features[BH:]
+        perm, inverse = plan.run(source)
+        perm, inverse = perm.view(shape), inverse.view(shape)
+        return perm, inverse, perm, inverse, plan.hierarchy
     if use_graph:
         transform(q, k, factors, video_tokens, out=plan.features_buffer(2 * B * H))
         perm, inverse = plan.replay(2 * B * H)
     else:
         perm, inverse = plan.run(transform(q, k, factors, video_tokens))
-    BH = B * H
-    shape = (B, H, video_tokens)
     return (perm[BH:].view(shape), inverse[BH:].view(shape), perm[:BH].view(shape), inverse[:BH].view(shape),
             plan.hierarchy)

@@ -300,6 +300,54 @@ def test_full_mode_layer(cuda_device):
     assert controller.counts["sol_landmark_preprocess_calls"] == 1
 
 
+def test_shared_layouts_take_one_sides_tree(cuda_device):
+    """landmark_tree_v2_layout_reuse (spark_integration.py:365-380, 562-585, 725-729):
+    "q_from_k" gives Q the permutation of K's tree, "k_from_q" gives K the permutation of Q's,
+    each equal bit for bit to that side's permutation in the independent layout."""
+    grid, H = (2, 16, 40), 2
+    q, k, _ = make_qkv(grid, H, 128, seed=8, dtype=torch.bfloat16, clustered=True, device=cuda_device)
+    T = q.shape[1]
+    qp, qi, kp, ki, _ = reblock.qk_block_permutations(q, k, T, grid)
+    for mode, (perm, inverse) in (("q_from_k", (kp, ki)), ("k_from_q", (qp, qi))):
+        sqp, sqi, skp, ski, _ = reblock.qk_block_permutations(q, k, T, grid, layout_reuse=mode)
+        assert torch.equal(sqp, perm) and torch.equal(skp, perm)
+        assert torch.equal(sqi, inverse) and torch.equal(ski, inverse)
+    with pytest.raises(ValueError, match="layout reuse"):
+        reblock.qk_block_permutations(q, k, T, grid, layout_reuse="both")
+
+
+def test_full_mode_layer_with_exact_block_radius(cuda_device):
+    """mode='full' with sol_exact_block_radius, which the reference allows only on a shared
+    layout: the layer equals the oracle layer, with the same radius, evaluated on Q/K/V
+    permuted by K's tree and permuted back."""
+    from spark_h3_b200.attention import spark_attention_bthd
+    from spark_h3_b200.config import H3SparseAttentionConfig
+    from spark_h3_b200.layout import PackedLayout
+    from spark_h3_b200.processor import _Controller
+
+    grid, H = (2, 16, 40), 2
+    q, k, v = make_qkv(grid, H, 128, seed=6, dtype=torch.bfloat16, q_scale=128 ** -0.5, clustered=True,
+                       device=cuda_device)
+    T = q.shape[1]
+    cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode="full", sol_route_topk_ratio=0.2,
+                                        sol_exact_block_radius=1, landmark_tree_v2_layout_reuse="q_from_k")
+    controller = _Controller(cfg)
+    ids = torch.arange(T)
+    layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=grid, video_tokens=T, sequence_length=T,
+                          video_positions=torch.zeros(T, 3, dtype=torch.long))
+    out = spark_attention_bthd(controller, q, k, v, layout, 0)
+    qp, qi, kp, _, _ = reblock.qk_block_permutations(q, k, T, grid, layout_reuse="q_from_k")
+    assert torch.equal(qp, kp)
+    q2, k2, v2 = (ops.headwise_permute(t, kp, T) for t in (q, k, v))
+    res = oracle.spark_layer(*(oracle.Tensor(bits(t), "bfloat16") for t in (q2, k2, v2)), block=64,
+                             topk_ratio=0.2, local_radius=1)
+    ref = torch.from_numpy(res["out"]).to(cuda_device)
+    expected = ops.headwise_permute(ref.to(torch.float32).contiguous(), qi, T)
+    diff = (out.float() - expected).abs().max().item()
+    cos = torch.nn.functional.cosine_similarity(out.float().flatten(), expected.flatten(), dim=0).item()
+    assert diff <= 2e-2 and cos >= 0.9995
+
+
 def test_graph_replay_matches_eager(cuda_device):
     """qk_block_permutations through the captured CUDA graph (first call eager, second
     captures, later calls replay) gives the eager pipeline's permutations, bit for bit, on
