@@ -270,9 +270,11 @@ def test_transform_and_tree_reproduce_reference_permutations_given_its_factors(c
     assert np.array_equal(inverse.cpu().numpy(), reference_inv)
 
 
-def test_full_mode_layer(cuda_device):
-    """mode='full': the layer equals the oracle Spark layer evaluated on the permuted Q/K/V,
-    inverse-permuted, for the permutations the GPU chose (checked bit-exact above)."""
+@pytest.mark.parametrize("mode", ["full", "reblock_only"])
+def test_full_mode_layer(cuda_device, mode):
+    """mode='full' (reblock + anchor-reweighted summaries) and 'reblock_only' (reblock + plain
+    block-mean summaries): the layer equals the oracle Spark layer evaluated on the permuted
+    Q/K/V, inverse-permuted, for the permutations the GPU chose (checked bit-exact above)."""
     from spark_h3_b200.attention import spark_attention_bthd
     from spark_h3_b200.config import H3SparseAttentionConfig
     from spark_h3_b200.layout import PackedLayout
@@ -282,7 +284,7 @@ def test_full_mode_layer(cuda_device):
     q, k, v = make_qkv(grid, H, 128, seed=5, dtype=torch.bfloat16, q_scale=128 ** -0.5, clustered=True,
                        device=cuda_device)
     T = q.shape[1]
-    cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode="full", sol_route_topk_ratio=0.2)
+    cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode=mode, sol_route_topk_ratio=0.2)
     controller = _Controller(cfg)
     ids = torch.arange(T)
     layout = PackedLayout(permutation=ids, inverse_permutation=ids, grid=grid, video_tokens=T, sequence_length=T,
@@ -290,8 +292,9 @@ def test_full_mode_layer(cuda_device):
     out = spark_attention_bthd(controller, q, k, v, layout, 0)
     qp, qi, kp, _, _ = reblock.qk_block_permutations(q, k, T, grid)
     q2, k2, v2 = (ops.headwise_permute(t, p, T) for t, p in ((q, qp), (k, kp), (v, kp)))
+    reweight = mode == "full"
     res = oracle.spark_layer(*(oracle.Tensor(bits(t), "bfloat16") for t in (q2, k2, v2)), block=64,
-                             topk_ratio=0.2)
+                             topk_ratio=0.2, weighted_kv=reweight, mass_bias=reweight)
     ref = torch.from_numpy(res["out"]).to(cuda_device)
     expected = ops.headwise_permute(ref.to(torch.float32).contiguous(), qi, T)
     diff = (out.float() - expected).abs().max().item()
