@@ -18,6 +18,7 @@
 // 16, 8, 4, 2, 1; unit(x) = x / max(sqrt(dot(x, x)), 1e-12) with IEEE division and square
 // root; weighted landmark means are fma chains over the 32 landmarks in index order.
 #include <algorithm>
+#include <cstdio>
 #include <vector>
 
 #include "common.cuh"
@@ -1891,25 +1892,37 @@ extern "C" int64_t sb_reblock_workspace_bytes(const int32_t* plan, int rows) {
   return (int64_t)workspace_layout(plan, rows).total;
 }
 
-static int reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
+// The tree's CUDA errors name the entry point the caller used.
+static int tree_cuda_error(cudaError_t err, const char* who, const char* what) {
+  char buf[160];
+  snprintf(buf, sizeof(buf), "%s: %s", who, what);
+  return cuda_error(err, buf);
+}
+#define TREE_CHECK_LAUNCH(who, what)                                     \
+  do {                                                                   \
+    cudaError_t err__ = cudaGetLastError();                              \
+    if (err__ != cudaSuccess) return tree_cuda_error(err__, who, what);  \
+  } while (0)
+
+static int reblock_tree(const char* who, const void* features, int rows, int tokens, int D, const int32_t* root_order,
                         const int32_t* frozen, const int32_t* plan_host, const int32_t* plan_device, void* workspace,
                         int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream) {
-  SB_CHECK_ARG(features && plan_host && plan_device && workspace && perm && inverse, "sb_reblock_tree: null pointer");
-  SB_CHECK_ARG(D == kDim, "sb_reblock_tree: feature dimension must be 128, got %d", D);
-  SB_CHECK_ARG(rows > 0 && rows < 65536, "sb_reblock_tree: rows must lie in [1, 65535]");
-  SB_CHECK_ARG(plan_host[1] == tokens, "sb_reblock_tree: the plan was built for %d tokens, not %d", plan_host[1],
+  SB_CHECK_ARG(features && plan_host && plan_device && workspace && perm && inverse, "%s: null pointer", who);
+  SB_CHECK_ARG(D == kDim, "%s: feature dimension must be 128, got %d", who, D);
+  SB_CHECK_ARG(rows > 0 && rows < 65536, "%s: rows must lie in [1, 65535]", who);
+  SB_CHECK_ARG(plan_host[1] == tokens, "%s: the plan was built for %d tokens, not %d", who, plan_host[1],
                tokens);
-  SB_CHECK_ARG(tokens < (1 << 25), "sb_reblock_tree: at most 2^25 - 1 tokens per row");
+  SB_CHECK_ARG(tokens < (1 << 25), "%s: at most 2^25 - 1 tokens per row", who);
   SB_CHECK_ARG(((uintptr_t)features % 16) == 0 && ((uintptr_t)workspace % 256) == 0,
-               "sb_reblock_tree: features must be 16-byte and the workspace 256-byte aligned");
+               "%s: features must be 16-byte and the workspace 256-byte aligned", who);
   SB_CHECK_ARG((plan_host[6] == 0 || plan_host[6] == 1 || plan_host[6] == 2 || plan_host[6] == 4) &&
                    (plan_host[7] == 0 || plan_host[7] == 1),
-               "sb_reblock_tree: the plan's proxy controls are invalid");
+               "%s: the plan's proxy controls are invalid", who);
   const WorkspaceLayout W = workspace_layout(plan_host, rows);
-  SB_CHECK_ARG((size_t)workspace_bytes >= W.total, "sb_reblock_tree: workspace holds %lld bytes, %zu needed",
+  SB_CHECK_ARG((size_t)workspace_bytes >= W.total, "%s: workspace holds %lld bytes, %zu needed", who,
                (long long)workspace_bytes, W.total);
   int* status = device_status_ptr();
-  if (status == nullptr) return cuda_error(cudaGetLastError(), "sb_reblock_tree: status word");
+  if (status == nullptr) return tree_cuda_error(cudaGetLastError(), who, "status word");
   cudaStream_t s = (cudaStream_t)stream;
   const __nv_bfloat16* F = static_cast<const __nv_bfloat16*>(features);
   uint8_t* ws = static_cast<uint8_t*>(workspace);
@@ -1922,15 +1935,15 @@ static int reblock_tree(const void* features, int rows, int tokens, int D, const
   const int L = plan_host[0], active = plan_host[2];
   reblock_root_kernel<<<rows, 1024, 0, s>>>(F, tokens, active, root_order, frozen, reinterpret_cast<float*>(keys),
                                             idx[0], perm, L == 0 ? 1 : 0, status);
-  SB_CHECK_LAUNCH("sb_reblock_tree: root");
+  TREE_CHECK_LAUNCH(who, "root");
   const ProxyKernel proxy_kernel = proxy_kernel_for(plan_host[6], plan_host[7]);
   cudaError_t err = cudaFuncSetAttribute(proxy_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                          (int)proxy_smem_bytes(kMaxChildren));
-  if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
+  if (err != cudaSuccess) return tree_cuda_error(err, who, "set smem");
   for (const void* fn : {(const void*)reblock_score3_kernel<2>, (const void*)reblock_score3_kernel<4>,
                          (const void*)reblock_score3_kernel<8>, (const void*)reblock_score3_kernel<16>}) {
     err = cudaFuncSetAttribute(fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kScoreRingBytes);
-    if (err != cudaSuccess) return cuda_error(err, "sb_reblock_tree: set smem");
+    if (err != cudaSuccess) return tree_cuda_error(err, who, "set smem");
   }
   int cur = 0;
   for (int l = 0; l < L; ++l) {
@@ -1938,7 +1951,7 @@ static int reblock_tree(const void* features, int rows, int tokens, int D, const
     TreeLevel lv{plan_device + lh[1], plan_device + lh[2], lh[0], lh[3], lh[4]};
     proxy_kernel<<<dim3(lv.count, rows), kProxyThreads, proxy_smem_bytes(lv.P), s>>>(F, tokens, active, lv, idx[cur],
                                                                                       dirs);
-    SB_CHECK_LAUNCH("sb_reblock_tree: proxy");
+    TREE_CHECK_LAUNCH(who, "proxy");
     const dim3 sgrid(ceil_div(active / 64, kScoreTiles), rows);
     switch (lv.P) {
       case 2: reblock_score3_kernel<2><<<sgrid, 128, kScoreRingBytes, s>>>(F, tokens, active, lv, idx[cur], dirs,
@@ -1951,9 +1964,9 @@ static int reblock_tree(const void* features, int rows, int tokens, int D, const
                                                                               scores); break;
       case 32: reblock_score_kernel<32><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
       case 64: reblock_score_kernel<64><<<sgrid, 256, 0, s>>>(F, tokens, active, lv, idx[cur], dirs, scores); break;
-      default: set_error("sb_reblock_tree: bad plan fanout %d", lv.P); return SB_ERR_INVALID;
+      default: set_error("%s: bad plan fanout %d", who, lv.P); return SB_ERR_INVALID;
     }
-    SB_CHECK_LAUNCH("sb_reblock_tree: scores");
+    TREE_CHECK_LAUNCH(who, "scores");
     const int32_t* first = plan_host + lh[1];  // the level's first node record (start, tokens, children)
     // the cluster form walks the heap of a power-of-two fanout; other roots take the radix form
     if (lv.count == 1 && first[1] > kSortMax && first[2] <= 2 * kClusterMaxNodes && (first[2] & (first[2] - 1)) == 0)
@@ -1965,20 +1978,20 @@ static int reblock_tree(const void* features, int rows, int tokens, int D, const
     else
       reblock_route_kernel<kRouteThreads, true><<<dim3(lv.count, rows), kRouteThreads, 0, s>>>(
           tokens, active, lv, idx[cur], scores, keys, state, idx[cur ^ 1], perm, status);
-    SB_CHECK_LAUNCH("sb_reblock_tree: route");
+    TREE_CHECK_LAUNCH(who, "route");
     cur ^= 1;
   }
   const int64_t total = (int64_t)rows * tokens;
   reblock_inverse_kernel<<<(unsigned)((total + 255) / 256), 256, 0, s>>>(perm, tokens, total, inverse);
-  SB_CHECK_LAUNCH("sb_reblock_tree: inverse");
+  TREE_CHECK_LAUNCH(who, "inverse");
   return SB_OK;
 }
 
 extern "C" int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int32_t* root_order,
                                const int32_t* plan_host, const int32_t* plan_device, void* workspace,
                                int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream) {
-  return reblock_tree(features, rows, tokens, D, root_order, nullptr, plan_host, plan_device, workspace,
-                      workspace_bytes, perm, inverse, stream);
+  return reblock_tree("sb_reblock_tree", features, rows, tokens, D, root_order, nullptr, plan_host, plan_device,
+                      workspace, workspace_bytes, perm, inverse, stream);
 }
 
 extern "C" int sb_reblock_tree_frozen(const void* features, int rows, int tokens, int D, const int32_t* root_order,
@@ -1987,6 +2000,6 @@ extern "C" int sb_reblock_tree_frozen(const void* features, int rows, int tokens
                                       void* stream) {
   SB_CHECK_ARG(excluded != nullptr || tokens % 64 == 0,
                "sb_reblock_tree_frozen: excluded ids are required for the %d remainder tokens", tokens % 64);
-  return reblock_tree(features, rows, tokens, D, root_order, excluded, plan_host, plan_device, workspace,
-                      workspace_bytes, perm, inverse, stream);
+  return reblock_tree("sb_reblock_tree_frozen", features, rows, tokens, D, root_order, excluded, plan_host,
+                      plan_device, workspace, workspace_bytes, perm, inverse, stream);
 }

@@ -194,3 +194,20 @@ def test_public_spark_names_match_reference_exports():
                  "convert_linear_to_fp8", "install_h3_spark_attn", "install_h3_sol_attn",
                  "install_h3_sparse_attention", "H3SparseAttentionConfig", "H3SparseAttentionPlugin"):
         assert name in spark_h3_b200.__all__, name
+
+
+def test_tree_entry_points_name_themselves_in_errors():
+    """Argument errors of the shared tree code name the entry point the caller used (no GPU:
+    both are refused before any launch)."""
+    from spark_h3_b200 import _lib
+
+    lib = _lib.load()
+    plan = np.zeros(16, dtype=np.int32)
+    assert lib.sb_reblock_tree(None, 1, 128, 128, None, plan.ctypes.data, None, None, 0, None, None, None) < 0
+    assert lib.sb_last_error().decode().startswith("sb_reblock_tree: null pointer")
+    assert lib.sb_reblock_tree_frozen(None, 1, 128, 128, None, None, plan.ctypes.data, None, None, 0, None, None,
+                                      None) < 0
+    assert lib.sb_last_error().decode().startswith("sb_reblock_tree_frozen: null pointer")
+    assert lib.sb_reblock_tree_frozen(None, 1, 130, 128, None, None, plan.ctypes.data, None, None, 0, None, None,
+                                      None) < 0
+    assert "excluded ids are required" in lib.sb_last_error().decode()
