@@ -6,7 +6,9 @@ its CuTe DSL is absent.
   H3_SPARK_REWEIGHT_FUSED=1) on the same Q/K/V, route, anchors and summaries: the north_star's
   bf16 attention bar, max-abs <= 2e-2 and cosine >= 0.9995.
 - Anchors and summaries against build_virtual_anchors and the Triton virtual_summaries
-  (sol_numerator_virtual_q.py:93-135, 268-353)."""
+  (sol_numerator_virtual_q.py:93-135, 268-353).
+- The e4m3 quantisers against the Triton ones of fp8_linear.py:75-239, and the head-wise
+  permute against headwise_permute_bthd (spark_integration.py:342-362)."""
 from __future__ import annotations
 
 import os
@@ -94,3 +96,43 @@ def test_anchor_and_summaries_match_the_references_triton_kernels(cuda_device, r
         assert bool((diff <= bound).all()), float(diff.max())
         assert float((diff == 0).float().mean()) >= 0.9999
     assert float((lm - rlm.reshape(lm.shape)).abs().max()) <= 1e-5
+
+
+def test_quantisers_and_permute_match_the_references_triton_kernels(cuda_device, reference_sm100):
+    """This build's quantisers are bit-exact with the reference's eager spellings (the
+    reference's own test oracles, tests/test_fp8_linear.py).  Its Triton kernels deviate from
+    those in the last bit: the fp32 division of x / scale is not IEEE-rounded, and swiglu's
+    sigmoid moves a row's maximum.  So: per-token and per-tensor scales bit-identical for the
+    plain quantisers, SwiGLU row scales within a few fp32 ulps (relative 2^-20), and at most
+    2 in 1,000 e4m3 codes one step apart.  The permute is a copy and is bit-identical."""
+    import h3_sparse_attention.fp8_linear as rf
+    from h3_sparse_attention.spark_integration import _headwise_permute_video_tokens
+
+    from spark_h3_b200 import fp8_linear as of
+
+    g = torch.Generator(device=cuda_device).manual_seed(0)
+    M, K = 2048, 4096
+    x = (torch.randn(M, K, device=cuda_device, generator=g)
+         * torch.empty(M, 1, device=cuda_device).log_normal_(0, 2, generator=g)).to(torch.bfloat16)
+    h = (torch.randn(M, 2 * K, device=cuda_device, generator=g) * 2).to(torch.bfloat16)
+    for name, ref_fn, our_fn, arg, exact_scale in (("rows", rf.quantize_rows, of.quantize_rows, x, True),
+                                                   ("tensor", rf.quantize_tensor, of.quantize_tensor, x, True),
+                                                   ("swiglu", rf.swiglu_quantize, of.swiglu_quantize, h, False),
+                                                   ("swiglu_tensor", rf.swiglu_quantize_tensor,
+                                                    of.swiglu_quantize_tensor, h, True)):
+        ry, rs = ref_fn(arg)
+        oy, os_ = our_fn(arg)
+        rs, os_ = rs.reshape(-1), os_.reshape(-1)
+        if exact_scale:
+            assert torch.equal(rs, os_), name
+        else:
+            rel = float(((rs - os_).abs() / rs.abs()).max())
+            assert rel <= 2.0 ** -20, (name, rel)
+        codes_r, codes_o = ry.view(torch.uint8).int(), oy.view(torch.uint8).int()
+        assert float((codes_r != codes_o).float().mean()) <= 2e-3, name
+        assert int((codes_r - codes_o).abs().max()) <= 1, name
+    B, T, H, video = 1, 5000, 4, 4800
+    v = torch.randn(B, T, H, 128, device=cuda_device, generator=g).to(torch.bfloat16)
+    perm = torch.stack([torch.randperm(video, device=cuda_device, generator=g) for _ in range(B * H)])
+    perm = perm.reshape(B, H, video).to(torch.int32).contiguous()
+    assert torch.equal(_headwise_permute_video_tokens(v, perm, video_tokens=video), ops.headwise_permute(v, perm, video))
