@@ -8,7 +8,9 @@ its CuTe DSL is absent.
 - Anchors and summaries against build_virtual_anchors and the Triton virtual_summaries
   (sol_numerator_virtual_q.py:93-135, 268-353).
 - The e4m3 quantisers against the Triton ones of fp8_linear.py:75-239, and the head-wise
-  permute against headwise_permute_bthd (spark_integration.py:342-362)."""
+  permute against headwise_permute_bthd (spark_integration.py:342-362).
+- The reblock metric factors and features against landmark_direction_factors and the
+  features bmm (landmark_direction.py:60-104, spark_integration.py:561-585) run on the GPU."""
 from __future__ import annotations
 
 import os
@@ -136,3 +138,29 @@ def test_quantisers_and_permute_match_the_references_triton_kernels(cuda_device,
     perm = torch.stack([torch.randperm(video, device=cuda_device, generator=g) for _ in range(B * H)])
     perm = perm.reshape(B, H, video).to(torch.int32).contiguous()
     assert torch.equal(_headwise_permute_video_tokens(v, perm, video_tokens=video), ops.headwise_permute(v, perm, video))
+
+
+def test_metric_factors_and_features_match_the_references_gpu_path(cuda_device, reference_sm100):
+    """Factors: fp32 moments and Cholesky on both sides, in different orders (this build's
+    canonical kernels against the reference's sgemm and cuSOLVER), within 1e-4 of the largest
+    element.  Features from the same factors: this build's tcgen05 transform against the
+    reference's bf16 bmm, within one bf16 ulp and equal in at least 99 % of the elements."""
+    from h3_sparse_attention.landmark_direction import landmark_direction_factors
+
+    from spark_h3_b200 import reblock
+
+    grid, heads = (2, 16, 40), 2
+    q, k, _ = make_qkv(grid, heads, 128, seed=7, dtype=torch.bfloat16, clustered=True, device=cuda_device)
+    T = q.shape[1]
+    samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype("int32")).to(cuda_device)
+    ours = reblock.metric_factors(q, k, samples, 1e-3)
+    flat_q = q.permute(0, 2, 1, 3).reshape(heads, T, 128)
+    flat_k = k.permute(0, 2, 1, 3).reshape(heads, T, 128)
+    lq, lk = landmark_direction_factors(flat_q, flat_k, samples.long(), ridge=1e-3)
+    ref = torch.cat([lq, lk]).float()
+    assert float((ours - ref).abs().max()) <= 1e-4 * float(ref.abs().max())
+    features = reblock.transform(q, k, ref.contiguous(), T)
+    ref_features = torch.cat([torch.bmm(flat_k, lq.to(torch.bfloat16)), torch.bmm(flat_q, lk.to(torch.bfloat16))])
+    a, b = features.float(), ref_features.float()
+    assert bool(((a - b).abs() <= 2.0 ** -7 * torch.maximum(a.abs(), b.abs()) + 1e-6).all())
+    assert float((a == b).float().mean()) >= 0.99
