@@ -10,7 +10,9 @@ its CuTe DSL is absent.
 - The e4m3 quantisers against the Triton ones of fp8_linear.py:75-239, and the head-wise
   permute against headwise_permute_bthd (spark_integration.py:342-362).
 - The reblock metric factors and features against landmark_direction_factors and the
-  features bmm (landmark_direction.py:60-104, spark_integration.py:561-585) run on the GPU."""
+  features bmm (landmark_direction.py:60-104, spark_integration.py:561-585) run on the GPU.
+- The Top-K route at config 1 against the reference's fp32 route (_sol_topk_policy_scores +
+  _sol_topk_route_from_scores, spark_integration.py:94-175) run on the GPU."""
 from __future__ import annotations
 
 import os
@@ -164,3 +166,35 @@ def test_metric_factors_and_features_match_the_references_gpu_path(cuda_device, 
     a, b = features.float(), ref_features.float()
     assert bool(((a - b).abs() <= 2.0 ** -7 * torch.maximum(a.abs(), b.abs()) + 1e-6).all())
     assert float((a == b).float().mean()) >= 0.99
+
+
+def test_route_matches_the_references_fp32_route_at_config1(cuda_device, reference_sm100):
+    """BASELINE config 1 at the reference's block size (N = 124,992, H = 32, 64-token blocks,
+    k = 195 of 1953): this build's route and the reference's fp32 route on the GPU, from the
+    same key means.  The two sum the query means and the dot products in different orders, so
+    a row may differ only where the reference's own k-th and (k+1)-th scores are within
+    rounding of each other; at most 1 in 1,000 rows may differ at all."""
+    from h3_sparse_attention.spark_integration import _sol_topk_policy_scores, _sol_topk_route_from_scores
+
+    q, k, _ = make_qkv((31, 48, 84), 32, 128, seed=0, device=cuda_device, dtype=torch.bfloat16,
+                       q_scale=128 ** -0.5)
+    T = q.shape[1]
+    n = T // 64
+    qc = ops.pool_queries(q, 64)
+    kc = ops.pool_keys_summaries(k, None, None, 64, want_summaries=False)[0]
+    topk = ops.target_topk(0.1, n)
+    _, idx = ops.route_topk(qc, kc, n, n, topk)
+    scores, adjacent, cand, qblocks, target = _sol_topk_policy_scores(q, kc, video_tokens=T, topk_ratio=0.1)
+    assert (cand, qblocks, target) == (n, n, topk)
+    route = _sol_topk_route_from_scores(scores, adjacent, candidate_blocks=cand, target_topk=target, video_tokens=T,
+                                        sink_tokens=0)
+    sel = route[0, :n, :, :n].reshape(-1, n)
+    ours = torch.zeros_like(sel)
+    ours.scatter_(1, idx[0].reshape(-1, topk).long(), True)
+    differ = (ours != sel).any(1)
+    assert float(differ.float().mean()) <= 1e-3
+    if bool(differ.any()):
+        s = scores[0, :n, :, :n].reshape(-1, n)[differ]
+        top = torch.topk(s, topk + 1, dim=-1).values
+        gap = top[:, topk - 1] - top[:, topk]
+        assert float(gap.max()) <= 1e-4 * float(top[:, 0].abs().max())
