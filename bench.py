@@ -54,10 +54,10 @@ HEAD_DIM = 128
 BLOCK = 128
 TOPK_RATIO = 0.1
 # DRAM bytes per launch of the attention kernel at this workload: dram__bytes_read.sum +
-# dram__bytes_write.sum of one launch of the same layer with 4 of the 32 heads (0.648 GB read
-# + 0.119 GB written), scaled by 8.  Heads run one after another through the grid, so the
+# dram__bytes_write.sum of one launch of the same layer with 4 of the 32 heads (0.662 GB read
+# + 0.126 GB written), scaled by 8.  Heads run one after another through the grid, so the
 # traffic grows with the head count.
-ATTENTION_TRAFFIC_BYTES = 8 * (647791616 + 118922240)
+ATTENTION_TRAFFIC_BYTES = 8 * (661666816 + 125626880)
 
 
 def dense_flops(tokens: int, heads: int, dim: int) -> float:
