@@ -12,7 +12,8 @@ its CuTe DSL is absent.
 - The reblock metric factors and features against landmark_direction_factors and the
   features bmm (landmark_direction.py:60-104, spark_integration.py:561-585) run on the GPU.
 - The Top-K route at config 1 against the reference's fp32 route (_sol_topk_policy_scores +
-  _sol_topk_route_from_scores, spark_integration.py:94-175) run on the GPU."""
+  _sol_topk_route_from_scores, spark_integration.py:94-175) run on the GPU, with one budget
+  for every head and with per-head budgets (route_with_head_budgets, head_budget.py:7-19)."""
 from __future__ import annotations
 
 import os
@@ -198,3 +199,33 @@ def test_route_matches_the_references_fp32_route_at_config1(cuda_device, referen
         top = torch.topk(s, topk + 1, dim=-1).values
         gap = top[:, topk - 1] - top[:, topk]
         assert float(gap.max()) <= 1e-4 * float(top[:, 0].abs().max())
+
+
+def test_head_budget_route_matches_the_references_at_config1(cuda_device, reference_sm100):
+    """Per-head Top-K budgets at config 1 (block 64): this build's route against
+    route_with_head_budgets on the reference's fp32 scores, from the same key means; the same
+    near-tie allowance as the fixed-budget route."""
+    from h3_sparse_attention.head_budget import route_with_head_budgets
+    from h3_sparse_attention.spark_integration import _sol_topk_policy_scores
+
+    q, k, _ = make_qkv((31, 48, 84), 32, 128, seed=0, device=cuda_device, dtype=torch.bfloat16,
+                       q_scale=128 ** -0.5)
+    T = q.shape[1]
+    n = T // 64
+    qc = ops.pool_queries(q, 64)
+    kc = ops.pool_keys_summaries(k, None, None, 64, want_summaries=False)[0]
+    budgets = torch.arange(32, device=cuda_device, dtype=torch.int32) * 13 + 40  # 40 .. 443 blocks
+    packed, _ = ops.route_topk(qc, kc, n, n, int(budgets.max()), head_budgets=budgets, want_indices=False)
+    scores, _, cand, _, _ = _sol_topk_policy_scores(q, kc, video_tokens=T, topk_ratio=0.1)
+    ref = route_with_head_budgets(scores, budgets.long(), cand, T, 0)[0, :n, :, :n]
+    bits = (packed[0].unsqueeze(-1) >> torch.arange(32, device=cuda_device, dtype=torch.int32)) & 1
+    ours = bits.reshape(n, 32, -1)[..., :n].bool()
+    assert torch.equal(ours.sum(-1), budgets.view(1, 32).expand(n, 32).to(ours.sum(-1).dtype))
+    differ = (ours != ref).any(-1).reshape(-1)
+    assert float(differ.float().mean()) <= 1e-3
+    if bool(differ.any()):
+        s = scores[0, :n, :, :n].reshape(-1, n)[differ]
+        kk = budgets.view(1, 32).expand(n, 32).reshape(-1)[differ].long()
+        ordered = s.sort(-1, descending=True).values
+        gap = ordered.gather(1, (kk - 1).view(-1, 1)) - ordered.gather(1, kk.view(-1, 1))
+        assert float(gap.max()) <= 1e-4 * float(ordered[:, 0].abs().max())
