@@ -479,6 +479,18 @@ int sb_reblock_tree(const void* features, int rows, int tokens, int D, const int
                     int64_t workspace_bytes, int32_t* perm, int32_t* inverse, void* stream);
 
 /*
+ * The protected remainder of each feature row, alone: the tokens mod 64 tokens of largest
+ * squared feature norm (equal norms: lower id), ascending ids.  Replaces
+ * landmark_tree_clustering.py:56-82 (_largest_norm_remainder) where spark_integration.py:
+ * 597-693 freezes the tail of the baseline (both-side Hilbert M2) features for the M2
+ * ablations, before the tree runs on other features (sb_reblock_tree_frozen).
+ * features: [rows, tokens, 128] bf16; workspace: 8 * rows * tokens bytes, 256-byte aligned;
+ * excluded: [rows, tokens mod 64] int32 (untouched when tokens is a multiple of 64).
+ */
+int sb_reblock_remainder(const void* features, int rows, int tokens, int D, void* workspace,
+                         int64_t workspace_bytes, int32_t* excluded, void* stream);
+
+/*
  * sb_reblock_tree with the protected remainder chosen by the caller: the excluded_indices
  * argument of landmark_tree_v2.py:790-832 and landmark_tree_clustering.py:85-119
  * (_initial_hilbert_partition's frozen tail).  excluded: [rows, tokens mod 64] device int32

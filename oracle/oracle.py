@@ -620,6 +620,22 @@ def hierarchy_schedule(split_budgets) -> np.ndarray:
     return np.asarray(words, dtype=np.int32)
 
 
+def remainder_ids(features_bits: np.ndarray) -> np.ndarray:
+    """The protected remainder of bf16 features [rows, N, D] (landmark_tree_clustering.py:56-82):
+    per row the N mod 64 ids of largest squared norm (reblock_oracle.c's canonical sum), equal
+    norms to the lower id, ascending; int32 [rows, N mod 64]."""
+    x = np.ascontiguousarray(features_bits, dtype=np.uint16)
+    rows, n, d = x.shape
+    rem = n % 64
+    out = np.zeros((rows, rem), dtype=np.int32)
+    norms = np.empty(n, dtype=np.float32)
+    for r in range(rows):
+        _lib().orc_rb_norms(x[r], n, d, norms)
+        order = np.lexsort((np.arange(n), -norms.astype(np.float64)))  # largest first, lower id first
+        out[r] = np.sort(order[:rem])
+    return out
+
+
 def reblock_tree(features_bits: np.ndarray, grid, split_budgets, order: str = "flat", *, proxy_iterations: int = 2,
                  seed_rule: str = "farthest_pair", excluded=None) -> tuple[np.ndarray, np.ndarray]:
     """Landmark-tree-v2 permutation of bf16 features [rows, N, D] (reblock_oracle.c), with the

@@ -2003,3 +2003,34 @@ extern "C" int sb_reblock_tree_frozen(const void* features, int rows, int tokens
   return reblock_tree("sb_reblock_tree_frozen", features, rows, tokens, D, root_order, excluded, plan_host,
                       plan_device, workspace, workspace_bytes, perm, inverse, stream);
 }
+
+extern "C" int sb_reblock_remainder(const void* features, int rows, int tokens, int D, void* workspace,
+                                    int64_t workspace_bytes, int32_t* excluded, void* stream) {
+  const char* who = "sb_reblock_remainder";
+  SB_CHECK_ARG(features && workspace, "%s: null pointer", who);
+  SB_CHECK_ARG(D == kDim, "%s: feature dimension must be 128, got %d", who, D);
+  SB_CHECK_ARG(rows > 0 && rows < 65536, "%s: rows must lie in [1, 65535]", who);
+  SB_CHECK_ARG(tokens >= 64 && tokens < (1 << 25), "%s: tokens must lie in [64, 2^25)", who);
+  SB_CHECK_ARG(((uintptr_t)features % 16) == 0 && ((uintptr_t)workspace % 256) == 0,
+               "%s: features must be 16-byte and the workspace 256-byte aligned", who);
+  SB_CHECK_ARG(workspace_bytes >= 8 * (int64_t)rows * tokens, "%s: workspace holds %lld bytes, %lld needed", who,
+               (long long)workspace_bytes, 8ll * rows * tokens);
+  const int rem = tokens % 64, active = tokens - rem;
+  if (rem == 0) return SB_OK;
+  SB_CHECK_ARG(excluded != nullptr, "%s: null excluded buffer for %d remainder tokens", who, rem);
+  int* status = device_status_ptr();
+  if (status == nullptr) return tree_cuda_error(cudaGetLastError(), who, "status word");
+  cudaStream_t s = (cudaStream_t)stream;
+  float* norms = static_cast<float*>(workspace);
+  int32_t* order = reinterpret_cast<int32_t*>(static_cast<uint8_t*>(workspace) + 4 * (size_t)rows * tokens);
+  // The root kernel in its direct form over the flat order: the tail of each row of `order`
+  // holds the remainder in ascending id order.
+  reblock_root_kernel<<<rows, 1024, 0, s>>>(static_cast<const __nv_bfloat16*>(features), tokens, active, nullptr,
+                                            nullptr, norms, order, order, 1, status);
+  TREE_CHECK_LAUNCH(who, "root");
+  const cudaError_t err = cudaMemcpy2DAsync(excluded, sizeof(int32_t) * rem, order + active,
+                                            sizeof(int32_t) * tokens, sizeof(int32_t) * rem, rows,
+                                            cudaMemcpyDeviceToDevice, s);
+  if (err != cudaSuccess) return tree_cuda_error(err, who, "copy");
+  return SB_OK;
+}

@@ -77,6 +77,7 @@ SIGNATURES = {
     "sb_reblock_workspace_bytes": (_i64, [_vp, _i]),
     "sb_reblock_tree": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
     "sb_reblock_tree_frozen": (_i, [_vp, _i, _i, _i, _vp, _vp, _vp, _vp, _vp, _i64, _vp, _vp, _vp]),
+    "sb_reblock_remainder": (_i, [_vp, _i, _i, _i, _vp, _i64, _vp, _vp]),
 }
 
 

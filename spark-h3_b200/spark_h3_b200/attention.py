@@ -177,7 +177,7 @@ def _head_budgets(budget, heads: int, device: torch.device) -> torch.Tensor | No
 _REBLOCK_DEFAULTS = dict(
     landmark_tree_v2_distance="cosine", landmark_tree_v2_order_mode="parent_order", landmark_tree_v2_mean_mode="raw",
     landmark_tree_v2_moment_mode="raw", landmark_tree_v2_group_size=1, landmark_tree_v2_landmark_mode="midpoint",
-    landmark_tree_v2_landmark_count=32, landmark_tree_v2_aggregation="linear", landmark_tree_v2_m2_side="both",
+    landmark_tree_v2_landmark_count=32, landmark_tree_v2_aggregation="linear",
     landmark_tree_v2_m2_estimator="hilbert_midpoint", landmark_tree_v2_proxy_update_rule="mean")
 
 
@@ -201,7 +201,8 @@ def _reblock_permutations(controller, q_bthd, k_bthd, layout, layer: int, video:
         fanout_mode=cfg.landmark_tree_v2_fanout_mode, final_fanout=cfg.landmark_tree_v2_final_fanout,
         root_fanout=cfg.landmark_tree_v2_root_fanout, ridge=cfg.rope_sol_key_ridge_epsilon,
         initial_order=cfg.landmark_tree_v2_initial_order, proxy_iterations=cfg.landmark_tree_v2_proxy_iterations,
-        seed_rule=cfg.landmark_tree_v2_proxy_seed_rule, layout_reuse=cfg.landmark_tree_v2_layout_reuse)
+        seed_rule=cfg.landmark_tree_v2_proxy_seed_rule, layout_reuse=cfg.landmark_tree_v2_layout_reuse,
+        m2_side=cfg.landmark_tree_v2_m2_side)
     controller.counts["rope_sol_landmark_tree_v2_key_assignments"] += 1
     controller.counts["rope_sol_landmark_tree_v2_query_assignments"] += 1
     result = (q_perm, query_inverse, k_perm, hierarchy)

@@ -245,6 +245,32 @@ class LandmarkTreeV2Result:
 _PLANS: dict[tuple, ReblockPlan] = {}
 
 
+def remainder_ids(features: torch.Tensor) -> torch.Tensor:
+    """The protected remainder of bf16 features [rows, tokens, 128]: the tokens mod 64 ids of
+    largest squared norm per row, equal norms to the lower id, ascending
+    (landmark_tree_clustering.py:56-82), int32 [rows, tokens mod 64]."""
+    device = _require_cuda(features)
+    rows, tokens, dim = features.shape
+    excluded = torch.empty((rows, tokens % BLOCK), dtype=torch.int32, device=device)
+    workspace = torch.empty(8 * rows * tokens, dtype=torch.uint8, device=device)
+    with torch.cuda.device(device):
+        _lib.call("sb_reblock_remainder", features.contiguous().data_ptr(), rows, tokens, dim, workspace.data_ptr(),
+                  workspace.numel(), excluded.data_ptr(), _stream(device))
+    return excluded
+
+
+def _required_m2_side(m2_side: str, layout_reuse: str) -> str:
+    """The feature sides that take the opposite side's second moment, given the layouts that
+    are built (spark_integration.py:365-380)."""
+    if m2_side not in ("both", "query", "key", "none"):
+        raise ValueError("m2_side must be both, query, key, or none")
+    if layout_reuse == "independent":
+        return m2_side
+    if layout_reuse == "q_from_k":
+        return "key" if m2_side in ("both", "key") else "none"
+    return "query" if m2_side in ("both", "query") else "none"
+
+
 def validate_excluded(excluded_indices, rows: int, tokens: int, device) -> torch.Tensor:
     """The caller's protected remainder, checked as landmark_tree_clustering.py:104-114 checks
     it (same messages): shape (rows, tokens mod 64), ids in range, unique per row.  Returns
@@ -381,7 +407,7 @@ def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, g
                           fanout_mode: str = "power_of_two_fanout", final_fanout=None, root_fanout=None,
                           ridge: float = 1e-3, initial_order: str = "flat", use_graph: bool = True,
                           proxy_iterations: int = 2, seed_rule: str = "farthest_pair",
-                          layout_reuse: str = "independent"):
+                          layout_reuse: str = "independent", m2_side: str = "both"):
     """Paired opposite-second-moment Q/K permutations (spark_integration.py:394-851):
     returns (q_perm, q_inv, k_perm, k_inv), int32 [B, H, video], plus the reblock hierarchy.
 
@@ -389,9 +415,16 @@ def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, g
     for K (features K . Lq) and one for Q (features Q . Lk); "q_from_k" builds only K's and Q
     takes the same permutation; "k_from_q" builds only Q's and K takes it.  With use_graph the
     independent trees replay a captured CUDA graph over the plan's static features buffer
-    (the transform writes into it); a shared layout runs its one tree eagerly."""
+    (the transform writes into it); a shared layout runs its one tree eagerly.
+
+    m2_side (landmark_tree_v2_m2_side; spark_integration.py:450-466, 562-585, 597-693): which
+    feature sides take the opposite side's second-moment factor -- "both", "key" (K . Lq
+    only), "query" (Q . Lk only) or "none"; a side without it clusters its raw rows.  When the
+    video leaves a remainder, the protected tail is frozen to the one the baseline (both-side)
+    features choose, so the ablation does not change which tokens stay exact."""
     if layout_reuse not in ("independent", "q_from_k", "k_from_q"):
         raise ValueError(f"unknown layout reuse mode: {layout_reuse}")
+    required = _required_m2_side(m2_side, layout_reuse)
     device = _require_cuda(q, k)
     B, T, H, D = q.shape
     grid = _grid_tuple(grid)
@@ -406,6 +439,24 @@ def qk_block_permutations(q: torch.Tensor, k: torch.Tensor, video_tokens: int, g
                  proxy_iterations, seed_rule)
     BH = B * H
     shape = (B, H, video_tokens)
+    baseline = "both" if layout_reuse == "independent" else ("key" if layout_reuse == "q_from_k" else "query")
+    if required != baseline:
+        # rows [0, BH) of the features are K . Lq, rows [BH, 2BH) Q . Lk; a side without its
+        # factor takes its raw rows, after the baseline features have chosen the tail
+        features = transform(q, k, factors, video_tokens)
+        rows = slice(0, 2 * BH) if layout_reuse == "independent" else (
+            slice(0, BH) if layout_reuse == "q_from_k" else slice(BH, 2 * BH))
+        excluded = remainder_ids(features[rows]) if video_tokens % BLOCK else None
+        if required in ("query", "none"):
+            features[:BH] = k[:, :video_tokens].permute(0, 2, 1, 3).reshape(BH, video_tokens, D)
+        if required in ("key", "none"):
+            features[BH:] = q[:, :video_tokens].permute(0, 2, 1, 3).reshape(BH, video_tokens, D)
+        perm, inverse = plan.run(features[rows], excluded_indices=excluded)
+        if layout_reuse != "independent":
+            perm, inverse = perm.view(shape), inverse.view(shape)
+            return perm, inverse, perm, inverse, plan.hierarchy
+        return (perm[BH:].view(shape), inverse[BH:].view(shape), perm[:BH].view(shape), inverse[:BH].view(shape),
+                plan.hierarchy)
     if layout_reuse != "independent":
         # rows [0, BH) of the features are K . Lq, rows [BH, 2BH) Q . Lk
         features = transform(q, k, factors, video_tokens)

@@ -38,6 +38,9 @@ Fixtures:
                   always runs through node_split_reference
   reblock_tree_frozen.npz  the same with a caller-chosen protected remainder (excluded_indices,
                   landmark_tree_clustering.py:99-119): the seeded ids and the permutation
+  reblock_m2.npz  the paired Q/K reblock with the M2 ablations (landmark_tree_v2_m2_side none /
+                  key / query, spark_integration.py:450-693: raw features on the sides without
+                  the factor, the baseline tail frozen) and a shared layout, on clustered Q/K
   reblock_qk.npz  the full paired Q/K reblock (_landmark_tree_v2_qk_block_permutations,
                   spark_integration.py:735-851, CPU controller, mode "full") on clustered
                   synthetic Q/K: Hilbert metric samples, the Cholesky factors, the bf16
@@ -398,6 +401,38 @@ def reblock_qk_fixture():
                         q_inv=qi.numpy().astype(np.int32), k_inv=ki.numpy().astype(np.int32))
 
 
+REBLOCK_M2_CASES = [
+    # (name, grid, heads, m2_side, layout_reuse, seed)
+    ("none_even", (2, 16, 40), 2, "none", "independent", 7),
+    ("none_rem", (2, 16, 41), 2, "none", "independent", 8),
+    ("key_rem", (2, 16, 41), 2, "key", "independent", 9),
+    ("query_rem", (2, 16, 41), 2, "query", "independent", 10),
+    ("shared_none_rem", (2, 16, 41), 2, "none", "q_from_k", 11),
+]
+
+
+def reblock_m2_fixture():
+    from types import SimpleNamespace
+
+    from h3_sparse_attention.processor import H3SparseAttentionConfig, _Controller
+    from h3_sparse_attention.spark_integration import _landmark_tree_v2_qk_block_permutations
+    from spark_h3_b200.synthetic import make_qkv
+
+    out = {}
+    for name, grid, heads, m2_side, reuse, seed in REBLOCK_M2_CASES:
+        q, k, _ = make_qkv(grid, heads, 128, seed=seed, dtype=torch.bfloat16, clustered=True)
+        T = q.shape[1]
+        cfg = H3SparseAttentionConfig.spark(num_inference_steps=4, mode="full", sol_route_topk_ratio=0.1,
+                                            landmark_tree_v2_m2_side=m2_side, landmark_tree_v2_layout_reuse=reuse)
+        layout = SimpleNamespace(video_tokens=T, grid=grid, sequence_length=T)
+        qp, qi, kp, ki, _, _ = _landmark_tree_v2_qk_block_permutations(_Controller(cfg), q, k, layout)
+        out[f"{name}_q_perm"] = qp.numpy().astype(np.int32)
+        out[f"{name}_k_perm"] = kp.numpy().astype(np.int32)
+        out[f"{name}_q_digest"] = np.array(digest(q))
+        out[f"{name}_k_digest"] = np.array(digest(k))
+    np.savez_compressed(HERE / "reblock_m2.npz", **out)
+
+
 def main():
     (HERE / "hierarchy.json").write_text(json.dumps(hierarchy_cases()))
     (HERE / "layout.json").write_text(json.dumps(layout_cases()))
@@ -410,6 +445,7 @@ def main():
     reblock_tree_modes_fixture()
     reblock_tree_proxy_fixture()
     reblock_tree_frozen_fixture()
+    reblock_m2_fixture()
     reblock_qk_fixture()
     print("golden fixtures written to", HERE)
 

@@ -351,6 +351,48 @@ def test_full_mode_layer_with_exact_block_radius(cuda_device):
     assert diff <= 2e-2 and cos >= 0.9995
 
 
+M2_CASES = [
+    # (name, grid, heads, m2_side, layout_reuse, seed)
+    ("none_even", (2, 16, 40), 2, "none", "independent", 7),
+    ("none_rem", (2, 16, 41), 2, "none", "independent", 8),
+    ("key_rem", (2, 16, 41), 2, "key", "independent", 9),
+    ("query_rem", (2, 16, 41), 2, "query", "independent", 10),
+    ("shared_none_rem", (2, 16, 41), 2, "none", "q_from_k", 11),
+]
+
+
+@pytest.mark.parametrize("name,grid,heads,m2_side,reuse,seed", M2_CASES)
+def test_m2_ablations(cuda_device, name, grid, heads, m2_side, reuse, seed):
+    """landmark_tree_v2_m2_side: the raw sides' permutations equal the reference's own
+    (tests/golden/reblock_m2.npz) bit for bit, and the factored sides equal the oracle tree on
+    this build's GPU features; the protected tail is the baseline features' (GPU
+    sb_reblock_remainder against the oracle's)."""
+    z = np.load(GOLDEN / "reblock_m2.npz")
+    q, k, _ = make_qkv(grid, heads, 128, seed=seed, dtype=torch.bfloat16, clustered=True)
+    q, k = q.to(cuda_device), k.to(cuda_device)
+    T = q.shape[1]
+    qp, _, kp, _, hierarchy = reblock.qk_block_permutations(q, k, T, grid, m2_side=m2_side, layout_reuse=reuse)
+    qp, kp = qp.cpu().numpy().reshape(heads, T), kp.cpu().numpy().reshape(heads, T)
+    samples = torch.from_numpy(reblock.hilbert_midpoint_sample_indices(grid, T // 64).astype(np.int32)).to(cuda_device)
+    features = reblock.transform(q, k, reblock.metric_factors(q, k, samples), T)
+    excluded = None
+    if T % 64:
+        excluded = reblock.remainder_ids(features).cpu().numpy()
+        assert np.array_equal(excluded, oracle.remainder_ids(bits(features)))
+    sides = {"k": (kp, 0, m2_side in ("query", "none")), "q": (qp, 1, m2_side in ("key", "none"))}
+    for side, (perm, half, raw) in sides.items():
+        if reuse == "q_from_k":
+            assert np.array_equal(perm, z[f"{name}_{side}_perm"].reshape(heads, T))
+            continue
+        if raw:
+            assert np.array_equal(perm, z[f"{name}_{side}_perm"].reshape(heads, T))
+        else:
+            rows = features[half * heads:(half + 1) * heads]
+            ref, _ = oracle.reblock_tree(bits(rows), grid, hierarchy.split_budgets,
+                                         excluded=None if excluded is None else excluded[half * heads:(half + 1) * heads])
+            assert np.array_equal(perm, ref)
+
+
 def test_graph_replay_matches_eager(cuda_device):
     """qk_block_permutations through the captured CUDA graph (first call eager, second
     captures, later calls replay) gives the eager pipeline's permutations, bit for bit, on

@@ -152,3 +152,43 @@ def test_qk_reblock_matches_reference():
     features = oracle.bf16_bits_to_f32(oracle.reblock_features(tq, tk, factors, T))
     ref_features = oracle.bf16_bits_to_f32(z["features"])
     assert np.abs(features - ref_features).max() <= 2 ** -7 * np.abs(ref_features).max()
+
+
+M2_CASES = [
+    # (name, grid, heads, m2_side, layout_reuse, seed)
+    ("none_even", (2, 16, 40), 2, "none", "independent", 7),
+    ("none_rem", (2, 16, 41), 2, "none", "independent", 8),
+    ("key_rem", (2, 16, 41), 2, "key", "independent", 9),
+    ("query_rem", (2, 16, 41), 2, "query", "independent", 10),
+    ("shared_none_rem", (2, 16, 41), 2, "none", "q_from_k", 11),
+]
+
+
+@pytest.mark.parametrize("name,grid,heads,m2_side,reuse,seed", M2_CASES)
+def test_m2_ablation_raw_sides_match_reference(name, grid, heads, m2_side, reuse, seed):
+    """landmark_tree_v2_m2_side (spark_integration.py:450-693): a side without the M2 factor
+    clusters its raw rows, with the protected tail the baseline (both-side) features choose.
+    The raw sides' permutations equal the reference's own; the factored sides go through the
+    factors, whose fp32 order is a library internal (pinned separately, given the factors)."""
+    z = np.load(GOLDEN / "reblock_m2.npz")
+    q, k, _ = make_qkv(grid, heads, 128, seed=seed, dtype=torch.bfloat16, clustered=True)
+    assert digest(q) == str(z[f"{name}_q_digest"]) and digest(k) == str(z[f"{name}_k_digest"])
+    T = int(np.prod(grid))
+    raw_k = bits(k[0].permute(1, 0, 2).contiguous())  # [H, T, 128]
+    raw_q = bits(q[0].permute(1, 0, 2).contiguous())
+    tq, tk = oracle.Tensor(bits(q), "bfloat16"), oracle.Tensor(bits(k), "bfloat16")
+    samples = oracle.hilbert_midpoint_samples(grid, T // 64)
+    features = oracle.reblock_features(tq, tk, oracle.metric_factors(tq, tk, samples, T), T)
+    excluded = oracle.remainder_ids(features) if T % 64 else None
+    budgets = build_reblock_hierarchy(T, 16).split_budgets
+    if reuse == "q_from_k":
+        perm, _ = oracle.reblock_tree(raw_k, grid, budgets, excluded=None if excluded is None else excluded[:heads])
+        assert np.array_equal(perm, z[f"{name}_k_perm"].reshape(heads, T))
+        assert np.array_equal(perm, z[f"{name}_q_perm"].reshape(heads, T))
+        return
+    if m2_side in ("query", "none"):
+        perm, _ = oracle.reblock_tree(raw_k, grid, budgets, excluded=None if excluded is None else excluded[:heads])
+        assert np.array_equal(perm, z[f"{name}_k_perm"].reshape(heads, T))
+    if m2_side in ("key", "none"):
+        perm, _ = oracle.reblock_tree(raw_q, grid, budgets, excluded=None if excluded is None else excluded[heads:])
+        assert np.array_equal(perm, z[f"{name}_q_perm"].reshape(heads, T))
