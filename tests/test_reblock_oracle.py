@@ -58,6 +58,8 @@ TREE_MODE_CASES = [
     ("p2final_8_16", 6016, 8, 16, "power_of_two_arbitrary_final", (4, 32, 47), "flat", 23),
     ("arb_final12", 13000, 16, 12, "arbitrary_fanout", (1, 1, 13000), "flat", 24),
     ("arb_root3", 12352, 4, 3, "arbitrary_fanout", (2, 32, 193), "hilbert_thw", 25),
+    ("arb_fanout64", 12800, 64, None, "arbitrary_fanout", (2, 80, 80), "flat", 26),
+    ("arb_final24", 20160, 32, 24, "arbitrary_fanout", (5, 63, 64), "flat", 27),
 ]
 
 
