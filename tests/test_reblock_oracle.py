@@ -65,8 +65,8 @@ TREE_MODE_CASES = [
 
 @pytest.mark.parametrize("name,tokens,children,final_fanout,mode,grid,order,seed", TREE_MODE_CASES)
 def test_tree_fanout_modes_match_reference(name, tokens, children, final_fanout, mode, grid, order, seed):
-    """The arbitrary and power-of-two-arbitrary-final fanout modes: nodes split into 3, 6, 7,
-    9, 10, 11, 12 or 15 children over the breadth-first split topology; the reference's own
+    """The arbitrary and power-of-two-arbitrary-final fanout modes: nodes split into 3 to 50
+    children over the breadth-first split topology; the reference's own
     CPU tree (recursive_landmark_tree_v2_reference) gave the permutations."""
     import json
 
