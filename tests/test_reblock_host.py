@@ -211,3 +211,40 @@ def test_tree_entry_points_name_themselves_in_errors():
     assert lib.sb_reblock_tree_frozen(None, 1, 130, 128, None, None, plan.ctypes.data, None, None, 0, None, None,
                                       None) < 0
     assert "excluded ids are required" in lib.sb_last_error().decode()
+
+
+def _no_gpu() -> bool:
+    import torch
+
+    return not torch.cuda.is_available()
+
+
+@pytest.mark.skipif(not _no_gpu(), reason="passes placeholder addresses; runs only where no GPU exists")
+def test_remainder_entry_point_validates_its_arguments():
+    """sb_reblock_remainder refuses bad arguments before any launch.  The non-null pointers are
+    placeholders the checks reject before any use, so this runs only on a host without a GPU,
+    where nothing could be launched on them."""
+    from spark_h3_b200 import _lib
+
+    lib = _lib.load()
+    assert lib.sb_reblock_remainder(None, 1, 130, 128, None, 0, None, None) < 0
+    assert "null pointer" in lib.sb_last_error().decode()
+    fake = 1 << 20  # a non-null, aligned address that is never dereferenced: checks fail first
+    assert lib.sb_reblock_remainder(fake, 1, 130, 64, fake, 8 * 130, fake, None) < 0
+    assert "feature dimension must be 128" in lib.sb_last_error().decode()
+    assert lib.sb_reblock_remainder(fake, 1, 130, 128, fake, 8 * 130 - 1, fake, None) < 0
+    assert "workspace holds" in lib.sb_last_error().decode()
+    assert lib.sb_reblock_remainder(fake, 1, 130, 128, fake, 8 * 130, None, None) < 0
+    assert "null excluded buffer" in lib.sb_last_error().decode()
+    assert lib.sb_reblock_remainder(fake, 1, 128, 128, fake, 8 * 128, None, None) == 0  # no remainder: nothing to do
+
+
+def test_m2_side_is_validated():
+    import torch
+
+    with pytest.raises(ValueError, match="m2_side"):
+        reblock._required_m2_side("diag", "independent")
+    assert reblock._required_m2_side("query", "q_from_k") == "none"
+    assert reblock._required_m2_side("both", "k_from_q") == "query"
+    with pytest.raises(RuntimeError):  # CUDA tensors only
+        reblock.remainder_ids(torch.zeros(1, 130, 128, dtype=torch.bfloat16))
