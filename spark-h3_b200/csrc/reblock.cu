@@ -1093,14 +1093,14 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
   __syncthreads();
   // st[t]: the token's internal proxy node, or kFinished + child once its child is decided
   for (int depth = 0; depth < topo.depths; ++depth) {
-    const int first_heap = topo.first[depth];
-    const int nd = topo.first[depth + 1] - first_heap;
+    const int first_node = topo.first[depth];
+    const int nd = topo.first[depth + 1] - first_node;
     if (tid < nd) {
       // the node's left capacity; the tokens of the depth's earlier nodes (their whole
       // capacities) come before its own in the sorted keys
-      const int k = first_heap + tid;
+      const int k = first_node + tid;
       int before = 0;
-      for (int jn = first_heap; jn < k; ++jn) before += topo.lc[jn] + topo.rc[jn];
+      for (int jn = first_node; jn < k; ++jn) before += topo.lc[jn] + topo.rc[jn];
       target[tid] = topo.lc[k];
       seg[tid] = before;
       prefix[tid] = 0;
@@ -1118,7 +1118,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
         if (e < n && st[e] < kFinished) {
           const int h = st[e];
           const uint32_t kk = order_key(sc[(int64_t)e * lv.S + h]);
-          k64 = ((unsigned long long)(h - first_heap) << 57) | ((unsigned long long)kk << 25) |
+          k64 = ((unsigned long long)(h - first_node) << 57) | ((unsigned long long)kk << 25) |
                 (unsigned long long)(uint32_t)ids[e];
         }
         mine[q] = k64;
@@ -1154,7 +1154,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
         const int e = tid + q * THREADS;
         if (e < n && mine[q] != ~0ull) {
           const int j = (int)(mine[q] >> 57);
-          const int hnode = first_heap + j;
+          const int hnode = first_node + j;
           st[e] = target[j] > 0 && mine[q] <= cut[j] ? topo.ltag[hnode] : topo.rtag[hnode];
         }
       }
@@ -1192,7 +1192,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
           for (int u = 0; u < kUnroll; ++u) {
             const int t = t0 + u * THREADS;
             const int h = t < n ? st[t] : kFinished;
-            js[u] = h < kFinished ? h - first_heap : -1;
+            js[u] = h < kFinished ? h - first_node : -1;
             ks[u] = h < kFinished ? key[t] : 0u;
           }
 #pragma unroll
@@ -1236,7 +1236,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
           for (int t = tid; t < n; t += THREADS) {
             const int h = st[t];
             if (h >= kFinished) continue;
-            const int j = h - first_heap;
+            const int j = h - first_node;
             if (!need_ids[j] || key[t] != prefix[j]) continue;
             const uint32_t id = (uint32_t)ids[t];
             if (pass == 0 || (id >> (shift + 8)) == (id_prefix[j] >> (shift + 8)))
@@ -1271,7 +1271,7 @@ __global__ void __launch_bounds__(THREADS) reblock_route_kernel(int N, int activ
         for (int u = 0; u < kUnroll; ++u) {
           const int t = t0 + u * THREADS;
           if (hs[u] >= kFinished) continue;
-          const int j = hs[u] - first_heap;
+          const int j = hs[u] - first_node;
           const bool left = ks[u] < prefix[j] ||
                             (ks[u] == prefix[j] && (!need_ids[j] || (uint32_t)ids[t] <= id_prefix[j]));
           st[t] = left ? topo.ltag[hs[u]] : topo.rtag[hs[u]];
