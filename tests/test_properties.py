@@ -143,3 +143,34 @@ def test_reblock_hierarchy_frontiers_partition_the_leaves(blocks, children):
             inside = [(x, y) for x, y in kids if a <= x and y <= b]
             assert sum(y - x for x, y in inside) == b - a
             assert len(inside) <= children  # no split has more children than the fanout
+
+
+@settings(max_examples=25, deadline=None, suppress_health_check=[HealthCheck.too_slow])
+@given(st.integers(2, 90), st.integers(0, 63), st.sampled_from([2, 4, 8, 16, 32, 64]),
+       st.sampled_from([None, 3, 5, 7, 12, 24, 32]), st.sampled_from(["arbitrary_fanout",
+                                                                   "power_of_two_arbitrary_final"]),
+       st.integers(0, 2**31 - 1))
+def test_arbitrary_fanout_trees_are_exact_partitions(blocks, rem, children, final_fanout, mode, seed):
+    """Any child count from 2 to 64 over the breadth-first split topology: the oracle tree is a
+    permutation of the tokens, every leaf holds its 64 tokens, the remainder sits at the tail,
+    and the C-ABI plan builder accepts the hierarchy with a power-of-two level width."""
+    from spark_h3_b200 import _lib, reblock
+
+    tokens = blocks * 64 + rem
+    h = build_reblock_hierarchy(tokens, children, final_fanout=final_fanout, fanout_mode=mode)
+    x = torch.randn(1, tokens, 128, generator=torch.Generator().manual_seed(seed)).to(torch.bfloat16)
+    bits_ = x.view(torch.int16).numpy().view(np.uint16)
+    perm, inverse = oracle.reblock_tree(bits_, (1, 1, tokens), h.split_budgets)
+    assert np.array_equal(np.sort(perm[0]), np.arange(tokens))
+    assert np.array_equal(inverse[0][perm[0]], np.arange(tokens))
+    if rem:
+        assert np.array_equal(perm[0, blocks * 64:], np.sort(oracle.remainder_ids(bits_)[0]))
+    schedule = reblock._schedule(h)
+    lib = _lib.load()
+    n = lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens, None, 0)
+    assert n > 0
+    plan = np.zeros(n, dtype=np.int32)
+    assert lib.sb_reblock_plan(schedule.ctypes.data, len(schedule), tokens, plan.ctypes.data, n) == n
+    for level in range(plan[0]):
+        P = plan[8 + 8 * level + 3]
+        assert P >= 2 and P & (P - 1) == 0 and P <= 64
