@@ -58,6 +58,9 @@ TOPK_RATIO = 0.1
 # + 0.126 GB written), scaled by 8.  Heads run one after another through the grid, so the
 # traffic grows with the head count.
 ATTENTION_TRAFFIC_BYTES = 8 * (661666816 + 125626880)
+# The same for the config-2 attention launch at top-k 0.1 (query blocks paired): one launch of
+# the full-mode layer with 2 of the 32 heads (3.135 GB read + 0.139 GB written), scaled by 16.
+CONFIG2_ATTENTION_TRAFFIC_BYTES = 16 * (3134581504 + 139380480)
 
 
 def dense_flops(tokens: int, heads: int, dim: int) -> float:
@@ -618,7 +621,11 @@ def run_config2(args) -> None:
             stages_ms=stages,
             roofline=dict(bound="tensor", kernel="sparse_attention_sm100_kernel", achieved=achieved,
                           peak=peaks["bf16"], unit="TFLOP/s", frac=achieved / peaks["bf16"],
-                          frac_of_sustained=achieved / peaks["bf16_sustained"], traffic=None,
+                          frac_of_sustained=achieved / peaks["bf16_sustained"],
+                          traffic=(CONFIG2_ATTENTION_TRAFFIC_BYTES
+                                   if (grid, heads, ratio) == ((61, 48, 84), 32, 0.1) else None),
+                          traffic_unit=("bytes per launch: ncu dram__bytes_read.sum + dram__bytes_write.sum of the "
+                                        "2-head layer at top-k 0.1, scaled x16 to 32 heads"),
                           peak_source=peaks["source"],
                           note="sparse FLOPs 4 D (k 64 + (n - k)) per routed query row; the kernel's 128-row tiles "
                                "pair two 64-row query blocks and compute the union of their key sets"),
